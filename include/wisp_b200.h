@@ -1,0 +1,106 @@
+/*
+ * wisp_b200.h -- C ABI of libwisp_b200.so, the B200 (sm_100a) kernels behind the WiSP decode hot path.
+ *
+ * Conventions
+ *   - Every entry point returns WISP_OK (0) or a WISP_ERR_* code; wisp_last_error() gives the message
+ *     (per host thread).  Argument checks happen on the host before anything is launched.
+ *   - All array pointers are DEVICE pointers unless the name ends in _host.  Nothing here allocates,
+ *     synchronises or reads device memory from the host, so every call can be captured in a CUDA
+ *     graph.  Work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ *   - Kernels never trap.  A bad slot id or position found on the device sets a bit of the per-device
+ *     status word (WISP_STATUS_*) and that access is skipped; wisp_device_status() reads it.
+ *   - dtypes: bf16/f16 are passed as uint16_t bit patterns, fp32 as float.
+ *   - Packed expert layout (byte-identical to the reference store):
+ *       [codes: 3*n*bits/8 bytes | fp16 scales [3n/group] | fp16 mins [3n/group]],
+ *     matrices gate [I,H], up [I,H], down [H,I] flat in that order; element e of the expert's
+ *     3n-element stream sits at bit bits*e of the code region (little endian); group g covers
+ *     `group` consecutive elements; value = fp32(q)*fp32(scale) + fp32(min).
+ *
+ * Reference citations are `path:line` in imronpuji/wisp-runtime 0.1.0.
+ */
+#ifndef WISP_B200_H
+#define WISP_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WISP_OK 0
+#define WISP_ERR_INVALID 1     /* bad argument (shape, dtype, size, alignment) */
+#define WISP_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define WISP_ERR_UNSUPPORTED 3 /* valid input this build does not handle */
+
+#define WISP_STATUS_BAD_SLOT 0x1u    /* a slot id outside [0, nslots) was skipped */
+#define WISP_STATUS_BAD_POS 0x2u     /* a position outside the KV capacity was skipped */
+#define WISP_STATUS_WAIT_TIMEOUT 0x4u /* a bounded device-side wait gave up */
+#define WISP_STATUS_BAD_ROUTE 0x8u   /* a routing entry (expert id / token index) was out of range */
+
+#define WISP_DTYPE_F32 0
+#define WISP_DTYPE_BF16 1
+#define WISP_DTYPE_F16 2
+
+/* ---- library ----------------------------------------------------------------------------------- */
+int wisp_version(void);                 /* 10000*major + 100*minor + patch */
+const char* wisp_last_error(void);      /* message of the last failed call on this host thread */
+/* Reads (and with clear != 0, resets) the status word of `device`.  Synchronises that device. */
+int wisp_device_status(int device, int clear, uint32_t* status_host);
+
+/* Bytes of one packed expert of 3*n elements, or -1 if the shape is invalid.
+ * Replaces wisp/quant.py:17-22 (expert_nbytes). */
+int64_t wisp_expert_nbytes(int64_t n, int bits, int group);
+
+/* ---- packed format ------------------------------------------------------------------------------ */
+/* Quantize `batch` experts [batch, 3, n] (w_dtype F32 or BF16) into `out` [batch, nbytes] with
+ * nbytes = wisp_expert_nbytes(n, bits, group), bit-exact with the reference RTN min/max quantizer
+ * (fp32 math, fp16 round-to-nearest-even scale/min, half-to-even code rounding).
+ * bits in {16, 8, 4, 3, 2}.  Replaces wisp/quant.py:60-73 (quantize) and the per-expert loop of
+ * wisp/store.py:38-40 (put). */
+int wisp_quantize(const void* w3, int w_dtype, int64_t batch, int64_t n, int bits, int group, uint8_t* out,
+                  void* stream);
+
+/* Dequantize rows of a packed pool [pool_rows, nbytes] into bf16 [nrows, 3, n], bit-exact with the
+ * reference (fp32 q*s then +m, each rounded, then round-to-nearest-even to bf16).  `rows` (int64
+ * [nrows]) selects pool rows; NULL means rows 0..nrows-1.  Replaces wisp/quant.py:76-111
+ * (dequant / dequant_fast) and the gather of wisp/cache.py:121-127 (weights_batched). */
+int wisp_dequant(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, const int64_t* rows, int64_t nrows,
+                 int64_t n, int bits, int group, uint16_t* out_bf16, void* stream);
+
+/* Integer codes of rows of a packed pool -> uint8 [nrows, 3n].  Same row selection as wisp_dequant.
+ * Replaces wisp/quant.py:44-57 (_unpack) for the code-level parity probe. */
+int wisp_unpack_codes(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, const int64_t* rows, int64_t nrows,
+                      int64_t n, int bits, uint8_t* codes, void* stream);
+
+/* ---- fused MoE decode, one token ---------------------------------------------------------------- */
+/* out[h] = sum_j w_j * Wd_j[h,:] . (silu(Wg_j x) * (Wu_j x)), dequant folded into the dot products,
+ * weights read straight from the slot pool.  meta: fp32 [2k] = [slot_0..slot_{k-1}, w_0..w_{k-1}] on
+ * the device.  x, out: bf16 [H].  scratch: fp32 [k*I] (intermediate a = silu(g)*u).
+ * bits in {8, 4, 3, 2}; H, I multiples of 32 and of group; group a multiple of 32; pool 16-byte
+ * aligned with nbytes a multiple of 16.
+ * Replaces wisp/kernels.py:188-203 (moe_decode_q4_fast), :310-322 (moe_decode_q3_fast), and adds the
+ * 2-bit and 8-bit variants the reference runs through dequant + bmm (wisp/moe.py:122-130). */
+int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
+                    const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out,
+                    void* stream);
+
+/* ---- decode-side ops ---------------------------------------------------------------------------- */
+/* Rotate-half RoPE for one token: q [Hq, D] (head stride q_stride elements), k [Hk, D] (k_stride),
+ * cos/sin bf16 [D]; writes contiguous qo [Hq, D], ko [Hk, D].  fp32 math, one rounding to bf16.
+ * Replaces wisp/kernels.py:328-371 (rope_decode). */
+int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t* k, int64_t k_stride, int Hk, int D,
+                     const uint16_t* cos, const uint16_t* sin, uint16_t* qo, uint16_t* ko, void* stream);
+
+/* RMSNorm of `rows` rows of H bf16 values: out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))).
+ * If `delta` is non-NULL the row is first replaced by bf16(x + delta) and, when `sum_out` is
+ * non-NULL, that sum is stored there (the residual add fused in).
+ * Replaces wisp/model.py:94-107 (patched Qwen3MoeRMSNorm) and the residual adds of
+ * wisp/graphdec.py:175-176, :209. */
+int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, const uint16_t* w, int64_t rows,
+                 int64_t H, float eps, uint16_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WISP_B200_H */

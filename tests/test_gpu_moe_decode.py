@@ -1,0 +1,123 @@
+"""GPU parity of the fused bs=1 MoE decode (gate/up + SwiGLU, down, weighted combine) through the
+C ABI against the oracle's dequantize-then-matmul fp32 reference (tolerance 1e-2 relative, the bar of
+the north star; the reference's own kernel tests use 2e-2)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import wisp_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _bf16_np(t):
+    return O.bf16_bits_to_f32(t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / np.abs(ref).max())
+
+
+def test_matches_reference_kernel_fixture(golden):
+    """The exact inputs of the reference tests/test_kernels.py (H=256, I=128, E=6, k=3)."""
+    from wisp import kernels
+
+    g = golden("kernels")
+    H, I, k = int(g["H"]), int(g["I"]), int(g["k"])
+    n = H * I
+    for bits, fn in ((4, kernels.moe_decode_q4_fast), (3, kernels.moe_decode_q3_fast)):
+        pool = torch.from_numpy(g[f"pool_b{bits}"]).cuda()
+        slots = torch.from_numpy(g[f"slots_b{bits}"]).cuda()
+        x = torch.from_numpy(g[f"x_b{bits}"].view(np.int16)).view(torch.bfloat16).cuda()
+        w = torch.from_numpy(g[f"w_b{bits}"]).cuda()
+        meta = torch.cat([slots.float(), w.float()])
+        got = _bf16_np(fn(pool, meta, x, k, n, H, I))
+        assert _rel(got, g[f"ref_b{bits}"]) < TOL
+        if bits == 4:
+            got1 = _bf16_np(kernels.moe_decode_q4(pool, slots, x, w, n, H, I))
+            assert _rel(got1, g["ref_b4"]) < TOL
+
+
+def _setup(bits, H, I, E, k, G=128, seed=0):
+    from wisp import quant
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    w3 = (torch.randn(E, 3, H * I, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    pool = quant.quantize_batch(w3, bits, G)
+    x = torch.randn(H, device="cuda", generator=gen).to(torch.bfloat16)
+    perm = torch.randperm(E, device="cuda", generator=gen)[:k]
+    wts = torch.softmax(torch.randn(k, device="cuda", generator=gen), 0).to(torch.bfloat16).float()
+    return pool, x, perm, wts
+
+
+@pytest.mark.parametrize("bits", [4, 3, 2, 8])
+def test_full_shape_vs_oracle(bits):
+    """Qwen3-30B-A3B layer shape: H=2048, I=768, top-8 of 16 resident experts."""
+    from wisp import kernels
+
+    H, I, E, k = 2048, 768, 16, 8
+    n = H * I
+    pool, x, slots, wts = _setup(bits, H, I, E, k, seed=bits)
+    meta = torch.cat([slots.float(), wts])
+    out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits)
+    ref = O.moe_decode_ref(pool.cpu().numpy(), slots.cpu().numpy(), _bf16_np(x), wts.cpu().numpy(), n, H, I, bits)
+    err = _rel(_bf16_np(out), ref)
+    assert err < TOL, err
+    # sabotage control: a wrong expert set must miss by far more than the tolerance
+    bad = torch.cat([((slots + 1) % E).float(), wts])
+    err_bad = _rel(_bf16_np(kernels.moe_decode_fast(pool, bad, x, k, n, H, I, bits)), ref)
+    assert err_bad > 10 * TOL, err_bad
+
+
+@pytest.mark.parametrize("H,I,k,G", [(256, 128, 3, 128), (64, 32, 2, 32), (4096, 1024, 4, 128), (2048, 768, 1, 64)])
+def test_other_shapes(H, I, k, G):
+    from wisp import kernels
+
+    bits = 4
+    n = H * I
+    pool, x, slots, wts = _setup(bits, H, I, max(k, 4), k, G=G, seed=H + k)
+    meta = torch.cat([slots.float(), wts])
+    out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, G)
+    ref = O.moe_decode_ref(pool.cpu().numpy(), slots.cpu().numpy(), _bf16_np(x), wts.cpu().numpy(), n, H, I, bits, G)
+    assert _rel(_bf16_np(out), ref) < TOL
+
+
+def test_bad_slot_flagged_and_skipped():
+    """An out-of-range slot id is skipped (contributes nothing) and flagged; no fault."""
+    from wisp import _lib, kernels
+
+    H, I, E, k = 256, 128, 4, 2
+    n = H * I
+    pool, x, slots, wts = _setup(4, H, I, E, k, seed=9)
+    _lib.device_status(0, clear=True)
+    meta = torch.tensor([float(slots[0]), 1e6, float(wts[0]), float(wts[1])], device="cuda")
+    out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, 4)
+    assert _lib.device_status(0) & _lib.STATUS_BAD_SLOT
+    only0 = O.moe_decode_ref(pool.cpu().numpy(), slots[:1].cpu().numpy(), _bf16_np(x), wts[:1].cpu().numpy(), n, H, I, 4)
+    assert _rel(_bf16_np(out), only0) < TOL
+
+
+def test_graph_capture_replays_with_new_routing():
+    """Routing lives in a device buffer, so a captured launch follows new slots/weights on replay."""
+    from wisp import kernels
+
+    H, I, E, k, bits = 2048, 768, 12, 8, 4
+    n = H * I
+    pool, x, slots, wts = _setup(bits, H, I, E, k, seed=21)
+    meta = torch.cat([slots.float(), wts])
+    kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits)  # warm-up outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits)
+    for seed in (1, 2):
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        s2 = torch.randperm(E, device="cuda", generator=gen)[:k]
+        meta.copy_(torch.cat([s2.float(), wts]))
+        g.replay()
+        torch.cuda.synchronize()
+        ref = O.moe_decode_ref(pool.cpu().numpy(), s2.cpu().numpy(), _bf16_np(x), wts.cpu().numpy(), n, H, I, bits)
+        assert _rel(_bf16_np(out), ref) < TOL

@@ -1,0 +1,202 @@
+// Fused group-wise dequant + GEMV over the top-k routed experts of one decode token, read straight
+// from the packed slot pool.  Two phases:
+//   gate/up : a[j, r]  = silu(s.(q_g . x) + m.sum(x)) * (s.(q_u . x) + m.sum(x))     (per group)
+//   down    : out[h]   = sum_j w_j * sum_groups (s.(q_d . a_j) + m.sum(a_j))
+// The dequant is folded into the dot products (sum_i (q_i s + m) x_i = s (q . x) + m sum x), so no
+// bf16 weight is ever materialised; the codes are unpacked in registers from 128-bit streaming loads.
+#pragma once
+#include "common.cuh"
+
+namespace wisp {
+
+struct MoeShape {
+  int64_t nslots, nbytes;
+  int k, H, I, group;
+  int64_t ncode;      // bytes of the code region
+  int64_t ng;         // groups per expert
+  int64_t mat_bytes;  // code bytes per matrix
+};
+
+__device__ __forceinline__ bool route_slot(const float* meta, int j, const MoeShape& S, int64_t& slot) {
+  const float f = meta[j];
+  if (!(f >= 0.0f) || f >= float(S.nslots)) return false;
+  slot = int64_t(f);
+  return true;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// grid (ceil(I / (8*RPW)), k); 8 warps; a warp owns RPW consecutive rows r of expert j (gate row r and
+// up row r together, so SwiGLU is applied in registers).  Lane l owns units l, l+32, ... of a row.
+template <int BITS, int UPL, int RPW>
+__global__ void __launch_bounds__(256) moe_gate_up_kernel(const uint8_t* __restrict__ pool,
+                                                          const float* __restrict__ meta,
+                                                          const uint16_t* __restrict__ x, MoeShape S,
+                                                          float* __restrict__ a_out) {
+  const int j = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * 8 + warp) * RPW;
+  if (row0 >= S.I) return;
+  int64_t slot;
+  if (!route_slot(meta, j, S, slot)) {
+    if (lane < RPW && row0 + lane < S.I) a_out[int64_t(j) * S.I + row0 + lane] = 0.0f;
+    if (lane == 0 && row0 == 0) flag(WISP_STATUS_BAD_SLOT);
+    return;
+  }
+  const int U = S.H / 32;
+  const int GPR = S.H / S.group;
+  const int64_t row_bytes = int64_t(S.H) * BITS / 8;
+  const uint8_t* base = pool + slot * S.nbytes;
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + S.ncode);
+  const uint16_t* mn = sc + S.ng;
+  const int64_t ngm = S.ng / 3;
+
+  // issue every weight load of this warp first (codes + scales), then fetch x and compute
+  Unit<BITS> cg[RPW][UPL], cu[RPW][UPL];
+  uint16_t sg[RPW][UPL], mg[RPW][UPL], su[RPW][UPL], mu[RPW][UPL];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int row = min(row0 + r, S.I - 1);
+#pragma unroll
+    for (int t = 0; t < UPL; ++t) {
+      const int u = min(lane + 32 * t, U - 1);
+      const uint8_t* p = base + row * row_bytes + u * (4 * BITS);
+      cg[r][t] = load_unit<BITS>(p);
+      cu[r][t] = load_unit<BITS>(p + S.mat_bytes);
+      const int64_t gi = int64_t(row) * GPR + (u * 32) / S.group;
+      sg[r][t] = ld_nc_u16(sc + gi);
+      mg[r][t] = ld_nc_u16(mn + gi);
+      su[r][t] = ld_nc_u16(sc + ngm + gi);
+      mu[r][t] = ld_nc_u16(mn + ngm + gi);
+    }
+  }
+  float xv[UPL][32], xs[UPL];
+#pragma unroll
+  for (int t = 0; t < UPL; ++t) {
+    const int u = min(lane + 32 * t, U - 1);
+    const uint4* xp = reinterpret_cast<const uint4*>(x + u * 32);
+    float s = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint4 q = xp[v];
+      uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        xv[t][8 * v + 2 * h] = __uint_as_float(wds[h] << 16);
+        xv[t][8 * v + 2 * h + 1] = __uint_as_float(wds[h] & 0xFFFF0000u);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) s += xv[t][i];
+    xs[t] = s;
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    float accg = 0.0f, accu = 0.0f;
+#pragma unroll
+    for (int t = 0; t < UPL; ++t) {
+      if (lane + 32 * t < U) {
+        float dg = 0.0f, du = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          dg = fmaf(small_u2f(unit_code<BITS>(cg[r][t], i)), xv[t][i], dg);
+          du = fmaf(small_u2f(unit_code<BITS>(cu[r][t], i)), xv[t][i], du);
+        }
+        accg += f16_bits_to_f32(sg[r][t]) * dg + f16_bits_to_f32(mg[r][t]) * xs[t];
+        accu += f16_bits_to_f32(su[r][t]) * du + f16_bits_to_f32(mu[r][t]) * xs[t];
+      }
+    }
+    accg = warp_sum(accg);
+    accu = warp_sum(accu);
+    if (lane == 0 && row0 + r < S.I) a_out[int64_t(j) * S.I + row0 + r] = silu_mul(accg, accu);
+  }
+}
+
+// grid ceil(H / 8); 8 warps; warp w owns output row h and walks all k experts, so the weighted
+// combine happens in registers and out[h] is written once.  a (fp32 [k, I]) is staged in shared memory
+// transposed per unit ([k][32][UP], UP odd) so lane l reading element i of unit l is conflict free.
+template <int BITS, int UPL>
+__global__ void __launch_bounds__(256) moe_down_kernel(const uint8_t* __restrict__ pool,
+                                                       const float* __restrict__ meta,
+                                                       const float* __restrict__ a, MoeShape S,
+                                                       uint16_t* __restrict__ out) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int U = S.I / 32, UP = U | 1;
+  float* at = sm;                          // [k][32][UP]
+  float* as = sm + S.k * 32 * UP;          // [k][U] unit sums
+  const int h = blockIdx.x * 8 + warp;
+  const int GPR = S.I / S.group;
+  const int64_t row_bytes = int64_t(S.I) * BITS / 8;
+  const int64_t ngm = S.ng / 3;
+  float acc = 0.0f;
+  for (int j0 = 0; j0 < S.k; j0 += 8) {
+    // issue this chunk's weight loads before waiting on anything
+    Unit<BITS> cd[8][UPL];
+    uint16_t sd[8][UPL], md[8][UPL];
+    bool ok[8];
+    float wj[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const int j = j0 + jj;
+      int64_t slot = 0;
+      ok[jj] = j < S.k && h < S.H && route_slot(meta, j, S, slot);
+      wj[jj] = j < S.k ? meta[S.k + j] : 0.0f;
+      const uint8_t* base = pool + slot * S.nbytes;
+      const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + S.ncode);
+      const uint16_t* mn = sc + S.ng;
+#pragma unroll
+      for (int t = 0; t < UPL; ++t) {
+        const int u = min(lane + 32 * t, U - 1);
+        if (ok[jj]) {
+          cd[jj][t] = load_unit<BITS>(base + 2 * S.mat_bytes + h * row_bytes + u * (4 * BITS));
+          const int64_t gi = 2 * ngm + int64_t(h) * GPR + (u * 32) / S.group;
+          sd[jj][t] = ld_nc_u16(sc + gi);
+          md[jj][t] = ld_nc_u16(mn + gi);
+        }
+      }
+    }
+    if (j0 == 0) {
+      // stage a (all experts) while the weight loads are in flight
+      for (int idx = threadIdx.x; idx < S.k * S.I; idx += blockDim.x) {
+        const int j = idx / S.I, e = idx - j * S.I;
+        at[(j * 32 + (e & 31)) * UP + (e >> 5)] = a[idx];
+      }
+      for (int idx = threadIdx.x; idx < S.k * U; idx += blockDim.x) {
+        const int j = idx / U, u = idx - j * U;
+        const float* ap = a + int64_t(j) * S.I + u * 32;
+        float s = 0.0f;
+        for (int i = 0; i < 32; ++i) s += ap[i];
+        as[idx] = s;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      if (!ok[jj]) continue;
+      const int j = j0 + jj;
+#pragma unroll
+      for (int t = 0; t < UPL; ++t) {
+        const int u = lane + 32 * t;
+        if (u < U) {
+          const float* ap = at + j * 32 * UP + u;
+          float d = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) d = fmaf(small_u2f(unit_code<BITS>(cd[jj][t], i)), ap[i * UP], d);
+          acc += wj[jj] * (f16_bits_to_f32(sd[jj][t]) * d + f16_bits_to_f32(md[jj][t]) * as[j * U + u]);
+        }
+      }
+    }
+  }
+  if (lane == 0 && threadIdx.x == 0) {
+    // one thread per block reports routing errors (cheap, idempotent)
+    for (int j = 0; j < S.k; ++j) {
+      int64_t slot;
+      if (!route_slot(meta, j, S, slot)) flag(WISP_STATUS_BAD_SLOT);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0 && h < S.H) out[h] = f32_to_bf16(acc);
+}
+
+}  // namespace wisp

@@ -1,0 +1,240 @@
+// libwisp_b200.so: the C ABI declared in include/wisp_b200.h.  One translation unit (the kernels live
+// in the included .cuh files) so the per-device status word is a single __device__ symbol.
+#include "common.cuh"
+#include "decode_ops.cuh"
+#include "moe_decode.cuh"
+#include "quant.cuh"
+
+namespace wisp {
+
+std::string& last_error_slot() {
+  static thread_local std::string s;
+  return s;
+}
+
+static int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+static int64_t grid_for(int64_t work, int threads, int per_sm = 8) {
+  int64_t g = (work + threads - 1) / threads;
+  const int64_t cap = int64_t(sm_count()) * per_sm;
+  if (g > cap) g = cap;
+  return g < 1 ? 1 : g;
+}
+
+static bool valid_bits(int b) { return b == 16 || b == 8 || b == 4 || b == 3 || b == 2; }
+
+}  // namespace wisp
+
+using namespace wisp;
+
+extern "C" {
+
+int wisp_version(void) { return 100; }
+
+const char* wisp_last_error(void) { return last_error_slot().c_str(); }
+
+int wisp_device_status(int device, int clear, uint32_t* status_host) {
+  WISP_REQUIRE(status_host != nullptr, "wisp_device_status: status_host is NULL");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+  unsigned int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+  if (e == cudaSuccess && clear) {
+    unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_status, &z, sizeof(z));
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_device_status: %s", cudaGetErrorString(e));
+  *status_host = v;
+  return WISP_OK;
+}
+
+int64_t wisp_expert_nbytes(int64_t n, int bits, int group) {
+  if (n <= 0 || !valid_bits(bits)) return -1;
+  if (bits == 16) return 3 * n * 2;
+  if (group <= 0 || (3 * n) % group != 0 || (3 * n * bits) % 8 != 0) return -1;
+  return (3 * n * bits) / 8 + 4 * (3 * n / group);
+}
+
+int wisp_quantize(const void* w3, int w_dtype, int64_t batch, int64_t n, int bits, int group, uint8_t* out,
+                  void* stream) {
+  WISP_REQUIRE(w3 && out, "wisp_quantize: NULL pointer");
+  WISP_REQUIRE(batch >= 0, "wisp_quantize: negative batch");
+  if (batch == 0) return WISP_OK;
+  WISP_REQUIRE(w_dtype == WISP_DTYPE_F32 || w_dtype == WISP_DTYPE_BF16, "wisp_quantize: w_dtype must be F32 or BF16");
+  const int64_t nb = wisp_expert_nbytes(n, bits, group);
+  WISP_REQUIRE(nb > 0, "wisp_quantize: invalid shape n=%lld bits=%d group=%d", (long long)n, bits, group);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bits == 16) {
+    const int64_t cnt = batch * 3 * n;
+    if (w_dtype == WISP_DTYPE_F32)
+      to_bf16_kernel<float><<<grid_for(cnt, 256), 256, 0, s>>>(static_cast<const float*>(w3), cnt, reinterpret_cast<uint16_t*>(out));
+    else
+      to_bf16_kernel<uint16_t><<<grid_for(cnt, 256), 256, 0, s>>>(static_cast<const uint16_t*>(w3), cnt, reinterpret_cast<uint16_t*>(out));
+    return check_launch("quantize(16)");
+  }
+  WISP_REQUIRE(group % 8 == 0, "wisp_quantize: group must be a multiple of 8 (got %d)", group);
+  if ((3 * n * bits / 8) % 2 != 0)
+    return fail(WISP_ERR_UNSUPPORTED, "wisp_quantize: the code region (3*n*bits/8 bytes) must be even so the fp16 scales stay aligned");
+  WISP_REQUIRE(aligned(out, 8) && (batch == 1 || nb % 8 == 0), "wisp_quantize: out rows must be 8-byte aligned");
+  const int64_t ngroups = 3 * n / group;
+  const int64_t ncode = 3 * n * bits / 8;
+  const int64_t grid = (batch * ngroups * 32 + 255) / 256;
+#define WISP_Q(B)                                                                                           \
+  if (w_dtype == WISP_DTYPE_F32)                                                                            \
+    quantize_kernel<B, float><<<grid, 256, 0, s>>>(static_cast<const float*>(w3), batch, ngroups, group, out, ncode, nb); \
+  else                                                                                                      \
+    quantize_kernel<B, uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(w3), batch, ngroups, group, out, ncode, nb);
+  switch (bits) {
+    case 8: WISP_Q(8) break;
+    case 4: WISP_Q(4) break;
+    case 3: WISP_Q(3) break;
+    case 2: WISP_Q(2) break;
+  }
+#undef WISP_Q
+  return check_launch("quantize");
+}
+
+static int unpack_common(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, const int64_t* rows, int64_t nrows,
+                         int64_t n, int bits, int group, void* out, int mode, void* stream) {
+  WISP_REQUIRE(pool && out, "NULL pointer");
+  WISP_REQUIRE(nrows >= 0 && pool_rows >= 0, "negative row count");
+  if (mode == 0) {
+    const int64_t nb = wisp_expert_nbytes(n, bits, group);
+    WISP_REQUIRE(nb > 0 && nb == nbytes, "nbytes=%lld does not match n=%lld bits=%d group=%d (expected %lld)",
+                 (long long)nbytes, (long long)n, bits, group, (long long)nb);
+  } else {
+    WISP_REQUIRE(n > 0 && nbytes >= 3 * n * bits / 8, "nbytes=%lld smaller than the code region", (long long)nbytes);
+    group = 32;  // unused for codes
+  }
+  WISP_REQUIRE(aligned(pool, 16) && nbytes % 16 == 0, "pool must be 16-byte aligned with nbytes a multiple of 16");
+  WISP_REQUIRE(aligned(out, 16), "out must be 16-byte aligned");
+  if (nrows == 0) return WISP_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bits == 16) {
+    WISP_REQUIRE(mode == 0, "16-bit experts have no codes");
+    gather_rows_kernel<<<grid_for(nrows * nbytes / 16, 256), 256, 0, s>>>(pool, pool_rows, nbytes, rows, nrows,
+                                                                          static_cast<uint8_t*>(out));
+    return check_launch("dequant(16)");
+  }
+  if (n % 32 != 0) return fail(WISP_ERR_UNSUPPORTED, "n must be a multiple of 32 (got %lld)", (long long)n);
+  const int64_t work = nrows * (3 * n / 32);
+  const int64_t grid = grid_for(work, 256);
+#define WISP_U(B)                                                                                                \
+  if (mode == 0)                                                                                                 \
+    unpack_kernel<B, 0><<<grid, 256, 0, s>>>(pool, pool_rows, nbytes, rows, nrows, n, group, out);               \
+  else                                                                                                           \
+    unpack_kernel<B, 1><<<grid, 256, 0, s>>>(pool, pool_rows, nbytes, rows, nrows, n, group, out);
+  switch (bits) {
+    case 8: WISP_U(8) break;
+    case 4: WISP_U(4) break;
+    case 3: WISP_U(3) break;
+    case 2: WISP_U(2) break;
+  }
+#undef WISP_U
+  return check_launch(mode == 0 ? "dequant" : "unpack_codes");
+}
+
+int wisp_dequant(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, const int64_t* rows, int64_t nrows, int64_t n,
+                 int bits, int group, uint16_t* out_bf16, void* stream) {
+  return unpack_common(pool, pool_rows, nbytes, rows, nrows, n, bits, group, out_bf16, 0, stream);
+}
+
+int wisp_unpack_codes(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, const int64_t* rows, int64_t nrows,
+                      int64_t n, int bits, uint8_t* codes, void* stream) {
+  WISP_REQUIRE(bits != 16, "wisp_unpack_codes: 16-bit experts have no codes");
+  return unpack_common(pool, pool_rows, nbytes, rows, nrows, n, bits, 32, codes, 1, stream);
+}
+
+int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k, const uint16_t* x,
+                    int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream) {
+  WISP_REQUIRE(pool && meta && x && scratch && out, "wisp_moe_decode: NULL pointer");
+  WISP_REQUIRE(bits == 8 || bits == 4 || bits == 3 || bits == 2, "wisp_moe_decode: bits must be 8, 4, 3 or 2 (got %d)", bits);
+  WISP_REQUIRE(k >= 1 && k <= 64, "wisp_moe_decode: k must be in [1, 64] (got %d)", k);
+  WISP_REQUIRE(group > 0 && group % 32 == 0, "wisp_moe_decode: group must be a positive multiple of 32 (got %d)", group);
+  WISP_REQUIRE(H > 0 && I > 0 && H % group == 0 && I % group == 0,
+               "wisp_moe_decode: H and I must be multiples of group (H=%lld I=%lld group=%d)", (long long)H, (long long)I, group);
+  const int64_t n = H * I;
+  const int64_t nb = wisp_expert_nbytes(n, bits, group);
+  WISP_REQUIRE(nb == nbytes, "wisp_moe_decode: nbytes=%lld, expected %lld", (long long)nbytes, (long long)nb);
+  WISP_REQUIRE(aligned(pool, 16) && nbytes % 16 == 0, "wisp_moe_decode: pool must be 16-byte aligned, nbytes % 16 == 0");
+  WISP_REQUIRE(aligned(x, 16), "wisp_moe_decode: x must be 16-byte aligned");
+  WISP_REQUIRE(H <= 4096 && I <= 4096, "wisp_moe_decode: H and I up to 4096 are supported");
+  MoeShape S;
+  S.nslots = nslots;
+  S.nbytes = nbytes;
+  S.k = k;
+  S.H = int(H);
+  S.I = int(I);
+  S.group = group;
+  S.ncode = 3 * n * bits / 8;
+  S.ng = 3 * n / group;
+  S.mat_bytes = n * bits / 8;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int upl_gu = int((H / 32 + 31) / 32);  // 1, 2 (H <= 2048) or up to 4
+  const int upl_dn = int((I / 32 + 31) / 32);
+  const int UP = int(I / 32) | 1;
+  const size_t smem = size_t(k) * 32 * UP * 4 + size_t(k) * (I / 32) * 4;
+  WISP_REQUIRE(smem <= 200 * 1024, "wisp_moe_decode: k*I too large for the shared-memory stage");
+  constexpr int RPW = 2;
+  dim3 g1((unsigned)((I + 8 * RPW - 1) / (8 * RPW)), (unsigned)k);
+  dim3 g2((unsigned)((H + 7) / 8));
+#define WISP_GU(B, U) moe_gate_up_kernel<B, U, RPW><<<g1, 256, 0, s>>>(pool, meta, x, S, scratch)
+#define WISP_DN(B, U)                                                                                   \
+  do {                                                                                                  \
+    auto kern = moe_down_kernel<B, U>;                                                                  \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+    kern<<<g2, 256, smem, s>>>(pool, meta, scratch, S, out);                                            \
+  } while (0)
+#define WISP_BITS(B)                                   \
+  {                                                    \
+    if (upl_gu <= 1) WISP_GU(B, 1);                    \
+    else if (upl_gu <= 2) WISP_GU(B, 2);               \
+    else WISP_GU(B, 4);                                \
+    int rc = check_launch("moe_decode gate/up");       \
+    if (rc) return rc;                                 \
+    if (upl_dn <= 1) WISP_DN(B, 1);                    \
+    else if (upl_dn <= 2) WISP_DN(B, 2);               \
+    else WISP_DN(B, 4);                                \
+  }
+  switch (bits) {
+    case 8: WISP_BITS(8) break;
+    case 4: WISP_BITS(4) break;
+    case 3: WISP_BITS(3) break;
+    case 2: WISP_BITS(2) break;
+  }
+#undef WISP_BITS
+#undef WISP_GU
+#undef WISP_DN
+  return check_launch("moe_decode down");
+}
+
+int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t* k, int64_t k_stride, int Hk, int D,
+                     const uint16_t* cos, const uint16_t* sin, uint16_t* qo, uint16_t* ko, void* stream) {
+  WISP_REQUIRE(q && k && cos && sin && qo && ko, "wisp_rope_decode: NULL pointer");
+  WISP_REQUIRE(Hq > 0 && Hk >= 0 && D > 0 && D % 2 == 0, "wisp_rope_decode: bad shape");
+  const int heads = Hq + Hk;
+  const int warps = 4;
+  rope_decode_kernel<<<(heads + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, q_stride, Hq, k, k_stride, Hk, D, cos, sin, qo, ko);
+  return check_launch("rope_decode");
+}
+
+int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, const uint16_t* w, int64_t rows, int64_t H,
+                 float eps, uint16_t* out, void* stream) {
+  WISP_REQUIRE(x && w && out, "wisp_rmsnorm: NULL pointer");
+  WISP_REQUIRE(rows >= 0 && H > 0 && H <= 16384, "wisp_rmsnorm: bad shape");
+  if (rows == 0) return WISP_OK;
+  const size_t smem = size_t(H) * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  rmsnorm_kernel<<<(unsigned)rows, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
+  return check_launch("rmsnorm");
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+"""ctypes binding of libwisp_b200.so (the C ABI in include/wisp_b200.h).
+
+There is no fallback: if the library is missing or a call fails, a WispError is raised.  The library
+loads without a GPU (its host-only entry points work on CPU machines); every compute entry point needs
+CUDA device pointers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("WISP_B200_LIB", os.path.join(os.path.dirname(_HERE), "lib", "libwisp_b200.so"))
+
+WISP_OK, WISP_ERR_INVALID, WISP_ERR_CUDA, WISP_ERR_UNSUPPORTED = 0, 1, 2, 3
+STATUS_BAD_SLOT, STATUS_BAD_POS, STATUS_WAIT_TIMEOUT, STATUS_BAD_ROUTE = 0x1, 0x2, 0x4, 0x8
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_F = ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/wisp_b200.h one to one
+SIGNATURES = {
+    "wisp_version": (_I, []),
+    "wisp_last_error": (ctypes.c_char_p, []),
+    "wisp_device_status": (_I, [_I, _I, ctypes.POINTER(ctypes.c_uint32)]),
+    "wisp_expert_nbytes": (_L, [_L, _I, _I]),
+    "wisp_quantize": (_I, [_P, _I, _L, _L, _I, _I, _P, _P]),
+    "wisp_dequant": (_I, [_P, _L, _L, _P, _L, _L, _I, _I, _P, _P]),
+    "wisp_unpack_codes": (_I, [_P, _L, _L, _P, _L, _L, _I, _P, _P]),
+    "wisp_moe_decode": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _P]),
+    "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
+    "wisp_rmsnorm": (_I, [_P, _P, _P, _P, _L, _L, _F, _P, _P]),
+}
+
+
+class WispError(RuntimeError):
+    """A libwisp_b200 entry point returned an error code."""
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise WispError(
+                f"{LIB_PATH} is missing: build it with `python wisp-runtime_b200/build.py` "
+                "(there is no fallback implementation)"
+            )
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def check(name: str, rc: int) -> None:
+    if rc != WISP_OK:
+        msg = lib().wisp_last_error().decode(errors="replace")
+        raise WispError(f"{name} failed ({rc}): {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(name, getattr(lib(), name)(*args))
+
+
+def device_status(device: int = 0, clear: bool = True) -> int:
+    """Read (and by default clear) the device-side status word (WISP_STATUS_* bits).  Synchronises."""
+    v = ctypes.c_uint32(0)
+    call("wisp_device_status", device, 1 if clear else 0, ctypes.byref(v))
+    return int(v.value)

@@ -1,0 +1,161 @@
+"""Drop-in for the reference ``wisp.kernels`` (wisp/kernels.py): the same entry points and argument
+meaning, computed by hand-written sm_100a CUDA kernels in libwisp_b200.so.
+
+    moe_decode_q4(pool, slots, x, w, n, H, I, group=128, ...)       wisp/kernels.py:115-137
+    moe_decode_q4_fast(pool, meta, x, k, n, H, I, group=128, ...)   wisp/kernels.py:188-203
+    moe_decode_q3_fast(pool, meta, x, k, n, H, I, group=128, ...)   wisp/kernels.py:310-322
+    moe_decode_q2_fast(pool, meta, x, k, n, H, I, group=128, ...)   (new: the reference has no 2-bit kernel)
+    rope_decode(q, k, cos, sin)                                      wisp/kernels.py:352-371
+
+The Triton tuning keywords (block_r, block_gu, block_down, num_warps) are accepted and ignored.
+Outputs and the fp32 intermediate are allocated with torch.empty on the caller's stream, so every call
+can be captured in a CUDA graph.  Preconditions raise AssertionError like the reference; a kernel-side
+failure raises WispError.  There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import WispError
+
+__all__ = [
+    "moe_decode_q4",
+    "moe_decode_q4_fast",
+    "moe_decode_q3_fast",
+    "moe_decode_q2_fast",
+    "moe_decode_fast",
+    "rope_decode",
+    "rmsnorm",
+    "WispError",
+]
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise WispError("wisp kernels need CUDA tensors (there is no CPU path)")
+
+
+def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratch=None):
+    """Fused dequant + GEMV MoE of one token over the k experts named by ``meta`` (fp32 [2k] =
+    [slots..., weights...]).  pool: uint8 [nslots, nbytes]; x: bf16 [H].  Returns bf16 [H]."""
+    assert H % group == 0 and I % group == 0 and n == H * I
+    _need_cuda(pool, meta, x)
+    assert pool.dtype == torch.uint8 and pool.dim() == 2 and pool.is_contiguous()
+    assert meta.dtype == torch.float32 and meta.numel() >= 2 * k and meta.is_contiguous()
+    if x.dtype != torch.bfloat16:
+        raise WispError(f"x must be bfloat16 (got {x.dtype})")
+    x = x.contiguous()
+    if scratch is None:
+        scratch = torch.empty((k, I), dtype=torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty((H,), dtype=x.dtype, device=x.device)
+    _lib.call(
+        "wisp_moe_decode",
+        pool.data_ptr(),
+        pool.shape[0],
+        pool.shape[1],
+        meta.data_ptr(),
+        k,
+        x.data_ptr(),
+        H,
+        I,
+        bits,
+        group,
+        scratch.data_ptr(),
+        out.data_ptr(),
+        _stream(x),
+    )
+    return out
+
+
+def moe_decode_q4_fast(pool, meta, x, k, n, H, I, group=128, block_gu=32, block_down=8, num_warps=4):
+    """4-bit fused MoE decode (2 launches), meta = fp32 [slot_0..slot_{k-1}, w_0..w_{k-1}].
+    Reference: wisp/kernels.py:188-203."""
+    return moe_decode_fast(pool, meta, x, k, n, H, I, 4, group)
+
+
+def moe_decode_q3_fast(pool, meta, x, k, n, H, I, group=128, block_gu=8, block_down=8, num_warps=4):
+    """3-bit twin of moe_decode_q4_fast.  Reference: wisp/kernels.py:310-322."""
+    return moe_decode_fast(pool, meta, x, k, n, H, I, 3, group)
+
+
+def moe_decode_q2_fast(pool, meta, x, k, n, H, I, group=128, block_gu=8, block_down=8, num_warps=4):
+    """2-bit fused MoE decode; the reference runs 2-bit experts through dequant + bmm
+    (wisp/moe.py:122-130), this is the same math fused."""
+    return moe_decode_fast(pool, meta, x, k, n, H, I, 2, group)
+
+
+def moe_decode_q4(pool, slots, x, w, n, H, I, group=128, block_r=32, num_warps=4):
+    """pool uint8 [nslots, nbytes] (4-bit experts); slots int64 [k]; x [H] bf16; w [k] routing weights.
+    Returns [H] in x.dtype.  Reference: wisp/kernels.py:115-137."""
+    assert H % group == 0 and I % group == 0 and n == H * I
+    _need_cuda(pool, slots, x, w)
+    k = slots.numel()
+    meta = torch.cat([slots.reshape(-1).to(torch.float32), w.reshape(-1).to(torch.float32)])
+    return moe_decode_fast(pool, meta, x, k, n, H, I, 4, group)
+
+
+def rope_decode(q, k, cos, sin):
+    """q: [1,Hq,1,D], k: [1,Hk,1,D] bf16 (any head stride, e.g. HF's transposed views), cos/sin [1,1,D]
+    -> rotated (qo, ko), contiguous, same shapes.  Reference: wisp/kernels.py:352-371."""
+    _need_cuda(q, k, cos, sin)
+    Hq, D = q.shape[1], q.shape[3]
+    Hk = k.shape[1]
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise WispError("rope_decode: q and k must be bfloat16")
+    assert q.stride(3) == 1 and k.stride(3) == 1, "rope_decode: the head dimension must be contiguous"
+    cos = cos.reshape(-1).to(torch.bfloat16).contiguous()
+    sin = sin.reshape(-1).to(torch.bfloat16).contiguous()
+    qo = torch.empty((1, Hq, 1, D), dtype=q.dtype, device=q.device)
+    ko = torch.empty((1, Hk, 1, D), dtype=k.dtype, device=k.device)
+    _lib.call(
+        "wisp_rope_decode",
+        q.data_ptr(),
+        q.stride(1),
+        Hq,
+        k.data_ptr(),
+        k.stride(1),
+        Hk,
+        D,
+        cos.data_ptr(),
+        sin.data_ptr(),
+        qo.data_ptr(),
+        ko.data_ptr(),
+        _stream(q),
+    )
+    return qo, ko
+
+
+def rmsnorm(x, weight, eps=1e-6, delta=None, sum_out=None, out=None):
+    """weight * rms_norm(x) over the last dim (the patched Qwen3MoeRMSNorm, wisp/model.py:101-102),
+    optionally with the residual add fused: x := x + delta (written to ``sum_out`` when given)."""
+    _need_cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise WispError("rmsnorm: bfloat16 tensors expected")
+    H = x.shape[-1]
+    x = x.contiguous()
+    rows = x.numel() // H
+    if out is None:
+        out = torch.empty_like(x)
+    if delta is not None:
+        delta = delta.contiguous()
+    _lib.call(
+        "wisp_rmsnorm",
+        x.data_ptr(),
+        delta.data_ptr() if delta is not None else None,
+        sum_out.data_ptr() if sum_out is not None else None,
+        weight.contiguous().data_ptr(),
+        rows,
+        H,
+        float(eps),
+        out.data_ptr(),
+        _stream(x),
+    )
+    return out
