@@ -40,7 +40,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
-    return ap.parse_args()
+    ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the model; fewer = a small ncu case)")
+    a = ap.parse_args()
+    global L
+    L = a.layers
+    return a
 
 
 def metric_name():
@@ -214,7 +218,7 @@ class MoEStack:
         out_host.copy_(self.h, non_blocking=True)
 
 
-def time_moe_kernel(W, reps=20):
+def time_moe_kernel(W, reps=20, variant=0):
     """Average duration of one fused MoE decode call (gate/up + down kernels), rotated over the 48
     layers' distinct experts (962 MB per sweep), measured with CUDA events on the launching stream."""
     import torch
@@ -228,7 +232,9 @@ def time_moe_kernel(W, reps=20):
 
     def sweep():
         for l in range(L):
-            kernels.moe_decode_fast(W["pool"], W["meta"][0, l], x[l], K_TOP, W["n"], H, I, W["bits"], G, out=out[l], scratch=scratch)
+            kernels.moe_decode_fast(
+                W["pool"], W["meta"][0, l], x[l], K_TOP, W["n"], H, I, W["bits"], G, out=out[l], scratch=scratch, variant=variant
+            )
 
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -388,6 +394,7 @@ def main():
     clk = clocks.stop()
     # roofline of the fused MoE decode (algorithmic bytes: 8 experts + x + out per call)
     per_call_ms = time_moe_kernel(W)
+    v1_ms = time_moe_kernel(W, variant=1)
     alg_bytes = K_TOP * W["nbytes"] + 2 * H * 2
     achieved = alg_bytes / (per_call_ms * 1e-3) / 1e9
     peak, peak_kind = load_peaks()
@@ -429,6 +436,7 @@ def main():
                 "kernel": "wisp_moe_decode (gate/up + down)",
                 "bytes_per_call": alg_bytes,
                 "us_per_call": per_call_ms * 1e3,
+                "us_per_call_warp_per_row_variant": v1_ms * 1e3,
                 "peak_source": peak_kind,
             },
             "cpu_baseline": {

@@ -84,6 +84,14 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
                     const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out,
                     void* stream);
 
+/* Same computation with an explicit kernel choice: 0 = automatic (what wisp_moe_decode does),
+ * 1 = warp-per-row kernels (any supported shape), 2 = persistent one-CTA-per-SM kernels streaming each
+ * CTA's rows into shared memory with bulk copies, chained with programmatic dependent launch
+ * (bits 4/3/2, H and I up to 2048, 16-byte aligned row and matrix sizes; WISP_ERR_UNSUPPORTED otherwise). */
+int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
+                            const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,
+                            uint16_t* out, int variant, void* stream);
+
 /* ---- decode-side ops ---------------------------------------------------------------------------- */
 /* Rotate-half RoPE for one token: q [Hq, D] (head stride q_stride elements), k [Hk, D] (k_stride),
  * cos/sin bf16 [D]; writes contiguous qo [Hq, D], ko [Hk, D].  fp32 math, one rounding to bf16.

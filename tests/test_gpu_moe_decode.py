@@ -53,36 +53,75 @@ def _setup(bits, H, I, E, k, G=128, seed=0):
     return pool, x, perm, wts
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("bits", [4, 3, 2, 8])
-def test_full_shape_vs_oracle(bits):
-    """Qwen3-30B-A3B layer shape: H=2048, I=768, top-8 of 16 resident experts."""
+def test_full_shape_vs_oracle(bits, variant):
+    """Qwen3-30B-A3B layer shape: H=2048, I=768, top-8 of 16 resident experts, every kernel variant
+    (0 = automatic choice, 1 = warp-per-row, 2 = persistent bulk-copy; 8-bit has no variant 2)."""
     from wisp import kernels
 
+    if bits == 8 and variant == 2:
+        pytest.skip("8-bit rows do not fit the variant-2 shared-memory stage")
     H, I, E, k = 2048, 768, 16, 8
     n = H * I
     pool, x, slots, wts = _setup(bits, H, I, E, k, seed=bits)
     meta = torch.cat([slots.float(), wts])
-    out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits)
+    out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=variant)
     ref = O.moe_decode_ref(pool.cpu().numpy(), slots.cpu().numpy(), _bf16_np(x), wts.cpu().numpy(), n, H, I, bits)
     err = _rel(_bf16_np(out), ref)
     assert err < TOL, err
     # sabotage control: a wrong expert set must miss by far more than the tolerance
     bad = torch.cat([((slots + 1) % E).float(), wts])
-    err_bad = _rel(_bf16_np(kernels.moe_decode_fast(pool, bad, x, k, n, H, I, bits)), ref)
+    err_bad = _rel(_bf16_np(kernels.moe_decode_fast(pool, bad, x, k, n, H, I, bits, variant=variant)), ref)
     assert err_bad > 10 * TOL, err_bad
 
 
-@pytest.mark.parametrize("H,I,k,G", [(256, 128, 3, 128), (64, 32, 2, 32), (4096, 1024, 4, 128), (2048, 768, 1, 64)])
-def test_other_shapes(H, I, k, G):
+@pytest.mark.parametrize("bits", [4, 3, 2])
+def test_variants_agree_and_are_deterministic(bits):
+    """Both kernel families compute the same sums (different association order only), and the
+    persistent variant reduces in a fixed order: repeated calls are bit-identical."""
     from wisp import kernels
 
-    bits = 4
+    H, I, E, k = 2048, 768, 16, 8
+    n = H * I
+    pool, x, slots, wts = _setup(bits, H, I, E, k, seed=40 + bits)
+    meta = torch.cat([slots.float(), wts])
+    o1 = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=1))
+    o2 = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=2))
+    assert _rel(o2, o1) < 2e-3
+    for _ in range(3):
+        assert np.array_equal(_bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=2)), o2)
+
+
+@pytest.mark.parametrize("bits", [4, 3, 2])
+@pytest.mark.parametrize(
+    "H,I,k,G", [(256, 128, 3, 128), (64, 32, 2, 32), (4096, 1024, 4, 128), (2048, 768, 1, 64), (1024, 2048, 20, 128)]
+)
+def test_other_shapes(H, I, k, G, bits):
+    """Small, odd and large shapes (k up to 20 > one warp-chunk of experts), automatic variant."""
+    from wisp import kernels
+
     n = H * I
     pool, x, slots, wts = _setup(bits, H, I, max(k, 4), k, G=G, seed=H + k)
     meta = torch.cat([slots.float(), wts])
     out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, G)
     ref = O.moe_decode_ref(pool.cpu().numpy(), slots.cpu().numpy(), _bf16_np(x), wts.cpu().numpy(), n, H, I, bits, G)
     assert _rel(_bf16_np(out), ref) < TOL
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+def test_bad_slot_flagged_and_skipped_per_variant(variant):
+    from wisp import _lib, kernels
+
+    H, I, E, k = 2048, 768, 4, 2
+    n = H * I
+    pool, x, slots, wts = _setup(4, H, I, E, k, seed=19)
+    _lib.device_status(0, clear=True)
+    meta = torch.tensor([float(slots[0]), -3.0, float(wts[0]), float(wts[1])], device="cuda")
+    out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, 4, variant=variant)
+    assert _lib.device_status(0) & _lib.STATUS_BAD_SLOT
+    only0 = O.moe_decode_ref(pool.cpu().numpy(), slots[:1].cpu().numpy(), _bf16_np(x), wts[:1].cpu().numpy(), n, H, I, 4)
+    assert _rel(_bf16_np(out), only0) < TOL
 
 
 def test_bad_slot_flagged_and_skipped():

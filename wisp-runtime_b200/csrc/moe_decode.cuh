@@ -157,16 +157,36 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const uint8_t* __restrict
       }
     }
     if (j0 == 0) {
-      // stage a (all experts) while the weight loads are in flight
-      for (int idx = threadIdx.x; idx < S.k * S.I; idx += blockDim.x) {
-        const int j = idx / S.I, e = idx - j * S.I;
-        at[(j * 32 + (e & 31)) * UP + (e >> 5)] = a[idx];
+      // stage a (all experts) while the weight loads are in flight: four independent 16-byte loads
+      // per thread per round, then the transposed scatter; unit sums are taken from shared memory
+      const float4* a4 = reinterpret_cast<const float4*>(a);
+      const int n4 = S.k * S.I / 4;
+      for (int b0 = threadIdx.x; b0 < n4; b0 += 4 * blockDim.x) {
+        float4 v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int idx = b0 + q * blockDim.x;
+          if (idx < n4) v[q] = a4[idx];
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int idx = b0 + q * blockDim.x;
+          if (idx < n4) {
+            const float vv[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int flat = 4 * idx + c;
+              const int j = flat / S.I, e = flat - j * S.I;
+              at[(j * 32 + (e & 31)) * UP + (e >> 5)] = vv[c];
+            }
+          }
+        }
       }
+      __syncthreads();
       for (int idx = threadIdx.x; idx < S.k * U; idx += blockDim.x) {
         const int j = idx / U, u = idx - j * U;
-        const float* ap = a + int64_t(j) * S.I + u * 32;
         float s = 0.0f;
-        for (int i = 0; i < 32; ++i) s += ap[i];
+        for (int i = 0; i < 32; ++i) s += at[(j * 32 + i) * UP + u];
         as[idx] = s;
       }
       __syncthreads();

@@ -3,6 +3,7 @@
 #include "common.cuh"
 #include "decode_ops.cuh"
 #include "moe_decode.cuh"
+#include "moe_decode_v2.cuh"
 #include "quant.cuh"
 
 namespace wisp {
@@ -152,8 +153,10 @@ int wisp_unpack_codes(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, co
   return unpack_common(pool, pool_rows, nbytes, rows, nrows, n, bits, 32, codes, 1, stream);
 }
 
-int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k, const uint16_t* x,
-                    int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream) {
+}  // extern "C"
+
+static int moe_shape(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k, const uint16_t* x,
+                     int64_t H, int64_t I, int bits, int group, const float* scratch, const uint16_t* out, MoeShape& S) {
   WISP_REQUIRE(pool && meta && x && scratch && out, "wisp_moe_decode: NULL pointer");
   WISP_REQUIRE(bits == 8 || bits == 4 || bits == 3 || bits == 2, "wisp_moe_decode: bits must be 8, 4, 3 or 2 (got %d)", bits);
   WISP_REQUIRE(k >= 1 && k <= 64, "wisp_moe_decode: k must be in [1, 64] (got %d)", k);
@@ -164,9 +167,8 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   const int64_t nb = wisp_expert_nbytes(n, bits, group);
   WISP_REQUIRE(nb == nbytes, "wisp_moe_decode: nbytes=%lld, expected %lld", (long long)nbytes, (long long)nb);
   WISP_REQUIRE(aligned(pool, 16) && nbytes % 16 == 0, "wisp_moe_decode: pool must be 16-byte aligned, nbytes % 16 == 0");
-  WISP_REQUIRE(aligned(x, 16), "wisp_moe_decode: x must be 16-byte aligned");
+  WISP_REQUIRE(aligned(x, 16) && aligned(scratch, 16), "wisp_moe_decode: x and scratch must be 16-byte aligned");
   WISP_REQUIRE(H <= 4096 && I <= 4096, "wisp_moe_decode: H and I up to 4096 are supported");
-  MoeShape S;
   S.nslots = nslots;
   S.nbytes = nbytes;
   S.k = k;
@@ -176,8 +178,14 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   S.ncode = 3 * n * bits / 8;
   S.ng = 3 * n / group;
   S.mat_bytes = n * bits / 8;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int upl_gu = int((H / 32 + 31) / 32);  // 1, 2 (H <= 2048) or up to 4
+  return WISP_OK;
+}
+
+static int v1_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
+                     float* scratch, uint16_t* out, cudaStream_t s) {
+  const int64_t H = S.H, I = S.I;
+  const int k = S.k;
+  const int upl_gu = int((H / 32 + 31) / 32);
   const int upl_dn = int((I / 32 + 31) / 32);
   const int UP = int(I / 32) | 1;
   const size_t smem = size_t(k) * 32 * UP * 4 + size_t(k) * (I / 32) * 4;
@@ -213,6 +221,88 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
 #undef WISP_GU
 #undef WISP_DN
   return check_launch("moe_decode down");
+}
+
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sm_count();
+  if (!cached[dev]) cached[dev] = sm_count();
+  return cached[dev];
+}
+
+// v2 applies when every bulk copy is 16-byte aligned by construction and both stages fit in shared memory
+static bool v2_supported(const MoeShape& S, int bits, int nctas) {
+  if (bits != 4 && bits != 3 && bits != 2) return false;
+  if (S.H > 2048 || S.I > 2048) return false;
+  if ((int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
+  if (S.mat_bytes % 16 || S.ncode % 16) return false;
+  if (int64_t(S.k) * S.I > int64_t(nctas) * S.I) return false;  // a CTA range spans at most two experts
+  const v2::GuLayout Lg = v2::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const v2::DnLayout Ld = v2::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  return Lg.bytes <= 200 * 1024 && Ld.bytes <= 200 * 1024 && Lg.max_rows <= S.I;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+static int v2_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
+                     float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
+  const v2::GuLayout Lg = v2::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const v2::DnLayout Ld = v2::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const bool two_gu = S.H > 1024;  // units per row > 32 -> two per lane
+  const bool two_dn = S.I > 1024;
+  cudaError_t e = cudaSuccess;
+#define WISP_V2(B)                                                                                               \
+  e = two_gu ? launch_pdl(v2::gate_up_kernel<B, 2>, nctas, v2::NTHREADS, Lg.bytes, s, pool, meta, x, S, scratch)     \
+             : launch_pdl(v2::gate_up_kernel<B, 1>, nctas, v2::NTHREADS, Lg.bytes, s, pool, meta, x, S, scratch);    \
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v2 gate/up: %s", cudaGetErrorString(e));          \
+  e = two_dn ? launch_pdl(v2::down_kernel<B, 2>, nctas, v2::NTHREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out) \
+             : launch_pdl(v2::down_kernel<B, 1>, nctas, v2::NTHREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out);
+  switch (bits) {
+    case 4: WISP_V2(4) break;
+    case 3: WISP_V2(3) break;
+    case 2: WISP_V2(2) break;
+  }
+#undef WISP_V2
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v2 down: %s", cudaGetErrorString(e));
+  return check_launch("moe_decode v2");
+}
+
+extern "C" {
+
+int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
+                            const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out,
+                            int variant, void* stream) {
+  MoeShape S;
+  int rc = moe_shape(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, S);
+  if (rc) return rc;
+  WISP_REQUIRE(variant >= 0 && variant <= 2, "wisp_moe_decode_variant: variant must be 0 (auto), 1 or 2");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nctas = num_sms();
+  const bool ok2 = v2_supported(S, bits, nctas);
+  if (variant == 2 && !ok2) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 2");
+  if (variant == 2 || (variant == 0 && ok2)) return v2_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
+  return v1_launch(pool, meta, x, S, bits, scratch, out, s);
+}
+
+int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k, const uint16_t* x,
+                    int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream) {
+  return wisp_moe_decode_variant(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, 0, stream);
 }
 
 int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t* k, int64_t k_stride, int Hk, int D,

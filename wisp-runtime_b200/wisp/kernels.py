@@ -42,9 +42,10 @@ def _need_cuda(*ts):
             raise WispError("wisp kernels need CUDA tensors (there is no CPU path)")
 
 
-def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratch=None):
+def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratch=None, variant=0):
     """Fused dequant + GEMV MoE of one token over the k experts named by ``meta`` (fp32 [2k] =
-    [slots..., weights...]).  pool: uint8 [nslots, nbytes]; x: bf16 [H].  Returns bf16 [H]."""
+    [slots..., weights...]).  pool: uint8 [nslots, nbytes]; x: bf16 [H].  Returns bf16 [H].
+    ``variant``: 0 automatic, 1 warp-per-row kernels, 2 persistent bulk-copy kernels."""
     assert H % group == 0 and I % group == 0 and n == H * I
     _need_cuda(pool, meta, x)
     assert pool.dtype == torch.uint8 and pool.dim() == 2 and pool.is_contiguous()
@@ -57,7 +58,7 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
     if out is None:
         out = torch.empty((H,), dtype=x.dtype, device=x.device)
     _lib.call(
-        "wisp_moe_decode",
+        "wisp_moe_decode_variant",
         pool.data_ptr(),
         pool.shape[0],
         pool.shape[1],
@@ -70,6 +71,7 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
         group,
         scratch.data_ptr(),
         out.data_ptr(),
+        variant,
         _stream(x),
     )
     return out
