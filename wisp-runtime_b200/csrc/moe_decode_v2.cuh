@@ -23,10 +23,15 @@
 namespace wisp {
 namespace v2 {
 
-constexpr int NWARPS = 16;
-constexpr int NTHREADS = NWARPS * 32;
+// Warps per CTA.  Sized so one gate/up CTA and one down CTA fit on an SM together (registers:
+// 12 x 32 x <=120 + 8 x 32 x <=64 <= 64K; shared memory well under 227 KB at the Qwen3 shape), which is
+// what lets the down grid start its weight copies while gate/up still computes.
+constexpr int GU_WARPS = 12;
+constexpr int DN_WARPS = 8;
+constexpr int GU_THREADS = GU_WARPS * 32;
+constexpr int DN_THREADS = DN_WARPS * 32;
 constexpr int CH = 8;  // rows per gate/up chunk
-constexpr unsigned WAIT_LIMIT = 1u << 26;  // ~seconds of polling; a stuck copy sets WAIT_TIMEOUT
+constexpr unsigned WAIT_LIMIT = 1u << 24;  // bounded polling; a stuck copy sets WAIT_TIMEOUT
 
 // ------------------------------------------------------------------------------------------------
 // PTX wrappers: mbarrier, bulk copy, PDL
@@ -147,8 +152,8 @@ __host__ __device__ inline DnLayout dn_layout(int H, int I, int k, int group, in
   const int64_t gpr = I / group;
   L.sc_win = ru16(int64_t(L.max_rows) * gpr * 2) + 16;
   L.per_expert = int64_t(L.max_rows) * L.row_bytes + 2 * L.sc_win;
-  // + mbarrier per expert + partial sums [NWARPS][max_rows]
-  L.bytes = int64_t(k) * L.per_expert + 8 * k + 4 * NWARPS * L.max_rows;
+  // + mbarrier per expert + partial sums [DN_WARPS][max_rows]
+  L.bytes = int64_t(k) * L.per_expert + 8 * k + 4 * DN_WARPS * L.max_rows;
   return L;
 }
 
@@ -156,7 +161,7 @@ __host__ __device__ inline DnLayout dn_layout(int H, int I, int k, int group, in
 // gate/up
 // ------------------------------------------------------------------------------------------------
 template <int BITS, int UPL>
-__global__ void __launch_bounds__(NTHREADS, 1) gate_up_kernel(const uint8_t* __restrict__ pool,
+__global__ void __maxnreg__(120) gate_up_kernel(const uint8_t* __restrict__ pool,
                                                               const float* __restrict__ meta,
                                                               const uint16_t* __restrict__ x, MoeShape S,
                                                               float* __restrict__ a_out) {
@@ -238,7 +243,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gate_up_kernel(const uint8_t* __r
   }
 
   // rows are dealt to warps round-robin; the chunk of row i is found by re-walking the cut rule
-  for (int i = warp; i < nrows; i += NWARPS) {
+  for (int i = warp; i < nrows; i += GU_WARPS) {
     // locate row i: chunks are cut every CH rows and at expert boundaries
     int c = 0;
     int64_t r = r_begin, idx_in_chunk = 0;
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gate_up_kernel(const uint8_t* __r
 // down + weighted combine
 // ------------------------------------------------------------------------------------------------
 template <int BITS, int UPL>
-__global__ void __launch_bounds__(NTHREADS, 1) down_kernel(const uint8_t* __restrict__ pool,
+__global__ void __maxnreg__(64) down_kernel(const uint8_t* __restrict__ pool,
                                                            const float* __restrict__ meta,
                                                            const float* __restrict__ a, MoeShape S,
                                                            uint16_t* __restrict__ out) {
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) down_kernel(const uint8_t* __rest
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const DnLayout Ld = dn_layout(S.H, S.I, S.k, S.group, BITS, gridDim.x);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + int64_t(S.k) * Ld.per_expert);
-  float* part = reinterpret_cast<float*>(bars + S.k);  // [NWARPS][max_rows]
+  float* part = reinterpret_cast<float*>(bars + S.k);  // [DN_WARPS][max_rows]
   const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
   const int nrows = h1 - h0;
   const int gpr = S.I / S.group;
@@ -352,18 +357,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) down_kernel(const uint8_t* __rest
       bulk_g2s(dst + int64_t(Ld.max_rows) * Ld.row_bytes + Ld.sc_win, base + wm.start, wm.bytes, &bars[j]);
     }
   }
-  for (int i = threadIdx.x; i < NWARPS * Ld.max_rows; i += NTHREADS) part[i] = 0.0f;
+  for (int i = threadIdx.x; i < DN_WARPS * Ld.max_rows; i += DN_THREADS) part[i] = 0.0f;
   __syncthreads();
   // a is written by the gate/up grid
   pdl_wait();
 
   const int U = S.I / 32;
   // work split: piece p = (expert j, row subset sub) with p = j * per + sub; warp w takes pieces
-  // w, w + NWARPS, ...; a warp accumulates into its own row of `part`, so the combine is ordered
-  const int per = S.k <= NWARPS ? NWARPS / S.k : 1;
+  // w, w + DN_WARPS, ...; a warp accumulates into its own row of `part`, so the combine is ordered
+  const int per = S.k <= DN_WARPS ? DN_WARPS / S.k : 1;
   const uint32_t sk_s = uint32_t((S.ncode + 2 * (2 * ngm + int64_t(h0) * gpr)) & 15);
   const uint32_t sk_m = uint32_t((S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * gpr)) & 15);
-  for (int p = warp; p < S.k * per; p += NWARPS) {
+  for (int p = warp; p < S.k * per; p += DN_WARPS) {
     const int j = p / per, sub = p - j * per;
     int64_t slot;
     if (!route_slot(meta, j, S, slot)) continue;
@@ -413,9 +418,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) down_kernel(const uint8_t* __rest
   }
   __syncthreads();
   // fixed-order reduction over warps: deterministic
-  for (int r = threadIdx.x; r < nrows; r += NTHREADS) {
+  for (int r = threadIdx.x; r < nrows; r += DN_THREADS) {
     float s = 0.0f;
-    for (int w = 0; w < NWARPS; ++w) s += part[w * Ld.max_rows + r];
+    for (int w = 0; w < DN_WARPS; ++w) s += part[w * Ld.max_rows + r];
     out[h0 + r] = f32_to_bf16(s);
   }
   // no copy may still be landing when the CTA retires (also covers experts no warp consumed)

@@ -268,11 +268,11 @@ static int v2_launch(const uint8_t* pool, const float* meta, const uint16_t* x, 
   const bool two_dn = S.I > 1024;
   cudaError_t e = cudaSuccess;
 #define WISP_V2(B)                                                                                               \
-  e = two_gu ? launch_pdl(v2::gate_up_kernel<B, 2>, nctas, v2::NTHREADS, Lg.bytes, s, pool, meta, x, S, scratch)     \
-             : launch_pdl(v2::gate_up_kernel<B, 1>, nctas, v2::NTHREADS, Lg.bytes, s, pool, meta, x, S, scratch);    \
+  e = two_gu ? launch_pdl(v2::gate_up_kernel<B, 2>, nctas, v2::GU_THREADS, Lg.bytes, s, pool, meta, x, S, scratch)     \
+             : launch_pdl(v2::gate_up_kernel<B, 1>, nctas, v2::GU_THREADS, Lg.bytes, s, pool, meta, x, S, scratch);    \
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v2 gate/up: %s", cudaGetErrorString(e));          \
-  e = two_dn ? launch_pdl(v2::down_kernel<B, 2>, nctas, v2::NTHREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out) \
-             : launch_pdl(v2::down_kernel<B, 1>, nctas, v2::NTHREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out);
+  e = two_dn ? launch_pdl(v2::down_kernel<B, 2>, nctas, v2::DN_THREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out) \
+             : launch_pdl(v2::down_kernel<B, 1>, nctas, v2::DN_THREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out);
   switch (bits) {
     case 4: WISP_V2(4) break;
     case 3: WISP_V2(3) break;
