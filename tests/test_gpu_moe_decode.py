@@ -53,15 +53,16 @@ def _setup(bits, H, I, E, k, G=128, seed=0):
     return pool, x, perm, wts
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 @pytest.mark.parametrize("bits", [4, 3, 2, 8])
 def test_full_shape_vs_oracle(bits, variant):
     """Qwen3-30B-A3B layer shape: H=2048, I=768, top-8 of 16 resident experts, every kernel variant
-    (0 = automatic choice, 1 = warp-per-row, 2 = persistent bulk-copy; 8-bit has no variant 2)."""
+    (0 = automatic, 1 = warp-per-row, 2 = persistent bulk-copy CUDA-core, 3 = persistent bulk-copy with
+    tensor-core MMA; variants 2 and 3 take 4/3/2-bit experts only)."""
     from wisp import kernels
 
-    if bits == 8 and variant == 2:
-        pytest.skip("8-bit rows do not fit the variant-2 shared-memory stage")
+    if bits == 8 and variant in (2, 3):
+        pytest.skip("8-bit experts run on variant 1")
     H, I, E, k = 2048, 768, 16, 8
     n = H * I
     pool, x, slots, wts = _setup(bits, H, I, E, k, seed=bits)
@@ -87,15 +88,18 @@ def test_variants_agree_and_are_deterministic(bits):
     pool, x, slots, wts = _setup(bits, H, I, E, k, seed=40 + bits)
     meta = torch.cat([slots.float(), wts])
     o1 = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=1))
-    o2 = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=2))
-    assert _rel(o2, o1) < 2e-3
-    for _ in range(3):
-        assert np.array_equal(_bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=2)), o2)
+    for v in (2, 3):
+        ov = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=v))
+        assert _rel(ov, o1) < 2e-3, v
+        for _ in range(3):
+            assert np.array_equal(_bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=v)), ov)
 
 
 @pytest.mark.parametrize("bits", [4, 3, 2])
 @pytest.mark.parametrize(
-    "H,I,k,G", [(256, 128, 3, 128), (64, 32, 2, 32), (4096, 1024, 4, 128), (2048, 768, 1, 64), (1024, 2048, 20, 128)]
+    "H,I,k,G",
+    [(256, 128, 3, 128), (64, 32, 2, 32), (4096, 1024, 4, 128), (2048, 768, 1, 64), (1024, 2048, 20, 128),
+     (2048, 768, 8, 256), (512, 384, 64, 128)],
 )
 def test_other_shapes(H, I, k, G, bits):
     """Small, odd and large shapes (k up to 20 > one warp-chunk of experts), automatic variant."""
@@ -109,7 +113,7 @@ def test_other_shapes(H, I, k, G, bits):
     assert _rel(_bf16_np(out), ref) < TOL
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 def test_bad_slot_flagged_and_skipped_per_variant(variant):
     from wisp import _lib, kernels
 

@@ -4,6 +4,7 @@
 #include "decode_ops.cuh"
 #include "moe_decode.cuh"
 #include "moe_decode_v2.cuh"
+#include "moe_decode_v3.cuh"
 #include "quant.cuh"
 
 namespace wisp {
@@ -283,6 +284,37 @@ static int v2_launch(const uint8_t* pool, const float* meta, const uint16_t* x, 
   return check_launch("moe_decode v2");
 }
 
+// v3 adds: groups of whole 128-code MMA blocks, 16-byte aligned rows, both stages in shared memory
+static bool v3_supported(const MoeShape& S, int bits, int nctas) {
+  if (bits != 4 && bits != 3 && bits != 2) return false;
+  if (S.group % 128 != 0) return false;
+  if ((int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
+  if (S.mat_bytes % 16 || S.ncode % 16) return false;
+  if (S.k > nctas) return false;
+  const v3::GuL Lg = v3::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const v3::DnL Ld = v3::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  return Lg.max_rows <= S.I && Lg.bytes <= 200 * 1024 && Ld.bytes <= 200 * 1024;
+}
+
+static int v3_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
+                     float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
+  const v3::GuL Lg = v3::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const v3::DnL Ld = v3::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  cudaError_t e = cudaSuccess;
+#define WISP_V3(B)                                                                                          \
+  e = launch_pdl(v3::gate_up_kernel<B>, nctas, v3::GU_THREADS, Lg.bytes, s, pool, meta, x, S, scratch);     \
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v3 gate/up: %s", cudaGetErrorString(e));     \
+  e = launch_pdl(v3::down_kernel<B>, nctas, v3::DN_THREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out);
+  switch (bits) {
+    case 4: WISP_V3(4) break;
+    case 3: WISP_V3(3) break;
+    case 2: WISP_V3(2) break;
+  }
+#undef WISP_V3
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v3 down: %s", cudaGetErrorString(e));
+  return check_launch("moe_decode v3");
+}
+
 extern "C" {
 
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
@@ -291,12 +323,16 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
   MoeShape S;
   int rc = moe_shape(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, S);
   if (rc) return rc;
-  WISP_REQUIRE(variant >= 0 && variant <= 2, "wisp_moe_decode_variant: variant must be 0 (auto), 1 or 2");
+  WISP_REQUIRE(variant >= 0 && variant <= 3, "wisp_moe_decode_variant: variant must be 0 (auto), 1, 2 or 3");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nctas = num_sms();
-  const bool ok2 = v2_supported(S, bits, nctas);
-  if (variant == 2 && !ok2) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 2");
-  if (variant == 2 || (variant == 0 && ok2)) return v2_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
+  if (variant == 2) {
+    if (!v2_supported(S, bits, nctas)) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 2");
+    return v2_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
+  }
+  const bool ok3 = v3_supported(S, bits, nctas);
+  if (variant == 3 && !ok3) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 3");
+  if (variant == 3 || (variant == 0 && ok3)) return v3_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
   return v1_launch(pool, meta, x, S, bits, scratch, out, s);
 }
 
