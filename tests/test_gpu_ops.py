@@ -51,10 +51,11 @@ def test_rmsnorm_matches_fixture(golden):
         assert (got != ref).mean() < 0.05
 
 
-def test_rmsnorm_fused_residual():
+@pytest.mark.parametrize("H", [2048, 1000, 100, 12288])
+def test_rmsnorm_fused_residual(H):
+    """Vector path (H % 8 == 0, H/8 <= 1024) and the generic loop path (H = 100, H = 12288)."""
     from wisp.kernels import rmsnorm
 
-    H = 2048
     gen = torch.Generator(device="cuda").manual_seed(0)
     x = torch.randn(3, H, device="cuda", generator=gen).to(torch.bfloat16)
     d = torch.randn(3, H, device="cuda", generator=gen).to(torch.bfloat16)

@@ -63,4 +63,56 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* x, const u
   }
 }
 
+// H % 8 == 0 and H / 8 <= 1024: one thread per 8 elements, every load issued before any arithmetic
+// (x, delta and w as 16-byte vectors), one block reduction.  Same rounding steps as rmsnorm_kernel.
+__global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const uint16_t* x, const uint16_t* __restrict__ delta,
+                                                           uint16_t* sum_out, const uint16_t* __restrict__ w, int64_t H,
+                                                           float eps, uint16_t* __restrict__ out) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const bool active = int64_t(t) * 8 < H;
+  uint4 xv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+  if (active) {
+    xv = reinterpret_cast<const uint4*>(x + row * H)[t];
+    if (delta) dv = reinterpret_cast<const uint4*>(delta + row * H)[t];
+    wv = reinterpret_cast<const uint4*>(w)[t];
+  }
+  float v[8];
+  const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(xw[i] << 16);
+    v[2 * i + 1] = __uint_as_float(xw[i] & 0xFFFF0000u);
+    if (delta) {
+      v[2 * i] = bf16_to_f32(f32_to_bf16(v[2 * i] + __uint_as_float(dw[i] << 16)));
+      v[2 * i + 1] = bf16_to_f32(f32_to_bf16(v[2 * i + 1] + __uint_as_float(dw[i] & 0xFFFF0000u)));
+    }
+    ss = fmaf(v[2 * i], v[2 * i], ss);
+    ss = fmaf(v[2 * i + 1], v[2 * i + 1], ss);
+  }
+  if (active && delta && sum_out) {
+    uint4 o;
+    uint32_t* op = &o.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) op[i] = uint32_t(f32_to_bf16(v[2 * i])) | (uint32_t(f32_to_bf16(v[2 * i + 1])) << 16);
+    reinterpret_cast<uint4*>(sum_out + row * H)[t] = o;
+  }
+  const float tot = block_sum(active ? ss : 0.0f, red);
+  const float inv = rsqrtf(tot / float(H) + eps);
+  if (active) {
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint4 o;
+    uint32_t* op = &o.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = __uint_as_float(ww[i] << 16) * bf16_to_f32(f32_to_bf16(v[2 * i] * inv));
+      const float b = __uint_as_float(ww[i] & 0xFFFF0000u) * bf16_to_f32(f32_to_bf16(v[2 * i + 1] * inv));
+      op[i] = uint32_t(f32_to_bf16(a)) | (uint32_t(f32_to_bf16(b)) << 16);
+    }
+    reinterpret_cast<uint4*>(out + row * H)[t] = o;
+  }
+}
+
 }  // namespace wisp

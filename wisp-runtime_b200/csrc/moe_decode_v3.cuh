@@ -112,15 +112,23 @@ __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bit
   return L;
 }
 
-// chunk walk of a gate/up CTA range: cut every CH rows and at expert boundaries
-struct ChunkIt {
-  int64_t r, r_end;
-  int I;
-  __device__ __forceinline__ int64_t count() const {
-    const int64_t row = r % I;
-    return min64(min64(CH, I - row), r_end - r);
-  }
+// Chunks of a gate/up CTA range [r_begin, r_end) of the k*I (expert, row) list: since I is a multiple
+// of CH, cutting at multiples of CH also cuts at every expert boundary, so chunk ci is closed-form.
+struct Chunk {
+  int lo, cnt, j, row0;  // first list index, rows, expert, first row in the expert
 };
+__device__ __forceinline__ int chunk_count(int r_begin, int r_end) {
+  return r_end > r_begin ? (r_end - 1) / CH - r_begin / CH + 1 : 0;
+}
+__device__ __forceinline__ Chunk chunk_at(int r_begin, int r_end, int I, int ci) {
+  Chunk c;
+  const int base = (r_begin / CH + ci) * CH;
+  c.lo = max(r_begin, base);
+  c.cnt = min(r_end, base + CH) - c.lo;
+  c.j = c.lo / I;
+  c.row0 = c.lo - c.j * I;
+  return c;
+}
 
 // ------------------------------------------------------------------------------------------------
 template <int BITS>
@@ -135,60 +143,58 @@ __global__ void __maxnreg__(72) gate_up_kernel(const uint8_t* __restrict__ pool,
   float* sxu = reinterpret_cast<float*>(sm + Lg.off_sx);
   float* part = reinterpret_cast<float*>(sm + Lg.off_part);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lg.off_bar);
-  const int64_t R = int64_t(S.k) * S.I;
-  const int64_t r_begin = R * blockIdx.x / gridDim.x, r_end = R * (blockIdx.x + 1) / gridDim.x;
+  const int R = S.k * S.I;
+  const int r_begin = int(int64_t(R) * blockIdx.x / gridDim.x), r_end = int(int64_t(R) * (blockIdx.x + 1) / gridDim.x);
   const int64_t ngm = S.ng / 3;
   const int gpr = Lg.gpr;
+  const int nchunks = chunk_count(r_begin, r_end);
 
   pdl_wait();  // routing and x come from earlier kernels in the stream
 
   // ---- copies: lane 0 arms the barriers, then warp 0's lanes issue one bulk copy per row / window
-  int nchunks = 0;
-  for (ChunkIt it{r_begin, r_end, S.I}; it.r < r_end; it.r += it.count()) ++nchunks;
   if (warp == 0) {
     if (lane == 0) {
       for (int ci = 0; ci < Lg.max_chunks; ++ci) mbar_init(&bars[ci], 1);
       mbar_fence_init();
-      int ci = 0;
-      for (ChunkIt it{r_begin, r_end, S.I}; it.r < r_end; it.r += it.count(), ++ci) {
-        const int j = int(it.r / S.I);
-        const int64_t row = it.r - int64_t(j) * S.I, cnt = it.count();
-        int64_t slot;
-        if (!route_slot(meta, j, S, slot)) {
-          flag(WISP_STATUS_BAD_SLOT);
-          mbar_expect_tx(&bars[ci], 0);
-          continue;
-        }
-        uint32_t tx = uint32_t(2 * cnt * Lg.row_bytes);
-        tx += window(S.ncode + 2 * (row * gpr), 2 * cnt * gpr).bytes;
-        tx += window(S.ncode + 2 * (S.ng + row * gpr), 2 * cnt * gpr).bytes;
-        tx += window(S.ncode + 2 * (ngm + row * gpr), 2 * cnt * gpr).bytes;
-        tx += window(S.ncode + 2 * (S.ng + ngm + row * gpr), 2 * cnt * gpr).bytes;
-        mbar_expect_tx(&bars[ci], tx);
-      }
     }
     __syncwarp();
-    int ci = 0, op = 0;
-    for (ChunkIt it{r_begin, r_end, S.I}; it.r < r_end; it.r += it.count(), ++ci) {
-      const int j = int(it.r / S.I);
-      const int64_t row = it.r - int64_t(j) * S.I, cnt = it.count();
+    // lane ci arms chunk ci (the copies of a chunk are issued only after its expect_tx below)
+    for (int ci = lane; ci < nchunks; ci += 32) {
+      const Chunk ch = chunk_at(r_begin, r_end, S.I, ci);
       int64_t slot;
-      if (!route_slot(meta, j, S, slot)) continue;
+      if (!route_slot(meta, ch.j, S, slot)) {
+        flag(WISP_STATUS_BAD_SLOT);
+        mbar_expect_tx(&bars[ci], 0);
+        continue;
+      }
+      const int64_t row = ch.row0, cnt = ch.cnt;
+      uint32_t tx = uint32_t(2 * cnt * Lg.row_bytes);
+      tx += window(S.ncode + 2 * (row * gpr), 2 * cnt * gpr).bytes;
+      tx += window(S.ncode + 2 * (S.ng + row * gpr), 2 * cnt * gpr).bytes;
+      tx += window(S.ncode + 2 * (ngm + row * gpr), 2 * cnt * gpr).bytes;
+      tx += window(S.ncode + 2 * (S.ng + ngm + row * gpr), 2 * cnt * gpr).bytes;
+      mbar_expect_tx(&bars[ci], tx);
+    }
+    __syncwarp();
+    // op list: per chunk 2*CH row slots (gate rows then up rows) + 4 windows; lane l takes ops l, l+32, ...
+    const int per_chunk = 2 * CH + 4;
+    for (int op = lane; op < nchunks * per_chunk; op += 32) {
+      const int ci = op / per_chunk, o = op - ci * per_chunk;
+      const Chunk ch = chunk_at(r_begin, r_end, S.I, ci);
+      int64_t slot;
+      if (!route_slot(meta, ch.j, S, slot)) continue;
       const uint8_t* base = pool + slot * S.nbytes;
       uint8_t* dst = sm + int64_t(ci) * Lg.chunk;
-      const int nops = int(2 * cnt) + 4;
-      for (int o = 0; o < nops; ++o, ++op) {
-        if ((op & 31) != lane) continue;
-        if (o < 2 * cnt) {
-          const int m = o / int(cnt), rr = o - m * int(cnt);  // matrix (0 gate, 1 up), row in chunk
-          bulk_g2s(dst + (m * CH + rr) * Lg.stride, base + m * S.mat_bytes + (row + rr) * Lg.row_bytes,
+      if (o < 2 * CH) {
+        const int m = o / CH, rr = o - m * CH;  // matrix (0 gate, 1 up), row in chunk
+        if (rr < ch.cnt)
+          bulk_g2s(dst + (m * CH + rr) * Lg.stride, base + m * S.mat_bytes + int64_t(ch.row0 + rr) * Lg.row_bytes,
                    uint32_t(Lg.row_bytes), &bars[ci]);
-        } else {
-          const int wsel = o - int(2 * cnt);  // 0 gate scale, 1 gate min, 2 up scale, 3 up min
-          const int64_t off = S.ncode + 2 * ((wsel & 1) * S.ng + (wsel >> 1) * ngm + row * gpr);
-          const Win w = window(off, 2 * cnt * gpr);
-          bulk_g2s(dst + 2 * CH * Lg.stride + wsel * Lg.sc_win, base + w.start, w.bytes, &bars[ci]);
-        }
+      } else {
+        const int wsel = o - 2 * CH;  // 0 gate scale, 1 gate min, 2 up scale, 3 up min
+        const int64_t off = S.ncode + 2 * ((wsel & 1) * S.ng + (wsel >> 1) * ngm + int64_t(ch.row0) * gpr);
+        const Win w = window(off, 2 * int64_t(ch.cnt) * gpr);
+        bulk_g2s(dst + 2 * CH * Lg.stride + wsel * Lg.sc_win, base + w.start, w.bytes, &bars[ci]);
       }
     }
   }
@@ -228,10 +234,9 @@ __global__ void __maxnreg__(72) gate_up_kernel(const uint8_t* __restrict__ pool,
   const int per_split = (groups + NSPLIT - 1) / NSPLIT;
   for (int piece = warp; piece < nchunks * NSPLIT; piece += GU_WARPS) {
     const int ci = piece / NSPLIT, sp = piece - ci * NSPLIT;
-    ChunkIt it{r_begin, r_end, S.I};
-    for (int q = 0; q < ci; ++q) it.r += it.count();
-    const int j = int(it.r / S.I);
-    const int64_t row0 = it.r - int64_t(j) * S.I, cnt = it.count();
+    const Chunk ch = chunk_at(r_begin, r_end, S.I, ci);
+    const int j = ch.j;
+    const int64_t row0 = ch.row0;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
     float accg = 0.0f, accu = 0.0f;
@@ -293,23 +298,17 @@ __global__ void __maxnreg__(72) gate_up_kernel(const uint8_t* __restrict__ pool,
   }
   __syncthreads();
   // ---- SwiGLU of the complete rows, written once
-  {
-    int ci = 0;
-    int64_t base_r = r_begin;
-    for (ChunkIt it{r_begin, r_end, S.I}; it.r < r_end; it.r += it.count(), ++ci) {
-      const int64_t cnt = it.count();
-      for (int rr = threadIdx.x; rr < cnt; rr += blockDim.x) {
-        float gs = 0.0f, us = 0.0f;
-        for (int sp = 0; sp < NSPLIT; ++sp) {
-          gs += part[((ci * NSPLIT + sp) * CH + rr) * 2];
-          us += part[((ci * NSPLIT + sp) * CH + rr) * 2 + 1];
-        }
-        const int j = int(it.r / S.I);
-        int64_t slot;
-        a_out[it.r + rr] = route_slot(meta, j, S, slot) ? silu_mul(gs, us) : 0.0f;
-      }
-      base_r += cnt;
+  for (int rr = threadIdx.x; rr < r_end - r_begin; rr += blockDim.x) {
+    const int r = r_begin + rr;
+    const int ci = r / CH - r_begin / CH;
+    const int in_chunk = r - max(r_begin, (r / CH) * CH);
+    float gs = 0.0f, us = 0.0f;
+    for (int sp = 0; sp < NSPLIT; ++sp) {
+      gs += part[((ci * NSPLIT + sp) * CH + in_chunk) * 2];
+      us += part[((ci * NSPLIT + sp) * CH + in_chunk) * 2 + 1];
     }
+    int64_t slot;
+    a_out[r] = route_slot(meta, r / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
   }
   if (threadIdx.x == 0)
     for (int ci = 0; ci < nchunks; ++ci) mbar_wait(&bars[ci]);

@@ -357,6 +357,13 @@ int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, co
   WISP_REQUIRE(x && w && out, "wisp_rmsnorm: NULL pointer");
   WISP_REQUIRE(rows >= 0 && H > 0 && H <= 16384, "wisp_rmsnorm: bad shape");
   if (rows == 0) return WISP_OK;
+  const bool vec_ok = H % 8 == 0 && H / 8 <= 1024 && aligned(x, 16) && aligned(w, 16) && aligned(out, 16) &&
+                      (!delta || aligned(delta, 16)) && (!sum_out || aligned(sum_out, 16));
+  if (vec_ok) {
+    const int threads = int((H / 8 + 31) / 32 * 32);
+    rmsnorm_vec_kernel<<<(unsigned)rows, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
+    return check_launch("rmsnorm");
+  }
   const size_t smem = size_t(H) * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   rmsnorm_kernel<<<(unsigned)rows, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
