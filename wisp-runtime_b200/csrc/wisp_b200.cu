@@ -365,7 +365,8 @@ int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, co
     return check_launch("rmsnorm");
   }
   const size_t smem = size_t(H) * 4;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  // the kernel also has a small static array: opt in to large dynamic shared memory well before 48 KB
+  if (smem > 32 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   rmsnorm_kernel<<<(unsigned)rows, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
   return check_launch("rmsnorm");
 }
