@@ -85,12 +85,11 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
                     void* stream);
 
 /* Same computation with an explicit kernel choice: 0 = automatic (what wisp_moe_decode does),
- * 1 = warp-per-row CUDA-core kernels (any supported shape), 2 = persistent one-CTA-per-SM kernels
- * streaming each CTA's rows into shared memory with bulk copies, chained with programmatic dependent
- * launch, CUDA-core math (bits 4/3/2, H and I up to 2048, 16-byte aligned rows), 3 = the same data
- * movement with the multiply-accumulate on warp-level tensor-core MMA fed by a one-op-per-pair code
- * unpack (bits 4/3/2, group a multiple of 128).  Automatic = 3 when it applies, else 1.  A variant
- * that does not apply returns WISP_ERR_UNSUPPORTED. */
+ * 1 = warp-per-row CUDA-core kernels (any supported shape), 2 = persistent per-warp cp.async pipelines
+ * feeding warp-level tensor-core MMA through a one-op-per-pair code unpack, with the down rows
+ * prefetched into L2 and the two kernels chained by programmatic dependent launch (bits 4/3/2, group
+ * a multiple of 128, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise).
+ * Automatic = 2 when it applies, else 1. */
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,
                             uint16_t* out, int variant, void* stream);

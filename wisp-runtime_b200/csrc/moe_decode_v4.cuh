@@ -1,0 +1,456 @@
+// Fused MoE decode for one token: persistent per-warp cp.async pipelines feeding warp-level MMA.
+//
+// Data movement.  Every warp owns one piece of work and streams exactly the bytes of that piece from
+// the slot pool into its own shared-memory region with 16-byte cp.async copies issued by all 32 lanes
+// (one commit group per 128-code MMA group, so compute starts on group 0 while later groups are still
+// in flight).  Rows land at stride (bytes + 16*BITS), which makes the per-lane fragment loads
+// bank-conflict free.  No CTA-wide barrier sits between issuing and consuming.  While it streams the
+// gate/up rows, each gate/up CTA also prefetches into L2 (cp.async.bulk.prefetch.L2) the down rows
+// its twin down CTA will read, so the down kernel, chained by programmatic dependent launch, finds
+// its 1/3 of the layer's bytes in L2.
+//
+// Math.  Codes become bf16 MMA operands with one LOP3 per pair (unpack_mma.cuh) and
+// mma.sync m16n8k16 accumulates in fp32; two accumulators per group break the MMA dependency chain.
+//   gate/up piece: 8 gate rows (A rows 0-7) + the same 8 up rows (A rows 8-15) over half of H;
+//                  B column 0 = scaled, permuted x.
+//   down piece:    16 output rows of one expert over all of I; B columns 0/1 = bf16 hi/lo of a_j.
+#pragma once
+#include "common.cuh"
+#include "moe_decode.cuh"
+#include "unpack_mma.cuh"
+
+namespace wisp {
+namespace v4 {
+
+constexpr int GU_WARPS = 16;
+constexpr int DN_WARPS = 8;
+constexpr int GU_THREADS = GU_WARPS * 32;
+constexpr int DN_THREADS = DN_WARPS * 32;
+constexpr int CH = 8;      // rows per gate/up piece (A rows 0-7 gate, 8-15 up)
+constexpr int NSPLIT = 2;  // gate/up pieces split H in two halves
+constexpr int MAXG = 16;   // max 128-code groups per piece (commit groups in flight)
+
+__host__ __device__ constexpr int row_pad(int bits) { return 16 * bits; }
+__host__ __device__ inline int64_t ru16(int64_t v) { return (v + 15) & ~int64_t(15); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// wait until at most n groups are pending (n runtime, 0..MAXG)
+__device__ __forceinline__ void cp_wait_n(int n) {
+  switch (n) {
+#define W(k) \
+  case k:    \
+    cp_wait<k>(); break;
+    W(0) W(1) W(2) W(3) W(4) W(5) W(6) W(7) W(8) W(9) W(10) W(11) W(12) W(13) W(14) W(15)
+#undef W
+    default: cp_wait<16>(); break;
+  }
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <int BITS>
+__device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) {
+  if constexpr (BITS == 4) {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  } else if constexpr (BITS == 2) {
+    const uint2 a = *reinterpret_cast<const uint2*>(p);
+    w[0] = a.x; w[1] = a.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < BITS; ++i) w[i] = reinterpret_cast<const uint32_t*>(p)[i];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// shared-memory layouts (host and device share these formulas)
+// ------------------------------------------------------------------------------------------------
+struct GuL {
+  int groups, groups_per_piece, gpr;  // 128-code groups per row / per piece; quant groups per row
+  int64_t piece_bytes, stride, sc_bytes, warp_bytes;
+  int64_t off_bx, off_sb, off_sx, bytes;
+};
+
+__host__ __device__ inline GuL gu_layout(int H, int group, int bits) {
+  GuL L;
+  L.groups = H / 128;
+  L.groups_per_piece = (L.groups + NSPLIT - 1) / NSPLIT;
+  L.gpr = H / group;
+  L.piece_bytes = int64_t(L.groups_per_piece) * 16 * bits;  // code bytes of one row inside a piece
+  L.stride = L.piece_bytes + row_pad(bits);
+  L.sc_bytes = int64_t(CH) * L.gpr * 2;                      // one scale (or min) array of the 8 rows
+  L.warp_bytes = ru16(2 * CH * L.stride + 4 * L.sc_bytes);
+  L.off_bx = GU_WARPS * L.warp_bytes;                        // [H/32 units][16] u32
+  L.off_sb = L.off_bx + int64_t(H / 32) * 16 * 4;            // [H/32] f32
+  L.off_sx = L.off_sb + int64_t(H / 32) * 4;                 // [H/32] f32
+  L.bytes = L.off_sx + int64_t(H / 32) * 4;
+  return L;
+}
+
+// dynamic shared memory of the gate/up kernel: layout + the per-piece partial sums
+__host__ __device__ inline int64_t gu_smem(int H, int I, int k, int group, int bits, int nctas) {
+  const GuL L = gu_layout(H, group, bits);
+  const int64_t nblk = int64_t(k) * I / CH;
+  const int64_t max_pieces = (nblk + nctas - 1) / nctas * NSPLIT;
+  return L.bytes + max_pieces * CH * 2 * 4;
+}
+
+struct DnL {
+  int groups, gpr, rows_max;
+  int64_t row_bytes, stride, sc_bytes, warp_bytes;
+  int64_t off_part, bytes;
+};
+
+__host__ __device__ inline DnL dn_layout(int H, int I, int group, int bits, int nctas) {
+  DnL L;
+  L.groups = I / 128;
+  L.gpr = I / group;
+  L.rows_max = (H + nctas - 1) / nctas;  // output rows per CTA, <= 16 (checked on the host)
+  L.row_bytes = int64_t(I) * bits / 8;
+  L.stride = L.row_bytes + row_pad(bits);
+  L.sc_bytes = ru16(int64_t(16) * L.gpr * 2);
+  // per warp: 16 rows + scale + min arrays + B pairs [I/32 units][2 parts][16] + unit sums [I/32][2]
+  L.warp_bytes = ru16(16 * L.stride + 2 * L.sc_bytes + int64_t(I / 32) * (2 * 16 * 4 + 2 * 4));
+  L.off_part = DN_WARPS * L.warp_bytes;  // [DN_WARPS][16] f32
+  L.bytes = L.off_part + DN_WARPS * 16 * 4;
+  return L;
+}
+
+// ------------------------------------------------------------------------------------------------
+template <int BITS>
+__global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* __restrict__ pool,
+                                                                const float* __restrict__ meta,
+                                                                const uint16_t* __restrict__ x, MoeShape S,
+                                                                float* __restrict__ a_out) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const GuL Lg = gu_layout(S.H, S.group, BITS);
+  uint32_t* bx = reinterpret_cast<uint32_t*>(sm + Lg.off_bx);
+  float* sbu = reinterpret_cast<float*>(sm + Lg.off_sb);
+  float* sxu = reinterpret_cast<float*>(sm + Lg.off_sx);
+  float* halves = reinterpret_cast<float*>(sm + Lg.bytes);  // [pieces of this CTA][CH][2]
+  const int64_t ngm = S.ng / 3;
+  const int64_t row_bytes = int64_t(S.H) * BITS / 8;
+  // this CTA owns 8-row blocks [b0, b1) of the k*I (expert, row) list; I % 8 == 0, so a block never
+  // straddles two experts.  Piece = (block, K half); warp w takes pieces w, w + GU_WARPS, ...
+  const int nblk_all = S.k * S.I / CH;
+  const int b0 = int(int64_t(nblk_all) * blockIdx.x / gridDim.x), b1 = int(int64_t(nblk_all) * (blockIdx.x + 1) / gridDim.x);
+  const int npieces = (b1 - b0) * NSPLIT;
+
+  pdl_wait();  // routing and x come from earlier kernels in the stream
+
+  // ---- L2 prefetch of the down rows the twin down CTA will read (same grid size, same row split)
+  if (warp == GU_WARPS - 1 && lane < S.k) {
+    const int j = lane;
+    int64_t slot;
+    if (route_slot(meta, j, S, slot)) {
+      const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
+      const int64_t drow = int64_t(S.I) * BITS / 8;
+      const uint8_t* base = pool + slot * S.nbytes;
+      const int64_t lo = 2 * S.mat_bytes + h0 * drow, hi = 2 * S.mat_bytes + h1 * drow;
+      if (hi > lo) prefetch_l2(base + (lo & ~int64_t(15)), uint32_t(ru16(hi) - (lo & ~int64_t(15))));
+      const int gd = S.I / S.group;
+      for (int w = 0; w < 2; ++w) {
+        const int64_t a0 = S.ncode + 2 * (w * S.ng + 2 * ngm + int64_t(h0) * gd), a1 = a0 + 2 * int64_t(h1 - h0) * gd;
+        if (a1 > a0) prefetch_l2(base + (a0 & ~int64_t(15)), uint32_t(ru16(a1) - (a0 & ~int64_t(15))));
+      }
+    }
+  }
+
+  uint8_t* wreg = sm + int64_t(warp) * Lg.warp_bytes;
+  // one commit group for the scales, then one per 128-code group of the piece
+  auto issue_piece = [&](int piece) {
+    const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
+    const int r0 = blk * CH;
+    const int j = r0 / S.I, row0 = r0 - j * S.I;
+    int64_t slot;
+    const bool ok = route_slot(meta, j, S, slot);
+    const uint8_t* base = pool + (ok ? slot : 0) * S.nbytes;
+    const int G0 = sp * Lg.groups_per_piece;
+    const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
+    if (ok) {
+      const int words = CH * Lg.gpr / 2;  // 4-byte words per array (2*gpr bytes per row, gpr even)
+      for (int t = lane; t < 4 * words; t += 32) {
+        const int arr = t / words, wd = t - arr * words;  // 0 gate s, 1 gate m, 2 up s, 3 up m
+        const int64_t off = S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr) + 4 * wd;
+        cp_async4(wreg + 2 * CH * Lg.stride + arr * Lg.sc_bytes + 4 * wd, base + off);
+      }
+    }
+    cp_commit();
+    for (int G = 0; G < ng; ++G) {
+      if (ok) {
+        for (int t = lane; t < 16 * BITS; t += 32) {
+          const int rr = t / BITS, q = t - rr * BITS;  // row of 16 (0-7 gate, 8-15 up), 16-B chunk
+          const int m = rr >> 3, rw = rr & 7;
+          const uint8_t* src = base + m * S.mat_bytes + int64_t(row0 + rw) * row_bytes + int64_t(G0 + G) * 16 * BITS + 16 * q;
+          cp_async16(wreg + rr * Lg.stride + G * 16 * BITS + 16 * q, src);
+        }
+      }
+      cp_commit();
+    }
+  };
+  if (warp < npieces) issue_piece(warp);
+
+  // ---- B operand from x (one thread per 32-element unit), visible to all warps after the barrier
+  const int units = S.H / 32;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    float v[32];
+    const uint4* xp = reinterpret_cast<const uint4*>(x + u * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 t = xp[q];
+      const uint32_t wd[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        v[8 * q + 2 * h] = __uint_as_float(wd[h] << 16);
+        v[8 * q + 2 * h + 1] = __uint_as_float(wd[h] & 0xFFFF0000u);
+      }
+    }
+    uint32_t b[16];
+    float bs;
+    build_b_pairs<BITS>(v, 0, b, bs);
+    uint4* dstb = reinterpret_cast<uint4*>(bx + u * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dstb[q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
+    float sx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sx += v[i];
+    sbu[u] = bs;
+    sxu[u] = sx;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  for (int piece = warp; piece < npieces; piece += GU_WARPS) {
+    if (piece != warp) {  // another round: the region is free once the previous piece was consumed
+      cp_wait<0>();
+      __syncwarp();
+      issue_piece(piece);
+    }
+    const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
+    const int r0 = blk * CH;
+    const int j = r0 / S.I;
+    int64_t slot;
+    const bool ok = route_slot(meta, j, S, slot);
+    const int G0 = sp * Lg.groups_per_piece;
+    const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
+    const uint8_t* sw = wreg + 2 * CH * Lg.stride;
+    const uint16_t* ssg = reinterpret_cast<const uint16_t*>(sw) + g * Lg.gpr;
+    const uint16_t* smg = reinterpret_cast<const uint16_t*>(sw + Lg.sc_bytes) + g * Lg.gpr;
+    const uint16_t* ssu = reinterpret_cast<const uint16_t*>(sw + 2 * Lg.sc_bytes) + g * Lg.gpr;
+    const uint16_t* smu = reinterpret_cast<const uint16_t*>(sw + 3 * Lg.sc_bytes) + g * Lg.gpr;
+    const uint8_t* rowg = wreg + g * Lg.stride;
+    const uint8_t* rowu = wreg + (CH + g) * Lg.stride;
+    float accg = 0.0f, accu = 0.0f;
+    for (int G = 0; G < ng; ++G) {
+      cp_wait_n(ng - 1 - G);  // the scale group and code groups 0..G of this piece have landed
+      __syncwarp();
+      if (!ok) continue;
+      const int u = 4 * (G0 + G) + c;
+      uint32_t wg[BITS], wu[BITS];
+      lds_unit<BITS>(rowg + (G * 4 + c) * 4 * BITS, wg);
+      lds_unit<BITS>(rowu + (G * 4 + c) * 4 * BITS, wu);
+      uint32_t b[16];
+      if (g == 0) {
+        const uint4* bp = reinterpret_cast<const uint4*>(bx + u * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 t = bp[q];
+          b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) b[q] = 0u;
+      }
+      uint32_t ag[16], au[16];
+      unpack_pairs<BITS>(wg, ag);
+      unpack_pairs<BITS>(wu, au);
+      float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int m = 0; m < 8; m += 2) {
+        mma_bf16(d0, ag[2 * m], au[2 * m], ag[2 * m + 1], au[2 * m + 1], b[2 * m], b[2 * m + 1]);
+        mma_bf16(d1, ag[2 * m + 2], au[2 * m + 2], ag[2 * m + 3], au[2 * m + 3], b[2 * m + 2], b[2 * m + 3]);
+      }
+      if (c == 0) {
+        const int U = 4 * (G0 + G);
+        const float sb = (sbu[U] + sbu[U + 1]) + (sbu[U + 2] + sbu[U + 3]);
+        const float sx = (sxu[U] + sxu[U + 1]) + (sxu[U + 2] + sxu[U + 3]);
+        const int qg = ((G0 + G) * 128) / S.group;
+        accg += f16_bits_to_f32(ssg[qg]) * ((d0[0] + d1[0]) - 128.0f * sb) + f16_bits_to_f32(smg[qg]) * sx;
+        accu += f16_bits_to_f32(ssu[qg]) * ((d0[2] + d1[2]) - 128.0f * sb) + f16_bits_to_f32(smu[qg]) * sx;
+      }
+    }
+    if (c == 0) {
+      halves[(piece * CH + g) * 2] = accg;
+      halves[(piece * CH + g) * 2 + 1] = accu;
+    }
+  }
+  __syncthreads();
+  // ---- SwiGLU of complete rows: sum the K parts of each block in a fixed order, write a once
+  for (int t = threadIdx.x; t < (b1 - b0) * CH; t += blockDim.x) {
+    const int bi = t / CH, rw = t - bi * CH;
+    float gs = 0.0f, us = 0.0f;
+    for (int sp = 0; sp < NSPLIT; ++sp) {
+      gs += halves[((bi * NSPLIT + sp) * CH + rw) * 2];
+      us += halves[((bi * NSPLIT + sp) * CH + rw) * 2 + 1];
+    }
+    const int r = (b0 + bi) * CH + rw;
+    int64_t slot;
+    a_out[r] = route_slot(meta, r / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
+  }
+  cp_wait<0>();
+}
+
+// ------------------------------------------------------------------------------------------------
+template <int BITS>
+__global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __restrict__ pool,
+                                                             const float* __restrict__ meta,
+                                                             const float* __restrict__ a, MoeShape S,
+                                                             uint16_t* __restrict__ out) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const DnL Ld = dn_layout(S.H, S.I, S.group, BITS, gridDim.x);
+  float* part = reinterpret_cast<float*>(sm + Ld.off_part);
+  const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
+  const int nrows = h1 - h0;
+  const int64_t ngm = S.ng / 3;
+  const int units = S.I / 32;
+  uint8_t* wreg = sm + int64_t(warp) * Ld.warp_bytes;
+  uint16_t* ss = reinterpret_cast<uint16_t*>(wreg + 16 * Ld.stride);
+  uint16_t* smn = reinterpret_cast<uint16_t*>(wreg + 16 * Ld.stride + Ld.sc_bytes);
+  uint32_t* bd = reinterpret_cast<uint32_t*>(wreg + 16 * Ld.stride + 2 * Ld.sc_bytes);  // [units][2][16]
+  float* sbx = reinterpret_cast<float*>(bd + units * 32);                               // [units][2] (sb, sx)
+
+  for (int i = threadIdx.x; i < DN_WARPS * 16; i += blockDim.x) part[i] = 0.0f;
+
+  // ---- warp w streams the down rows of experts w, w+DN_WARPS, ... (the routing is final already)
+  auto issue_expert = [&](int j) {
+    int64_t slot;
+    if (route_slot(meta, j, S, slot) && nrows > 0) {
+      const uint8_t* base = pool + slot * S.nbytes;
+      const int chunks = int(Ld.row_bytes / 16);
+      for (int t = lane; t < nrows * chunks; t += 32) {
+        const int r = t / chunks, q = t - r * chunks;
+        cp_async16(wreg + r * Ld.stride + 16 * q, base + 2 * S.mat_bytes + int64_t(h0 + r) * Ld.row_bytes + 16 * q);
+      }
+      const int words = nrows * Ld.gpr / 2;
+      for (int t = lane; t < 2 * words; t += 32) {
+        const int arr = t / words, wd = t - arr * words;
+        const int64_t off = S.ncode + 2 * (arr * S.ng + 2 * ngm + int64_t(h0) * Ld.gpr) + 4 * wd;
+        cp_async4(reinterpret_cast<uint8_t*>(arr ? smn : ss) + 4 * wd, base + off);
+      }
+    }
+    cp_commit();
+  };
+  if (warp < S.k) issue_expert(warp);
+
+  pdl_wait();  // a is written by the gate/up grid
+
+  for (int j = warp; j < S.k; j += DN_WARPS) {
+    if (j != warp) {
+      __syncwarp();
+      issue_expert(j);
+    }
+    int64_t slot;
+    const bool ok = route_slot(meta, j, S, slot);
+    const float wj = meta[S.k + j];
+    // B pairs of a_j for this warp (hi and lo parts), lane per unit
+    for (int u = lane; u < units; u += 32) {
+      float v[32];
+      const float4* ap = reinterpret_cast<const float4*>(a + int64_t(j) * S.I + u * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = ap[q];
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+      }
+      uint32_t b[16];
+      float bs0, bs1;
+      uint4* dstb = reinterpret_cast<uint4*>(bd + u * 32);
+      build_b_pairs<BITS>(v, 0, b, bs0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dstb[q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
+      build_b_pairs<BITS>(v, 1, b, bs1);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dstb[4 + q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
+      float sx = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sx += v[i];
+      sbx[2 * u] = bs0 + bs1;
+      sbx[2 * u + 1] = sx;
+    }
+    cp_wait<0>();
+    __syncwarp();
+    if (!ok) continue;
+    const int r_a = g, r_b = g + 8;
+    float acc_a = 0.0f, acc_b = 0.0f;
+    for (int G = 0; G < Ld.groups; ++G) {
+      const int u = 4 * G + c;
+      uint32_t wa[BITS], wb[BITS];
+      lds_unit<BITS>(wreg + r_a * Ld.stride + u * 4 * BITS, wa);
+      lds_unit<BITS>(wreg + r_b * Ld.stride + u * 4 * BITS, wb);
+      uint32_t b[16];
+      if (g < 2) {
+        const uint4* bp = reinterpret_cast<const uint4*>(bd + u * 32 + g * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 t = bp[q];
+          b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) b[q] = 0u;
+      }
+      uint32_t aa[16], ab[16];
+      unpack_pairs<BITS>(wa, aa);
+      unpack_pairs<BITS>(wb, ab);
+      float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int m = 0; m < 8; m += 2) {
+        mma_bf16(d0, aa[2 * m], ab[2 * m], aa[2 * m + 1], ab[2 * m + 1], b[2 * m], b[2 * m + 1]);
+        mma_bf16(d1, aa[2 * m + 2], ab[2 * m + 2], aa[2 * m + 3], ab[2 * m + 3], b[2 * m + 2], b[2 * m + 3]);
+      }
+      if (c == 0) {
+        const float sb = (sbx[2 * (4 * G)] + sbx[2 * (4 * G + 1)]) + (sbx[2 * (4 * G + 2)] + sbx[2 * (4 * G + 3)]);
+        const float sx = (sbx[2 * (4 * G) + 1] + sbx[2 * (4 * G + 1) + 1]) + (sbx[2 * (4 * G + 2) + 1] + sbx[2 * (4 * G + 3) + 1]);
+        const int qg = (G * 128) / S.group;
+        if (r_a < nrows)
+          acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * ((d0[0] + d0[1] + d1[0] + d1[1]) - 128.0f * sb) +
+                   f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
+        if (r_b < nrows)
+          acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * ((d0[2] + d0[3] + d1[2] + d1[3]) - 128.0f * sb) +
+                   f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
+      }
+    }
+    if (c == 0) {
+      if (r_a < nrows) part[warp * 16 + r_a] += wj * acc_a;
+      if (r_b < nrows) part[warp * 16 + r_b] += wj * acc_b;
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
+    float s = 0.0f;
+    for (int w = 0; w < DN_WARPS; ++w) s += part[w * 16 + r];
+    out[h0 + r] = f32_to_bf16(s);
+  }
+  cp_wait<0>();
+}
+
+}  // namespace v4
+}  // namespace wisp

@@ -3,8 +3,7 @@
 #include "common.cuh"
 #include "decode_ops.cuh"
 #include "moe_decode.cuh"
-#include "moe_decode_v2.cuh"
-#include "moe_decode_v3.cuh"
+#include "moe_decode_v4.cuh"
 #include "quant.cuh"
 
 namespace wisp {
@@ -233,18 +232,6 @@ static int num_sms() {
   return cached[dev];
 }
 
-// v2 applies when every bulk copy is 16-byte aligned by construction and both stages fit in shared memory
-static bool v2_supported(const MoeShape& S, int bits, int nctas) {
-  if (bits != 4 && bits != 3 && bits != 2) return false;
-  if (S.H > 2048 || S.I > 2048) return false;
-  if ((int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
-  if (S.mat_bytes % 16 || S.ncode % 16) return false;
-  if (int64_t(S.k) * S.I > int64_t(nctas) * S.I) return false;  // a CTA range spans at most two experts
-  const v2::GuLayout Lg = v2::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  const v2::DnLayout Ld = v2::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  return Lg.bytes <= 200 * 1024 && Ld.bytes <= 200 * 1024 && Lg.max_rows <= S.I;
-}
-
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -261,58 +248,40 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-static int v2_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
-                     float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
-  const v2::GuLayout Lg = v2::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  const v2::DnLayout Ld = v2::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  const bool two_gu = S.H > 1024;  // units per row > 32 -> two per lane
-  const bool two_dn = S.I > 1024;
-  cudaError_t e = cudaSuccess;
-#define WISP_V2(B)                                                                                               \
-  e = two_gu ? launch_pdl(v2::gate_up_kernel<B, 2>, nctas, v2::GU_THREADS, Lg.bytes, s, pool, meta, x, S, scratch)     \
-             : launch_pdl(v2::gate_up_kernel<B, 1>, nctas, v2::GU_THREADS, Lg.bytes, s, pool, meta, x, S, scratch);    \
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v2 gate/up: %s", cudaGetErrorString(e));          \
-  e = two_dn ? launch_pdl(v2::down_kernel<B, 2>, nctas, v2::DN_THREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out) \
-             : launch_pdl(v2::down_kernel<B, 1>, nctas, v2::DN_THREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out);
-  switch (bits) {
-    case 4: WISP_V2(4) break;
-    case 3: WISP_V2(3) break;
-    case 2: WISP_V2(2) break;
-  }
-#undef WISP_V2
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v2 down: %s", cudaGetErrorString(e));
-  return check_launch("moe_decode v2");
-}
-
-// v3 adds: groups of whole 128-code MMA blocks, 16-byte aligned rows, both stages in shared memory
-static bool v3_supported(const MoeShape& S, int bits, int nctas) {
+// the tensor-core pipeline applies when: 4/3/2-bit codes, quantization groups made of whole
+// 128-code MMA groups with an even count per row (4-byte scale copies), 8-row blocks never
+// straddling experts, at most 16 down rows per CTA, and both kernels' shared memory fits
+static bool v4_supported(const MoeShape& S, int bits, int nctas) {
   if (bits != 4 && bits != 3 && bits != 2) return false;
-  if (S.group % 128 != 0) return false;
-  if ((int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
-  if (S.mat_bytes % 16 || S.ncode % 16) return false;
-  if (S.k > nctas) return false;
-  const v3::GuL Lg = v3::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  const v3::DnL Ld = v3::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  return Lg.max_rows <= S.I && Lg.bytes <= 200 * 1024 && Ld.bytes <= 200 * 1024;
+  if (S.group % 128 != 0 || S.H % 128 != 0 || S.I % 128 != 0) return false;
+  if ((S.H / S.group) % 2 || (S.I / S.group) % 2 || S.ng % 2) return false;
+  if (S.ncode % 16 || S.mat_bytes % 16 || (int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
+  if ((S.H + nctas - 1) / nctas > 16) return false;
+  if (S.k > 32) return false;  // one prefetch lane per expert
+  const v4::GuL Lg = v4::gu_layout(S.H, S.group, bits);
+  if (Lg.groups_per_piece > v4::MAXG) return false;
+  const int64_t gsm = v4::gu_smem(S.H, S.I, S.k, S.group, bits, nctas);
+  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.group, bits, nctas);
+  return gsm <= 220 * 1024 && Ld.bytes <= 220 * 1024;
 }
 
-static int v3_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
+static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
                      float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
-  const v3::GuL Lg = v3::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  const v3::DnL Ld = v3::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const int64_t gsm = v4::gu_smem(S.H, S.I, S.k, S.group, bits, nctas);
+  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.group, bits, nctas);
   cudaError_t e = cudaSuccess;
-#define WISP_V3(B)                                                                                          \
-  e = launch_pdl(v3::gate_up_kernel<B>, nctas, v3::GU_THREADS, Lg.bytes, s, pool, meta, x, S, scratch);     \
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v3 gate/up: %s", cudaGetErrorString(e));     \
-  e = launch_pdl(v3::down_kernel<B>, nctas, v3::DN_THREADS, Ld.bytes, s, pool, meta, (const float*)scratch, S, out);
+#define WISP_V4(B)                                                                                          \
+  e = launch_pdl(v4::gate_up_kernel<B>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch);  \
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode gate/up: %s", cudaGetErrorString(e));        \
+  e = launch_pdl(v4::down_kernel<B>, nctas, v4::DN_THREADS, size_t(Ld.bytes), s, pool, meta, (const float*)scratch, S, out);
   switch (bits) {
-    case 4: WISP_V3(4) break;
-    case 3: WISP_V3(3) break;
-    case 2: WISP_V3(2) break;
+    case 4: WISP_V4(4) break;
+    case 3: WISP_V4(3) break;
+    case 2: WISP_V4(2) break;
   }
-#undef WISP_V3
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode v3 down: %s", cudaGetErrorString(e));
-  return check_launch("moe_decode v3");
+#undef WISP_V4
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode down: %s", cudaGetErrorString(e));
+  return check_launch("moe_decode");
 }
 
 extern "C" {
@@ -323,16 +292,12 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
   MoeShape S;
   int rc = moe_shape(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, S);
   if (rc) return rc;
-  WISP_REQUIRE(variant >= 0 && variant <= 3, "wisp_moe_decode_variant: variant must be 0 (auto), 1, 2 or 3");
+  WISP_REQUIRE(variant >= 0 && variant <= 2, "wisp_moe_decode_variant: variant must be 0 (auto), 1 or 2");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nctas = num_sms();
-  if (variant == 2) {
-    if (!v2_supported(S, bits, nctas)) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 2");
-    return v2_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
-  }
-  const bool ok3 = v3_supported(S, bits, nctas);
-  if (variant == 3 && !ok3) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 3");
-  if (variant == 3 || (variant == 0 && ok3)) return v3_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
+  const bool ok2 = v4_supported(S, bits, nctas);
+  if (variant == 2 && !ok2) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 2");
+  if (variant == 2 || (variant == 0 && ok2)) return v4_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
   return v1_launch(pool, meta, x, S, bits, scratch, out, s);
 }
 
