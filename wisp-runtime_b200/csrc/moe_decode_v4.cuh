@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int j = r0 / S.I, row0 = r0 - j * S.I;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
+    if (!ok && lane == 0) flag(WISP_STATUS_BAD_SLOT);  // skipped: contributes nothing
     const uint8_t* base = pool + (ok ? slot : 0) * S.nbytes;
     const int G0 = sp * Lg.groups_per_piece;
     const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
@@ -343,7 +344,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   // ---- warp w streams the down rows of experts w, w+DN_WARPS, ... (the routing is final already)
   auto issue_expert = [&](int j) {
     int64_t slot;
-    if (route_slot(meta, j, S, slot) && nrows > 0) {
+    const bool ok = route_slot(meta, j, S, slot);
+    if (!ok && lane == 0) flag(WISP_STATUS_BAD_SLOT);
+    if (ok && nrows > 0) {
       const uint8_t* base = pool + slot * S.nbytes;
       const int chunks = int(Ld.row_bytes / 16);
       for (int t = lane; t < nrows * chunks; t += 32) {
