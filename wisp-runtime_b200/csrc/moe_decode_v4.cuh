@@ -10,7 +10,8 @@
 // its 1/3 of the layer's bytes in L2.
 //
 // Math.  Codes become bf16 MMA operands with one LOP3 per pair (unpack_mma.cuh) and
-// mma.sync m16n8k16 accumulates in fp32; two accumulators per group break the MMA dependency chain.
+// mma.sync m16n8k16 accumulates in fp32.  Groups are processed in pairs with four independent
+// accumulator chains; lanes that hold no B column read a shared zero block (no divergence).
 //   gate/up piece: 8 gate rows (A rows 0-7) + the same 8 up rows (A rows 8-15) over half of H;
 //                  B column 0 = scaled, permuted x.
 //   down piece:    16 output rows of one expert over all of I; B columns 0/1 = bf16 hi/lo of a_j.
@@ -83,7 +84,7 @@ __device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) 
 struct GuL {
   int groups, groups_per_piece, gpr;  // 128-code groups per row / per piece; quant groups per row
   int64_t piece_bytes, stride, sc_bytes, warp_bytes;
-  int64_t off_bx, off_sb, off_sx, bytes;
+  int64_t off_bx, off_gsum, off_zero, off_halves;
 };
 
 __host__ __device__ inline GuL gu_layout(int H, int group, int bits) {
@@ -93,42 +94,60 @@ __host__ __device__ inline GuL gu_layout(int H, int group, int bits) {
   L.gpr = H / group;
   L.piece_bytes = int64_t(L.groups_per_piece) * 16 * bits;  // code bytes of one row inside a piece
   L.stride = L.piece_bytes + row_pad(bits);
-  L.sc_bytes = int64_t(CH) * L.gpr * 2;                      // one scale (or min) array of the 8 rows
+  L.sc_bytes = ru16(int64_t(CH) * L.gpr * 2);                // one scale (or min) array of the 8 rows
   L.warp_bytes = ru16(2 * CH * L.stride + 4 * L.sc_bytes);
   L.off_bx = GU_WARPS * L.warp_bytes;                        // [H/32 units][16] u32
-  L.off_sb = L.off_bx + int64_t(H / 32) * 16 * 4;            // [H/32] f32
-  L.off_sx = L.off_sb + int64_t(H / 32) * 4;                 // [H/32] f32
-  L.bytes = L.off_sx + int64_t(H / 32) * 4;
+  L.off_gsum = L.off_bx + int64_t(H / 32) * 16 * 4;          // [H/128][2] f32: (sum of B, sum of x)
+  L.off_zero = L.off_gsum + int64_t(L.groups) * 2 * 4;       // 64 zero bytes
+  L.off_halves = ru16(L.off_zero + 64);                      // [pieces][CH][2] f32
   return L;
 }
 
-// dynamic shared memory of the gate/up kernel: layout + the per-piece partial sums
+// dynamic shared memory of the gate/up kernel
 __host__ __device__ inline int64_t gu_smem(int H, int I, int k, int group, int bits, int nctas) {
   const GuL L = gu_layout(H, group, bits);
   const int64_t nblk = int64_t(k) * I / CH;
   const int64_t max_pieces = (nblk + nctas - 1) / nctas * NSPLIT;
-  return L.bytes + max_pieces * CH * 2 * 4;
+  return L.off_halves + max_pieces * CH * 2 * 4;
 }
 
 struct DnL {
-  int groups, gpr, rows_max;
+  int groups, gpr, units;
   int64_t row_bytes, stride, sc_bytes, warp_bytes;
-  int64_t off_part, bytes;
+  int64_t off_bd, off_dsum, off_zero, off_part, bytes;
 };
 
-__host__ __device__ inline DnL dn_layout(int H, int I, int group, int bits, int nctas) {
+__host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bits) {
   DnL L;
   L.groups = I / 128;
   L.gpr = I / group;
-  L.rows_max = (H + nctas - 1) / nctas;  // output rows per CTA, <= 16 (checked on the host)
+  L.units = I / 32;
   L.row_bytes = int64_t(I) * bits / 8;
   L.stride = L.row_bytes + row_pad(bits);
   L.sc_bytes = ru16(int64_t(16) * L.gpr * 2);
-  // per warp: 16 rows + scale + min arrays + B pairs [I/32 units][2 parts][16] + unit sums [I/32][2]
-  L.warp_bytes = ru16(16 * L.stride + 2 * L.sc_bytes + int64_t(I / 32) * (2 * 16 * 4 + 2 * 4));
-  L.off_part = DN_WARPS * L.warp_bytes;  // [DN_WARPS][16] f32
+  L.warp_bytes = ru16(16 * L.stride + 2 * L.sc_bytes);
+  L.off_bd = DN_WARPS * L.warp_bytes;                           // [k][units][2 parts][16] u32
+  L.off_dsum = L.off_bd + int64_t(k) * L.units * 2 * 16 * 4;    // [k][groups][2] f32
+  L.off_zero = L.off_dsum + int64_t(k) * L.groups * 2 * 4;      // 64 zero bytes
+  L.off_part = ru16(L.off_zero + 64);                           // [DN_WARPS][16] f32
   L.bytes = L.off_part + DN_WARPS * 16 * 4;
   return L;
+}
+
+__device__ __forceinline__ void lds_b16(const uint32_t* p, uint32_t (&b)[16]) {
+  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 t = p4[q];
+    b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
+  }
+}
+
+// sum over the 4 lanes that hold the 4 units of one 128-code group (lanes 4i..4i+3)
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  return v;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -142,13 +161,13 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
   const int g = lane >> 2, c = lane & 3;
   const GuL Lg = gu_layout(S.H, S.group, BITS);
   uint32_t* bx = reinterpret_cast<uint32_t*>(sm + Lg.off_bx);
-  float* sbu = reinterpret_cast<float*>(sm + Lg.off_sb);
-  float* sxu = reinterpret_cast<float*>(sm + Lg.off_sx);
-  float* halves = reinterpret_cast<float*>(sm + Lg.bytes);  // [pieces of this CTA][CH][2]
+  float* gsum = reinterpret_cast<float*>(sm + Lg.off_gsum);
+  const uint32_t* zero = reinterpret_cast<const uint32_t*>(sm + Lg.off_zero);
+  float* halves = reinterpret_cast<float*>(sm + Lg.off_halves);
   const int64_t ngm = S.ng / 3;
   const int64_t row_bytes = int64_t(S.H) * BITS / 8;
   // this CTA owns 8-row blocks [b0, b1) of the k*I (expert, row) list; I % 8 == 0, so a block never
-  // straddles two experts.  Piece = (block, K half); warp w takes pieces w, w + GU_WARPS, ...
+  // straddles two experts.  Piece = (block, K part); warp w takes pieces w, w + GU_WARPS, ...
   const int nblk_all = S.k * S.I / CH;
   const int b0 = int(int64_t(nblk_all) * blockIdx.x / gridDim.x), b1 = int(int64_t(nblk_all) * (blockIdx.x + 1) / gridDim.x);
   const int npieces = (b1 - b0) * NSPLIT;
@@ -174,7 +193,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
   }
 
   uint8_t* wreg = sm + int64_t(warp) * Lg.warp_bytes;
-  // one commit group for the scales, then one per 128-code group of the piece
+  // commit groups of a piece: [scales], [code groups 0..h-1], [code groups h..ng-1]
   auto issue_piece = [&](int piece) {
     const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
     const int r0 = blk * CH;
@@ -185,6 +204,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const uint8_t* base = pool + (ok ? slot : 0) * S.nbytes;
     const int G0 = sp * Lg.groups_per_piece;
     const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
+    const int h = (ng + 1) / 2;
     if (ok) {
       const int words = CH * Lg.gpr / 2;  // 4-byte words per array (2*gpr bytes per row, gpr even)
       for (int t = lane; t < 4 * words; t += 32) {
@@ -194,47 +214,64 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
       }
     }
     cp_commit();
+    // per lane: at most two 16-byte chunks of each group (16 rows x BITS chunks / 32 lanes)
+    const uint8_t* src[2];
+    uint32_t dst[2];
+    int nch = 0;
+    for (int t = lane; t < 16 * BITS; t += 32, ++nch) {
+      const int rr = t / BITS, q = t - rr * BITS;  // row of 16 (0-7 gate, 8-15 up), 16-B chunk
+      src[nch] = base + (rr >> 3) * S.mat_bytes + int64_t(row0 + (rr & 7)) * row_bytes + int64_t(G0) * 16 * BITS + 16 * q;
+      dst[nch] = uint32_t(rr * Lg.stride + 16 * q);
+    }
     for (int G = 0; G < ng; ++G) {
-      if (ok) {
-        for (int t = lane; t < 16 * BITS; t += 32) {
-          const int rr = t / BITS, q = t - rr * BITS;  // row of 16 (0-7 gate, 8-15 up), 16-B chunk
-          const int m = rr >> 3, rw = rr & 7;
-          const uint8_t* src = base + m * S.mat_bytes + int64_t(row0 + rw) * row_bytes + int64_t(G0 + G) * 16 * BITS + 16 * q;
-          cp_async16(wreg + rr * Lg.stride + G * 16 * BITS + 16 * q, src);
-        }
-      }
-      cp_commit();
+      if (ok)
+        for (int i = 0; i < nch; ++i) cp_async16(wreg + dst[i] + G * 16 * BITS, src[i] + G * 16 * BITS);
+      if (G == h - 1 || G == ng - 1) cp_commit();
     }
   };
   if (warp < npieces) issue_piece(warp);
 
-  // ---- B operand from x (one thread per 32-element unit), visible to all warps after the barrier
+  // ---- B operand from x, one thread per 32-element unit: on the warps without a piece when there
+  //      are enough of them, else on all threads after their copies are issued
   const int units = S.H / 32;
-  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+  const int spare = (GU_WARPS - npieces) * 32;
+  const int first = spare >= units ? npieces * 32 : 0;  // multiple of 32: whole warps build
+  const int nthr = int(blockDim.x) - first;
+  // warp-uniform loop (the quad shuffles need every lane); lanes past the last unit read a valid
+  // unit and store nothing
+  for (int ub = (int(threadIdx.x) - first) & ~31; int(threadIdx.x) >= first && ub < units; ub += nthr) {
+    const int u = ub + lane;
+    const int uu = min(u, units - 1);
     float v[32];
-    const uint4* xp = reinterpret_cast<const uint4*>(x + u * 32);
+    const uint4* xp = reinterpret_cast<const uint4*>(x + uu * 32);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 t = xp[q];
       const uint32_t wd[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        v[8 * q + 2 * h] = __uint_as_float(wd[h] << 16);
-        v[8 * q + 2 * h + 1] = __uint_as_float(wd[h] & 0xFFFF0000u);
+      for (int hh = 0; hh < 4; ++hh) {
+        v[8 * q + 2 * hh] = __uint_as_float(wd[hh] << 16);
+        v[8 * q + 2 * hh + 1] = __uint_as_float(wd[hh] & 0xFFFF0000u);
       }
     }
     uint32_t b[16];
-    float bs;
-    build_b_pairs<BITS>(v, 0, b, bs);
-    uint4* dstb = reinterpret_cast<uint4*>(bx + u * 16);
+    float sb, sx = 0.0f;
+    build_b_pairs<BITS>(v, 0, b, sb);
+    if (u < units) {
+      uint4* d4 = reinterpret_cast<uint4*>(bx + u * 16);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) dstb[q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
-    float sx = 0.0f;
+      for (int q = 0; q < 4; ++q) d4[q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i) sx += v[i];
-    sbu[u] = bs;
-    sxu[u] = sx;
+    sb = quad_sum(sb);
+    sx = quad_sum(sx);
+    if (u < units && (u & 3) == 0) {
+      gsum[2 * (u >> 2)] = sb;
+      gsum[2 * (u >> 2) + 1] = sx;
+    }
   }
+  if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Lg.off_zero)[threadIdx.x] = 0u;
   __syncthreads();
   pdl_launch_dependents();
 
@@ -246,11 +283,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     }
     const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
     const int r0 = blk * CH;
-    const int j = r0 / S.I;
     int64_t slot;
-    const bool ok = route_slot(meta, j, S, slot);
+    const bool ok = route_slot(meta, r0 / S.I, S, slot);
     const int G0 = sp * Lg.groups_per_piece;
     const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
+    const int h = (ng + 1) / 2;
     const uint8_t* sw = wreg + 2 * CH * Lg.stride;
     const uint16_t* ssg = reinterpret_cast<const uint16_t*>(sw) + g * Lg.gpr;
     const uint16_t* smg = reinterpret_cast<const uint16_t*>(sw + Lg.sc_bytes) + g * Lg.gpr;
@@ -259,42 +296,32 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const uint8_t* rowg = wreg + g * Lg.stride;
     const uint8_t* rowu = wreg + (CH + g) * Lg.stride;
     float accg = 0.0f, accu = 0.0f;
-    for (int G = 0; G < ng; ++G) {
-      cp_wait_n(ng - 1 - G);  // the scale group and code groups 0..G of this piece have landed
+    for (int G = 0; G < ng; G += 2) {
+      if (G == 0) cp_wait<1>();   // scales + first half landed
+      if (G == h) cp_wait<0>();   // second half landed
       __syncwarp();
       if (!ok) continue;
-      const int u = 4 * (G0 + G) + c;
-      uint32_t wg[BITS], wu[BITS];
-      lds_unit<BITS>(rowg + (G * 4 + c) * 4 * BITS, wg);
-      lds_unit<BITS>(rowu + (G * 4 + c) * 4 * BITS, wu);
-      uint32_t b[16];
-      if (g == 0) {
-        const uint4* bp = reinterpret_cast<const uint4*>(bx + u * 16);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 t = bp[q];
-          b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) b[q] = 0u;
-      }
-      uint32_t ag[16], au[16];
-      unpack_pairs<BITS>(wg, ag);
-      unpack_pairs<BITS>(wu, au);
-      float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int m = 0; m < 8; m += 2) {
-        mma_bf16(d0, ag[2 * m], au[2 * m], ag[2 * m + 1], au[2 * m + 1], b[2 * m], b[2 * m + 1]);
-        mma_bf16(d1, ag[2 * m + 2], au[2 * m + 2], ag[2 * m + 3], au[2 * m + 3], b[2 * m + 2], b[2 * m + 3]);
-      }
-      if (c == 0) {
-        const int U = 4 * (G0 + G);
-        const float sb = (sbu[U] + sbu[U + 1]) + (sbu[U + 2] + sbu[U + 3]);
-        const float sx = (sxu[U] + sxu[U + 1]) + (sxu[U + 2] + sxu[U + 3]);
+      const int G1 = min(G + 1, ng - 1);  // an odd tail repeats the last group; its result is dropped
+      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[16], bb1[16];
+      lds_unit<BITS>(rowg + (G * 4 + c) * 4 * BITS, wa0);
+      lds_unit<BITS>(rowu + (G * 4 + c) * 4 * BITS, wb0);
+      lds_unit<BITS>(rowg + (G1 * 4 + c) * 4 * BITS, wa1);
+      lds_unit<BITS>(rowu + (G1 * 4 + c) * 4 * BITS, wb1);
+      lds_b16(g == 0 ? bx + (4 * (G0 + G) + c) * 16 : zero, bb0);
+      lds_b16(g == 0 ? bx + (4 * (G0 + G1) + c) * 16 : zero, bb1);
+      float d0[4], d1[4];
+      mma_two_groups<BITS>(wa0, wb0, wa1, wb1, bb0, bb1, d0, d1);
+      {
         const int qg = ((G0 + G) * 128) / S.group;
-        accg += f16_bits_to_f32(ssg[qg]) * ((d0[0] + d1[0]) - 128.0f * sb) + f16_bits_to_f32(smg[qg]) * sx;
-        accu += f16_bits_to_f32(ssu[qg]) * ((d0[2] + d1[2]) - 128.0f * sb) + f16_bits_to_f32(smu[qg]) * sx;
+        const float sb = gsum[2 * (G0 + G)], sx = gsum[2 * (G0 + G) + 1];
+        accg += f16_bits_to_f32(ssg[qg]) * (d0[0] - 128.0f * sb) + f16_bits_to_f32(smg[qg]) * sx;
+        accu += f16_bits_to_f32(ssu[qg]) * (d0[2] - 128.0f * sb) + f16_bits_to_f32(smu[qg]) * sx;
+      }
+      if (G1 != G) {
+        const int qg = ((G0 + G1) * 128) / S.group;
+        const float sb = gsum[2 * (G0 + G1)], sx = gsum[2 * (G0 + G1) + 1];
+        accg += f16_bits_to_f32(ssg[qg]) * (d1[0] - 128.0f * sb) + f16_bits_to_f32(smg[qg]) * sx;
+        accu += f16_bits_to_f32(ssu[qg]) * (d1[2] - 128.0f * sb) + f16_bits_to_f32(smu[qg]) * sx;
       }
     }
     if (c == 0) {
@@ -327,21 +354,21 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const DnL Ld = dn_layout(S.H, S.I, S.group, BITS, gridDim.x);
+  const DnL Ld = dn_layout(S.H, S.I, S.k, S.group, BITS);
+  uint32_t* bd = reinterpret_cast<uint32_t*>(sm + Ld.off_bd);
+  float* dsum = reinterpret_cast<float*>(sm + Ld.off_dsum);
+  const uint32_t* zero = reinterpret_cast<const uint32_t*>(sm + Ld.off_zero);
   float* part = reinterpret_cast<float*>(sm + Ld.off_part);
   const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
   const int nrows = h1 - h0;
   const int64_t ngm = S.ng / 3;
-  const int units = S.I / 32;
+  const int units = Ld.units;
   uint8_t* wreg = sm + int64_t(warp) * Ld.warp_bytes;
-  uint16_t* ss = reinterpret_cast<uint16_t*>(wreg + 16 * Ld.stride);
-  uint16_t* smn = reinterpret_cast<uint16_t*>(wreg + 16 * Ld.stride + Ld.sc_bytes);
-  uint32_t* bd = reinterpret_cast<uint32_t*>(wreg + 16 * Ld.stride + 2 * Ld.sc_bytes);  // [units][2][16]
-  float* sbx = reinterpret_cast<float*>(bd + units * 32);                               // [units][2] (sb, sx)
+  const uint16_t* ss = reinterpret_cast<const uint16_t*>(wreg + 16 * Ld.stride);
+  const uint16_t* smn = reinterpret_cast<const uint16_t*>(wreg + 16 * Ld.stride + Ld.sc_bytes);
 
-  for (int i = threadIdx.x; i < DN_WARPS * 16; i += blockDim.x) part[i] = 0.0f;
-
-  // ---- warp w streams the down rows of experts w, w+DN_WARPS, ... (the routing is final already)
+  // ---- warp w streams the down rows of experts w, w+DN_WARPS, ... (the routing is final already;
+  //      the gate/up grid prefetched these rows into L2)
   auto issue_expert = [&](int j) {
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
@@ -357,88 +384,97 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
       for (int t = lane; t < 2 * words; t += 32) {
         const int arr = t / words, wd = t - arr * words;
         const int64_t off = S.ncode + 2 * (arr * S.ng + 2 * ngm + int64_t(h0) * Ld.gpr) + 4 * wd;
-        cp_async4(reinterpret_cast<uint8_t*>(arr ? smn : ss) + 4 * wd, base + off);
+        cp_async4(wreg + 16 * Ld.stride + arr * Ld.sc_bytes + 4 * wd, base + off);
       }
     }
     cp_commit();
   };
   if (warp < S.k) issue_expert(warp);
+  for (int i = threadIdx.x; i < DN_WARPS * 16; i += blockDim.x) part[i] = 0.0f;
+  if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Ld.off_zero)[threadIdx.x] = 0u;
 
   pdl_wait();  // a is written by the gate/up grid
 
+  // ---- B operand of every routed expert, CTA-wide: one thread per (expert, unit), both parts.
+  //      Warp-uniform loop (quad shuffles need every lane); tail lanes redo the last unit, store nothing.
+  const int ntask = S.k * units;
+  for (int tb = int(threadIdx.x) & ~31; tb < ntask; tb += blockDim.x) {
+    const int t = tb + lane, tt = min(t, ntask - 1);
+    const int j = tt / units, u = tt - j * units;
+    float v[32];
+    const float4* ap = reinterpret_cast<const float4*>(a + int64_t(j) * S.I + u * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 f = ap[q];
+      v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+    }
+    uint32_t b0[16], b1[16];
+    float sb0, sb1, sx = 0.0f;
+    build_b_pairs<BITS>(v, 0, b0, sb0);
+    build_b_pairs<BITS>(v, 1, b1, sb1);
+    if (t < ntask) {
+      uint4* d0 = reinterpret_cast<uint4*>(bd + (int64_t(t) * 2) * 16);
+      uint4* d1 = reinterpret_cast<uint4*>(bd + (int64_t(t) * 2 + 1) * 16);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        d0[q] = make_uint4(b0[4 * q], b0[4 * q + 1], b0[4 * q + 2], b0[4 * q + 3]);
+        d1[q] = make_uint4(b1[4 * q], b1[4 * q + 1], b1[4 * q + 2], b1[4 * q + 3]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sx += v[i];
+    // the 4 units of a group sit in 4 consecutive lanes (units % 4 == 0 and tb % 32 == 0)
+    const float sb = quad_sum(sb0 + sb1);
+    sx = quad_sum(sx);
+    if (t < ntask && (u & 3) == 0) {
+      dsum[2 * (j * Ld.groups + (u >> 2))] = sb;
+      dsum[2 * (j * Ld.groups + (u >> 2)) + 1] = sx;
+    }
+  }
+  __syncthreads();
+
   for (int j = warp; j < S.k; j += DN_WARPS) {
     if (j != warp) {
+      cp_wait<0>();
       __syncwarp();
       issue_expert(j);
     }
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
     const float wj = meta[S.k + j];
-    // B pairs of a_j for this warp (hi and lo parts), lane per unit
-    for (int u = lane; u < units; u += 32) {
-      float v[32];
-      const float4* ap = reinterpret_cast<const float4*>(a + int64_t(j) * S.I + u * 32);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 f = ap[q];
-        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
-      }
-      uint32_t b[16];
-      float bs0, bs1;
-      uint4* dstb = reinterpret_cast<uint4*>(bd + u * 32);
-      build_b_pairs<BITS>(v, 0, b, bs0);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) dstb[q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
-      build_b_pairs<BITS>(v, 1, b, bs1);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) dstb[4 + q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
-      float sx = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) sx += v[i];
-      sbx[2 * u] = bs0 + bs1;
-      sbx[2 * u + 1] = sx;
-    }
     cp_wait<0>();
     __syncwarp();
     if (!ok) continue;
     const int r_a = g, r_b = g + 8;
     float acc_a = 0.0f, acc_b = 0.0f;
-    for (int G = 0; G < Ld.groups; ++G) {
-      const int u = 4 * G + c;
-      uint32_t wa[BITS], wb[BITS];
-      lds_unit<BITS>(wreg + r_a * Ld.stride + u * 4 * BITS, wa);
-      lds_unit<BITS>(wreg + r_b * Ld.stride + u * 4 * BITS, wb);
-      uint32_t b[16];
-      if (g < 2) {
-        const uint4* bp = reinterpret_cast<const uint4*>(bd + u * 32 + g * 16);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 t = bp[q];
-          b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) b[q] = 0u;
-      }
-      uint32_t aa[16], ab[16];
-      unpack_pairs<BITS>(wa, aa);
-      unpack_pairs<BITS>(wb, ab);
-      float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int m = 0; m < 8; m += 2) {
-        mma_bf16(d0, aa[2 * m], ab[2 * m], aa[2 * m + 1], ab[2 * m + 1], b[2 * m], b[2 * m + 1]);
-        mma_bf16(d1, aa[2 * m + 2], ab[2 * m + 2], aa[2 * m + 3], ab[2 * m + 3], b[2 * m + 2], b[2 * m + 3]);
-      }
-      if (c == 0) {
-        const float sb = (sbx[2 * (4 * G)] + sbx[2 * (4 * G + 1)]) + (sbx[2 * (4 * G + 2)] + sbx[2 * (4 * G + 3)]);
-        const float sx = (sbx[2 * (4 * G) + 1] + sbx[2 * (4 * G + 1) + 1]) + (sbx[2 * (4 * G + 2) + 1] + sbx[2 * (4 * G + 3) + 1]);
+    const uint32_t* bj = bd + int64_t(j) * units * 32;
+    for (int G = 0; G < Ld.groups; G += 2) {
+      const int G1 = min(G + 1, Ld.groups - 1);
+      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[16], bb1[16];
+      lds_unit<BITS>(wreg + r_a * Ld.stride + (4 * G + c) * 4 * BITS, wa0);
+      lds_unit<BITS>(wreg + r_b * Ld.stride + (4 * G + c) * 4 * BITS, wb0);
+      lds_unit<BITS>(wreg + r_a * Ld.stride + (4 * G1 + c) * 4 * BITS, wa1);
+      lds_unit<BITS>(wreg + r_b * Ld.stride + (4 * G1 + c) * 4 * BITS, wb1);
+      lds_b16(g < 2 ? bj + (4 * G + c) * 32 + g * 16 : zero, bb0);
+      lds_b16(g < 2 ? bj + (4 * G1 + c) * 32 + g * 16 : zero, bb1);
+      float d0[4], d1[4];
+      mma_two_groups<BITS>(wa0, wb0, wa1, wb1, bb0, bb1, d0, d1);
+      const float* ds = dsum + 2 * int64_t(j) * Ld.groups;
+      {
         const int qg = (G * 128) / S.group;
-        if (r_a < nrows)
-          acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * ((d0[0] + d0[1] + d1[0] + d1[1]) - 128.0f * sb) +
-                   f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
-        if (r_b < nrows)
-          acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * ((d0[2] + d0[3] + d1[2] + d1[3]) - 128.0f * sb) +
-                   f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
+        const float sb = ds[2 * G], sx = ds[2 * G + 1];
+        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * ((d0[0] + d0[1]) - 128.0f * sb) +
+                 f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
+        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * ((d0[2] + d0[3]) - 128.0f * sb) +
+                 f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
+      }
+      if (G1 != G) {
+        const int qg = (G1 * 128) / S.group;
+        const float sb = ds[2 * G1], sx = ds[2 * G1 + 1];
+        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * ((d1[0] + d1[1]) - 128.0f * sb) +
+                 f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
+        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * ((d1[2] + d1[3]) - 128.0f * sb) +
+                 f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
       }
     }
     if (c == 0) {

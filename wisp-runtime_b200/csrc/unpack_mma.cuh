@@ -78,23 +78,26 @@ __device__ __forceinline__ uint32_t pair_window(const uint32_t (&w)[BITS], const
   return w[s.word] >> s.shift;
 }
 
+// pair p of a unit -> one bf16x2 A register
+template <int BITS>
+__device__ __forceinline__ uint32_t unpack_pair(const uint32_t (&w)[BITS], int p) {
+  constexpr uint32_t M = (1u << BITS) - 1u;
+  const PairSpec s = PairTable<BITS>::get(p);
+  if (s.funnel == 2) {
+    // code `lo` from word 0 at p = lo_p, code `hi` from the funnel window: two sources, one extra op
+    const uint32_t lo = (w[0] >> (BITS * s.lo - s.lo_p)) & (M << s.lo_p);
+    const uint32_t hi = pair_window<BITS>(w, s) & (M << (16 + s.hi_p));
+    return (lo | hi) | 0x43004300u;
+  }
+  const uint32_t mask = (M << s.lo_p) | (M << (16 + s.hi_p));
+  return (pair_window<BITS>(w, s) & mask) | 0x43004300u;
+}
+
 // unit words -> 16 bf16x2 A registers (pair order)
 template <int BITS>
 __device__ __forceinline__ void unpack_pairs(const uint32_t (&w)[BITS], uint32_t (&a)[16]) {
 #pragma unroll
-  for (int p = 0; p < 16; ++p) {
-    constexpr uint32_t M = (1u << BITS) - 1u;
-    const PairSpec s = PairTable<BITS>::get(p);
-    if (s.funnel == 2) {
-      // code `lo` from word 0 at p = lo_p, code `hi` from the funnel window: two sources, one extra op
-      const uint32_t lo = (w[0] >> (BITS * s.lo - s.lo_p)) & (M << s.lo_p);
-      const uint32_t hi = pair_window<BITS>(w, s) & (M << (16 + s.hi_p));
-      a[p] = (lo | hi) | 0x43004300u;
-    } else {
-      const uint32_t mask = (M << s.lo_p) | (M << (16 + s.hi_p));
-      a[p] = (pair_window<BITS>(w, s) & mask) | 0x43004300u;
-    }
-  }
+  for (int p = 0; p < 16; ++p) a[p] = unpack_pair<BITS>(w, p);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -131,6 +134,35 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two 128-code groups of a 16-row MMA block (rows g and g+8 per lane), four independent accumulator
+// chains.  wa*/wb*: the lane's unit words of rows g / g+8 for groups 0 and 1; b0/b1: the B pairs
+// (zeros in lanes that hold no B column).  d0/d1 receive the two groups' results.
+template <int BITS>
+__device__ __forceinline__ void mma_two_groups(const uint32_t (&wa0)[BITS], const uint32_t (&wb0)[BITS],
+                                               const uint32_t (&wa1)[BITS], const uint32_t (&wb1)[BITS],
+                                               const uint32_t (&b0)[16], const uint32_t (&b1)[16], float (&d0)[4],
+                                               float (&d1)[4]) {
+  float e0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, e1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d0[i] = d1[i] = 0.0f;
+#pragma unroll
+  for (int m = 0; m < 8; m += 2) {
+    mma_bf16(d0, unpack_pair<BITS>(wa0, 2 * m), unpack_pair<BITS>(wb0, 2 * m), unpack_pair<BITS>(wa0, 2 * m + 1),
+             unpack_pair<BITS>(wb0, 2 * m + 1), b0[2 * m], b0[2 * m + 1]);
+    mma_bf16(d1, unpack_pair<BITS>(wa1, 2 * m), unpack_pair<BITS>(wb1, 2 * m), unpack_pair<BITS>(wa1, 2 * m + 1),
+             unpack_pair<BITS>(wb1, 2 * m + 1), b1[2 * m], b1[2 * m + 1]);
+    mma_bf16(e0, unpack_pair<BITS>(wa0, 2 * m + 2), unpack_pair<BITS>(wb0, 2 * m + 2),
+             unpack_pair<BITS>(wa0, 2 * m + 3), unpack_pair<BITS>(wb0, 2 * m + 3), b0[2 * m + 2], b0[2 * m + 3]);
+    mma_bf16(e1, unpack_pair<BITS>(wa1, 2 * m + 2), unpack_pair<BITS>(wb1, 2 * m + 2),
+             unpack_pair<BITS>(wa1, 2 * m + 3), unpack_pair<BITS>(wb1, 2 * m + 3), b1[2 * m + 2], b1[2 * m + 3]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    d0[i] += e0[i];
+    d1[i] += e1[i];
+  }
 }
 
 }  // namespace wisp
