@@ -9,16 +9,17 @@
 // its twin down CTA will read, so the down kernel, chained by programmatic dependent launch, finds
 // its 1/3 of the layer's bytes in L2.
 //
-// Math.  Codes become bf16 MMA operands with one LOP3 per pair (unpack_mma.cuh) and
-// mma.sync m16n8k16 accumulates in fp32.  Groups are processed in pairs with four independent
-// accumulator chains; lanes that hold no B column read a shared zero block (no divergence).
+// Math.  Codes become u8 operands of the integer MMA (mma.sync m16n8k32, u8 x s8 -> s32) with one AND
+// per 4 codes (unpack_imma.cuh); activations enter as three int8 limbs of a per-group 23-bit fixed
+// point, so every partial sum is an exact int32.  Groups are processed in pairs (independent chains);
+// lanes that hold no B column read a shared zero block (no divergence).
 //   gate/up piece: 8 gate rows (A rows 0-7) + the same 8 up rows (A rows 8-15) over half of H;
 //                  B column 0 = scaled, permuted x.
 //   down piece:    16 output rows of one expert over all of I; B columns 0/1 = bf16 hi/lo of a_j.
 #pragma once
 #include "common.cuh"
 #include "moe_decode.cuh"
-#include "unpack_mma.cuh"
+#include "unpack_imma.cuh"
 
 namespace wisp {
 namespace v4 {
@@ -96,8 +97,8 @@ __host__ __device__ inline GuL gu_layout(int H, int group, int bits) {
   L.stride = L.piece_bytes + row_pad(bits);
   L.sc_bytes = ru16(int64_t(CH) * L.gpr * 2);                // one scale (or min) array of the 8 rows
   L.warp_bytes = ru16(2 * CH * L.stride + 4 * L.sc_bytes);
-  L.off_bx = GU_WARPS * L.warp_bytes;                        // [H/32 units][16] u32
-  L.off_gsum = L.off_bx + int64_t(H / 32) * 16 * 4;          // [H/128][2] f32: (sum of B, sum of x)
+  L.off_bx = GU_WARPS * L.warp_bytes;                        // [H/32 units][3 limbs][8] u32
+  L.off_gsum = L.off_bx + int64_t(H / 32) * 24 * 4;          // [H/128][2] f32: (sum of x, 2^-e)
   L.off_zero = L.off_gsum + int64_t(L.groups) * 2 * 4;       // 64 zero bytes
   L.off_halves = ru16(L.off_zero + 64);                      // [pieces][CH][2] f32
   return L;
@@ -126,21 +127,45 @@ __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bit
   L.stride = L.row_bytes + row_pad(bits);
   L.sc_bytes = ru16(int64_t(16) * L.gpr * 2);
   L.warp_bytes = ru16(16 * L.stride + 2 * L.sc_bytes);
-  L.off_bd = DN_WARPS * L.warp_bytes;                           // [k][units][2 parts][16] u32
-  L.off_dsum = L.off_bd + int64_t(k) * L.units * 2 * 16 * 4;    // [k][groups][2] f32
+  L.off_bd = DN_WARPS * L.warp_bytes;                           // [k][units][3 limbs][8] u32
+  L.off_dsum = L.off_bd + int64_t(k) * L.units * 24 * 4;        // [k][groups][2] f32: (sum of a, 2^-e)
   L.off_zero = L.off_dsum + int64_t(k) * L.groups * 2 * 4;      // 64 zero bytes
   L.off_part = ru16(L.off_zero + 64);                           // [DN_WARPS][16] f32
   L.bytes = L.off_part + DN_WARPS * 16 * 4;
   return L;
 }
 
-__device__ __forceinline__ void lds_b16(const uint32_t* p, uint32_t (&b)[16]) {
+__device__ __forceinline__ void lds_b8(const uint32_t* p, uint32_t (&b)[8]) {
   const uint4* p4 = reinterpret_cast<const uint4*>(p);
+  const uint4 t0 = p4[0], t1 = p4[1];
+  b[0] = t0.x; b[1] = t0.y; b[2] = t0.z; b[3] = t0.w;
+  b[4] = t1.x; b[5] = t1.y; b[6] = t1.z; b[7] = t1.w;
+}
+
+__device__ __forceinline__ float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+// one unit's activations -> its B limbs in shared memory; returns its exponent e (shared by the
+// 4 lanes of the group, which must be the 4 consecutive lanes calling together)
+template <int BITS>
+__device__ __forceinline__ int store_b_limbs(const float (&v)[32], uint32_t* dst, bool store) {
+  float am = 0.0f;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 t = p4[q];
-    b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
+  for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+  const int e = group_exponent(quad_max(am));
+  uint32_t L[3][8];
+  build_b_limbs<BITS>(v, e, L);
+  if (store) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      d4[2 * l] = make_uint4(L[l][0], L[l][1], L[l][2], L[l][3]);
+      d4[2 * l + 1] = make_uint4(L[l][4], L[l][5], L[l][6], L[l][7]);
+    }
   }
+  return e;
 }
 
 // sum over the 4 lanes that hold the 4 units of one 128-code group (lanes 4i..4i+3)
@@ -254,21 +279,14 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
         v[8 * q + 2 * hh + 1] = __uint_as_float(wd[hh] & 0xFFFF0000u);
       }
     }
-    uint32_t b[16];
-    float sb, sx = 0.0f;
-    build_b_pairs<BITS>(v, 0, b, sb);
-    if (u < units) {
-      uint4* d4 = reinterpret_cast<uint4*>(bx + u * 16);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) d4[q] = make_uint4(b[4 * q], b[4 * q + 1], b[4 * q + 2], b[4 * q + 3]);
-    }
+    const int e = store_b_limbs<BITS>(v, bx + u * 24, u < units);
+    float sx = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) sx += v[i];
-    sb = quad_sum(sb);
-    sx = quad_sum(sx);
+    sx = quad_sum(u < units ? sx : 0.0f);
     if (u < units && (u & 3) == 0) {
-      gsum[2 * (u >> 2)] = sb;
-      gsum[2 * (u >> 2) + 1] = sx;
+      gsum[2 * (u >> 2)] = sx;
+      gsum[2 * (u >> 2) + 1] = pow2(-e);
     }
   }
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Lg.off_zero)[threadIdx.x] = 0u;
@@ -302,26 +320,30 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
       __syncwarp();
       if (!ok) continue;
       const int G1 = min(G + 1, ng - 1);  // an odd tail repeats the last group; its result is dropped
-      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[16], bb1[16];
+      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
       lds_unit<BITS>(rowg + (G * 4 + c) * 4 * BITS, wa0);
       lds_unit<BITS>(rowu + (G * 4 + c) * 4 * BITS, wb0);
       lds_unit<BITS>(rowg + (G1 * 4 + c) * 4 * BITS, wa1);
       lds_unit<BITS>(rowu + (G1 * 4 + c) * 4 * BITS, wb1);
-      lds_b16(g == 0 ? bx + (4 * (G0 + G) + c) * 16 : zero, bb0);
-      lds_b16(g == 0 ? bx + (4 * (G0 + G1) + c) * 16 : zero, bb1);
-      float d0[4], d1[4];
-      mma_two_groups<BITS>(wa0, wb0, wa1, wb1, bb0, bb1, d0, d1);
+      lds_b8(g < 3 ? bx + ((4 * (G0 + G) + c) * 3 + g) * 8 : zero, bb0);
+      lds_b8(g < 3 ? bx + ((4 * (G0 + G1) + c) * 3 + g) * 8 : zero, bb1);
+      int d0[4], d1[4];
+      imma_group<BITS>(wa0, wb0, bb0, d0);
+      imma_group<BITS>(wa1, wb1, bb1, d1);
+      // limb column 2 of rows g / g+8 sits in lane (g, 1)
+      const int n0a = __shfl_down_sync(0xffffffffu, d0[0], 1), n0b = __shfl_down_sync(0xffffffffu, d0[2], 1);
+      const int n1a = __shfl_down_sync(0xffffffffu, d1[0], 1), n1b = __shfl_down_sync(0xffffffffu, d1[2], 1);
       {
         const int qg = ((G0 + G) * 128) / S.group;
-        const float sb = gsum[2 * (G0 + G)], sx = gsum[2 * (G0 + G) + 1];
-        accg += f16_bits_to_f32(ssg[qg]) * (d0[0] - 128.0f * sb) + f16_bits_to_f32(smg[qg]) * sx;
-        accu += f16_bits_to_f32(ssu[qg]) * (d0[2] - 128.0f * sb) + f16_bits_to_f32(smu[qg]) * sx;
+        const float sx = gsum[2 * (G0 + G)], fi = gsum[2 * (G0 + G) + 1];
+        accg += f16_bits_to_f32(ssg[qg]) * (limbs_to_float(d0[0], d0[1], n0a) * fi) + f16_bits_to_f32(smg[qg]) * sx;
+        accu += f16_bits_to_f32(ssu[qg]) * (limbs_to_float(d0[2], d0[3], n0b) * fi) + f16_bits_to_f32(smu[qg]) * sx;
       }
       if (G1 != G) {
         const int qg = ((G0 + G1) * 128) / S.group;
-        const float sb = gsum[2 * (G0 + G1)], sx = gsum[2 * (G0 + G1) + 1];
-        accg += f16_bits_to_f32(ssg[qg]) * (d1[0] - 128.0f * sb) + f16_bits_to_f32(smg[qg]) * sx;
-        accu += f16_bits_to_f32(ssu[qg]) * (d1[2] - 128.0f * sb) + f16_bits_to_f32(smu[qg]) * sx;
+        const float sx = gsum[2 * (G0 + G1)], fi = gsum[2 * (G0 + G1) + 1];
+        accg += f16_bits_to_f32(ssg[qg]) * (limbs_to_float(d1[0], d1[1], n1a) * fi) + f16_bits_to_f32(smg[qg]) * sx;
+        accu += f16_bits_to_f32(ssu[qg]) * (limbs_to_float(d1[2], d1[3], n1b) * fi) + f16_bits_to_f32(smu[qg]) * sx;
       }
     }
     if (c == 0) {
@@ -408,27 +430,15 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
       const float4 f = ap[q];
       v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
     }
-    uint32_t b0[16], b1[16];
-    float sb0, sb1, sx = 0.0f;
-    build_b_pairs<BITS>(v, 0, b0, sb0);
-    build_b_pairs<BITS>(v, 1, b1, sb1);
-    if (t < ntask) {
-      uint4* d0 = reinterpret_cast<uint4*>(bd + (int64_t(t) * 2) * 16);
-      uint4* d1 = reinterpret_cast<uint4*>(bd + (int64_t(t) * 2 + 1) * 16);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        d0[q] = make_uint4(b0[4 * q], b0[4 * q + 1], b0[4 * q + 2], b0[4 * q + 3]);
-        d1[q] = make_uint4(b1[4 * q], b1[4 * q + 1], b1[4 * q + 2], b1[4 * q + 3]);
-      }
-    }
+    const int e = store_b_limbs<BITS>(v, bd + int64_t(t) * 24, t < ntask);
+    float sx = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) sx += v[i];
     // the 4 units of a group sit in 4 consecutive lanes (units % 4 == 0 and tb % 32 == 0)
-    const float sb = quad_sum(sb0 + sb1);
     sx = quad_sum(sx);
     if (t < ntask && (u & 3) == 0) {
-      dsum[2 * (j * Ld.groups + (u >> 2))] = sb;
-      dsum[2 * (j * Ld.groups + (u >> 2)) + 1] = sx;
+      dsum[2 * (j * Ld.groups + (u >> 2))] = sx;
+      dsum[2 * (j * Ld.groups + (u >> 2)) + 1] = pow2(-e);
     }
   }
   __syncthreads();
@@ -447,33 +457,36 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
     if (!ok) continue;
     const int r_a = g, r_b = g + 8;
     float acc_a = 0.0f, acc_b = 0.0f;
-    const uint32_t* bj = bd + int64_t(j) * units * 32;
+    const uint32_t* bj = bd + int64_t(j) * units * 24;
     for (int G = 0; G < Ld.groups; G += 2) {
       const int G1 = min(G + 1, Ld.groups - 1);
-      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[16], bb1[16];
+      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
       lds_unit<BITS>(wreg + r_a * Ld.stride + (4 * G + c) * 4 * BITS, wa0);
       lds_unit<BITS>(wreg + r_b * Ld.stride + (4 * G + c) * 4 * BITS, wb0);
       lds_unit<BITS>(wreg + r_a * Ld.stride + (4 * G1 + c) * 4 * BITS, wa1);
       lds_unit<BITS>(wreg + r_b * Ld.stride + (4 * G1 + c) * 4 * BITS, wb1);
-      lds_b16(g < 2 ? bj + (4 * G + c) * 32 + g * 16 : zero, bb0);
-      lds_b16(g < 2 ? bj + (4 * G1 + c) * 32 + g * 16 : zero, bb1);
-      float d0[4], d1[4];
-      mma_two_groups<BITS>(wa0, wb0, wa1, wb1, bb0, bb1, d0, d1);
+      lds_b8(g < 3 ? bj + ((4 * G + c) * 3 + g) * 8 : zero, bb0);
+      lds_b8(g < 3 ? bj + ((4 * G1 + c) * 3 + g) * 8 : zero, bb1);
+      int d0[4], d1[4];
+      imma_group<BITS>(wa0, wb0, bb0, d0);
+      imma_group<BITS>(wa1, wb1, bb1, d1);
+      const int n0a = __shfl_down_sync(0xffffffffu, d0[0], 1), n0b = __shfl_down_sync(0xffffffffu, d0[2], 1);
+      const int n1a = __shfl_down_sync(0xffffffffu, d1[0], 1), n1b = __shfl_down_sync(0xffffffffu, d1[2], 1);
       const float* ds = dsum + 2 * int64_t(j) * Ld.groups;
       {
         const int qg = (G * 128) / S.group;
-        const float sb = ds[2 * G], sx = ds[2 * G + 1];
-        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * ((d0[0] + d0[1]) - 128.0f * sb) +
+        const float sx = ds[2 * G], fi = ds[2 * G + 1];
+        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * (limbs_to_float(d0[0], d0[1], n0a) * fi) +
                  f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
-        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * ((d0[2] + d0[3]) - 128.0f * sb) +
+        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * (limbs_to_float(d0[2], d0[3], n0b) * fi) +
                  f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
       }
       if (G1 != G) {
         const int qg = (G1 * 128) / S.group;
-        const float sb = ds[2 * G1], sx = ds[2 * G1 + 1];
-        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * ((d1[0] + d1[1]) - 128.0f * sb) +
+        const float sx = ds[2 * G1], fi = ds[2 * G1 + 1];
+        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * (limbs_to_float(d1[0], d1[1], n1a) * fi) +
                  f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
-        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * ((d1[2] + d1[3]) - 128.0f * sb) +
+        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * (limbs_to_float(d1[2], d1[3], n1b) * fi) +
                  f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
       }
     }
