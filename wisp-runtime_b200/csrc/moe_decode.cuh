@@ -12,6 +12,7 @@ namespace wisp {
 struct MoeShape {
   int64_t nslots, nbytes;
   int k, H, I, group;
+  int gshift;         // log2(group / 128) when group is 128 * 2^s (tensor-core path), else 0
   int64_t ncode;      // bytes of the code region
   int64_t ng;         // groups per expert
   int64_t mat_bytes;  // code bytes per matrix

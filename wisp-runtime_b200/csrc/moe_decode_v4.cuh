@@ -25,11 +25,11 @@ namespace wisp {
 namespace v4 {
 
 constexpr int GU_WARPS = 16;
-constexpr int DN_WARPS = 8;
+constexpr int DN_WARPS = 16;
 constexpr int GU_THREADS = GU_WARPS * 32;
 constexpr int DN_THREADS = DN_WARPS * 32;
 constexpr int CH = 8;      // rows per gate/up piece (A rows 0-7 gate, 8-15 up)
-constexpr int NSPLIT = 2;  // gate/up pieces split H in two halves
+constexpr int NSPLIT = 2;  // gate/up pieces split H in two halves; down pieces split I in two halves
 constexpr int MAXG = 16;   // max 128-code groups per piece (commit groups in flight)
 
 __host__ __device__ constexpr int row_pad(int bits) { return 16 * bits; }
@@ -113,18 +113,20 @@ __host__ __device__ inline int64_t gu_smem(int H, int I, int k, int group, int b
 }
 
 struct DnL {
-  int groups, gpr, units;
-  int64_t row_bytes, stride, sc_bytes, warp_bytes;
+  int groups, groups_per_piece, gpr, units;
+  int64_t row_bytes, piece_bytes, stride, sc_bytes, warp_bytes;
   int64_t off_bd, off_dsum, off_zero, off_part, bytes;
 };
 
 __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bits) {
   DnL L;
   L.groups = I / 128;
+  L.groups_per_piece = (L.groups + NSPLIT - 1) / NSPLIT;
   L.gpr = I / group;
   L.units = I / 32;
   L.row_bytes = int64_t(I) * bits / 8;
-  L.stride = L.row_bytes + row_pad(bits);
+  L.piece_bytes = int64_t(L.groups_per_piece) * 16 * bits;  // code bytes of one row inside a piece
+  L.stride = L.piece_bytes + row_pad(bits);
   L.sc_bytes = ru16(int64_t(16) * L.gpr * 2);
   L.warp_bytes = ru16(16 * L.stride + 2 * L.sc_bytes);
   L.off_bd = DN_WARPS * L.warp_bytes;                           // [k][units][3 limbs][8] u32
@@ -232,10 +234,10 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int h = (ng + 1) / 2;
     if (ok) {
       const int words = CH * Lg.gpr / 2;  // 4-byte words per array (2*gpr bytes per row, gpr even)
-      for (int t = lane; t < 4 * words; t += 32) {
-        const int arr = t / words, wd = t - arr * words;  // 0 gate s, 1 gate m, 2 up s, 3 up m
-        const int64_t off = S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr) + 4 * wd;
-        cp_async4(wreg + 2 * CH * Lg.stride + arr * Lg.sc_bytes + 4 * wd, base + off);
+#pragma unroll
+      for (int arr = 0; arr < 4; ++arr) {  // 0 gate s, 1 gate m, 2 up s, 3 up m
+        const uint8_t* srca = base + S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr);
+        for (int wd = lane; wd < words; wd += 32) cp_async4(wreg + 2 * CH * Lg.stride + arr * Lg.sc_bytes + 4 * wd, srca + 4 * wd);
       }
     }
     cp_commit();
@@ -306,14 +308,13 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int G0 = sp * Lg.groups_per_piece;
     const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
     const int h = (ng + 1) / 2;
+    // lane c = 0 finishes the gate row g, lane c = 1 the up row g (same instructions, quad_row_dot)
     const uint8_t* sw = wreg + 2 * CH * Lg.stride;
-    const uint16_t* ssg = reinterpret_cast<const uint16_t*>(sw) + g * Lg.gpr;
-    const uint16_t* smg = reinterpret_cast<const uint16_t*>(sw + Lg.sc_bytes) + g * Lg.gpr;
-    const uint16_t* ssu = reinterpret_cast<const uint16_t*>(sw + 2 * Lg.sc_bytes) + g * Lg.gpr;
-    const uint16_t* smu = reinterpret_cast<const uint16_t*>(sw + 3 * Lg.sc_bytes) + g * Lg.gpr;
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(sw + (c == 1 ? 2 : 0) * Lg.sc_bytes) + g * Lg.gpr;
+    const uint16_t* mrow = reinterpret_cast<const uint16_t*>(sw + (c == 1 ? 3 : 1) * Lg.sc_bytes) + g * Lg.gpr;
     const uint8_t* rowg = wreg + g * Lg.stride;
     const uint8_t* rowu = wreg + (CH + g) * Lg.stride;
-    float accg = 0.0f, accu = 0.0f;
+    float acc = 0.0f;
     for (int G = 0; G < ng; G += 2) {
       if (G == 0) cp_wait<1>();   // scales + first half landed
       if (G == h) cp_wait<0>();   // second half landed
@@ -330,26 +331,17 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
       int d0[4], d1[4];
       imma_group<BITS>(wa0, wb0, bb0, d0);
       imma_group<BITS>(wa1, wb1, bb1, d1);
-      // limb column 2 of rows g / g+8 sits in lane (g, 1)
-      const int n0a = __shfl_down_sync(0xffffffffu, d0[0], 1), n0b = __shfl_down_sync(0xffffffffu, d0[2], 1);
-      const int n1a = __shfl_down_sync(0xffffffffu, d1[0], 1), n1b = __shfl_down_sync(0xffffffffu, d1[2], 1);
+      const float D0 = quad_row_dot(d0, c), D1 = quad_row_dot(d1, c);
       {
-        const int qg = ((G0 + G) * 128) / S.group;
-        const float sx = gsum[2 * (G0 + G)], fi = gsum[2 * (G0 + G) + 1];
-        accg += f16_bits_to_f32(ssg[qg]) * (limbs_to_float(d0[0], d0[1], n0a) * fi) + f16_bits_to_f32(smg[qg]) * sx;
-        accu += f16_bits_to_f32(ssu[qg]) * (limbs_to_float(d0[2], d0[3], n0b) * fi) + f16_bits_to_f32(smu[qg]) * sx;
+        const int qg = (G0 + G) >> S.gshift;
+        acc += f16_bits_to_f32(srow[qg]) * (D0 * gsum[2 * (G0 + G) + 1]) + f16_bits_to_f32(mrow[qg]) * gsum[2 * (G0 + G)];
       }
       if (G1 != G) {
-        const int qg = ((G0 + G1) * 128) / S.group;
-        const float sx = gsum[2 * (G0 + G1)], fi = gsum[2 * (G0 + G1) + 1];
-        accg += f16_bits_to_f32(ssg[qg]) * (limbs_to_float(d1[0], d1[1], n1a) * fi) + f16_bits_to_f32(smg[qg]) * sx;
-        accu += f16_bits_to_f32(ssu[qg]) * (limbs_to_float(d1[2], d1[3], n1b) * fi) + f16_bits_to_f32(smu[qg]) * sx;
+        const int qg = (G0 + G1) >> S.gshift;
+        acc += f16_bits_to_f32(srow[qg]) * (D1 * gsum[2 * (G0 + G1) + 1]) + f16_bits_to_f32(mrow[qg]) * gsum[2 * (G0 + G1)];
       }
     }
-    if (c == 0) {
-      halves[(piece * CH + g) * 2] = accg;
-      halves[(piece * CH + g) * 2 + 1] = accu;
-    }
+    if (c < 2) halves[(piece * CH + g) * 2 + c] = acc;
   }
   __syncthreads();
   // ---- SwiGLU of complete rows: sum the K parts of each block in a fixed order, write a once
@@ -385,39 +377,41 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   const int nrows = h1 - h0;
   const int64_t ngm = S.ng / 3;
   const int units = Ld.units;
+  const int npieces = S.k * NSPLIT;  // (expert, K half)
   uint8_t* wreg = sm + int64_t(warp) * Ld.warp_bytes;
   const uint16_t* ss = reinterpret_cast<const uint16_t*>(wreg + 16 * Ld.stride);
   const uint16_t* smn = reinterpret_cast<const uint16_t*>(wreg + 16 * Ld.stride + Ld.sc_bytes);
 
-  // ---- warp w streams the down rows of experts w, w+DN_WARPS, ... (the routing is final already;
-  //      the gate/up grid prefetched these rows into L2)
-  auto issue_expert = [&](int j) {
+  // ---- warp w streams piece w (the routing is final already; the gate/up grid prefetched these rows
+  //      into L2): rows h0..h1 of expert j, code bytes of one K half, plus the rows' scales and mins
+  auto issue_piece = [&](int piece) {
+    const int j = piece / NSPLIT, sp = piece % NSPLIT;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
-    if (!ok && lane == 0) flag(WISP_STATUS_BAD_SLOT);
+    if (!ok && lane == 0 && sp == 0) flag(WISP_STATUS_BAD_SLOT);
     if (ok && nrows > 0) {
       const uint8_t* base = pool + slot * S.nbytes;
-      const int chunks = int(Ld.row_bytes / 16);
-      for (int t = lane; t < nrows * chunks; t += 32) {
-        const int r = t / chunks, q = t - r * chunks;
-        cp_async16(wreg + r * Ld.stride + 16 * q, base + 2 * S.mat_bytes + int64_t(h0 + r) * Ld.row_bytes + 16 * q);
-      }
+      const int chunks = int(Ld.piece_bytes / 16);
+      const int64_t koff = int64_t(sp) * Ld.groups_per_piece * 16 * BITS;
+      for (int r = 0; r < nrows; ++r)
+        for (int q = lane; q < chunks; q += 32)
+          cp_async16(wreg + r * Ld.stride + 16 * q, base + 2 * S.mat_bytes + int64_t(h0 + r) * Ld.row_bytes + koff + 16 * q);
       const int words = nrows * Ld.gpr / 2;
-      for (int t = lane; t < 2 * words; t += 32) {
-        const int arr = t / words, wd = t - arr * words;
-        const int64_t off = S.ncode + 2 * (arr * S.ng + 2 * ngm + int64_t(h0) * Ld.gpr) + 4 * wd;
-        cp_async4(wreg + 16 * Ld.stride + arr * Ld.sc_bytes + 4 * wd, base + off);
+#pragma unroll
+      for (int arr = 0; arr < 2; ++arr) {
+        const uint8_t* srca = base + S.ncode + 2 * (arr * S.ng + 2 * ngm + int64_t(h0) * Ld.gpr);
+        for (int wd = lane; wd < words; wd += 32) cp_async4(wreg + 16 * Ld.stride + arr * Ld.sc_bytes + 4 * wd, srca + 4 * wd);
       }
     }
     cp_commit();
   };
-  if (warp < S.k) issue_expert(warp);
+  if (warp < npieces) issue_piece(warp);
   for (int i = threadIdx.x; i < DN_WARPS * 16; i += blockDim.x) part[i] = 0.0f;
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Ld.off_zero)[threadIdx.x] = 0u;
 
   pdl_wait();  // a is written by the gate/up grid
 
-  // ---- B operand of every routed expert, CTA-wide: one thread per (expert, unit), both parts.
+  // ---- B limbs of every routed expert, CTA-wide: one thread per (expert, unit).
   //      Warp-uniform loop (quad shuffles need every lane); tail lanes redo the last unit, store nothing.
   const int ntask = S.k * units;
   for (int tb = int(threadIdx.x) & ~31; tb < ntask; tb += blockDim.x) {
@@ -443,57 +437,51 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   }
   __syncthreads();
 
-  for (int j = warp; j < S.k; j += DN_WARPS) {
-    if (j != warp) {
+  for (int piece = warp; piece < npieces; piece += DN_WARPS) {
+    if (piece != warp) {
       cp_wait<0>();
       __syncwarp();
-      issue_expert(j);
+      issue_piece(piece);
     }
+    const int j = piece / NSPLIT, sp = piece % NSPLIT;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
     const float wj = meta[S.k + j];
     cp_wait<0>();
     __syncwarp();
     if (!ok) continue;
-    const int r_a = g, r_b = g + 8;
-    float acc_a = 0.0f, acc_b = 0.0f;
+    // lane c = 0 finishes output row g, lane c = 1 row g + 8
+    const int myrow = (c == 1) ? g + 8 : g;
+    const uint16_t* srow = ss + myrow * Ld.gpr;
+    const uint16_t* mrow = smn + myrow * Ld.gpr;
+    const int G0 = sp * Ld.groups_per_piece;
+    const int ng = min(Ld.groups_per_piece, Ld.groups - G0);
+    float acc = 0.0f;
     const uint32_t* bj = bd + int64_t(j) * units * 24;
-    for (int G = 0; G < Ld.groups; G += 2) {
-      const int G1 = min(G + 1, Ld.groups - 1);
+    const float* ds = dsum + 2 * int64_t(j) * Ld.groups;
+    for (int G = 0; G < ng; G += 2) {
+      const int G1 = min(G + 1, ng - 1);
       uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
-      lds_unit<BITS>(wreg + r_a * Ld.stride + (4 * G + c) * 4 * BITS, wa0);
-      lds_unit<BITS>(wreg + r_b * Ld.stride + (4 * G + c) * 4 * BITS, wb0);
-      lds_unit<BITS>(wreg + r_a * Ld.stride + (4 * G1 + c) * 4 * BITS, wa1);
-      lds_unit<BITS>(wreg + r_b * Ld.stride + (4 * G1 + c) * 4 * BITS, wb1);
-      lds_b8(g < 3 ? bj + ((4 * G + c) * 3 + g) * 8 : zero, bb0);
-      lds_b8(g < 3 ? bj + ((4 * G1 + c) * 3 + g) * 8 : zero, bb1);
+      lds_unit<BITS>(wreg + g * Ld.stride + (4 * G + c) * 4 * BITS, wa0);
+      lds_unit<BITS>(wreg + (g + 8) * Ld.stride + (4 * G + c) * 4 * BITS, wb0);
+      lds_unit<BITS>(wreg + g * Ld.stride + (4 * G1 + c) * 4 * BITS, wa1);
+      lds_unit<BITS>(wreg + (g + 8) * Ld.stride + (4 * G1 + c) * 4 * BITS, wb1);
+      lds_b8(g < 3 ? bj + ((4 * (G0 + G) + c) * 3 + g) * 8 : zero, bb0);
+      lds_b8(g < 3 ? bj + ((4 * (G0 + G1) + c) * 3 + g) * 8 : zero, bb1);
       int d0[4], d1[4];
       imma_group<BITS>(wa0, wb0, bb0, d0);
       imma_group<BITS>(wa1, wb1, bb1, d1);
-      const int n0a = __shfl_down_sync(0xffffffffu, d0[0], 1), n0b = __shfl_down_sync(0xffffffffu, d0[2], 1);
-      const int n1a = __shfl_down_sync(0xffffffffu, d1[0], 1), n1b = __shfl_down_sync(0xffffffffu, d1[2], 1);
-      const float* ds = dsum + 2 * int64_t(j) * Ld.groups;
+      const float D0 = quad_row_dot(d0, c), D1 = quad_row_dot(d1, c);
       {
-        const int qg = (G * 128) / S.group;
-        const float sx = ds[2 * G], fi = ds[2 * G + 1];
-        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * (limbs_to_float(d0[0], d0[1], n0a) * fi) +
-                 f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
-        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * (limbs_to_float(d0[2], d0[3], n0b) * fi) +
-                 f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
+        const int qg = (G0 + G) >> S.gshift;
+        acc += f16_bits_to_f32(srow[qg]) * (D0 * ds[2 * (G0 + G) + 1]) + f16_bits_to_f32(mrow[qg]) * ds[2 * (G0 + G)];
       }
       if (G1 != G) {
-        const int qg = (G1 * 128) / S.group;
-        const float sx = ds[2 * G1], fi = ds[2 * G1 + 1];
-        acc_a += f16_bits_to_f32(ss[r_a * Ld.gpr + qg]) * (limbs_to_float(d1[0], d1[1], n1a) * fi) +
-                 f16_bits_to_f32(smn[r_a * Ld.gpr + qg]) * sx;
-        acc_b += f16_bits_to_f32(ss[r_b * Ld.gpr + qg]) * (limbs_to_float(d1[2], d1[3], n1b) * fi) +
-                 f16_bits_to_f32(smn[r_b * Ld.gpr + qg]) * sx;
+        const int qg = (G0 + G1) >> S.gshift;
+        acc += f16_bits_to_f32(srow[qg]) * (D1 * ds[2 * (G0 + G1) + 1]) + f16_bits_to_f32(mrow[qg]) * ds[2 * (G0 + G1)];
       }
     }
-    if (c == 0) {
-      if (r_a < nrows) part[warp * 16 + r_a] += wj * acc_a;
-      if (r_b < nrows) part[warp * 16 + r_b] += wj * acc_b;
-    }
+    if (c < 2 && myrow < nrows) part[warp * 16 + myrow] += wj * acc;
   }
   __syncthreads();
   for (int r = threadIdx.x; r < nrows; r += blockDim.x) {

@@ -107,27 +107,30 @@ __device__ __forceinline__ int group_exponent(float amax) {
 }
 __device__ __forceinline__ float pow2(int e) { return __uint_as_float(uint32_t(e + 127) << 23); }
 
-// B limbs of one unit: L[limb][r] for the 8 registers (limb 0 = 2^16, 1 = 2^8, 2 = 1)
+// B limbs of one unit: L[limb][r] for the 8 registers (limb 0 = 2^16, 1 = 2^8, 2 = 1).
+// For |xs| < 2^22 the balanced base-256 digits of xs (each in [-128, 127]) are exactly the bytes of
+// (xs + 0x808080) ^ 0x808080 read as int8: adding 128 to every digit makes the digits of a 24-bit
+// unsigned number, and XOR 0x80 turns a digit d + 128 back into the two's-complement byte of d.
+// The magic-number rounding yields 0x4B400000 + xs, so one IADD and one XOR give all three limbs.
 template <int BITS>
 __device__ __forceinline__ void build_b_limbs(const float (&v)[32], int e, uint32_t (&L)[3][8]) {
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const ByteReg R = ByteTable<BITS>::get(r);
-    uint32_t l0 = 0, l1 = 0, l2 = 0;
+    uint32_t y[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const int xs = small_f2i(v[R.code[b]] * pow2(e - R.p[b]));
-      const int lo = ((xs + 128) & 255) - 128;
-      const int rest = (xs - lo) >> 8;
-      const int mid = ((rest + 128) & 255) - 128;
-      const int hi = (rest - mid) >> 8;
-      l0 |= uint32_t(hi & 255) << (8 * b);
-      l1 |= uint32_t(mid & 255) << (8 * b);
-      l2 |= uint32_t(lo & 255) << (8 * b);
+      const float f = v[R.code[b]] * pow2(e - R.p[b]) + 12582912.0f;  // round to nearest even
+      y[b] = (__float_as_uint(f) + (0x808080u - 0x4B400000u)) ^ 0x808080u;
     }
-    L[0][r] = l0;
-    L[1][r] = l1;
-    L[2][r] = l2;
+    // gather byte l of y0..y3 into limb register l
+    const uint32_t p01 = __byte_perm(y[0], y[1], 0x5140);  // y0.b0 y1.b0 y0.b1 y1.b1
+    const uint32_t p23 = __byte_perm(y[2], y[3], 0x5140);
+    const uint32_t q01 = __byte_perm(y[0], y[1], 0x0062);  // y0.b2 y1.b2 . .
+    const uint32_t q23 = __byte_perm(y[2], y[3], 0x6200);  // . . y2.b2 y3.b2
+    L[2][r] = __byte_perm(p01, p23, 0x5410);               // lo limbs
+    L[1][r] = __byte_perm(p01, p23, 0x7632);               // mid limbs
+    L[0][r] = __byte_perm(q01, q23, 0x7610);               // hi limbs
   }
 }
 
@@ -156,9 +159,14 @@ __device__ __forceinline__ void imma_group(const uint32_t (&wa)[BITS], const uin
   for (int i = 0; i < 4; ++i) d[i] += e[i];
 }
 
-// combine the three limb columns of a row held by lanes (g, 0) [cols 0, 1] and (g, 1) [col 2]
-__device__ __forceinline__ float limbs_to_float(int d_col0, int d_col1, int d_col2_from_next_lane) {
-  return (small_i2f(d_col0) * 65536.0f + small_i2f(d_col1) * 256.0f) + small_i2f(d_col2_from_next_lane);
+// Dot product of one 16-row block row per lane, from the limb columns (cols 0/1 in lane (g,0), col 2
+// in lane (g,1)): lane c = 0 gets row g, lane c = 1 gets row g+8, both in the same instructions.
+__device__ __forceinline__ float quad_row_dot(const int (&d)[4], int c) {
+  const int x = __shfl_xor_sync(0xffffffffu, d[0], 1);  // c=0: row g col 2
+  const int y = __shfl_xor_sync(0xffffffffu, d[2], 1);  // c=1: row g+8 col 0
+  const int z = __shfl_xor_sync(0xffffffffu, d[3], 1);  // c=1: row g+8 col 1
+  const int c0 = c == 0 ? d[0] : y, c1 = c == 0 ? d[1] : z, c2 = c == 0 ? x : d[2];
+  return (small_i2f(c0) * 65536.0f + small_i2f(c1) * 256.0f) + small_i2f(c2);
 }
 
 }  // namespace wisp

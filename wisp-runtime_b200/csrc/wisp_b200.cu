@@ -178,6 +178,8 @@ static int moe_shape(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   S.ncode = 3 * n * bits / 8;
   S.ng = 3 * n / group;
   S.mat_bytes = n * bits / 8;
+  S.gshift = 0;
+  for (int gq = group / 128; gq > 1 && (gq & 1) == 0; gq >>= 1) ++S.gshift;
   return WISP_OK;
 }
 
@@ -253,7 +255,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
 // straddling experts, at most 16 down rows per CTA, and both kernels' shared memory fits
 static bool v4_supported(const MoeShape& S, int bits, int nctas) {
   if (bits != 4 && bits != 3 && bits != 2) return false;
-  if (S.group % 128 != 0 || S.H % 128 != 0 || S.I % 128 != 0) return false;
+  if (S.group % 128 != 0 || (128 << S.gshift) != S.group || S.H % 128 != 0 || S.I % 128 != 0) return false;
   if ((S.H / S.group) % 2 || (S.I / S.group) % 2 || S.ng % 2) return false;
   if (S.ncode % 16 || S.mat_bytes % 16 || (int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
   if ((S.H + nctas - 1) / nctas > 16) return false;
