@@ -1,13 +1,13 @@
-// Fused MoE decode for one token: persistent per-warp cp.async pipelines feeding warp-level MMA.
+// Fused MoE decode for one token: TMA bulk copies (cp.async.bulk, no multicast) feeding warp-level MMA.
 //
-// Data movement.  Every warp owns one piece of work and streams exactly the bytes of that piece from
-// the slot pool into its own shared-memory region with 16-byte cp.async copies issued by all 32 lanes
-// (one commit group per 128-code MMA group, so compute starts on group 0 while later groups are still
-// in flight).  Rows land at stride (bytes + 16*BITS), which makes the per-lane fragment loads
-// bank-conflict free.  No CTA-wide barrier sits between issuing and consuming.  While it streams the
-// gate/up rows, each gate/up CTA also prefetches into L2 (cp.async.bulk.prefetch.L2) the down rows
-// its twin down CTA will read, so the down kernel, chained by programmatic dependent launch, finds
-// its 1/3 of the layer's bytes in L2.
+// Data movement.  gate/up: every warp owns one piece of work (8 gate + the same 8 up rows over one K
+// half) and brings exactly its bytes from the slot pool into its own shared-memory region with one
+// bulk copy per row, issued by lanes 0-15, plus four scale/min windows issued by lanes 16-19; all
+// complete on the warp's mbarrier.  Rows land at stride (bytes + 16*BITS), which makes the per-lane
+// fragment loads bank-conflict free.  No CTA-wide barrier sits between issuing and consuming.
+// down: the CTA's output rows are contiguous in each expert's down matrix, so one bulk copy per
+// routed expert (plus two windows) brings them in; it is issued before the grid waits on the gate/up
+// grid (programmatic dependent launch), so the down weights stream while gate/up still computes.
 //
 // Math.  Codes become u8 operands of the integer MMA (mma.sync m16n8k32, u8 x s8 -> s32) with one AND
 // per 4 codes (unpack_imma.cuh); activations enter as three int8 limbs of a per-group 23-bit fixed
@@ -30,37 +30,55 @@ constexpr int GU_THREADS = GU_WARPS * 32;
 constexpr int DN_THREADS = DN_WARPS * 32;
 constexpr int CH = 8;      // rows per gate/up piece (A rows 0-7 gate, 8-15 up)
 constexpr int NSPLIT = 2;  // gate/up pieces split H in two halves; down pieces split I in two halves
-constexpr int MAXG = 16;   // max 128-code groups per piece (commit groups in flight)
+constexpr int MAXG = 16;   // max 128-code groups per piece
 
 __host__ __device__ constexpr int row_pad(int bits) { return 16 * bits; }
 __host__ __device__ inline int64_t ru16(int64_t v) { return (v + 15) & ~int64_t(15); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+constexpr unsigned WAIT_LIMIT = 1u << 24;  // bounded polling; a copy that never lands sets WAIT_TIMEOUT
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
-// wait until at most n groups are pending (n runtime, 0..MAXG)
-__device__ __forceinline__ void cp_wait_n(int n) {
-  switch (n) {
-#define W(k) \
-  case k:    \
-    cp_wait<k>(); break;
-    W(0) W(1) W(2) W(3) W(4) W(5) W(6) W(7) W(8) W(9) W(10) W(11) W(12) W(13) W(14) W(15)
-#undef W
-    default: cp_wait<16>(); break;
-  }
+// bounded wait on the given phase parity; flags and returns false if it gave up
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (unsigned it = 0; it < WAIT_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  flag(WISP_STATUS_WAIT_TIMEOUT);
+  return false;
 }
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// TMA bulk copy global -> shared (no multicast), completing on an mbarrier
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// 16-byte aligned window [start, start+bytes) covering [off, off+len); skip = off - start
+struct Win {
+  int64_t start;
+  uint32_t bytes, skip;
+};
+__device__ __forceinline__ Win window(int64_t off, int64_t len) {
+  Win w;
+  w.start = off & ~int64_t(15);
+  w.bytes = uint32_t(ru16(off + len) - w.start);
+  w.skip = uint32_t(off - w.start);
+  return w;
 }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -84,7 +102,7 @@ __device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) 
 // ------------------------------------------------------------------------------------------------
 struct GuL {
   int groups, groups_per_piece, gpr;  // 128-code groups per row / per piece; quant groups per row
-  int64_t piece_bytes, stride, sc_bytes, warp_bytes;
+  int64_t piece_bytes, stride, sc_win, warp_bytes;
   int64_t off_bx, off_gsum, off_zero, off_halves;
 };
 
@@ -95,8 +113,8 @@ __host__ __device__ inline GuL gu_layout(int H, int group, int bits) {
   L.gpr = H / group;
   L.piece_bytes = int64_t(L.groups_per_piece) * 16 * bits;  // code bytes of one row inside a piece
   L.stride = L.piece_bytes + row_pad(bits);
-  L.sc_bytes = ru16(int64_t(CH) * L.gpr * 2);                // one scale (or min) array of the 8 rows
-  L.warp_bytes = ru16(2 * CH * L.stride + 4 * L.sc_bytes);
+  L.sc_win = ru16(int64_t(CH) * L.gpr * 2) + 16;             // one scale (or min) window of the 8 rows
+  L.warp_bytes = ru16(2 * CH * L.stride + 4 * L.sc_win + 8);  // + the warp's mbarrier
   L.off_bx = GU_WARPS * L.warp_bytes;                        // [H/32 units][3 limbs][8] u32
   L.off_gsum = L.off_bx + int64_t(H / 32) * 24 * 4;          // [H/128][2] f32: (sum of x, 2^-e)
   L.off_zero = L.off_gsum + int64_t(L.groups) * 2 * 4;       // 64 zero bytes
@@ -113,27 +131,29 @@ __host__ __device__ inline int64_t gu_smem(int H, int I, int k, int group, int b
 }
 
 struct DnL {
-  int groups, groups_per_piece, gpr, units;
-  int64_t row_bytes, piece_bytes, stride, sc_bytes, warp_bytes;
-  int64_t off_bd, off_dsum, off_zero, off_part, bytes;
+  int groups, groups_per_piece, gpr, units, rows_max;
+  int64_t row_bytes, sc_win, per_expert;
+  int64_t off_bd, off_dsum, off_zero, off_part, off_bar, bytes;
 };
 
-__host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bits) {
+__host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bits, int nctas) {
   DnL L;
   L.groups = I / 128;
   L.groups_per_piece = (L.groups + NSPLIT - 1) / NSPLIT;
   L.gpr = I / group;
   L.units = I / 32;
+  L.rows_max = (H + nctas - 1) / nctas;  // <= 16 (checked on the host)
   L.row_bytes = int64_t(I) * bits / 8;
-  L.piece_bytes = int64_t(L.groups_per_piece) * 16 * bits;  // code bytes of one row inside a piece
-  L.stride = L.piece_bytes + row_pad(bits);
-  L.sc_bytes = ru16(int64_t(16) * L.gpr * 2);
-  L.warp_bytes = ru16(16 * L.stride + 2 * L.sc_bytes);
-  L.off_bd = DN_WARPS * L.warp_bytes;                           // [k][units][3 limbs][8] u32
+  L.sc_win = ru16(int64_t(16) * L.gpr * 2) + 16;
+  // an expert's rows land contiguous (one bulk copy); 16 rows reserved so the MMA block never reads
+  // past its slab (rows past nrows hold stale bytes and are never stored)
+  L.per_expert = ru16(16 * L.row_bytes + 2 * L.sc_win);
+  L.off_bd = int64_t(k) * L.per_expert;                         // [k][units][3 limbs][8] u32
   L.off_dsum = L.off_bd + int64_t(k) * L.units * 24 * 4;        // [k][groups][2] f32: (sum of a, 2^-e)
   L.off_zero = L.off_dsum + int64_t(k) * L.groups * 2 * 4;      // 64 zero bytes
   L.off_part = ru16(L.off_zero + 64);                           // [DN_WARPS][16] f32
-  L.bytes = L.off_part + DN_WARPS * 16 * 4;
+  L.off_bar = L.off_part + DN_WARPS * 16 * 4;                   // [k] mbarriers
+  L.bytes = L.off_bar + 8 * int64_t(k);
   return L;
 }
 
@@ -201,59 +221,46 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
 
   pdl_wait();  // routing and x come from earlier kernels in the stream
 
-  // ---- L2 prefetch of the down rows the twin down CTA will read (same grid size, same row split)
-  if (warp == GU_WARPS - 1 && lane < S.k) {
-    const int j = lane;
-    int64_t slot;
-    if (route_slot(meta, j, S, slot)) {
-      const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
-      const int64_t drow = int64_t(S.I) * BITS / 8;
-      const uint8_t* base = pool + slot * S.nbytes;
-      const int64_t lo = 2 * S.mat_bytes + h0 * drow, hi = 2 * S.mat_bytes + h1 * drow;
-      if (hi > lo) prefetch_l2(base + (lo & ~int64_t(15)), uint32_t(ru16(hi) - (lo & ~int64_t(15))));
-      const int gd = S.I / S.group;
-      for (int w = 0; w < 2; ++w) {
-        const int64_t a0 = S.ncode + 2 * (w * S.ng + 2 * ngm + int64_t(h0) * gd), a1 = a0 + 2 * int64_t(h1 - h0) * gd;
-        if (a1 > a0) prefetch_l2(base + (a0 & ~int64_t(15)), uint32_t(ru16(a1) - (a0 & ~int64_t(15))));
-      }
-    }
-  }
-
   uint8_t* wreg = sm + int64_t(warp) * Lg.warp_bytes;
-  // commit groups of a piece: [scales], [code groups 0..h-1], [code groups h..ng-1]
+  uint64_t* wbar = reinterpret_cast<uint64_t*>(wreg + 2 * CH * Lg.stride + 4 * Lg.sc_win);
+  if (lane == 0) {
+    mbar_init(wbar, 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  // one bulk copy per row (16 rows: 8 gate, 8 up; the piece's K range) into the padded region, plus
+  // the four scale/min windows of the 8 rows; all complete on the warp's mbarrier
   auto issue_piece = [&](int piece) {
     const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
     const int r0 = blk * CH;
     const int j = r0 / S.I, row0 = r0 - j * S.I;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
-    if (!ok && lane == 0) flag(WISP_STATUS_BAD_SLOT);  // skipped: contributes nothing
     const uint8_t* base = pool + (ok ? slot : 0) * S.nbytes;
     const int G0 = sp * Lg.groups_per_piece;
     const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
-    const int h = (ng + 1) / 2;
-    if (ok) {
-      const int words = CH * Lg.gpr / 2;  // 4-byte words per array (2*gpr bytes per row, gpr even)
-#pragma unroll
-      for (int arr = 0; arr < 4; ++arr) {  // 0 gate s, 1 gate m, 2 up s, 3 up m
-        const uint8_t* srca = base + S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr);
-        for (int wd = lane; wd < words; wd += 32) cp_async4(wreg + 2 * CH * Lg.stride + arr * Lg.sc_bytes + 4 * wd, srca + 4 * wd);
+    const uint32_t cb = uint32_t(ng * 16 * BITS);
+    if (lane == 0) {
+      if (!ok) flag(WISP_STATUS_BAD_SLOT);  // skipped: contributes nothing
+      uint32_t tx = 0;
+      if (ok) {
+        tx = 16 * cb;
+        for (int arr = 0; arr < 4; ++arr)
+          tx += window(S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr), 2 * CH * Lg.gpr).bytes;
       }
+      mbar_expect_tx(wbar, tx);
     }
-    cp_commit();
-    // per lane: at most two 16-byte chunks of each group (16 rows x BITS chunks / 32 lanes)
-    const uint8_t* src[2];
-    uint32_t dst[2];
-    int nch = 0;
-    for (int t = lane; t < 16 * BITS; t += 32, ++nch) {
-      const int rr = t / BITS, q = t - rr * BITS;  // row of 16 (0-7 gate, 8-15 up), 16-B chunk
-      src[nch] = base + (rr >> 3) * S.mat_bytes + int64_t(row0 + (rr & 7)) * row_bytes + int64_t(G0) * 16 * BITS + 16 * q;
-      dst[nch] = uint32_t(rr * Lg.stride + 16 * q);
-    }
-    for (int G = 0; G < ng; ++G) {
-      if (ok)
-        for (int i = 0; i < nch; ++i) cp_async16(wreg + dst[i] + G * 16 * BITS, src[i] + G * 16 * BITS);
-      if (G == h - 1 || G == ng - 1) cp_commit();
+    __syncwarp();
+    if (ok) {
+      if (lane < 16) {
+        const int m = lane >> 3, rw = lane & 7;
+        bulk_g2s(wreg + lane * Lg.stride, base + m * S.mat_bytes + int64_t(row0 + rw) * row_bytes + int64_t(G0) * 16 * BITS,
+                 cb, wbar);
+      } else if (lane < 20) {
+        const int arr = lane - 16;  // 0 gate s, 1 gate m, 2 up s, 3 up m
+        const Win w = window(S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr), 2 * CH * Lg.gpr);
+        bulk_g2s(wreg + 2 * CH * Lg.stride + arr * Lg.sc_win, base + w.start, w.bytes, wbar);
+      }
     }
   };
   if (warp < npieces) issue_piece(warp);
@@ -295,9 +302,8 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
   __syncthreads();
   pdl_launch_dependents();
 
-  for (int piece = warp; piece < npieces; piece += GU_WARPS) {
+  for (int piece = warp, round = 0; piece < npieces; piece += GU_WARPS, ++round) {
     if (piece != warp) {  // another round: the region is free once the previous piece was consumed
-      cp_wait<0>();
       __syncwarp();
       issue_piece(piece);
     }
@@ -307,19 +313,20 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const bool ok = route_slot(meta, r0 / S.I, S, slot);
     const int G0 = sp * Lg.groups_per_piece;
     const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
-    const int h = (ng + 1) / 2;
     // lane c = 0 finishes the gate row g, lane c = 1 the up row g (same instructions, quad_row_dot)
+    const int row0 = r0 - (r0 / S.I) * S.I;
     const uint8_t* sw = wreg + 2 * CH * Lg.stride;
-    const uint16_t* srow = reinterpret_cast<const uint16_t*>(sw + (c == 1 ? 2 : 0) * Lg.sc_bytes) + g * Lg.gpr;
-    const uint16_t* mrow = reinterpret_cast<const uint16_t*>(sw + (c == 1 ? 3 : 1) * Lg.sc_bytes) + g * Lg.gpr;
+    const int sarr = c == 1 ? 2 : 0;  // scale array of this lane's row: gate (0) or up (2); mins follow
+    const uint32_t sskip = window(S.ncode + 2 * ((sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
+    const uint32_t mskip = window(S.ncode + 2 * (S.ng + (sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(sw + sarr * Lg.sc_win + sskip) + g * Lg.gpr;
+    const uint16_t* mrow = reinterpret_cast<const uint16_t*>(sw + (sarr + 1) * Lg.sc_win + mskip) + g * Lg.gpr;
     const uint8_t* rowg = wreg + g * Lg.stride;
     const uint8_t* rowu = wreg + (CH + g) * Lg.stride;
+    if (ok) mbar_wait(wbar, uint32_t(round & 1));
     float acc = 0.0f;
     for (int G = 0; G < ng; G += 2) {
-      if (G == 0) cp_wait<1>();   // scales + first half landed
-      if (G == h) cp_wait<0>();   // second half landed
-      __syncwarp();
-      if (!ok) continue;
+      if (!ok) break;
       const int G1 = min(G + 1, ng - 1);  // an odd tail repeats the last group; its result is dropped
       uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
       lds_unit<BITS>(rowg + (G * 4 + c) * 4 * BITS, wa0);
@@ -356,7 +363,6 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     int64_t slot;
     a_out[r] = route_slot(meta, r / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
   }
-  cp_wait<0>();
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -368,44 +374,42 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const DnL Ld = dn_layout(S.H, S.I, S.k, S.group, BITS);
+  const DnL Ld = dn_layout(S.H, S.I, S.k, S.group, BITS, gridDim.x);
   uint32_t* bd = reinterpret_cast<uint32_t*>(sm + Ld.off_bd);
   float* dsum = reinterpret_cast<float*>(sm + Ld.off_dsum);
   const uint32_t* zero = reinterpret_cast<const uint32_t*>(sm + Ld.off_zero);
   float* part = reinterpret_cast<float*>(sm + Ld.off_part);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ld.off_bar);
   const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
   const int nrows = h1 - h0;
   const int64_t ngm = S.ng / 3;
   const int units = Ld.units;
   const int npieces = S.k * NSPLIT;  // (expert, K half)
-  uint8_t* wreg = sm + int64_t(warp) * Ld.warp_bytes;
-  const uint16_t* ss = reinterpret_cast<const uint16_t*>(wreg + 16 * Ld.stride);
-  const uint16_t* smn = reinterpret_cast<const uint16_t*>(wreg + 16 * Ld.stride + Ld.sc_bytes);
 
-  // ---- warp w streams piece w (the routing is final already; the gate/up grid prefetched these rows
-  //      into L2): rows h0..h1 of expert j, code bytes of one K half, plus the rows' scales and mins
-  auto issue_piece = [&](int piece) {
-    const int j = piece / NSPLIT, sp = piece % NSPLIT;
-    int64_t slot;
-    const bool ok = route_slot(meta, j, S, slot);
-    if (!ok && lane == 0 && sp == 0) flag(WISP_STATUS_BAD_SLOT);
-    if (ok && nrows > 0) {
-      const uint8_t* base = pool + slot * S.nbytes;
-      const int chunks = int(Ld.piece_bytes / 16);
-      const int64_t koff = int64_t(sp) * Ld.groups_per_piece * 16 * BITS;
-      for (int r = 0; r < nrows; ++r)
-        for (int q = lane; q < chunks; q += 32)
-          cp_async16(wreg + r * Ld.stride + 16 * q, base + 2 * S.mat_bytes + int64_t(h0 + r) * Ld.row_bytes + koff + 16 * q);
-      const int words = nrows * Ld.gpr / 2;
-#pragma unroll
-      for (int arr = 0; arr < 2; ++arr) {
-        const uint8_t* srca = base + S.ncode + 2 * (arr * S.ng + 2 * ngm + int64_t(h0) * Ld.gpr);
-        for (int wd = lane; wd < words; wd += 32) cp_async4(wreg + 16 * Ld.stride + arr * Ld.sc_bytes + 4 * wd, srca + 4 * wd);
+  // ---- the down rows of every routed expert: one bulk copy of the CTA's contiguous rows plus the
+  //      scale and min windows, issued before waiting on the gate/up grid (the routing is final)
+  if (warp == 0) {
+    for (int j = lane; j < S.k; j += 32) {
+      mbar_init(&bars[j], 1);
+      mbar_fence_init();
+      int64_t slot;
+      const bool ok = route_slot(meta, j, S, slot);
+      if (!ok) flag(WISP_STATUS_BAD_SLOT);
+      if (!ok || nrows <= 0) {
+        mbar_expect_tx(&bars[j], 0);
+        continue;
       }
+      const uint8_t* base = pool + slot * S.nbytes;
+      const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
+      const Win wm = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
+      const uint32_t cb = uint32_t(int64_t(nrows) * Ld.row_bytes);
+      uint8_t* dst = sm + int64_t(j) * Ld.per_expert;
+      mbar_expect_tx(&bars[j], cb + ws.bytes + wm.bytes);
+      bulk_g2s(dst, base + 2 * S.mat_bytes + int64_t(h0) * Ld.row_bytes, cb, &bars[j]);
+      bulk_g2s(dst + 16 * Ld.row_bytes, base + ws.start, ws.bytes, &bars[j]);
+      bulk_g2s(dst + 16 * Ld.row_bytes + Ld.sc_win, base + wm.start, wm.bytes, &bars[j]);
     }
-    cp_commit();
-  };
-  if (warp < npieces) issue_piece(warp);
+  }
   for (int i = threadIdx.x; i < DN_WARPS * 16; i += blockDim.x) part[i] = 0.0f;
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Ld.off_zero)[threadIdx.x] = 0u;
 
@@ -438,18 +442,17 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   __syncthreads();
 
   for (int piece = warp; piece < npieces; piece += DN_WARPS) {
-    if (piece != warp) {
-      cp_wait<0>();
-      __syncwarp();
-      issue_piece(piece);
-    }
     const int j = piece / NSPLIT, sp = piece % NSPLIT;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
     const float wj = meta[S.k + j];
-    cp_wait<0>();
-    __syncwarp();
-    if (!ok) continue;
+    if (!ok || nrows <= 0) continue;
+    mbar_wait(&bars[j], 0);
+    const uint8_t* eb = sm + int64_t(j) * Ld.per_expert;
+    const uint32_t sskip = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * Ld.gpr), 1).skip;
+    const uint32_t mskip = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * Ld.gpr), 1).skip;
+    const uint16_t* ss = reinterpret_cast<const uint16_t*>(eb + 16 * Ld.row_bytes + sskip);
+    const uint16_t* smn = reinterpret_cast<const uint16_t*>(eb + 16 * Ld.row_bytes + Ld.sc_win + mskip);
     // lane c = 0 finishes output row g, lane c = 1 row g + 8
     const int myrow = (c == 1) ? g + 8 : g;
     const uint16_t* srow = ss + myrow * Ld.gpr;
@@ -462,10 +465,10 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
     for (int G = 0; G < ng; G += 2) {
       const int G1 = min(G + 1, ng - 1);
       uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
-      lds_unit<BITS>(wreg + g * Ld.stride + (4 * G + c) * 4 * BITS, wa0);
-      lds_unit<BITS>(wreg + (g + 8) * Ld.stride + (4 * G + c) * 4 * BITS, wb0);
-      lds_unit<BITS>(wreg + g * Ld.stride + (4 * G1 + c) * 4 * BITS, wa1);
-      lds_unit<BITS>(wreg + (g + 8) * Ld.stride + (4 * G1 + c) * 4 * BITS, wb1);
+      lds_unit<BITS>(eb + g * Ld.row_bytes + (4 * (G0 + G) + c) * 4 * BITS, wa0);
+      lds_unit<BITS>(eb + (g + 8) * Ld.row_bytes + (4 * (G0 + G) + c) * 4 * BITS, wb0);
+      lds_unit<BITS>(eb + g * Ld.row_bytes + (4 * (G0 + G1) + c) * 4 * BITS, wa1);
+      lds_unit<BITS>(eb + (g + 8) * Ld.row_bytes + (4 * (G0 + G1) + c) * 4 * BITS, wb1);
       lds_b8(g < 3 ? bj + ((4 * (G0 + G) + c) * 3 + g) * 8 : zero, bb0);
       lds_b8(g < 3 ? bj + ((4 * (G0 + G1) + c) * 3 + g) * 8 : zero, bb1);
       int d0[4], d1[4];
@@ -489,7 +492,9 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
     for (int w = 0; w < DN_WARPS; ++w) s += part[w * 16 + r];
     out[h0 + r] = f32_to_bf16(s);
   }
-  cp_wait<0>();
+  // no copy may still be landing in shared memory when the CTA retires
+  if (warp == 0)
+    for (int j = lane; j < S.k; j += 32) mbar_wait(&bars[j], 0);
 }
 
 }  // namespace v4

@@ -259,18 +259,18 @@ static bool v4_supported(const MoeShape& S, int bits, int nctas) {
   if ((S.H / S.group) % 2 || (S.I / S.group) % 2 || S.ng % 2) return false;
   if (S.ncode % 16 || S.mat_bytes % 16 || (int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
   if ((S.H + nctas - 1) / nctas > 16) return false;
-  if (S.k > 32) return false;  // one prefetch lane per expert
+  if (S.k > 32) return false;  // one copy lane of warp 0 per routed expert
   const v4::GuL Lg = v4::gu_layout(S.H, S.group, bits);
   if (Lg.groups_per_piece > v4::MAXG) return false;
   const int64_t gsm = v4::gu_smem(S.H, S.I, S.k, S.group, bits, nctas);
-  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits);
+  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
   return gsm <= 220 * 1024 && Ld.bytes <= 220 * 1024;
 }
 
 static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
                      float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
   const int64_t gsm = v4::gu_smem(S.H, S.I, S.k, S.group, bits, nctas);
-  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits);
+  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
   cudaError_t e = cudaSuccess;
 #define WISP_V4(B)                                                                                          \
   e = launch_pdl(v4::gate_up_kernel<B>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch);  \
