@@ -85,10 +85,11 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
                     void* stream);
 
 /* Same computation with an explicit kernel choice: 0 = automatic (what wisp_moe_decode does),
- * 1 = warp-per-row CUDA-core kernels (any supported shape), 2 = persistent per-warp cp.async pipelines
- * feeding warp-level tensor-core MMA through a one-op-per-pair code unpack, with the down rows
- * prefetched into L2 and the two kernels chained by programmatic dependent launch (bits 4/3/2, group
- * a multiple of 128, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise).
+ * 1 = warp-per-row CUDA-core kernels (any supported shape), 2 = TMA bulk copies into shared memory
+ * feeding the warp-level integer MMA (u8 codes x int8 activation limbs, exact int32 sums), the two
+ * kernels chained by programmatic dependent launch so the down rows stream in while gate/up computes
+ * (bits 4/3/2, group a multiple of 128, H and I multiples of 128, k <= 32, at most 16 output rows
+ * per SM; WISP_ERR_UNSUPPORTED otherwise).
  * Automatic = 2 when it applies, else 1. */
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,

@@ -45,7 +45,7 @@ def _need_cuda(*ts):
 def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratch=None, variant=0):
     """Fused dequant + GEMV MoE of one token over the k experts named by ``meta`` (fp32 [2k] =
     [slots..., weights...]).  pool: uint8 [nslots, nbytes]; x: bf16 [H].  Returns bf16 [H].
-    ``variant``: 0 automatic, 1 warp-per-row CUDA-core kernels, 2 cp.async pipelines + tensor-core MMA."""
+    ``variant``: 0 automatic, 1 warp-per-row CUDA-core kernels, 2 TMA bulk copies + integer MMA."""
     assert H % group == 0 and I % group == 0 and n == H * I
     _need_cuda(pool, meta, x)
     assert pool.dtype == torch.uint8 and pool.dim() == 2 and pool.is_contiguous()
