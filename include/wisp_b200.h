@@ -95,6 +95,23 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,
                             uint16_t* out, int variant, void* stream);
 
+/* Allocation-free twin of wisp_moe_decode for callers that cannot allocate device memory (a host
+ * stack that owns no allocator, e.g. a CUDA-graph node builder or an embedding runtime that hands over
+ * only the pool, x and out): the fp32 intermediate a = silu(g)*u lives in a file-scope device array
+ * of WISP_MOE_NOALLOC_MAX_SCRATCH floats inside the library, so no scratch argument is taken and no
+ * device memory is allocated or freed.  Everything else (arguments, kernels, results) is
+ * wisp_moe_decode's.  k*I must be <= WISP_MOE_NOALLOC_MAX_SCRATCH (WISP_ERR_INVALID otherwise).
+ *   - Nothing in the array needs to start at zero: each call writes all k*I values before reading them.
+ *   - The array is one per device and shared by every call on that device: two calls that can run at
+ *     the same time (different streams, or threads without ordering) race on it.  Order them.
+ *   - The array's address is looked up once per device (cudaGetSymbolAddress, with that device
+ *     current); make the first call on each device outside stream capture.
+ * No counterpart in the reference (its kernels allocate their intermediate with torch.empty). */
+#define WISP_MOE_NOALLOC_MAX_SCRATCH 65536
+int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
+                            const uint16_t* x, int64_t H, int64_t I, int bits, int group, uint16_t* out,
+                            void* stream);
+
 /* ---- decode-side ops ---------------------------------------------------------------------------- */
 /* Rotate-half RoPE for one token: q [Hq, D] (head stride q_stride elements), k [Hk, D] (k_stride),
  * cos/sin bf16 [D]; writes contiguous qo [Hq, D], ko [Hk, D].  fp32 math, one rounding to bf16.

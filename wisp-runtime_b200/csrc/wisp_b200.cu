@@ -1,5 +1,7 @@
 // libwisp_b200.so: the C ABI declared in include/wisp_b200.h.  One translation unit (the kernels live
 // in the included .cuh files) so the per-device status word is a single __device__ symbol.
+#include <mutex>
+
 #include "common.cuh"
 #include "decode_ops.cuh"
 #include "moe_decode.cuh"
@@ -286,6 +288,31 @@ static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, 
   return check_launch("moe_decode");
 }
 
+// ---- built-in scratch of wisp_moe_decode_noalloc -------------------------------------------------
+// One array per device (a __device__ variable exists once in every context that loads the module).
+static __device__ __align__(256) float g_noalloc_scratch[WISP_MOE_NOALLOC_MAX_SCRATCH];
+constexpr int kMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[kMaxDevices] = {};
+
+// address of the current device's array, looked up once per device with that device current
+static int noalloc_scratch(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_noalloc: device %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cudaGetSymbolAddress on device %d: %s", dev, cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return WISP_OK;
+}
+
 extern "C" {
 
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
@@ -305,6 +332,20 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
 
 int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k, const uint16_t* x,
                     int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream) {
+  return wisp_moe_decode_variant(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, 0, stream);
+}
+
+int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
+                            const uint16_t* x, int64_t H, int64_t I, int bits, int group, uint16_t* out,
+                            void* stream) {
+  WISP_REQUIRE(k >= 1 && I > 0, "wisp_moe_decode_noalloc: k and I must be positive (k=%d I=%lld)", k, (long long)I);
+  WISP_REQUIRE(int64_t(k) * I <= WISP_MOE_NOALLOC_MAX_SCRATCH,
+               "wisp_moe_decode_noalloc: k*I = %lld exceeds the built-in scratch of %d floats "
+               "(use wisp_moe_decode with caller-provided scratch)",
+               (long long)(int64_t(k) * I), WISP_MOE_NOALLOC_MAX_SCRATCH);
+  float* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
   return wisp_moe_decode_variant(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, 0, stream);
 }
 

@@ -16,6 +16,7 @@ LIB_PATH = os.environ.get("WISP_B200_LIB", os.path.join(os.path.dirname(_HERE), 
 WISP_OK, WISP_ERR_INVALID, WISP_ERR_CUDA, WISP_ERR_UNSUPPORTED = 0, 1, 2, 3
 STATUS_BAD_SLOT, STATUS_BAD_POS, STATUS_WAIT_TIMEOUT, STATUS_BAD_ROUTE = 0x1, 0x2, 0x4, 0x8
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+MOE_NOALLOC_MAX_SCRATCH = 65536  # WISP_MOE_NOALLOC_MAX_SCRATCH: fp32 values of k*I
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -33,6 +34,7 @@ SIGNATURES = {
     "wisp_unpack_codes": (_I, [_P, _L, _L, _P, _L, _L, _I, _P, _P]),
     "wisp_moe_decode": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _P]),
     "wisp_moe_decode_variant": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _I, _P]),
+    "wisp_moe_decode_noalloc": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
     "wisp_rmsnorm": (_I, [_P, _P, _P, _P, _L, _L, _F, _P, _P]),
 }

@@ -77,6 +77,37 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
     return out
 
 
+def moe_decode_noalloc(pool, meta, x, k, n, H, I, bits, group=128, out=None):
+    """moe_decode_fast through wisp_moe_decode_noalloc: the fp32 intermediate lives in the library's
+    built-in per-device array (k*I <= MOE_NOALLOC_MAX_SCRATCH), so the call allocates nothing on the
+    device when ``out`` is given.  Calls on one device that can overlap race on that array."""
+    assert H % group == 0 and I % group == 0 and n == H * I
+    _need_cuda(pool, meta, x)
+    assert pool.dtype == torch.uint8 and pool.dim() == 2 and pool.is_contiguous()
+    assert meta.dtype == torch.float32 and meta.numel() >= 2 * k and meta.is_contiguous()
+    if x.dtype != torch.bfloat16:
+        raise WispError(f"x must be bfloat16 (got {x.dtype})")
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty((H,), dtype=x.dtype, device=x.device)
+    _lib.call(
+        "wisp_moe_decode_noalloc",
+        pool.data_ptr(),
+        pool.shape[0],
+        pool.shape[1],
+        meta.data_ptr(),
+        k,
+        x.data_ptr(),
+        H,
+        I,
+        bits,
+        group,
+        out.data_ptr(),
+        _stream(x),
+    )
+    return out
+
+
 def moe_decode_q4_fast(pool, meta, x, k, n, H, I, group=128, block_gu=32, block_down=8, num_warps=4):
     """4-bit fused MoE decode (2 launches), meta = fp32 [slot_0..slot_{k-1}, w_0..w_{k-1}].
     Reference: wisp/kernels.py:188-203."""
