@@ -31,6 +31,9 @@ sys.path.insert(0, ROOT)
 
 H, I, E, K_TOP, L, G = 2048, 768, 128, 8, 48, 128
 N_ROUTES = 16  # distinct seeded routings (tokens) cycled through by the timed steps
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up + one down launch (4-bit, this shape),
+# from the ncu capture summarised in profiles/moe_decode_q4_qwen3_gate_up_down_full.md
+NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
 
 
 def parse():
@@ -432,7 +435,7 @@ def main():
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": None,
+                "traffic": NCU_TRAFFIC_PER_CALL if a.bits == 4 else None,
                 "kernel": "wisp_moe_decode (gate/up + down)",
                 "bytes_per_call": alg_bytes,
                 "us_per_call": per_call_ms * 1e3,
