@@ -39,8 +39,8 @@ NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
     ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the model; fewer = a small ncu case)")
@@ -70,44 +70,61 @@ def workload_config(a, n):
 # clocks sampled during the timed region
 # ------------------------------------------------------------------------------------------------
 class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 50 ms.  start() returns once the first sample
+    has arrived (NVML initialised), so the sampler's start-up does not land inside a timed region;
+    window() marks the timed regions and stop() summarises the samples taken inside them (or, when
+    the regions are shorter than the sampling period, the samples taken around them)."""
+
     FIELDS = (
         "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
     )
+    PERIOD_MS = 50
 
     def __init__(self, index):
-        self.index, self.proc, self.lines = index, None, []
+        self.index, self.proc, self.lines, self.windows = index, None, [], []
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.PERIOD_MS)],
                 stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL,
                 text=True,
             )
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 10 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def window(self, t0, t1):
+        self.windows.append((t0, t1))
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(2 * self.PERIOD_MS / 1e3)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
+        slack = self.PERIOD_MS / 1e3
+        inside = [ln for t, ln in self.lines if any(a <= t <= b for a, b in self.windows)]
+        around = [ln for t, ln in self.lines if any(a - slack <= t <= b + slack for a, b in self.windows)]
+        use, where = (inside, "inside") if inside else (around, "within one period of")
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in use:
             p = [x.strip() for x in ln.split(",")]
             if len(p) < 9:
                 continue
@@ -124,6 +141,8 @@ class ClockSampler:
             "sm_max_mhz": mx,
             "reasons": sorted(reasons),
             "samples": len(sm),
+            "period_ms": self.PERIOD_MS,
+            "samples_taken": f"{where} the timed regions",
         }
 
 
@@ -161,12 +180,14 @@ class MoEStack:
     def __init__(self, W):
         import torch
 
+        from wisp import kernels
+
         self.W = W
         dev = W["pool"].device
         self.h = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.xn = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.moe = torch.zeros(H, dtype=torch.bfloat16, device=dev)
-        self.scratch = torch.empty(K_TOP * I, dtype=torch.float32, device=dev)
+        self.scratch = kernels.moe_scratch(K_TOP, I, dev)
         self.meta_in = torch.zeros(L, 2 * K_TOP, dtype=torch.float32, device=dev)  # e2e routing input
         self.x_in = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.graphs = []
@@ -231,7 +252,7 @@ def time_moe_kernel(W, reps=20, variant=0):
     dev = W["pool"].device
     x = torch.randn(L, H, device=dev).to(torch.bfloat16)
     out = torch.empty(L, H, dtype=torch.bfloat16, device=dev)
-    scratch = torch.empty(K_TOP * I, dtype=torch.float32, device=dev)
+    scratch = kernels.moe_scratch(K_TOP, I, dev)
 
     def sweep():
         for l in range(L):
@@ -374,11 +395,13 @@ def main():
     barrier()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
     e0.record(st)
     for t in range(a.steps):
         stack.step(t)
     e1.record(st)
     barrier()
+    clocks.window(w0, time.perf_counter())
     ms = e0.elapsed_time(e1)
     # e2e: host buffers, copies inside the timed region
     x_host = W["x0"].cpu().pin_memory()
@@ -388,11 +411,13 @@ def main():
         stack.step_e2e(x_host[t % N_ROUTES], meta_host[t % N_ROUTES], out_host)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
     e2.record(st)
     for t in range(a.steps):
         stack.step_e2e(x_host[t % N_ROUTES], meta_host[t % N_ROUTES], out_host)
     e3.record(st)
     barrier()
+    clocks.window(w0, time.perf_counter())
     ms_e2e = e2.elapsed_time(e3)
     clk = clocks.stop()
     # roofline of the fused MoE decode (algorithmic bytes: 8 experts + x + out per call)

@@ -86,10 +86,10 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
 
 /* Same computation with an explicit kernel choice: 0 = automatic (what wisp_moe_decode does),
  * 1 = warp-per-row CUDA-core kernels (any supported shape), 2 = TMA bulk copies into shared memory
- * feeding the warp-level integer MMA (u8 codes x int8 activation limbs, exact int32 sums), the two
- * kernels chained by programmatic dependent launch so the down rows stream in while gate/up computes
- * (bits 4/3/2, group a multiple of 128, H and I multiples of 128, k <= 32, at most 16 output rows
- * per SM; WISP_ERR_UNSUPPORTED otherwise).
+ * feeding the warp-level integer MMA (u8 codes x int8 activation limbs, exact int32 sums), gate/up
+ * and down as two kernels chained by programmatic dependent launch, the gate/up grid pulling the
+ * down rows into L2 while it computes (bits 4/3/2, group a multiple of 128, H and I multiples of
+ * 128, k <= 32, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise).
  * Automatic = 2 when it applies, else 1. */
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,

@@ -57,8 +57,8 @@ def _setup(bits, H, I, E, k, G=128, seed=0):
 @pytest.mark.parametrize("bits", [4, 3, 2, 8])
 def test_full_shape_vs_oracle(bits, variant):
     """Qwen3-30B-A3B layer shape: H=2048, I=768, top-8 of 16 resident experts, every kernel variant
-    (0 = automatic, 1 = warp-per-row CUDA cores, 2 = cp.async pipelines + tensor-core MMA, which takes
-    4/3/2-bit experts only)."""
+    (0 = automatic, 1 = warp-per-row CUDA cores, 2 = bulk copies + integer MMA, which takes 4/3/2-bit
+    experts only)."""
     from wisp import kernels
 
     if bits == 8 and variant == 2:
@@ -165,3 +165,33 @@ def test_graph_capture_replays_with_new_routing():
         torch.cuda.synchronize()
         ref = O.moe_decode_ref(pool.cpu().numpy(), s2.cpu().numpy(), _bf16_np(x), wts.cpu().numpy(), n, H, I, bits)
         assert _rel(_bf16_np(out), ref) < TOL
+
+
+def test_scratch_reused_across_many_calls():
+    """One scratch serves many calls: results stay bit-identical and nothing is flagged."""
+    from wisp import _lib, kernels
+
+    H, I, E, k, bits = 2048, 768, 16, 8, 4
+    n = H * I
+    pool, x, slots, wts = _setup(bits, H, I, E, k, seed=23)
+    meta = torch.cat([slots.float(), wts])
+    scratch = kernels.moe_scratch(k, I, "cuda")
+    _lib.device_status(0, clear=True)
+    first = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, scratch=scratch).clone()
+    for _ in range(50):
+        out = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, scratch=scratch)
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+    assert _lib.device_status(0) == 0
+
+
+def test_short_scratch_rejected():
+    from wisp import kernels
+    from wisp._lib import WispError
+
+    H, I, E, k, bits = 256, 128, 4, 2, 4
+    n = H * I
+    pool, x, slots, wts = _setup(bits, H, I, E, k, seed=3)
+    meta = torch.cat([slots.float(), wts])
+    with pytest.raises(WispError, match="scratch"):
+        kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, scratch=torch.zeros(k * I - 1, device="cuda"))

@@ -51,6 +51,11 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 // defined here: the library is built as one translation unit (wisp_b200.cu includes every .cuh)
 __device__ unsigned int g_status = 0;
 
+// programmatic dependent launch: wait for the preceding grid's completion and memory flush / allow
+// the next grid in the stream to launch.  Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void flag(unsigned int bit) { atomicOr(&g_status, bit); }
 
 // ------------------------------------------------------------------------------------------------

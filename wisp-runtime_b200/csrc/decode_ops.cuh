@@ -73,10 +73,12 @@ __global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const uint16_t* x, co
   const int t = threadIdx.x;
   const bool active = int64_t(t) * 8 < H;
   uint4 xv = make_uint4(0, 0, 0, 0), dv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+  if (active) wv = reinterpret_cast<const uint4*>(w)[t];  // weights are not written by earlier kernels
+  pdl_wait();
+  pdl_launch_dependents();
   if (active) {
     xv = reinterpret_cast<const uint4*>(x + row * H)[t];
     if (delta) dv = reinterpret_cast<const uint4*>(delta + row * H)[t];
-    wv = reinterpret_cast<const uint4*>(w)[t];
   }
   float v[8];
   const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};

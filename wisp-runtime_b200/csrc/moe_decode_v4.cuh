@@ -28,9 +28,10 @@ constexpr int GU_WARPS = 16;
 constexpr int DN_WARPS = 16;
 constexpr int GU_THREADS = GU_WARPS * 32;
 constexpr int DN_THREADS = DN_WARPS * 32;
-constexpr int CH = 8;      // rows per gate/up piece (A rows 0-7 gate, 8-15 up)
-constexpr int NSPLIT = 2;  // gate/up pieces split H in two halves; down pieces split I in two halves
-constexpr int MAXG = 16;   // max 128-code groups per piece
+constexpr int CH = 8;           // rows per gate/up block (A rows 0-7 gate, 8-15 the same up rows)
+constexpr int NSPLIT = 2;       // K halves: two warps per gate/up block, two pieces per down expert
+constexpr int MAX_REGIONS = 8;  // gate/up blocks in flight per CTA (two warps each)
+constexpr int SMEM_LIMIT = 220 * 1024;
 
 __host__ __device__ constexpr int row_pad(int bits) { return 16 * bits; }
 __host__ __device__ inline int64_t ru16(int64_t v) { return (v + 15) & ~int64_t(15); }
@@ -80,8 +81,6 @@ __device__ __forceinline__ Win window(int64_t off, int64_t len) {
   w.skip = uint32_t(off - w.start);
   return w;
 }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 template <int BITS>
 __device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) {
@@ -101,33 +100,42 @@ __device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) 
 // shared-memory layouts (host and device share these formulas)
 // ------------------------------------------------------------------------------------------------
 struct GuL {
-  int groups, groups_per_piece, gpr;  // 128-code groups per row / per piece; quant groups per row
-  int64_t piece_bytes, stride, sc_win, warp_bytes;
-  int64_t off_bx, off_gsum, off_zero, off_halves;
+  int groups, gph, gpr;  // 128-code groups per row / per K half; quant groups per row
+  int nblk_max, R;       // max 8-row blocks per CTA; block regions in flight
+  int64_t row_bytes, sc_win, region;
+  int64_t off_bx, off_gsum, off_zero, off_halves, off_bars, bytes;
 };
 
-__host__ __device__ inline GuL gu_layout(int H, int group, int bits) {
+// gate/up shared memory: R regions of [8 gate rows | 8 up rows | 4 scale/min windows], each row
+// a contiguous copy of the matrix (row stride = row bytes), then the B operand and bookkeeping; every
+// part starts on a 16-byte boundary
+__host__ __device__ inline GuL gu_layout_for(int H, int I, int k, int group, int bits, int nctas, int R) {
   GuL L;
   L.groups = H / 128;
-  L.groups_per_piece = (L.groups + NSPLIT - 1) / NSPLIT;
+  L.gph = (L.groups + 1) / 2;
   L.gpr = H / group;
-  L.piece_bytes = int64_t(L.groups_per_piece) * 16 * bits;  // code bytes of one row inside a piece
-  L.stride = L.piece_bytes + row_pad(bits);
-  L.sc_win = ru16(int64_t(CH) * L.gpr * 2) + 16;             // one scale (or min) window of the 8 rows
-  L.warp_bytes = ru16(2 * CH * L.stride + 4 * L.sc_win + 8);  // + the warp's mbarrier
-  L.off_bx = GU_WARPS * L.warp_bytes;                        // [H/32 units][3 limbs][8] u32
-  L.off_gsum = L.off_bx + int64_t(H / 32) * 24 * 4;          // [H/128][2] f32: (sum of x, 2^-e)
-  L.off_zero = L.off_gsum + int64_t(L.groups) * 2 * 4;       // 64 zero bytes
-  L.off_halves = ru16(L.off_zero + 64);                      // [pieces][CH][2] f32
+  L.nblk_max = (k * I / CH + nctas - 1) / nctas;
+  L.R = R;
+  L.row_bytes = int64_t(H) * bits / 8;
+  L.sc_win = ru16(int64_t(CH) * L.gpr * 2) + 16;
+  L.region = ru16(2 * CH * L.row_bytes + 4 * L.sc_win);
+  L.off_bx = int64_t(R) * L.region;                             // [H/32 units][3 limbs][8] u32
+  L.off_gsum = ru16(L.off_bx + int64_t(H / 32) * 24 * 4);       // [H/128][2] f32: (sum of x, 2^-e)
+  L.off_zero = ru16(L.off_gsum + int64_t(L.groups) * 2 * 4);    // 64 zero bytes
+  L.off_halves = ru16(L.off_zero + 64);                         // [nblk_max][2 halves][CH][2] f32
+  L.off_bars = ru16(L.off_halves + int64_t(L.nblk_max) * NSPLIT * CH * 2 * 4);  // [R] mbarriers
+  L.bytes = ru16(L.off_bars + 8 * int64_t(R));
   return L;
 }
 
-// dynamic shared memory of the gate/up kernel
-__host__ __device__ inline int64_t gu_smem(int H, int I, int k, int group, int bits, int nctas) {
-  const GuL L = gu_layout(H, group, bits);
-  const int64_t nblk = int64_t(k) * I / CH;
-  const int64_t max_pieces = (nblk + nctas - 1) / nctas * NSPLIT;
-  return L.off_halves + max_pieces * CH * 2 * 4;
+// the largest region count (<= MAX_REGIONS, <= blocks per CTA) whose layout fits; R = 0 if none
+__host__ __device__ inline GuL gu_layout(int H, int I, int k, int group, int bits, int nctas) {
+  const int nblk_max = (k * I / CH + nctas - 1) / nctas;
+  int R = nblk_max < MAX_REGIONS ? nblk_max : MAX_REGIONS;
+  GuL L = gu_layout_for(H, I, k, group, bits, nctas, R);
+  while (R > 1 && L.bytes > SMEM_LIMIT) L = gu_layout_for(H, I, k, group, bits, nctas, --R);
+  if (L.bytes > SMEM_LIMIT) L.R = 0;
+  return L;
 }
 
 struct DnL {
@@ -148,12 +156,12 @@ __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bit
   // an expert's rows land contiguous (one bulk copy); 16 rows reserved so the MMA block never reads
   // past its slab (rows past nrows hold stale bytes and are never stored)
   L.per_expert = ru16(16 * L.row_bytes + 2 * L.sc_win);
-  L.off_bd = int64_t(k) * L.per_expert;                         // [k][units][3 limbs][8] u32
-  L.off_dsum = L.off_bd + int64_t(k) * L.units * 24 * 4;        // [k][groups][2] f32: (sum of a, 2^-e)
-  L.off_zero = L.off_dsum + int64_t(k) * L.groups * 2 * 4;      // 64 zero bytes
-  L.off_part = ru16(L.off_zero + 64);                           // [DN_WARPS][16] f32
-  L.off_bar = L.off_part + DN_WARPS * 16 * 4;                   // [k] mbarriers
-  L.bytes = L.off_bar + 8 * int64_t(k);
+  L.off_bd = int64_t(k) * L.per_expert;                              // [k][units][3 limbs][8] u32
+  L.off_dsum = ru16(L.off_bd + int64_t(k) * L.units * 24 * 4);       // [k][groups][2] f32: (sum of a, 2^-e)
+  L.off_zero = ru16(L.off_dsum + int64_t(k) * L.groups * 2 * 4);     // 64 zero bytes
+  L.off_part = ru16(L.off_zero + 64);                                // [DN_WARPS][16] f32
+  L.off_bar = ru16(L.off_part + DN_WARPS * 16 * 4);                  // [k] mbarriers
+  L.bytes = ru16(L.off_bar + 8 * int64_t(k));
   return L;
 }
 
@@ -198,6 +206,14 @@ __device__ __forceinline__ float quad_sum(float v) {
 }
 
 // ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// pull [src, src + bytes) into L2 (16-byte aligned address, size a multiple of 16)
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 template <int BITS>
 __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* __restrict__ pool,
                                                                 const float* __restrict__ meta,
@@ -206,70 +222,88 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const GuL Lg = gu_layout(S.H, S.group, BITS);
+  const GuL Lg = gu_layout(S.H, S.I, S.k, S.group, BITS, gridDim.x);
+  const int R = Lg.R;
   uint32_t* bx = reinterpret_cast<uint32_t*>(sm + Lg.off_bx);
   float* gsum = reinterpret_cast<float*>(sm + Lg.off_gsum);
   const uint32_t* zero = reinterpret_cast<const uint32_t*>(sm + Lg.off_zero);
   float* halves = reinterpret_cast<float*>(sm + Lg.off_halves);
+  uint64_t* gbar = reinterpret_cast<uint64_t*>(sm + Lg.off_bars);
   const int64_t ngm = S.ng / 3;
-  const int64_t row_bytes = int64_t(S.H) * BITS / 8;
-  // this CTA owns 8-row blocks [b0, b1) of the k*I (expert, row) list; I % 8 == 0, so a block never
-  // straddles two experts.  Piece = (block, K part); warp w takes pieces w, w + GU_WARPS, ...
+  // this CTA owns 8-row blocks [b0, b1) of the k*I (expert, row) list (I % 8 == 0: a block never
+  // straddles two experts); region r takes blocks b0 + r, b0 + r + R, ...; warps 2r and 2r+1 take
+  // its two K halves
   const int nblk_all = S.k * S.I / CH;
   const int b0 = int(int64_t(nblk_all) * blockIdx.x / gridDim.x), b1 = int(int64_t(nblk_all) * (blockIdx.x + 1) / gridDim.x);
-  const int npieces = (b1 - b0) * NSPLIT;
+  const int nb = b1 - b0;
 
   pdl_wait();  // routing and x come from earlier kernels in the stream
+  // the down grid may launch now: routing is final (its CTAs read the intermediate only after their
+  // own griddepcontrol.wait)
+  pdl_launch_dependents();
 
-  uint8_t* wreg = sm + int64_t(warp) * Lg.warp_bytes;
-  uint64_t* wbar = reinterpret_cast<uint64_t*>(wreg + 2 * CH * Lg.stride + 4 * Lg.sc_win);
-  if (lane == 0) {
-    mbar_init(wbar, 1);
-    mbar_fence_init();
-  }
-  __syncwarp();
-  // one bulk copy per row (16 rows: 8 gate, 8 up; the piece's K range) into the padded region, plus
-  // the four scale/min windows of the 8 rows; all complete on the warp's mbarrier
-  auto issue_piece = [&](int piece) {
-    const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
-    const int r0 = blk * CH;
-    const int j = r0 / S.I, row0 = r0 - j * S.I;
+  // one warp (lanes 0-5) issues block bi into region bi % R: the 8 gate rows and the same 8 up rows
+  // (each one contiguous range of its matrix) and the four scale/min windows, on the region's mbarrier
+  auto issue_block = [&](int bi) {
+    const int r = bi % R;
+    const int blk = b0 + bi;
+    const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
     int64_t slot;
     const bool ok = route_slot(meta, j, S, slot);
-    const uint8_t* base = pool + (ok ? slot : 0) * S.nbytes;
-    const int G0 = sp * Lg.groups_per_piece;
-    const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
-    const uint32_t cb = uint32_t(ng * 16 * BITS);
+    uint8_t* reg = sm + int64_t(r) * Lg.region;
+    const uint32_t cb = uint32_t(CH * Lg.row_bytes);
     if (lane == 0) {
       if (!ok) flag(WISP_STATUS_BAD_SLOT);  // skipped: contributes nothing
       uint32_t tx = 0;
       if (ok) {
-        tx = 16 * cb;
+        tx = 2 * cb;
         for (int arr = 0; arr < 4; ++arr)
           tx += window(S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr), 2 * CH * Lg.gpr).bytes;
       }
-      mbar_expect_tx(wbar, tx);
+      mbar_expect_tx(&gbar[r], tx);
     }
     __syncwarp();
-    if (ok) {
-      if (lane < 16) {
-        const int m = lane >> 3, rw = lane & 7;
-        bulk_g2s(wreg + lane * Lg.stride, base + m * S.mat_bytes + int64_t(row0 + rw) * row_bytes + int64_t(G0) * 16 * BITS,
-                 cb, wbar);
-      } else if (lane < 20) {
-        const int arr = lane - 16;  // 0 gate s, 1 gate m, 2 up s, 3 up m
+    if (ok && lane < 6) {
+      const uint8_t* base = pool + slot * S.nbytes;
+      if (lane < 2) {  // 0: gate rows, 1: up rows
+        bulk_g2s(reg + lane * cb, base + lane * S.mat_bytes + int64_t(row0) * Lg.row_bytes, cb, &gbar[r]);
+      } else {
+        const int arr = lane - 2;  // 0 gate s, 1 gate m, 2 up s, 3 up m
         const Win w = window(S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr), 2 * CH * Lg.gpr);
-        bulk_g2s(wreg + 2 * CH * Lg.stride + arr * Lg.sc_win, base + w.start, w.bytes, wbar);
+        bulk_g2s(reg + 2 * cb + arr * Lg.sc_win, base + w.start, w.bytes, &gbar[r]);
       }
     }
   };
-  if (warp < npieces) issue_piece(warp);
+  if (warp < 2 * R && (warp & 1) == 0) {
+    if (lane == 0) {
+      mbar_init(&gbar[warp >> 1], 1);
+      mbar_fence_init();
+    }
+    __syncwarp();
+    if ((warp >> 1) < nb) issue_block(warp >> 1);
+  }
+  // the down rows the down kernel's CTA of the same index will read, pulled into L2 now
+  if (warp == GU_WARPS - 1) {
+    const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
+    const int64_t gpr_d = S.I / S.group, row_d = int64_t(S.I) * BITS / 8;
+    for (int j = lane; j < S.k && h1 > h0; j += 32) {
+      int64_t slot;
+      if (!route_slot(meta, j, S, slot)) continue;
+      const uint8_t* base = pool + slot * S.nbytes;
+      prefetch_l2(base + 2 * S.mat_bytes + int64_t(h0) * row_d, uint32_t(int64_t(h1 - h0) * row_d));
+      const int64_t len = 2 * int64_t(h1 - h0) * gpr_d;
+      const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * gpr_d), len);
+      const Win wm = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * gpr_d), len);
+      prefetch_l2(base + ws.start, ws.bytes);
+      prefetch_l2(base + wm.start, wm.bytes);
+    }
+  }
 
-  // ---- B operand from x, one thread per 32-element unit: on the warps without a piece when there
+  // ---- B operand from x, one thread per 32-element unit: on the warps without a block when there
   //      are enough of them, else on all threads after their copies are issued
   const int units = S.H / 32;
-  const int spare = (GU_WARPS - npieces) * 32;
-  const int first = spare >= units ? npieces * 32 : 0;  // multiple of 32: whole warps build
+  const int spare = (GU_WARPS - 2 * R) * 32;
+  const int first = spare >= units ? 2 * R * 32 : 0;  // multiple of 32: whole warps build
   const int nthr = int(blockDim.x) - first;
   // warp-uniform loop (the quad shuffles need every lane); lanes past the last unit read a valid
   // unit and store nothing
@@ -300,68 +334,69 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
   }
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Lg.off_zero)[threadIdx.x] = 0u;
   __syncthreads();
-  pdl_launch_dependents();
 
-  for (int piece = warp, round = 0; piece < npieces; piece += GU_WARPS, ++round) {
-    if (piece != warp) {  // another round: the region is free once the previous piece was consumed
-      __syncwarp();
-      issue_piece(piece);
-    }
-    const int blk = b0 + piece / NSPLIT, sp = piece % NSPLIT;
-    const int r0 = blk * CH;
-    int64_t slot;
-    const bool ok = route_slot(meta, r0 / S.I, S, slot);
-    const int G0 = sp * Lg.groups_per_piece;
-    const int ng = min(Lg.groups_per_piece, Lg.groups - G0);
-    // lane c = 0 finishes the gate row g, lane c = 1 the up row g (same instructions, quad_row_dot)
-    const int row0 = r0 - (r0 / S.I) * S.I;
-    const uint8_t* sw = wreg + 2 * CH * Lg.stride;
-    const int sarr = c == 1 ? 2 : 0;  // scale array of this lane's row: gate (0) or up (2); mins follow
-    const uint32_t sskip = window(S.ncode + 2 * ((sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
-    const uint32_t mskip = window(S.ncode + 2 * (S.ng + (sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
-    const uint16_t* srow = reinterpret_cast<const uint16_t*>(sw + sarr * Lg.sc_win + sskip) + g * Lg.gpr;
-    const uint16_t* mrow = reinterpret_cast<const uint16_t*>(sw + (sarr + 1) * Lg.sc_win + mskip) + g * Lg.gpr;
-    const uint8_t* rowg = wreg + g * Lg.stride;
-    const uint8_t* rowu = wreg + (CH + g) * Lg.stride;
-    if (ok) mbar_wait(wbar, uint32_t(round & 1));
-    float acc = 0.0f;
-    for (int G = 0; G < ng; G += 2) {
-      if (!ok) break;
-      const int G1 = min(G + 1, ng - 1);  // an odd tail repeats the last group; its result is dropped
-      uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
-      lds_unit<BITS>(rowg + (G * 4 + c) * 4 * BITS, wa0);
-      lds_unit<BITS>(rowu + (G * 4 + c) * 4 * BITS, wb0);
-      lds_unit<BITS>(rowg + (G1 * 4 + c) * 4 * BITS, wa1);
-      lds_unit<BITS>(rowu + (G1 * 4 + c) * 4 * BITS, wb1);
-      lds_b8(g < 3 ? bx + ((4 * (G0 + G) + c) * 3 + g) * 8 : zero, bb0);
-      lds_b8(g < 3 ? bx + ((4 * (G0 + G1) + c) * 3 + g) * 8 : zero, bb1);
-      int d0[4], d1[4];
-      imma_group<BITS>(wa0, wb0, bb0, d0);
-      imma_group<BITS>(wa1, wb1, bb1, d1);
-      const float D0 = quad_row_dot(d0, c), D1 = quad_row_dot(d1, c);
-      {
-        const int qg = (G0 + G) >> S.gshift;
-        acc += f16_bits_to_f32(srow[qg]) * (D0 * gsum[2 * (G0 + G) + 1]) + f16_bits_to_f32(mrow[qg]) * gsum[2 * (G0 + G)];
+  // ---- warp (2r + h) computes K half h of the blocks of region r
+  if (warp < 2 * R) {
+    const int r = warp >> 1, hf = warp & 1;
+    const uint8_t* reg = sm + int64_t(r) * Lg.region;
+    const int64_t cb = CH * Lg.row_bytes;
+    const int G0 = hf * Lg.gph;
+    const int ng = min(Lg.gph, Lg.groups - G0);
+    const int sarr = c == 1 ? 2 : 0;  // lane c = 0 finishes the gate row g, c = 1 the up row g
+    int round = 0;
+    for (int bi = r; bi < nb; bi += R, ++round) {
+      if (round > 0) {  // the region is free once both halves of its previous block are done
+        named_sync(1 + r, 64);
+        if (hf == 0) issue_block(bi);
       }
-      if (G1 != G) {
-        const int qg = (G0 + G1) >> S.gshift;
-        acc += f16_bits_to_f32(srow[qg]) * (D1 * gsum[2 * (G0 + G1) + 1]) + f16_bits_to_f32(mrow[qg]) * gsum[2 * (G0 + G1)];
+      const int blk = b0 + bi;
+      const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
+      int64_t slot;
+      const bool ok = route_slot(meta, j, S, slot);
+      const uint32_t sskip = window(S.ncode + 2 * ((sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
+      const uint32_t mskip = window(S.ncode + 2 * (S.ng + (sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
+      const uint8_t* sw = reg + 2 * cb;
+      const uint16_t* srow = reinterpret_cast<const uint16_t*>(sw + sarr * Lg.sc_win + sskip) + g * Lg.gpr;
+      const uint16_t* mrow = reinterpret_cast<const uint16_t*>(sw + (sarr + 1) * Lg.sc_win + mskip) + g * Lg.gpr;
+      const uint8_t* rowg = reg + g * Lg.row_bytes;
+      const uint8_t* rowu = reg + cb + g * Lg.row_bytes;
+      mbar_wait(&gbar[r], uint32_t(round & 1));  // completes at once (no bytes) for a skipped expert
+      float acc = 0.0f;
+      for (int G = 0; G < ng; G += 2) {
+        if (!ok) break;
+        const int Ga = G0 + G, Gb = G0 + min(G + 1, ng - 1);  // an odd tail repeats the last group
+        uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
+        lds_unit<BITS>(rowg + (Ga * 4 + c) * 4 * BITS, wa0);
+        lds_unit<BITS>(rowu + (Ga * 4 + c) * 4 * BITS, wb0);
+        lds_unit<BITS>(rowg + (Gb * 4 + c) * 4 * BITS, wa1);
+        lds_unit<BITS>(rowu + (Gb * 4 + c) * 4 * BITS, wb1);
+        lds_b8(g < 3 ? bx + ((4 * Ga + c) * 3 + g) * 8 : zero, bb0);
+        lds_b8(g < 3 ? bx + ((4 * Gb + c) * 3 + g) * 8 : zero, bb1);
+        int d0[4], d1[4];
+        imma_group<BITS>(wa0, wb0, bb0, d0);
+        imma_group<BITS>(wa1, wb1, bb1, d1);
+        const float D0 = quad_row_dot(d0, c), D1 = quad_row_dot(d1, c);
+        {
+          const int qg = Ga >> S.gshift;
+          acc += f16_bits_to_f32(srow[qg]) * (D0 * gsum[2 * Ga + 1]) + f16_bits_to_f32(mrow[qg]) * gsum[2 * Ga];
+        }
+        if (Gb != Ga) {
+          const int qg = Gb >> S.gshift;
+          acc += f16_bits_to_f32(srow[qg]) * (D1 * gsum[2 * Gb + 1]) + f16_bits_to_f32(mrow[qg]) * gsum[2 * Gb];
+        }
       }
+      if (c < 2) halves[((bi * NSPLIT + hf) * CH + g) * 2 + c] = acc;
     }
-    if (c < 2) halves[(piece * CH + g) * 2 + c] = acc;
   }
   __syncthreads();
-  // ---- SwiGLU of complete rows: sum the K parts of each block in a fixed order, write a once
-  for (int t = threadIdx.x; t < (b1 - b0) * CH; t += blockDim.x) {
+  // ---- SwiGLU of complete rows: K halves summed in a fixed order, a written once
+  for (int t = threadIdx.x; t < nb * CH; t += blockDim.x) {
     const int bi = t / CH, rw = t - bi * CH;
-    float gs = 0.0f, us = 0.0f;
-    for (int sp = 0; sp < NSPLIT; ++sp) {
-      gs += halves[((bi * NSPLIT + sp) * CH + rw) * 2];
-      us += halves[((bi * NSPLIT + sp) * CH + rw) * 2 + 1];
-    }
-    const int r = (b0 + bi) * CH + rw;
+    const float gs = halves[((bi * NSPLIT) * CH + rw) * 2] + halves[((bi * NSPLIT + 1) * CH + rw) * 2];
+    const float us = halves[((bi * NSPLIT) * CH + rw) * 2 + 1] + halves[((bi * NSPLIT + 1) * CH + rw) * 2 + 1];
+    const int rr = (b0 + bi) * CH + rw;
     int64_t slot;
-    a_out[r] = route_slot(meta, r / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
+    a_out[rr] = route_slot(meta, rr / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
   }
 }
 
@@ -392,8 +427,11 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
     for (int j = lane; j < S.k; j += 32) {
       mbar_init(&bars[j], 1);
       mbar_fence_init();
-      int64_t slot;
-      const bool ok = route_slot(meta, j, S, slot);
+      // read through L2 (ld.global.cg): this runs before griddepcontrol.wait, after the producer of
+      // meta has completed (the gate/up grid triggers this launch only after its own wait)
+      const float f = __ldcg(meta + j);
+      const bool ok = f >= 0.0f && f < float(S.nslots);
+      const int64_t slot = ok ? int64_t(f) : 0;
       if (!ok) flag(WISP_STATUS_BAD_SLOT);
       if (!ok || nrows <= 0) {
         mbar_expect_tx(&bars[j], 0);
@@ -440,6 +478,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
     }
   }
   __syncthreads();
+  pdl_launch_dependents();
 
   for (int piece = warp; piece < npieces; piece += DN_WARPS) {
     const int j = piece / NSPLIT, sp = piece % NSPLIT;

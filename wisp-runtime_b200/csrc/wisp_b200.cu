@@ -238,7 +238,12 @@ static int num_sms() {
 
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    // the whole unified L1 as shared memory, so CTAs of the next kernel in a PDL chain fit beside
+    // this one's (the carveout is chosen per launch; a smaller one would keep them out)
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(block);
@@ -252,26 +257,23 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// the tensor-core pipeline applies when: 4/3/2-bit codes, quantization groups made of whole
-// 128-code MMA groups with an even count per row (4-byte scale copies), 8-row blocks never
-// straddling experts, at most 16 down rows per CTA, and both kernels' shared memory fits
+// the two-kernel tensor-core pipeline applies when: 4/3/2-bit codes, quantization groups made of whole
+// 128-code MMA groups, 8-row blocks never straddling experts, at most 16 down rows per CTA, k <= 32
+// (one copy lane per routed expert), and both kernels' shared memory fits
 static bool v4_supported(const MoeShape& S, int bits, int nctas) {
   if (bits != 4 && bits != 3 && bits != 2) return false;
   if (S.group % 128 != 0 || (128 << S.gshift) != S.group || S.H % 128 != 0 || S.I % 128 != 0) return false;
-  if ((S.H / S.group) % 2 || (S.I / S.group) % 2 || S.ng % 2) return false;
   if (S.ncode % 16 || S.mat_bytes % 16 || (int64_t(S.H) * bits / 8) % 16 || (int64_t(S.I) * bits / 8) % 16) return false;
   if ((S.H + nctas - 1) / nctas > 16) return false;
-  if (S.k > 32) return false;  // one copy lane of warp 0 per routed expert
-  const v4::GuL Lg = v4::gu_layout(S.H, S.group, bits);
-  if (Lg.groups_per_piece > v4::MAXG) return false;
-  const int64_t gsm = v4::gu_smem(S.H, S.I, S.k, S.group, bits, nctas);
+  if (S.k > 32) return false;
+  const v4::GuL Lg = v4::gu_layout(S.H, S.I, S.k, S.group, bits, nctas);
   const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
-  return gsm <= 220 * 1024 && Ld.bytes <= 220 * 1024;
+  return Lg.R > 0 && Ld.bytes <= v4::SMEM_LIMIT;
 }
 
 static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
                      float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
-  const int64_t gsm = v4::gu_smem(S.H, S.I, S.k, S.group, bits, nctas);
+  const int64_t gsm = v4::gu_layout(S.H, S.I, S.k, S.group, bits, nctas).bytes;
   const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
   cudaError_t e = cudaSuccess;
 #define WISP_V4(B)                                                                                          \
@@ -369,7 +371,9 @@ int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, co
                       (!delta || aligned(delta, 16)) && (!sum_out || aligned(sum_out, 16));
   if (vec_ok) {
     const int threads = int((H / 8 + 31) / 32 * 32);
-    rmsnorm_vec_kernel<<<(unsigned)rows, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
+    const cudaError_t e = launch_pdl(rmsnorm_vec_kernel, int(rows), threads, 0, static_cast<cudaStream_t>(stream), x, delta,
+                                     sum_out, w, H, eps, out);
+    if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "rmsnorm: %s", cudaGetErrorString(e));
     return check_launch("rmsnorm");
   }
   const size_t smem = size_t(H) * 4;

@@ -42,10 +42,18 @@ def _need_cuda(*ts):
             raise WispError("wisp kernels need CUDA tensors (there is no CPU path)")
 
 
+def moe_scratch(k, I, device):
+    """Scratch for moe_decode_fast (the fp32 intermediate a, k*I values); reusable by calls that do
+    not overlap."""
+    return torch.empty(k * I, dtype=torch.float32, device=device)
+
+
 def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratch=None, variant=0):
     """Fused dequant + GEMV MoE of one token over the k experts named by ``meta`` (fp32 [2k] =
     [slots..., weights...]).  pool: uint8 [nslots, nbytes]; x: bf16 [H].  Returns bf16 [H].
-    ``variant``: 0 automatic, 1 warp-per-row CUDA-core kernels, 2 TMA bulk copies + integer MMA."""
+    ``variant``: 0 automatic, 1 warp-per-row CUDA-core kernels, 2 TMA bulk copies + integer MMA in
+    two chained kernels.  ``scratch`` (reusable across calls that do not overlap) comes from
+    ``moe_scratch``; one is allocated per call when omitted."""
     assert H % group == 0 and I % group == 0 and n == H * I
     _need_cuda(pool, meta, x)
     assert pool.dtype == torch.uint8 and pool.dim() == 2 and pool.is_contiguous()
@@ -54,7 +62,9 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
         raise WispError(f"x must be bfloat16 (got {x.dtype})")
     x = x.contiguous()
     if scratch is None:
-        scratch = torch.empty((k, I), dtype=torch.float32, device=x.device)
+        scratch = moe_scratch(k, I, x.device)
+    elif scratch.numel() < k * I or scratch.dtype != torch.float32 or not scratch.is_contiguous():
+        raise WispError(f"scratch must be a contiguous float32 tensor of >= {k * I} elements")
     if out is None:
         out = torch.empty((H,), dtype=x.dtype, device=x.device)
     _lib.call(
