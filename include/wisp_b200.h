@@ -119,6 +119,56 @@ int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes,
 int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t* k, int64_t k_stride, int Hk, int D,
                      const uint16_t* cos, const uint16_t* sin, uint16_t* qo, uint16_t* ko, void* stream);
 
+/* ---- decoder step (bs = 1) --------------------------------------------------------------------- */
+/* y[n] = bf16(W[n,:] . x') for W row-major [N, K] bf16 (fp32 accumulation), where x' is x, or
+ * bf16(x + x_add) when x_add is given (stored to x_sum_out when non-NULL), then RMSNorm-ed with
+ * norm_w when given: x' = bf16(norm_w * bf16(x' * rsqrt(mean(x'^2) + eps))) (stored to xn_out when
+ * non-NULL).  With res: y[n] = bf16(res[n] + bf16(W[n,:] . x')).  K % 8 == 0, K <= 4096; W, x,
+ * x_add, norm_w, x_sum_out and xn_out 16-byte aligned; y, x_sum_out and xn_out must not alias x or
+ * x_add (y may alias res).  The weight stream starts before the previous kernel in the stream ends
+ * (programmatic dependent launch).
+ * Replaces the bf16 nn.Linear calls of the decode step (q/k/v/o projections, the router gate, lm_head:
+ * wisp/graphdec.py:160-162, :175, :177, :213) together with the RMSNorm before them and the residual
+ * add after them (wisp/graphdec.py:159, :175-176, :209, :213; wisp/model.py:94-107). */
+int wisp_gemv(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const uint16_t* x_add, uint16_t* x_sum_out,
+              const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* res, uint16_t* y, void* stream);
+
+/* Per-head RMSNorm of the q and k heads of qkv = [Hq*D | Hk*D | Hk*D] (weights qn_w, kn_w [D]),
+ * rotate-half rotary with cos/sin rows `*pos` of the [tmax, D] tables (fp32 math, one rounding), q to
+ * q_out [Hq, D], k and v into row `*pos` of the caches [Hk, tmax, D].  *pos outside [0, tmax) writes
+ * nothing and sets WISP_STATUS_BAD_POS.  D even, D <= 256.
+ * Replaces wisp/graphdec.py:160-170 (q_norm/k_norm, rope_decode, the two index_copy_ into the cache). */
+int wisp_qk_norm_rope_kv(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t* qn_w, const uint16_t* kn_w, float eps,
+                         const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos, int64_t tmax, uint16_t* q_out,
+                         uint16_t* k_cache, uint16_t* v_cache, void* stream);
+
+/* fp32 elements of the workspace wisp_gqa_decode_attn needs (host-only; -1 for a bad shape). */
+int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax);
+
+/* GQA decode attention of one token: q [Hq, D] (query head i uses KV head i / (Hq/Hk)) over cache
+ * positions 0..*pos of k_cache, v_cache [Hk, tmax, D]; softmax(scale * q.k) fp32; out [Hq, D] bf16.
+ * Split over chunks of 64 positions, then one combine launch.  Hq/Hk <= 8, D % 32 == 0, D <= 128.
+ * Replaces wisp/graphdec.py:171-174 (SDPA over the static cache with mask ar <= pos) and the patched
+ * decode attention of wisp/model.py:136-150. */
+int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache, int64_t tmax,
+                         const int64_t* pos, float scale, float* workspace, uint16_t* out, void* stream);
+
+/* Router of one token: p = softmax(logits bf16 [E]) in fp32, the k largest (ties: lower expert id),
+ * renormalised when norm_topk, rounded to bf16.  row (nullable) = fp32 [k experts | k weights];
+ * meta = fp32 [k slots | k weights], slot = slot_table[base + e] when slot_table is given, else
+ * base + e.  E <= 1024, k <= 32.
+ * Replaces wisp/graphdec.py:177-182 and wisp/moe.py:67-72 (softmax, topk, renormalise, bf16). */
+int wisp_router_topk(const uint16_t* logits, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* row,
+                     float* meta, void* stream);
+
+/* out [H] = table[*token] (bf16 rows, H % 8 == 0).  *token outside [0, V) sets WISP_STATUS_BAD_ROUTE. */
+int wisp_embed(const uint16_t* table, int64_t V, int64_t H, const int64_t* token, uint16_t* out, void* stream);
+
+/* *out = the index of the largest of x[0..n) (bf16; ties: the lower index; NaN never wins), over a
+ * workspace of WISP_ARGMAX_WORKSPACE u64. */
+#define WISP_ARGMAX_WORKSPACE 256
+int wisp_argmax(const uint16_t* x, int64_t n, uint64_t* workspace, int64_t* out, void* stream);
+
 /* RMSNorm of `rows` rows of H bf16 values: out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))).
  * If `delta` is non-NULL the row is first replaced by bf16(x + delta) and, when `sum_out` is
  * non-NULL, that sum is stored there (the residual add fused in).

@@ -1,0 +1,195 @@
+"""GPU parity of the decode-step kernels (GEMV with fused residual/RMSNorm, q/k norm + rotary + cache
+write, GQA decode attention, router top-k, embedding, argmax) through the C ABI, against plain torch
+fp32 references of the same rounding steps, the oracle, and the reference's SDPA fixture."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import wisp_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(u16):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def _np(t):
+    return O.bf16_bits_to_f32(t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def _gen(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+def _ref_gemv(W, x, x_add=None, norm_w=None, eps=1e-6, res=None):
+    """torch fp32 reference with the kernel's rounding steps (bf16 after every named op)."""
+    xs = x.float()
+    if x_add is not None:
+        xs = (xs + x_add.float()).to(torch.bfloat16).float()
+    xn = xs
+    if norm_w is not None:
+        inv = torch.rsqrt((xs * xs).mean() + eps)
+        xn = (norm_w.float() * (xs * inv).to(torch.bfloat16).float()).to(torch.bfloat16).float()
+    y = (W.float() @ xn).to(torch.bfloat16).float()
+    if res is not None:
+        y = (res.float() + y).to(torch.bfloat16).float()
+    return xs, xn, y
+
+
+@pytest.mark.parametrize("N,K", [(5120, 2048), (2048, 4096), (128, 2048), (1000, 64), (37, 1024), (151936 // 16, 2048)])
+def test_gemv_plain(N, K):
+    from wisp import kernels
+
+    g = _gen(N + K)
+    W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16)
+    y = kernels.gemv(W, x)
+    _, _, ref = _ref_gemv(W, x)
+    # fp32 sums in another order: at most one bf16 rounding step apart
+    tol = 2.0**-7 * ref.abs().max().item()
+    assert (y.float() - ref).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("K", [2048, 64])
+def test_gemv_fused_residual_norm(K):
+    from wisp import kernels
+
+    N = 3 * K
+    g = _gen(K)
+    W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16)
+    xa = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(K, device="cuda", generator=g)).to(torch.bfloat16)
+    res = torch.randn(N, device="cuda", generator=g).to(torch.bfloat16)
+    xs_out = torch.empty(K, dtype=torch.bfloat16, device="cuda")
+    xn_out = torch.empty(K, dtype=torch.bfloat16, device="cuda")
+    y = kernels.gemv(W, x, x_add=xa, x_sum_out=xs_out, norm_w=nw, eps=1e-6, xn_out=xn_out, res=res)
+    xs, xn, ref = _ref_gemv(W, x, xa, nw, 1e-6, res)
+    assert torch.equal(xs_out.float(), xs)  # bf16 add: exact
+    assert (xn_out.float() - xn).abs().max().item() <= 2.0**-7 * xn.abs().max().item()  # rsqrt rounding
+    assert (y.float() - ref).abs().max().item() <= 2.0**-6 * ref.abs().max().item()
+
+
+def test_gemv_rejects_aliasing():
+    from wisp import kernels
+    from wisp._lib import WispError
+
+    W = torch.zeros(64, 64, dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros(64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(WispError, match="alias"):
+        kernels.gemv(W, x, out=x)
+
+
+@pytest.mark.parametrize("pos", [0, 5, 700])
+def test_qk_norm_rope_kv(pos):
+    from wisp import kernels
+    from wisp.model import rotary_tables
+
+    Hq, Hk, D, tmax, eps = 32, 4, 128, 1024, 1e-6
+    g = _gen(pos)
+    qkv = torch.randn((Hq + 2 * Hk) * D, device="cuda", generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16)
+    cos, sin = rotary_tables(D, tmax, 1e6, "cuda")
+    kc = torch.zeros(Hk, tmax, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    p = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    q = kernels.qk_norm_rope_kv(qkv, Hq, Hk, D, qn, kn, eps, cos, sin, p, kc, vc)
+    heads = _np(qkv).reshape(Hq + 2 * Hk, D)
+    c, s = _np(cos[pos]), _np(sin[pos])
+
+    def normed(x, w):
+        inv = 1.0 / np.sqrt(np.mean(x * x, -1, keepdims=True) + np.float32(eps))
+        return O.round_bf16(_np(w) * O.round_bf16(x * inv))
+
+    want_q = O.round_bf16(O.rope(normed(heads[:Hq], qn), c, s))
+    want_k = O.round_bf16(O.rope(normed(heads[Hq : Hq + Hk], kn), c, s))
+    got_q = _np(q).reshape(Hq, D)
+    got_k = _np(kc[:, pos])
+    # rsqrt and the fp32 products may round one bf16 ulp apart
+    assert np.abs(got_q - want_q).max() <= 2.0**-6 * np.abs(want_q).max()
+    assert np.abs(got_k - want_k).max() <= 2.0**-6 * np.abs(want_k).max()
+    assert np.array_equal(_np(vc[:, pos]), heads[Hq + Hk :])
+    others = torch.ones(tmax, dtype=torch.bool)
+    others[pos] = False
+    assert not kc[:, others].any() and not vc[:, others].any()
+
+
+def test_attention_matches_reference_fixture(golden):
+    """The reference graph decoder's masked GQA SDPA on the fixture's cache (tmax 64)."""
+    from wisp import kernels
+
+    a = golden("attn")
+    Hq, D = a["q"].shape
+    Hk = a["kc"].shape[0]
+    q, kc, vc = _bf(a["q"]), _bf(a["kc"]), _bf(a["vc"])
+    pos = torch.tensor([int(a["pos"])], dtype=torch.int64, device="cuda")
+    out = kernels.gqa_decode_attn(q.reshape(-1), Hq, Hk, D, kc, vc, pos, D**-0.5)
+    ref = a["out"]
+    assert np.abs(_np(out).reshape(Hq, D) - ref).max() <= 1e-2 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("pos", [0, 1, 63, 64, 65, 777, 4095])
+@pytest.mark.parametrize("G,D", [(8, 128), (8, 64), (2, 32)])
+def test_attention_vs_oracle(pos, G, D):
+    from wisp import kernels
+
+    Hk, tmax = 4, 4096
+    Hq = Hk * G
+    g = _gen(pos + D)
+    q = torch.randn(Hq * D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    p = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    out = kernels.gqa_decode_attn(q, Hq, Hk, D, kc, vc, p, D**-0.5)
+    want = O.gqa_decode_attention(_np(q).reshape(Hq, D), _np(kc), _np(vc), pos, D**-0.5)
+    assert np.abs(_np(out).reshape(Hq, D) - want).max() <= 1e-2 * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("E,k", [(128, 8), (32, 4), (8, 2)])
+def test_router_topk_vs_oracle(E, k):
+    from wisp import kernels
+
+    for seed in range(5):
+        g = _gen(seed * 100 + E)
+        logits = (torch.randn(E, device="cuda", generator=g) * 2).to(torch.bfloat16)
+        row = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        meta = kernels.router_topk(logits, k, True, base=5 * E, row=row)
+        sel, rw = O.router_topk(_np(logits)[None], k)
+        got_sel = row[:k].long().cpu().numpy()
+        assert np.array_equal(np.sort(got_sel), np.sort(sel[0]))
+        order = np.argsort(sel[0])
+        gorder = np.argsort(got_sel)
+        assert np.abs(row[k:].cpu().numpy()[gorder] - rw[0][order]).max() <= 2.0**-8
+        assert np.array_equal(meta[:k].long().cpu().numpy(), got_sel + 5 * E)
+        assert torch.equal(meta[k:], row[k:])
+
+
+def test_router_slot_table():
+    from wisp import kernels
+
+    E, k = 16, 2
+    logits = torch.zeros(E, dtype=torch.bfloat16, device="cuda")
+    logits[3], logits[9] = 4.0, 3.0
+    table = torch.arange(100, 100 + 2 * E, dtype=torch.int32, device="cuda")
+    table[E + 9] = -1
+    meta = kernels.router_topk(logits, k, True, slot_table=table, base=E)
+    assert meta[:k].tolist() == [100.0 + E + 3, -1.0]
+
+
+def test_embed_and_argmax():
+    from wisp import kernels
+
+    V, H = 5000, 2048
+    g = _gen(3)
+    table = torch.randn(V, H, device="cuda", generator=g).to(torch.bfloat16)
+    tok = torch.tensor([4321], dtype=torch.int64, device="cuda")
+    assert torch.equal(kernels.embed(table, tok), table[4321])
+    x = torch.randn(151936, device="cuda", generator=g).to(torch.bfloat16)
+    assert int(kernels.argmax(x)) == int(torch.argmax(x.float()))
+    x[7] = x[100000] = 50.0  # tie: the lower index wins
+    assert int(kernels.argmax(x)) == 7
+    x[3] = float("nan")
+    assert int(kernels.argmax(x)) == 7

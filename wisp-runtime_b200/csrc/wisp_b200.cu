@@ -4,6 +4,8 @@
 
 #include "common.cuh"
 #include "decode_ops.cuh"
+#include "decoder.cuh"
+#include "dense.cuh"
 #include "moe_decode.cuh"
 #include "moe_decode_v4.cuh"
 #include "quant.cuh"
@@ -360,6 +362,106 @@ int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t
   rope_decode_kernel<<<(heads + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(
       q, q_stride, Hq, k, k_stride, Hk, D, cos, sin, qo, ko);
   return check_launch("rope_decode");
+}
+
+int wisp_gemv(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const uint16_t* x_add, uint16_t* x_sum_out,
+              const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* res, uint16_t* y, void* stream) {
+  WISP_REQUIRE(W && x && y, "wisp_gemv: NULL pointer");
+  WISP_REQUIRE(N > 0 && K > 0 && K % 8 == 0 && K <= 4096, "wisp_gemv: need N > 0, K a multiple of 8 and <= 4096 (N=%lld K=%lld)",
+               (long long)N, (long long)K);
+  WISP_REQUIRE(aligned(W, 16) && aligned(x, 16) && (!x_add || aligned(x_add, 16)) && (!x_sum_out || aligned(x_sum_out, 16)) &&
+                   (!norm_w || aligned(norm_w, 16)) && (!xn_out || aligned(xn_out, 16)),
+               "wisp_gemv: W, x, x_add, x_sum_out, norm_w and xn_out must be 16-byte aligned");
+  WISP_REQUIRE(x_sum_out == nullptr || x_add != nullptr, "wisp_gemv: x_sum_out needs x_add");
+  WISP_REQUIRE(y != x && y != x_add && (!x_sum_out || (x_sum_out != x && x_sum_out != x_add)) &&
+                   (!xn_out || (xn_out != x && xn_out != x_add)),
+               "wisp_gemv: y, x_sum_out and xn_out must not alias x or x_add");
+  dense::GemvArgs A{W, N, K, x, x_add, x_sum_out, norm_w, eps, xn_out, res, y};
+  const dense::GemvLayout L = dense::gemv_layout(K);
+  const int grid = int(N < num_sms() ? N : num_sms());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (K <= 256) e = launch_pdl(dense::gemv_kernel<1>, grid, dense::THREADS, size_t(L.bytes), s, A);
+  else if (K <= 512) e = launch_pdl(dense::gemv_kernel<2>, grid, dense::THREADS, size_t(L.bytes), s, A);
+  else if (K <= 1024) e = launch_pdl(dense::gemv_kernel<4>, grid, dense::THREADS, size_t(L.bytes), s, A);
+  else if (K <= 2048) e = launch_pdl(dense::gemv_kernel<8>, grid, dense::THREADS, size_t(L.bytes), s, A);
+  else e = launch_pdl(dense::gemv_kernel<16>, grid, dense::THREADS, size_t(L.bytes), s, A);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gemv: %s", cudaGetErrorString(e));
+  return check_launch("gemv");
+}
+
+int wisp_qk_norm_rope_kv(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t* qn_w, const uint16_t* kn_w, float eps,
+                         const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos, int64_t tmax, uint16_t* q_out,
+                         uint16_t* k_cache, uint16_t* v_cache, void* stream) {
+  WISP_REQUIRE(qkv && qn_w && kn_w && cos_t && sin_t && pos && q_out && k_cache && v_cache, "wisp_qk_norm_rope_kv: NULL pointer");
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && D > 0 && D % 2 == 0 && D <= dec::QK_MAX_D && tmax > 0, "wisp_qk_norm_rope_kv: bad shape");
+  const int heads = Hq + 2 * Hk;
+  const cudaError_t e = launch_pdl(dec::qk_norm_rope_kv_kernel, (heads + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream), qkv, Hq,
+                                   Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax, q_out, k_cache, v_cache);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_qk_norm_rope_kv: %s", cudaGetErrorString(e));
+  return check_launch("qk_norm_rope_kv");
+}
+
+int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {
+  if (Hq <= 0 || Hk <= 0 || D <= 0 || tmax <= 0 || Hq % Hk) return -1;
+  return int64_t(Hk) * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * (D + 2);
+}
+
+int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache, int64_t tmax,
+                         const int64_t* pos, float scale, float* workspace, uint16_t* out, void* stream) {
+  WISP_REQUIRE(q && k_cache && v_cache && pos && workspace && out, "wisp_gqa_decode_attn: NULL pointer");
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && Hq % Hk == 0 && Hq / Hk <= dec::MAX_G, "wisp_gqa_decode_attn: need Hq a multiple of Hk, Hq/Hk <= %d",
+               dec::MAX_G);
+  WISP_REQUIRE(D > 0 && D % 32 == 0 && D <= dec::MAX_D && tmax > 0, "wisp_gqa_decode_attn: need D a multiple of 32, <= %d", dec::MAX_D);
+  const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(Hk, nchunk);
+  cfg.blockDim = dim3(dec::ATTN_THREADS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, dec::attn_split_kernel, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
+  e = launch_pdl(dec::attn_combine_kernel, Hq, 128, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
+  return check_launch("gqa_decode_attn");
+}
+
+int wisp_router_topk(const uint16_t* logits, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* row,
+                     float* meta, void* stream) {
+  WISP_REQUIRE(logits && meta, "wisp_router_topk: NULL pointer");
+  WISP_REQUIRE(E > 0 && E <= 1024 && k >= 1 && k <= 32 && k <= E, "wisp_router_topk: need 1 <= k <= min(E, 32), E <= 1024");
+  const cudaError_t e = launch_pdl(dec::router_topk_kernel, 1, 32, 0, static_cast<cudaStream_t>(stream), logits, E, k, norm_topk,
+                                   slot_table, base, row, meta);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_router_topk: %s", cudaGetErrorString(e));
+  return check_launch("router_topk");
+}
+
+int wisp_embed(const uint16_t* table, int64_t V, int64_t H, const int64_t* token, uint16_t* out, void* stream) {
+  WISP_REQUIRE(table && token && out, "wisp_embed: NULL pointer");
+  WISP_REQUIRE(V > 0 && H > 0 && H % 8 == 0 && aligned(table, 16) && aligned(out, 16), "wisp_embed: need H % 8 == 0, 16-byte aligned rows");
+  const int threads = 256;
+  const int grid = int((H / 8 + threads - 1) / threads);
+  const cudaError_t e = launch_pdl(dec::embed_kernel, grid, threads, 0, static_cast<cudaStream_t>(stream), table, V, H, token, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_embed: %s", cudaGetErrorString(e));
+  return check_launch("embed");
+}
+
+int wisp_argmax(const uint16_t* x, int64_t n, uint64_t* workspace, int64_t* out, void* stream) {
+  WISP_REQUIRE(x && workspace && out, "wisp_argmax: NULL pointer");
+  WISP_REQUIRE(n > 0 && n < (int64_t(1) << 32), "wisp_argmax: need 0 < n < 2^32");
+  const int parts = WISP_ARGMAX_WORKSPACE;
+  const int grid = int((n + 255) / 256 < parts ? (n + 255) / 256 : parts);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_pdl(dec::argmax_partial_kernel, grid, 256, 0, s, x, n, (unsigned long long*)workspace);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_argmax: %s", cudaGetErrorString(e));
+  e = launch_pdl(dec::argmax_final_kernel, 1, 32, 0, s, (const unsigned long long*)workspace, grid, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_argmax: %s", cudaGetErrorString(e));
+  return check_launch("argmax");
 }
 
 int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, const uint16_t* w, int64_t rows, int64_t H,

@@ -17,6 +17,7 @@ WISP_OK, WISP_ERR_INVALID, WISP_ERR_CUDA, WISP_ERR_UNSUPPORTED = 0, 1, 2, 3
 STATUS_BAD_SLOT, STATUS_BAD_POS, STATUS_WAIT_TIMEOUT, STATUS_BAD_ROUTE = 0x1, 0x2, 0x4, 0x8
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 MOE_NOALLOC_MAX_SCRATCH = 65536  # WISP_MOE_NOALLOC_MAX_SCRATCH: fp32 values of k*I
+ARGMAX_WORKSPACE = 256  # WISP_ARGMAX_WORKSPACE: u64 entries
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -36,6 +37,13 @@ SIGNATURES = {
     "wisp_moe_decode_variant": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _I, _P]),
     "wisp_moe_decode_noalloc": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
+    "wisp_gemv": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P]),
+    "wisp_qk_norm_rope_kv": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _P, _P]),
+    "wisp_attn_workspace_floats": (_L, [_I, _I, _I, _L]),
+    "wisp_gqa_decode_attn": (_I, [_P, _I, _I, _I, _P, _P, _L, _P, _F, _P, _P, _P]),
+    "wisp_router_topk": (_I, [_P, _I, _I, _I, _P, _L, _P, _P, _P]),
+    "wisp_embed": (_I, [_P, _L, _L, _P, _P, _P]),
+    "wisp_argmax": (_I, [_P, _L, _P, _P, _P]),
     "wisp_rmsnorm": (_I, [_P, _P, _P, _P, _L, _L, _F, _P, _P]),
 }
 

@@ -1,0 +1,177 @@
+"""CUDA-graph decode of one token at a time (bs = 1), every op a libwisp_b200 kernel.
+
+Drop-in for the reference ``wisp.graphdec.GraphDecoder`` (wisp/graphdec.py): static buffers (KV
+cache [L, Hk, tmax, D], position and token in ``ctl``, routing in ``meta``) so that nothing captured
+depends on the current length.  The reference cuts a token at its 48 host decisions (expert paging)
+and records the pieces between them; with the experts resident (or a device-side slot table) there
+is no host decision, so a whole token is one graph:
+
+    embed -> per layer: [RMSNorm+qkv GEMV] [q/k norm, rotary, cache write] [attention split, combine]
+                        [o GEMV + residual] [RMSNorm+router GEMV] [top-k -> meta] [MoE gate/up, down]
+          -> [residual + final RMSNorm + lm_head GEMV] [argmax]
+
+Each kernel is launched with programmatic dependent launch, so its prologue (and the weight stream of
+the GEMVs) overlaps the tail of the kernel before it.  ``greedy`` appends the position/token update
+to the graph, so a whole generation runs with no host round trip per token.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import kernels
+from .model import DecoderWeights, rotary_tables
+
+
+class GraphDecoder:
+    def __init__(self, w: DecoderWeights, tmax=2048, use_graph=True, slot_table=None):
+        cfg = w.cfg
+        self.w, self.cfg = w, cfg
+        dev = w.embed.device
+        self.dev = dev
+        self.L, self.H = cfg.layers, cfg.hidden
+        self.Hq, self.Hk, self.D = cfg.heads, cfg.kv_heads, cfg.head_dim
+        self.k, self.E, self.I = cfg.top_k, cfg.experts, cfg.moe_inter
+        self.tmax = (tmax + 63) // 64 * 64
+        self.use_graph = use_graph
+        self.slot_table = slot_table
+        bf, H = torch.bfloat16, self.H
+        d = dict(device=dev, dtype=bf)
+        self.kc = torch.zeros(self.L, self.Hk, self.tmax, self.D, **d)
+        self.vc = torch.zeros(self.L, self.Hk, self.tmax, self.D, **d)
+        self.cos, self.sin = rotary_tables(self.D, self.tmax, cfg.rope_theta, dev)
+        self.ctl = torch.zeros(2, dtype=torch.int64, device=dev)  # [token, position]
+        self.h_emb = torch.zeros(H, **d)
+        self.h_res = torch.zeros(H, **d)  # residual stream entering a layer
+        self.h_mid = torch.zeros(H, **d)  # residual stream after attention
+        self.xn = torch.zeros(H, **d)  # MoE input (post-attention RMSNorm)
+        self.moe = torch.zeros(H, **d)
+        self.qkv = torch.zeros((self.Hq + 2 * self.Hk) * self.D, **d)
+        self.q = torch.zeros(self.Hq * self.D, **d)
+        self.att = torch.zeros(self.Hq * self.D, **d)
+        self.rlog = torch.zeros(self.E, **d)
+        self.rows = torch.zeros(self.L, 2 * self.k, dtype=torch.float32, device=dev)  # per layer [experts | weights]
+        self.meta = torch.zeros(2 * self.k, dtype=torch.float32, device=dev)
+        self.scratch = kernels.moe_scratch(self.k, self.I, dev)
+        self.attn_ws = kernels.attn_workspace(self.Hq, self.Hk, self.D, self.tmax, dev)
+        self.argmax_ws = torch.zeros(256, dtype=torch.int64, device=dev)
+        self.logits = torch.zeros(cfg.vocab, **d)
+        self.next_token = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.scale = self.D ** -0.5
+        self.pos = 0
+        self.graph = self.greedy_graph = None
+
+    # ---------------------------------------------------------------------------------------------
+    def _layer(self, l):
+        w, c, lw = self.w, self.cfg, self.w.layers[l]
+        pos = self.ctl[1:2]
+        first = l == 0
+        # residual add of the previous MoE + input RMSNorm + q/k/v projections
+        kernels.gemv(
+            lw["wqkv"], self.h_emb if first else self.h_mid, x_add=None if first else self.moe,
+            x_sum_out=None if first else self.h_res, norm_w=lw["in_norm"], eps=c.eps, out=self.qkv,
+        )
+        kernels.qk_norm_rope_kv(
+            self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos,
+            self.kc[l], self.vc[l], q_out=self.q,
+        )
+        kernels.gqa_decode_attn(
+            self.q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], pos, self.scale, workspace=self.attn_ws, out=self.att
+        )
+        # o projection + residual, then post-attention RMSNorm + router
+        kernels.gemv(lw["wo"], self.att, res=self.h_emb if first else self.h_res, out=self.h_mid)
+        kernels.gemv(lw["router"], self.h_mid, norm_w=lw["post_norm"], eps=c.eps, xn_out=self.xn, out=self.rlog)
+        kernels.router_topk(
+            self.rlog, self.k, c.norm_topk, slot_table=self.slot_table, base=l * self.E, row=self.rows[l], meta=self.meta
+        )
+        kernels.moe_decode_fast(
+            w.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
+            scratch=self.scratch,
+        )
+
+    def _step(self):
+        kernels.embed(self.w.embed, self.ctl[0:1], out=self.h_emb)
+        for l in range(self.L):
+            self._layer(l)
+        kernels.gemv(
+            self.w.lm_head, self.h_mid, x_add=self.moe, x_sum_out=self.h_res, norm_w=self.w.final_norm,
+            eps=self.cfg.eps, out=self.logits,
+        )
+        kernels.argmax(self.logits, workspace=self.argmax_ws, out=self.next_token)
+
+    def _advance(self):
+        self.ctl[0:1].copy_(self.next_token)
+        self.ctl[1:2].add_(1)
+
+    def _capture(self, body):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        saved = self.ctl.clone()
+        with torch.cuda.stream(s):  # warm-up outside capture (aims the cache write at the last slot)
+            self.ctl[1] = self.tmax - 1
+            self._step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.ctl.copy_(saved)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            body()
+        return g
+
+    def capture(self):
+        """Record one decode step (and the greedy variant that also advances token and position)."""
+        self.graph = self._capture(self._step)
+
+        def greedy():
+            self._step()
+            self._advance()
+
+        self.greedy_graph = self._capture(greedy)
+
+    # ---------------------------------------------------------------------------------------------
+    @torch.no_grad()
+    def load_kv(self, k, v, T):
+        """Context of T positions: k, v [L, Hk, T, D] (e.g. from an HF prefill)."""
+        assert T < self.tmax, f"context {T} >= tmax {self.tmax}"
+        self.kc[:, :, :T].copy_(k)
+        self.vc[:, :, :T].copy_(v)
+        self.pos = T
+
+    @torch.no_grad()
+    def next(self, token):
+        """token: LongTensor [1] on the device -> logits [V] (bf16) for the following position."""
+        assert self.pos < self.tmax, "context full"
+        if self.use_graph and self.graph is None:
+            self.capture()
+        self.ctl[0:1].copy_(token.reshape(1))
+        self.ctl[1].fill_(self.pos)
+        if self.use_graph:
+            self.graph.replay()
+        else:
+            self._step()
+        self.pos += 1
+        return self.logits
+
+    @torch.no_grad()
+    def prefill(self, ids):
+        """Run prompt tokens one decode step each (positions pos, pos+1, ...); returns the last logits."""
+        logits = None
+        for t in ids.reshape(-1):
+            logits = self.next(t.reshape(1))
+        return logits
+
+    @torch.no_grad()
+    def greedy(self, token, steps):
+        """Greedy generation of ``steps`` tokens after ``token`` without host round trips; returns the
+        generated ids (device tensor)."""
+        assert self.pos + steps <= self.tmax, "context full"
+        if self.greedy_graph is None:
+            self.capture()
+        out = torch.empty(steps, dtype=torch.int64, device=self.dev)
+        self.ctl[0:1].copy_(token.reshape(1))
+        self.ctl[1].fill_(self.pos)
+        for i in range(steps):
+            self.greedy_graph.replay()
+            out[i : i + 1].copy_(self.next_token)
+        self.pos += steps
+        return out

@@ -28,6 +28,12 @@ __all__ = [
     "moe_decode_fast",
     "rope_decode",
     "rmsnorm",
+    "gemv",
+    "qk_norm_rope_kv",
+    "gqa_decode_attn",
+    "router_topk",
+    "embed",
+    "argmax",
     "WispError",
 ]
 
@@ -201,4 +207,108 @@ def rmsnorm(x, weight, eps=1e-6, delta=None, sum_out=None, out=None):
         out.data_ptr(),
         _stream(x),
     )
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# decoder step (bs = 1)
+# ------------------------------------------------------------------------------------------------
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _bf16(*ts):
+    for t in ts:
+        if t is not None and (t.dtype != torch.bfloat16 or not t.is_contiguous()):
+            raise WispError("contiguous bfloat16 tensors expected")
+
+
+def gemv(W, x, x_add=None, x_sum_out=None, norm_w=None, eps=1e-6, xn_out=None, res=None, out=None):
+    """y = W x' (W [N, K] bf16, one token), x' = rmsnorm(x + x_add) as requested; see wisp_gemv."""
+    _need_cuda(W, x)
+    _bf16(W, x, x_add, x_sum_out, norm_w, xn_out, res, out)
+    N, K = W.shape
+    if out is None:
+        out = torch.empty(N, dtype=torch.bfloat16, device=x.device)
+    _lib.call(
+        "wisp_gemv", W.data_ptr(), N, K, x.data_ptr(), _ptr(x_add), _ptr(x_sum_out), _ptr(norm_w), float(eps),
+        _ptr(xn_out), _ptr(res), out.data_ptr(), _stream(x),
+    )
+    return out
+
+
+def qk_norm_rope_kv(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, k_cache, v_cache, q_out=None):
+    """Per-head q/k RMSNorm, rotary at position ``pos`` (int64 device scalar), K/V cache write."""
+    _need_cuda(qkv, pos)
+    _bf16(qkv, qn_w, kn_w, cos_t, sin_t, k_cache, v_cache)
+    if q_out is None:
+        q_out = torch.empty(Hq * D, dtype=torch.bfloat16, device=qkv.device)
+    tmax = k_cache.shape[-2]
+    _lib.call(
+        "wisp_qk_norm_rope_kv", qkv.data_ptr(), Hq, Hk, D, qn_w.data_ptr(), kn_w.data_ptr(), float(eps), cos_t.data_ptr(),
+        sin_t.data_ptr(), pos.data_ptr(), tmax, q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _stream(qkv),
+    )
+    return q_out
+
+
+def attn_workspace(Hq, Hk, D, tmax, device):
+    n = _lib.lib().wisp_attn_workspace_floats(Hq, Hk, D, tmax)
+    if n < 0:
+        raise WispError("attn_workspace: bad shape")
+    return torch.empty(n, dtype=torch.float32, device=device)
+
+
+def gqa_decode_attn(q, Hq, Hk, D, k_cache, v_cache, pos, scale, workspace=None, out=None):
+    """Decode attention of one token over cache positions 0..pos; q [Hq*D], caches [Hk, tmax, D]."""
+    _need_cuda(q, pos)
+    _bf16(q, k_cache, v_cache)
+    tmax = k_cache.shape[-2]
+    if workspace is None:
+        workspace = attn_workspace(Hq, Hk, D, tmax, q.device)
+    if out is None:
+        out = torch.empty(Hq * D, dtype=torch.bfloat16, device=q.device)
+    _lib.call(
+        "wisp_gqa_decode_attn", q.data_ptr(), Hq, Hk, D, k_cache.data_ptr(), v_cache.data_ptr(), tmax, pos.data_ptr(),
+        float(scale), workspace.data_ptr(), out.data_ptr(), _stream(q),
+    )
+    return out
+
+
+def router_topk(logits, k, norm_topk=True, slot_table=None, base=0, row=None, meta=None):
+    """softmax -> top-k -> renormalise -> bf16 of one token's router logits (bf16 [E]); fills the
+    routing row [experts | weights] and the MoE meta [slots | weights] (fp32)."""
+    _need_cuda(logits)
+    _bf16(logits)
+    E = logits.numel()
+    if meta is None:
+        meta = torch.empty(2 * k, dtype=torch.float32, device=logits.device)
+    if slot_table is not None and (slot_table.dtype != torch.int32 or not slot_table.is_contiguous()):
+        raise WispError("slot_table must be contiguous int32")
+    _lib.call(
+        "wisp_router_topk", logits.data_ptr(), E, k, 1 if norm_topk else 0, _ptr(slot_table), int(base), _ptr(row),
+        meta.data_ptr(), _stream(logits),
+    )
+    return meta
+
+
+def embed(table, token, out=None):
+    """out = table[token] for an int64 device scalar ``token``."""
+    _need_cuda(table, token)
+    _bf16(table)
+    V, H = table.shape
+    if out is None:
+        out = torch.empty(H, dtype=torch.bfloat16, device=table.device)
+    _lib.call("wisp_embed", table.data_ptr(), V, H, token.data_ptr(), out.data_ptr(), _stream(table))
+    return out
+
+
+def argmax(x, workspace=None, out=None):
+    """Index of the largest bf16 value (ties: lowest index) as an int64 device scalar."""
+    _need_cuda(x)
+    _bf16(x)
+    if workspace is None:
+        workspace = torch.empty(_lib.ARGMAX_WORKSPACE, dtype=torch.int64, device=x.device)
+    if out is None:
+        out = torch.empty(1, dtype=torch.int64, device=x.device)
+    _lib.call("wisp_argmax", x.data_ptr(), x.numel(), workspace.data_ptr(), out.data_ptr(), _stream(x))
     return out
