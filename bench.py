@@ -1,17 +1,20 @@
 """Benchmark of the WiSP decode hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wisp|reference] [--bits 4]
+                    [--workload decoder|moe-stack] [--layers 48]
 
-Workload (``config.workload``): the bs=1 decode hot path of a Qwen3-30B-A3B-shaped model, 48 MoE layers
-(H=2048, I=768, 128 experts, top-8, group 128), all 6144 packed experts resident in HBM (15.4 GB at
-4 bit).  One step = one token through the 48 layers: RMSNorm with the residual add fused, then the
-fused dequant+GEMV MoE (gate/up + SwiGLU, down, weighted combine) over that layer's seeded top-8.
-Attention is not part of this workload; the metric is therefore reported as "moe decode tok/s".
-Synthetic seeded data (weights N(0, 0.02), router logits N(0,1)); the per-token working set (962 MB
-of expert bytes) is far larger than L2, so no flush is needed between steps.
+Workload ``decoder`` (default; BASELINE config 3 with every expert resident): greedy bs=1 decode of a
+Qwen3-30B-A3B-shaped random-init model (48 layers, hidden 2048, 32 query / 4 KV heads x 128, rotary
+base 1e6, RMSNorm eps 1e-6, vocab 151936, 128 experts top-8, intermediate 768, 4-bit g128 experts,
+bf16 attention and embeddings).  A 512-token seeded prompt is run first; one step = one generated
+token through the whole-token CUDA graph (embedding, 48 x [attention block, router, fused MoE], final
+norm, lm_head, argmax, position update).  The per-token working set (3.4 GB of weights) is far larger
+than L2, so no flush is needed between steps.  Workload ``moe-stack``: the 48 fused MoE layers alone
+with RMSNorm + residual between them (the MoE part of the same step).
 
 One JSON line is printed by rank 0.  ``--impl reference`` times the CPU restatement of the reference
-path (dequantize then fp32 matmul, the oracle) on the host cores on a bounded sample.
+path (oracle: dequantize then fp32 matmul, fp32 attention) on the host cores on a bounded sample.
+With N > 1 GPUs every rank runs an independent replica (bs=1 decode does not shard).
 """
 
 from __future__ import annotations
@@ -30,7 +33,8 @@ sys.path.insert(0, os.path.join(ROOT, "wisp-runtime_b200"))
 sys.path.insert(0, ROOT)
 
 H, I, E, K_TOP, L, G = 2048, 768, 128, 8, 48, 128
-N_ROUTES = 16  # distinct seeded routings (tokens) cycled through by the timed steps
+HQ, HK, D, VOCAB = 32, 4, 128, 151936
+N_ROUTES = 16  # moe-stack: distinct seeded routings (tokens) cycled through by the timed steps
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up + one down launch (4-bit, this shape),
 # from the ncu capture summarised in profiles/moe_decode_q4_qwen3_gate_up_down_full.md
 NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
@@ -39,22 +43,35 @@ NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
-    ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the model; fewer = a small ncu case)")
+    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack"])
+    ap.add_argument("--layers", type=int, default=48, help="layers (48 = the model; fewer = a small ncu case)")
+    ap.add_argument("--prompt", type=int, default=512)
     a = ap.parse_args()
     global L
     L = a.layers
     return a
 
 
-def metric_name():
-    return "moe decode tok/s"
+def metric_name(a):
+    return "decode tok/s" if a.workload == "decoder" else "moe decode tok/s"
 
 
 def workload_config(a, n):
+    if a.workload == "decoder":
+        return {
+            "workload": f"qwen3-30b-a3b greedy decode bs=1: {L} layers, 32q/4kv heads x 128, {E} experts top-{K_TOP}, "
+            f"{a.bits}-bit g{G} experts all resident, bf16 attention/embeddings, vocab {VOCAB}, "
+            f"{a.prompt}-token seeded prompt then one token per step (whole-token CUDA graph)",
+            "model": "Qwen3-30B-A3B-shaped (random init)",
+            "global_batch": n,
+            "seq_len": a.prompt,
+            "parallelism": "replicas" if n > 1 else "single",
+            "l2": "working set 3.4 GB/token >> 126 MB L2; no flush",
+        }
     return {
         "workload": f"qwen3-30b-a3b moe stack: {L} layers x {E} experts, top-{K_TOP}, bs=1, {a.bits}-bit g{G}, "
         "all experts resident, rmsnorm+residual between layers (no attention)",
@@ -146,10 +163,218 @@ class ClockSampler:
         }
 
 
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs"), "measured"
+    return 6650.0, "fallback"
+
+
 # ------------------------------------------------------------------------------------------------
-# workload construction (GPU)
+# the fused MoE call in isolation (roofline of the dominant kernel pair)
 # ------------------------------------------------------------------------------------------------
-def build_workload(bits, device, seed=0):
+def time_moe_kernel(pool, nbytes, bits, reps=20, variant=0):
+    """Average duration of one fused MoE decode call (gate/up + down kernels), rotated over L layers'
+    distinct experts (L*8 experts per sweep, 962 MB at 48 layers and 4 bits), CUDA events on the
+    launching stream around a graph of the sweep."""
+    import torch
+
+    from wisp import kernels
+
+    dev = pool.device
+    g = torch.Generator(device=dev).manual_seed(99)
+    x = torch.randn(L, H, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(L, H, dtype=torch.bfloat16, device=dev)
+    scratch = kernels.moe_scratch(K_TOP, I, dev)
+    metas = []
+    for l in range(L):
+        sel = torch.randperm(E, device=dev, generator=g)[:K_TOP] + l * E
+        metas.append(torch.cat([sel.float(), torch.full((K_TOP,), 1.0 / K_TOP, device=dev)]))
+
+    def sweep():
+        for l in range(L):
+            kernels.moe_decode_fast(pool, metas[l], x[l], K_TOP, H * I, H, I, bits, G, out=out[l], scratch=scratch, variant=variant)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        sweep()
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        sweep()
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        gr.replay()
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * L)
+    del gr
+    return ms
+
+
+def moe_roofline(pool, nbytes, bits):
+    per_call_ms = time_moe_kernel(pool, nbytes, bits)
+    v1_ms = time_moe_kernel(pool, nbytes, bits, variant=1)
+    alg = K_TOP * nbytes + 2 * H * 2
+    achieved = alg / (per_call_ms * 1e-3) / 1e9
+    peak, kind = load_peaks()
+    return {
+        "bound": "hbm",
+        "achieved": achieved,
+        "peak": peak,
+        "unit": "GB/s",
+        "frac": achieved / peak,
+        "traffic": NCU_TRAFFIC_PER_CALL if bits == 4 else None,
+        "kernel": "wisp_moe_decode (gate/up + down), one layer's 8 routed experts",
+        "bytes_per_call": alg,
+        "us_per_call": per_call_ms * 1e3,
+        "us_per_call_cuda_core_variant": v1_ms * 1e3,
+        "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback",
+    }, per_call_ms
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU legs (oracle): cpu_baseline on rank 0, and the --impl reference arm
+# ------------------------------------------------------------------------------------------------
+_CPU_WEIGHTS = {}
+
+
+def _cpu_weights(bits, attention, context):
+    """Seeded host copies of one layer's weights (built once per process)."""
+    import numpy as np
+
+    from oracle import wisp_oracle as O
+
+    key = (bits, attention, context)
+    if key not in _CPU_WEIGHTS:
+        rng = np.random.default_rng(1234)
+        n = H * I
+        wt = dict(pool=np.stack([O.quantize((rng.standard_normal((3, n)) * 0.02).astype(np.float32), bits, G) for _ in range(K_TOP)]))
+        if attention:
+            wt.update(
+                wqkv=(rng.standard_normal(((HQ + 2 * HK) * D, H)) * 0.02).astype(np.float32),
+                wo=(rng.standard_normal((H, HQ * D)) * 0.02).astype(np.float32),
+                wr=(rng.standard_normal((E, H)) * 0.02).astype(np.float32),
+                kc=rng.standard_normal((HK, context, D)).astype(np.float32),
+                vc=rng.standard_normal((HK, context, D)).astype(np.float32),
+            )
+        _CPU_WEIGHTS[key] = wt
+    return _CPU_WEIGHTS[key]
+
+
+def cpu_layer_sample(bits, seed=0, attention=False, context=512):
+    """One layer, one token, on the CPU with the oracle (dequantize -> fp32 matmul; experts in
+    parallel over the host cores): the fused MoE, plus (attention=True) RMSNorm, q/k/v/o projections,
+    GQA attention over ``context`` cached positions and the router.  Returns (seconds, threads)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import wisp_oracle as O
+
+    wt = _cpu_weights(bits, attention, context)
+    rng = np.random.default_rng(seed)
+    n = H * I
+    x = rng.standard_normal(H).astype(np.float32)
+    w = np.full(K_TOP, 1.0 / K_TOP, np.float32)
+    nw = np.ones(H, np.float32)
+    threads = os.cpu_count() or 1
+
+    def one(j):
+        gm, um, dm = O.expert_weights(wt["pool"], j, n, bits, G, H, I)
+        return w[j] * (dm @ (O.silu(gm @ x) * (um @ x)))
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        t0 = time.perf_counter()
+        if attention:
+            xn = O.rmsnorm(x, nw)
+            qkv = wt["wqkv"] @ xn
+            q = qkv[: HQ * D].reshape(HQ, D)
+            att = O.gqa_decode_attention(q, wt["kc"], wt["vc"], context - 1, D**-0.5)
+            hm = x + wt["wo"] @ att.reshape(-1)
+            O.router_topk((wt["wr"] @ O.rmsnorm(hm, nw))[None], K_TOP)
+        out = sum(ex.map(one, range(K_TOP)))
+        dt = time.perf_counter() - t0
+    assert np.isfinite(out).all()
+    return dt, threads
+
+
+def cpu_head_sample(seed=0, frac=16):
+    """lm_head GEMV (fp32) over 1/frac of the vocabulary rows; returns the extrapolated seconds."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    rows = VOCAB // frac
+    W = (rng.standard_normal((rows, H)) * 0.02).astype(np.float32)
+    x = rng.standard_normal(H).astype(np.float32)
+    W @ x
+    t0 = time.perf_counter()
+    y = W @ x
+    dt = time.perf_counter() - t0
+    assert np.isfinite(y).all()
+    return dt * frac
+
+
+def cpu_tok_s(a, seed=0):
+    """Tokens/s of the CPU path, extrapolated from one sampled layer (x L) and a sampled lm_head."""
+    if a.workload == "decoder":
+        dt, threads = cpu_layer_sample(a.bits, seed=seed, attention=True, context=a.prompt)
+        return 1.0 / (dt * L + cpu_head_sample(seed)), threads, (
+            f"1 decoder layer (RMSNorm, q/k/v/o projections, GQA attention over {a.prompt} positions, router, "
+            f"8 experts) + 1/16 of lm_head on the oracle, extrapolated x{L} layers and x16 rows"
+        )
+    dt, threads = cpu_layer_sample(a.bits, seed=seed)
+    return 1.0 / (dt * L), threads, f"1 MoE layer (8 experts, 1 token) on the oracle, extrapolated x{L} layers"
+
+
+CPU_SAMPLES = 5  # timed CPU samples per reference run (about a second each on 16 cores)
+
+
+def run_reference(a, rank):
+    """The reference arm: the CPU path on the host cores, one warm-up sample and up to CPU_SAMPLES
+    timed samples (each one sampled layer, extrapolated), so the run ends within a few minutes."""
+    if rank != 0:
+        return
+    vals = []
+    threads, sample = os.cpu_count() or 1, ""
+    nt = min(a.steps, CPU_SAMPLES)
+    for i in range(1 + nt):
+        v, threads, sample = cpu_tok_s(a, seed=i)
+        if i >= 1:
+            vals.append(v)
+    sample += f"; mean of {nt} timed samples after 1 warm-up"
+    tok_s = statistics.mean(vals)
+    line = {
+        "impl": "reference",
+        "metric": metric_name(a),
+        "value": tok_s,
+        "unit": "tok/s",
+        "n_gpus": a.gpus,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": 1e3 / tok_s,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": workload_config(a, 1),
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# moe-stack workload
+# ------------------------------------------------------------------------------------------------
+def build_moe_workload(bits, device, seed=0):
     import torch
 
     from wisp import quant
@@ -175,7 +400,7 @@ def build_workload(bits, device, seed=0):
 
 
 class MoEStack:
-    """One token through the 48-layer MoE stack, captured as one CUDA graph per routing."""
+    """One token through the MoE layers, captured as one CUDA graph per routing."""
 
     def __init__(self, W):
         import torch
@@ -199,7 +424,6 @@ class MoEStack:
         self.h.copy_(x0)
         self.moe.zero_()
         for l in range(L):
-            # h = h + moe_{l-1};  xn = rmsnorm(h)
             kernels.rmsnorm(self.h, W["norm_w"][l], 1e-6, delta=self.moe, sum_out=self.h, out=self.xn)
             kernels.moe_decode_fast(
                 W["pool"], meta[l], self.xn, K_TOP, W["n"], H, I, W["bits"], G, out=self.moe, scratch=self.scratch
@@ -233,131 +457,84 @@ class MoEStack:
     def step(self, t):
         self.graphs[t % N_ROUTES].replay()
 
-    def step_e2e(self, x_host, meta_host, out_host):
-        """Public-API step from host buffers: H2D of the token's input and routing, the captured
-        48-layer graph, D2H of the result."""
-        self.x_in.copy_(x_host, non_blocking=True)
-        self.meta_in.copy_(meta_host, non_blocking=True)
+    def e2e_inputs(self):
+        import torch
+
+        return (self.W["x0"].cpu().pin_memory(), self.W["meta"].cpu().pin_memory(),
+                torch.empty(H, dtype=torch.bfloat16).pin_memory())
+
+    def step_e2e(self, t, inp):
+        x_host, meta_host, out_host = inp
+        self.x_in.copy_(x_host[t % N_ROUTES], non_blocking=True)
+        self.meta_in.copy_(meta_host[t % N_ROUTES], non_blocking=True)
         self.graphs[N_ROUTES].replay()
         out_host.copy_(self.h, non_blocking=True)
 
+    def e2e_bytes(self):
+        return H * 2 + L * 2 * K_TOP * 4, H * 2
 
-def time_moe_kernel(W, reps=20, variant=0):
-    """Average duration of one fused MoE decode call (gate/up + down kernels), rotated over the 48
-    layers' distinct experts (962 MB per sweep), measured with CUDA events on the launching stream."""
-    import torch
-
-    from wisp import kernels
-
-    dev = W["pool"].device
-    x = torch.randn(L, H, device=dev).to(torch.bfloat16)
-    out = torch.empty(L, H, dtype=torch.bfloat16, device=dev)
-    scratch = kernels.moe_scratch(K_TOP, I, dev)
-
-    def sweep():
-        for l in range(L):
-            kernels.moe_decode_fast(
-                W["pool"], W["meta"][0, l], x[l], K_TOP, W["n"], H, I, W["bits"], G, out=out[l], scratch=scratch, variant=variant
-            )
-
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        sweep()
-    torch.cuda.current_stream().wait_stream(s)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        sweep()
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(reps):
-        g.replay()
-    e1.record(st)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / (reps * L)
-    del g
-    return ms
-
-
-def load_peaks():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
-        d = json.load(open(p))
-        return d.get("hbm_gbs"), "measured"
-    return 6650.0, "fallback"
+    def release(self):
+        self.graphs = []
 
 
 # ------------------------------------------------------------------------------------------------
-# CPU legs (oracle): cpu_baseline on rank 0, and the --impl reference arm
+# decoder workload
 # ------------------------------------------------------------------------------------------------
-def cpu_layer_sample(bits, seed=0):
-    """One MoE layer, one token, on the CPU with the oracle (dequantize -> fp32 matmul), experts in
-    parallel over the host cores.  Returns (seconds, threads)."""
-    import numpy as np
-    from concurrent.futures import ThreadPoolExecutor
+class DecodeBench:
+    """Greedy bs=1 decode through the whole-token graph (GraphDecoder.greedy_graph)."""
 
-    from oracle import wisp_oracle as O
+    def __init__(self, a, device, seed):
+        import torch
 
-    rng = np.random.default_rng(seed)
-    n = H * I
-    pool = np.stack([O.quantize((rng.standard_normal((3, n)) * 0.02).astype(np.float32), bits, G) for _ in range(K_TOP)])
-    x = rng.standard_normal(H).astype(np.float32)
-    w = np.full(K_TOP, 1.0 / K_TOP, np.float32)
-    threads = os.cpu_count() or 1
+        from wisp.graphdec import GraphDecoder
+        from wisp.model import DecoderConfig, DecoderWeights
 
-    def one(j):
-        gm, um, dm = O.expert_weights(pool, j, n, bits, G, H, I)
-        return w[j] * (dm @ (O.silu(gm @ x) * (um @ x)))
+        cfg = DecoderConfig(layers=L, bits=a.bits)
+        self.w = DecoderWeights.random(cfg, device=device, seed=seed)
+        need = a.prompt + 2 * (a.warmup + a.steps) + 16
+        self.dec = GraphDecoder(self.w, tmax=need)
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.prompt = torch.randint(0, cfg.vocab, (a.prompt,), device=device, generator=g)
+        self.dec.prefill(self.prompt)
+        self.tok = self.dec.logits.argmax().reshape(1)
+        self.dec.ctl[0:1].copy_(self.tok)
+        self.dec.ctl[1].fill_(self.dec.pos)
 
-    with ThreadPoolExecutor(max_workers=threads) as ex:
-        list(ex.map(one, range(K_TOP)))  # warm
-        t0 = time.perf_counter()
-        out = sum(ex.map(one, range(K_TOP)))
-        dt = time.perf_counter() - t0
-    assert np.isfinite(out).all()
-    return dt, threads
+    def launches_per_step(self):
+        return 1 + 9 * L + 1 + 2  # embed; per layer 3 GEMVs, norm/rope/cache, attention x2, top-k, MoE x2; lm_head; argmax x2
 
+    def step(self, t):
+        """One generated token: the step graph plus the on-device token/position update."""
+        self.dec.greedy_graph.replay()
 
-def run_reference(a, rank):
-    if rank != 0:
-        return
-    times = []
-    threads = os.cpu_count() or 1
-    for i in range(a.warmup + a.steps):
-        dt, threads = cpu_layer_sample(a.bits, seed=i)
-        if i >= a.warmup:
-            times.append(dt)
-    per_layer = statistics.mean(times)
-    tok_s = 1.0 / (per_layer * L)
-    line = {
-        "impl": "reference",
-        "metric": metric_name(),
-        "value": tok_s,
-        "unit": "tok/s",
-        "n_gpus": a.gpus,
-        "steps": a.steps,
-        "warmup": a.warmup,
-        "ms_per_step": per_layer * L * 1e3,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic",
-        "config": workload_config(a, 1),
-        "cpu_baseline": {
-            "value": tok_s,
-            "unit": "tok/s",
-            "cores": threads,
-            "kind": "port",
-            "sample": f"1 MoE layer (8 experts, 1 token) per step, extrapolated x{L} layers",
-        },
-        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    def e2e_inputs(self):
+        import torch
+
+        return torch.zeros(1, dtype=torch.int64).pin_memory(), torch.zeros(1, dtype=torch.int64).pin_memory()
+
+    def step_e2e(self, t, inp):
+        """Public-API step from host buffers: the token H2D, one decode step (which also advances the
+        position), the next token D2H."""
+        tok_host, out_host = inp
+        self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
+        self.dec.greedy_graph.replay()
+        out_host.copy_(self.dec.next_token, non_blocking=True)
+
+    def e2e_bytes(self):
+        return 8, 8
+
+    def pool(self):
+        return self.w.pool, self.w.nbytes
+
+    def release(self):
+        self.dec.graph = self.dec.greedy_graph = None
+
+    def bytes_per_token(self, ctx):
+        cfg = self.w.cfg
+        attn = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim * cfg.hidden * 2 + cfg.hidden * cfg.heads * cfg.head_dim * 2
+        router = cfg.experts * cfg.hidden * 2
+        kv = 2 * cfg.kv_heads * ctx * cfg.head_dim * 2
+        return L * (attn + router + K_TOP * self.w.nbytes + kv) + cfg.vocab * cfg.hidden * 2 + cfg.hidden * 2
 
 
 # ------------------------------------------------------------------------------------------------
@@ -378,11 +555,16 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
-    W = build_workload(a.bits, dev, seed=rank)
-    stack = MoEStack(W)
-    stack.capture()
+    if a.workload == "decoder":
+        bench = DecodeBench(a, dev, seed=rank)
+        pool, nbytes = bench.pool()
+    else:
+        W = build_moe_workload(a.bits, dev, seed=rank)
+        bench = MoEStack(W)
+        bench.capture()
+        pool, nbytes = W["pool"], W["nbytes"]
     for t in range(a.warmup):
-        stack.step(t)
+        bench.step(t)
     torch.cuda.synchronize()
 
     def barrier():
@@ -398,44 +580,41 @@ def main():
     w0 = time.perf_counter()
     e0.record(st)
     for t in range(a.steps):
-        stack.step(t)
+        bench.step(t)
     e1.record(st)
     barrier()
     clocks.window(w0, time.perf_counter())
     ms = e0.elapsed_time(e1)
     # e2e: host buffers, copies inside the timed region
-    x_host = W["x0"].cpu().pin_memory()
-    meta_host = W["meta"].cpu().pin_memory()
-    out_host = torch.empty(H, dtype=torch.bfloat16).pin_memory()
+    inp = bench.e2e_inputs()
     for t in range(3):
-        stack.step_e2e(x_host[t % N_ROUTES], meta_host[t % N_ROUTES], out_host)
+        bench.step_e2e(t, inp)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
     e2.record(st)
     for t in range(a.steps):
-        stack.step_e2e(x_host[t % N_ROUTES], meta_host[t % N_ROUTES], out_host)
+        bench.step_e2e(t, inp)
     e3.record(st)
     barrier()
     clocks.window(w0, time.perf_counter())
     ms_e2e = e2.elapsed_time(e3)
     clk = clocks.stop()
-    # roofline of the fused MoE decode (algorithmic bytes: 8 experts + x + out per call)
-    per_call_ms = time_moe_kernel(W)
-    v1_ms = time_moe_kernel(W, variant=1)
-    alg_bytes = K_TOP * W["nbytes"] + 2 * H * 2
-    achieved = alg_bytes / (per_call_ms * 1e-3) / 1e9
-    peak, peak_kind = load_peaks()
-    t = torch.tensor([ms, ms_e2e, per_call_ms], device=dev, dtype=torch.float64)
+    roof, _ = moe_roofline(pool, nbytes, a.bits)
+    if a.workload == "decoder":
+        ctx = bench.dec.pos + a.warmup + 2 * a.steps + 3  # context length at the end of the timed steps
+        roof["step_bytes_per_token"] = bench.bytes_per_token(ctx)
+        roof["step_achieved_gbs"] = bench.bytes_per_token(ctx) / (ms / a.steps * 1e-3) / 1e9
+    t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, per_call_ms = t.tolist()
+    ms, ms_e2e = t.tolist()
     if rank == 0:
-        cpu_s, cores = cpu_layer_sample(a.bits)
-        cpu_tok_s = 1.0 / (cpu_s * L)
+        cpu_v, cores, sample = cpu_tok_s(a)
         tok = a.steps * world
+        h2d, d2h = bench.e2e_bytes()
         line = {
-            "metric": metric_name(),
+            "metric": metric_name(a),
             "value": tok / (ms * 1e-3),
             "unit": "tok/s",
             "n_gpus": world,
@@ -445,42 +624,19 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": f"u{a.bits}->f32",
+            "dtype": f"u{a.bits}->f32 experts, bf16 dense",
             "data": "synthetic",
             "config": workload_config(a, world),
-            "e2e": {
-                "value": tok / (ms_e2e * 1e-3),
-                "unit": "tok/s",
-                "h2d_bytes_per_step": H * 2 + L * 2 * K_TOP * 4,
-                "d2h_bytes_per_step": H * 2,
-            },
-            "roofline": {
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "traffic": NCU_TRAFFIC_PER_CALL if a.bits == 4 else None,
-                "kernel": "wisp_moe_decode (gate/up + down)",
-                "bytes_per_call": alg_bytes,
-                "us_per_call": per_call_ms * 1e3,
-                "us_per_call_cuda_core_variant": v1_ms * 1e3,
-                "peak_source": peak_kind,
-            },
-            "cpu_baseline": {
-                "value": cpu_tok_s,
-                "unit": "tok/s",
-                "cores": cores,
-                "kind": "port",
-                "sample": f"1 MoE layer (8 experts, 1 token) on the oracle, extrapolated x{L} layers",
-            },
-            "gpu_launches": stack.launches_per_step() * a.steps,
+            "e2e": {"value": tok / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": roof,
+            "cpu_baseline": {"value": cpu_v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "gpu_launches": bench.launches_per_step() * a.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    bench.release()
     if world > 1:
         dist.barrier()
-        stack.graphs = []
         dist.destroy_process_group()
 
 
