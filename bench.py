@@ -501,7 +501,7 @@ class DecodeBench:
         self.dec.ctl[1].fill_(self.dec.pos)
 
     def launches_per_step(self):
-        return 1 + 9 * L + 1 + 2  # embed; per layer 3 GEMVs, norm/rope/cache, attention x2, top-k, MoE x2; lm_head; argmax x2
+        return self.dec.kernels_per_step()  # embed; per layer 3 GEMVs, attention, top-k, MoE x2; lm_head; argmax x2
 
     def step(self, t):
         """One generated token: the step graph plus the on-device token/position update."""

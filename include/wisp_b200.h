@@ -153,6 +153,16 @@ int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax);
 int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache, int64_t tmax,
                          const int64_t* pos, float scale, float* workspace, uint16_t* out, void* stream);
 
+/* Fused decode attention of one token: wisp_qk_norm_rope_kv and wisp_gqa_decode_attn in one launch.
+ * One cluster of 16 (or 8) CTAs per KV head splits positions 0..*pos; each CTA norms and rotates its
+ * query heads itself, the CTA holding *pos writes the new K/V row, scores and P.V run on the tensor
+ * cores, and the partial softmax states are merged through distributed shared memory (no
+ * workspace).  D == 128, Hq/Hk <= 8.
+ * Replaces wisp/graphdec.py:160-174 (q/k norms, rope_decode, cache writes, masked SDPA). */
+int wisp_attn_decode(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t* qn_w, const uint16_t* kn_w, float eps,
+                     const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos, int64_t tmax, uint16_t* k_cache,
+                     uint16_t* v_cache, float scale, uint16_t* out, void* stream);
+
 /* Router of one token: p = softmax(logits bf16 [E]) in fp32, the k largest (ties: lower expert id),
  * renormalised when norm_topk, rounded to bf16.  row (nullable) = fp32 [k experts | k weights];
  * meta = fp32 [k slots | k weights], slot = slot_table[base + e] when slot_table is given, else

@@ -193,3 +193,33 @@ def test_embed_and_argmax():
     assert int(kernels.argmax(x)) == 7
     x[3] = float("nan")
     assert int(kernels.argmax(x)) == 7
+
+
+@pytest.mark.parametrize("pos", [0, 1, 7, 127, 128, 700, 1031, 4095])
+@pytest.mark.parametrize("Hq,Hk", [(32, 4), (16, 4), (4, 4)])
+def test_fused_attention_matches_two_kernel_path(pos, Hq, Hk):
+    """One-launch norm/rotary/cache-write/attention (cluster + distributed shared memory merge) against
+    the two separate kernels and the oracle: the cache rows are bit-identical, the output within
+    tolerance."""
+    from wisp import kernels
+    from wisp.model import rotary_tables
+
+    D, tmax, eps = 128, 4096, 1e-6
+    g = _gen(pos + Hq)
+    qkv = torch.randn((Hq + 2 * Hk) * D, device="cuda", generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16)
+    cos, sin = rotary_tables(D, tmax, 1e6, "cuda")
+    kc = torch.randn(Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    kc2, vc2 = kc.clone(), vc.clone()
+    p = torch.tensor([pos], dtype=torch.int64, device="cuda")
+    out = kernels.attn_decode(qkv, Hq, Hk, D, qn, kn, eps, cos, sin, p, kc, vc, D**-0.5)
+    q = kernels.qk_norm_rope_kv(qkv, Hq, Hk, D, qn, kn, eps, cos, sin, p, kc2, vc2)
+    ref = kernels.gqa_decode_attn(q, Hq, Hk, D, kc2, vc2, p, D**-0.5)
+    torch.cuda.synchronize()
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    want = O.gqa_decode_attention(_np(q).reshape(Hq, D), _np(kc2), _np(vc2), pos, D**-0.5)
+    got = _np(out).reshape(Hq, D)
+    assert np.abs(got - want).max() <= 1e-2 * max(1.0, np.abs(want).max())
+    assert np.abs(got - _np(ref).reshape(Hq, D)).max() <= 1e-2 * max(1.0, np.abs(want).max())

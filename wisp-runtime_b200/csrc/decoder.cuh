@@ -193,6 +193,270 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int Hq, int 
   }
 }
 
+// ---- fused decode attention: one cluster of CTAs per KV head --------------------------------------
+// Per-head RMSNorm + rotary of the G query heads and of the new key (the arithmetic of
+// qk_norm_rope_kv_kernel), the new K/V row written into the cache at *pos, then attention over
+// positions [0, *pos]: CTA r of the cluster takes the r-th slice of the positions and streams it
+// through shared memory in chunks of FCHUNK.  Scores and P.V run on the tensor cores (mma.sync
+// m16n8k16 bf16, fp32 accumulation; the G query heads are rows 0..G-1 of the 16-row A tile), softmax
+// is online in fp32 on log2-scaled scores, and the per-CTA partial states are merged through
+// distributed shared memory: CTA r finishes one (head, half of D) piece of the output.
+constexpr int FCHUNK = 128;              // positions per shared-memory chunk
+constexpr int FWARPS = 8;
+constexpr int FTHREADS = FWARPS * 32;
+constexpr int FD = 128;                  // head_dim of this kernel
+constexpr int KP = FD + 8;               // padded row (bf16): fragment loads are conflict-free
+constexpr int PP = FCHUNK + 8;           // padded P row (bf16)
+constexpr int MAX_SPLIT = 16;
+
+struct AttnSmem {
+  uint16_t q[MAX_G][KP];       // normed, rotated query heads (bf16)
+  uint16_t k[FCHUNK][KP];
+  uint16_t v[FCHUNK][KP];
+  uint16_t p[16][PP];          // probabilities (bf16), rows >= G stay zero
+  float s[MAX_G][FCHUNK];      // log2-scaled scores of the chunk
+  float o[MAX_G][FD];          // this CTA's unnormalised output
+  uint16_t knew[FD], vnew[FD];
+  float m[MAX_G], l[MAX_G], alpha[MAX_G];
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+// one warp, one head of FD values (4 per lane): bf16(w * bf16(x * rsqrt(mean(x^2) + eps))), then
+// rotate-half rotary (fp32, one rounding) -> 4 bf16 packed in two words; every load issued first
+__device__ __forceinline__ uint2 norm_rope_head(const uint16_t* __restrict__ src, const uint16_t* __restrict__ w, float eps,
+                                                const uint16_t* __restrict__ cs, const uint16_t* __restrict__ sn, int lane) {
+  const uint2 xv = reinterpret_cast<const uint2*>(src)[lane];
+  const uint2 wv = reinterpret_cast<const uint2*>(w)[lane];
+  const uint2 cv = reinterpret_cast<const uint2*>(cs)[lane];
+  const uint2 sv = reinterpret_cast<const uint2*>(sn)[lane];
+  float x[4] = {__uint_as_float(xv.x << 16), __uint_as_float(xv.x & 0xFFFF0000u), __uint_as_float(xv.y << 16),
+                __uint_as_float(xv.y & 0xFFFF0000u)};
+  const float wf[4] = {__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xFFFF0000u), __uint_as_float(wv.y << 16),
+                       __uint_as_float(wv.y & 0xFFFF0000u)};
+  const float c[4] = {__uint_as_float(cv.x << 16), __uint_as_float(cv.x & 0xFFFF0000u), __uint_as_float(cv.y << 16),
+                      __uint_as_float(cv.y & 0xFFFF0000u)};
+  const float sn4[4] = {__uint_as_float(sv.x << 16), __uint_as_float(sv.x & 0xFFFF0000u), __uint_as_float(sv.y << 16),
+                        __uint_as_float(sv.y & 0xFFFF0000u)};
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / float(FD) + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = bf16_to_f32(f32_to_bf16(wf[i] * bf16_to_f32(f32_to_bf16(x[i] * inv))));
+  // partner of element 4*lane + i is 4*(lane ^ 16) + i (D / 2 = 64 elements = 16 lanes away)
+  uint32_t o[2];
+#pragma unroll
+  for (int i = 0; i < 4; i += 2) {
+    const float p0 = __shfl_xor_sync(0xffffffffu, x[i], 16), p1 = __shfl_xor_sync(0xffffffffu, x[i + 1], 16);
+    const float xp0 = lane < 16 ? -p0 : p0, xp1 = lane < 16 ? -p1 : p1;
+    const float r0 = __fadd_rn(__fmul_rn(x[i], c[i]), __fmul_rn(xp0, sn4[i]));
+    const float r1 = __fadd_rn(__fmul_rn(x[i + 1], c[i + 1]), __fmul_rn(xp1, sn4[i + 1]));
+    o[i / 2] = uint32_t(f32_to_bf16(r0)) | (uint32_t(f32_to_bf16(r1)) << 16);
+  }
+  return make_uint2(o[0], o[1]);
+}
+
+__global__ void __launch_bounds__(FTHREADS)
+    attn_fused_kernel(const uint16_t* __restrict__ qkv, int Hq, int Hk, const uint16_t* __restrict__ qn_w,
+                      const uint16_t* __restrict__ kn_w, float eps, const uint16_t* __restrict__ cos_t,
+                      const uint16_t* __restrict__ sin_t, const int64_t* __restrict__ pos_ptr, int64_t tmax,
+                      uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, float scale, uint16_t* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t smraw[];
+  AttnSmem& S = *reinterpret_cast<AttnSmem*>(smraw);
+  const int h = blockIdx.y;
+  const int G = Hq / Hk;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int rank = int(cluster_rank()), nsplit = int(cluster_size());
+  // zero the padding rows of P and the per-head state while the previous kernel finishes
+  for (int i = tid; i < 16 * PP / 2; i += FTHREADS) reinterpret_cast<uint32_t*>(&S.p[0][0])[i] = 0u;
+  for (int i = tid; i < MAX_G * FD; i += FTHREADS) (&S.o[0][0])[i] = 0.0f;
+  if (tid < MAX_G) {
+    S.m[tid] = -INFINITY;
+    S.l[tid] = 0.0f;
+  }
+  pdl_wait();  // qkv comes from the projection GEMV
+  pdl_launch_dependents();
+  const int64_t pos = *pos_ptr;
+  const bool pos_ok = pos >= 0 && pos < tmax;
+  if (!pos_ok && rank == 0 && h == 0 && tid == 0) flag(WISP_STATUS_BAD_POS);
+  const int64_t n_all = pos_ok ? pos + 1 : 0;
+  const int64_t per = (n_all + nsplit - 1) / nsplit;
+  const int64_t t0 = rank * per, t1 = (t0 + per) < n_all ? (t0 + per) : n_all;
+  const uint16_t* cs = cos_t + (pos_ok ? pos : 0) * FD;
+  const uint16_t* sn = sin_t + (pos_ok ? pos : 0) * FD;
+  const bool mine = pos_ok && pos >= t0 && pos < t1;  // this CTA holds the new position
+
+  // ---- query heads (warp j: head j), the new key and value --------------------------------------
+  if (warp < G) reinterpret_cast<uint2*>(S.q[warp])[lane] = norm_rope_head(qkv + int64_t(h * G + warp) * FD, qn_w, eps, cs, sn, lane);
+  if (mine && warp == FWARPS - 1) {
+    const uint2 kn = norm_rope_head(qkv + int64_t(Hq + h) * FD, kn_w, eps, cs, sn, lane);
+    const uint2 vv = reinterpret_cast<const uint2*>(qkv + int64_t(Hq + Hk + h) * FD)[lane];
+    reinterpret_cast<uint2*>(S.knew)[lane] = kn;
+    reinterpret_cast<uint2*>(S.vnew)[lane] = vv;
+    reinterpret_cast<uint2*>(kc + (int64_t(h) * tmax + pos) * FD)[lane] = kn;
+    reinterpret_cast<uint2*>(vc + (int64_t(h) * tmax + pos) * FD)[lane] = vv;
+  }
+  __syncthreads();
+  // A fragments of the query tile (rows g < G real, rows g + 8 zero), all 8 k-steps
+  uint32_t qa[FD / 16][2];
+#pragma unroll
+  for (int j = 0; j < FD / 16; ++j) {
+    qa[j][0] = g < G ? *reinterpret_cast<const uint32_t*>(&S.q[g][16 * j + 2 * c]) : 0u;
+    qa[j][1] = g < G ? *reinterpret_cast<const uint32_t*>(&S.q[g][16 * j + 8 + 2 * c]) : 0u;
+  }
+  const float qscale = scale * 1.4426950408889634f;  // scores in log2 units
+  float oacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // this warp's d n-tiles 2w, 2w+1
+
+  const uint16_t* kb = kc + int64_t(h) * tmax * FD;
+  const uint16_t* vb = vc + int64_t(h) * tmax * FD;
+  for (int64_t c0 = t0; c0 < t1; c0 += FCHUNK) {
+    const int n = int((t1 - c0) < FCHUNK ? (t1 - c0) : FCHUNK);
+    // K and V rows [c0, c0 + n) into padded rows; rows past n are zero (P is zero there too)
+    for (int i = tid; i < FCHUNK * (FD / 8); i += FTHREADS) {
+      const int r = i / (FD / 8), cpart = i % (FD / 8);
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (r < n) {
+        kv = reinterpret_cast<const uint4*>(kb + (c0 + r) * FD)[cpart];
+        vv = reinterpret_cast<const uint4*>(vb + (c0 + r) * FD)[cpart];
+      }
+      reinterpret_cast<uint4*>(&S.k[r][0])[cpart] = kv;
+      reinterpret_cast<uint4*>(&S.v[r][0])[cpart] = vv;
+    }
+    __syncthreads();
+    if (mine && pos >= c0 && pos < c0 + n) {  // the cache row of pos may not be visible yet: patch it
+      const int r = int(pos - c0);
+      if (tid < FD / 2) {
+        reinterpret_cast<uint32_t*>(&S.k[r][0])[tid] = reinterpret_cast<const uint32_t*>(S.knew)[tid];
+        reinterpret_cast<uint32_t*>(&S.v[r][0])[tid] = reinterpret_cast<const uint32_t*>(S.vnew)[tid];
+      }
+      __syncthreads();
+    }
+    // scores: warp w takes positions 16w .. 16w + 15 (two n-tiles of 8)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int t = 16 * warp + 8 * nt;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < FD / 16; ++j) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&S.k[t + g][16 * j + 2 * c]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&S.k[t + g][16 * j + 8 + 2 * c]);
+        mma_bf16(d, qa[j][0], 0u, qa[j][1], 0u, b0, b1);
+      }
+      if (g < G) {
+        const int p0 = t + 2 * c;
+        S.s[g][p0] = p0 < n ? d[0] * qscale : -INFINITY;
+        S.s[g][p0 + 1] = p0 + 1 < n ? d[1] * qscale : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // online softmax: warp w -> head w
+    if (warp < G) {
+      float v4[FCHUNK / 32], mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < FCHUNK / 32; ++i) {
+        v4[i] = S.s[warp][lane + 32 * i];
+        mx = fmaxf(mx, v4[i]);
+      }
+      mx = warp_max(mx);
+      const float m_old = S.m[warp], m_new = fmaxf(m_old, mx);
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < FCHUNK / 32; ++i) {
+        const float e = exp2f(v4[i] - m_new);
+        sum += e;
+        S.p[warp][lane + 32 * i] = f32_to_bf16(e);
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        const float al = exp2f(m_old - m_new);
+        S.alpha[warp] = al;
+        S.l[warp] = S.l[warp] * al + sum;
+        S.m[warp] = m_new;
+      }
+    }
+    __syncthreads();
+    // P V: warp w owns output columns 16w .. 16w + 15 (two n-tiles), all positions of the chunk
+    {
+      const float al = g < G ? S.alpha[g] : 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        oacc[nt][0] *= al;
+        oacc[nt][1] *= al;
+      }
+      const int mi = lane >> 3, ri = lane & 7;  // ldmatrix: matrix mi, row ri
+#pragma unroll 4
+      for (int j = 0; j < FCHUNK / 16; ++j) {
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.p[g][16 * j + 2 * c]);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.p[g][16 * j + 8 + 2 * c]);
+        uint32_t bv[4];
+        ldsm_x4_trans(bv, &S.v[16 * j + (mi & 1) * 8 + ri][16 * warp + (mi >> 1) * 8]);
+        mma_bf16(oacc[0], a0, 0u, a2, 0u, bv[0], bv[1]);
+        mma_bf16(oacc[1], a0, 0u, a2, 0u, bv[2], bv[3]);
+      }
+    }
+    __syncthreads();
+  }
+  if (g < G) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      S.o[g][16 * warp + 8 * nt + 2 * c] = oacc[nt][0];
+      S.o[g][16 * warp + 8 * nt + 2 * c + 1] = oacc[nt][1];
+    }
+  }
+
+  // ---- merge the partials through distributed shared memory ---------------------------------------
+  cluster_sync_all();
+  const int pieces = G * 2;  // (head, half of D)
+  for (int pc = rank; pos_ok && pc < pieces; pc += nsplit) {
+    const int hg = pc >> 1, d0 = (pc & 1) * (FD / 2);
+    float M = -INFINITY;
+    for (int r = 0; r < nsplit; ++r) {
+      const AttnSmem* R = static_cast<const AttnSmem*>(__cluster_map_shared_rank(static_cast<void*>(&S), r));
+      M = fmaxf(M, R->m[hg]);
+    }
+    float Ls = 0.0f;
+    for (int r = 0; r < nsplit; ++r) {
+      const AttnSmem* R = static_cast<const AttnSmem*>(__cluster_map_shared_rank(static_cast<void*>(&S), r));
+      Ls += R->l[hg] * exp2f(R->m[hg] - M);
+    }
+    for (int d = d0 + tid; d < d0 + FD / 2; d += FTHREADS) {
+      float o = 0.0f;
+      for (int r = 0; r < nsplit; ++r) {
+        const AttnSmem* R = static_cast<const AttnSmem*>(__cluster_map_shared_rank(static_cast<void*>(&S), r));
+        o += R->o[hg][d] * exp2f(R->m[hg] - M);
+      }
+      out[int64_t(h * G + hg) * FD + d] = f32_to_bf16(o / Ls);
+    }
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its shared memory
+}
+
 // ---- router ------------------------------------------------------------------------------------
 // One warp.  logits bf16 [E] -> p = softmax(fp32) -> top-k (ties: lower expert id first) -> p / sum
 // -> bf16.  row (nullable) = [experts as float..., weights...]; meta = [slots..., weights...] with

@@ -431,6 +431,52 @@ int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_
   return check_launch("gqa_decode_attn");
 }
 
+int wisp_attn_decode(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t* qn_w, const uint16_t* kn_w, float eps,
+                     const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos, int64_t tmax, uint16_t* k_cache,
+                     uint16_t* v_cache, float scale, uint16_t* out, void* stream) {
+  WISP_REQUIRE(qkv && qn_w && kn_w && cos_t && sin_t && pos && k_cache && v_cache && out, "wisp_attn_decode: NULL pointer");
+  WISP_REQUIRE(D == dec::FD, "wisp_attn_decode: head_dim must be %d (got %d)", dec::FD, D);
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && Hq % Hk == 0 && Hq / Hk <= dec::MAX_G && tmax > 0,
+               "wisp_attn_decode: need Hq a multiple of Hk with Hq/Hk <= %d", dec::MAX_G);
+  WISP_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16), "wisp_attn_decode: caches must be 16-byte aligned");
+  const size_t smem = sizeof(dec::AttnSmem);
+  cudaFuncSetAttribute(dec::attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  cudaFuncSetAttribute(dec::attn_fused_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  auto config = [&](int split, cudaLaunchAttribute (&attr)[2]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(split, Hk);
+    cfg.blockDim = dim3(dec::FTHREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = split;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cfg;
+  };
+  // 16 CTAs per KV head where the GPU can co-schedule such clusters, else the portable 8 (decided once)
+  static int split = 0;
+  if (split == 0) {
+    split = 8;
+    cudaLaunchAttribute attr[2];
+    const cudaLaunchConfig_t cfg = config(dec::MAX_SPLIT, attr);
+    int nclusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&nclusters, dec::attn_fused_kernel, &cfg) == cudaSuccess && nclusters >= 1)
+      split = dec::MAX_SPLIT;
+    cudaGetLastError();
+  }
+  cudaLaunchAttribute attr[2];
+  const cudaLaunchConfig_t cfg = config(split, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, dec::attn_fused_kernel, qkv, Hq, Hk, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax,
+                                           k_cache, v_cache, scale, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_attn_decode: %s", cudaGetErrorString(e));
+  return check_launch("attn_decode");
+}
+
 int wisp_router_topk(const uint16_t* logits, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* row,
                      float* meta, void* stream) {
   WISP_REQUIRE(logits && meta, "wisp_router_topk: NULL pointer");

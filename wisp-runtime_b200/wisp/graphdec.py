@@ -71,13 +71,19 @@ class GraphDecoder:
             lw["wqkv"], self.h_emb if first else self.h_mid, x_add=None if first else self.moe,
             x_sum_out=None if first else self.h_res, norm_w=lw["in_norm"], eps=c.eps, out=self.qkv,
         )
-        kernels.qk_norm_rope_kv(
-            self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos,
-            self.kc[l], self.vc[l], q_out=self.q,
-        )
-        kernels.gqa_decode_attn(
-            self.q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], pos, self.scale, workspace=self.attn_ws, out=self.att
-        )
+        if self.D == 128 and self.Hq // self.Hk <= 8:  # one cluster launch: norms, rotary, cache write, attention
+            kernels.attn_decode(
+                self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos,
+                self.kc[l], self.vc[l], self.scale, out=self.att,
+            )
+        else:
+            kernels.qk_norm_rope_kv(
+                self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos,
+                self.kc[l], self.vc[l], q_out=self.q,
+            )
+            kernels.gqa_decode_attn(
+                self.q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], pos, self.scale, workspace=self.attn_ws, out=self.att
+            )
         # o projection + residual, then post-attention RMSNorm + router
         kernels.gemv(lw["wo"], self.att, res=self.h_emb if first else self.h_res, out=self.h_mid)
         kernels.gemv(lw["router"], self.h_mid, norm_w=lw["post_norm"], eps=c.eps, xn_out=self.xn, out=self.rlog)
@@ -88,6 +94,11 @@ class GraphDecoder:
             w.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
             scratch=self.scratch,
         )
+
+    def kernels_per_step(self):
+        """Kernels launched by one decode step (what the graph replays, torch copies excluded)."""
+        attn = 1 if (self.D == 128 and self.Hq // self.Hk <= 8) else 3
+        return 1 + self.L * (attn + 6) + 3
 
     def _step(self):
         kernels.embed(self.w.embed, self.ctl[0:1], out=self.h_emb)

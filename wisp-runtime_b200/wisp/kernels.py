@@ -31,6 +31,7 @@ __all__ = [
     "gemv",
     "qk_norm_rope_kv",
     "gqa_decode_attn",
+    "attn_decode",
     "router_topk",
     "embed",
     "argmax",
@@ -270,6 +271,21 @@ def gqa_decode_attn(q, Hq, Hk, D, k_cache, v_cache, pos, scale, workspace=None, 
     _lib.call(
         "wisp_gqa_decode_attn", q.data_ptr(), Hq, Hk, D, k_cache.data_ptr(), v_cache.data_ptr(), tmax, pos.data_ptr(),
         float(scale), workspace.data_ptr(), out.data_ptr(), _stream(q),
+    )
+    return out
+
+
+def attn_decode(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, k_cache, v_cache, scale, out=None):
+    """qk_norm_rope_kv + gqa_decode_attn in one cluster launch (D = 128): returns attention out [Hq*D]."""
+    _need_cuda(qkv, pos)
+    _bf16(qkv, qn_w, kn_w, cos_t, sin_t, k_cache, v_cache)
+    if out is None:
+        out = torch.empty(Hq * D, dtype=torch.bfloat16, device=qkv.device)
+    tmax = k_cache.shape[-2]
+    _lib.call(
+        "wisp_attn_decode", qkv.data_ptr(), Hq, Hk, D, qn_w.data_ptr(), kn_w.data_ptr(), float(eps), cos_t.data_ptr(),
+        sin_t.data_ptr(), pos.data_ptr(), tmax, k_cache.data_ptr(), v_cache.data_ptr(), float(scale), out.data_ptr(),
+        _stream(qkv),
     )
     return out
 
