@@ -95,6 +95,16 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,
                             uint16_t* out, int variant, void* stream);
 
+/* wisp_moe_decode with the router's top-k folded into the MoE kernels: every CTA computes the
+ * routing from the router logits (bf16 [E], E <= 512) itself -- softmax in fp32, the k largest (ties:
+ * lower expert id), renormalised when norm_topk, bf16 weights; slot of expert e = slot_table[base + e]
+ * when slot_table is given (a negative entry is skipped and flagged), else base + e.  row (nullable)
+ * receives [k experts | k weights] as fp32.  Tensor-core shapes only (WISP_ERR_UNSUPPORTED otherwise).
+ * Replaces wisp/graphdec.py:177-182 + :194-203 (router softmax/top-k, then moe_decode_q*_fast). */
+int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, const uint16_t* logits, int E, int k,
+                           int norm_topk, const int32_t* slot_table, int64_t base, float* row, const uint16_t* x, int64_t H,
+                           int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream);
+
 /* Allocation-free twin of wisp_moe_decode for callers that cannot allocate device memory (a host
  * stack that owns no allocator, e.g. a CUDA-graph node builder or an embedding runtime that hands over
  * only the pool, x and out): the fp32 intermediate a = silu(g)*u lives in a file-scope device array

@@ -195,3 +195,53 @@ def test_short_scratch_rejected():
     meta = torch.cat([slots.float(), wts])
     with pytest.raises(WispError, match="scratch"):
         kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, scratch=torch.zeros(k * I - 1, device="cuda"))
+
+
+@pytest.mark.parametrize("bits", [4, 3, 2])
+@pytest.mark.parametrize("E,k", [(128, 8), (32, 4)])
+def test_routed_matches_router_then_moe(bits, E, k):
+    """Top-k inside the MoE kernels (from the router logits) against the separate router kernel
+    followed by the meta-driven MoE: same experts, same weights, same output within tolerance."""
+    from wisp import kernels
+
+    H, I = 2048, 768
+    n = H * I
+    pool, x, _, _ = _setup(bits, H, I, E, k, seed=60 + bits + E)
+    g = torch.Generator(device="cuda").manual_seed(bits * E)
+    for trial in range(3):
+        logits = (torch.randn(E, device="cuda", generator=g) * 2).to(torch.bfloat16)
+        row = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        got = kernels.moe_decode_routed(pool, logits, x, k, n, H, I, bits, row=row)
+        row2 = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        meta = kernels.router_topk(logits, k, True, row=row2)
+        want = kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits)
+        assert torch.equal(row[:k], row2[:k]), (row, row2)
+        assert (row[k:] - row2[k:]).abs().max().item() <= 2.0**-8
+        ref = _bf16_np(want)
+        assert _rel(_bf16_np(got), ref) < TOL
+        sel, rw = O.router_topk(O.bf16_bits_to_f32(logits.view(torch.int16).cpu().numpy().view(np.uint16))[None], k)
+        assert np.array_equal(np.sort(row[:k].long().cpu().numpy()), np.sort(sel[0]))
+
+
+def test_routed_slot_table_and_missing_slot():
+    from wisp import _lib, kernels
+
+    H, I, E, k, bits = 2048, 768, 16, 2, 4
+    n = H * I
+    pool, x, _, _ = _setup(bits, H, I, E, k, seed=77)
+    logits = torch.zeros(E, dtype=torch.bfloat16, device="cuda")
+    logits[5], logits[11] = 3.0, 2.0
+    table = torch.arange(E, dtype=torch.int32, device="cuda").flip(0).contiguous()  # expert e in slot E-1-e
+    _lib.device_status(0, clear=True)
+    got = kernels.moe_decode_routed(pool, logits, x, k, n, H, I, bits, slot_table=table)
+    meta = torch.tensor([E - 1 - 5.0, E - 1 - 11.0], device="cuda")
+    w = kernels.router_topk(logits, k, True)[k:]
+    want = kernels.moe_decode_fast(pool, torch.cat([meta, w]), x, k, n, H, I, bits)
+    assert _rel(_bf16_np(got), _bf16_np(want)) < TOL
+    assert _lib.device_status(0) == 0
+    table[11] = -1  # expert 11 not resident: skipped and flagged
+    got = kernels.moe_decode_routed(pool, logits, x, k, n, H, I, bits, slot_table=table)
+    assert _lib.device_status(0) & _lib.STATUS_BAD_SLOT
+    only = kernels.moe_decode_fast(pool, torch.cat([meta[:1], torch.tensor([-1.0], device="cuda"), w]), x, k, n, H, I, bits)
+    _lib.device_status(0, clear=True)
+    assert _rel(_bf16_np(got), _bf16_np(only)) < TOL

@@ -21,7 +21,7 @@ namespace dense {
 
 constexpr int CONSUMERS = 8;
 constexpr int THREADS = 32 * (CONSUMERS + 1);  // warp 0 produces, warps 1..8 consume
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;  // 96 KB ring: a GEMV CTA fits beside the previous kernel's CTA (PDL prefetch)
 constexpr int STAGE_BYTES = 32 * 1024;
 
 struct GemvArgs {
@@ -62,8 +62,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// KCH = 16-byte chunks of x held per lane (K <= 256 * KCH)
-template <int KCH>
 __global__ void __launch_bounds__(THREADS, 1) gemv_kernel(GemvArgs A) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -154,16 +152,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemv_kernel(GemvArgs A) {
     for (int64_t c = ct; c < nch; c += 32 * CONSUMERS) reinterpret_cast<uint4*>(A.xn_out)[c] = reinterpret_cast<const uint4*>(xs)[c];
   }
   named_sync(2, 32 * CONSUMERS);
-  // this lane's chunks of x: c = lane + 32 i
-  uint4 xr[KCH];
-#pragma unroll
-  for (int i = 0; i < KCH; ++i) {
-    const int64_t c = lane + 32 * i;
-    xr[i] = c < nch ? reinterpret_cast<const uint4*>(xs)[c] : make_uint4(0, 0, 0, 0);
-  }
 
-  // ---- rows: consumer warp w takes rows w, w + 8, ... of every stage ---------------------------
+  // ---- rows: consumer warp w takes rows w, w + 8, ... of every stage; x read from shared memory ---
   const int cw = warp - 1;
+  const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
   for (int s = 0; s < nstages; ++s) {
     const int slot = s % STAGES;
     if (!mbar_wait(&full[slot], uint32_t((s / STAGES) & 1))) break;
@@ -173,18 +165,15 @@ __global__ void __launch_bounds__(THREADS, 1) gemv_kernel(GemvArgs A) {
     for (int r = cw; r < nr; r += CONSUMERS) {
       const uint4* wrow = reinterpret_cast<const uint4*>(stage + int64_t(r) * row_bytes);
       float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 4
+      for (int64_t c = lane; c < nch; c += 32) {
+        const uint4 w = wrow[c], xv4 = xs4[c];
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+        const uint32_t xv[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
 #pragma unroll
-      for (int i = 0; i < KCH; ++i) {
-        const int64_t c = lane + 32 * i;
-        if (c < nch) {
-          const uint4 w = wrow[c];
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-          const uint32_t xv[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            acc0 = fmaf(bf_lo(wv[q]), bf_lo(xv[q]), acc0);
-            acc1 = fmaf(bf_hi(wv[q]), bf_hi(xv[q]), acc1);
-          }
+        for (int q = 0; q < 4; ++q) {
+          acc0 = fmaf(bf_lo(wv[q]), bf_lo(xv[q]), acc0);
+          acc1 = fmaf(bf_hi(wv[q]), bf_hi(xv[q]), acc1);
         }
       }
       const float acc = warp_sum(acc0 + acc1);

@@ -18,6 +18,70 @@ struct MoeShape {
   int64_t mat_bytes;  // code bytes per matrix
 };
 
+// Routing computed inside the MoE kernels from the router logits (instead of a meta buffer written
+// by a separate top-k launch): softmax in fp32, the k largest (ties: lower expert id), renormalised
+// when norm_topk, rounded to bf16 (wisp/graphdec.py:177-182, wisp/moe.py:67-72).
+struct MoeRoute {
+  const uint16_t* logits;     // bf16 [E]; NULL: the kernels read the meta buffer instead
+  int E, norm_topk;
+  const int32_t* slot_table;  // NULL: slot = base + e
+  int64_t base;
+  float* row_out;             // nullable: [k experts | k weights], written by CTA 0 of the gate/up grid
+};
+
+// All threads of the CTA (blockDim.x >= E, k <= 32): meta[0..2k) in shared memory = [slots | weights];
+// red: blockDim.x / 32 floats, xs: E + 64 floats of scratch.  LDCG: read the logits through L2 (the
+// caller may run before its griddepcontrol.wait, after the producer of the logits has completed).
+template <bool LDCG>
+__device__ void route_from_logits(const MoeRoute& R, int k, float* meta, float* red, float* xs) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+  float x = -INFINITY;
+  if (t < R.E) {
+    const uint16_t b = LDCG ? __ldcg(reinterpret_cast<const unsigned short*>(R.logits) + t) : R.logits[t];
+    x = bf16_to_f32(b);
+    xs[t] = x;
+  }
+  float m = warp_max(x);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+  for (int w = 1; w < nw; ++w) m = fmaxf(m, red[w]);
+  const float e = t < R.E ? expf(x - m) : 0.0f;
+  __syncthreads();
+  float s = warp_sum(e);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  s = 0.0f;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  // rank of this expert: experts with a larger logit, or an equal one and a lower id, come first
+  int rank = 0;
+  if (t < R.E)
+    for (int u = 0; u < R.E; ++u) {
+      const float y = xs[u];
+      rank += (y > x || (y == x && u < t)) ? 1 : 0;
+    }
+  __syncthreads();
+  const float p = e / s;
+  if (t < R.E && rank < k) {
+    meta[rank] = float(R.slot_table ? int64_t(R.slot_table[R.base + t]) : R.base + t);
+    xs[R.E + rank] = float(t);
+    xs[R.E + 32 + rank] = p;
+  }
+  __syncthreads();
+  if (t < k) {
+    float tot = 0.0f;
+    for (int j = 0; j < k; ++j) tot += xs[R.E + 32 + j];  // fixed order: the same sum in every CTA
+    const float pt = xs[R.E + 32 + t];
+    const float w = bf16_to_f32(f32_to_bf16(R.norm_topk ? pt / tot : pt));
+    meta[k + t] = w;
+    if (R.row_out && blockIdx.x == 0) {
+      R.row_out[t] = xs[R.E + t];
+      R.row_out[k + t] = w;
+    }
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ bool route_slot(const float* meta, int j, const MoeShape& S, int64_t& slot) {
   const float f = meta[j];
   if (!(f >= 0.0f) || f >= float(S.nslots)) return false;

@@ -51,11 +51,14 @@ __device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) 
 // ------------------------------------------------------------------------------------------------
 // shared-memory layouts (host and device share these formulas)
 // ------------------------------------------------------------------------------------------------
+// routing scratch (MoeRoute): meta [64] + reduction [32] + logits/ids/probabilities [512 + 64] floats
+constexpr int ROUTE_BYTES = (64 + 32 + 512 + 64) * 4;
+
 struct GuL {
   int groups, gph, gpr;  // 128-code groups per row / per K half; quant groups per row
   int nblk_max, R;       // max 8-row blocks per CTA; block regions in flight
   int64_t row_bytes, sc_win, region;
-  int64_t off_bx, off_gsum, off_zero, off_halves, off_bars, bytes;
+  int64_t off_bx, off_gsum, off_zero, off_halves, off_bars, off_route, bytes;
 };
 
 // gate/up shared memory: R regions of [8 gate rows | 8 up rows | 4 scale/min windows], each row
@@ -76,7 +79,8 @@ __host__ __device__ inline GuL gu_layout_for(int H, int I, int k, int group, int
   L.off_zero = ru16(L.off_gsum + int64_t(L.groups) * 2 * 4);    // 64 zero bytes
   L.off_halves = ru16(L.off_zero + 64);                         // [nblk_max][2 halves][CH][2] f32
   L.off_bars = ru16(L.off_halves + int64_t(L.nblk_max) * NSPLIT * CH * 2 * 4);  // [R] mbarriers
-  L.bytes = ru16(L.off_bars + 8 * int64_t(R));
+  L.off_route = ru16(L.off_bars + 8 * int64_t(R));                 // routing scratch
+  L.bytes = L.off_route + ROUTE_BYTES;
   return L;
 }
 
@@ -93,7 +97,7 @@ __host__ __device__ inline GuL gu_layout(int H, int I, int k, int group, int bit
 struct DnL {
   int groups, groups_per_piece, gpr, units, rows_max;
   int64_t row_bytes, sc_win, per_expert;
-  int64_t off_bd, off_dsum, off_zero, off_part, off_bar, bytes;
+  int64_t off_bd, off_dsum, off_zero, off_part, off_bar, off_route, bytes;
 };
 
 __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bits, int nctas) {
@@ -113,7 +117,8 @@ __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bit
   L.off_zero = ru16(L.off_dsum + int64_t(k) * L.groups * 2 * 4);     // 64 zero bytes
   L.off_part = ru16(L.off_zero + 64);                                // [DN_WARPS][16] f32
   L.off_bar = ru16(L.off_part + DN_WARPS * 16 * 4);                  // [k] mbarriers
-  L.bytes = ru16(L.off_bar + 8 * int64_t(k));
+  L.off_route = ru16(L.off_bar + 8 * int64_t(k));                    // routing scratch
+  L.bytes = L.off_route + ROUTE_BYTES;
   return L;
 }
 
@@ -162,7 +167,7 @@ template <int BITS>
 __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* __restrict__ pool,
                                                                 const float* __restrict__ meta,
                                                                 const uint16_t* __restrict__ x, MoeShape S,
-                                                                float* __restrict__ a_out) {
+                                                                float* __restrict__ a_out, MoeRoute RT) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -185,6 +190,12 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
   // the down grid may launch now: routing is final (its CTAs read the intermediate only after their
   // own griddepcontrol.wait)
   pdl_launch_dependents();
+  const float* mt = meta;  // [slots | weights]: the caller's buffer, or computed here from the logits
+  if (RT.logits) {
+    float* rs = reinterpret_cast<float*>(sm + Lg.off_route);
+    route_from_logits<true>(RT, S.k, rs, rs + 64, rs + 96);
+    mt = rs;
+  }
 
   // one warp (lanes 0-5) issues block bi into region bi % R: the 8 gate rows and the same 8 up rows
   // (each one contiguous range of its matrix) and the four scale/min windows, on the region's mbarrier
@@ -193,7 +204,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int blk = b0 + bi;
     const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
     int64_t slot;
-    const bool ok = route_slot(meta, j, S, slot);
+    const bool ok = route_slot(mt, j, S, slot);
     uint8_t* reg = sm + int64_t(r) * Lg.region;
     const uint32_t cb = uint32_t(CH * Lg.row_bytes);
     if (lane == 0) {
@@ -232,7 +243,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int64_t gpr_d = S.I / S.group, row_d = int64_t(S.I) * BITS / 8;
     for (int j = lane; j < S.k && h1 > h0; j += 32) {
       int64_t slot;
-      if (!route_slot(meta, j, S, slot)) continue;
+      if (!route_slot(mt, j, S, slot)) continue;
       const uint8_t* base = pool + slot * S.nbytes;
       prefetch_l2(base + 2 * S.mat_bytes + int64_t(h0) * row_d, uint32_t(int64_t(h1 - h0) * row_d));
       const int64_t len = 2 * int64_t(h1 - h0) * gpr_d;
@@ -296,7 +307,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
       const int blk = b0 + bi;
       const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
       int64_t slot;
-      const bool ok = route_slot(meta, j, S, slot);
+      const bool ok = route_slot(mt, j, S, slot);
       const uint32_t sskip = window(S.ncode + 2 * ((sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
       const uint32_t mskip = window(S.ncode + 2 * (S.ng + (sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
       const uint8_t* sw = reg + 2 * cb;
@@ -340,7 +351,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const float us = halves[((bi * NSPLIT) * CH + rw) * 2 + 1] + halves[((bi * NSPLIT + 1) * CH + rw) * 2 + 1];
     const int rr = (b0 + bi) * CH + rw;
     int64_t slot;
-    a_out[rr] = route_slot(meta, rr / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
+    a_out[rr] = route_slot(mt, rr / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
   }
 }
 
@@ -349,7 +360,7 @@ template <int BITS>
 __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __restrict__ pool,
                                                              const float* __restrict__ meta,
                                                              const float* __restrict__ a, MoeShape S,
-                                                             uint16_t* __restrict__ out) {
+                                                             uint16_t* __restrict__ out, MoeRoute RT) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -365,15 +376,21 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   const int units = Ld.units;
   const int npieces = S.k * NSPLIT;  // (expert, K half)
 
+  // routing: this runs before griddepcontrol.wait, after the producer of the routing inputs has
+  // completed (the gate/up grid triggers this launch only after its own wait), so reads go to L2
+  const float* mt = meta;
+  if (RT.logits) {
+    float* rs = reinterpret_cast<float*>(sm + Ld.off_route);
+    route_from_logits<true>(RT, S.k, rs, rs + 64, rs + 96);
+    mt = rs;
+  }
   // ---- the down rows of every routed expert: one bulk copy of the CTA's contiguous rows plus the
   //      scale and min windows, issued before waiting on the gate/up grid (the routing is final)
   if (warp == 0) {
     for (int j = lane; j < S.k; j += 32) {
       mbar_init(&bars[j], 1);
       mbar_fence_init();
-      // read through L2 (ld.global.cg): this runs before griddepcontrol.wait, after the producer of
-      // meta has completed (the gate/up grid triggers this launch only after its own wait)
-      const float f = __ldcg(meta + j);
+      const float f = RT.logits ? mt[j] : __ldcg(meta + j);
       const bool ok = f >= 0.0f && f < float(S.nslots);
       const int64_t slot = ok ? int64_t(f) : 0;
       if (!ok) flag(WISP_STATUS_BAD_SLOT);
@@ -427,8 +444,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   for (int piece = warp; piece < npieces; piece += DN_WARPS) {
     const int j = piece / NSPLIT, sp = piece % NSPLIT;
     int64_t slot;
-    const bool ok = route_slot(meta, j, S, slot);
-    const float wj = meta[S.k + j];
+    const bool ok = route_slot(mt, j, S, slot);
+    const float wj = mt[S.k + j];
     if (!ok || nrows <= 0) continue;
     mbar_wait(&bars[j], 0);
     const uint8_t* eb = sm + int64_t(j) * Ld.per_expert;

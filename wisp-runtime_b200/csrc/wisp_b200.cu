@@ -274,14 +274,14 @@ static bool v4_supported(const MoeShape& S, int bits, int nctas) {
 }
 
 static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
-                     float* scratch, uint16_t* out, cudaStream_t s, int nctas) {
+                     float* scratch, uint16_t* out, cudaStream_t s, int nctas, const MoeRoute& RT = MoeRoute{}) {
   const int64_t gsm = v4::gu_layout(S.H, S.I, S.k, S.group, bits, nctas).bytes;
   const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
   cudaError_t e = cudaSuccess;
 #define WISP_V4(B)                                                                                          \
-  e = launch_pdl(v4::gate_up_kernel<B>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch);  \
+  e = launch_pdl(v4::gate_up_kernel<B>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch, RT); \
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode gate/up: %s", cudaGetErrorString(e));        \
-  e = launch_pdl(v4::down_kernel<B>, nctas, v4::DN_THREADS, size_t(Ld.bytes), s, pool, meta, (const float*)scratch, S, out);
+  e = launch_pdl(v4::down_kernel<B>, nctas, v4::DN_THREADS, size_t(Ld.bytes), s, pool, meta, (const float*)scratch, S, out, RT);
   switch (bits) {
     case 4: WISP_V4(4) break;
     case 3: WISP_V4(3) break;
@@ -339,6 +339,23 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   return wisp_moe_decode_variant(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, 0, stream);
 }
 
+int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, const uint16_t* logits, int E, int k,
+                           int norm_topk, const int32_t* slot_table, int64_t base, float* row, const uint16_t* x, int64_t H,
+                           int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream) {
+  WISP_REQUIRE(logits, "wisp_moe_decode_routed: NULL logits");
+  WISP_REQUIRE(E >= 1 && E <= v4::GU_THREADS && E <= v4::DN_THREADS && k >= 1 && k <= E,
+               "wisp_moe_decode_routed: need 1 <= k <= E <= %d", v4::GU_THREADS);
+  MoeShape S;
+  // the routing lives in shared memory; moe_shape only needs a non-NULL meta to validate the rest
+  int rc = moe_shape(pool, nslots, nbytes, reinterpret_cast<const float*>(logits), k, x, H, I, bits, group, scratch, out, S);
+  if (rc) return rc;
+  const int nctas = num_sms();
+  if (!v4_supported(S, bits, nctas))
+    return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_routed: shape not supported by the tensor-core kernels");
+  MoeRoute RT{logits, E, norm_topk, slot_table, base, row};
+  return v4_launch(pool, nullptr, x, S, bits, scratch, out, static_cast<cudaStream_t>(stream), nctas, RT);
+}
+
 int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, uint16_t* out,
                             void* stream) {
@@ -381,11 +398,7 @@ int wisp_gemv(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const 
   const int grid = int(N < num_sms() ? N : num_sms());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (K <= 256) e = launch_pdl(dense::gemv_kernel<1>, grid, dense::THREADS, size_t(L.bytes), s, A);
-  else if (K <= 512) e = launch_pdl(dense::gemv_kernel<2>, grid, dense::THREADS, size_t(L.bytes), s, A);
-  else if (K <= 1024) e = launch_pdl(dense::gemv_kernel<4>, grid, dense::THREADS, size_t(L.bytes), s, A);
-  else if (K <= 2048) e = launch_pdl(dense::gemv_kernel<8>, grid, dense::THREADS, size_t(L.bytes), s, A);
-  else e = launch_pdl(dense::gemv_kernel<16>, grid, dense::THREADS, size_t(L.bytes), s, A);
+  e = launch_pdl(dense::gemv_kernel, grid, dense::THREADS, size_t(L.bytes), s, A);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gemv: %s", cudaGetErrorString(e));
   return check_launch("gemv");
 }

@@ -35,6 +35,7 @@ SIGNATURES = {
     "wisp_unpack_codes": (_I, [_P, _L, _L, _P, _L, _L, _I, _P, _P]),
     "wisp_moe_decode": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _P]),
     "wisp_moe_decode_variant": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _I, _P]),
+    "wisp_moe_decode_routed": (_I, [_P, _L, _L, _P, _I, _I, _I, _P, _L, _P, _P, _L, _L, _I, _I, _P, _P, _P]),
     "wisp_moe_decode_noalloc": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
     "wisp_gemv": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P]),

@@ -60,6 +60,8 @@ class GraphDecoder:
         self.scale = self.D ** -0.5
         self.pos = 0
         self.graph = self.greedy_graph = None
+        # router top-k folded into the MoE kernels where the tensor-core MoE path takes the shape
+        self.routed_moe = self._try_routed_moe()
 
     # ---------------------------------------------------------------------------------------------
     def _layer(self, l):
@@ -87,18 +89,37 @@ class GraphDecoder:
         # o projection + residual, then post-attention RMSNorm + router
         kernels.gemv(lw["wo"], self.att, res=self.h_emb if first else self.h_res, out=self.h_mid)
         kernels.gemv(lw["router"], self.h_mid, norm_w=lw["post_norm"], eps=c.eps, xn_out=self.xn, out=self.rlog)
-        kernels.router_topk(
-            self.rlog, self.k, c.norm_topk, slot_table=self.slot_table, base=l * self.E, row=self.rows[l], meta=self.meta
-        )
-        kernels.moe_decode_fast(
-            w.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
-            scratch=self.scratch,
-        )
+        if self.routed_moe:
+            kernels.moe_decode_routed(
+                w.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, norm_topk=c.norm_topk,
+                slot_table=self.slot_table, base=l * self.E, row=self.rows[l], out=self.moe, scratch=self.scratch,
+            )
+        else:
+            kernels.router_topk(
+                self.rlog, self.k, c.norm_topk, slot_table=self.slot_table, base=l * self.E, row=self.rows[l], meta=self.meta
+            )
+            kernels.moe_decode_fast(
+                w.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
+                scratch=self.scratch,
+            )
+
+    def _try_routed_moe(self):
+        c = self.cfg
+        try:
+            kernels.moe_decode_routed(
+                self.w.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group,
+                norm_topk=c.norm_topk, slot_table=self.slot_table, out=self.moe, scratch=self.scratch,
+            )
+            torch.cuda.synchronize()
+            return True
+        except kernels.WispError:
+            return False
 
     def kernels_per_step(self):
         """Kernels launched by one decode step (what the graph replays, torch copies excluded)."""
         attn = 1 if (self.D == 128 and self.Hq // self.Hk <= 8) else 3
-        return 1 + self.L * (attn + 6) + 3
+        moe = 2 if self.routed_moe else 3
+        return 1 + self.L * (attn + 3 + moe) + 3
 
     def _step(self):
         kernels.embed(self.w.embed, self.ctl[0:1], out=self.h_emb)

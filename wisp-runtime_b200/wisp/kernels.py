@@ -26,6 +26,7 @@ __all__ = [
     "moe_decode_q3_fast",
     "moe_decode_q2_fast",
     "moe_decode_fast",
+    "moe_decode_routed",
     "rope_decode",
     "rmsnorm",
     "gemv",
@@ -90,6 +91,30 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
         out.data_ptr(),
         variant,
         _stream(x),
+    )
+    return out
+
+
+def moe_decode_routed(pool, logits, x, k, n, H, I, bits, group=128, norm_topk=True, slot_table=None, base=0, row=None,
+                      out=None, scratch=None):
+    """moe_decode_fast with the router's softmax / top-k computed inside the MoE kernels from the
+    router logits (bf16 [E]); ``row`` (fp32 [2k]) optionally receives [experts | weights]."""
+    assert H % group == 0 and I % group == 0 and n == H * I
+    _need_cuda(pool, logits, x)
+    _bf16(logits)
+    if x.dtype != torch.bfloat16:
+        raise WispError(f"x must be bfloat16 (got {x.dtype})")
+    if slot_table is not None and (slot_table.dtype != torch.int32 or not slot_table.is_contiguous()):
+        raise WispError("slot_table must be contiguous int32")
+    x = x.contiguous()
+    if scratch is None:
+        scratch = moe_scratch(k, I, x.device)
+    if out is None:
+        out = torch.empty((H,), dtype=x.dtype, device=x.device)
+    _lib.call(
+        "wisp_moe_decode_routed", pool.data_ptr(), pool.shape[0], pool.shape[1], logits.data_ptr(), logits.numel(), k,
+        1 if norm_topk else 0, _ptr(slot_table), int(base), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(),
+        out.data_ptr(), _stream(x),
     )
     return out
 
