@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack"])
     ap.add_argument("--layers", type=int, default=48, help="layers (48 = the model; fewer = a small ncu case)")
     ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--cache-frac", type=float, default=0.4,
+                    help="decoder: fraction of the L*E experts resident in the GPU slot pool (config 3: 0.4; 1 = all)")
+    ap.add_argument("--no-prefetch", action="store_true", help="paged decoder: no next-layer expert prefetch")
     a = ap.parse_args()
     global L
     L = a.layers
@@ -62,10 +65,15 @@ def metric_name(a):
 
 def workload_config(a, n):
     if a.workload == "decoder":
+        paged = a.cache_frac < 1.0
+        res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU, pinned host store, "
+               f"cudaMemcpyAsync on a side stream{'' if a.no_prefetch else ', next-layer prefetch'})" if paged
+               else "all experts resident")
         return {
             "workload": f"qwen3-30b-a3b greedy decode bs=1: {L} layers, 32q/4kv heads x 128, {E} experts top-{K_TOP}, "
-            f"{a.bits}-bit g{G} experts all resident, bf16 attention/embeddings, vocab {VOCAB}, "
-            f"{a.prompt}-token seeded prompt then one token per step (whole-token CUDA graph)",
+            f"{a.bits}-bit g{G} experts, {res}, bf16 attention/embeddings, vocab {VOCAB}, "
+            f"{a.prompt}-token seeded prompt then one token per step "
+            + ("(one CUDA graph per layer segment)" if paged else "(whole-token CUDA graph)"),
             "model": "Qwen3-30B-A3B-shaped (random init)",
             "global_batch": n,
             "seq_len": a.prompt,
@@ -188,8 +196,11 @@ def time_moe_kernel(pool, nbytes, bits, reps=20, variant=0):
     out = torch.empty(L, H, dtype=torch.bfloat16, device=dev)
     scratch = kernels.moe_scratch(K_TOP, I, dev)
     metas = []
+    nslots = pool.shape[0]
     for l in range(L):
-        sel = torch.randperm(E, device=dev, generator=g)[:K_TOP] + l * E
+        # distinct slots per call; with a full pool, layer l's experts (l*E ..), else any slots
+        sel = torch.randperm(E, device=dev, generator=g)[:K_TOP] + l * E if nslots >= L * E else \
+            torch.randperm(nslots, device=dev, generator=g)[:K_TOP]
         metas.append(torch.cat([sel.float(), torch.full((K_TOP,), 1.0 / K_TOP, device=dev)]))
 
     def sweep():
@@ -481,31 +492,49 @@ class MoEStack:
 # decoder workload
 # ------------------------------------------------------------------------------------------------
 class DecodeBench:
-    """Greedy bs=1 decode through the whole-token graph (GraphDecoder.greedy_graph)."""
+    """Greedy bs=1 decode: the whole-token graph (GraphDecoder.greedy_graph) with every expert
+    resident, or the segmented paged decoder (PagedGraphDecoder) with a capped expert cache."""
 
     def __init__(self, a, device, seed):
         import torch
 
-        from wisp.graphdec import GraphDecoder
+        from wisp.graphdec import GraphDecoder, PagedGraphDecoder
         from wisp.model import DecoderConfig, DecoderWeights
 
         cfg = DecoderConfig(layers=L, bits=a.bits)
         self.w = DecoderWeights.random(cfg, device=device, seed=seed)
         need = a.prompt + 2 * (a.warmup + a.steps) + 16
-        self.dec = GraphDecoder(self.w, tmax=need)
+        self.paged = a.cache_frac < 1.0
+        if self.paged:
+            from wisp.cache import ExpertCache
+            from wisp.store import ExpertStore
+
+            store = ExpertStore.from_pool(self.w.pool, H * I, a.bits, G, L, E)
+            self.w.pool = None  # only the capped slot pool stays on the device
+            torch.cuda.empty_cache()
+            self.cache = ExpertCache(store, nslots=int(a.cache_frac * L * E), device=device)
+            self.dec = PagedGraphDecoder(self.w, self.cache, tmax=need, prefetch=not a.no_prefetch)
+        else:
+            self.dec = GraphDecoder(self.w, tmax=need)
         g = torch.Generator(device=device).manual_seed(seed)
         self.prompt = torch.randint(0, cfg.vocab, (a.prompt,), device=device, generator=g)
         self.dec.prefill(self.prompt)
         self.tok = self.dec.logits.argmax().reshape(1)
         self.dec.ctl[0:1].copy_(self.tok)
         self.dec.ctl[1].fill_(self.dec.pos)
+        if self.paged:
+            self.stats0 = dict(self.cache.stats), self.cache.bytes_h2d
 
     def launches_per_step(self):
         return self.dec.kernels_per_step()  # embed; per layer 3 GEMVs, attention, top-k, MoE x2; lm_head; argmax x2
 
     def step(self, t):
-        """One generated token: the step graph plus the on-device token/position update."""
-        self.dec.greedy_graph.replay()
+        """One generated token: the step graph plus the on-device token/position update (paged: the
+        L + 1 segments with the host's paging decisions between them)."""
+        if self.paged:
+            self.dec.next(self.dec.next_token)
+        else:
+            self.dec.greedy_graph.replay()
 
     def e2e_inputs(self):
         import torch
@@ -516,18 +545,35 @@ class DecodeBench:
         """Public-API step from host buffers: the token H2D, one decode step (which also advances the
         position), the next token D2H."""
         tok_host, out_host = inp
-        self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
-        self.dec.greedy_graph.replay()
+        if self.paged:
+            self.dec.next(tok_host.to(self.dec.dev, non_blocking=True))
+        else:
+            self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
+            self.dec.greedy_graph.replay()
         out_host.copy_(self.dec.next_token, non_blocking=True)
 
     def e2e_bytes(self):
         return 8, 8
 
     def pool(self):
-        return self.w.pool, self.w.nbytes
+        return (self.cache.gpu if self.paged else self.w.pool), self.w.nbytes
+
+    def paging_stats(self, tokens):
+        if not self.paged:
+            return None
+        st0, b0 = self.stats0
+        st = self.cache.stats
+        hits, misses = st["hits"] - st0["hits"], st["misses"] - st0["misses"]
+        return {
+            "slots": self.cache.nslots,
+            "hit_rate": hits / max(1, hits + misses),
+            "h2d_mb_per_token": (self.cache.bytes_h2d - b0) / tokens / 1e6,
+        }
 
     def release(self):
         self.dec.graph = self.dec.greedy_graph = None
+        if self.paged:
+            self.dec.segs = None
 
     def bytes_per_token(self, ctx):
         cfg = self.w.cfg
@@ -600,6 +646,8 @@ def main():
     clocks.window(w0, time.perf_counter())
     ms_e2e = e2.elapsed_time(e3)
     clk = clocks.stop()
+    if a.workload == "decoder" and bench.paged:
+        paging = bench.paging_stats(a.warmup + 2 * a.steps + 3)
     roof, _ = moe_roofline(pool, nbytes, a.bits)
     if a.workload == "decoder":
         ctx = bench.dec.pos + a.warmup + 2 * a.steps + 3  # context length at the end of the timed steps
@@ -633,6 +681,8 @@ def main():
             "gpu_launches": bench.launches_per_step() * a.steps,
             "clocks": clk,
         }
+        if a.workload == "decoder" and bench.paged:
+            line["paging"] = paging
         print(json.dumps(line), flush=True)
     bench.release()
     if world > 1:

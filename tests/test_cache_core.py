@@ -1,0 +1,73 @@
+"""Host logic of the expert cache (CPU): the slot policies of the reference CacheCore
+(wisp/cache_core.py) -- hits, misses, LRU and frequency eviction, protection of the current request,
+the static region, admission, resize."""
+
+import pytest
+
+from wisp.cache_core import CacheCore
+
+
+def test_ensure_hits_misses_and_lru_eviction():
+    c = CacheCore(4)
+    slots, loads = c.ensure([10, 11])
+    assert slots == [0, 1] and loads == [(10, 0), (11, 1)]
+    slots, loads = c.ensure([10, 12])
+    assert slots == [0, 2] and loads == [(12, 2)]
+    c.ensure([13])
+    assert sorted(c.key2slot) == [10, 11, 12, 13]
+    # full: the least recently used (11, last used at tick 1) goes
+    slots, loads = c.ensure([14])
+    assert loads == [(14, 1)] and 11 not in c.key2slot
+    assert c.stats == dict(hits=1, misses=5, evictions=1, calls=4)
+
+
+def test_current_request_is_protected():
+    c = CacheCore(3)
+    c.ensure([1, 2, 3])
+    slots, loads = c.ensure([1, 4, 5])  # 1 is a hit and must not be evicted for 4 or 5
+    assert 1 in c.key2slot and slots[0] == c.key2slot[1]
+    assert len(set(slots)) == 3
+    with pytest.raises(RuntimeError):
+        c.ensure([6, 7, 8, 9])  # more keys than slots
+
+
+def test_wsa_keeps_frequent_keys():
+    c = CacheCore(2, policy="wsa", decay=0.99)
+    for _ in range(5):
+        c.ensure([1])
+    c.ensure([2])
+    c.ensure([3])  # evicts 2 (seen once) rather than 1 (seen five times, decayed)
+    assert 1 in c.key2slot and 2 not in c.key2slot
+
+
+def test_static_region_never_evicted():
+    c = CacheCore(3, policy="static", n_static=2)
+    assert c.preload([7, 8]) == [(7, 0), (8, 1)]
+    for k in (20, 21, 22):
+        slots, _ = c.ensure([k])
+        assert slots == [2]
+    assert c.key2slot[7] == 0 and c.key2slot[8] == 1
+
+
+def test_split_and_admit():
+    c = CacheCore(2, admit_after=2.0)
+    c.ensure([1])
+    hk, hs, mk = c.split([1, 2])
+    assert hk == [1] and hs == [c.key2slot[1]] and mk == [2]
+    assert c.admit(2, set()) is None or c.norm_freq(2) >= 2.0
+    c.split([2])
+    c.split([2])
+    s = c.admit(2, {c.key2slot[1]})
+    assert s is not None and c.key2slot[2] == s
+
+
+def test_resized_keeps_hottest():
+    c = CacheCore(4)
+    for k in (1, 2, 3, 4):
+        c.ensure([k])
+    c.ensure([2])
+    nc, loads = c.resized(2)
+    assert [k for k, _ in loads] == [2, 4] and [s for _, s in loads] == [0, 1]
+    assert nc.free == [] and nc.key2slot == {2: 0, 4: 1}
+    nc2, loads2 = c.resized(6)
+    assert len(loads2) == 4 and nc2.free == [5, 4]

@@ -150,3 +150,31 @@ def test_greedy_graph_matches_stepwise():
         want.append(int(t))
     assert ids == want
     assert torch.equal(a.kc, b.kc) and torch.equal(a.vc, b.vc)
+
+
+@pytest.mark.parametrize("prefetch", [False, True])
+def test_paged_decoder_matches_resident(prefetch):
+    """40% of the experts resident, the rest paged in per layer from pinned host memory: the same
+    tokens and (up to the routing weights' last bit) the same logits as with every expert resident."""
+    from wisp.cache import ExpertCache
+    from wisp.graphdec import GraphDecoder, PagedGraphDecoder
+    from wisp.model import DecoderConfig, DecoderWeights
+    from wisp.store import ExpertStore
+
+    cfg = DecoderConfig(vocab=2000, hidden=2048, layers=3, heads=32, kv_heads=4, head_dim=128, experts=32, top_k=8,
+                        moe_inter=768)
+    w = DecoderWeights.random(cfg, seed=11)
+    store = ExpertStore.from_pool(w.pool, cfg.hidden * cfg.moe_inter, cfg.bits, cfg.group, cfg.layers, cfg.experts)
+    cache = ExpertCache(store, nslots=int(0.4 * cfg.layers * cfg.experts))
+    a = GraphDecoder(w, tmax=128)
+    b = PagedGraphDecoder(w, cache, tmax=128, prefetch=prefetch)
+    t = torch.tensor([5], device="cuda")
+    for step in range(8):
+        la = a.next(t).float().clone()
+        lb = b.next(t).float()
+        assert (la - lb).abs().max().item() <= 2e-2 * la.abs().max().item(), step
+        assert torch.equal(a.rows, b.rows) or (a.rows[:, : cfg.top_k] == b.rows[:, : cfg.top_k]).all()
+        t = la.argmax().reshape(1)
+    st = cache.stats
+    assert st["misses"] > 0 and st["hits"] + st["misses"] == 8 * cfg.layers * cfg.top_k
+    assert cache.bytes_h2d >= st["misses"] * store.nbytes

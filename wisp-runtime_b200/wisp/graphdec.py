@@ -207,3 +207,144 @@ class GraphDecoder:
             out[i : i + 1].copy_(self.next_token)
         self.pos += steps
         return out
+
+
+class PagedGraphDecoder(GraphDecoder):
+    """Decode with only part of the experts resident: the reference's segmented scheme
+    (wisp/graphdec.py:1-16, :215-308).  A token is cut at its L routing decisions; the pieces between
+    them are CUDA graphs:
+
+        graph[0]   embed -> layer 0 attention block -> router(0)                 -> row(0) to the host
+        graph[i]   MoE(i-1) -> layer i attention block -> router(i)              -> row(i) to the host
+        graph[L]   MoE(L-1) -> final norm -> lm_head -> argmax
+
+    Between graph[i] and graph[i+1] the host reads row(i), ``cache.ensure`` picks slots and copies the
+    missing experts in on the cache's copy stream (pinned cudaMemcpyAsync), and the slots + weights go
+    to the device meta buffer ahead of graph[i+1] on the compute stream.  With ``prefetch`` the next
+    layer's router is also applied to this layer's MoE input and its top-k are paged in without waiting
+    (the reference's next_gate predictor), overlapping PCIe with the compute of this layer."""
+
+    def __init__(self, w: DecoderWeights, cache, tmax=2048, prefetch=False):
+        super().__init__(w, tmax=tmax, use_graph=True)
+        self.cache = cache
+        self.prefetch = prefetch
+        self.row_host = torch.zeros(self.L, 2 * self.k, dtype=torch.float32, pin_memory=True)
+        self.pred_host = torch.zeros(self.L, self.k, dtype=torch.float32, pin_memory=True)
+        self.pred_log = torch.zeros(self.E, dtype=torch.bfloat16, device=self.dev)
+        self.meta_pred = torch.zeros(2 * self.k, dtype=torch.float32, device=self.dev)
+        self.meta_host = torch.zeros(2 * self.k, dtype=torch.float32, pin_memory=True)
+        self.segs = None
+        self.evt = [torch.cuda.Event() for _ in range(self.L)]
+
+    def _try_routed_moe(self):
+        return False  # routing comes from the host (slots of the paged pool)
+
+    def kernels_per_step(self):
+        attn = 1 if (self.D == 128 and self.Hq // self.Hk <= 8) else 3
+        return 1 + self.L * (attn + 3 + 1 + 2) + 3 + (2 * (self.L - 1) if self.prefetch else 0)
+
+    def _attn_router(self, l):
+        """Layer l up to its routing row (copied to pinned host memory)."""
+        c, lw = self.cfg, self.w.layers[l]
+        pos = self.ctl[1:2]
+        first = l == 0
+        kernels.gemv(
+            lw["wqkv"], self.h_emb if first else self.h_mid, x_add=None if first else self.moe,
+            x_sum_out=None if first else self.h_res, norm_w=lw["in_norm"], eps=c.eps, out=self.qkv,
+        )
+        if self.D == 128 and self.Hq // self.Hk <= 8:
+            kernels.attn_decode(
+                self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos,
+                self.kc[l], self.vc[l], self.scale, out=self.att,
+            )
+        else:
+            kernels.qk_norm_rope_kv(
+                self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos,
+                self.kc[l], self.vc[l], q_out=self.q,
+            )
+            kernels.gqa_decode_attn(
+                self.q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], pos, self.scale, workspace=self.attn_ws, out=self.att
+            )
+        kernels.gemv(lw["wo"], self.att, res=self.h_emb if first else self.h_res, out=self.h_mid)
+        kernels.gemv(lw["router"], self.h_mid, norm_w=lw["post_norm"], eps=c.eps, xn_out=self.xn, out=self.rlog)
+        kernels.router_topk(self.rlog, self.k, c.norm_topk, row=self.rows[l], meta=self.meta)
+        if self.prefetch and l + 1 < self.L:  # next layer's router on this layer's MoE input
+            kernels.gemv(self.w.layers[l + 1]["router"], self.xn, out=self.pred_log)
+            kernels.router_topk(self.pred_log, self.k, c.norm_topk, meta=self.meta_pred)  # base 0: expert ids
+            self.pred_host[l].copy_(self.meta_pred[: self.k], non_blocking=True)
+        self.row_host[l].copy_(self.rows[l], non_blocking=True)
+
+    def _moe(self, l):
+        c = self.cfg
+        kernels.moe_decode_fast(
+            self.cache.gpu, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
+            scratch=self.scratch,
+        )
+
+    def _seg(self, j):
+        if j == 0:
+            kernels.embed(self.w.embed, self.ctl[0:1], out=self.h_emb)
+        else:
+            self._moe(j - 1)
+        if j < self.L:
+            self._attn_router(j)
+        else:
+            kernels.gemv(
+                self.w.lm_head, self.h_mid, x_add=self.moe, x_sum_out=self.h_res, norm_w=self.w.final_norm,
+                eps=self.cfg.eps, out=self.logits,
+            )
+            kernels.argmax(self.logits, workspace=self.argmax_ws, out=self.next_token)
+
+    def capture(self):
+        # warm-up (aims the cache write at the last slot; experts 0..k-1 of the pool as routing)
+        saved = self.ctl.clone()
+        self.ctl[1] = self.tmax - 1
+        self.meta.copy_(torch.cat([torch.arange(self.k, device=self.dev).float(), torch.full((self.k,), 1.0 / self.k, device=self.dev)]))
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for j in range(self.L + 1):
+                self._seg(j)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.ctl.copy_(saved)
+        pool = torch.cuda.graph_pool_handle()
+        self.segs = []
+        for j in range(self.L + 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                self._seg(j)
+            self.segs.append(g)
+        torch.cuda.synchronize()
+
+    def _prepare(self, l):
+        """Host side of layer l: routing row -> resident slots (+ prefetch of the predicted next layer)."""
+        self.evt[l].synchronize()
+        row = self.row_host[l]
+        k = self.k
+        base = l * self.E
+        experts = [int(v) for v in row[:k].tolist()]
+        slots = self.cache.ensure([base + e for e in experts])
+        self.meta_host[:k] = torch.tensor(slots, dtype=torch.float32)
+        self.meta_host[k:] = row[k:]
+        self.meta.copy_(self.meta_host, non_blocking=True)  # ordered before the next replay on this stream
+        if self.prefetch and l + 1 < self.L:
+            nb = (l + 1) * self.E
+            self.cache.prefetch([nb + int(e) for e in self.pred_host[l].tolist()], slots)
+
+    @torch.no_grad()
+    def next(self, token):
+        assert self.pos < self.tmax, "context full"
+        if self.segs is None:
+            self.capture()
+        self.ctl[0:1].copy_(token.reshape(1))
+        self.ctl[1].fill_(self.pos)
+        self.segs[0].replay()
+        self.evt[0].record()
+        for l in range(self.L):
+            self._prepare(l)
+            self.segs[l + 1].replay()
+            if l + 1 < self.L:
+                self.evt[l + 1].record()
+        self.pos += 1
+        return self.logits
