@@ -105,6 +105,23 @@ int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, 
                            int norm_topk, const int32_t* slot_table, int64_t base, float* row, const uint16_t* x, int64_t H,
                            int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream);
 
+/* ---- batched MoE decode ------------------------------------------------------------------------ */
+/* Bytes of the workspace wisp_moe_batched needs for N tokens of k choices (host-only; -1 if N*k is
+ * outside [1, 2048]). */
+int64_t wisp_moe_batched_workspace_bytes(int N, int k, int64_t H, int64_t I);
+
+/* MoE of N tokens: meta fp32 [N, 2k] = per token [k slots | k weights]; x bf16 [N, H]; out bf16 [N, H],
+ * out[t] = sum_j w[t,j] * Wd_j (silu(Wg_j x_t) * (Wu_j x_t)).  The (token, choice) pairs are grouped by
+ * slot on the device, so each routed expert's weights are read once per call; the products run on the
+ * tensor cores with the weights dequantized bit-exactly to bf16 (q*s + m).  bits 8/4/3/2, H and I
+ * multiples of 128, group a multiple of 32; workspace 256-byte aligned, of the size above.  Invalid
+ * slots are skipped and flagged.
+ * Replaces the reference's bs > 1 MoE (wisp/moe.py:62-137: unique experts, dequant, per-expert MLP,
+ * weighted index_add). */
+int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
+                     int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
+                     void* stream);
+
 /* Allocation-free twin of wisp_moe_decode for callers that cannot allocate device memory (a host
  * stack that owns no allocator, e.g. a CUDA-graph node builder or an embedding runtime that hands over
  * only the pool, x and out): the fp32 intermediate a = silu(g)*u lives in a file-scope device array

@@ -8,6 +8,7 @@
 #include "dense.cuh"
 #include "moe_decode.cuh"
 #include "moe_decode_v4.cuh"
+#include "moe_batched.cuh"
 #include "quant.cuh"
 
 namespace wisp {
@@ -354,6 +355,43 @@ int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, 
     return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_routed: shape not supported by the tensor-core kernels");
   MoeRoute RT{logits, E, norm_topk, slot_table, base, row};
   return v4_launch(pool, nullptr, x, S, bits, scratch, out, static_cast<cudaStream_t>(stream), nctas, RT);
+}
+
+int64_t wisp_moe_batched_workspace_bytes(int N, int k, int64_t H, int64_t I) {
+  if (N < 1 || k < 1 || int64_t(N) * k > batched::MAX_PAIRS || H <= 0 || I <= 0) return -1;
+  return batched::ws_bytes(N * k, H, I);
+}
+
+int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
+                     int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
+                     void* stream) {
+  WISP_REQUIRE(N >= 1 && k >= 1 && int64_t(N) * k <= batched::MAX_PAIRS, "wisp_moe_batched: need 1 <= N*k <= %d", batched::MAX_PAIRS);
+  MoeShape S;
+  int rc = moe_shape(pool, nslots, nbytes, meta, k, x, H, I, bits, group, reinterpret_cast<const float*>(workspace), out, S);
+  if (rc) return rc;
+  WISP_REQUIRE(H % 128 == 0 && I % 128 == 0, "wisp_moe_batched: H and I must be multiples of 128");
+  WISP_REQUIRE(bits == 8 || bits == 4 || bits == 3 || bits == 2, "wisp_moe_batched: bits must be 8, 4, 3 or 2");
+  WISP_REQUIRE(workspace_bytes >= batched::ws_bytes(N * k, H, I), "wisp_moe_batched: workspace of %lld bytes is too small (%lld needed)",
+               (long long)workspace_bytes, (long long)batched::ws_bytes(N * k, H, I));
+  WISP_REQUIRE(aligned(workspace, 256), "wisp_moe_batched: workspace must be 256-byte aligned");
+  const batched::Ws W = batched::ws_carve(workspace, N * k, I);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = num_sms();
+  cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
+#define WISP_BATCHED(B)                                                                                     \
+  e = launch_pdl(batched::gate_up_kernel<B>, grid, batched::THREADS, 0, s, pool, S, x, W);                  \
+  if (e == cudaSuccess) e = launch_pdl(batched::down_kernel<B>, grid, batched::THREADS, 0, s, pool, S, W);
+  switch (bits) {
+    case 8: WISP_BATCHED(8) break;
+    case 4: WISP_BATCHED(4) break;
+    case 3: WISP_BATCHED(3) break;
+    default: WISP_BATCHED(2) break;
+  }
+#undef WISP_BATCHED
+  if (e == cudaSuccess) e = launch_pdl(batched::combine_kernel, grid, 256, 0, s, meta, N, k, H, W, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
+  return check_launch("moe_batched");
 }
 
 int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,

@@ -27,6 +27,7 @@ __all__ = [
     "moe_decode_q2_fast",
     "moe_decode_fast",
     "moe_decode_routed",
+    "moe_batched",
     "rope_decode",
     "rmsnorm",
     "gemv",
@@ -115,6 +116,31 @@ def moe_decode_routed(pool, logits, x, k, n, H, I, bits, group=128, norm_topk=Tr
         "wisp_moe_decode_routed", pool.data_ptr(), pool.shape[0], pool.shape[1], logits.data_ptr(), logits.numel(), k,
         1 if norm_topk else 0, _ptr(slot_table), int(base), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(),
         out.data_ptr(), _stream(x),
+    )
+    return out
+
+
+def moe_batched_workspace(N, k, H, I, device):
+    nb = _lib.lib().wisp_moe_batched_workspace_bytes(N, k, H, I)
+    if nb < 0:
+        raise WispError("moe_batched: N*k must be in [1, 2048]")
+    return torch.empty(nb, dtype=torch.uint8, device=device)
+
+
+def moe_batched(pool, meta, x, k, n, H, I, bits, group=128, out=None, workspace=None):
+    """MoE of N tokens (x bf16 [N, H], meta fp32 [N, 2k] = per token [slots | weights]) -> bf16 [N, H]."""
+    assert H % group == 0 and I % group == 0 and n == H * I
+    _need_cuda(pool, meta, x)
+    _bf16(x)
+    N = x.shape[0]
+    assert meta.dtype == torch.float32 and meta.is_contiguous() and meta.numel() == N * 2 * k
+    if workspace is None:
+        workspace = moe_batched_workspace(N, k, H, I, x.device)
+    if out is None:
+        out = torch.empty((N, H), dtype=torch.bfloat16, device=x.device)
+    _lib.call(
+        "wisp_moe_batched", pool.data_ptr(), pool.shape[0], pool.shape[1], meta.data_ptr(), N, k, x.data_ptr(), H, I, bits,
+        group, workspace.data_ptr(), workspace.numel(), out.data_ptr(), _stream(x),
     )
     return out
 
