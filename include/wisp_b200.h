@@ -122,6 +122,20 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
                      int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
                      void* stream);
 
+/* ---- gpt-oss experts ------------------------------------------------------------------------------ */
+/* Bytes of the workspace wisp_moe_gptoss needs (host-only; -1 if N*k is outside [1, 2048]). */
+int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I);
+
+/* gpt-oss MoE of N tokens: experts packed as [gate_up [H, 2I] (gate/up interleaved) | down [I, H]],
+ * input-major, wisp.quant layout (H == I); meta fp32 [N, 2k] = per token [k slots | k weights],
+ * experts int32 [N, k] = the expert ids (bias rows), gate_up_bias bf16 [E, 2I], down_bias bf16 [E, H].
+ * out[t] = sum_j w[t,j] * (bf16(a . W_d) + b_d), a = (clamp(up, -7, 7) + 1) * g * sigmoid(1.702 g),
+ * g = min(gate, 7), [gate | up] = bf16(x . W_gu) + b_gu (interleaved).  Dequant bit-exact (bf16(q*s+m)).
+ * Replaces the reference's PagedGptOssBlock expert math (wisp/gptoss.py:107-143: dequant + bmm). */
+int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, const int32_t* experts, int N, int k,
+                    const uint16_t* x, int64_t H, int64_t I, int bits, int group, const uint16_t* gate_up_bias,
+                    const uint16_t* down_bias, void* workspace, int64_t workspace_bytes, uint16_t* out, void* stream);
+
 /* Allocation-free twin of wisp_moe_decode for callers that cannot allocate device memory (a host
  * stack that owns no allocator, e.g. a CUDA-graph node builder or an embedding runtime that hands over
  * only the pool, x and out): the fp32 intermediate a = silu(g)*u lives in a file-scope device array
@@ -191,7 +205,8 @@ int wisp_attn_decode(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t*
                      uint16_t* v_cache, float scale, uint16_t* out, void* stream);
 
 /* Router of one token: p = softmax(logits bf16 [E]) in fp32, the k largest (ties: lower expert id),
- * renormalised when norm_topk, rounded to bf16.  row (nullable) = fp32 [k experts | k weights];
+ * renormalised when norm_topk == 1; norm_topk == 2 (gpt-oss): softmax over the k selected logits
+ * (wisp/gptoss.py:122-123); rounded to bf16.  row (nullable) = fp32 [k experts | k weights];
  * meta = fp32 [k slots | k weights], slot = slot_table[base + e] when slot_table is given, else
  * base + e.  E <= 1024, k <= 32.
  * Replaces wisp/graphdec.py:177-182 and wisp/moe.py:67-72 (softmax, topk, renormalise, bf16). */

@@ -1,0 +1,87 @@
+"""GPU parity of the gpt-oss expert kernels through the C ABI: against the reference
+PagedGptOssBlock outputs (fixture gptoss.npz: its decode branch N=1 and grouped branch N=5) and the
+oracle at the gpt-oss-20b layer shape (H = I = 2880, 32 experts, top-4) for N = 1 and 32."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import wisp_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _np(t):
+    return O.bf16_bits_to_f32(t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def _bf(u16):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / np.abs(ref).max())
+
+
+def _route(logits, k):
+    """Router of gpt-oss through the library: top-k of the logits, softmax over the selected."""
+    from wisp import kernels
+
+    rows = []
+    for t in range(logits.shape[0]):
+        row = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        kernels.router_topk(logits[t].contiguous(), k, "selected", row=row)
+        rows.append(row)
+    row = torch.stack(rows)
+    return row[:, :k].to(torch.int32).contiguous(), row[:, k:].contiguous()
+
+
+@pytest.mark.parametrize("N", [1, 5])
+def test_matches_reference_block(golden, N):
+    from wisp import kernels
+
+    g = golden("gptoss")
+    H, I, k, G = int(g["H"]), int(g["I"]), int(g["k"]), int(g["G"])
+    x = _bf(g[f"x_N{N}"])
+    logits = torch.nn.functional.linear(x, _bf(g["router_w"]), _bf(g["router_b"]))
+    experts, w = _route(logits, k)
+    # the reference: torch.topk of the logits, softmax over them in bf16
+    tv, ti = torch.topk(logits, k, dim=-1)
+    sc = torch.softmax(tv, dim=1, dtype=tv.dtype).float()
+    assert torch.equal(experts.long().sort(1).values, ti.sort(1).values)
+    order = torch.argsort(experts.long(), 1)
+    assert (w.gather(1, order) - sc.gather(1, torch.argsort(ti, 1))).abs().max().item() <= 2.0**-7
+    pool = torch.from_numpy(g["pool"]).cuda()
+    meta = torch.cat([experts.float(), w], 1).contiguous()
+    out = kernels.moe_gptoss(pool, meta, experts, x, k, H, I, 4, _bf(g["gub"]), _bf(g["db"]), G)
+    ref = O.bf16_bits_to_f32(g[f"out_N{N}"])
+    assert _rel(_np(out), ref) < 2e-2
+    want = O.gptoss_ref(g["pool"], experts.cpu().numpy(), w.cpu().numpy(), _np(x), H, I, 4, G, g["gub"], g["db"])
+    assert _rel(_np(out), want) < 1e-2
+
+
+@pytest.mark.parametrize("N", [1, 32])
+def test_gptoss_20b_layer_vs_oracle(N):
+    from wisp import kernels, quant
+
+    H = I = 2880
+    E, k, G, bits = 32, 4, 128, 4
+    n = H * I
+    gen = torch.Generator(device="cuda").manual_seed(N)
+    logits = torch.randn(N, E, device="cuda", generator=gen).to(torch.bfloat16)
+    experts, w = _route(logits, k)
+    used = torch.unique(experts.long()).tolist()
+    nb = quant.expert_nbytes(n, bits, G)
+    pool = torch.zeros((E, nb), dtype=torch.uint8, device="cuda")
+    for e in used:
+        w3 = (torch.randn(1, 3, n, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+        pool[e : e + 1] = quant.quantize_batch(w3, bits, G)
+    gub = (torch.randn(E, 2 * I, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    db = (torch.randn(E, H, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    x = torch.randn(N, H, device="cuda", generator=gen).to(torch.bfloat16)
+    meta = torch.cat([experts.float(), w], 1).contiguous()
+    out = kernels.moe_gptoss(pool, meta, experts, x, k, H, I, bits, gub, db, G)
+    tok = list(range(N)) if N <= 4 else [0, 7, 31]  # the oracle dequantizes per token: sample a few
+    want = O.gptoss_ref(pool.cpu().numpy(), experts.cpu().numpy()[tok], w.cpu().numpy()[tok], _np(x)[tok], H, I, bits, G,
+                        gub.view(torch.int16).cpu().numpy().view(np.uint16), db.view(torch.int16).cpu().numpy().view(np.uint16))
+    assert _rel(_np(out)[tok], want) < 1e-2

@@ -154,3 +154,23 @@ def test_sabotage_detected(golden):
     shuffled = (slots + 1) % pool.shape[0]  # every token routed to the wrong expert
     bad = O.moe_decode_ref(pool, shuffled, x, w, H * I, H, I, 4)
     assert np.abs(bad - ref).max() > 10 * 2e-2 * np.abs(ref).max()
+
+
+def test_gptoss_oracle_matches_reference_block(golden):
+    """The oracle's gpt-oss expert math against PagedGptOssBlock (wisp/gptoss.py:111-143) on the
+    fixture, routing as the reference does it (top-k of the bf16 logits, softmax over them in bf16)."""
+    import torch
+
+    g = golden("gptoss")
+    H, I, k, G = int(g["H"]), int(g["I"]), int(g["k"]), int(g["G"])
+    for N in (1, 5):
+        x = O.bf16_bits_to_f32(g[f"x_N{N}"])
+        xb = torch.from_numpy(g[f"x_N{N}"].view(np.int16)).view(torch.bfloat16)
+        wr = torch.from_numpy(g["router_w"].view(np.int16)).view(torch.bfloat16)
+        br = torch.from_numpy(g["router_b"].view(np.int16)).view(torch.bfloat16)
+        logits = torch.nn.functional.linear(xb, wr, br)
+        tv, ti = torch.topk(logits, k, dim=-1)
+        sc = torch.softmax(tv, dim=1, dtype=tv.dtype).float().numpy()
+        out = O.gptoss_ref(g["pool"], ti.numpy(), sc, x, H, I, 4, G, g["gub"], g["db"])
+        ref = O.bf16_bits_to_f32(g[f"out_N{N}"])
+        assert np.abs(out - ref).max() <= 2e-2 * np.abs(ref).max()

@@ -502,8 +502,18 @@ __global__ void router_topk_kernel(const uint16_t* __restrict__ logits, int E, i
     if (lane == 0) p[be] = -2.0f;
     __syncwarp();
   }
+  // norm_topk 2 (gpt-oss, wisp/gptoss.py:122-123): softmax over the k selected logits only
+  float sm_w = 0.0f;
+  if (norm_topk == 2) {
+    // p = e^(l - m) / s is monotone in l, so the selected probabilities give back the logits' ratios:
+    // e^(l_j - l_max) = p_j / p_max
+    const float pmax = __shfl_sync(0xffffffffu, selw, 0);  // the first pick is the largest
+    float r = lane < k ? selw / pmax : 0.0f;
+    float rs = warp_sum(r);
+    sm_w = r / rs;
+  }
   if (lane < k) {
-    const float w = bf16_to_f32(f32_to_bf16(norm_topk ? selw / tot : selw));
+    const float w = bf16_to_f32(f32_to_bf16(norm_topk == 2 ? sm_w : (norm_topk ? selw / tot : selw)));
     if (row) {
       row[lane] = float(sele);
       row[k + lane] = w;

@@ -9,6 +9,7 @@
 #include "moe_decode.cuh"
 #include "moe_decode_v4.cuh"
 #include "moe_batched.cuh"
+#include "moe_gptoss.cuh"
 #include "quant.cuh"
 
 namespace wisp {
@@ -392,6 +393,67 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   if (e == cudaSuccess) e = launch_pdl(batched::combine_kernel, grid, 256, 0, s, meta, N, k, H, W, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
   return check_launch("moe_batched");
+}
+
+static int gptoss_splits(int P) {
+  const int s = 128 / (P < 1 ? 1 : P);
+  return s < 1 ? 1 : (s > 32 ? 32 : s);
+}
+
+int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I) {
+  if (N < 1 || k < 1 || int64_t(N) * k > batched::MAX_PAIRS || H <= 0 || I <= 0) return -1;
+  return gptoss::ws_bytes(N * k, gptoss_splits(N * k), H, I);
+}
+
+int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, const int32_t* experts, int N, int k,
+                    const uint16_t* x, int64_t H, int64_t I, int bits, int group, const uint16_t* gate_up_bias,
+                    const uint16_t* down_bias, void* workspace, int64_t workspace_bytes, uint16_t* out, void* stream) {
+  WISP_REQUIRE(experts && gate_up_bias && down_bias, "wisp_moe_gptoss: NULL pointer");
+  WISP_REQUIRE(N >= 1 && k >= 1 && int64_t(N) * k <= batched::MAX_PAIRS, "wisp_moe_gptoss: need 1 <= N*k <= %d", batched::MAX_PAIRS);
+  WISP_REQUIRE(H == I, "wisp_moe_gptoss: the gpt-oss layout needs intermediate == hidden (got H=%lld I=%lld)", (long long)H,
+               (long long)I);
+  // quantization groups run along the flat code stream and may straddle rows (2880 % 128 = 64): an
+  // 8-code word never straddles a group as long as group and H are multiples of 8
+  WISP_REQUIRE(pool && meta && x && workspace && out, "wisp_moe_gptoss: NULL pointer");
+  WISP_REQUIRE(bits == 8 || bits == 4 || bits == 3 || bits == 2, "wisp_moe_gptoss: bits must be 8, 4, 3 or 2");
+  WISP_REQUIRE(group > 0 && group % 8 == 0 && H > 0 && H % 8 == 0 && H <= 8192, "wisp_moe_gptoss: group and H must be multiples of 8");
+  const int64_t n = H * I;
+  WISP_REQUIRE(wisp_expert_nbytes(n, bits, group) == nbytes, "wisp_moe_gptoss: nbytes=%lld, expected %lld", (long long)nbytes,
+               (long long)wisp_expert_nbytes(n, bits, group));
+  WISP_REQUIRE(aligned(pool, 16) && nbytes % 16 == 0 && aligned(x, 16), "wisp_moe_gptoss: pool and x must be 16-byte aligned");
+  MoeShape S;
+  S.nslots = nslots;
+  S.nbytes = nbytes;
+  S.k = k;
+  S.H = int(H);
+  S.I = int(I);
+  S.group = group;
+  S.gshift = 0;
+  S.ncode = 3 * n * bits / 8;
+  S.ng = 3 * n / group;
+  S.mat_bytes = n * bits / 8;
+  const int P = N * k, ns = gptoss_splits(P);
+  WISP_REQUIRE(workspace_bytes >= gptoss::ws_bytes(P, ns, H, I), "wisp_moe_gptoss: workspace too small (%lld needed)",
+               (long long)gptoss::ws_bytes(P, ns, H, I));
+  WISP_REQUIRE(aligned(workspace, 256), "wisp_moe_gptoss: workspace must be 256-byte aligned");
+  const gptoss::Ws W = gptoss::ws_carve(workspace, P, ns, H, I);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = num_sms() * 2;
+  cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
+#define WISP_GPTOSS(B)                                                                                                 \
+  if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 0>, grid, gptoss::THREADS, 0, s, pool, S, P, ns, x, W);     \
+  if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, 256, 0, s, S, P, ns, experts, gate_up_bias, W);        \
+  if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 1>, grid, gptoss::THREADS, 0, s, pool, S, P, ns, x, W);
+  switch (bits) {
+    case 8: WISP_GPTOSS(8) break;
+    case 4: WISP_GPTOSS(4) break;
+    case 3: WISP_GPTOSS(3) break;
+    default: WISP_GPTOSS(2) break;
+  }
+#undef WISP_GPTOSS
+  if (e == cudaSuccess) e = launch_pdl(gptoss::combine_kernel, grid, 256, 0, s, meta, N, k, S, ns, experts, down_bias, W, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_gptoss: %s", cudaGetErrorString(e));
+  return check_launch("moe_gptoss");
 }
 
 int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,

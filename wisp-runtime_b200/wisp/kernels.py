@@ -28,6 +28,7 @@ __all__ = [
     "moe_decode_fast",
     "moe_decode_routed",
     "moe_batched",
+    "moe_gptoss",
     "rope_decode",
     "rmsnorm",
     "gemv",
@@ -141,6 +142,29 @@ def moe_batched(pool, meta, x, k, n, H, I, bits, group=128, out=None, workspace=
     _lib.call(
         "wisp_moe_batched", pool.data_ptr(), pool.shape[0], pool.shape[1], meta.data_ptr(), N, k, x.data_ptr(), H, I, bits,
         group, workspace.data_ptr(), workspace.numel(), out.data_ptr(), _stream(x),
+    )
+    return out
+
+
+def moe_gptoss(pool, meta, experts, x, k, H, I, bits, gate_up_bias, down_bias, group=128, out=None, workspace=None):
+    """gpt-oss experts of N tokens (x bf16 [N, H]; meta fp32 [N, 2k] = per token [slots | weights];
+    experts int32 [N, k] = expert ids for the biases) -> bf16 [N, H]."""
+    _need_cuda(pool, meta, x, experts)
+    _bf16(x, gate_up_bias, down_bias)
+    N = x.shape[0]
+    assert meta.dtype == torch.float32 and meta.is_contiguous() and meta.numel() == N * 2 * k
+    assert experts.dtype == torch.int32 and experts.is_contiguous() and experts.numel() == N * k
+    if workspace is None:
+        nb = _lib.lib().wisp_moe_gptoss_workspace_bytes(N, k, H, I)
+        if nb < 0:
+            raise WispError("moe_gptoss: N*k must be in [1, 2048]")
+        workspace = torch.empty(nb, dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty((N, H), dtype=torch.bfloat16, device=x.device)
+    _lib.call(
+        "wisp_moe_gptoss", pool.data_ptr(), pool.shape[0], pool.shape[1], meta.data_ptr(), experts.data_ptr(), N, k,
+        x.data_ptr(), H, I, bits, group, gate_up_bias.data_ptr(), down_bias.data_ptr(), workspace.data_ptr(),
+        workspace.numel(), out.data_ptr(), _stream(x),
     )
     return out
 
@@ -343,7 +367,8 @@ def attn_decode(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, k_cache, v_c
 
 def router_topk(logits, k, norm_topk=True, slot_table=None, base=0, row=None, meta=None):
     """softmax -> top-k -> renormalise -> bf16 of one token's router logits (bf16 [E]); fills the
-    routing row [experts | weights] and the MoE meta [slots | weights] (fp32)."""
+    routing row [experts | weights] and the MoE meta [slots | weights] (fp32).  ``norm_topk``:
+    True (Qwen3 norm_topk_prob), False, or "selected" (gpt-oss: softmax over the k selected logits)."""
     _need_cuda(logits)
     _bf16(logits)
     E = logits.numel()
@@ -351,8 +376,9 @@ def router_topk(logits, k, norm_topk=True, slot_table=None, base=0, row=None, me
         meta = torch.empty(2 * k, dtype=torch.float32, device=logits.device)
     if slot_table is not None and (slot_table.dtype != torch.int32 or not slot_table.is_contiguous()):
         raise WispError("slot_table must be contiguous int32")
+    mode = 2 if norm_topk == "selected" else (1 if norm_topk else 0)
     _lib.call(
-        "wisp_router_topk", logits.data_ptr(), E, k, 1 if norm_topk else 0, _ptr(slot_table), int(base), _ptr(row),
+        "wisp_router_topk", logits.data_ptr(), E, k, mode, _ptr(slot_table), int(base), _ptr(row),
         meta.data_ptr(), _stream(logits),
     )
     return meta
