@@ -35,6 +35,7 @@ sys.path.insert(0, ROOT)
 H, I, E, K_TOP, L, G = 2048, 768, 128, 8, 48, 128
 HQ, HK, D, VOCAB = 32, 4, 128, 151936
 N_ROUTES = 16  # moe-stack: distinct seeded routings (tokens) cycled through by the timed steps
+EP_BATCH = 64  # moe-ep: tokens per step over all ranks (config 4 batch)
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up + one down launch (4-bit, this shape),
 # from the ncu capture summarised in profiles/moe_decode_q4_qwen3_gate_up_down_full.md
 NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
@@ -47,7 +48,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
-    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack"])
+    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack", "moe-ep"])
     ap.add_argument("--layers", type=int, default=48, help="layers (48 = the model; fewer = a small ncu case)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--cache-frac", type=float, default=0.4,
@@ -60,7 +61,7 @@ def parse():
 
 
 def metric_name(a):
-    return "decode tok/s" if a.workload == "decoder" else "moe decode tok/s"
+    return {"decoder": "decode tok/s", "moe-stack": "moe decode tok/s", "moe-ep": "batched moe tok/s"}[a.workload]
 
 
 def workload_config(a, n):
@@ -79,6 +80,18 @@ def workload_config(a, n):
             "seq_len": a.prompt,
             "parallelism": "replicas" if n > 1 else "single",
             "l2": "working set 3.4 GB/token >> 126 MB L2; no flush",
+        }
+    if a.workload == "moe-ep":
+        return {
+            "workload": f"qwen3-30b-a3b batched moe stack (config 4 MoE): {EP_BATCH} tokens in total, {L} layers x {E} "
+            f"experts top-{K_TOP}, Zipf(1.1) expert popularity, {a.bits}-bit g{G}, experts sharded expert-parallel "
+            f"over {n} GPU(s) ({E // n} per layer each), NCCL all-to-all dispatch and combine, rmsnorm+residual "
+            "between layers (no attention)",
+            "model": "Qwen3-30B-A3B-shaped (random init)",
+            "global_batch": EP_BATCH,
+            "seq_len": 1,
+            "parallelism": f"ep{n}",
+            "l2": "expert working set per layer >> 126 MB L2; no flush",
         }
     return {
         "workload": f"qwen3-30b-a3b moe stack: {L} layers x {E} experts, top-{K_TOP}, bs=1, {a.bits}-bit g{G}, "
@@ -332,8 +345,34 @@ def cpu_head_sample(seed=0, frac=16):
     return dt * frac
 
 
-def cpu_tok_s(a, seed=0):
+def cpu_ep_tok_s(a, seed=0, distinct=60.0, sample_experts=4):
+    """Batched tokens/s of the CPU path: the oracle's per-expert cost (dequantize + fp32 MLP for the
+    average number of tokens an expert receives), measured on a few experts, times the distinct experts
+    of a layer, times L, for EP_BATCH tokens."""
+    import numpy as np
+
+    from oracle import wisp_oracle as O
+
+    rng = np.random.default_rng(seed)
+    n = H * I
+    toks = max(1, int(round(EP_BATCH * K_TOP / distinct)))
+    pool = np.stack([O.quantize((rng.standard_normal((3, n)) * 0.02).astype(np.float32), a.bits, G) for _ in range(sample_experts)])
+    x = rng.standard_normal((toks, H)).astype(np.float32)
+    t0 = time.perf_counter()
+    for j in range(sample_experts):
+        gm, um, dm = O.expert_weights(pool, j, n, a.bits, G, H, I)
+        y = (O.silu(x @ gm.T) * (x @ um.T)) @ dm.T
+    per_expert = (time.perf_counter() - t0) / sample_experts
+    assert np.isfinite(y).all()
+    step = per_expert * distinct * L
+    return EP_BATCH / step, 1, (f"oracle per-expert cost (dequantize + fp32 MLP of {toks} tokens) on {sample_experts} "
+                               f"experts x {distinct:.0f} distinct experts per layer x {L} layers, {EP_BATCH} tokens per step")
+
+
+def cpu_tok_s(a, seed=0, distinct=60.0):
     """Tokens/s of the CPU path, extrapolated from one sampled layer (x L) and a sampled lm_head."""
+    if a.workload == "moe-ep":
+        return cpu_ep_tok_s(a, seed, distinct)
     if a.workload == "decoder":
         dt, threads = cpu_layer_sample(a.bits, seed=seed, attention=True, context=a.prompt)
         return 1.0 / (dt * L + cpu_head_sample(seed)), threads, (
@@ -584,6 +623,75 @@ class DecodeBench:
 
 
 # ------------------------------------------------------------------------------------------------
+# moe-ep workload (config 4 MoE part, strong scaling over the ranks)
+# ------------------------------------------------------------------------------------------------
+class EPStack:
+    """EP_BATCH tokens through the MoE layers with the experts sharded over the ranks; each rank keeps
+    EP_BATCH / world tokens.  Routing: seeded logits biased to Zipf(1.1) popularity, softmax top-8."""
+
+    def __init__(self, a, device, rank, world):
+        import torch
+
+        from wisp import kernels, quant
+        from wisp.ep import ExpertParallelMoE, batched_expert_fn
+
+        assert EP_BATCH % world == 0 and E % world == 0
+        self.N, self.El = EP_BATCH // world, E // world
+        n = H * I
+        self.nb = quant.expert_nbytes(n, a.bits, G)
+        # this rank's experts of every layer: slot l * El + e holds expert rank*El + e of layer l
+        self.pool = torch.empty((L * self.El, self.nb), dtype=torch.uint8, device=device)
+        gen = torch.Generator(device=device).manual_seed(1000 + rank)
+        for l in range(L):
+            w3 = (torch.randn(self.El, 3, n, device=device, generator=gen) * 0.02).to(torch.bfloat16)
+            self.pool[l * self.El : (l + 1) * self.El].copy_(quant.quantize_batch(w3, a.bits, G))
+            del w3
+        g = torch.Generator(device=device).manual_seed(7)  # the same routing tables on every rank
+        rank_pop = torch.randperm(E, device=device, generator=g).float() + 1
+        bias = torch.log(rank_pop ** -1.1)
+        logits = torch.randn(L, EP_BATCH, E, device=device, generator=g) + bias
+        p = torch.softmax(logits.to(torch.bfloat16).float(), -1)
+        rw, sel = torch.topk(p, K_TOP, -1)
+        rw = (rw / rw.sum(-1, keepdim=True)).to(torch.bfloat16).float()
+        lo = rank * self.N
+        self.sel, self.rw = sel[:, lo : lo + self.N].contiguous(), rw[:, lo : lo + self.N].contiguous()
+        self.distinct = float(torch.tensor([len(torch.unique(sel[l])) for l in range(L)]).float().mean())
+        self.norm_w = (1.0 + 0.1 * torch.randn(L, H, device=device, generator=g)).to(torch.bfloat16)
+        self.x0 = torch.randn(self.N, H, device=device, generator=gen).to(torch.bfloat16)
+        fn = batched_expert_fn(self.pool, lambda l, e: l * self.El + e, n, H, I, a.bits, G)
+        self.ep = ExpertParallelMoE(E, K_TOP, H, self.N, fn, device=device)
+        self.h = torch.empty(self.N, H, dtype=torch.bfloat16, device=device)
+        self.xn = torch.empty_like(self.h)
+        self.kernels = kernels
+
+    def launches_per_step(self):
+        return L * 5  # rmsnorm + the batched MoE's group, gate/up, down, combine per layer
+
+    def step(self, t):
+        self.h.copy_(self.x0)
+        for l in range(L):
+            self.kernels.rmsnorm(self.h, self.norm_w[l], 1e-6, out=self.xn)
+            self.h.add_(self.ep.forward(self.xn, self.sel[l], self.rw[l], layer=l))
+
+    def e2e_inputs(self):
+        import torch
+
+        return self.x0.cpu().pin_memory(), torch.empty(self.N, H, dtype=torch.bfloat16).pin_memory()
+
+    def step_e2e(self, t, inp):
+        x_host, out_host = inp
+        self.x0.copy_(x_host, non_blocking=True)
+        self.step(t)
+        out_host.copy_(self.h, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.N * H * 2, self.N * H * 2
+
+    def release(self):
+        pass
+
+
+# ------------------------------------------------------------------------------------------------
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -604,6 +712,9 @@ def main():
     if a.workload == "decoder":
         bench = DecodeBench(a, dev, seed=rank)
         pool, nbytes = bench.pool()
+    elif a.workload == "moe-ep":
+        bench = EPStack(a, dev, rank, world)
+        pool, nbytes = bench.pool, bench.nb
     else:
         W = build_moe_workload(a.bits, dev, seed=rank)
         bench = MoEStack(W)
@@ -648,7 +759,7 @@ def main():
     clk = clocks.stop()
     if a.workload == "decoder" and bench.paged:
         paging = bench.paging_stats(a.warmup + 2 * a.steps + 3)
-    roof, _ = moe_roofline(pool, nbytes, a.bits)
+    roof, _ = moe_roofline(pool, nbytes, a.bits) if pool.shape[0] >= K_TOP * L else (None, None)
     if a.workload == "decoder":
         ctx = bench.dec.pos + a.warmup + 2 * a.steps + 3  # context length at the end of the timed steps
         roof["step_bytes_per_token"] = bench.bytes_per_token(ctx)
@@ -658,8 +769,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = t.tolist()
     if rank == 0:
-        cpu_v, cores, sample = cpu_tok_s(a)
-        tok = a.steps * world
+        cpu_v, cores, sample = cpu_tok_s(a, distinct=bench.distinct if a.workload == "moe-ep" else 60.0)
+        tok = a.steps * (EP_BATCH if a.workload == "moe-ep" else world)
         h2d, d2h = bench.e2e_bytes()
         line = {
             "metric": metric_name(a),
@@ -670,7 +781,7 @@ def main():
             "warmup": a.warmup,
             "ms_per_step": ms / a.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if a.workload == "moe-ep" else "weak",
             "vs_baseline": None,
             "dtype": f"u{a.bits}->f32 experts, bf16 dense",
             "data": "synthetic",
@@ -683,6 +794,10 @@ def main():
         }
         if a.workload == "decoder" and bench.paged:
             line["paging"] = paging
+        if a.workload == "moe-ep":
+            line["distinct_experts_per_layer"] = bench.distinct
+            # expert bytes each GPU streams per layer (its share of the distinct experts) per layer time
+            line["ep_weight_gbs_per_gpu"] = bench.distinct / world * nbytes / (ms / a.steps / L * 1e-3) / 1e9
         print(json.dumps(line), flush=True)
     bench.release()
     if world > 1:

@@ -114,8 +114,8 @@ int64_t wisp_moe_batched_workspace_bytes(int N, int k, int64_t H, int64_t I);
  * out[t] = sum_j w[t,j] * Wd_j (silu(Wg_j x_t) * (Wu_j x_t)).  The (token, choice) pairs are grouped by
  * slot on the device, so each routed expert's weights are read once per call; the products run on the
  * tensor cores with the weights dequantized bit-exactly to bf16 (q*s + m).  bits 8/4/3/2, H and I
- * multiples of 128, group a multiple of 32; workspace 256-byte aligned, of the size above.  Invalid
- * slots are skipped and flagged.
+ * multiples of 128, group a multiple of 32; workspace 256-byte aligned, of the size above.  A slot of
+ * -1 marks an empty pair (contributes nothing); other invalid slots are skipped and flagged.
  * Replaces the reference's bs > 1 MoE (wisp/moe.py:62-137: unique experts, dequant, per-expert MLP,
  * weighted index_add). */
 int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,

@@ -112,8 +112,10 @@ def test_invalid_slot_skipped_and_flagged():
     x = torch.randn(3, H, device="cuda", generator=gen).to(torch.bfloat16)
     meta = torch.tensor([[0, 1, 0.5, 0.5], [2, 99, 0.5, 0.5], [3, -1, 0.5, 0.5]], dtype=torch.float32, device="cuda")
     _lib.device_status(0, clear=True)
+    kernels.moe_batched(pool, meta[2:].contiguous(), x[2:].contiguous(), k, n, H, I, bits, G)
+    assert _lib.device_status(0) == 0  # -1: an empty pair, not an error
     out = kernels.moe_batched(pool, meta, x, k, n, H, I, bits, G)
-    assert _lib.device_status(0) & _lib.STATUS_BAD_SLOT
+    assert _lib.device_status(0) & _lib.STATUS_BAD_SLOT  # 99: out of range
     sel = np.array([[0, 1], [2, 2], [3, 3]])
     rw = np.array([[0.5, 0.5], [0.5, 0.0], [0.5, 0.0]], np.float32)
     want = O.moe_batched_ref(pool.cpu().numpy(), sel, rw, _np(x), n, H, I, bits, G)

@@ -59,7 +59,8 @@ __host__ __device__ inline Ws ws_carve(void* base, int P, int64_t I) {
 }
 
 // ---- grouping ---------------------------------------------------------------------------------------
-// One CTA of 1024 threads.  Key = slot << 32 | pair; invalid slots sort last and are skipped (flagged).
+// One CTA of 1024 threads.  Key = slot << 32 | pair; invalid slots sort last and are skipped (flagged,
+// except -1, which marks an empty pair such as the padding of an expert-parallel dispatch buffer).
 __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {
   __shared__ unsigned long long key[MAX_PAIRS];
   __shared__ int scan[MAX_PAIRS];
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ m
       const float f = meta[int64_t(t) * 2 * k + j];
       if (f >= 0.0f && f < float(nslots)) kk = (static_cast<unsigned long long>(int64_t(f)) << 32) | unsigned(i);
       else {
-        flag(WISP_STATUS_BAD_SLOT);
+        if (f != -1.0f) flag(WISP_STATUS_BAD_SLOT);  // -1: an empty pair (padding), skipped silently
         kk = (0xFFFFFFFFull << 32) | unsigned(i);
       }
     }
