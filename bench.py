@@ -667,11 +667,30 @@ class EPStack:
     def launches_per_step(self):
         return L * 5  # rmsnorm + the batched MoE's group, gate/up, down, combine per layer
 
-    def step(self, t):
+    def _body(self):
         self.h.copy_(self.x0)
         for l in range(L):
             self.kernels.rmsnorm(self.h, self.norm_w[l], 1e-6, out=self.xn)
             self.h.add_(self.ep.forward(self.xn, self.sel[l], self.rw[l], layer=l))
+
+    def capture(self):
+        """The whole step (all layers, NCCL exchanges included) as one CUDA graph."""
+        import torch
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        torch.cuda.synchronize()
+
+    def step(self, t):
+        self.graph.replay()
 
     def e2e_inputs(self):
         import torch
@@ -688,7 +707,7 @@ class EPStack:
         return self.N * H * 2, self.N * H * 2
 
     def release(self):
-        pass
+        self.graph = None  # graphs holding NCCL calls go before the process group
 
 
 # ------------------------------------------------------------------------------------------------
@@ -714,6 +733,7 @@ def main():
         pool, nbytes = bench.pool()
     elif a.workload == "moe-ep":
         bench = EPStack(a, dev, rank, world)
+        bench.capture()
         pool, nbytes = bench.pool, bench.nb
     else:
         W = build_moe_workload(a.bits, dev, seed=rank)

@@ -39,6 +39,7 @@ class ExpertParallelMoE:
         self.send_id = torch.full((W, C), -1.0, dtype=torch.float32, device=device)
         self.recv_id = torch.full_like(self.send_id, -1.0)
         self.y_back = torch.zeros_like(self.send_x)
+        self.ranks = torch.arange(W, device=device)
 
     def _a2a(self, out, inp):
         if self.world == 1:
@@ -53,7 +54,7 @@ class ExpertParallelMoE:
         P = N * k
         dest = (sel // self.E_local).reshape(P)
         local = (sel - dest.view(N, k) * self.E_local).reshape(P).to(torch.float32)
-        onehot = torch.nn.functional.one_hot(dest, W)  # [P, W]
+        onehot = (dest[:, None] == self.ranks[None, :]).to(torch.int64)  # [P, W], no host-side checks
         pos = (torch.cumsum(onehot, 0) - 1).gather(1, dest[:, None])[:, 0]  # rank of the pair in its bucket
         tok = torch.arange(P, device=x.device) // k
         # 1-2. dispatch
