@@ -11,8 +11,8 @@
 // products are the plain dot products.
 //
 //   group_kernel    sort the N*k pairs by slot (bitonic, one CTA): groups (slot, start, count)
-//   gate_up_kernel  per (group, 16 rows of I): a = silu(Wg x) * (Wu x) for the group's tokens, bf16
-//   down_kernel     per (group, 16 rows of H): y = Wd a, fp32
+//   grouped_kernel<0>  per (group, 128 rows of I): a = silu(Wg x) * (Wu x) for the group's tokens, bf16
+//   grouped_kernel<2>  per (group, 128 rows of H): y = Wd a, fp32
 //   combine_kernel  out[t] = bf16(sum_j w[t,j] * y[t,j]) in a fixed order
 #pragma once
 #include "common.cuh"
@@ -160,49 +160,93 @@ __device__ __forceinline__ void row_unit(const uint8_t* base, const MoeShape& S,
   dequant_unit<BITS>(u, s, m, pr);
 }
 
-// ---- gate/up: a[pos][r] = bf16(silu(Wg[r] . x_t) * (Wu[r] . x_t)) ---------------------------------------
-template <int BITS>
-__global__ void __launch_bounds__(THREADS) gate_up_kernel(const uint8_t* __restrict__ pool, MoeShape S,
-                                                          const uint16_t* __restrict__ x, Ws W) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+// ---- the grouped products -----------------------------------------------------------------------------
+// A CTA takes one group (expert) and 8 tiles of 16 rows (one per warp) of the output matrix; the
+// activation rows of the group's tokens (up to TOK per pass) are staged once in shared memory (rows
+// padded by 4 elements: the fragment loads stay within two-way bank conflicts) and every warp streams
+// its rows' weight units from HBM, the next K block's units loaded while the current one computes.
+constexpr int TOK = 8 * NT_MAX;  // tokens per pass
+constexpr int ROWS_PER_CTA = 16 * WARPS;
+
+__host__ __device__ inline int64_t stage_bytes(int64_t K) { return int64_t(TOK) * (K + 4) * 2; }
+
+// MAT 0: gate and up (rows of I, K = H, input x of the tokens) -> a = bf16(silu(g) * u)
+// MAT 2: down (rows of H, K = I, input a of the pairs) -> y (fp32)
+template <int BITS, int MAT>
+__global__ void __launch_bounds__(THREADS, 1) grouped_kernel(const uint8_t* __restrict__ pool, MoeShape S,
+                                                             const uint16_t* __restrict__ x, Ws W) {
+  extern __shared__ __align__(16) uint16_t xs[];  // [TOK][K + 4]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   pdl_wait();
   pdl_launch_dependents();
   const int ngr = W.n_groups[0];
-  const int tiles = S.I / 16;
-  const int64_t nunits = int64_t(ngr) * tiles;
-  const int gw = blockIdx.x * WARPS + (threadIdx.x >> 5), nw = gridDim.x * WARPS;
-  for (int64_t u = gw; u < nunits; u += nw) {
-    const int grp = int(u / tiles), tile = int(u - int64_t(grp) * tiles);
+  const int64_t rows = MAT == 0 ? S.I : S.H;
+  const int64_t K = MAT == 0 ? S.H : S.I;
+  const int64_t KP = K + 4;
+  const int chunks = int((rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA);
+  for (int64_t u = blockIdx.x; u < int64_t(ngr) * chunks; u += gridDim.x) {
+    const int grp = int(u / chunks), ch = int(u - int64_t(grp) * chunks);
     const uint8_t* base = pool + int64_t(W.grp_slot[grp]) * S.nbytes;
     const int start = W.grp_start[grp], cnt = W.grp_count[grp];
-    const int r0 = tile * 16;
-    for (int t0 = 0; t0 < cnt; t0 += 8 * NT_MAX) {
-      // the B column (token) each lane feeds for each n-tile: lane g' -> token of position t0 + 8 nt + g'
-      const uint16_t* xrow[NT_MAX];
-#pragma unroll
-      for (int nt = 0; nt < NT_MAX; ++nt) {
-        const int p = t0 + 8 * nt + g;
-        xrow[nt] = p < cnt ? x + int64_t(W.order[start + p] / S.k) * S.H : nullptr;
+    const int64_t r0 = int64_t(ch) * ROWS_PER_CTA + 16 * warp;
+    const bool active = r0 < rows;  // warp-uniform
+    for (int t0 = 0; t0 < cnt; t0 += TOK) {
+      const int nt_used = (cnt - t0 + 7) / 8 < NT_MAX ? (cnt - t0 + 7) / 8 : NT_MAX;
+      // ---- stage the activation rows of tokens [t0, t0 + TOK) (zeros past the group)
+      __syncthreads();  // the previous pass's readers are done
+      for (int64_t i = threadIdx.x; i < int64_t(TOK) * (K / 8); i += blockDim.x) {
+        const int t = int(i / (K / 8));
+        const int64_t cp = i - int64_t(t) * (K / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t0 + t < cnt) {
+          const uint16_t* src = MAT == 0 ? x + int64_t(W.order[start + t0 + t] / S.k) * S.H : W.a + int64_t(start + t0 + t) * S.I;
+          v = reinterpret_cast<const uint4*>(src)[cp];
+        }
+        uint2* d = reinterpret_cast<uint2*>(xs + int64_t(t) * KP + cp * 8);  // KP % 4 == 0: 8-byte aligned
+        d[0] = make_uint2(v.x, v.y);
+        d[1] = make_uint2(v.z, v.w);
       }
-      float dg[NT_MAX][4] = {}, du[NT_MAX][4] = {};
-      for (int64_t kb = 0; kb < S.H; kb += 128) {
+      __syncthreads();
+      if (!active) continue;
+      float d0[NT_MAX][4] = {}, d1[NT_MAX][4] = {};
+      // weight units of the current K block (cur) and the next one (nxt)
+      Unit<BITS> cu[4], nu[4];
+      float csc[4], cmn[4], nsc[4], nmn[4];
+      auto fetch = [&](int64_t kb, Unit<BITS> (&uu)[4], float (&sc)[4], float (&mn)[4]) {
+#pragma unroll
+        for (int q = 0; q < (MAT == 0 ? 4 : 2); ++q) {
+          const int mat = MAT == 0 ? (q >> 1) : 2;
+          const int64_t row = r0 + g + (q & 1) * 8;
+          const int64_t e = int64_t(mat) * S.H * S.I + row * K + kb + 32 * c;
+          uu[q] = load_unit<BITS>(base + e * BITS / 8);
+          const int64_t gi = e / S.group;
+          sc[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + gi));
+          mn[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + S.ng + gi));
+        }
+      };
+      fetch(0, cu, csc, cmn);
+      for (int64_t kb = 0; kb < K; kb += 128) {
+        if (kb + 128 < K) fetch(kb + 128, nu, nsc, nmn);
+        uint32_t pa[4][16];
+#pragma unroll
+        for (int q = 0; q < (MAT == 0 ? 4 : 2); ++q) dequant_unit<BITS>(cu[q], csc[q], cmn[q], pa[q]);
         const int64_t kc = kb + 32 * c;
-        uint32_t ga[16], gb[16], ua[16], ub[16];
-        row_unit<BITS>(base, S, 0, r0 + g, S.H, kc, ga);
-        row_unit<BITS>(base, S, 0, r0 + g + 8, S.H, kc, gb);
-        row_unit<BITS>(base, S, 1, r0 + g, S.H, kc, ua);
-        row_unit<BITS>(base, S, 1, r0 + g + 8, S.H, kc, ub);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
 #pragma unroll
           for (int nt = 0; nt < NT_MAX; ++nt) {
-            if (8 * nt < cnt - t0) {  // warp-uniform
-              uint2 b = make_uint2(0, 0);
-              if (xrow[nt]) b = *reinterpret_cast<const uint2*>(xrow[nt] + kc + 4 * s);
-              mma16816(dg[nt], ga[2 * s], gb[2 * s], ga[2 * s + 1], gb[2 * s + 1], b.x, b.y);
-              mma16816(du[nt], ua[2 * s], ub[2 * s], ua[2 * s + 1], ub[2 * s + 1], b.x, b.y);
+            if (nt < nt_used) {  // warp-uniform
+              const uint2 bb = *reinterpret_cast<const uint2*>(xs + int64_t(8 * nt + g) * KP + kc + 4 * s);
+              mma16816(d0[nt], pa[0][2 * s], pa[1][2 * s], pa[0][2 * s + 1], pa[1][2 * s + 1], bb.x, bb.y);
+              if (MAT == 0) mma16816(d1[nt], pa[2][2 * s], pa[3][2 * s], pa[2][2 * s + 1], pa[3][2 * s + 1], bb.x, bb.y);
             }
           }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          cu[q] = nu[q];
+          csc[q] = nsc[q];
+          cmn[q] = nmn[q];
         }
       }
       // D: rows r0 + g (d0, d1) and r0 + g + 8 (d2, d3), token columns 2c, 2c + 1 of each n-tile
@@ -211,61 +255,11 @@ __global__ void __launch_bounds__(THREADS) gate_up_kernel(const uint8_t* __restr
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int p = t0 + 8 * nt + 2 * c + (q & 1);
-          const int r = r0 + g + (q >> 1) * 8;
-          if (p < cnt) W.a[int64_t(start + p) * S.I + r] = f32_to_bf16(silu_mul(dg[nt][q], du[nt][q]));
-        }
-      }
-    }
-  }
-}
-
-// ---- down: y[pos][h] = Wd[h] . a[pos] --------------------------------------------------------------------
-template <int BITS>
-__global__ void __launch_bounds__(THREADS) down_kernel(const uint8_t* __restrict__ pool, MoeShape S, Ws W) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  pdl_wait();
-  pdl_launch_dependents();
-  const int ngr = W.n_groups[0];
-  const int tiles = S.H / 16;
-  const int64_t nunits = int64_t(ngr) * tiles;
-  const int gw = blockIdx.x * WARPS + (threadIdx.x >> 5), nw = gridDim.x * WARPS;
-  for (int64_t u = gw; u < nunits; u += nw) {
-    const int grp = int(u / tiles), tile = int(u - int64_t(grp) * tiles);
-    const uint8_t* base = pool + int64_t(W.grp_slot[grp]) * S.nbytes;
-    const int start = W.grp_start[grp], cnt = W.grp_count[grp];
-    const int r0 = tile * 16;
-    for (int t0 = 0; t0 < cnt; t0 += 8 * NT_MAX) {
-      const uint16_t* arow[NT_MAX];
-#pragma unroll
-      for (int nt = 0; nt < NT_MAX; ++nt) {
-        const int p = t0 + 8 * nt + g;
-        arow[nt] = p < cnt ? W.a + int64_t(start + p) * S.I : nullptr;
-      }
-      float d[NT_MAX][4] = {};
-      for (int64_t kb = 0; kb < S.I; kb += 128) {
-        const int64_t kc = kb + 32 * c;
-        uint32_t wa[16], wb[16];
-        row_unit<BITS>(base, S, 2, r0 + g, S.I, kc, wa);
-        row_unit<BITS>(base, S, 2, r0 + g + 8, S.I, kc, wb);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-#pragma unroll
-          for (int nt = 0; nt < NT_MAX; ++nt) {
-            if (8 * nt < cnt - t0) {
-              uint2 b = make_uint2(0, 0);
-              if (arow[nt]) b = *reinterpret_cast<const uint2*>(arow[nt] + kc + 4 * s);
-              mma16816(d[nt], wa[2 * s], wb[2 * s], wa[2 * s + 1], wb[2 * s + 1], b.x, b.y);
-            }
+          const int64_t r = r0 + g + (q >> 1) * 8;
+          if (p < cnt) {
+            if (MAT == 0) W.a[int64_t(start + p) * S.I + r] = f32_to_bf16(silu_mul(d0[nt][q], d1[nt][q]));
+            else W.y[int64_t(start + p) * S.H + r] = d0[nt][q];
           }
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT_MAX; ++nt) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int p = t0 + 8 * nt + 2 * c + (q & 1);
-          const int r = r0 + g + (q >> 1) * 8;
-          if (p < cnt) W.y[int64_t(start + p) * S.H + r] = d[nt][q];
         }
       }
     }

@@ -380,9 +380,10 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   const int grid = num_sms();
   cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
-#define WISP_BATCHED(B)                                                                                     \
-  e = launch_pdl(batched::gate_up_kernel<B>, grid, batched::THREADS, 0, s, pool, S, x, W);                  \
-  if (e == cudaSuccess) e = launch_pdl(batched::down_kernel<B>, grid, batched::THREADS, 0, s, pool, S, W);
+  const size_t sm_gu = size_t(batched::stage_bytes(H)), sm_dn = size_t(batched::stage_bytes(I));
+#define WISP_BATCHED(B)                                                                                                \
+  if (e == cudaSuccess) e = launch_pdl(batched::grouped_kernel<B, 0>, grid, batched::THREADS, sm_gu, s, pool, S, x, W); \
+  if (e == cudaSuccess) e = launch_pdl(batched::grouped_kernel<B, 2>, grid, batched::THREADS, sm_dn, s, pool, S, x, W);
   switch (bits) {
     case 8: WISP_BATCHED(8) break;
     case 4: WISP_BATCHED(4) break;
