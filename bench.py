@@ -53,7 +53,11 @@ def parse():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--cache-frac", type=float, default=0.4,
                     help="decoder: fraction of the L*E experts resident in the GPU slot pool (config 3: 0.4; 1 = all)")
-    ap.add_argument("--no-prefetch", action="store_true", help="paged decoder: no next-layer expert prefetch")
+    ap.add_argument("--paging", default="device", choices=["device", "host"],
+                    help="decoder with a capped cache: device slot table, misses read from the pinned host store by "
+                    "the MoE kernels, page-ins one token behind (device), or the reference's per-layer host "
+                    "decision with page-in before use (host)")
+    ap.add_argument("--no-prefetch", action="store_true", help="host paging: no next-layer expert prefetch")
     a = ap.parse_args()
     global L
     L = a.layers
@@ -67,14 +71,21 @@ def metric_name(a):
 def workload_config(a, n):
     if a.workload == "decoder":
         paged = a.cache_frac < 1.0
-        res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU, pinned host store, "
-               f"cudaMemcpyAsync on a side stream{'' if a.no_prefetch else ', next-layer prefetch'})" if paged
-               else "all experts resident")
+        if not paged:
+            res, graph = "all experts resident", "(whole-token CUDA graph)"
+        elif a.paging == "device":
+            res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU; residency in a device slot "
+                   "table, non-resident experts read by the MoE kernels from the pinned host store, page-ins decided "
+                   "one token behind and copied with cudaMemcpyAsync on a side stream)")
+            graph = "(whole-token CUDA graph)"
+        else:
+            res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU, pinned host store, "
+                   f"per-layer host decision, cudaMemcpyAsync on a side stream{'' if a.no_prefetch else ', next-layer prefetch'})")
+            graph = "(one CUDA graph per layer segment)"
         return {
             "workload": f"qwen3-30b-a3b greedy decode bs=1: {L} layers, 32q/4kv heads x 128, {E} experts top-{K_TOP}, "
             f"{a.bits}-bit g{G} experts, {res}, bf16 attention/embeddings, vocab {VOCAB}, "
-            f"{a.prompt}-token seeded prompt then one token per step "
-            + ("(one CUDA graph per layer segment)" if paged else "(whole-token CUDA graph)"),
+            f"{a.prompt}-token seeded prompt then one token per step " + graph,
             "model": "Qwen3-30B-A3B-shaped (random init)",
             "global_batch": n,
             "seq_len": a.prompt,
@@ -537,13 +548,14 @@ class DecodeBench:
     def __init__(self, a, device, seed):
         import torch
 
-        from wisp.graphdec import GraphDecoder, PagedGraphDecoder
+        from wisp.graphdec import DevicePagedDecoder, GraphDecoder, PagedGraphDecoder
         from wisp.model import DecoderConfig, DecoderWeights
 
         cfg = DecoderConfig(layers=L, bits=a.bits)
         self.w = DecoderWeights.random(cfg, device=device, seed=seed)
         need = a.prompt + 2 * (a.warmup + a.steps) + 16
         self.paged = a.cache_frac < 1.0
+        self.device_paged = self.paged and a.paging == "device"
         if self.paged:
             from wisp.cache import ExpertCache
             from wisp.store import ExpertStore
@@ -552,7 +564,10 @@ class DecodeBench:
             self.w.pool = None  # only the capped slot pool stays on the device
             torch.cuda.empty_cache()
             self.cache = ExpertCache(store, nslots=int(a.cache_frac * L * E), device=device)
-            self.dec = PagedGraphDecoder(self.w, self.cache, tmax=need, prefetch=not a.no_prefetch)
+            if self.device_paged:
+                self.dec = DevicePagedDecoder(self.w, self.cache, tmax=need)
+            else:
+                self.dec = PagedGraphDecoder(self.w, self.cache, tmax=need, prefetch=not a.no_prefetch)
         else:
             self.dec = GraphDecoder(self.w, tmax=need)
         g = torch.Generator(device=device).manual_seed(seed)
@@ -563,6 +578,8 @@ class DecodeBench:
         self.dec.ctl[1].fill_(self.dec.pos)
         if self.paged:
             self.stats0 = dict(self.cache.stats), self.cache.bytes_h2d
+        if self.device_paged:
+            self.reads0 = self.dec.host_reads_total()
 
     def launches_per_step(self):
         return self.dec.kernels_per_step()  # embed; per layer 3 GEMVs, attention, top-k, MoE x2; lm_head; argmax x2
@@ -570,7 +587,9 @@ class DecodeBench:
     def step(self, t):
         """One generated token: the step graph plus the on-device token/position update (paged: the
         L + 1 segments with the host's paging decisions between them)."""
-        if self.paged:
+        if self.device_paged:
+            self.dec.step_greedy()
+        elif self.paged:
             self.dec.next(self.dec.next_token)
         else:
             self.dec.greedy_graph.replay()
@@ -584,7 +603,10 @@ class DecodeBench:
         """Public-API step from host buffers: the token H2D, one decode step (which also advances the
         position), the next token D2H."""
         tok_host, out_host = inp
-        if self.paged:
+        if self.device_paged:
+            self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
+            self.dec.step_greedy()
+        elif self.paged:
             self.dec.next(tok_host.to(self.dec.dev, non_blocking=True))
         else:
             self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
@@ -603,15 +625,19 @@ class DecodeBench:
         st0, b0 = self.stats0
         st = self.cache.stats
         hits, misses = st["hits"] - st0["hits"], st["misses"] - st0["misses"]
-        return {
+        out = {
             "slots": self.cache.nslots,
             "hit_rate": hits / max(1, hits + misses),
             "h2d_mb_per_token": (self.cache.bytes_h2d - b0) / tokens / 1e6,
+            "mode": "device slot table" if self.device_paged else "per-layer host decision",
         }
+        if self.device_paged:
+            out["host_store_expert_reads_per_token"] = (self.dec.host_reads_total() - self.reads0) / tokens
+        return out
 
     def release(self):
         self.dec.graph = self.dec.greedy_graph = None
-        if self.paged:
+        if self.paged and not self.device_paged:
             self.dec.segs = None
 
     def bytes_per_token(self, ctx):

@@ -105,6 +105,22 @@ int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, 
                            int norm_topk, const int32_t* slot_table, int64_t base, float* row, const uint16_t* x, int64_t H,
                            int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream);
 
+/* wisp_moe_decode_routed over a partially resident expert pool with no host decision: slot_table
+ * (int32 [host_rows], required) maps key = base + e to a slot, or to a negative value when the expert
+ * is not resident; such experts are read by the kernels from store_host, one pinned host allocation of
+ * host_rows * nbytes bytes whose row `key` is that expert (the ExpertStore layout), so the call needs
+ * no synchronisation and a whole decode step stays one CUDA graph.  miss_count (nullable int32 on the
+ * device) is incremented once per expert read from store_host.  The table may be rewritten by
+ * copies on other streams while the call runs: an entry is read once per CTA through L2, and both
+ * sources of an expert hold the same bytes, so either answer is correct.  Replaces the per-layer host
+ * decision of the reference's paged decoder (wisp/graphdec.py:216-235, :296-308: row to the host,
+ * cache.ensure / split, slots into meta) and its hybrid miss path (wisp/moe.py:152-164: misses
+ * computed outside the cache, cache.admit_async, wisp/cache.py:96-104). */
+int wisp_moe_decode_paged(const uint8_t* pool, int64_t nslots, int64_t nbytes, const uint16_t* logits, int E, int k,
+                          int norm_topk, const int32_t* slot_table, int64_t base, const uint8_t* store_host, int64_t host_rows,
+                          int* miss_count, float* row, const uint16_t* x, int64_t H, int64_t I, int bits, int group,
+                          float* scratch, uint16_t* out, void* stream);
+
 /* ---- batched MoE decode ------------------------------------------------------------------------ */
 /* Bytes of the workspace wisp_moe_batched needs for N tokens of k choices (host-only; -1 if N*k is
  * outside [1, 2048]). */

@@ -2,6 +2,7 @@
 (wisp/cache_core.py) -- hits, misses, LRU and frequency eviction, protection of the current request,
 the static region, admission, resize."""
 
+import numpy as np
 import pytest
 
 from wisp.cache_core import CacheCore
@@ -71,3 +72,59 @@ def test_resized_keeps_hottest():
     assert nc.free == [] and nc.key2slot == {2: 0, 4: 1}
     nc2, loads2 = c.resized(6)
     assert len(loads2) == 4 and nc2.free == [5, 4]
+
+
+def _tokens(n, L, E, k, seed):
+    rng = np.random.default_rng(seed)
+    return [[list(rng.choice(E, k, replace=False)) for _ in range(L)] for _ in range(n)]
+
+
+@pytest.mark.parametrize("policy", ["lru"])
+def test_plan_token_follows_per_layer_ensure(policy):
+    """With nothing in flight, the token-level plan makes the same decisions as the reference's
+    per-layer ensure under LRU: same hits, misses, evictions and final residency.  (Under wsa the
+    plan may differ: a page-in issued for an earlier layer of the same token is still in flight, so it
+    is never the victim, while the reference could evict a just-loaded, rarely used key.)"""
+    from wisp.cache import plan_token
+
+    L, E, k = 3, 8, 2
+    a, b = CacheCore(10, policy), CacheCore(10, policy)
+    for rows in _tokens(40, L, E, k, seed=1):
+        evicted, loads = plan_token(a, rows, E, set())
+        want_loads = []
+        for l, row in enumerate(rows):
+            _, ld = b.ensure([l * E + int(e) for e in row])
+            want_loads += ld
+        assert loads == want_loads
+        assert len(evicted) <= len(loads)
+        assert a.key2slot == b.key2slot
+    assert a.stats == b.stats
+
+
+def test_plan_token_never_evicts_busy_slots():
+    from wisp.cache import plan_token
+
+    L, E, k = 2, 16, 4
+    core = CacheCore(8)
+    busy = set()
+    plan_token(core, [[0, 1, 2, 3], [0, 1, 2, 3]], E, busy)
+    assert busy == set(range(8))  # every page-in is in flight
+    before = dict(core.key2slot)
+    evicted, loads = plan_token(core, [[4, 5, 6, 7], [4, 5, 6, 7]], E, busy)
+    assert evicted == [] and loads == []  # nothing admitted, the misses stay host-served
+    assert core.key2slot == before
+    assert core.stats["misses"] == 16
+    busy.clear()
+    evicted, loads = plan_token(core, [[4, 5, 6, 7], [0, 1, 2, 3]], E, busy)
+    assert sorted(k for k, _ in loads) == [4, 5, 6, 7]
+    assert len(evicted) == 4 and all(e < E for e in evicted)  # layer 0's old keys went
+
+
+def test_plan_token_hot_admission():
+    from wisp.cache import plan_token
+
+    core = CacheCore(4, decay=1.0, admit_after=2.0)
+    _, loads = plan_token(core, [[1]], 8, set(), admit="hot")
+    assert loads == []  # seen once
+    _, loads = plan_token(core, [[1]], 8, set(), admit="hot")
+    assert loads == [(1, 0)]  # seen twice: admitted

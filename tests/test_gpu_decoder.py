@@ -178,3 +178,42 @@ def test_paged_decoder_matches_resident(prefetch):
     st = cache.stats
     assert st["misses"] > 0 and st["hits"] + st["misses"] == 8 * cfg.layers * cfg.top_k
     assert cache.bytes_h2d >= st["misses"] * store.nbytes
+
+
+@pytest.mark.parametrize("frac,admit", [(0.4, "all"), (0.1, "all"), (0.4, "hot")])
+def test_device_paged_decoder_matches_resident(frac, admit):
+    """Part of the experts resident, residency in a device slot table, misses read by the MoE kernels
+    from the pinned host store, page-ins published one token behind: the logits are bit-identical to
+    the all-resident decoder's, and after a flush the table, the policy and the slot bytes agree."""
+    from wisp.cache import ExpertCache
+    from wisp.graphdec import DevicePagedDecoder, GraphDecoder
+    from wisp.model import DecoderConfig, DecoderWeights
+    from wisp.store import ExpertStore
+
+    cfg = DecoderConfig(vocab=2000, hidden=2048, layers=3, heads=32, kv_heads=4, head_dim=128, experts=32, top_k=8,
+                        moe_inter=768)
+    w = DecoderWeights.random(cfg, seed=11)
+    store = ExpertStore.from_pool(w.pool, cfg.hidden * cfg.moe_inter, cfg.bits, cfg.group, cfg.layers, cfg.experts)
+    cache = ExpertCache(store, nslots=max(cfg.top_k, int(frac * cfg.layers * cfg.experts)))
+    a = GraphDecoder(w, tmax=128)
+    b = DevicePagedDecoder(w, cache, tmax=128, admit=admit)
+    t = torch.tensor([5], device="cuda")
+    steps = 12
+    for step in range(steps):
+        la = a.next(t).clone()
+        lb = b.next(t)
+        assert torch.equal(la, lb), step
+        t = la.argmax().reshape(1)
+    b.flush()
+    torch.cuda.synchronize()
+    tbl = b.pager.table.cpu()
+    core = cache.core
+    assert int((tbl >= 0).sum()) == len(core.key2slot)
+    for key, slot in core.key2slot.items():
+        assert int(tbl[key]) == slot
+        assert torch.equal(cache.gpu[slot].cpu(), store.host[key]), key
+    st = cache.stats
+    assert st["hits"] + st["misses"] == steps * cfg.layers * cfg.top_k
+    assert st["misses"] > 0 and b.host_reads_total() > 0
+    if admit == "all":
+        assert cache.n_loads > 0

@@ -245,3 +245,55 @@ def test_routed_slot_table_and_missing_slot():
     only = kernels.moe_decode_fast(pool, torch.cat([meta[:1], torch.tensor([-1.0], device="cuda"), w]), x, k, n, H, I, bits)
     _lib.device_status(0, clear=True)
     assert _rel(_bf16_np(got), _bf16_np(only)) < TOL
+
+
+@pytest.mark.parametrize("bits", [4, 3, 2])
+@pytest.mark.parametrize("resident", [0.5, 0.0, 1.0])
+def test_paged_reads_missing_experts_from_host_store(bits, resident):
+    """wisp_moe_decode_paged over a partly resident pool: experts whose table entry is -1 are read
+    from the pinned host store.  Same bytes, same kernels: the output and the routing row are
+    bit-identical to the all-resident routed call, for a layer other than the first (base > 0)."""
+    from wisp import _lib, kernels
+
+    H, I, E, k, L = 2048, 768, 32, 8, 2
+    n = H * I
+    pool, x, _, _ = _setup(bits, H, I, L * E, k, seed=90 + bits)  # rows l*E + e: expert e of layer l
+    host = pool.cpu().pin_memory()
+    g = torch.Generator(device="cuda").manual_seed(bits)
+    gc = torch.Generator().manual_seed(bits)
+    _lib.device_status(0, clear=True)
+    for trial in range(3):
+        logits = (torch.randn(E, device="cuda", generator=g) * 2).to(torch.bfloat16)
+        row_ref = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        ref = kernels.moe_decode_routed(pool, logits, x, k, n, H, I, bits, base=E, row=row_ref)
+        keep = torch.rand(L * E, generator=gc) < resident
+        keys = torch.nonzero(keep).flatten()
+        table = torch.full((L * E,), -1, dtype=torch.int32)
+        table[keys] = torch.arange(keys.numel(), dtype=torch.int32).flip(0)  # scrambled slot order
+        part = torch.zeros(max(1, keys.numel()), pool.shape[1], dtype=torch.uint8, device="cuda")
+        if keys.numel():
+            part[table[keys].long().cuda()] = pool[keys.cuda()]
+        miss = torch.zeros(1, dtype=torch.int32, device="cuda")
+        row = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        got = kernels.moe_decode_paged(part, logits, x, k, n, H, I, bits, slot_table=table.cuda(), base=E,
+                                       store_host=host, miss_count=miss, row=row)
+        assert torch.equal(got, ref), trial
+        assert torch.equal(row, row_ref)
+        chosen = row_ref[:k].long().cpu() + E
+        assert miss.item() == int((~keep[chosen]).sum())
+    assert _lib.device_status(0) == 0
+
+
+def test_paged_rejects_unpinned_store_and_short_table():
+    from wisp import kernels
+
+    H, I, E, k, bits = 2048, 768, 8, 2, 4
+    n = H * I
+    pool, x, _, _ = _setup(bits, H, I, E, k, seed=5)
+    logits = torch.zeros(E, dtype=torch.bfloat16, device="cuda")
+    table = torch.full((E,), -1, dtype=torch.int32, device="cuda")
+    with pytest.raises(kernels.WispError):
+        kernels.moe_decode_paged(pool, logits, x, k, n, H, I, bits, slot_table=table, store_host=pool.cpu())
+    with pytest.raises(kernels.WispError):
+        kernels.moe_decode_paged(pool, logits, x, k, n, H, I, bits, slot_table=table[:4].contiguous(),
+                                 store_host=pool.cpu().pin_memory())

@@ -27,6 +27,13 @@ struct MoeRoute {
   const int32_t* slot_table;  // NULL: slot = base + e
   int64_t base;
   float* row_out;             // nullable: [k experts | k weights], written by CTA 0 of the gate/up grid
+  // Expert paging without a host decision: a negative slot_table entry means "not resident", and
+  // when host_store (a device-accessible pointer to pinned host memory, rows of nbytes, key =
+  // base + e) is given the kernels read that expert's bytes from it instead of from a slot.  The
+  // routing entry then holds -(key + 1).  miss_count (nullable) counts such experts per call.
+  const uint8_t* host_store;
+  int64_t host_rows;
+  int* miss_count;
 };
 
 // All threads of the CTA (blockDim.x >= E, k <= 32): meta[0..2k) in shared memory = [slots | weights];
@@ -63,7 +70,12 @@ __device__ void route_from_logits(const MoeRoute& R, int k, float* meta, float* 
   __syncthreads();
   const float p = e / s;
   if (t < R.E && rank < k) {
-    meta[rank] = float(R.slot_table ? int64_t(R.slot_table[R.base + t]) : R.base + t);
+    float m = float(R.base + t);
+    if (R.slot_table) {  // through L2: the table may be republished by copies on another stream
+      const int32_t s = __ldcg(R.slot_table + R.base + t);
+      m = (s < 0 && R.host_store) ? -float(R.base + t) - 1.0f : float(s);
+    }
+    meta[rank] = m;
     xs[R.E + rank] = float(t);
     xs[R.E + 32 + rank] = p;
   }
@@ -87,6 +99,39 @@ __device__ __forceinline__ bool route_slot(const float* meta, int j, const MoeSh
   if (!(f >= 0.0f) || f >= float(S.nslots)) return false;
   slot = int64_t(f);
   return true;
+}
+
+// Bytes of routed expert j given its routing entry f: slot f of the pool, or row -(f + 1) of the
+// host store (when one is given); NULL when the entry is neither (the expert is skipped and flagged).
+__device__ __forceinline__ const uint8_t* expert_src(float f, const MoeShape& S, const uint8_t* pool, const MoeRoute& RT,
+                                                     bool& host) {
+  host = false;
+  if (f >= 0.0f && f < float(S.nslots)) return pool + int64_t(f) * S.nbytes;
+  if (RT.host_store && f <= -1.0f) {
+    const int64_t key = int64_t(-f) - 1;
+    if (key < RT.host_rows) {
+      host = true;
+      return RT.host_store + key * S.nbytes;
+    }
+  }
+  return nullptr;
+}
+
+// Warp-wide copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory
+// (device or mapped pinned host memory) into shared memory, four 16-byte loads in flight per lane.
+__device__ __forceinline__ void warp_copy_g2s(void* dst, const void* src, int64_t bytes, int lane) {
+  const uint4* s = static_cast<const uint4*>(src);
+  uint4* d = static_cast<uint4*>(dst);
+  const int64_t n = bytes >> 4;
+  int64_t i = lane;
+  for (; i + 96 < n; i += 128) {
+    const uint4 a = s[i], b = s[i + 32], c = s[i + 64], e = s[i + 96];
+    d[i] = a;
+    d[i + 32] = b;
+    d[i + 64] = c;
+    d[i + 96] = e;
+  }
+  for (; i < n; i += 32) d[i] = s[i];
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }

@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     float* rs = reinterpret_cast<float*>(sm + Lg.off_route);
     route_from_logits<true>(RT, S.k, rs, rs + 64, rs + 96);
     mt = rs;
+    if (RT.miss_count && blockIdx.x == 0 && int(threadIdx.x) < S.k && rs[threadIdx.x] <= -1.0f) atomicAdd(RT.miss_count, 1);
   }
 
   // one warp (lanes 0-5) issues block bi into region bi % R: the 8 gate rows and the same 8 up rows
@@ -203,10 +204,22 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int r = bi % R;
     const int blk = b0 + bi;
     const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
-    int64_t slot;
-    const bool ok = route_slot(mt, j, S, slot);
+    bool host;
+    const uint8_t* base = expert_src(mt[j], S, pool, RT, host);
+    const bool ok = base != nullptr;
     uint8_t* reg = sm + int64_t(r) * Lg.region;
     const uint32_t cb = uint32_t(CH * Lg.row_bytes);
+    if (host) {  // not resident: the warp copies the same ranges from the host store, then arrives
+      warp_copy_g2s(reg, base + int64_t(row0) * Lg.row_bytes, cb, lane);
+      warp_copy_g2s(reg + cb, base + S.mat_bytes + int64_t(row0) * Lg.row_bytes, cb, lane);
+      for (int arr = 0; arr < 4; ++arr) {
+        const Win w = window(S.ncode + 2 * ((arr & 1) * S.ng + (arr >> 1) * ngm + int64_t(row0) * Lg.gpr), 2 * CH * Lg.gpr);
+        warp_copy_g2s(reg + 2 * cb + arr * Lg.sc_win, base + w.start, w.bytes, lane);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_expect_tx(&gbar[r], 0);
+      return;
+    }
     if (lane == 0) {
       if (!ok) flag(WISP_STATUS_BAD_SLOT);  // skipped: contributes nothing
       uint32_t tx = 0;
@@ -219,7 +232,6 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     }
     __syncwarp();
     if (ok && lane < 6) {
-      const uint8_t* base = pool + slot * S.nbytes;
       if (lane < 2) {  // 0: gate rows, 1: up rows
         bulk_g2s(reg + lane * cb, base + lane * S.mat_bytes + int64_t(row0) * Lg.row_bytes, cb, &gbar[r]);
       } else {
@@ -242,9 +254,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
     const int64_t gpr_d = S.I / S.group, row_d = int64_t(S.I) * BITS / 8;
     for (int j = lane; j < S.k && h1 > h0; j += 32) {
-      int64_t slot;
-      if (!route_slot(mt, j, S, slot)) continue;
-      const uint8_t* base = pool + slot * S.nbytes;
+      bool host;
+      const uint8_t* base = expert_src(mt[j], S, pool, RT, host);
+      if (!base || host) continue;
       prefetch_l2(base + 2 * S.mat_bytes + int64_t(h0) * row_d, uint32_t(int64_t(h1 - h0) * row_d));
       const int64_t len = 2 * int64_t(h1 - h0) * gpr_d;
       const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * gpr_d), len);
@@ -306,8 +318,8 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
       }
       const int blk = b0 + bi;
       const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
-      int64_t slot;
-      const bool ok = route_slot(mt, j, S, slot);
+      bool host;
+      const bool ok = expert_src(mt[j], S, pool, RT, host) != nullptr;
       const uint32_t sskip = window(S.ncode + 2 * ((sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
       const uint32_t mskip = window(S.ncode + 2 * (S.ng + (sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
       const uint8_t* sw = reg + 2 * cb;
@@ -350,8 +362,8 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const float gs = halves[((bi * NSPLIT) * CH + rw) * 2] + halves[((bi * NSPLIT + 1) * CH + rw) * 2];
     const float us = halves[((bi * NSPLIT) * CH + rw) * 2 + 1] + halves[((bi * NSPLIT + 1) * CH + rw) * 2 + 1];
     const int rr = (b0 + bi) * CH + rw;
-    int64_t slot;
-    a_out[rr] = route_slot(mt, rr / S.I, S, slot) ? silu_mul(gs, us) : 0.0f;
+    bool host;
+    a_out[rr] = expert_src(mt[rr / S.I], S, pool, RT, host) ? silu_mul(gs, us) : 0.0f;
   }
 }
 
@@ -386,19 +398,24 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   }
   // ---- the down rows of every routed expert: one bulk copy of the CTA's contiguous rows plus the
   //      scale and min windows, issued before waiting on the gate/up grid (the routing is final)
+  __shared__ uint32_t host_mask;  // routed experts read from the host store (k <= 32)
   if (warp == 0) {
+    uint32_t hm = 0;
     for (int j = lane; j < S.k; j += 32) {
       mbar_init(&bars[j], 1);
       mbar_fence_init();
       const float f = RT.logits ? mt[j] : __ldcg(meta + j);
-      const bool ok = f >= 0.0f && f < float(S.nslots);
-      const int64_t slot = ok ? int64_t(f) : 0;
-      if (!ok) flag(WISP_STATUS_BAD_SLOT);
-      if (!ok || nrows <= 0) {
+      bool host;
+      const uint8_t* base = expert_src(f, S, pool, RT, host);
+      if (!base) flag(WISP_STATUS_BAD_SLOT);
+      if (!base || nrows <= 0) {
         mbar_expect_tx(&bars[j], 0);
         continue;
       }
-      const uint8_t* base = pool + slot * S.nbytes;
+      if (host) {  // copied below by the whole CTA, which then arrives on the barrier
+        hm |= 1u << j;
+        continue;
+      }
       const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
       const Win wm = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
       const uint32_t cb = uint32_t(int64_t(nrows) * Ld.row_bytes);
@@ -408,6 +425,26 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
       bulk_g2s(dst + 16 * Ld.row_bytes, base + ws.start, ws.bytes, &bars[j]);
       bulk_g2s(dst + 16 * Ld.row_bytes + Ld.sc_win, base + wm.start, wm.bytes, &bars[j]);
     }
+    hm = __reduce_or_sync(0xffffffffu, hm);
+    if (lane == 0) host_mask = hm;
+  }
+  __syncthreads();
+  if (const uint32_t hm = host_mask) {
+    // non-resident experts: the same three ranges from the host store, one warp per (expert, range)
+    const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
+    const Win wm = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
+    for (int task = warp; task < S.k * 3; task += DN_WARPS) {
+      const int j = task / 3, part = task - 3 * j;
+      if (!((hm >> j) & 1u)) continue;
+      bool host;
+      const uint8_t* base = expert_src(RT.logits ? mt[j] : __ldcg(meta + j), S, pool, RT, host);
+      uint8_t* dst = sm + int64_t(j) * Ld.per_expert;
+      if (part == 0) warp_copy_g2s(dst, base + 2 * S.mat_bytes + int64_t(h0) * Ld.row_bytes, int64_t(nrows) * Ld.row_bytes, lane);
+      else if (part == 1) warp_copy_g2s(dst + 16 * Ld.row_bytes, base + ws.start, ws.bytes, lane);
+      else warp_copy_g2s(dst + 16 * Ld.row_bytes + Ld.sc_win, base + wm.start, wm.bytes, lane);
+    }
+    __syncthreads();
+    if (warp == 0 && ((hm >> lane) & 1u)) mbar_expect_tx(&bars[lane], 0);
   }
   for (int i = threadIdx.x; i < DN_WARPS * 16; i += blockDim.x) part[i] = 0.0f;
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(sm + Ld.off_zero)[threadIdx.x] = 0u;
@@ -443,8 +480,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
 
   for (int piece = warp; piece < npieces; piece += DN_WARPS) {
     const int j = piece / NSPLIT, sp = piece % NSPLIT;
-    int64_t slot;
-    const bool ok = route_slot(mt, j, S, slot);
+    bool host;
+    const bool ok = expert_src(mt[j], S, pool, RT, host) != nullptr;
     const float wj = mt[S.k + j];
     if (!ok || nrows <= 0) continue;
     mbar_wait(&bars[j], 0);

@@ -358,6 +358,51 @@ int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, 
   return v4_launch(pool, nullptr, x, S, bits, scratch, out, static_cast<cudaStream_t>(stream), nctas, RT);
 }
 
+// Device address of [p, p + bytes) in pinned host memory, or NULL when the range is not one mapped
+// pinned allocation (the last answer is kept: the decoder asks once before capturing its graph).
+static const uint8_t* mapped_host_range(const uint8_t* p, int64_t bytes) {
+  static std::mutex mu;
+  static const uint8_t *last_p = nullptr, *last_dev = nullptr;
+  static int64_t last_bytes = 0;
+  static int last_device = -1;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (p == last_p && bytes == last_bytes && device == last_device) return last_dev;
+  cudaPointerAttributes a0{}, a1{};
+  if (cudaPointerGetAttributes(&a0, p) != cudaSuccess || cudaPointerGetAttributes(&a1, p + bytes - 1) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (a0.type != cudaMemoryTypeHost || a1.type != cudaMemoryTypeHost || !a0.devicePointer || !a1.devicePointer) return nullptr;
+  const uint8_t* d0 = static_cast<const uint8_t*>(a0.devicePointer);
+  if (static_cast<const uint8_t*>(a1.devicePointer) != d0 + bytes - 1) return nullptr;  // not one contiguous mapping
+  last_p = p, last_bytes = bytes, last_device = device, last_dev = d0;
+  return d0;
+}
+
+int wisp_moe_decode_paged(const uint8_t* pool, int64_t nslots, int64_t nbytes, const uint16_t* logits, int E, int k,
+                          int norm_topk, const int32_t* slot_table, int64_t base, const uint8_t* store_host, int64_t host_rows,
+                          int* miss_count, float* row, const uint16_t* x, int64_t H, int64_t I, int bits, int group,
+                          float* scratch, uint16_t* out, void* stream) {
+  WISP_REQUIRE(logits && slot_table && store_host, "wisp_moe_decode_paged: NULL logits, slot_table or store_host");
+  WISP_REQUIRE(E >= 1 && E <= v4::GU_THREADS && E <= v4::DN_THREADS && k >= 1 && k <= E,
+               "wisp_moe_decode_paged: need 1 <= k <= E <= %d", v4::GU_THREADS);
+  WISP_REQUIRE(base >= 0 && host_rows >= base + E, "wisp_moe_decode_paged: host store of %lld rows has no row %lld",
+               (long long)host_rows, (long long)(base + E - 1));
+  MoeShape S;
+  int rc = moe_shape(pool, nslots, nbytes, reinterpret_cast<const float*>(logits), k, x, H, I, bits, group, scratch, out, S);
+  if (rc) return rc;
+  const int nctas = num_sms();
+  if (!v4_supported(S, bits, nctas))
+    return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_paged: shape not supported by the tensor-core kernels");
+  const uint8_t* hs = mapped_host_range(store_host, host_rows * nbytes);
+  WISP_REQUIRE(hs, "wisp_moe_decode_paged: store_host must be one pinned (page-locked, mapped) host allocation of host_rows * nbytes bytes");
+  WISP_REQUIRE(aligned(hs, 16), "wisp_moe_decode_paged: store_host must be 16-byte aligned");
+  MoeRoute RT{logits, E, norm_topk, slot_table, base, row, hs, host_rows, miss_count};
+  return v4_launch(pool, nullptr, x, S, bits, scratch, out, static_cast<cudaStream_t>(stream), nctas, RT);
+}
+
 int64_t wisp_moe_batched_workspace_bytes(int N, int k, int64_t H, int64_t I) {
   if (N < 1 || k < 1 || int64_t(N) * k > batched::MAX_PAIRS || H <= 0 || I <= 0) return -1;
   return batched::ws_bytes(N * k, H, I);

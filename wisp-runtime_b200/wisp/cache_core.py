@@ -34,6 +34,7 @@ class CacheCore:
         self.tick, self.inc = 0, 1.0
         self.freq = defaultdict(float)
         self.stats = dict(hits=0, misses=0, evictions=0, calls=0)
+        self.last_evicted = None  # key that the last acquire() evicted (None: it took a free slot)
 
     # ---- clock and frequency --------------------------------------------------------------------
     def step(self):
@@ -79,6 +80,7 @@ class CacheCore:
     def acquire(self, key, protected):
         """A slot for ``key``: a free one, else the dynamic slot the policy ranks lowest outside
         ``protected`` (slots the current request already uses)."""
+        self.last_evicted = None
         if self.free:
             s = self.free.pop()
         else:
@@ -91,7 +93,8 @@ class CacheCore:
             if not np.isfinite(rank[j]):
                 raise RuntimeError("no evictable slot: dynamic region smaller than the working request")
             s = base + j
-            del self.key2slot[int(self.slot_key[s])]
+            self.last_evicted = int(self.slot_key[s])
+            del self.key2slot[self.last_evicted]
             self.stats["evictions"] += 1
         self.slot_key[s] = key
         self.key2slot[key] = s

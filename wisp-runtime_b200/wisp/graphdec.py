@@ -24,9 +24,11 @@ from .model import DecoderWeights, rotary_tables
 
 
 class GraphDecoder:
-    def __init__(self, w: DecoderWeights, tmax=2048, use_graph=True, slot_table=None):
+    def __init__(self, w: DecoderWeights, tmax=2048, use_graph=True, slot_table=None, pool=None, store_host=None):
         cfg = w.cfg
         self.w, self.cfg = w, cfg
+        self.pool = w.pool if pool is None else pool
+        self.store_host = store_host  # pinned host store: non-resident experts are read from it
         dev = w.embed.device
         self.dev = dev
         self.L, self.H = cfg.layers, cfg.hidden
@@ -53,6 +55,7 @@ class GraphDecoder:
         self.rows = torch.zeros(self.L, 2 * self.k, dtype=torch.float32, device=dev)  # per layer [experts | weights]
         self.meta = torch.zeros(2 * self.k, dtype=torch.float32, device=dev)
         self.scratch = kernels.moe_scratch(self.k, self.I, dev)
+        self.miss_count = torch.zeros(1, dtype=torch.int32, device=dev) if store_host is not None else None
         self.attn_ws = kernels.attn_workspace(self.Hq, self.Hk, self.D, self.tmax, dev)
         self.argmax_ws = torch.zeros(256, dtype=torch.int64, device=dev)
         self.logits = torch.zeros(cfg.vocab, **d)
@@ -89,9 +92,15 @@ class GraphDecoder:
         # o projection + residual, then post-attention RMSNorm + router
         kernels.gemv(lw["wo"], self.att, res=self.h_emb if first else self.h_res, out=self.h_mid)
         kernels.gemv(lw["router"], self.h_mid, norm_w=lw["post_norm"], eps=c.eps, xn_out=self.xn, out=self.rlog)
-        if self.routed_moe:
+        if self.store_host is not None:
+            kernels.moe_decode_paged(
+                self.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, norm_topk=c.norm_topk,
+                slot_table=self.slot_table, base=l * self.E, store_host=self.store_host, miss_count=self.miss_count,
+                row=self.rows[l], out=self.moe, scratch=self.scratch,
+            )
+        elif self.routed_moe:
             kernels.moe_decode_routed(
-                w.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, norm_topk=c.norm_topk,
+                self.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, norm_topk=c.norm_topk,
                 slot_table=self.slot_table, base=l * self.E, row=self.rows[l], out=self.moe, scratch=self.scratch,
             )
         else:
@@ -99,15 +108,23 @@ class GraphDecoder:
                 self.rlog, self.k, c.norm_topk, slot_table=self.slot_table, base=l * self.E, row=self.rows[l], meta=self.meta
             )
             kernels.moe_decode_fast(
-                w.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
+                self.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group, out=self.moe,
                 scratch=self.scratch,
             )
 
     def _try_routed_moe(self):
         c = self.cfg
+        if self.store_host is not None:  # the paged kernels need the tensor-core path: no fallback
+            kernels.moe_decode_paged(
+                self.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group,
+                norm_topk=c.norm_topk, slot_table=self.slot_table, store_host=self.store_host, out=self.moe,
+                scratch=self.scratch,
+            )
+            torch.cuda.synchronize()
+            return True
         try:
             kernels.moe_decode_routed(
-                self.w.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group,
+                self.pool, self.rlog, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group,
                 norm_topk=c.norm_topk, slot_table=self.slot_table, out=self.moe, scratch=self.scratch,
             )
             torch.cuda.synchronize()
@@ -348,3 +365,69 @@ class PagedGraphDecoder(GraphDecoder):
                 self.evt[l + 1].record()
         self.pos += 1
         return self.logits
+
+
+class DevicePagedDecoder(GraphDecoder):
+    """Decode with only part of the experts resident and no host decision inside a token.
+
+    Residency is a device slot table (``SlotTablePager.table``) read by the MoE kernels; an expert that
+    is not resident is read straight from the pinned host store by the same kernels
+    (wisp_moe_decode_paged), so a whole token -- embed, 48 layers, lm_head, argmax -- is one CUDA graph
+    as in the all-resident decoder.  The cache policy runs one token behind on the host: after token t
+    is replayed, the routing rows of token t-1 (copied to pinned memory when that token ran) go
+    through the policy while the GPU computes token t, and the page-ins it decides are copied on the
+    cache's side stream and published into the table once they have landed.  The reference's paged
+    decoder (wisp/graphdec.py:216-235, :296-308) instead stops at every layer for the host to read the
+    routing, page experts in and write the slots back."""
+
+    def __init__(self, w: DecoderWeights, cache, tmax=2048, admit="all"):
+        from .cache import SlotTablePager
+
+        self.cache = cache
+        self.pager = SlotTablePager(cache, admit)
+        super().__init__(w, tmax=tmax, use_graph=True, slot_table=self.pager.table, pool=cache.gpu,
+                         store_host=cache.store.host)
+        self.rows_host = [torch.zeros(self.L, 2 * self.k, dtype=torch.float32, pin_memory=True) for _ in range(2)]
+        self.turn = 0
+        self.waiting = None  # (rows_host index, event) of the last replayed token, not yet planned
+
+    def _after_replay(self):
+        i = self.turn
+        self.turn ^= 1
+        self.rows_host[i].copy_(self.rows, non_blocking=True)
+        evt = torch.cuda.Event()
+        evt.record()
+        prev, self.waiting = self.waiting, (i, evt)
+        if prev is not None:
+            j, e = prev
+            e.synchronize()  # the token before this one has finished; this one keeps the GPU busy
+            self.pager.apply(self.rows_host[j][:, : self.k].to(torch.int64).tolist())
+
+    @torch.no_grad()
+    def next(self, token):
+        logits = super().next(token)
+        self._after_replay()
+        return logits
+
+    @torch.no_grad()
+    def step_greedy(self):
+        """One greedy token from the device-side token and position (no host input)."""
+        if self.greedy_graph is None:
+            self.capture()
+        self.greedy_graph.replay()
+        self.pos += 1
+        self._after_replay()
+
+    @torch.no_grad()
+    def flush(self):
+        """Run the policy on the last replayed token and wait for every page-in."""
+        if self.waiting is not None:
+            j, e = self.waiting
+            self.waiting = None
+            e.synchronize()
+            self.pager.apply(self.rows_host[j][:, : self.k].to(torch.int64).tolist())
+        self.pager.drain()
+
+    def host_reads_total(self):
+        """Experts read from the host store so far (synchronises)."""
+        return int(self.miss_count.item())

@@ -27,6 +27,7 @@ __all__ = [
     "moe_decode_q2_fast",
     "moe_decode_fast",
     "moe_decode_routed",
+    "moe_decode_paged",
     "moe_batched",
     "moe_gptoss",
     "rope_decode",
@@ -117,6 +118,45 @@ def moe_decode_routed(pool, logits, x, k, n, H, I, bits, group=128, norm_topk=Tr
         "wisp_moe_decode_routed", pool.data_ptr(), pool.shape[0], pool.shape[1], logits.data_ptr(), logits.numel(), k,
         1 if norm_topk else 0, _ptr(slot_table), int(base), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(),
         out.data_ptr(), _stream(x),
+    )
+    return out
+
+
+def moe_decode_paged(pool, logits, x, k, n, H, I, bits, group=128, norm_topk=True, slot_table=None, base=0,
+                     store_host=None, miss_count=None, row=None, out=None, scratch=None):
+    """moe_decode_routed over a partially resident pool: ``slot_table`` (int32 [L*E] on the device)
+    maps key = base + e to a slot, or to -1 when the expert is not resident; those experts are read
+    by the kernels straight from ``store_host`` (the pinned uint8 [L*E, nbytes] host store), so no
+    host decision sits between the router and the MoE.  ``miss_count`` (int32 [1], nullable) counts
+    the experts read from the host store."""
+    assert H % group == 0 and I % group == 0 and n == H * I
+    _need_cuda(pool, logits, x, slot_table)
+    _bf16(logits)
+    if x.dtype != torch.bfloat16:
+        raise WispError(f"x must be bfloat16 (got {x.dtype})")
+    if slot_table.dtype != torch.int32 or not slot_table.is_contiguous():
+        raise WispError("slot_table must be contiguous int32")
+    if not (isinstance(store_host, torch.Tensor) and store_host.device.type == "cpu" and store_host.is_pinned()):
+        raise WispError("store_host must be a pinned host tensor")
+    if store_host.dtype != torch.uint8 or store_host.dim() != 2 or not store_host.is_contiguous():
+        raise WispError("store_host must be contiguous uint8 [rows, nbytes]")
+    if store_host.shape[1] != pool.shape[1]:
+        raise WispError(f"store_host rows of {store_host.shape[1]} bytes, pool slots of {pool.shape[1]}")
+    if slot_table.numel() < store_host.shape[0]:
+        raise WispError("slot_table must cover every row of store_host")
+    if miss_count is not None:
+        _need_cuda(miss_count)
+        if miss_count.dtype != torch.int32:
+            raise WispError("miss_count must be int32")
+    x = x.contiguous()
+    if scratch is None:
+        scratch = moe_scratch(k, I, x.device)
+    if out is None:
+        out = torch.empty((H,), dtype=x.dtype, device=x.device)
+    _lib.call(
+        "wisp_moe_decode_paged", pool.data_ptr(), pool.shape[0], pool.shape[1], logits.data_ptr(), logits.numel(), k,
+        1 if norm_topk else 0, slot_table.data_ptr(), int(base), store_host.data_ptr(), store_host.shape[0],
+        _ptr(miss_count), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(), out.data_ptr(), _stream(x),
     )
     return out
 
