@@ -41,6 +41,9 @@ EP_BATCH = 64  # moe-ep: tokens per step over all ranks (config 4 batch)
 NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
 
 
+GO_L, GO_H, GO_I, GO_E, GO_K = 24, 2880, 2880, 32, 4  # gpt-oss-20b MoE shape (config 5)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -48,7 +51,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
-    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack", "moe-ep"])
+    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack", "moe-ep", "gptoss-moe"])
+    ap.add_argument("--batch", type=int, default=1, help="gptoss-moe: tokens per step (config 5: 1 or 32)")
     ap.add_argument("--layers", type=int, default=48, help="layers (48 = the model; fewer = a small ncu case)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--cache-frac", type=float, default=0.4,
@@ -65,7 +69,8 @@ def parse():
 
 
 def metric_name(a):
-    return {"decoder": "decode tok/s", "moe-stack": "moe decode tok/s", "moe-ep": "batched moe tok/s"}[a.workload]
+    return {"decoder": "decode tok/s", "moe-stack": "moe decode tok/s", "moe-ep": "batched moe tok/s",
+            "gptoss-moe": "moe decode tok/s"}[a.workload]
 
 
 def workload_config(a, n):
@@ -91,6 +96,17 @@ def workload_config(a, n):
             "seq_len": a.prompt,
             "parallelism": "replicas" if n > 1 else "single",
             "l2": "working set 3.4 GB/token >> 126 MB L2; no flush",
+        }
+    if a.workload == "gptoss-moe":
+        return {
+            "workload": f"gpt-oss-20b moe stack (config 5 MoE): {a.batch} token(s) per step, {GO_L} layers x {GO_E} experts "
+            f"top-{GO_K}, hidden = intermediate = {GO_H}, clamped SwiGLU with biases, {a.bits}-bit g{G} experts (input-major "
+            "gate_up/down), all experts resident, top-k then softmax routing, rmsnorm+residual between layers (no attention)",
+            "model": "gpt-oss-20b-shaped (random init)",
+            "global_batch": a.batch * n,
+            "seq_len": 1,
+            "parallelism": "replicas" if n > 1 else "single",
+            "l2": f"expert working set {GO_L * GO_E * 13.2:.0f} MB >> 126 MB L2; no flush",
         }
     if a.workload == "moe-ep":
         return {
@@ -380,10 +396,36 @@ def cpu_ep_tok_s(a, seed=0, distinct=60.0, sample_experts=4):
                                f"experts x {distinct:.0f} distinct experts per layer x {L} layers, {EP_BATCH} tokens per step")
 
 
+def cpu_gptoss_tok_s(a, seed=0, distinct=4.0):
+    """Tokens/s of the CPU path for the gpt-oss MoE stack: the oracle's gpt-oss expert (dequantize,
+    x W_gu + b, clamped SwiGLU, . W_d + b) on one sampled expert for the average number of tokens an
+    expert receives, times the distinct experts of a layer, times the layers."""
+    import numpy as np
+
+    from oracle import wisp_oracle as O
+
+    rng = np.random.default_rng(seed)
+    n = GO_H * GO_I
+    toks = max(1, int(round(a.batch * GO_K / distinct)))
+    pool = O.quantize((rng.standard_normal((3, n)) * 0.02).astype(np.float32), a.bits, G)[None]
+    gub = np.zeros((1, 2 * GO_I), np.uint16)
+    db = np.zeros((1, GO_H), np.uint16)
+    x = rng.standard_normal((toks, GO_H)).astype(np.float32)
+    t0 = time.perf_counter()
+    y = O.gptoss_ref(pool, np.zeros((toks, 1), np.int64), np.ones((toks, 1), np.float32), x, GO_H, GO_I, a.bits, G, gub, db)
+    per_expert = time.perf_counter() - t0
+    assert np.isfinite(y).all()
+    step = per_expert * distinct * GO_L
+    return a.batch / step, 1, (f"oracle gpt-oss expert (dequantize + fp32 MLP of {toks} token(s)) on 1 expert x "
+                               f"{distinct:.1f} distinct experts per layer x {GO_L} layers, {a.batch} token(s) per step")
+
+
 def cpu_tok_s(a, seed=0, distinct=60.0):
     """Tokens/s of the CPU path, extrapolated from one sampled layer (x L) and a sampled lm_head."""
     if a.workload == "moe-ep":
         return cpu_ep_tok_s(a, seed, distinct)
+    if a.workload == "gptoss-moe":
+        return cpu_gptoss_tok_s(a, seed, distinct if distinct < 60.0 else float(min(GO_E, a.batch * GO_K)))
     if a.workload == "decoder":
         dt, threads = cpu_layer_sample(a.bits, seed=seed, attention=True, context=a.prompt)
         return 1.0 / (dt * L + cpu_head_sample(seed)), threads, (
@@ -539,6 +581,126 @@ class MoEStack:
 
 
 # ------------------------------------------------------------------------------------------------
+# gptoss-moe workload (config 5 MoE part)
+# ------------------------------------------------------------------------------------------------
+class GptOssStack:
+    """``a.batch`` tokens through the 24 gpt-oss-20b-shaped MoE layers, RMSNorm + residual between them,
+    one CUDA graph per seeded routing (top-4 of the logits, then softmax over the selected,
+    wisp/gptoss.py:116-118)."""
+
+    def __init__(self, a, device, seed):
+        import torch
+
+        from wisp import kernels, quant
+
+        self.N, self.bits = a.batch, a.bits
+        n = GO_H * GO_I
+        self.nb = quant.expert_nbytes(n, a.bits, G)
+        bf = torch.bfloat16
+        self.pool = torch.empty((GO_L * GO_E, self.nb), dtype=torch.uint8, device=device)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        for l in range(GO_L):
+            for e0 in range(0, GO_E, 8):
+                w3 = (torch.randn(8, 3, n, device=device, generator=gen) * 0.02).to(bf)
+                self.pool[l * GO_E + e0 : l * GO_E + e0 + 8].copy_(quant.quantize_batch(w3, a.bits, G))
+                del w3
+        self.gub = (torch.randn(GO_L, GO_E, 2 * GO_I, device=device, generator=gen) * 0.02).to(bf)
+        self.db = (torch.randn(GO_L, GO_E, GO_H, device=device, generator=gen) * 0.02).to(bf)
+        self.norm_w = (1.0 + 0.1 * torch.randn(GO_L, GO_H, device=device, generator=gen)).to(bf)
+        logits = torch.randn(N_ROUTES, GO_L, self.N, GO_E, device=device, generator=gen).to(bf)
+        tv, ti = torch.topk(logits.float(), GO_K, -1)
+        sc = torch.softmax(tv, -1).to(bf).float()
+        slots = ti + (torch.arange(GO_L, device=device) * GO_E)[None, :, None, None]
+        self.meta = torch.cat([slots.float(), sc], -1).contiguous()  # [R, L, N, 2k]
+        self.experts = ti.to(torch.int32).contiguous()  # [R, L, N, k]
+        self.distinct = float(
+            sum(torch.unique(ti[r, l]).numel() for r in range(N_ROUTES) for l in range(GO_L)) / (N_ROUTES * GO_L)
+        )
+        self.x0 = torch.randn(N_ROUTES, self.N, GO_H, device=device, generator=gen).to(bf)
+        self.h = torch.zeros(self.N, GO_H, dtype=bf, device=device)
+        self.xn = torch.zeros_like(self.h)
+        self.moe = torch.zeros_like(self.h)
+        from wisp import _lib
+
+        self.ws = torch.empty(_lib.lib().wisp_moe_gptoss_workspace_bytes(self.N, GO_K, GO_H, GO_I), dtype=torch.uint8,
+                              device=device)
+        self.meta_in = torch.zeros_like(self.meta[0])
+        self.exp_in = torch.zeros_like(self.experts[0])
+        self.x_in = torch.zeros_like(self.h)
+        self.graphs = []
+
+    def _layer_loop(self, meta, experts, x0):
+        from wisp import kernels
+
+        self.h.copy_(x0)
+        self.moe.zero_()
+        for l in range(GO_L):
+            kernels.rmsnorm(self.h, self.norm_w[l], 1e-5, delta=self.moe, sum_out=self.h, out=self.xn)
+            kernels.moe_gptoss(self.pool, meta[l], experts[l], self.xn, GO_K, GO_H, GO_I, self.bits, self.gub[l], self.db[l],
+                               group=G, out=self.moe, workspace=self.ws)
+        self.h.add_(self.moe)
+
+    def launches_per_step(self):
+        return 6 * GO_L  # rmsnorm; grouping, gate_up GEMV, activation, down GEMV, combine
+
+    def capture(self):
+        import torch
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._layer_loop(self.meta[0], self.experts[0], self.x0[0])
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        pool = torch.cuda.graph_pool_handle()
+        for r in range(N_ROUTES + 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                if r < N_ROUTES:
+                    self._layer_loop(self.meta[r], self.experts[r], self.x0[r])
+                else:
+                    self._layer_loop(self.meta_in, self.exp_in, self.x_in)
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+
+    def step(self, t):
+        self.graphs[t % N_ROUTES].replay()
+
+    def e2e_inputs(self):
+        import torch
+
+        return (self.x0.cpu().pin_memory(), self.meta.cpu().pin_memory(), self.experts.cpu().pin_memory(),
+                torch.empty(self.N, GO_H, dtype=torch.bfloat16).pin_memory())
+
+    def step_e2e(self, t, inp):
+        x_host, meta_host, exp_host, out_host = inp
+        r = t % N_ROUTES
+        self.x_in.copy_(x_host[r], non_blocking=True)
+        self.meta_in.copy_(meta_host[r], non_blocking=True)
+        self.exp_in.copy_(exp_host[r], non_blocking=True)
+        self.graphs[N_ROUTES].replay()
+        out_host.copy_(self.h, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.x_in.numel() * 2 + self.meta_in.numel() * 4 + self.exp_in.numel() * 4, self.h.numel() * 2
+
+    def roofline(self, ms_per_step, peak, peak_src):
+        """Per layer: the distinct routed experts' bytes (+ activations in and out) over the step time
+        per layer (RMSNorm included, so a lower bound on the MoE kernels' own rate)."""
+        bytes_layer = self.distinct * self.nb + 2 * self.N * GO_H * 2
+        us = ms_per_step / GO_L * 1e3
+        ach = bytes_layer / (us * 1e-6) / 1e9
+        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "traffic": None,
+                "kernel": "wisp_moe_gptoss (grouping, gate_up GEMV, activation, down GEMV, combine) per layer, timed as "
+                "the step time / layers (RMSNorm included)", "bytes_per_call": bytes_layer, "us_per_call": us,
+                "peak_source": peak_src}
+
+    def release(self):
+        self.graphs = []
+
+
+# ------------------------------------------------------------------------------------------------
 # decoder workload
 # ------------------------------------------------------------------------------------------------
 class DecodeBench:
@@ -685,13 +847,14 @@ class EPStack:
         self.norm_w = (1.0 + 0.1 * torch.randn(L, H, device=device, generator=g)).to(torch.bfloat16)
         self.x0 = torch.randn(self.N, H, device=device, generator=gen).to(torch.bfloat16)
         fn = batched_expert_fn(self.pool, lambda l, e: l * self.El + e, n, H, I, a.bits, G)
-        self.ep = ExpertParallelMoE(E, K_TOP, H, self.N, fn, device=device)
+        self.ep = ExpertParallelMoE(E, K_TOP, H, self.N, fn, device=device, slot_base=lambda l: l * self.El)
         self.h = torch.empty(self.N, H, dtype=torch.bfloat16, device=device)
         self.xn = torch.empty_like(self.h)
         self.kernels = kernels
 
     def launches_per_step(self):
-        return L * 5  # rmsnorm + the batched MoE's group, gate/up, down, combine per layer
+        # rmsnorm, dispatch, the batched MoE (grouping, permute, gate/up, down, combine), combine per layer
+        return L * 8
 
     def _body(self):
         self.h.copy_(self.x0)
@@ -761,6 +924,10 @@ def main():
         bench = EPStack(a, dev, rank, world)
         bench.capture()
         pool, nbytes = bench.pool, bench.nb
+    elif a.workload == "gptoss-moe":
+        bench = GptOssStack(a, dev, seed=rank)
+        bench.capture()
+        pool, nbytes = None, bench.nb
     else:
         W = build_moe_workload(a.bits, dev, seed=rank)
         bench = MoEStack(W)
@@ -805,7 +972,11 @@ def main():
     clk = clocks.stop()
     if a.workload == "decoder" and bench.paged:
         paging = bench.paging_stats(a.warmup + 2 * a.steps + 3)
-    roof, _ = moe_roofline(pool, nbytes, a.bits) if pool.shape[0] >= K_TOP * L else (None, None)
+    if a.workload == "gptoss-moe":
+        peak, src = load_peaks()
+        roof = bench.roofline(ms / a.steps, peak, f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src)
+    else:
+        roof, _ = moe_roofline(pool, nbytes, a.bits) if pool.shape[0] >= K_TOP * L else (None, None)
     if a.workload == "decoder":
         ctx = bench.dec.pos + a.warmup + 2 * a.steps + 3  # context length at the end of the timed steps
         roof["step_bytes_per_token"] = bench.bytes_per_token(ctx)
@@ -815,8 +986,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = t.tolist()
     if rank == 0:
-        cpu_v, cores, sample = cpu_tok_s(a, distinct=bench.distinct if a.workload == "moe-ep" else 60.0)
-        tok = a.steps * (EP_BATCH if a.workload == "moe-ep" else world)
+        cpu_v, cores, sample = cpu_tok_s(a, distinct=bench.distinct if a.workload in ("moe-ep", "gptoss-moe") else 60.0)
+        tok = a.steps * (EP_BATCH if a.workload == "moe-ep" else (a.batch * world if a.workload == "gptoss-moe" else world))
         h2d, d2h = bench.e2e_bytes()
         line = {
             "metric": metric_name(a),
@@ -840,6 +1011,8 @@ def main():
         }
         if a.workload == "decoder" and bench.paged:
             line["paging"] = paging
+        if a.workload == "gptoss-moe":
+            line["distinct_experts_per_layer"] = bench.distinct
         if a.workload == "moe-ep":
             line["distinct_experts_per_layer"] = bench.distinct
             # expert bytes each GPU streams per layer (its share of the distinct experts) per layer time

@@ -138,6 +138,23 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
                      int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
                      void* stream);
 
+/* ---- expert parallelism (batched decode over ranks) ------------------------------------------------ */
+/* Pack for the dispatch all-to-all: pair p = t*k + j of this rank's N tokens (sel: int64 [N, k] global
+ * expert ids) goes to rank d = sel / E_local at capacity slot c = its rank among the pairs bound for d
+ * (pair order).  send_x [world, capacity, H] bf16 gets x[t] at (d, c); send_meta [world, capacity, 2]
+ * fp32 gets [slot_base + sel - d*E_local, 1] there and [-1, 0] in unused capacity (the batched MoE
+ * skips those), so after the exchange the receiver's meta feeds wisp_moe_batched with k = 1;
+ * src_pos [N*k] int32 = d*capacity + c for the combine.  capacity >= N*k.  Replaces the dispatch
+ * bucketing the survey plans around NCCL (the reference has no expert parallelism). */
+int wisp_ep_dispatch(const uint16_t* x, int N, int64_t H, const int64_t* sel, int k, int E_local, int world, int64_t capacity,
+                     int64_t slot_base, uint16_t* send_x, float* send_meta, int32_t* src_pos, void* stream);
+
+/* Unpack after the combine all-to-all: out[t] = bf16(sum_j w[t, j] * y_back[src_pos[t*k + j]]) with
+ * the choices summed in order (w: fp32 [N, k]; y_back: bf16 [world * capacity, H]), the weighted sum of
+ * wisp/moe.py:131-137 (index_add over the experts). */
+int wisp_ep_combine(const uint16_t* y_back, int N, int k, int64_t H, const int32_t* src_pos, const float* w, uint16_t* out,
+                    void* stream);
+
 /* ---- gpt-oss experts ------------------------------------------------------------------------------ */
 /* Bytes of the workspace wisp_moe_gptoss needs (host-only; -1 if N*k is outside [1, 2048]). */
 int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I);

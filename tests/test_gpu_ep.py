@@ -49,14 +49,16 @@ def _worker(rank, world, port, q):
         El = E // world
         local = pool[rank * El : (rank + 1) * El].contiguous()
         fn = batched_expert_fn(local, lambda l, e: l * El + e, H * I, H, I, BITS, G)
-        ep = ExpertParallelMoE(E, K, H, N, fn, device=dev)
         x, sel, w = _tokens(rank, dev)
-        out = ep.forward(x, sel, w)
         meta = torch.cat([sel.float(), w], 1).contiguous()
         ref = kernels.moe_batched(pool, meta, x, K, H * I, H, I, BITS, G)
-        torch.cuda.synchronize()
-        err = (out.float() - ref.float()).abs().max().item() / ref.float().abs().max().item()
-        q.put((rank, err))
+        errs = []
+        for slot_base in (None, lambda l: l * El):  # torch bucketing, then the dispatch/combine kernels
+            ep = ExpertParallelMoE(E, K, H, N, fn, device=dev, slot_base=slot_base)
+            out = ep.forward(x, sel, w)
+            torch.cuda.synchronize()
+            errs.append((out.float() - ref.float()).abs().max().item() / ref.float().abs().max().item())
+        q.put((rank, max(errs)))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -78,3 +80,55 @@ def test_two_gpu_expert_parallel_matches_single_gpu():
         # each pair's expert output is rounded to bf16 before the weighted sum (the reference's
         # per-expert path rounds the same way); the one-GPU kernel sums in fp32
         assert err < 1e-2, (rank, err)
+
+
+def test_dispatch_combine_kernels_one_rank():
+    """wisp_ep_dispatch / wisp_ep_combine with world = 1 (no process group): the kernel path matches the
+    torch bucketing path (the same bf16 expert outputs, summed in a fixed order instead of torch's
+    reduction: within one bf16 rounding), and the packed meta rows carry [slot_base + expert, 1] in
+    pair order with [-1, 0] nowhere (one rank receives every pair)."""
+    from wisp import kernels
+    from wisp.ep import ExpertParallelMoE, batched_expert_fn
+
+    dev = torch.device("cuda", 0)
+    pool = _setup(dev)
+    fn = batched_expert_fn(pool, lambda l, e: l * E + e, H * I, H, I, BITS, G)
+    x, sel, w = _tokens(0, dev)
+    a = ExpertParallelMoE(E, K, H, N, fn, device=dev).forward(x, sel, w)
+    kp = ExpertParallelMoE(E, K, H, N, fn, device=dev, slot_base=lambda l: l * E)
+    b = kp.forward(x, sel, w)
+    assert (a.float() - b.float()).abs().max().item() <= 2.0**-7 * a.float().abs().max().item()
+    meta = kp.send_meta.view(-1, 2).cpu()
+    assert torch.equal(meta[:, 0], sel.reshape(-1).float().cpu()) and bool((meta[:, 1] == 1).all())
+    assert torch.equal(kp.src_pos.cpu(), torch.arange(N * K, dtype=torch.int32))
+    assert torch.equal(kp.send_x.view(N * K, H).cpu(), x.repeat_interleave(K, 0).cpu())
+
+
+def test_dispatch_buckets_by_destination_rank():
+    """world = 4 packing on one GPU (no exchange): every pair lands in its owner's bucket at its rank
+    among that owner's pairs, unused capacity is [-1, 0], and combine over a y equal to the packed x
+    returns sum_j w_j x (the row each pair carried)."""
+    from wisp import kernels
+
+    dev = torch.device("cuda", 0)
+    world, El = 4, E // 4
+    x, sel, w = _tokens(1, dev)
+    C = N * K
+    send_x = torch.zeros(world, C, H, dtype=torch.bfloat16, device=dev)
+    send_meta = torch.zeros(world, C, 2, dtype=torch.float32, device=dev)
+    src_pos = torch.zeros(N * K, dtype=torch.int32, device=dev)
+    kernels.ep_dispatch(x, sel.contiguous(), El, world, C, 100, send_x, send_meta, src_pos)
+    s, m, sp = sel.cpu().reshape(-1), send_meta.cpu(), src_pos.cpu()
+    seen = [0] * world
+    for p in range(N * K):
+        d = int(s[p]) // El
+        assert int(sp[p]) == d * C + seen[d]
+        assert m[d, seen[d]].tolist() == [100.0 + int(s[p]) - d * El, 1.0]
+        assert torch.equal(send_x[d, seen[d]].cpu(), x[p // K].cpu())
+        seen[d] += 1
+    for d in range(world):
+        assert bool((m[d, seen[d]:, 0] == -1).all()) and bool((m[d, seen[d]:, 1] == 0).all())
+    out = torch.empty(N, H, dtype=torch.bfloat16, device=dev)
+    kernels.ep_combine(send_x.view(world * C, H), src_pos, w, out)
+    want = (w.view(N, K, 1) * x.float().view(N, 1, H)).sum(1)
+    assert (out.float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()

@@ -17,6 +17,7 @@
 #pragma once
 #include "common.cuh"
 #include "moe_decode.cuh"
+#include "tma.cuh"
 
 namespace wisp {
 namespace batched {
@@ -26,6 +27,8 @@ constexpr int WARPS = 8;
 constexpr int THREADS = WARPS * 32;
 constexpr int NT_MAX = 4;        // token n-tiles (of 8) per pass over the weights
 
+constexpr int TOK = 8 * NT_MAX;  // tokens per pass over an expert's weights
+
 struct Ws {
   int* n_groups;     // [1]
   int* grp_slot;     // [P]
@@ -33,14 +36,21 @@ struct Ws {
   int* grp_count;    // [P]
   int* order;        // [P] pair index at each sorted position
   int* posof;        // [P] sorted position of each pair (-1: skipped)
+  int* n_gp;         // [1] number of (group, pass) entries
+  int* next_unit;    // [2] work counters of the gate/up and down grids
+  int* gp_list;      // [P] (group << 8 | pass), passes with more token tiles first
   uint16_t* a;       // [P][I] bf16
   float* y;          // [P][H] fp32
+  uint16_t* xp;      // [P][H] bf16: the tokens' rows pair-permuted (4-bit / 2-bit kernels)
 };
 
+__host__ __device__ inline int64_t ws_ints_bytes(int P) { return ((4 + 6 * int64_t(P)) * 4 + 255) / 256 * 256; }
+
 __host__ __device__ inline int64_t ws_bytes(int P, int64_t H, int64_t I) {
-  const int64_t ints = ((1 + 5 * int64_t(P)) * 4 + 255) / 256 * 256;
+  const int64_t ints = ws_ints_bytes(P);
   const int64_t a = (int64_t(P) * I * 2 + 255) / 256 * 256;
-  return ints + a + int64_t(P) * H * 4;
+  const int64_t y = (int64_t(P) * H * 4 + 255) / 256 * 256;
+  return ints + a + y + int64_t(P) * H * 2;
 }
 
 __host__ __device__ inline Ws ws_carve(void* base, int P, int64_t I) {
@@ -52,10 +62,22 @@ __host__ __device__ inline Ws ws_carve(void* base, int P, int64_t I) {
   w.grp_count = w.grp_start + P;
   w.order = w.grp_count + P;
   w.posof = w.order + P;
-  uint8_t* b = static_cast<uint8_t*>(base) + ((1 + 5 * int64_t(P)) * 4 + 255) / 256 * 256;
+  w.n_gp = w.posof + P;
+  w.next_unit = w.n_gp + 1;
+  w.gp_list = w.next_unit + 2;
+  uint8_t* b = static_cast<uint8_t*>(base) + ws_ints_bytes(P);
   w.a = reinterpret_cast<uint16_t*>(b);
   w.y = reinterpret_cast<float*>(b + (int64_t(P) * I * 2 + 255) / 256 * 256);
+  w.xp = nullptr;
   return w;
+}
+
+// the pair-permuted token rows live after the grouping ints, a and y
+__host__ __device__ inline uint16_t* ws_xp(void* base, int P, int64_t H, int64_t I) {
+  const int64_t ints = ws_ints_bytes(P);
+  const int64_t a = (int64_t(P) * I * 2 + 255) / 256 * 256;
+  const int64_t y = (int64_t(P) * H * 4 + 255) / 256 * 256;
+  return reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(base) + ints + a + y);
 }
 
 // ---- grouping ---------------------------------------------------------------------------------------
@@ -127,6 +149,32 @@ __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ m
     }
   }
   if (threadIdx.x == 0) W.n_groups[0] = n2 > 0 ? scan[P - 1 < 0 ? 0 : P - 1] : 0;
+  // the (group, pass) work list of the grouped kernels, bucketed by the pass's token tiles (4 first), so
+  // the dynamically scheduled grids start with their most expensive units
+  __shared__ int bcnt[NT_MAX + 1], bofs[NT_MAX + 1];
+  if (threadIdx.x <= NT_MAX) bcnt[threadIdx.x] = 0;
+  __syncthreads();  // group arrays (written above by this CTA) and the bucket counters
+  const int ngr = P > 0 ? scan[P - 1] : 0;
+  for (int gid = threadIdx.x; gid < ngr; gid += blockDim.x) {
+    const int cnt = W.grp_count[gid];
+    for (int t0 = 0; t0 < cnt; t0 += TOK) atomicAdd(&bcnt[min(NT_MAX, (cnt - t0 + 7) / 8)], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o = 0;
+    for (int nt = NT_MAX; nt >= 1; --nt) {
+      bofs[nt] = o;
+      o += bcnt[nt];
+    }
+    W.n_gp[0] = o;
+    W.next_unit[0] = 0;
+    W.next_unit[1] = 0;
+  }
+  __syncthreads();
+  for (int gid = threadIdx.x; gid < ngr; gid += blockDim.x) {
+    const int cnt = W.grp_count[gid];
+    for (int t0 = 0, p = 0; t0 < cnt; t0 += TOK, ++p) W.gp_list[atomicAdd(&bofs[min(NT_MAX, (cnt - t0 + 7) / 8)], 1)] = gid << 8 | p;
+  }
   pdl_launch_dependents();
 }
 
@@ -165,7 +213,6 @@ __device__ __forceinline__ void row_unit(const uint8_t* base, const MoeShape& S,
 // activation rows of the group's tokens (up to TOK per pass) are staged once in shared memory (rows
 // padded by 4 elements: the fragment loads stay within two-way bank conflicts) and every warp streams
 // its rows' weight units from HBM, the next K block's units loaded while the current one computes.
-constexpr int TOK = 8 * NT_MAX;  // tokens per pass
 constexpr int ROWS_PER_CTA = 16 * WARPS;
 
 __host__ __device__ inline int64_t stage_bytes(int64_t K) { return int64_t(TOK) * (K + 4) * 2; }
@@ -266,19 +313,242 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_kernel(const uint8_t* __re
   }
 }
 
+// ---- 4-bit and 2-bit codes straight into the MMA ----------------------------------------------------------
+// bf16(128 + q) is exact for q < 128, so two codes become one A register with two integer ops: the pair
+// (n_i, n_{i + W/2}) of a 32-bit code word (W = 32 / BITS codes) is ((w >> BITS*i) & mask) | 0x43004300.
+// Over one 128-code block (one scale s and min m per row: group % 128 == 0) the MMA then yields
+// D = sum_k (128 + q_k) x_k, and the block's dot product with the dequantized weights q*s + m is
+// s*D + (m - 128 s) * sum_k x_k, folded once per block.  (The reference rounds each weight to bf16
+// before the product; this form skips that rounding, well inside the parity tolerance.)
+//
+// Activations are kept "pair-permuted": inside every W-element word, position 2i holds element i and
+// 2i + 1 holds element i + W/2, so the four B elements of MMA step s of a lane's 32-code unit sit at
+// unit offset 4s, contiguous.  In shared memory each 128-element block is further stored step-major
+// ([step][lane c][4]) with a row pitch of K + 16 elements: the fragment loads are bank-conflict free.
+template <int BITS>
+__host__ __device__ constexpr int pair_word() { return 32 / BITS; }
+
+template <int BITS>
+__device__ __forceinline__ int perm_pos(int e) {  // position of natural element e in the pair-permuted row
+  constexpr int Wc = 32 / BITS, h = Wc / 2;
+  const int i = e & (Wc - 1);
+  return (e & ~(Wc - 1)) + (i < h ? 2 * i : 2 * (i - h) + 1);
+}
+
+template <int BITS>
+__device__ __forceinline__ uint32_t code_pair(uint32_t w, int i) {
+  constexpr uint32_t mask = BITS == 4 ? 0x000F000Fu : 0x00030003u;
+  return ((w >> (BITS * i)) & mask) | 0x43004300u;
+}
+
+// rows [rows][K] bf16 (natural order) -> pair-permuted copy
+template <int BITS>
+__global__ void permute_rows_kernel(const uint16_t* __restrict__ x, int64_t nwords, uint16_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < nwords; i += int64_t(gridDim.x) * blockDim.x) {
+    if constexpr (BITS == 4) {  // 8 elements: out word q = (x_q, x_{q+4})
+      const uint4 a = reinterpret_cast<const uint4*>(x)[i];
+      reinterpret_cast<uint4*>(out)[i] = make_uint4(__byte_perm(a.x, a.z, 0x5410), __byte_perm(a.x, a.z, 0x7632),
+                                                    __byte_perm(a.y, a.w, 0x5410), __byte_perm(a.y, a.w, 0x7632));
+    } else {  // 16 elements: out word q = (x_q, x_{q+8})
+      const uint4 a = reinterpret_cast<const uint4*>(x)[2 * i], b = reinterpret_cast<const uint4*>(x)[2 * i + 1];
+      reinterpret_cast<uint4*>(out)[2 * i] = make_uint4(__byte_perm(a.x, b.x, 0x5410), __byte_perm(a.x, b.x, 0x7632),
+                                                        __byte_perm(a.y, b.y, 0x5410), __byte_perm(a.y, b.y, 0x7632));
+      reinterpret_cast<uint4*>(out)[2 * i + 1] = make_uint4(__byte_perm(a.z, b.z, 0x5410), __byte_perm(a.z, b.z, 0x7632),
+                                                            __byte_perm(a.w, b.w, 0x5410), __byte_perm(a.w, b.w, 0x7632));
+    }
+  }
+}
+
+constexpr int NIB_PAD = 16;  // row pitch K + 16 elements: (K + 16) / 2 words = 8 mod 32 banks
+__host__ __device__ inline int64_t nib_stage_bytes(int64_t K) {
+  return int64_t(TOK) * (K + NIB_PAD) * 2 + int64_t(TOK) * (K / 128) * 4;
+}
+
+// MAT 0: gate and up (rows of I, K = H, input the pair-permuted x of the tokens) -> a (pair-permuted, bf16)
+// MAT 2: down (rows of H, K = I, input the pair-permuted a of the pairs) -> y (fp32)
+// A unit is (group, pass of up to TOK tokens, 128-row chunk); CTAs take units from a counter in the
+// order of the work list (passes with more token tiles first), which balances Zipf-skewed groups.  At
+// the start of a unit every warp asks L2 for its 16 rows (one contiguous range per matrix) and the
+// per-lane register loads then find them there.
+template <int BITS, int MAT>
+__global__ void __launch_bounds__(THREADS, 1) grouped_nib_kernel(const uint8_t* __restrict__ pool, MoeShape S,
+                                                                 const uint16_t* __restrict__ xp, Ws W) {
+  extern __shared__ __align__(16) uint16_t xs[];  // [TOK][K + NIB_PAD] bf16, then xsum [TOK][K / 128] fp32
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int ngr = W.n_groups[0];
+  const int64_t rows = MAT == 0 ? S.I : S.H;
+  const int64_t K = MAT == 0 ? S.H : S.I;
+  const int64_t KP = K + NIB_PAD;
+  const int nblk = int(K / 128);
+  float* xsum = reinterpret_cast<float*>(xs + int64_t(TOK) * KP);
+  const int chunks = int((rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA);
+  const int64_t nunits = int64_t(W.n_gp[0]) * chunks;
+  (void)ngr;
+  constexpr int NQ = MAT == 0 ? 4 : 2;  // rows of a lane: gate g, gate g+8, up g, up g+8 (MAT 0); g, g+8
+  const int64_t row_bytes = K * BITS / 8;
+  int staged_grp = -1, staged_t0 = -1;
+  __shared__ int64_t s_unit;
+  for (;;) {
+    __syncthreads();  // every thread has read s_unit
+    if (threadIdx.x == 0) s_unit = atomicAdd(&W.next_unit[MAT == 0 ? 0 : 1], 1);
+    __syncthreads();
+    const int64_t u = s_unit;
+    if (u >= nunits) break;
+    const int gp = W.gp_list[u / chunks];
+    const int grp = gp >> 8, ch = int(u % chunks);
+    const uint8_t* base = pool + int64_t(W.grp_slot[grp]) * S.nbytes;
+    const int start = W.grp_start[grp], cnt = W.grp_count[grp];
+    const int64_t r0 = int64_t(ch) * ROWS_PER_CTA + 16 * warp;
+    const bool active = r0 < rows;  // warp-uniform
+    if (active && lane < (MAT == 0 ? 2 : 1)) {
+      // lane 0: gate (or down) rows r0..r0+15, lane 1 (MAT 0): up rows -- one contiguous range each
+      const int mat = MAT == 0 ? lane : 2;
+      prefetch_l2(base + int64_t(mat) * S.mat_bytes + r0 * row_bytes, uint32_t(16 * row_bytes));
+    }
+    {
+      const int t0 = (gp & 255) * TOK;
+      const int nt_used = (cnt - t0 + 7) / 8 < NT_MAX ? (cnt - t0 + 7) / 8 : NT_MAX;
+      if (grp != staged_grp || t0 != staged_t0) {
+        // ---- stage the activation rows of tokens [t0, t0 + TOK) (zeros past the group), block b's
+        //      4-element chunk q = 8 c + s at chunk 4 s + c; block sums into xsum
+        __syncthreads();  // the previous readers are done
+        const int nchunk = int(K / 4);
+        const int rows_used = 8 * nt_used;  // rows past the pass's token tiles are never read
+        for (int i = threadIdx.x; i < rows_used * (nchunk / 2); i += blockDim.x) {
+          const int t = i / (nchunk / 2);
+          const int q2 = i - t * (nchunk / 2);  // a pair of chunks: 2 q2, 2 q2 + 1 (same block)
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (t0 + t < cnt) {
+            const uint16_t* src = MAT == 0 ? xp + int64_t(W.order[start + t0 + t] / S.k) * S.H : W.a + int64_t(start + t0 + t) * S.I;
+            v = reinterpret_cast<const uint4*>(src)[q2];
+          }
+          const int q = 2 * q2, blk = q >> 5, qq = q & 31;  // 32 chunks per 128-element block
+          const int d0 = blk * 32 + (qq & 7) * 4 + (qq >> 3), d1 = blk * 32 + ((qq + 1) & 7) * 4 + ((qq + 1) >> 3);
+          uint16_t* row = xs + int64_t(t) * KP;
+          *reinterpret_cast<uint2*>(row + 4 * d0) = make_uint2(v.x, v.y);
+          *reinterpret_cast<uint2*>(row + 4 * d1) = make_uint2(v.z, v.w);
+        }
+        __syncthreads();
+        // block sums: one warp per (token, block), fixed order
+        for (int i = warp; i < rows_used * nblk; i += WARPS) {
+          const int t = i / nblk, blk = i - t * nblk;
+          const uint2 v = *reinterpret_cast<const uint2*>(xs + int64_t(t) * KP + blk * 128 + 4 * lane);
+          float sx = __uint_as_float(v.x << 16) + __uint_as_float(v.x & 0xFFFF0000u) + __uint_as_float(v.y << 16) +
+                     __uint_as_float(v.y & 0xFFFF0000u);
+          sx = warp_sum(sx);
+          if (lane == 0) xsum[t * nblk + blk] = sx;
+        }
+        __syncthreads();
+        staged_grp = grp, staged_t0 = t0;
+      }
+      if (!active) continue;
+      float acc0[NT_MAX][4] = {}, acc1[NT_MAX][4] = {};
+      uint32_t cw[NQ][BITS], nw[NQ][BITS];
+      float csc[NQ], cmn[NQ], nsc[NQ], nmn[NQ];
+      auto fetch = [&](int blk, uint32_t (&ww)[NQ][BITS], float (&sc)[NQ], float (&mn)[NQ]) {
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          const int mat = MAT == 0 ? (q >> 1) : 2;
+          const int64_t row = r0 + g + (q & 1) * 8;
+          const int64_t e = int64_t(mat) * S.H * S.I + row * K + int64_t(blk) * 128 + 32 * c;
+          const Unit<BITS> uu = load_unit<BITS>(base + e * BITS / 8);
+#pragma unroll
+          for (int i = 0; i < BITS; ++i) ww[q][i] = uu.w[i];
+          const int64_t gi = e / S.group;
+          sc[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + gi));
+          mn[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + S.ng + gi));
+        }
+      };
+      fetch(0, cw, csc, cmn);
+      for (int blk = 0; blk < nblk; ++blk) {
+        if (blk + 1 < nblk) fetch(blk + 1, nw, nsc, nmn);
+        float D0[NT_MAX][4] = {}, D1[NT_MAX][4] = {};
+        const uint16_t* xb = xs + int64_t(blk) * 128 + 4 * c;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          constexpr int SPW = 32 / BITS / 4;  // MMA steps per code word: 2 (4-bit), 4 (2-bit)
+          const int j = s / SPW, i0 = 2 * (s % SPW);
+          uint32_t a[NQ][2];
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            a[q][0] = code_pair<BITS>(cw[q][j], i0);
+            a[q][1] = code_pair<BITS>(cw[q][j], i0 + 1);
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT_MAX; ++nt) {
+            if (nt < nt_used) {  // warp-uniform
+              const uint2 bb = *reinterpret_cast<const uint2*>(xb + int64_t(8 * nt + g) * KP + 16 * s);
+              mma16816(D0[nt], a[0][0], a[1][0], a[0][1], a[1][1], bb.x, bb.y);
+              if (MAT == 0) mma16816(D1[nt], a[2][0], a[3][0], a[2][1], a[3][1], bb.x, bb.y);
+            }
+          }
+        }
+        // fold: rows g (q 0, 1) and g + 8 (q 2, 3) of the tile, token columns 2c, 2c + 1
+#pragma unroll
+        for (int nt = 0; nt < NT_MAX; ++nt) {
+          if (nt < nt_used) {
+            const float xs0 = xsum[(8 * nt + 2 * c) * nblk + blk], xs1 = xsum[(8 * nt + 2 * c + 1) * nblk + blk];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int rq = q >> 1;  // 0: row g, 1: row g + 8
+              const float xsv = (q & 1) ? xs1 : xs0;
+              acc0[nt][q] = fmaf(csc[rq], D0[nt][q], fmaf(cmn[rq] - 128.0f * csc[rq], xsv, acc0[nt][q]));
+              if (MAT == 0)
+                acc1[nt][q] = fmaf(csc[2 + rq], D1[nt][q], fmaf(cmn[2 + rq] - 128.0f * csc[2 + rq], xsv, acc1[nt][q]));
+            }
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+#pragma unroll
+          for (int i = 0; i < BITS; ++i) cw[q][i] = nw[q][i];
+          csc[q] = nsc[q];
+          cmn[q] = nmn[q];
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT_MAX; ++nt) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int p = t0 + 8 * nt + 2 * c + (q & 1);
+          const int64_t r = r0 + g + (q >> 1) * 8;
+          if (p < cnt) {
+            if (MAT == 0) W.a[int64_t(start + p) * S.I + perm_pos<BITS>(int(r))] = f32_to_bf16(silu_mul(acc0[nt][q], acc1[nt][q]));
+            else W.y[int64_t(start + p) * S.H + r] = acc0[nt][q];
+          }
+        }
+      }
+    }
+  }
+}
+
 // ---- combine: out[t][h] = bf16(sum_j w[t][j] * y[posof(t, j)][h]), j in order ------------------------------
+// four outputs per thread (H % 4 == 0): float4 loads of y, one 8-byte store
 __global__ void combine_kernel(const float* __restrict__ meta, int N, int k, int64_t H, Ws W, uint16_t* __restrict__ out) {
   pdl_wait();
   pdl_launch_dependents();
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(N) * H; i += int64_t(gridDim.x) * blockDim.x) {
-    const int t = int(i / H);
-    const int64_t h = i - int64_t(t) * H;
-    float s = 0.0f;
+  const int64_t H4 = H / 4;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(N) * H4; i += int64_t(gridDim.x) * blockDim.x) {
+    const int t = int(i / H4);
+    const int64_t h4 = i - int64_t(t) * H4;
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int j = 0; j < k; ++j) {
       const int pos = W.posof[t * k + j];
-      if (pos >= 0) s = fmaf(meta[int64_t(t) * 2 * k + k + j], W.y[int64_t(pos) * H + h], s);
+      if (pos < 0) continue;
+      const float w = meta[int64_t(t) * 2 * k + k + j];
+      const float4 y = reinterpret_cast<const float4*>(W.y + int64_t(pos) * H)[h4];
+      s.x = fmaf(w, y.x, s.x);
+      s.y = fmaf(w, y.y, s.y);
+      s.z = fmaf(w, y.z, s.z);
+      s.w = fmaf(w, y.w, s.w);
     }
-    out[i] = f32_to_bf16(s);
+    const uint32_t lo = uint32_t(f32_to_bf16(s.x)) | (uint32_t(f32_to_bf16(s.y)) << 16);
+    const uint32_t hi = uint32_t(f32_to_bf16(s.z)) | (uint32_t(f32_to_bf16(s.w)) << 16);
+    reinterpret_cast<uint2*>(out + int64_t(t) * H)[h4] = make_uint2(lo, hi);
   }
 }
 

@@ -48,53 +48,86 @@ __host__ __device__ inline Ws ws_carve(void* base, int P, int S, int64_t H, int6
   return w;
 }
 
-// 8 codes starting at element e (e % 8 == 0) of the code stream
+// the packed bytes of 8 codes starting at element e (e % 8 == 0) of the code stream
 template <int BITS>
-__device__ __forceinline__ void load8(const uint8_t* codes, int64_t e, uint32_t (&q)[8]) {
+struct Word8 {
+  uint32_t v[BITS == 8 ? 2 : 1];
+};
+
+template <int BITS>
+__device__ __forceinline__ Word8<BITS> load_word8(const uint8_t* codes, int64_t e) {
   const uint8_t* p = codes + e * BITS / 8;
+  Word8<BITS> w;
   if constexpr (BITS == 4) {
-    const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(p));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = (v >> (4 * i)) & 15u;
+    w.v[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
   } else if constexpr (BITS == 2) {
-    const uint32_t v = __ldg(reinterpret_cast<const uint16_t*>(p));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = (v >> (2 * i)) & 3u;
+    w.v[0] = __ldg(reinterpret_cast<const uint16_t*>(p));
   } else if constexpr (BITS == 3) {
-    const uint32_t v = uint32_t(__ldg(p)) | (uint32_t(__ldg(p + 1)) << 8) | (uint32_t(__ldg(p + 2)) << 16);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = (v >> (3 * i)) & 7u;
+    w.v[0] = uint32_t(__ldg(p)) | (uint32_t(__ldg(p + 1)) << 8) | (uint32_t(__ldg(p + 2)) << 16);
   } else {
-    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      q[i] = (v.x >> (8 * i)) & 255u;
-      q[4 + i] = (v.y >> (8 * i)) & 255u;
-    }
+    const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+    w.v[0] = t.x;
+    w.v[1] = t.y;
   }
+  return w;
 }
 
-// acc[c][t] += sum over rows r in [r0, r1) of bf16(q*s+m)(row r, column j0 + c) * in[t][r]
-// (matrix base element e0, row pitch `pitch` elements)
 template <int BITS>
+__device__ __forceinline__ uint32_t word8_code(const Word8<BITS>& w, int i) {
+  if constexpr (BITS == 8) return (w.v[i >> 2] >> (8 * (i & 3))) & 255u;
+  else return (w.v[0] >> (BITS * i)) & ((1u << BITS) - 1u);
+}
+
+// Partial products of one (group, column tile, K split) unit for tokens [t0, t0 + NT) of the group:
+// part[sp][pos][j0 + c] = sum over rows r in [r0, r1) of bf16(q*s+m)(row r, column j0 + c) * in[t][r]
+// (matrix base element e0, row pitch `pitch` elements).  The loads of RIF rows are issued together so
+// that each lane keeps that many in flight.
+template <int BITS, int MAT, int NT>
 __device__ __forceinline__ void column_dot(const uint8_t* base, const MoeShape& S, int64_t e0, int64_t pitch, int64_t j0,
-                                           int r0, int r1, const uint16_t* const (&in)[NTOK], int nt,
-                                           float (&acc)[8][NTOK]) {
+                                           int r0, int r1, const uint16_t* x, const Ws& W, int pos0, float* dst0,
+                                           int64_t dst_pitch, int nt) {
+  constexpr int RIF = NT >= 8 ? 4 : (NT >= 4 ? 8 : 16);
   const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + S.ncode);
-  for (int r = r0; r < r1; ++r) {
-    const int64_t e = e0 + int64_t(r) * pitch + j0;
-    uint32_t q[8];
-    load8<BITS>(base, e, q);
-    const int64_t gi = e / S.group;
-    const float s = f16_bits_to_f32(ld_nc_u16(sc + gi)), m = f16_bits_to_f32(ld_nc_u16(sc + S.ng + gi));
-    float xv[NTOK];
+  const uint16_t* in[NT];  // input rows of the tokens (t >= nt repeats the first)
 #pragma unroll
-    for (int t = 0; t < NTOK; ++t) xv[t] = t < nt ? bf16_to_f32(in[t][r]) : 0.0f;
+  for (int t = 0; t < NT; ++t) {
+    const int pos = pos0 + (t < nt ? t : 0);
+    in[t] = MAT == 0 ? x + int64_t(W.g.order[pos] / S.k) * S.H : W.act + int64_t(pos) * S.I;
+  }
+  float acc[8][NT] = {};
+  for (int rb = r0; rb < r1; rb += RIF) {
+    Word8<BITS> w[RIF];
+    uint16_t sb[RIF], mb[RIF];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float w = bf16_to_f32(f32_to_bf16(__fadd_rn(__fmul_rn(small_u2f(q[c]), s), m)));
+    for (int i = 0; i < RIF; ++i) {
+      const int r = rb + i < r1 ? rb + i : r1 - 1;  // the tail repeats the last row and adds nothing
+      const int64_t e = e0 + int64_t(r) * pitch + j0;
+      w[i] = load_word8<BITS>(base, e);
+      const int64_t gi = e / S.group;
+      sb[i] = ld_nc_u16(sc + gi);
+      mb[i] = ld_nc_u16(sc + S.ng + gi);
+    }
 #pragma unroll
-      for (int t = 0; t < NTOK; ++t) acc[c][t] = fmaf(w, xv[t], acc[c][t]);
+    for (int i = 0; i < RIF; ++i) {
+      if (rb + i >= r1) break;
+      const float s = f16_bits_to_f32(sb[i]), m = f16_bits_to_f32(mb[i]);
+      float xv[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) xv[t] = bf16_to_f32(in[t][rb + i]);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float wv = bf16_to_f32(f32_to_bf16(__fadd_rn(__fmul_rn(small_u2f(word8_code<BITS>(w[i], c)), s), m)));
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[c][t] = fmaf(wv, xv[t], acc[c][t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    if (t < nt) {
+      float* dst = dst0 + int64_t(t) * dst_pitch;
+      reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0][t], acc[1][t], acc[2][t], acc[3][t]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4][t], acc[5][t], acc[6][t], acc[7][t]);
     }
   }
 }
@@ -102,8 +135,8 @@ __device__ __forceinline__ void column_dot(const uint8_t* base, const MoeShape& 
 // one kernel for both products: MAT 0 = gate_up (K = H rows, 2I columns, input x rows of tokens),
 // MAT 1 = down (K = I rows, H columns, input the activations a of the pairs)
 template <int BITS, int MAT>
-__global__ void __launch_bounds__(THREADS) gemv_kernel(const uint8_t* __restrict__ pool, MoeShape S, int P, int nsplit,
-                                                       const uint16_t* __restrict__ x, Ws W) {
+__global__ void __launch_bounds__(THREADS, 2) gemv_kernel(const uint8_t* __restrict__ pool, MoeShape S, int P, int nsplit,
+                                                          const uint16_t* __restrict__ x, Ws W) {
   const int lane = threadIdx.x & 31;
   pdl_wait();
   pdl_launch_dependents();
@@ -123,24 +156,15 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const uint8_t* __restrict
     const int start = W.g.grp_start[grp], cnt = W.g.grp_count[grp];
     const int r0 = int(int64_t(K) * sp / nsplit), r1 = int(int64_t(K) * (sp + 1) / nsplit);
     const int64_t j0 = int64_t(tile) * 256 + 8 * lane;
+    if (j0 >= ncol || r1 <= r0) continue;  // lanes past the last column (lane-divergent; no shuffles below)
     for (int t0 = 0; t0 < cnt; t0 += NTOK) {
       const int nt = cnt - t0 < NTOK ? cnt - t0 : NTOK;
-      const uint16_t* in[NTOK];
-#pragma unroll
-      for (int t = 0; t < NTOK; ++t) {
-        const int pos = start + t0 + (t < nt ? t : 0);
-        in[t] = MAT == 0 ? x + int64_t(W.g.order[pos] / S.k) * S.H : W.act + int64_t(pos) * S.I;
-      }
-      float acc[8][NTOK] = {};
-      if (j0 < ncol) column_dot<BITS>(base, S, e0, ncol, j0, r0, r1, in, nt, acc);
-#pragma unroll
-      for (int t = 0; t < NTOK; ++t) {
-        if (j0 < ncol && t < nt) {
-          float* dst = W.part + (int64_t(sp) * P + start + t0 + t) * wd + j0;
-          reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0][t], acc[1][t], acc[2][t], acc[3][t]);
-          reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4][t], acc[5][t], acc[6][t], acc[7][t]);
-        }
-      }
+      float* dst0 = W.part + (int64_t(sp) * P + start + t0) * wd + j0;
+      // the token count picks the unrolled width
+      if (nt == 1) column_dot<BITS, MAT, 1>(base, S, e0, ncol, j0, r0, r1, x, W, start + t0, dst0, wd, nt);
+      else if (nt == 2) column_dot<BITS, MAT, 2>(base, S, e0, ncol, j0, r0, r1, x, W, start + t0, dst0, wd, nt);
+      else if (nt <= 4) column_dot<BITS, MAT, 4>(base, S, e0, ncol, j0, r0, r1, x, W, start + t0, dst0, wd, nt);
+      else column_dot<BITS, MAT, NTOK>(base, S, e0, ncol, j0, r0, r1, x, W, start + t0, dst0, wd, nt);
     }
   }
 }

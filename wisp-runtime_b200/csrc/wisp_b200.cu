@@ -10,6 +10,7 @@
 #include "moe_decode_v4.cuh"
 #include "moe_batched.cuh"
 #include "moe_gptoss.cuh"
+#include "ep.cuh"
 #include "quant.cuh"
 
 namespace wisp {
@@ -420,35 +421,59 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   WISP_REQUIRE(workspace_bytes >= batched::ws_bytes(N * k, H, I), "wisp_moe_batched: workspace of %lld bytes is too small (%lld needed)",
                (long long)workspace_bytes, (long long)batched::ws_bytes(N * k, H, I));
   WISP_REQUIRE(aligned(workspace, 256), "wisp_moe_batched: workspace must be 256-byte aligned");
-  const batched::Ws W = batched::ws_carve(workspace, N * k, I);
+  batched::Ws W = batched::ws_carve(workspace, N * k, I);
+  W.xp = batched::ws_xp(workspace, N * k, H, I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms();
   cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
-  const size_t sm_gu = size_t(batched::stage_bytes(H)), sm_dn = size_t(batched::stage_bytes(I));
+  // 4-bit and 2-bit codes with 128-multiple groups go straight into the MMA; 3-bit, 8-bit and finer
+  // groups dequantize to bf16 first
+  const bool nib = (bits == 4 || bits == 2) && group % 128 == 0;
+  if (nib) {
+    const size_t sm_gu = size_t(batched::nib_stage_bytes(H)), sm_dn = size_t(batched::nib_stage_bytes(I));
+    const int64_t nwords = int64_t(N) * H / (32 / bits);
+    const int pgrid = int(nwords / 256 + 1 < int64_t(grid) * 4 ? nwords / 256 + 1 : int64_t(grid) * 4);
+#define WISP_NIB(B)                                                                                                     \
+  if (e == cudaSuccess) e = launch_pdl(batched::permute_rows_kernel<B>, pgrid, 256, 0, s, x, nwords, W.xp);              \
+  if (e == cudaSuccess) e = launch_pdl(batched::grouped_nib_kernel<B, 0>, grid, batched::THREADS, sm_gu, s, pool, S, W.xp, W); \
+  if (e == cudaSuccess) e = launch_pdl(batched::grouped_nib_kernel<B, 2>, grid, batched::THREADS, sm_dn, s, pool, S, W.xp, W);
+    if (bits == 4) {
+      WISP_NIB(4)
+    } else {
+      WISP_NIB(2)
+    }
+#undef WISP_NIB
+  } else {
+    const size_t sm_gu = size_t(batched::stage_bytes(H)), sm_dn = size_t(batched::stage_bytes(I));
 #define WISP_BATCHED(B)                                                                                                \
   if (e == cudaSuccess) e = launch_pdl(batched::grouped_kernel<B, 0>, grid, batched::THREADS, sm_gu, s, pool, S, x, W); \
   if (e == cudaSuccess) e = launch_pdl(batched::grouped_kernel<B, 2>, grid, batched::THREADS, sm_dn, s, pool, S, x, W);
-  switch (bits) {
-    case 8: WISP_BATCHED(8) break;
-    case 4: WISP_BATCHED(4) break;
-    case 3: WISP_BATCHED(3) break;
-    default: WISP_BATCHED(2) break;
-  }
+    switch (bits) {
+      case 8: WISP_BATCHED(8) break;
+      case 4: WISP_BATCHED(4) break;
+      case 3: WISP_BATCHED(3) break;
+      default: WISP_BATCHED(2) break;
+    }
 #undef WISP_BATCHED
-  if (e == cudaSuccess) e = launch_pdl(batched::combine_kernel, grid, 256, 0, s, meta, N, k, H, W, out);
+  }
+  if (e == cudaSuccess) e = launch_pdl(batched::combine_kernel, grid * 4, 256, 0, s, meta, N, k, H, W, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
   return check_launch("moe_batched");
 }
 
-static int gptoss_splits(int P) {
-  const int s = 128 / (P < 1 ? 1 : P);
-  return s < 1 ? 1 : (s > 32 ? 32 : s);
+// K splits of the gpt-oss GEMVs: enough (group, column tile, split) units for about four per warp of
+// the grid (2 CTAs x 8 warps per SM on 148 SMs), estimating the groups as min(pairs, 32)
+static int gptoss_splits(int P, int64_t I) {
+  const int64_t groups = P < 1 ? 1 : (P < 32 ? P : 32);
+  const int64_t tiles = (2 * I + 255) / 256;
+  const int64_t s = 4 * 2 * 148 * 8 / (groups * tiles);
+  return int(s < 1 ? 1 : (s > 32 ? 32 : s));
 }
 
 int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I) {
   if (N < 1 || k < 1 || int64_t(N) * k > batched::MAX_PAIRS || H <= 0 || I <= 0) return -1;
-  return gptoss::ws_bytes(N * k, gptoss_splits(N * k), H, I);
+  return gptoss::ws_bytes(N * k, gptoss_splits(N * k, I), H, I);
 }
 
 int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, const int32_t* experts, int N, int k,
@@ -478,7 +503,7 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   S.ncode = 3 * n * bits / 8;
   S.ng = 3 * n / group;
   S.mat_bytes = n * bits / 8;
-  const int P = N * k, ns = gptoss_splits(P);
+  const int P = N * k, ns = gptoss_splits(P, I);
   WISP_REQUIRE(workspace_bytes >= gptoss::ws_bytes(P, ns, H, I), "wisp_moe_gptoss: workspace too small (%lld needed)",
                (long long)gptoss::ws_bytes(P, ns, H, I));
   WISP_REQUIRE(aligned(workspace, 256), "wisp_moe_gptoss: workspace must be 256-byte aligned");
@@ -688,6 +713,37 @@ int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, co
   if (smem > 32 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   rmsnorm_kernel<<<(unsigned)rows, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
   return check_launch("rmsnorm");
+}
+
+
+int wisp_ep_dispatch(const uint16_t* x, int N, int64_t H, const int64_t* sel, int k, int E_local, int world, int64_t capacity,
+                     int64_t slot_base, uint16_t* send_x, float* send_meta, int32_t* src_pos, void* stream) {
+  WISP_REQUIRE(x && sel && send_x && send_meta && src_pos, "wisp_ep_dispatch: NULL pointer");
+  WISP_REQUIRE(N >= 1 && k >= 1 && int64_t(N) * k <= ep::MAX_PAIRS, "wisp_ep_dispatch: need 1 <= N*k <= %d", ep::MAX_PAIRS);
+  WISP_REQUIRE(world >= 1 && world <= ep::MAX_WORLD && E_local >= 1, "wisp_ep_dispatch: need 1 <= world <= %d, E_local >= 1",
+               ep::MAX_WORLD);
+  WISP_REQUIRE(capacity >= int64_t(N) * k, "wisp_ep_dispatch: capacity %lld < N*k = %d (a rank may send every pair to one peer)",
+               (long long)capacity, N * k);
+  WISP_REQUIRE(H > 0 && H % 8 == 0 && aligned(x, 16) && aligned(send_x, 16), "wisp_ep_dispatch: H %% 8 == 0 and 16-byte aligned rows");
+  const int P = N * k;
+  const int grid = P < 2 * num_sms() ? P : 2 * num_sms();
+  cudaError_t e = launch_pdl(ep::ep_dispatch_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), x, N, H, sel, k, E_local,
+                             world, capacity, slot_base, send_x, send_meta, src_pos);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_dispatch: %s", cudaGetErrorString(e));
+  return check_launch("ep_dispatch");
+}
+
+int wisp_ep_combine(const uint16_t* y_back, int N, int k, int64_t H, const int32_t* src_pos, const float* w, uint16_t* out,
+                    void* stream) {
+  WISP_REQUIRE(y_back && src_pos && w && out, "wisp_ep_combine: NULL pointer");
+  WISP_REQUIRE(N >= 1 && k >= 1 && H > 0 && H % 4 == 0, "wisp_ep_combine: need N, k >= 1 and H %% 4 == 0");
+  WISP_REQUIRE(aligned(y_back, 8) && aligned(out, 8), "wisp_ep_combine: y_back and out must be 8-byte aligned");
+  const int64_t work = int64_t(N) * H / 4;
+  const int64_t g = (work + 255) / 256;
+  const int grid = int(g < 4 * num_sms() ? g : 4 * num_sms());
+  cudaError_t e = launch_pdl(ep::ep_combine_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), y_back, N, k, H, src_pos, w, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_combine: %s", cudaGetErrorString(e));
+  return check_launch("ep_combine");
 }
 
 }  // extern "C"

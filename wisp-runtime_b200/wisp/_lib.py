@@ -41,6 +41,8 @@ SIGNATURES = {
     "wisp_moe_batched": (_I, [_P, _L, _L, _P, _I, _I, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
     "wisp_moe_gptoss_workspace_bytes": (_L, [_I, _I, _L, _L]),
     "wisp_moe_gptoss": (_I, [_P, _L, _L, _P, _P, _I, _I, _P, _L, _L, _I, _I, _P, _P, _P, _L, _P, _P]),
+    "wisp_ep_dispatch": (_I, [_P, _I, _L, _P, _I, _I, _I, _L, _L, _P, _P, _P, _P]),
+    "wisp_ep_combine": (_I, [_P, _I, _I, _L, _P, _P, _P, _P]),
     "wisp_moe_decode_noalloc": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
     "wisp_gemv": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P]),

@@ -3,15 +3,21 @@ contiguously over the ranks of a process group (E / P each); every rank keeps it
 (data-parallel attention), and per MoE layer
 
     1. buckets its (token, choice) pairs by the rank that owns the chosen expert,
-    2. dispatch all-to-all: token vectors + local expert ids, fixed capacity per destination,
+    2. dispatch all-to-all: token vectors + routing of the receiving rank, fixed capacity per destination,
     3. runs its local experts on what it received (the batched MoE kernel, each pair weight 1),
     4. combine all-to-all: the expert outputs go back to the pair's source rank,
     5. sums w[t, j] * y[t, j] over the choices in a fixed order.
 
 Buffers have a fixed capacity C = (tokens per rank) * k per destination (the worst case: every pair to
 one rank), so all shapes are static: no host synchronisation, and the whole exchange can be captured
-in a CUDA graph with NCCL.  Empty capacity slots carry expert id -1 (the kernels skip them).  The
-collective is torch.distributed's all_to_all_single (NCCL over NVLink on the GPU, gloo on CPU).
+in a CUDA graph with NCCL.  The collective is torch.distributed's all_to_all_single (NCCL over NVLink
+on the GPU, gloo on CPU).
+
+On CUDA tensors with a ``slot_base`` (layer -> slot of the layer's first local expert, the same on every
+rank), steps 1 and 5 are single kernels (wisp_ep_dispatch / wisp_ep_combine) and the receiver's routing
+travels as the batched MoE's meta rows [slot, 1] ([-1, 0] for unused capacity), so ``expert_fn`` gets
+(x, meta, layer).  Otherwise (the gloo tests on CPU) the bucketing is plain torch indexing and
+``expert_fn`` gets (x, local expert ids as float with -1 for unused capacity, layer).
 """
 
 from __future__ import annotations
@@ -22,7 +28,7 @@ import torch.distributed as dist
 
 class ExpertParallelMoE:
     def __init__(self, experts_per_layer, k, hidden, tokens_per_rank, expert_fn, group=None, device="cuda",
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, slot_base=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -32,23 +38,34 @@ class ExpertParallelMoE:
         self.lo = self.rank * self.E_local
         self.N = tokens_per_rank
         self.C = tokens_per_rank * k
-        self.expert_fn = expert_fn  # (x [R, H], local ids float [R] (-1 = empty), layer) -> y [R, H]
+        self.expert_fn = expert_fn
+        self.slot_base = slot_base
+        self.kernel_mode = torch.device(device).type == "cuda" and slot_base is not None
         W, C = self.world, self.C
         self.send_x = torch.zeros(W, C, hidden, dtype=dtype, device=device)
-        self.recv_x = torch.zeros_like(self.send_x)
-        self.send_id = torch.full((W, C), -1.0, dtype=torch.float32, device=device)
-        self.recv_id = torch.full_like(self.send_id, -1.0)
-        self.y_back = torch.zeros_like(self.send_x)
-        self.ranks = torch.arange(W, device=device)
+        self.recv_x = torch.zeros_like(self.send_x) if W > 1 else self.send_x
+        if self.kernel_mode:
+            self.send_meta = torch.zeros(W, C, 2, dtype=torch.float32, device=device)
+            self.recv_meta = torch.zeros_like(self.send_meta) if W > 1 else self.send_meta
+            self.src_pos = torch.zeros(tokens_per_rank * k, dtype=torch.int32, device=device)
+            self.out = torch.zeros(tokens_per_rank, hidden, dtype=dtype, device=device)
+        else:
+            self.send_id = torch.full((W, C), -1.0, dtype=torch.float32, device=device)
+            self.recv_id = torch.full_like(self.send_id, -1.0)
+            self.ranks = torch.arange(W, device=device)
+        self.y_back = torch.zeros(W, C, hidden, dtype=dtype, device=device)
 
     def _a2a(self, out, inp):
         if self.world == 1:
-            out.copy_(inp)
+            if out.data_ptr() != inp.data_ptr():
+                out.copy_(inp)
         else:
             dist.all_to_all_single(out, inp, group=self.group)
 
     def forward(self, x, sel, w, layer=0):
         """x [N, H]; sel int64 [N, k] global expert ids; w float32 [N, k] -> [N, H] (x.dtype)."""
+        if self.kernel_mode:
+            return self._forward_kernels(x, sel, w, layer)
         N, k, W, C = x.shape[0], self.k, self.world, self.C
         assert N == self.N and sel.shape == (N, k)
         P = N * k
@@ -72,14 +89,32 @@ class ExpertParallelMoE:
         out = (yb * w.view(N, k, 1)).sum(1)
         return out.to(x.dtype)
 
+    def _forward_kernels(self, x, sel, w, layer):
+        from . import kernels
+
+        N, k, W, C = x.shape[0], self.k, self.world, self.C
+        assert N == self.N and sel.shape == (N, k)
+        kernels.ep_dispatch(x.contiguous(), sel.contiguous(), self.E_local, W, C, self.slot_base(layer), self.send_x,
+                            self.send_meta, self.src_pos)
+        self._a2a(self.recv_x.view(-1), self.send_x.view(-1))
+        self._a2a(self.recv_meta.view(-1), self.send_meta.view(-1))
+        y = self.expert_fn(self.recv_x.view(W * C, self.H), self.recv_meta.view(W * C, 2), layer)
+        if W > 1:
+            self._a2a(self.y_back.view(-1), y.reshape(-1))
+            y = self.y_back.view(W * C, self.H)
+        return kernels.ep_combine(y, self.src_pos, w.contiguous(), self.out)
+
 
 def batched_expert_fn(pool, layer_slots, n, H, I, bits, group):
     """expert_fn running this rank's experts with the batched MoE kernel: local id e of layer l is slot
-    layer_slots(l, e) of ``pool``; every received pair gets weight 1 (the source applies w)."""
+    layer_slots(l, e) of ``pool``; every received pair gets weight 1 (the source applies w).  Takes the
+    receiver meta rows [slot, 1] (kernel mode) or local ids (-1 = unused capacity)."""
     from . import kernels
 
-    def fn(xr, ids, layer):
-        R = xr.shape[0]
+    def fn(xr, ids_or_meta, layer):
+        if ids_or_meta.dim() == 2:  # meta rows from wisp_ep_dispatch
+            return kernels.moe_batched(pool, ids_or_meta, xr, 1, n, H, I, bits, group)
+        ids = ids_or_meta
         base = float(layer_slots(layer, 0))
         slots = torch.where(ids >= 0, ids + base, torch.full_like(ids, -1.0))
         meta = torch.stack([slots, torch.ones_like(ids)], 1).contiguous()

@@ -30,6 +30,8 @@ __all__ = [
     "moe_decode_paged",
     "moe_batched",
     "moe_gptoss",
+    "ep_dispatch",
+    "ep_combine",
     "rope_decode",
     "rmsnorm",
     "gemv",
@@ -206,6 +208,36 @@ def moe_gptoss(pool, meta, experts, x, k, H, I, bits, gate_up_bias, down_bias, g
         x.data_ptr(), H, I, bits, group, gate_up_bias.data_ptr(), down_bias.data_ptr(), workspace.data_ptr(),
         workspace.numel(), out.data_ptr(), _stream(x),
     )
+    return out
+
+
+def ep_dispatch(x, sel, E_local, world, capacity, slot_base, send_x, send_meta, src_pos):
+    """Pack this rank's (token, choice) pairs for the dispatch all-to-all (wisp_ep_dispatch): x bf16
+    [N, H], sel int64 [N, k] global expert ids -> send_x [world, capacity, H], send_meta [world,
+    capacity, 2] ([slot_base + local id, 1], [-1, 0] when unused), src_pos int32 [N*k]."""
+    _need_cuda(x, sel, send_x, send_meta, src_pos)
+    _bf16(x, send_x)
+    if sel.dtype != torch.int64 or not sel.is_contiguous():
+        raise WispError("sel must be contiguous int64")
+    if send_meta.dtype != torch.float32 or src_pos.dtype != torch.int32:
+        raise WispError("send_meta must be float32 and src_pos int32")
+    N, k = sel.shape
+    H = x.shape[-1]
+    assert send_x.numel() == world * capacity * H and send_meta.numel() == world * capacity * 2 and src_pos.numel() == N * k
+    _lib.call(
+        "wisp_ep_dispatch", x.data_ptr(), N, H, sel.data_ptr(), k, E_local, world, capacity, int(slot_base), send_x.data_ptr(),
+        send_meta.data_ptr(), src_pos.data_ptr(), _stream(x),
+    )
+
+
+def ep_combine(y_back, src_pos, w, out):
+    """out[t] = bf16(sum_j w[t, j] * y_back[src_pos[t*k + j]]), choices in order (wisp_ep_combine)."""
+    _need_cuda(y_back, src_pos, w, out)
+    _bf16(y_back, out)
+    if w.dtype != torch.float32 or not w.is_contiguous():
+        raise WispError("w must be contiguous float32")
+    N, k = w.shape
+    _lib.call("wisp_ep_combine", y_back.data_ptr(), N, k, out.shape[-1], src_pos.data_ptr(), w.data_ptr(), out.data_ptr(), _stream(out))
     return out
 
 
