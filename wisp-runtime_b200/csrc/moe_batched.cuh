@@ -25,7 +25,7 @@ namespace batched {
 constexpr int MAX_PAIRS = 2048;  // N * k
 constexpr int WARPS = 8;
 constexpr int THREADS = WARPS * 32;
-constexpr int NT_MAX = 4;        // token n-tiles (of 8) per pass over the weights
+constexpr int NT_MAX = 1;        // token n-tiles (of 8) per pass over the weights
 
 constexpr int TOK = 8 * NT_MAX;  // tokens per pass over an expert's weights
 
@@ -373,7 +373,7 @@ __host__ __device__ inline int64_t nib_stage_bytes(int64_t K) {
 // the start of a unit every warp asks L2 for its 16 rows (one contiguous range per matrix) and the
 // per-lane register loads then find them there.
 template <int BITS, int MAT>
-__global__ void __launch_bounds__(THREADS, 1) grouped_nib_kernel(const uint8_t* __restrict__ pool, MoeShape S,
+__global__ void __launch_bounds__(THREADS, 3) grouped_nib_kernel(const uint8_t* __restrict__ pool, MoeShape S,
                                                                  const uint16_t* __restrict__ xp, Ws W) {
   extern __shared__ __align__(16) uint16_t xs[];  // [TOK][K + NIB_PAD] bf16, then xsum [TOK][K / 128] fp32
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;

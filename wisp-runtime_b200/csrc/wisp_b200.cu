@@ -427,8 +427,8 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   const int grid = num_sms();
   cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
-  // 4-bit and 2-bit codes with 128-multiple groups go straight into the MMA; 3-bit, 8-bit and finer
-  // groups dequantize to bf16 first
+  // 4-bit and 2-bit codes with 128-multiple groups go straight into the MMA (two CTAs per SM, units
+  // taken from a counter); 3-bit, 8-bit and finer groups dequantize to bf16 first
   const bool nib = (bits == 4 || bits == 2) && group % 128 == 0;
   if (nib) {
     const size_t sm_gu = size_t(batched::nib_stage_bytes(H)), sm_dn = size_t(batched::nib_stage_bytes(I));
@@ -436,8 +436,8 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
     const int pgrid = int(nwords / 256 + 1 < int64_t(grid) * 4 ? nwords / 256 + 1 : int64_t(grid) * 4);
 #define WISP_NIB(B)                                                                                                     \
   if (e == cudaSuccess) e = launch_pdl(batched::permute_rows_kernel<B>, pgrid, 256, 0, s, x, nwords, W.xp);              \
-  if (e == cudaSuccess) e = launch_pdl(batched::grouped_nib_kernel<B, 0>, grid, batched::THREADS, sm_gu, s, pool, S, W.xp, W); \
-  if (e == cudaSuccess) e = launch_pdl(batched::grouped_nib_kernel<B, 2>, grid, batched::THREADS, sm_dn, s, pool, S, W.xp, W);
+  if (e == cudaSuccess) e = launch_pdl(batched::grouped_nib_kernel<B, 0>, 3 * grid, batched::THREADS, sm_gu, s, pool, S, W.xp, W); \
+  if (e == cudaSuccess) e = launch_pdl(batched::grouped_nib_kernel<B, 2>, 3 * grid, batched::THREADS, sm_dn, s, pool, S, W.xp, W);
     if (bits == 4) {
       WISP_NIB(4)
     } else {
