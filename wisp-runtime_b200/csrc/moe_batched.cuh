@@ -143,9 +143,14 @@ __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ m
       const int gid = scan[i] - 1;
       W.grp_slot[gid] = int(s);
       W.grp_start[gid] = i;
-      int e = i + 1;
-      while (e < P && unsigned(key[e] >> 32) == s) ++e;
-      W.grp_count[gid] = e - i;
+    }
+  }
+  __syncthreads();  // group starts are written (global memory, this CTA)
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {  // the last pair of each group closes it
+    const unsigned s = unsigned(key[i] >> 32);
+    if (s != 0xFFFFFFFFu && (i + 1 == P || unsigned(key[i + 1] >> 32) != s)) {
+      const int gid = scan[i] - 1;
+      W.grp_count[gid] = i + 1 - W.grp_start[gid];
     }
   }
   if (threadIdx.x == 0) W.n_groups[0] = n2 > 0 ? scan[P - 1 < 0 ? 0 : P - 1] : 0;
@@ -202,7 +207,7 @@ __device__ __forceinline__ void row_unit(const uint8_t* base, const MoeShape& S,
                                          uint32_t (&pr)[16]) {
   const int64_t e = int64_t(mat) * S.H * S.I + row * K + kc;  // element index in the expert's code stream
   const Unit<BITS> u = load_unit<BITS>(base + e * BITS / 8);
-  const int64_t gi = e / S.group;
+  const int64_t gi = group_of(e, S);
   const float s = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + gi));
   const float m = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + S.ng + gi));
   dequant_unit<BITS>(u, s, m, pr);
@@ -266,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_kernel(const uint8_t* __re
           const int64_t row = r0 + g + (q & 1) * 8;
           const int64_t e = int64_t(mat) * S.H * S.I + row * K + kb + 32 * c;
           uu[q] = load_unit<BITS>(base + e * BITS / 8);
-          const int64_t gi = e / S.group;
+          const int64_t gi = group_of(e, S);
           sc[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + gi));
           mn[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + S.ng + gi));
         }
@@ -458,7 +463,7 @@ __global__ void __launch_bounds__(THREADS, 3) grouped_nib_kernel(const uint8_t* 
           const Unit<BITS> uu = load_unit<BITS>(base + e * BITS / 8);
 #pragma unroll
           for (int i = 0; i < BITS; ++i) ww[q][i] = uu.w[i];
-          const int64_t gi = e / S.group;
+          const int64_t gi = group_of(e, S);
           sc[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + gi));
           mn[q] = f16_bits_to_f32(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + S.ncode) + S.ng + gi));
         }

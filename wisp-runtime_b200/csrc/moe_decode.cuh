@@ -16,7 +16,21 @@ struct MoeShape {
   int64_t ncode;      // bytes of the code region
   int64_t ng;         // groups per expert
   int64_t mat_bytes;  // code bytes per matrix
+  int glog;           // log2(group) when group is a power of two, else -1
 };
+
+// group index of element e of an expert's code stream (3n < 2^32 for every accepted shape): a shift
+// when group is a power of two, else one 32-bit division
+__device__ __forceinline__ int64_t group_of(int64_t e, const MoeShape& S) {
+  return S.glog >= 0 ? (e >> S.glog) : int64_t(uint32_t(e) / uint32_t(S.group));
+}
+
+__host__ __device__ inline int log2_or_neg(int v) {
+  if (v <= 0 || (v & (v - 1)) != 0) return -1;
+  int l = 0;
+  while ((1 << l) < v) ++l;
+  return l;
+}
 
 // Routing computed inside the MoE kernels from the router logits (instead of a meta buffer written
 // by a separate top-k launch): softmax in fp32, the k largest (ties: lower expert id), renormalised

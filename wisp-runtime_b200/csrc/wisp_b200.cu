@@ -187,6 +187,7 @@ static int moe_shape(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   S.mat_bytes = n * bits / 8;
   S.gshift = 0;
   for (int gq = group / 128; gq > 1 && (gq & 1) == 0; gq >>= 1) ++S.gshift;
+  S.glog = log2_or_neg(group);
   return WISP_OK;
 }
 
@@ -500,6 +501,7 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   S.I = int(I);
   S.group = group;
   S.gshift = 0;
+  S.glog = log2_or_neg(group);
   S.ncode = 3 * n * bits / 8;
   S.ng = 3 * n / group;
   S.mat_bytes = n * bits / 8;
