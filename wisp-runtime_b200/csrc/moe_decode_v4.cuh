@@ -163,7 +163,19 @@ __device__ __forceinline__ float quad_sum(float v) {
 }
 
 // ------------------------------------------------------------------------------------------------
-template <int BITS>
+// Source of routed expert j.  PAGED = false compiles the host-store branch away (slots only), so the
+// resident-pool path is the same code whether or not paging exists.
+template <bool PAGED>
+__device__ __forceinline__ const uint8_t* src_of(float f, const MoeShape& S, const uint8_t* pool, const MoeRoute& RT, bool& host) {
+  if constexpr (PAGED) {
+    return expert_src(f, S, pool, RT, host);
+  } else {
+    host = false;
+    return (f >= 0.0f && f < float(S.nslots)) ? pool + int64_t(f) * S.nbytes : nullptr;
+  }
+}
+
+template <int BITS, bool PAGED>
 __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* __restrict__ pool,
                                                                 const float* __restrict__ meta,
                                                                 const uint16_t* __restrict__ x, MoeShape S,
@@ -195,7 +207,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     float* rs = reinterpret_cast<float*>(sm + Lg.off_route);
     route_from_logits<true>(RT, S.k, rs, rs + 64, rs + 96);
     mt = rs;
-    if (RT.miss_count && blockIdx.x == 0 && int(threadIdx.x) < S.k && rs[threadIdx.x] <= -1.0f) atomicAdd(RT.miss_count, 1);
+    if (PAGED && RT.miss_count && blockIdx.x == 0 && int(threadIdx.x) < S.k && rs[threadIdx.x] <= -1.0f) atomicAdd(RT.miss_count, 1);
   }
 
   // one warp (lanes 0-5) issues block bi into region bi % R: the 8 gate rows and the same 8 up rows
@@ -205,11 +217,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int blk = b0 + bi;
     const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
     bool host;
-    const uint8_t* base = expert_src(mt[j], S, pool, RT, host);
+    const uint8_t* base = src_of<PAGED>(mt[j], S, pool, RT, host);
     const bool ok = base != nullptr;
     uint8_t* reg = sm + int64_t(r) * Lg.region;
     const uint32_t cb = uint32_t(CH * Lg.row_bytes);
-    if (host) {  // not resident: the warp copies the same ranges from the host store, then arrives
+    if (PAGED && host) {  // not resident: the warp copies the same ranges from the host store, then arrives
       warp_copy_g2s(reg, base + int64_t(row0) * Lg.row_bytes, cb, lane);
       warp_copy_g2s(reg + cb, base + S.mat_bytes + int64_t(row0) * Lg.row_bytes, cb, lane);
       for (int arr = 0; arr < 4; ++arr) {
@@ -255,7 +267,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const int64_t gpr_d = S.I / S.group, row_d = int64_t(S.I) * BITS / 8;
     for (int j = lane; j < S.k && h1 > h0; j += 32) {
       bool host;
-      const uint8_t* base = expert_src(mt[j], S, pool, RT, host);
+      const uint8_t* base = src_of<PAGED>(mt[j], S, pool, RT, host);
       if (!base || host) continue;
       prefetch_l2(base + 2 * S.mat_bytes + int64_t(h0) * row_d, uint32_t(int64_t(h1 - h0) * row_d));
       const int64_t len = 2 * int64_t(h1 - h0) * gpr_d;
@@ -319,7 +331,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
       const int blk = b0 + bi;
       const int j = blk * CH / S.I, row0 = blk * CH - j * S.I;
       bool host;
-      const bool ok = expert_src(mt[j], S, pool, RT, host) != nullptr;
+      const bool ok = src_of<PAGED>(mt[j], S, pool, RT, host) != nullptr;
       const uint32_t sskip = window(S.ncode + 2 * ((sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
       const uint32_t mskip = window(S.ncode + 2 * (S.ng + (sarr >> 1) * ngm + int64_t(row0) * Lg.gpr), 1).skip;
       const uint8_t* sw = reg + 2 * cb;
@@ -363,12 +375,12 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     const float us = halves[((bi * NSPLIT) * CH + rw) * 2 + 1] + halves[((bi * NSPLIT + 1) * CH + rw) * 2 + 1];
     const int rr = (b0 + bi) * CH + rw;
     bool host;
-    a_out[rr] = expert_src(mt[rr / S.I], S, pool, RT, host) ? silu_mul(gs, us) : 0.0f;
+    a_out[rr] = src_of<PAGED>(mt[rr / S.I], S, pool, RT, host) ? silu_mul(gs, us) : 0.0f;
   }
 }
 
 // ------------------------------------------------------------------------------------------------
-template <int BITS>
+template <int BITS, bool PAGED>
 __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __restrict__ pool,
                                                              const float* __restrict__ meta,
                                                              const float* __restrict__ a, MoeShape S,
@@ -398,24 +410,19 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   }
   // ---- the down rows of every routed expert: one bulk copy of the CTA's contiguous rows plus the
   //      scale and min windows, issued before waiting on the gate/up grid (the routing is final)
-  __shared__ uint32_t host_mask;  // routed experts read from the host store (k <= 32)
   if (warp == 0) {
-    uint32_t hm = 0;
     for (int j = lane; j < S.k; j += 32) {
       mbar_init(&bars[j], 1);
       mbar_fence_init();
       const float f = RT.logits ? mt[j] : __ldcg(meta + j);
       bool host;
-      const uint8_t* base = expert_src(f, S, pool, RT, host);
+      const uint8_t* base = src_of<PAGED>(f, S, pool, RT, host);
       if (!base) flag(WISP_STATUS_BAD_SLOT);
       if (!base || nrows <= 0) {
         mbar_expect_tx(&bars[j], 0);
         continue;
       }
-      if (host) {  // copied below by the whole CTA, which then arrives on the barrier
-        hm |= 1u << j;
-        continue;
-      }
+      if (host) continue;  // copied below by the whole CTA, which then arrives on the barrier
       const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
       const Win wm = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
       const uint32_t cb = uint32_t(int64_t(nrows) * Ld.row_bytes);
@@ -425,11 +432,16 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
       bulk_g2s(dst + 16 * Ld.row_bytes, base + ws.start, ws.bytes, &bars[j]);
       bulk_g2s(dst + 16 * Ld.row_bytes + Ld.sc_win, base + wm.start, wm.bytes, &bars[j]);
     }
-    hm = __reduce_or_sync(0xffffffffu, hm);
-    if (lane == 0) host_mask = hm;
   }
-  __syncthreads();
-  if (const uint32_t hm = host_mask) {
+  // experts read from the host store (paged calls only): the same mask in every thread, from the routing
+  uint32_t hm = 0;
+  if (PAGED && RT.host_store && nrows > 0)
+    for (int j = 0; j < S.k; ++j) {
+      bool host;
+      src_of<PAGED>(RT.logits ? mt[j] : __ldcg(meta + j), S, pool, RT, host);
+      hm |= host ? (1u << j) : 0u;
+    }
+  if (hm) {
     // non-resident experts: the same three ranges from the host store, one warp per (expert, range)
     const Win ws = window(S.ncode + 2 * (2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
     const Win wm = window(S.ncode + 2 * (S.ng + 2 * ngm + int64_t(h0) * Ld.gpr), 2 * int64_t(nrows) * Ld.gpr);
@@ -437,7 +449,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
       const int j = task / 3, part = task - 3 * j;
       if (!((hm >> j) & 1u)) continue;
       bool host;
-      const uint8_t* base = expert_src(RT.logits ? mt[j] : __ldcg(meta + j), S, pool, RT, host);
+      const uint8_t* base = src_of<PAGED>(RT.logits ? mt[j] : __ldcg(meta + j), S, pool, RT, host);
       uint8_t* dst = sm + int64_t(j) * Ld.per_expert;
       if (part == 0) warp_copy_g2s(dst, base + 2 * S.mat_bytes + int64_t(h0) * Ld.row_bytes, int64_t(nrows) * Ld.row_bytes, lane);
       else if (part == 1) warp_copy_g2s(dst + 16 * Ld.row_bytes, base + ws.start, ws.bytes, lane);
@@ -481,7 +493,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   for (int piece = warp; piece < npieces; piece += DN_WARPS) {
     const int j = piece / NSPLIT, sp = piece % NSPLIT;
     bool host;
-    const bool ok = expert_src(mt[j], S, pool, RT, host) != nullptr;
+    const bool ok = src_of<PAGED>(mt[j], S, pool, RT, host) != nullptr;
     const float wj = mt[S.k + j];
     if (!ok || nrows <= 0) continue;
     mbar_wait(&bars[j], 0);

@@ -282,10 +282,15 @@ static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, 
   const int64_t gsm = v4::gu_layout(S.H, S.I, S.k, S.group, bits, nctas).bytes;
   const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
   cudaError_t e = cudaSuccess;
-#define WISP_V4(B)                                                                                          \
-  e = launch_pdl(v4::gate_up_kernel<B>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch, RT); \
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode gate/up: %s", cudaGetErrorString(e));        \
-  e = launch_pdl(v4::down_kernel<B>, nctas, v4::DN_THREADS, size_t(Ld.bytes), s, pool, meta, (const float*)scratch, S, out, RT);
+  const bool paged = RT.host_store != nullptr;
+#define WISP_V4(B)                                                                                                    \
+  e = paged ? launch_pdl(v4::gate_up_kernel<B, true>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch, RT)   \
+            : launch_pdl(v4::gate_up_kernel<B, false>, nctas, v4::GU_THREADS, size_t(gsm), s, pool, meta, x, S, scratch, RT); \
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode gate/up: %s", cudaGetErrorString(e));                  \
+  e = paged ? launch_pdl(v4::down_kernel<B, true>, nctas, v4::DN_THREADS, size_t(Ld.bytes), s, pool, meta,              \
+                         (const float*)scratch, S, out, RT)                                                           \
+            : launch_pdl(v4::down_kernel<B, false>, nctas, v4::DN_THREADS, size_t(Ld.bytes), s, pool, meta,             \
+                         (const float*)scratch, S, out, RT);
   switch (bits) {
     case 4: WISP_V4(4) break;
     case 3: WISP_V4(3) break;
