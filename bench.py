@@ -39,6 +39,8 @@ EP_BATCH = 64  # moe-ep: tokens per step over all ranks (config 4 batch)
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up + one down launch (4-bit, this shape),
 # from the ncu capture summarised in profiles/moe_decode_q4_qwen3_gate_up_down_full.md
 NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
+# DRAM read + write of the batched gate/up and down grids for one 64-token Zipf(1.1) layer (ncu)
+NCU_TRAFFIC_BATCHED_LAYER = 96_768_256 + 3_038_720 + 48_437_504 + 489_472
 
 
 GO_L, GO_H, GO_I, GO_E, GO_K = 24, 2880, 2880, 32, 4  # gpt-oss-20b MoE shape (config 5)
@@ -895,6 +897,18 @@ class EPStack:
     def e2e_bytes(self):
         return self.N * H * 2, self.N * H * 2
 
+    def roofline(self, ms_per_step, peak, peak_src, world):
+        """Per layer on one GPU: its share of the distinct routed experts' bytes over the step time per
+        layer (exchanges, grouping and combine included, so a lower bound on the grouped kernels' rate)."""
+        bytes_layer = self.distinct / world * self.nb + 2 * self.N * H * 2
+        us = ms_per_step / L * 1e3
+        ach = bytes_layer / (us * 1e-6) / 1e9
+        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                # ncu, gate/up + down grids of one 64-token Zipf(1.1) layer (profiles/moe_batched_q4_zipf64_gate_up_down_full.md)
+                "traffic": NCU_TRAFFIC_BATCHED_LAYER if world == 1 else None,
+                "kernel": "batched MoE layer (dispatch, grouping, gate/up and down grids, combine) per GPU, timed as the "
+                "step time / layers", "bytes_per_call": bytes_layer, "us_per_call": us, "peak_source": peak_src}
+
     def release(self):
         self.graph = None  # graphs holding NCCL calls go before the process group
 
@@ -972,9 +986,10 @@ def main():
     clk = clocks.stop()
     if a.workload == "decoder" and bench.paged:
         paging = bench.paging_stats(a.warmup + 2 * a.steps + 3)
-    if a.workload == "gptoss-moe":
+    if a.workload in ("gptoss-moe", "moe-ep"):
         peak, src = load_peaks()
-        roof = bench.roofline(ms / a.steps, peak, f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src)
+        src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
+        roof = bench.roofline(ms / a.steps, peak, src) if a.workload == "gptoss-moe" else bench.roofline(ms / a.steps, peak, src, world)
     else:
         roof, _ = moe_roofline(pool, nbytes, a.bits) if pool.shape[0] >= K_TOP * L else (None, None)
     if a.workload == "decoder":
