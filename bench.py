@@ -64,6 +64,8 @@ def parse():
                     "the MoE kernels, page-ins one token behind (device), or the reference's per-layer host "
                     "decision with page-in before use (host)")
     ap.add_argument("--no-prefetch", action="store_true", help="host paging: no next-layer expert prefetch")
+    ap.add_argument("--transport", default="auto", choices=["auto", "nccl", "p2p"],
+                    help="moe-ep exchange: NCCL all-to-alls or kernel stores into peer memory (auto: p2p when N > 1)")
     a = ap.parse_args()
     global L
     L = a.layers
@@ -114,8 +116,10 @@ def workload_config(a, n):
         return {
             "workload": f"qwen3-30b-a3b batched moe stack (config 4 MoE): {EP_BATCH} tokens in total, {L} layers x {E} "
             f"experts top-{K_TOP}, Zipf(1.1) expert popularity, {a.bits}-bit g{G}, experts sharded expert-parallel "
-            f"over {n} GPU(s) ({E // n} per layer each), NCCL all-to-all dispatch and combine, rmsnorm+residual "
-            "between layers (no attention)",
+            f"over {n} GPU(s) ({E // n} per layer each), "
+            + ("dispatch and combine as kernel stores into peer memory (CUDA IPC over NVLink, flags)"
+               if (a.transport == "p2p" or (a.transport == "auto" and n > 1)) else "NCCL all-to-all dispatch and combine")
+            + ", rmsnorm+residual between layers (no attention)",
             "model": "Qwen3-30B-A3B-shaped (random init)",
             "global_batch": EP_BATCH,
             "seq_len": 1,
@@ -849,14 +853,18 @@ class EPStack:
         self.norm_w = (1.0 + 0.1 * torch.randn(L, H, device=device, generator=g)).to(torch.bfloat16)
         self.x0 = torch.randn(self.N, H, device=device, generator=gen).to(torch.bfloat16)
         fn = batched_expert_fn(self.pool, lambda l, e: l * self.El + e, n, H, I, a.bits, G)
-        self.ep = ExpertParallelMoE(E, K_TOP, H, self.N, fn, device=device, slot_base=lambda l: l * self.El)
+        self.transport = a.transport if a.transport != "auto" else ("p2p" if world > 1 else "nccl")
+        assert self.transport == "nccl" or L % 2 == 0, "the p2p buffer sets alternate per layer: use an even layer count"
+        self.ep = ExpertParallelMoE(E, K_TOP, H, self.N, fn, device=device, slot_base=lambda l: l * self.El,
+                                    transport=self.transport)
         self.h = torch.empty(self.N, H, dtype=torch.bfloat16, device=device)
         self.xn = torch.empty_like(self.h)
         self.kernels = kernels
 
     def launches_per_step(self):
         # rmsnorm, dispatch, the batched MoE (grouping, permute, gate/up, down, combine), combine per layer
-        return L * 8
+        # (+ the dispatch wait and the return with the p2p transport)
+        return L * (10 if self.transport == "p2p" else 8)
 
     def _body(self):
         self.h.copy_(self.x0)
@@ -911,6 +919,7 @@ class EPStack:
 
     def release(self):
         self.graph = None  # graphs holding NCCL calls go before the process group
+        self.ep.close()
 
 
 # ------------------------------------------------------------------------------------------------

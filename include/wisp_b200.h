@@ -155,6 +155,33 @@ int wisp_ep_dispatch(const uint16_t* x, int N, int64_t H, const int64_t* sel, in
 int wisp_ep_combine(const uint16_t* y_back, int N, int k, int64_t H, const int32_t* src_pos, const float* w, uint16_t* out,
                     void* stream);
 
+/* Peer-memory variant of the exchange (one process per GPU on one node, NVLink): every rank owns one
+ * device allocation of wisp_ep_p2p_bytes(world, capacity, H) bytes (receive rows and routing rows,
+ * returned results, flags, counters; two buffer sets) that every peer maps with CUDA IPC.
+ * peers_host[r] = rank r's allocation as mapped in this process (the local one for r = rank).
+ * Call n of a run (the same sequence on every rank) uses buffer set n % 2:
+ *   wisp_ep_dispatch_p2p  stores this rank's rows and routing rows straight into each destination's
+ *                         receive buffers and then raises its dispatch flag there (release, system scope)
+ *   wisp_ep_wait          (phase 0) waits until every source's dispatch flag reached this call
+ *   ...                   the batched MoE on receive rows [world * capacity, H] / routing [.., 2] of the set
+ *   wisp_ep_return_p2p    stores result row (s, c) into rank s's returned-results buffer, raises its flag
+ *   wisp_ep_combine_p2p   waits for every rank's return flag, then the fixed-order weighted sum
+ * Waits are bounded (2 s): a peer that never signals sets WISP_STATUS_WAIT_TIMEOUT instead of hanging.
+ * No TMA: peers are written with ordinary stores.  The kernel-fused form of the dispatch / combine
+ * all-to-alls that wisp_ep_dispatch / wisp_ep_combine surround with NCCL. */
+int wisp_ipc_alloc(int64_t bytes, void** ptr_host, uint8_t* handle_host); /* cudaMalloc (zeroed) + 64-byte IPC handle */
+int wisp_ipc_open(const uint8_t* handle_host, void** ptr_host);          /* map a peer's allocation */
+int wisp_ipc_close(void* ptr);
+int wisp_ipc_free(void* ptr);
+int64_t wisp_ep_p2p_bytes(int world, int64_t capacity, int64_t H);       /* -1 if world is outside [1, 8] */
+int wisp_ep_dispatch_p2p(const uint16_t* x, int N, int64_t H, const int64_t* sel, int k, int E_local, int world, int rank,
+                         int64_t capacity, int64_t slot_base, int set, void* const* peers_host, int32_t* src_pos, void* stream);
+int wisp_ep_wait(void* local, int world, int64_t capacity, int64_t H, int phase, void* stream);
+int wisp_ep_return_p2p(const uint16_t* y, int world, int rank, int64_t capacity, int64_t H, int set, void* const* peers_host,
+                       void* stream);
+int wisp_ep_combine_p2p(void* local, int world, int64_t capacity, int64_t H, int set, int N, int k, const int32_t* src_pos,
+                        const float* w, uint16_t* out, void* stream);
+
 /* ---- gpt-oss experts ------------------------------------------------------------------------------ */
 /* Bytes of the workspace wisp_moe_gptoss needs (host-only; -1 if N*k is outside [1, 2048]). */
 int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I);

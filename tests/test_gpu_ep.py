@@ -31,6 +31,12 @@ def _tokens(rank, device):
     return x, sel, w
 
 
+def _lib_status(dev):
+    from wisp import _lib
+
+    return _lib.device_status(dev.index, clear=True)
+
+
 def _worker(rank, world, port, q):
     from datetime import timedelta
 
@@ -53,11 +59,15 @@ def _worker(rank, world, port, q):
         meta = torch.cat([sel.float(), w], 1).contiguous()
         ref = kernels.moe_batched(pool, meta, x, K, H * I, H, I, BITS, G)
         errs = []
-        for slot_base in (None, lambda l: l * El):  # torch bucketing, then the dispatch/combine kernels
-            ep = ExpertParallelMoE(E, K, H, N, fn, device=dev, slot_base=slot_base)
-            out = ep.forward(x, sel, w)
+        # torch bucketing + NCCL, the dispatch/combine kernels + NCCL, then the peer-memory transport
+        for slot_base, transport in ((None, "nccl"), (lambda l: l * El, "nccl"), (lambda l: l * El, "p2p")):
+            ep = ExpertParallelMoE(E, K, H, N, fn, device=dev, slot_base=slot_base, transport=transport)
+            for _ in range(3):  # consecutive calls alternate the p2p buffer sets
+                out = ep.forward(x, sel, w)
             torch.cuda.synchronize()
             errs.append((out.float() - ref.float()).abs().max().item() / ref.float().abs().max().item())
+            ep.close()
+        assert kernels.__name__ and _lib_status(dev) == 0
         q.put((rank, max(errs)))
     finally:
         dist.barrier()
@@ -132,3 +142,51 @@ def test_dispatch_buckets_by_destination_rank():
     kernels.ep_combine(send_x.view(world * C, H), src_pos, w, out)
     want = (w.view(N, K, 1) * x.float().view(N, 1, H)).sum(1)
     assert (out.float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+
+
+def test_p2p_transport_one_rank_matches_kernel_path():
+    """The peer-memory transport with world = 1 (the exchange is this GPU's own buffers): the same
+    result as the kernel path over consecutive calls (alternating buffer sets, increasing epochs), and
+    no wait ran out."""
+    from wisp import _lib
+    from wisp.ep import ExpertParallelMoE, batched_expert_fn
+
+    dev = torch.device("cuda", 0)
+    pool = _setup(dev)
+    fn = batched_expert_fn(pool, lambda l, e: l * E + e, H * I, H, I, BITS, G)
+    a = ExpertParallelMoE(E, K, H, N, fn, device=dev, slot_base=lambda l: l * E)
+    b = ExpertParallelMoE(E, K, H, N, fn, device=dev, slot_base=lambda l: l * E, transport="p2p")
+    _lib.device_status(0, clear=True)
+    for seed in range(4):
+        x, sel, w = _tokens(seed, dev)
+        assert torch.equal(a.forward(x, sel, w), b.forward(x, sel, w)), seed
+    torch.cuda.synchronize()
+    assert _lib.device_status(0) == 0
+    b.close()
+
+
+def test_p2p_wait_runs_out_and_reports():
+    """A wait for a flag that nothing raises ends after its bound (2 s) with WISP_STATUS_WAIT_TIMEOUT
+    instead of hanging, and the context stays usable."""
+    from wisp import _lib, kernels
+
+    dev = torch.device("cuda", 0)
+    ex = kernels.P2PExchange(1, 0, 8, 64, dev)
+    ex.open([ex.handle])
+    x = torch.zeros(1, 64, dtype=torch.bfloat16, device=dev)
+    sel = torch.zeros(1, 1, dtype=torch.int64, device=dev)
+    src_pos = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.device_status(0, clear=True)
+    ex.dispatch(x, sel, 4, 0, 0, src_pos)  # raises the dispatch flag to epoch 1
+    ex.wait_dispatch(x)
+    torch.cuda.synchronize()
+    assert _lib.device_status(0) == 0
+    _lib.call("wisp_ep_wait", ex.local, 1, 8, 64, 1, _stream0())  # the return flag is never raised
+    torch.cuda.synchronize()
+    assert _lib.device_status(0, clear=True) & _lib.STATUS_WAIT_TIMEOUT
+    assert (x + 1).sum().item() == 64  # the context still works
+    ex.close()
+
+
+def _stream0():
+    return torch.cuda.current_stream(0).cuda_stream

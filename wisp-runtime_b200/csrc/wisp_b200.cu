@@ -1,5 +1,6 @@
 // libwisp_b200.so: the C ABI declared in include/wisp_b200.h.  One translation unit (the kernels live
 // in the included .cuh files) so the per-device status word is a single __device__ symbol.
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -751,6 +752,116 @@ int wisp_ep_combine(const uint16_t* y_back, int N, int k, int64_t H, const int32
   cudaError_t e = launch_pdl(ep::ep_combine_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), y_back, N, k, H, src_pos, w, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_combine: %s", cudaGetErrorString(e));
   return check_launch("ep_combine");
+}
+
+
+// ---- peer-memory expert-parallel exchange ---------------------------------------------------------------
+int wisp_ipc_alloc(int64_t bytes, void** ptr_host, uint8_t* handle_host) {
+  WISP_REQUIRE(bytes > 0 && ptr_host && handle_host, "wisp_ipc_alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, size_t(bytes));
+  if (e == cudaSuccess) e = cudaMemset(p, 0, size_t(bytes));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return fail(WISP_ERR_CUDA, "wisp_ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  std::memcpy(handle_host, &h, 64);
+  *ptr_host = p;
+  return WISP_OK;
+}
+
+int wisp_ipc_open(const uint8_t* handle_host, void** ptr_host) {
+  WISP_REQUIRE(handle_host && ptr_host, "wisp_ipc_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle_host, 64);
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ipc_open: %s", cudaGetErrorString(e));
+  *ptr_host = p;
+  return WISP_OK;
+}
+
+int wisp_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ipc_close: %s", cudaGetErrorString(e));
+  return WISP_OK;
+}
+
+int wisp_ipc_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ipc_free: %s", cudaGetErrorString(e));
+  return WISP_OK;
+}
+
+int64_t wisp_ep_p2p_bytes(int world, int64_t capacity, int64_t H) {
+  if (world < 1 || world > ep::MAX_P2P || capacity < 1 || H < 1) return -1;
+  return ep::p2p_layout(world, capacity, H).bytes;
+}
+
+static int p2p_peers(void* const* peers_host, int world, int rank, ep::Peers& P) {
+  WISP_REQUIRE(peers_host && world >= 1 && world <= ep::MAX_P2P && rank >= 0 && rank < world,
+               "ep p2p: need 1 <= world <= %d, 0 <= rank < world and the peers' base pointers", ep::MAX_P2P);
+  for (int r = 0; r < ep::MAX_P2P; ++r) {
+    P.base[r] = r < world ? static_cast<uint8_t*>(peers_host[r]) : nullptr;
+    if (r < world) WISP_REQUIRE(P.base[r] && aligned(P.base[r], 256), "ep p2p: peer %d base must be a 256-byte aligned mapping", r);
+  }
+  return WISP_OK;
+}
+
+int wisp_ep_dispatch_p2p(const uint16_t* x, int N, int64_t H, const int64_t* sel, int k, int E_local, int world, int rank,
+                         int64_t capacity, int64_t slot_base, int set, void* const* peers_host, int32_t* src_pos, void* stream) {
+  WISP_REQUIRE(x && sel && src_pos, "wisp_ep_dispatch_p2p: NULL pointer");
+  WISP_REQUIRE(N >= 1 && k >= 1 && int64_t(N) * k <= ep::MAX_PAIRS, "wisp_ep_dispatch_p2p: need 1 <= N*k <= %d", ep::MAX_PAIRS);
+  WISP_REQUIRE(E_local >= 1 && capacity >= int64_t(N) * k && (set == 0 || set == 1), "wisp_ep_dispatch_p2p: bad capacity or set");
+  WISP_REQUIRE(H > 0 && H % 8 == 0 && aligned(x, 16), "wisp_ep_dispatch_p2p: H %% 8 == 0 and 16-byte aligned x");
+  ep::Peers P;
+  int rc = p2p_peers(peers_host, world, rank, P);
+  if (rc) return rc;
+  const int Pn = N * k;
+  const int grid = Pn < 2 * num_sms() ? Pn : 2 * num_sms();
+  cudaError_t e = launch_pdl(ep::ep_dispatch_p2p_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), x, N, H, sel, k,
+                             E_local, world, rank, capacity, slot_base, set, P, src_pos);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_dispatch_p2p: %s", cudaGetErrorString(e));
+  return check_launch("ep_dispatch_p2p");
+}
+
+int wisp_ep_wait(void* local, int world, int64_t capacity, int64_t H, int phase, void* stream) {
+  WISP_REQUIRE(local && world >= 1 && world <= ep::MAX_P2P && (phase == 0 || phase == 1), "wisp_ep_wait: bad arguments");
+  cudaError_t e = launch_pdl(ep::ep_wait_kernel, 1, 32, 0, static_cast<cudaStream_t>(stream), static_cast<uint8_t*>(local), world,
+                             capacity, H, phase);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_wait: %s", cudaGetErrorString(e));
+  return check_launch("ep_wait");
+}
+
+int wisp_ep_return_p2p(const uint16_t* y, int world, int rank, int64_t capacity, int64_t H, int set, void* const* peers_host,
+                       void* stream) {
+  WISP_REQUIRE(y && (set == 0 || set == 1) && H % 8 == 0 && aligned(y, 16), "wisp_ep_return_p2p: bad arguments");
+  ep::Peers P;
+  int rc = p2p_peers(peers_host, world, rank, P);
+  if (rc) return rc;
+  const int64_t rows = int64_t(world) * capacity;
+  const int grid = int(rows < 2 * num_sms() ? rows : 2 * num_sms());
+  cudaError_t e = launch_pdl(ep::ep_return_p2p_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), y, world, rank, capacity, H,
+                             set, P);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_return_p2p: %s", cudaGetErrorString(e));
+  return check_launch("ep_return_p2p");
+}
+
+int wisp_ep_combine_p2p(void* local, int world, int64_t capacity, int64_t H, int set, int N, int k, const int32_t* src_pos,
+                        const float* w, uint16_t* out, void* stream) {
+  WISP_REQUIRE(local && src_pos && w && out && (set == 0 || set == 1), "wisp_ep_combine_p2p: bad arguments");
+  WISP_REQUIRE(world >= 1 && world <= ep::MAX_P2P && N >= 1 && k >= 1 && H % 4 == 0 && aligned(out, 8),
+               "wisp_ep_combine_p2p: bad shape");
+  const int64_t work = int64_t(N) * H / 4;
+  const int64_t g = (work + 255) / 256;
+  const int grid = int(g < 4 * num_sms() ? g : 4 * num_sms());
+  cudaError_t e = launch_pdl(ep::ep_combine_p2p_kernel, grid, 256, 0, static_cast<cudaStream_t>(stream), static_cast<uint8_t*>(local),
+                             world, capacity, set, N, k, H, src_pos, w, out);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_ep_combine_p2p: %s", cudaGetErrorString(e));
+  return check_launch("ep_combine_p2p");
 }
 
 }  // extern "C"

@@ -43,6 +43,15 @@ SIGNATURES = {
     "wisp_moe_gptoss": (_I, [_P, _L, _L, _P, _P, _I, _I, _P, _L, _L, _I, _I, _P, _P, _P, _L, _P, _P]),
     "wisp_ep_dispatch": (_I, [_P, _I, _L, _P, _I, _I, _I, _L, _L, _P, _P, _P, _P]),
     "wisp_ep_combine": (_I, [_P, _I, _I, _L, _P, _P, _P, _P]),
+    "wisp_ipc_alloc": (_I, [_L, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
+    "wisp_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "wisp_ipc_close": (_I, [_P]),
+    "wisp_ipc_free": (_I, [_P]),
+    "wisp_ep_p2p_bytes": (_L, [_I, _L, _L]),
+    "wisp_ep_dispatch_p2p": (_I, [_P, _I, _L, _P, _I, _I, _I, _I, _L, _L, _I, ctypes.POINTER(ctypes.c_void_p), _P, _P]),
+    "wisp_ep_wait": (_I, [_P, _I, _L, _L, _I, _P]),
+    "wisp_ep_return_p2p": (_I, [_P, _I, _I, _L, _L, _I, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "wisp_ep_combine_p2p": (_I, [_P, _I, _L, _L, _I, _I, _I, _P, _P, _P, _P]),
     "wisp_moe_decode_noalloc": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
     "wisp_gemv": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P]),

@@ -28,7 +28,7 @@ import torch.distributed as dist
 
 class ExpertParallelMoE:
     def __init__(self, experts_per_layer, k, hidden, tokens_per_rank, expert_fn, group=None, device="cuda",
-                 dtype=torch.bfloat16, slot_base=None):
+                 dtype=torch.bfloat16, slot_base=None, transport="nccl"):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -54,6 +54,24 @@ class ExpertParallelMoE:
             self.recv_id = torch.full_like(self.send_id, -1.0)
             self.ranks = torch.arange(W, device=device)
         self.y_back = torch.zeros(W, C, hidden, dtype=dtype, device=device)
+        # transport "p2p": the exchanges are kernel stores into peer memory (CUDA IPC over NVLink) with
+        # flags instead of NCCL all-to-alls; buffer set = call index % 2 (so a captured step must make an
+        # even number of calls, e.g. one per layer of an even layer count)
+        self.p2p = None
+        self.calls = 0
+        if transport == "p2p":
+            assert self.kernel_mode, "the p2p transport needs CUDA tensors and slot_base"
+            from .kernels import P2PExchange
+
+            self.p2p = P2PExchange(W, self.rank, C, hidden, device)
+            handles = [None] * W
+            if W > 1:
+                dist.all_gather_object(handles, self.p2p.handle, group=self.group)
+            else:
+                handles = [self.p2p.handle]
+            self.p2p.open(handles)
+            if W > 1:
+                dist.barrier(group=self.group)  # every rank has mapped every allocation
 
     def _a2a(self, out, inp):
         if self.world == 1:
@@ -89,9 +107,33 @@ class ExpertParallelMoE:
         out = (yb * w.view(N, k, 1)).sum(1)
         return out.to(x.dtype)
 
+    def _forward_p2p(self, x, sel, w, layer):
+        N, k, W, C = x.shape[0], self.k, self.world, self.C
+        assert N == self.N and sel.shape == (N, k)
+        st = self.calls % 2
+        self.calls += 1
+        ex = self.p2p
+        ex.dispatch(x.contiguous(), sel.contiguous(), self.E_local, self.slot_base(layer), st, self.src_pos)
+        ex.wait_dispatch(x)
+        y = self.expert_fn(ex.recv_x(st), ex.recv_meta(st), layer)
+        ex.give_back(y.contiguous(), st)
+        return ex.combine(st, self.src_pos, w.contiguous(), self.out)
+
+    def close(self):
+        """Unmap the peers' buffers, wait for every rank to do the same, then free this rank's buffer."""
+        if self.p2p is not None:
+            torch.cuda.synchronize(self.out.device)
+            self.p2p.close_peers()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self.p2p.close()
+            self.p2p = None
+
     def _forward_kernels(self, x, sel, w, layer):
         from . import kernels
 
+        if self.p2p is not None:
+            return self._forward_p2p(x, sel, w, layer)
         N, k, W, C = x.shape[0], self.k, self.world, self.C
         assert N == self.N and sel.shape == (N, k)
         kernels.ep_dispatch(x.contiguous(), sel.contiguous(), self.E_local, W, C, self.slot_base(layer), self.send_x,

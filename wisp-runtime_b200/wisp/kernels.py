@@ -32,6 +32,7 @@ __all__ = [
     "moe_gptoss",
     "ep_dispatch",
     "ep_combine",
+    "P2PExchange",
     "rope_decode",
     "rmsnorm",
     "gemv",
@@ -239,6 +240,114 @@ def ep_combine(y_back, src_pos, w, out):
     N, k = w.shape
     _lib.call("wisp_ep_combine", y_back.data_ptr(), N, k, out.shape[-1], src_pos.data_ptr(), w.data_ptr(), out.data_ptr(), _stream(out))
     return out
+
+
+class _DevArray:
+    """A device range described by __cuda_array_interface__ (to view library-owned memory as a tensor)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False), "version": 3}
+
+
+class P2PExchange:
+    """One rank's side of the peer-memory expert-parallel exchange (wisp_ep_*_p2p): a library-owned
+    device allocation mapped by every peer through CUDA IPC.  ``open(handles)`` maps the peers' handles
+    (gathered from all ranks, in rank order); ``recv_x(set)`` / ``recv_meta(set)`` view the receive
+    buffers the batched MoE reads.  Layout as p2p_layout in csrc/ep.cuh."""
+
+    def __init__(self, world, rank, capacity, hidden, device):
+        import ctypes
+
+        self.world, self.rank, self.C, self.H, self.device = world, rank, capacity, hidden, torch.device(device)
+        nb = _lib.lib().wisp_ep_p2p_bytes(world, capacity, hidden)
+        if nb < 0:
+            raise WispError(f"ep p2p: world {world} outside [1, 8]")
+        self.nbytes = nb
+        ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            _lib.call("wisp_ipc_alloc", nb, ctypes.byref(ptr), handle)
+        self.local = ptr.value
+        self.handle = handle.raw
+        self.peers = None
+        self._opened = []
+        self._views()
+
+    def open(self, handles):
+        import ctypes
+
+        assert len(handles) == self.world
+        bases = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self.local)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.call("wisp_ipc_open", h, ctypes.byref(p))
+                self._opened.append(p.value)
+                bases.append(p.value)
+        self.peers = (ctypes.c_void_p * self.world)(*bases)
+
+    def _off(self):
+        W, C, H = self.world, self.C, self.H
+        r256 = lambda v: (v + 255) // 256 * 256  # noqa: E731
+        recv_meta = r256(2 * W * C * H * 2)
+        y_back = r256(recv_meta + 2 * W * C * 2 * 4)
+        return 0, recv_meta, y_back
+
+    def _views(self):
+        W, C, H = self.world, self.C, self.H
+        o = self._off()
+        self._rx = [torch.as_tensor(_DevArray(self.local + o[0] + st * W * C * H * 2, (W * C, H), "<i2"), device=self.device)
+                    .view(torch.bfloat16) for st in (0, 1)]
+        self._rm = [torch.as_tensor(_DevArray(self.local + o[1] + st * W * C * 2 * 4, (W * C, 2), "<f4"), device=self.device)
+                    for st in (0, 1)]
+
+    def recv_x(self, st):
+        return self._rx[st]
+
+    def recv_meta(self, st):
+        return self._rm[st]
+
+    def dispatch(self, x, sel, E_local, slot_base, st, src_pos):
+        _need_cuda(x, sel, src_pos)
+        _bf16(x)
+        N, k = sel.shape
+        _lib.call(
+            "wisp_ep_dispatch_p2p", x.data_ptr(), N, self.H, sel.data_ptr(), k, E_local, self.world, self.rank, self.C,
+            int(slot_base), st, self.peers, src_pos.data_ptr(), _stream(x),
+        )
+
+    def wait_dispatch(self, stream_of):
+        _lib.call("wisp_ep_wait", self.local, self.world, self.C, self.H, 0, _stream(stream_of))
+
+    def give_back(self, y, st):
+        _bf16(y)
+        _lib.call("wisp_ep_return_p2p", y.data_ptr(), self.world, self.rank, self.C, self.H, st, self.peers, _stream(y))
+
+    def combine(self, st, src_pos, w, out):
+        N, k = w.shape
+        _lib.call(
+            "wisp_ep_combine_p2p", self.local, self.world, self.C, self.H, st, N, k, src_pos.data_ptr(), w.data_ptr(),
+            out.data_ptr(), _stream(out),
+        )
+        return out
+
+    def close_peers(self):
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.call("wisp_ipc_close", p)
+        self._opened = []
+        self.peers = None
+
+    def close(self):
+        """Unmap the peers and free the local allocation (every peer must have unmapped it first)."""
+        self.close_peers()
+        self._rx = self._rm = None  # views of the allocation go first
+        if self.local:
+            with torch.cuda.device(self.device):
+                _lib.call("wisp_ipc_free", self.local)
+            self.local = None
 
 
 def moe_decode_noalloc(pool, meta, x, k, n, H, I, bits, group=128, out=None):
