@@ -183,6 +183,134 @@ __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ m
   pdl_launch_dependents();
 }
 
+// ---- grouping by counting sort (pools up to CS_MAX_SLOTS slots) -------------------------------------------
+// The same outputs as group_kernel (groups in slot order, pairs of a group contiguous, invalid pairs
+// after the valid ones, the work list) from a shared-memory histogram of the slots: one atomic per
+// pair, two block scans over the slots, one scatter.  Pairs inside a group come in atomic order, which
+// changes nothing downstream: every pair's result is computed on its own.
+constexpr int CS_MAX_SLOTS = 24576;  // counts + starts: 192 KB of shared memory
+__host__ __device__ inline size_t count_group_smem(int64_t nslots) { return size_t(nslots) * 8; }
+
+// exclusive block scan of two values (blockDim.x a multiple of 32, <= 1024); totals to every thread
+__device__ __forceinline__ void block_scan2(int a, int g, int& ea, int& eg, int& ta, int& tg, int* wa, int* wg) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int ia = a, ig = g;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ya = __shfl_up_sync(0xffffffffu, ia, o), yg = __shfl_up_sync(0xffffffffu, ig, o);
+    if (lane >= o) {
+      ia += ya;
+      ig += yg;
+    }
+  }
+  if (lane == 31) {
+    wa[warp] = ia;
+    wg[warp] = ig;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int va = lane < nw ? wa[lane] : 0, vg = lane < nw ? wg[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ya = __shfl_up_sync(0xffffffffu, va, o), yg = __shfl_up_sync(0xffffffffu, vg, o);
+      if (lane >= o) {
+        va += ya;
+        vg += yg;
+      }
+    }
+    if (lane < nw) {
+      wa[lane] = va;
+      wg[lane] = vg;
+    }
+  }
+  __syncthreads();
+  const int pa = warp > 0 ? wa[warp - 1] : 0, pg = warp > 0 ? wg[warp - 1] : 0;
+  ea = pa + ia - a;
+  eg = pg + ig - g;
+  ta = wa[nw - 1];
+  tg = wg[nw - 1];
+  __syncthreads();  // wa / wg may be reused
+}
+
+__global__ void __launch_bounds__(1024) count_group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {
+  extern __shared__ int cs[];  // [nslots] counts, then [nslots] group starts
+  __shared__ int rank_in[MAX_PAIRS];
+  __shared__ int slot_of[MAX_PAIRS];
+  __shared__ int wa[32], wg[32];
+  __shared__ int tail;
+  __shared__ int bcnt[NT_MAX + 1], bofs[NT_MAX + 1];
+  int* cnt = cs;
+  int* st = cs + nslots;
+  const int P = N * k, t = threadIdx.x, nt = blockDim.x;
+  pdl_wait();
+  for (int64_t i = t; i < nslots; i += nt) cnt[i] = 0;
+  if (t == 0) tail = 0;
+  if (t <= NT_MAX) bcnt[t] = 0;
+  __syncthreads();
+  for (int p = t; p < P; p += nt) {
+    const int tk = p / k, j = p - tk * k;
+    const float f = meta[int64_t(tk) * 2 * k + j];
+    int sl = -1;
+    if (f >= 0.0f && f < float(nslots)) sl = int(f);
+    else if (f != -1.0f) flag(WISP_STATUS_BAD_SLOT);  // -1: an empty pair (padding), skipped silently
+    slot_of[p] = sl;
+    rank_in[p] = sl >= 0 ? atomicAdd(&cnt[sl], 1) : -1;
+  }
+  __syncthreads();
+  // slot range of this thread: counts -> starts, non-empty slots -> groups
+  const int64_t per = (nslots + nt - 1) / nt;
+  const int64_t lo = int64_t(t) * per, hi = lo + per < nslots ? lo + per : nslots;
+  int a = 0, g = 0;
+  for (int64_t i = lo; i < hi; ++i) {
+    a += cnt[i];
+    g += cnt[i] > 0 ? 1 : 0;
+  }
+  int ea, eg, ta, tg;
+  block_scan2(a, g, ea, eg, ta, tg, wa, wg);
+  for (int64_t i = lo; i < hi; ++i) {
+    const int c = cnt[i];
+    st[i] = ea;
+    if (c > 0) {
+      W.grp_slot[eg] = int(i);
+      W.grp_start[eg] = ea;
+      W.grp_count[eg] = c;
+      ++eg;
+    }
+    ea += c;
+  }
+  if (t == 0) W.n_groups[0] = tg;
+  __syncthreads();
+  for (int p = t; p < P; p += nt) {
+    const int sl = slot_of[p];
+    const int pos = sl >= 0 ? st[sl] + rank_in[p] : ta + atomicAdd(&tail, 1);  // invalid pairs after the valid ones
+    W.order[pos] = p;
+    W.posof[p] = sl >= 0 ? pos : -1;
+  }
+  __syncthreads();  // group arrays (global memory, this CTA)
+  // the (group, pass) work list, bucketed by the pass's token tiles (as group_kernel)
+  for (int gid = t; gid < tg; gid += nt) {
+    const int c = W.grp_count[gid];
+    for (int t0 = 0; t0 < c; t0 += TOK) atomicAdd(&bcnt[min(NT_MAX, (c - t0 + 7) / 8)], 1);
+  }
+  __syncthreads();
+  if (t == 0) {
+    int o = 0;
+    for (int ntl = NT_MAX; ntl >= 1; --ntl) {
+      bofs[ntl] = o;
+      o += bcnt[ntl];
+    }
+    W.n_gp[0] = o;
+    W.next_unit[0] = 0;
+    W.next_unit[1] = 0;
+  }
+  __syncthreads();
+  for (int gid = t; gid < tg; gid += nt) {
+    const int c = W.grp_count[gid];
+    for (int t0 = 0, pp = 0; t0 < c; t0 += TOK, ++pp) W.gp_list[atomicAdd(&bofs[min(NT_MAX, (c - t0 + 7) / 8)], 1)] = gid << 8 | pp;
+  }
+  pdl_launch_dependents();
+}
+
 // ---- dequantized A fragments ------------------------------------------------------------------------
 // 32 codes (one unit) of a row -> 16 bf16 pairs: pair p = codes 2p, 2p+1 -> bf16(q*s + m)
 template <int BITS>

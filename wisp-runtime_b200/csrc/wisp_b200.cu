@@ -245,8 +245,9 @@ static int num_sms() {
 
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {
+  // dynamic shared memory beyond the default 48 KB window (static + dynamic) needs the opt-in
+  if (smem > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (smem > 48 * 1024) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     // the whole unified L1 as shared memory, so CTAs of the next kernel in a PDL chain fit beside
     // this one's (the carveout is chosen per launch; a smaller one would keep them out)
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
@@ -432,7 +433,9 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   W.xp = batched::ws_xp(workspace, N * k, H, I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms();
-  cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
+  cudaError_t e = nslots <= batched::CS_MAX_SLOTS
+                      ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W)
+                      : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
   // 4-bit and 2-bit codes with 128-multiple groups go straight into the MMA (two CTAs per SM, units
   // taken from a counter); 3-bit, 8-bit and finer groups dequantize to bf16 first
@@ -518,7 +521,9 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   const gptoss::Ws W = gptoss::ws_carve(workspace, P, ns, H, I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms() * 2;
-  cudaError_t e = launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
+  cudaError_t e = nslots <= batched::CS_MAX_SLOTS
+                      ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W.g)
+                      : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
 #define WISP_GPTOSS(B)                                                                                                 \
   if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 0>, grid, gptoss::THREADS, 0, s, pool, S, P, ns, x, W);     \
   if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, 256, 0, s, S, P, ns, experts, gate_up_bias, W);        \
