@@ -186,9 +186,9 @@ __device__ __forceinline__ void p2p_wait_flags(const uint32_t* flags, int world,
 // local counter (reset by that CTA), `ctr_epoch` the local call counter (bumped when bump != 0)
 __device__ __forceinline__ void p2p_publish(const Peers& P, const P2PLayout& L, int world, int rank, int phase, uint32_t epoch,
                                             uint32_t* done, uint32_t* ctr_epoch, bool bump) {
-  __threadfence_system();  // this CTA's peer stores before its arrival
-  __syncthreads();
+  __syncthreads();  // the CTA's peer stores happen before thread 0's fence (cumulative), one fence per CTA
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const uint32_t prev = atomicAdd(done, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();  // every CTA's stores (their fences precede their arrivals)
