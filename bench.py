@@ -240,7 +240,7 @@ def time_moe_kernel(pool, nbytes, bits, reps=20, variant=0):
     g = torch.Generator(device=dev).manual_seed(99)
     x = torch.randn(L, H, device=dev, generator=g).to(torch.bfloat16)
     out = torch.empty(L, H, dtype=torch.bfloat16, device=dev)
-    scratch = kernels.moe_scratch(K_TOP, I, dev)
+    scratch = kernels.moe_scratch(K_TOP, I, dev, H, bits, G)
     metas = []
     nslots = pool.shape[0]
     for l in range(L):
@@ -521,7 +521,7 @@ class MoEStack:
         self.h = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.xn = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.moe = torch.zeros(H, dtype=torch.bfloat16, device=dev)
-        self.scratch = kernels.moe_scratch(K_TOP, I, dev)
+        self.scratch = kernels.moe_scratch(K_TOP, I, dev, H, W["bits"], G)
         self.meta_in = torch.zeros(L, 2 * K_TOP, dtype=torch.float32, device=dev)  # e2e routing input
         self.x_in = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.graphs = []

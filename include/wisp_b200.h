@@ -73,27 +73,38 @@ int wisp_unpack_codes(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, co
                       int64_t n, int bits, uint8_t* codes, void* stream);
 
 /* ---- fused MoE decode, one token ---------------------------------------------------------------- */
+/* Floats of scratch that let every path run for this shape on the current device: at least k*I (the
+ * two-kernel path's intermediate a), k * cs * H when the single-grid variant 3 applies (its partial
+ * output vectors, cs = CTAs per expert).  Host-only; -1 for an invalid shape. */
+int64_t wisp_moe_scratch_floats(int k, int64_t H, int64_t I, int bits, int group);
+
 /* out[h] = sum_j w_j * Wd_j[h,:] . (silu(Wg_j x) * (Wu_j x)), dequant folded into the dot products,
  * weights read straight from the slot pool.  meta: fp32 [2k] = [slot_0..slot_{k-1}, w_0..w_{k-1}] on
- * the device.  x, out: bf16 [H].  scratch: fp32 [k*I] (intermediate a = silu(g)*u).
+ * the device.  x, out: bf16 [H].  scratch: fp32 [scratch_floats], at least k*I (the intermediate
+ * a = silu(g) * u); wisp_moe_scratch_floats() floats also admit variant 3.
  * bits in {8, 4, 3, 2}; H, I multiples of 32 and of group; group a multiple of 32; pool 16-byte
  * aligned with nbytes a multiple of 16.
  * Replaces wisp/kernels.py:188-203 (moe_decode_q4_fast), :310-322 (moe_decode_q3_fast), and adds the
  * 2-bit and 8-bit variants the reference runs through dequant + bmm (wisp/moe.py:122-130). */
 int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
-                    const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch, uint16_t* out,
-                    void* stream);
+                    const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch, int64_t scratch_floats,
+                    uint16_t* out, void* stream);
 
 /* Same computation with an explicit kernel choice: 0 = automatic (what wisp_moe_decode does),
  * 1 = warp-per-row CUDA-core kernels (any supported shape), 2 = TMA bulk copies into shared memory
  * feeding the warp-level integer MMA (u8 codes x int8 activation limbs, exact int32 sums), gate/up
  * and down as two kernels chained by programmatic dependent launch, the gate/up grid pulling the
  * down rows into L2 while it computes (bits 4/3/2, group a multiple of 128, H and I multiples of
- * 128, k <= 32, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise).
+ * 128, k <= 32, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise), 3 = one grid of
+ * k * cs CTAs: CTA (j, r) computes rows [i0, i1) of a_j (the variant-2 math) and at once their
+ * contribution to every output row from the down matrix's column slice (no grid-wide dependency),
+ * then a small grid sums the k * cs partials in a fixed order (the variant-2 shape rules, a plan
+ * that fits shared memory, scratch of wisp_moe_scratch_floats() floats; only on request: its
+ * serialized load / gate-up / down / combine phases measured slower than variant 2).
  * Automatic = 2 when it applies, else 1. */
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,
-                            uint16_t* out, int variant, void* stream);
+                            int64_t scratch_floats, uint16_t* out, int variant, void* stream);
 
 /* wisp_moe_decode with the router's top-k folded into the MoE kernels: every CTA computes the
  * routing from the router logits (bf16 [E], E <= 512) itself -- softmax in fp32, the k largest (ties:
@@ -103,7 +114,7 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
  * Replaces wisp/graphdec.py:177-182 + :194-203 (router softmax/top-k, then moe_decode_q*_fast). */
 int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, const uint16_t* logits, int E, int k,
                            int norm_topk, const int32_t* slot_table, int64_t base, float* row, const uint16_t* x, int64_t H,
-                           int64_t I, int bits, int group, float* scratch, uint16_t* out, void* stream);
+                           int64_t I, int bits, int group, float* scratch, int64_t scratch_floats, uint16_t* out, void* stream);
 
 /* wisp_moe_decode_routed over a partially resident expert pool with no host decision: slot_table
  * (int32 [host_rows], required) maps key = base + e to a slot, or to a negative value when the expert
@@ -119,7 +130,7 @@ int wisp_moe_decode_routed(const uint8_t* pool, int64_t nslots, int64_t nbytes, 
 int wisp_moe_decode_paged(const uint8_t* pool, int64_t nslots, int64_t nbytes, const uint16_t* logits, int E, int k,
                           int norm_topk, const int32_t* slot_table, int64_t base, const uint8_t* store_host, int64_t host_rows,
                           int* miss_count, float* row, const uint16_t* x, int64_t H, int64_t I, int bits, int group,
-                          float* scratch, uint16_t* out, void* stream);
+                          float* scratch, int64_t scratch_floats, uint16_t* out, void* stream);
 
 /* ---- batched MoE decode ------------------------------------------------------------------------ */
 /* Bytes of the workspace wisp_moe_batched needs for N tokens of k choices (host-only; -1 if N*k is

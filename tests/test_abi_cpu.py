@@ -52,8 +52,8 @@ def test_expert_nbytes_rejects_bad_shapes():
 def test_invalid_arguments_fail_on_host_without_a_gpu():
     """Argument checks run before any launch, so they report cleanly even on a CPU-only machine."""
     L = _lib.lib()
-    rc = L.wisp_moe_decode(None, 8, 2506752, None, 8, None, 2048, 768, 4, 128, None, None, None)
+    rc = L.wisp_moe_decode(None, 8, 2506752, None, 8, None, 2048, 768, 4, 128, None, 0, None, None)
     assert rc == _lib.WISP_ERR_INVALID
     assert b"NULL" in L.wisp_last_error()
     with pytest.raises(_lib.WispError, match="bits must be"):
-        _lib.call("wisp_moe_decode", 16, 8, 2506752, 16, 8, 16, 2048, 768, 5, 128, 16, 16, None)
+        _lib.call("wisp_moe_decode", 16, 8, 2506752, 16, 8, 16, 2048, 768, 5, 128, 16, 8 * 768, 16, None)

@@ -33,10 +33,11 @@ SIGNATURES = {
     "wisp_quantize": (_I, [_P, _I, _L, _L, _I, _I, _P, _P]),
     "wisp_dequant": (_I, [_P, _L, _L, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_unpack_codes": (_I, [_P, _L, _L, _P, _L, _L, _I, _P, _P]),
-    "wisp_moe_decode": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _P]),
-    "wisp_moe_decode_variant": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P, _I, _P]),
-    "wisp_moe_decode_routed": (_I, [_P, _L, _L, _P, _I, _I, _I, _P, _L, _P, _P, _L, _L, _I, _I, _P, _P, _P]),
-    "wisp_moe_decode_paged": (_I, [_P, _L, _L, _P, _I, _I, _I, _P, _L, _P, _L, _P, _P, _P, _L, _L, _I, _I, _P, _P, _P]),
+    "wisp_moe_scratch_floats": (_L, [_I, _L, _L, _I, _I]),
+    "wisp_moe_decode": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
+    "wisp_moe_decode_variant": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _L, _P, _I, _P]),
+    "wisp_moe_decode_routed": (_I, [_P, _L, _L, _P, _I, _I, _I, _P, _L, _P, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
+    "wisp_moe_decode_paged": (_I, [_P, _L, _L, _P, _I, _I, _I, _P, _L, _P, _L, _P, _P, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
     "wisp_moe_batched_workspace_bytes": (_L, [_I, _I, _L, _L]),
     "wisp_moe_batched": (_I, [_P, _L, _L, _P, _I, _I, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
     "wisp_moe_gptoss_workspace_bytes": (_L, [_I, _I, _L, _L]),

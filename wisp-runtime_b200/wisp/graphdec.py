@@ -54,7 +54,7 @@ class GraphDecoder:
         self.rlog = torch.zeros(self.E, **d)
         self.rows = torch.zeros(self.L, 2 * self.k, dtype=torch.float32, device=dev)  # per layer [experts | weights]
         self.meta = torch.zeros(2 * self.k, dtype=torch.float32, device=dev)
-        self.scratch = kernels.moe_scratch(self.k, self.I, dev)
+        self.scratch = kernels.moe_scratch(self.k, self.I, dev, self.H, cfg.bits, cfg.group)
         self.miss_count = torch.zeros(1, dtype=torch.int32, device=dev) if store_host is not None else None
         self.attn_ws = kernels.attn_workspace(self.Hq, self.Hk, self.D, self.tmax, dev)
         self.argmax_ws = torch.zeros(256, dtype=torch.int64, device=dev)

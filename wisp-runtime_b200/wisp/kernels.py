@@ -56,10 +56,23 @@ def _need_cuda(*ts):
             raise WispError("wisp kernels need CUDA tensors (there is no CPU path)")
 
 
-def moe_scratch(k, I, device):
-    """Scratch for moe_decode_fast (the fp32 intermediate a, k*I values); reusable by calls that do
-    not overlap."""
-    return torch.empty(k * I, dtype=torch.float32, device=device)
+def moe_scratch(k, I, device, H=None, bits=4, group=128):
+    """Scratch for the fused MoE calls; reusable by calls that do not overlap.  With H (and the
+    quantization) it is sized for the fastest path (wisp_moe_scratch_floats: the single-grid path's
+    partial vectors), else k*I floats (the two-kernel path's intermediate a)."""
+    n = k * I
+    if H is not None:
+        with torch.cuda.device(torch.device(device)) if torch.device(device).type == "cuda" else _null():
+            n = max(n, int(_lib.lib().wisp_moe_scratch_floats(k, H, I, bits, group)))
+    return torch.empty(n, dtype=torch.float32, device=device)
+
+
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
 
 
 def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratch=None, variant=0):
@@ -76,7 +89,7 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
         raise WispError(f"x must be bfloat16 (got {x.dtype})")
     x = x.contiguous()
     if scratch is None:
-        scratch = moe_scratch(k, I, x.device)
+        scratch = moe_scratch(k, I, x.device, H, bits, group)
     elif scratch.numel() < k * I or scratch.dtype != torch.float32 or not scratch.is_contiguous():
         raise WispError(f"scratch must be a contiguous float32 tensor of >= {k * I} elements")
     if out is None:
@@ -94,6 +107,7 @@ def moe_decode_fast(pool, meta, x, k, n, H, I, bits, group=128, out=None, scratc
         bits,
         group,
         scratch.data_ptr(),
+        scratch.numel(),
         out.data_ptr(),
         variant,
         _stream(x),
@@ -114,13 +128,13 @@ def moe_decode_routed(pool, logits, x, k, n, H, I, bits, group=128, norm_topk=Tr
         raise WispError("slot_table must be contiguous int32")
     x = x.contiguous()
     if scratch is None:
-        scratch = moe_scratch(k, I, x.device)
+        scratch = moe_scratch(k, I, x.device, H, bits, group)
     if out is None:
         out = torch.empty((H,), dtype=x.dtype, device=x.device)
     _lib.call(
         "wisp_moe_decode_routed", pool.data_ptr(), pool.shape[0], pool.shape[1], logits.data_ptr(), logits.numel(), k,
         1 if norm_topk else 0, _ptr(slot_table), int(base), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(),
-        out.data_ptr(), _stream(x),
+        scratch.numel(), out.data_ptr(), _stream(x),
     )
     return out
 
@@ -153,13 +167,14 @@ def moe_decode_paged(pool, logits, x, k, n, H, I, bits, group=128, norm_topk=Tru
             raise WispError("miss_count must be int32")
     x = x.contiguous()
     if scratch is None:
-        scratch = moe_scratch(k, I, x.device)
+        scratch = moe_scratch(k, I, x.device, H, bits, group)
     if out is None:
         out = torch.empty((H,), dtype=x.dtype, device=x.device)
     _lib.call(
         "wisp_moe_decode_paged", pool.data_ptr(), pool.shape[0], pool.shape[1], logits.data_ptr(), logits.numel(), k,
         1 if norm_topk else 0, slot_table.data_ptr(), int(base), store_host.data_ptr(), store_host.shape[0],
-        _ptr(miss_count), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(), out.data_ptr(), _stream(x),
+        _ptr(miss_count), _ptr(row), x.data_ptr(), H, I, bits, group, scratch.data_ptr(), scratch.numel(), out.data_ptr(),
+        _stream(x),
     )
     return out
 
