@@ -85,3 +85,52 @@ def test_gptoss_20b_layer_vs_oracle(N):
     want = O.gptoss_ref(pool.cpu().numpy(), experts.cpu().numpy()[tok], w.cpu().numpy()[tok], _np(x)[tok], H, I, bits, G,
                         gub.view(torch.int16).cpu().numpy().view(np.uint16), db.view(torch.int16).cpu().numpy().view(np.uint16))
     assert _rel(_np(out)[tok], want) < 1e-2
+
+
+def _layer_case(H, bits, G, N, E, k, seed, hot=None):
+    """One gpt-oss layer of shape H = I through the library and the oracle on a sample of tokens, and the
+    same call twice (bitwise equal). `hot` routes every token to experts drawn from the first `hot`
+    ids, so each expert's tokens span several 8-token passes."""
+    from wisp import kernels, quant
+
+    I = H
+    n = H * I
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    logits = torch.randn(N, E, device="cuda", generator=gen)
+    if hot is not None:
+        logits[:, hot:] -= 100.0
+    experts, w = _route(logits.to(torch.bfloat16), k)
+    used = torch.unique(experts.long()).tolist()
+    nb = quant.expert_nbytes(n, bits, G)
+    pool = torch.zeros((E, nb), dtype=torch.uint8, device="cuda")
+    for e in used:
+        w3 = (torch.randn(1, 3, n, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+        pool[e : e + 1] = quant.quantize_batch(w3, bits, G)
+    gub = (torch.randn(E, 2 * I, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    db = (torch.randn(E, H, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    x = torch.randn(N, H, device="cuda", generator=gen).to(torch.bfloat16)
+    meta = torch.cat([experts.float(), w], 1).contiguous()
+    out = kernels.moe_gptoss(pool, meta, experts, x, k, H, I, bits, gub, db, G)
+    again = kernels.moe_gptoss(pool, meta, experts, x, k, H, I, bits, gub, db, G)
+    assert torch.equal(out.view(torch.int16), again.view(torch.int16)), "two calls differ"
+    tok = list(range(N)) if N <= 4 else [0, N // 2, N - 1]
+    want = O.gptoss_ref(pool.cpu().numpy(), experts.cpu().numpy()[tok], w.cpu().numpy()[tok], _np(x)[tok], H, I, bits, G,
+                        gub.view(torch.int16).cpu().numpy().view(np.uint16), db.view(torch.int16).cpu().numpy().view(np.uint16))
+    return _rel(_np(out)[tok], want)
+
+
+@pytest.mark.parametrize("bits,G", [(8, 128), (3, 128), (2, 128), (4, 32)])
+def test_column_path_other_formats(bits, G):
+    """Formats outside the row-streaming kernel (other widths, groups below 64) take the column kernel."""
+    assert _layer_case(512, bits, G, N=3, E=8, k=2, seed=bits * 100 + G) < 1e-2
+
+
+@pytest.mark.parametrize("G", [64, 256])
+def test_row_path_ragged_slab_and_groups(G):
+    """H = 640: gate_up has 1280 columns (slabs of 960 and 320) and down 640 (one narrower slab)."""
+    assert _layer_case(640, 4, G, N=2, E=8, k=2, seed=G) < 1e-2
+
+
+def test_row_path_many_passes():
+    """24 tokens on 3 hot experts: each expert's tokens span several 8-token passes."""
+    assert _layer_case(512, 4, 128, N=24, E=16, k=2, seed=7, hot=3) < 1e-2

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ m
   int n2 = 1;
   while (n2 < P) n2 <<= 1;
   pdl_wait();
+  pdl_launch_dependents();  // the next grid may launch now; its own wait covers this whole grid
   for (int i = threadIdx.x; i < n2; i += blockDim.x) {
     unsigned long long kk = ~0ull;
     if (i < P) {
@@ -180,7 +181,6 @@ __global__ void __launch_bounds__(1024) group_kernel(const float* __restrict__ m
     const int cnt = W.grp_count[gid];
     for (int t0 = 0, p = 0; t0 < cnt; t0 += TOK, ++p) W.gp_list[atomicAdd(&bofs[min(NT_MAX, (cnt - t0 + 7) / 8)], 1)] = gid << 8 | p;
   }
-  pdl_launch_dependents();
 }
 
 // ---- grouping by counting sort (pools up to CS_MAX_SLOTS slots) -------------------------------------------
@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(1024) count_group_kernel(const float* __restri
   int* st = cs + nslots;
   const int P = N * k, t = threadIdx.x, nt = blockDim.x;
   pdl_wait();
+  pdl_launch_dependents();  // the next grid may launch now; its own wait covers this whole grid
   for (int64_t i = t; i < nslots; i += nt) cnt[i] = 0;
   if (t == 0) tail = 0;
   if (t <= NT_MAX) bcnt[t] = 0;
@@ -308,7 +309,6 @@ __global__ void __launch_bounds__(1024) count_group_kernel(const float* __restri
     const int c = W.grp_count[gid];
     for (int t0 = 0, pp = 0; t0 < c; t0 += TOK, ++pp) W.gp_list[atomicAdd(&bofs[min(NT_MAX, (c - t0 + 7) / 8)], 1)] = gid << 8 | pp;
   }
-  pdl_launch_dependents();
 }
 
 // ---- dequantized A fragments ------------------------------------------------------------------------

@@ -1,5 +1,7 @@
 // libwisp_b200.so: the C ABI declared in include/wisp_b200.h.  One translation unit (the kernels live
 // in the included .cuh files) so the per-device status word is a single __device__ symbol.
+#include <cudaTypedefs.h>
+
 #include <cstring>
 #include <mutex>
 
@@ -544,9 +546,66 @@ static int gptoss_splits(int P, int64_t I) {
   return int(s < 1 ? 1 : (s > 32 ? 32 : s));
 }
 
+// K splits of the row-streaming GEMVs (gate_up, down): about four (pass, split, slab) units per CTA of
+// the grid (1 per SM), estimating the 8-token passes as min(pairs, 32); every split keeps >= 1 k-step
+static void gptoss_rows_splits(int P, int64_t H, int64_t I, int& ns0, int& ns1) {
+  const int64_t passes = P < 1 ? 1 : (P < 32 ? P : 32), ctas = int64_t(num_sms());
+  auto pick = [&](int64_t ncol, int64_t K) {
+    const int64_t slabs = (ncol + gptoss::rows::SLAB - 1) / gptoss::rows::SLAB, kst = K / 16 > 0 ? K / 16 : 1;
+    const int64_t sp = (4 * ctas + passes * slabs - 1) / (passes * slabs);
+    return int(sp < 1 ? 1 : (sp > kst ? kst : sp));
+  };
+  ns0 = pick(2 * I, H);
+  ns1 = pick(H, I);
+}
+
+// the row-streaming path: 4-bit codes, power-of-two groups >= 64, 64 | H (so every 64-column block of
+// both matrices lies in one group and rows are 16-byte multiples), scale and min arrays 16-byte aligned
+static bool gptoss_rows_ok(int64_t H, int64_t I, int bits, int group) {
+  const int64_t n = H * I;
+  return bits == 4 && group >= 64 && (group & (group - 1)) == 0 && H == I && H % 64 == 0 && (3 * n * bits / 8) % 16 == 0 &&
+         (2 * (3 * n / group)) % 16 == 0;
+}
+
+// splits the workspace is sized for: the larger of the column path's and the row path's
+static int gptoss_ws_splits(int P, int64_t H, int64_t I) {
+  int ns0, ns1;
+  gptoss_rows_splits(P, H, I, ns0, ns1);
+  const int c = gptoss_splits(P, I);
+  const int r = ns0 > ns1 ? ns0 : ns1;
+  return c > r ? c : r;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library does not link libcuda)
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// the 3-D map (row words, rows, slots) of one gpt-oss matrix across the pool, boxes of one slab x 16 rows
+static bool gptoss_tmap(CUtensorMap* m, const uint8_t* pool, int64_t nslots, int64_t nbytes, int64_t mat_off, int64_t ncol, int64_t K) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tmap_encoder();
+  if (!enc) return false;
+  const int64_t rowbytes = ncol / 2;
+  cuuint64_t dims[3] = {cuuint64_t(rowbytes / 4), cuuint64_t(K), cuuint64_t(nslots)};
+  cuuint64_t strides[2] = {cuuint64_t(rowbytes), cuuint64_t(nbytes)};
+  cuuint32_t box[3] = {gptoss::rows::SLAB / 8, gptoss::rows::BOX_ROWS, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(pool + mat_off), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I) {
   if (N < 1 || k < 1 || int64_t(N) * k > batched::MAX_PAIRS || H <= 0 || I <= 0) return -1;
-  return gptoss::ws_bytes(N * k, gptoss_splits(N * k, I), H, I);
+  return gptoss::ws_bytes(N * k, gptoss_ws_splits(N * k, H, I), H, I);
 }
 
 int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, const int32_t* experts, int N, int k,
@@ -565,6 +624,7 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   WISP_REQUIRE(wisp_expert_nbytes(n, bits, group) == nbytes, "wisp_moe_gptoss: nbytes=%lld, expected %lld", (long long)nbytes,
                (long long)wisp_expert_nbytes(n, bits, group));
   WISP_REQUIRE(aligned(pool, 16) && nbytes % 16 == 0 && aligned(x, 16), "wisp_moe_gptoss: pool and x must be 16-byte aligned");
+  WISP_REQUIRE(aligned(out, 8), "wisp_moe_gptoss: out must be 8-byte aligned");
   MoeShape S;
   S.nslots = nslots;
   S.nbytes = nbytes;
@@ -577,28 +637,44 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   S.ncode = 3 * n * bits / 8;
   S.ng = 3 * n / group;
   S.mat_bytes = n * bits / 8;
-  const int P = N * k, ns = gptoss_splits(P, I);
-  WISP_REQUIRE(workspace_bytes >= gptoss::ws_bytes(P, ns, H, I), "wisp_moe_gptoss: workspace too small (%lld needed)",
-               (long long)gptoss::ws_bytes(P, ns, H, I));
+  const int P = N * k, nsw = gptoss_ws_splits(P, H, I);
+  WISP_REQUIRE(workspace_bytes >= gptoss::ws_bytes(P, nsw, H, I), "wisp_moe_gptoss: workspace too small (%lld needed)",
+               (long long)gptoss::ws_bytes(P, nsw, H, I));
   WISP_REQUIRE(aligned(workspace, 256), "wisp_moe_gptoss: workspace must be 256-byte aligned");
-  const gptoss::Ws W = gptoss::ws_carve(workspace, P, ns, H, I);
+  const gptoss::Ws W = gptoss::ws_carve(workspace, P, nsw, H, I);
+  CUtensorMap map0, map1;
+  const bool rows = gptoss_rows_ok(H, I, bits, group) && nslots < (int64_t(1) << 31) &&
+                    gptoss_tmap(&map0, pool, nslots, nbytes, 0, 2 * I, H) &&
+                    gptoss_tmap(&map1, pool, nslots, nbytes, H * I * bits / 4, H, I);
+  int ns0 = gptoss_splits(P, I), ns1 = ns0;
+  if (rows) gptoss_rows_splits(P, H, I, ns0, ns1);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms() * 2;
   cudaError_t e = nslots <= batched::CS_MAX_SLOTS
                       ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W.g)
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
-#define WISP_GPTOSS(B)                                                                                                 \
-  if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 0>, grid, gptoss::THREADS, 0, s, pool, S, P, ns, x, W);     \
-  if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, 256, 0, s, S, P, ns, experts, gate_up_bias, W);        \
-  if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 1>, grid, gptoss::THREADS, 0, s, pool, S, P, ns, x, W);
-  switch (bits) {
-    case 8: WISP_GPTOSS(8) break;
-    case 4: WISP_GPTOSS(4) break;
-    case 3: WISP_GPTOSS(3) break;
-    default: WISP_GPTOSS(2) break;
+#define WISP_GPTOSS(B)                                                                                                      \
+  if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 0>, grid, gptoss::THREADS, 0, s, pool, S, P, ns0, x, W);         \
+  if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W); \
+  if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 1>, grid, gptoss::THREADS, 0, s, pool, S, P, ns1, x, W);
+  if (rows) {
+    const int rgrid = num_sms();  // one CTA per SM (its shared memory)
+    if (e == cudaSuccess)
+      e = launch_pdl(gptoss::rows::rows_kernel<0>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map0, pool, S, P, ns0, x, W);
+    if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W);
+    if (e == cudaSuccess)
+      e = launch_pdl(gptoss::rows::rows_kernel<1>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map1, pool, S, P, ns1, x, W);
+  } else {
+    switch (bits) {
+      case 8: WISP_GPTOSS(8) break;
+      case 4: WISP_GPTOSS(4) break;
+      case 3: WISP_GPTOSS(3) break;
+      default: WISP_GPTOSS(2) break;
+    }
   }
 #undef WISP_GPTOSS
-  if (e == cudaSuccess) e = launch_pdl(gptoss::combine_kernel, grid, 256, 0, s, meta, N, k, S, ns, experts, down_bias, W, out);
+  if (e == cudaSuccess)
+    e = launch_pdl(gptoss::combine_kernel, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_gptoss: %s", cudaGetErrorString(e));
   return check_launch("moe_gptoss");
 }
