@@ -284,12 +284,12 @@ __global__ void __launch_bounds__(RED_THREADS) combine_kernel(const float* __res
 
 // ------------------------------------------------------------------------------------------------
 // Row-streaming GEMV for 4-bit codes with groups of 2^glog >= 64 along the output axis (the
-// gpt-oss configuration).  A stored row of the matrix is contiguous, so a slab of 960 output
-// columns over 16 rows is a 480-byte x 16-row box of a 3-D tensor map (uint32 elements; dimensions
+// gpt-oss configuration).  A stored row of the matrix is contiguous, so a slab of 576 output
+// columns over 16 rows is a 288-byte x 16-row box of a 3-D tensor map (uint32 elements; dimensions
 // row words, rows, expert slots): a producer warp moves four such boxes per stage into shared memory
 // with TMA tensor loads (no multicast), and the scale / min windows of those rows and the tokens'
 // activation rows with 16-byte cp.async, all completing on one mbarrier per stage of a 4-deep ring.
-// Fifteen consumer warps each own a 64-column block of the slab (a block never straddles a
+// Nine consumer warps each own a 64-column block of the slab (a block never straddles a
 // quantization group: 64 divides the group, the row length and the matrix offset), so within one
 // k-step of 16 rows every output column of the block shares the scale s[r] and min m[r] of row r,
 //   y[c] = sum_r (q[r,c] s[r] + m[r]) x[r] = sum_r q[r,c] (s[r] x[r]) + sum_r m[r] x[r].
@@ -301,26 +301,27 @@ __global__ void __launch_bounds__(RED_THREADS) combine_kernel(const float* __res
 // The MMA's output rows (m) are mapped to columns so that every A register of one MMA has the same
 // nibble position: m = g <-> column 8g + {0, 2, 4, 6} (low nibbles) or {1, 3, 5, 7} (high); its
 // reduction index k is mapped to rows so that one load instruction reads rows t, t + 4, t + 8 or
-// t + 12 (t = lane % 4), which with the 480-byte row pitch fall in disjoint banks.  The slab is as
-// wide as the register budget allows (one CTA per SM) because every row piece costs the DRAM a row
-// activation: 288-byte pieces ran at 1.5 TB/s.
+// t + 12 (t = lane % 4), which with the 288-byte row pitch fall in disjoint banks.  Two CTAs per SM
+// (18 consumer warps, 8 stages in flight) measured 50 us per gpt-oss-20b layer at one token against
+// 62 us for one CTA of 15 consumer warps on 960-column slabs, and 52 us for four CTAs of 5.
 // Units (8-token pass, K split, slab) are dealt round-robin, so neighbouring CTAs read the slabs of
 // the same rows at about the same time; the producer decodes a pass (slot, positions, token rows)
 // only when it changes.  Each unit writes its own split partial, summed in a fixed order by the
 // activation / combine kernels.
 // ------------------------------------------------------------------------------------------------
 namespace rows {
-constexpr int CONS = 15;                   // consumer warps, one 64-column block each (15 | 45 and 90 blocks)
+constexpr int CONS = 9;                    // consumer warps, one 64-column block each (9 | 45 and 90 blocks)
 constexpr int THREADS = (CONS + 1) * 32;   // + the producer warp
 constexpr int SLAB = CONS * 64;            // output columns per slab
 constexpr int SR = 64;                     // rows per stage
 constexpr int STAGES = 4;
-constexpr int PITCH = SLAB / 2;            // bytes per staged row (the tensor box is dense): 120 words, rows t..t+3 in disjoint banks
+constexpr int PITCH = SLAB / 2;            // bytes per staged row (the tensor box is dense): 72 words, rows t..t+3 in disjoint banks
 constexpr int BOX_ROWS = 16;               // rows per tensor box (one k-step)
 constexpr int XP = SR + 8;                 // bf16 per staged activation row (36 words: conflict-free across tokens)
 constexpr int CODE_BYTES = SR * PITCH;
-constexpr int WIN = 32;                    // halfs per window: the slab's groups (<= 15) after a 16-byte aligned start (<= 7 before)
-constexpr int SWS = 4 * WIN + 16;          // bytes per row of windows: scales, mins, pad (rows 4 banks apart)
+// halfs per window: a 16-byte aligned start (<= 7 groups before the slab's first) and the slab's groups (groups >= 64)
+constexpr int WIN = 7 + (SLAB - 1) / 64 + 1 <= 16 ? 16 : 32;
+constexpr int SWS = 4 * WIN + 16;          // bytes per row of windows: scales, mins, pad (rows 4 or 20 banks apart)
 constexpr int SCALE_BYTES = SR * SWS;
 constexpr int X_BYTES = 8 * XP * 2;
 constexpr int STAGE_BYTES = CODE_BYTES + SCALE_BYTES + X_BYTES;
@@ -391,7 +392,7 @@ __device__ __forceinline__ Geo geo(const MoeShape& S) {
 }
 
 template <int MAT>
-__global__ void __launch_bounds__(THREADS, 1) rows_kernel(const __grid_constant__ CUtensorMap tmap, const uint8_t* __restrict__ pool,
+__global__ void __launch_bounds__(THREADS, 2) rows_kernel(const __grid_constant__ CUtensorMap tmap, const uint8_t* __restrict__ pool,
                                                           MoeShape S, int P, int nsplit, const uint16_t* __restrict__ x, Ws W) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -466,8 +467,9 @@ __global__ void __launch_bounds__(THREADS, 1) rows_kernel(const __grid_constant_
             tma_load_3d(stg + lane * BOX_ROWS * PITCH, &tmap, int(c0 / 8), row0 + lane * BOX_ROWS, slot, &full[b]);
           // scale and min windows: 16-byte chunk c of array a (0 scales, 1 mins) of row r, the chunks the row's groups reach
           uint8_t* sw = stg + CODE_BYTES;
-          for (int t = lane; t < 8 * nrows; t += 32) {
-            const int r = t >> 3, a = (t >> 2) & 1, c = t & 3;
+          constexpr int NCH = WIN / 8;  // 16-byte chunks per window
+          for (int t = lane; t < 2 * NCH * nrows; t += 32) {
+            const int r = t / (2 * NCH), a = (t / NCH) & 1, c = t % NCH;
             const int64_t e = G.e0 + int64_t(row0 + r) * G.ncol + c0;
             const int64_t g0 = e >> S.glog, gw = g0 & ~int64_t(7), g1 = (e + ncols - 1) >> S.glog;
             if (g1 >= gw + 8 * c) cp16(sw + r * SWS + 2 * WIN * a + 16 * c, sc + int64_t(a) * S.ng + gw + 8 * c);

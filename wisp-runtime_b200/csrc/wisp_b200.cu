@@ -547,9 +547,9 @@ static int gptoss_splits(int P, int64_t I) {
 }
 
 // K splits of the row-streaming GEMVs (gate_up, down): about four (pass, split, slab) units per CTA of
-// the grid (1 per SM), estimating the 8-token passes as min(pairs, 32); every split keeps >= 1 k-step
+// the grid (2 per SM), estimating the 8-token passes as min(pairs, 32); every split keeps >= 1 k-step
 static void gptoss_rows_splits(int P, int64_t H, int64_t I, int& ns0, int& ns1) {
-  const int64_t passes = P < 1 ? 1 : (P < 32 ? P : 32), ctas = int64_t(num_sms());
+  const int64_t passes = P < 1 ? 1 : (P < 32 ? P : 32), ctas = 2 * int64_t(num_sms());
   auto pick = [&](int64_t ncol, int64_t K) {
     const int64_t slabs = (ncol + gptoss::rows::SLAB - 1) / gptoss::rows::SLAB, kst = K / 16 > 0 ? K / 16 : 1;
     const int64_t sp = (4 * ctas + passes * slabs - 1) / (passes * slabs);
@@ -658,7 +658,7 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W); \
   if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 1>, grid, gptoss::THREADS, 0, s, pool, S, P, ns1, x, W);
   if (rows) {
-    const int rgrid = num_sms();  // one CTA per SM (its shared memory)
+    const int rgrid = 2 * num_sms();  // two CTAs per SM (shared memory and registers)
     if (e == cudaSuccess)
       e = launch_pdl(gptoss::rows::rows_kernel<0>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map0, pool, S, P, ns0, x, W);
     if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W);
