@@ -203,53 +203,70 @@ __global__ void __launch_bounds__(RED_THREADS) act_kernel(MoeShape S, int P, int
     const int pos = int(blk / chunks);
     const int64_t col4 = (blk - int64_t(pos) * chunks) * RED_C4 + c4;
     const int pair = W.g.order[pos];
-    if (W.g.posof[pair] < 0) continue;  // block-uniform
+    const int valid = W.g.posof[pair], e = experts[pair];
+    if (valid < 0) continue;  // block-uniform
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (col4 < n4)
+    uint2 bias = make_uint2(0u, 0u);  // (gate, up) bf16 of activations 2 col4 and 2 col4 + 1
+    if (col4 < n4) {
+      if (sg == 0) bias = *reinterpret_cast<const uint2*>(gub + int64_t(e) * 2 * S.I + 4 * col4);
+#pragma unroll 4
       for (int sp = sg; sp < nsplit; sp += RED_SG) acc = f4add(acc, part[((int64_t(sp) * P + pos) * wd) / 4 + col4]);
+    }
     red[sg][c4] = acc;
     __syncthreads();
     if (sg == 0 && col4 < n4) {
       float4 v = red[0][c4];
 #pragma unroll
       for (int g = 1; g < RED_SG; ++g) v = f4add(v, red[g][c4]);
-      const int e = experts[pair];
-      const uint16_t* b = gub + int64_t(e) * 2 * S.I + 4 * col4;  // (gate, up) of activations 2 col4 and 2 col4 + 1
-      const uint32_t lo = swiglu_clamped(v.x, v.y, b[0], b[1]), hi = swiglu_clamped(v.z, v.w, b[2], b[3]);
+      const uint32_t lo = swiglu_clamped(v.x, v.y, uint16_t(bias.x), uint16_t(bias.x >> 16)),
+                     hi = swiglu_clamped(v.z, v.w, uint16_t(bias.y), uint16_t(bias.y >> 16));
       *reinterpret_cast<uint32_t*>(W.act + int64_t(pos) * S.I + 2 * col4) = lo | (hi << 16);
     }
     __syncthreads();
   }
 }
 
-// out[t] = bf16(sum_j w[t,j] * (bf16(sum of splits) + bias_d[e]))
+// out[t] = bf16(sum_j w[t,j] * (bf16(sum of splits) + bias_d[e])); CMB_SG split groups of RED_THREADS / CMB_SG
+// float4 columns (32 groups when there are many splits: one token has few columns to spread over)
+template <int CMB_SG>
 __global__ void __launch_bounds__(RED_THREADS) combine_kernel(const float* __restrict__ meta, int N, int k, MoeShape S,
                                                               int nsplit, const int32_t* __restrict__ experts,
                                                               const uint16_t* __restrict__ db, Ws W,
                                                               uint16_t* __restrict__ out) {
-  __shared__ float4 red[RED_KB][RED_SG][RED_C4];
+  constexpr int CMB_C4 = RED_THREADS / CMB_SG;
+  __shared__ float4 red[RED_KB][CMB_SG][CMB_C4];
   pdl_wait();
   pdl_launch_dependents();
   const int64_t P = int64_t(N) * k;
   const int64_t wd = (2 * int64_t(S.I) > S.H ? 2 * int64_t(S.I) : S.H);
   const int64_t n4 = S.H / 4;
-  const int c4 = threadIdx.x % RED_C4, sg = threadIdx.x / RED_C4;
-  const int64_t chunks = (n4 + RED_C4 - 1) / RED_C4;
+  const int c4 = threadIdx.x % CMB_C4, sg = threadIdx.x / CMB_C4;
+  const int64_t chunks = (n4 + CMB_C4 - 1) / CMB_C4;
   const float4* part = reinterpret_cast<const float4*>(W.part);
   for (int64_t blk = blockIdx.x; blk < int64_t(N) * chunks; blk += gridDim.x) {
     const int t = int(blk / chunks);
-    const int64_t col4 = (blk - int64_t(t) * chunks) * RED_C4 + c4;
+    const int64_t col4 = (blk - int64_t(t) * chunks) * CMB_C4 + c4;
     float o[4] = {0.f, 0.f, 0.f, 0.f};
     for (int j0 = 0; j0 < k; j0 += RED_KB) {
       const int nj = k - j0 < RED_KB ? k - j0 : RED_KB;
       float4 acc[RED_KB];
       int pos[RED_KB];
+      uint2 bias[RED_KB];
+      float w[RED_KB];
+      // everything but the partials first: positions, routing weights and biases of the experts
 #pragma unroll
       for (int jj = 0; jj < RED_KB; ++jj) {
         acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
         pos[jj] = jj < nj && col4 < n4 ? W.g.posof[t * k + j0 + jj] : -1;
+        bias[jj] = make_uint2(0u, 0u);
+        w[jj] = 0.0f;
+        if (sg == 0 && pos[jj] >= 0) {
+          bias[jj] = *reinterpret_cast<const uint2*>(db + int64_t(experts[t * k + j0 + jj]) * S.H + 4 * col4);
+          w[jj] = meta[int64_t(t) * 2 * k + k + j0 + jj];
+        }
       }
-      for (int sp = sg; sp < nsplit; sp += RED_SG) {  // the experts' loads of one split are independent
+#pragma unroll 2
+      for (int sp = sg; sp < nsplit; sp += CMB_SG) {  // the experts' loads of one split are independent
 #pragma unroll
         for (int jj = 0; jj < RED_KB; ++jj)
           if (pos[jj] >= 0) acc[jj] = f4add(acc[jj], part[((int64_t(sp) * P + pos[jj]) * wd) / 4 + col4]);
@@ -258,18 +275,17 @@ __global__ void __launch_bounds__(RED_THREADS) combine_kernel(const float* __res
       for (int jj = 0; jj < RED_KB; ++jj) red[jj][sg][c4] = acc[jj];
       __syncthreads();
       if (sg == 0 && col4 < n4) {
-        for (int jj = 0; jj < nj; ++jj) {
-          const int pair = t * k + j0 + jj;
-          if (W.g.posof[pair] < 0) continue;
+#pragma unroll
+        for (int jj = 0; jj < RED_KB; ++jj) {
+          if (pos[jj] < 0) continue;
           float4 v = red[jj][0][c4];
 #pragma unroll
-          for (int g = 1; g < RED_SG; ++g) v = f4add(v, red[jj][g][c4]);
-          const uint16_t* b = db + int64_t(experts[pair]) * S.H + 4 * col4;
-          const float w = meta[int64_t(t) * 2 * k + k + j0 + jj];
+          for (int g = 1; g < CMB_SG; ++g) v = f4add(v, red[jj][g][c4]);
           const float y[4] = {v.x, v.y, v.z, v.w};
+          const uint16_t b[4] = {uint16_t(bias[jj].x), uint16_t(bias[jj].x >> 16), uint16_t(bias[jj].y), uint16_t(bias[jj].y >> 16)};
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            o[c] = fmaf(w, bf16_to_f32(f32_to_bf16(bf16_to_f32(f32_to_bf16(y[c])) + bf16_to_f32(b[c]))), o[c]);
+            o[c] = fmaf(w[jj], bf16_to_f32(f32_to_bf16(bf16_to_f32(f32_to_bf16(y[c])) + bf16_to_f32(b[c]))), o[c]);
         }
       }
       __syncthreads();

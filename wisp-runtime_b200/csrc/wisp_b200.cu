@@ -624,7 +624,8 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   WISP_REQUIRE(wisp_expert_nbytes(n, bits, group) == nbytes, "wisp_moe_gptoss: nbytes=%lld, expected %lld", (long long)nbytes,
                (long long)wisp_expert_nbytes(n, bits, group));
   WISP_REQUIRE(aligned(pool, 16) && nbytes % 16 == 0 && aligned(x, 16), "wisp_moe_gptoss: pool and x must be 16-byte aligned");
-  WISP_REQUIRE(aligned(out, 8), "wisp_moe_gptoss: out must be 8-byte aligned");
+  WISP_REQUIRE(aligned(out, 8) && aligned(gate_up_bias, 8) && aligned(down_bias, 8),
+               "wisp_moe_gptoss: out and the biases must be 8-byte aligned");
   MoeShape S;
   S.nslots = nslots;
   S.nbytes = nbytes;
@@ -674,7 +675,8 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   }
 #undef WISP_GPTOSS
   if (e == cudaSuccess)
-    e = launch_pdl(gptoss::combine_kernel, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out);
+    e = ns1 > 16 ? launch_pdl(gptoss::combine_kernel<32>, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out)
+                 : launch_pdl(gptoss::combine_kernel<16>, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_gptoss: %s", cudaGetErrorString(e));
   return check_launch("moe_gptoss");
 }
