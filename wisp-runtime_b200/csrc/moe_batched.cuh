@@ -232,6 +232,78 @@ __device__ __forceinline__ void block_scan2(int a, int g, int& ea, int& eg, int&
   __syncthreads();  // wa / wg may be reused
 }
 
+// The same outputs for at most 32 pairs, in one warp: each lane ranks its pair by (slot, index) with
+// shuffles (invalid pairs after the valid ones), the ranked keys go through shared memory, and group
+// starts, indices and sizes come from ballots.  No histogram over the slots and no global read-back,
+// which is what the one-CTA kernels spend their time on for a handful of pairs.
+constexpr int SMALL_PAIRS = 32;
+static_assert(NT_MAX == 1, "the warp grouping lists passes in group order (no token-tile buckets)");
+__global__ void __launch_bounds__(32) small_group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {
+  __shared__ int key_at[SMALL_PAIRS];
+  const int P = N * k, p = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();  // the next grid may launch now; its own wait covers this whole grid
+  int sl = -1;
+  if (p < P) {
+    const int tk = p / k, j = p - tk * k;
+    const float f = meta[int64_t(tk) * 2 * k + j];
+    if (f >= 0.0f && f < float(nslots)) sl = int(f);
+    else if (f != -1.0f) flag(WISP_STATUS_BAD_SLOT);  // -1: an empty pair (padding), skipped silently
+  }
+  // sort key: valid pairs by slot, then invalid ones; ties by pair index; lanes >= P last of all
+  const int key = p >= P ? 0x7FFFFFFF : (sl >= 0 ? sl : 0x7FFFFFFE);
+  int rank = 0;
+  for (int q = 0; q < SMALL_PAIRS; ++q) {
+    const int kq = __shfl_sync(0xffffffffu, key, q);
+    rank += (kq < key || (kq == key && q < p)) ? 1 : 0;
+  }
+  key_at[rank] = key;
+  __syncwarp();
+  if (p < P) {
+    W.order[rank] = p;
+    W.posof[p] = sl >= 0 ? rank : -1;
+  }
+  // lane i now stands for sorted position i
+  const int ki = key_at[p], kprev = p > 0 ? key_at[p - 1] : -1;
+  const bool valid = p < P && ki < 0x7FFFFFFE;
+  const unsigned starts = __ballot_sync(0xffffffffu, valid && ki != kprev);
+  const unsigned validm = __ballot_sync(0xffffffffu, valid);
+  const int ngroups = __popc(starts);
+  if (valid && ki != kprev) {
+    const int gid = __popc(starts & ((1u << p) - 1u));
+    const unsigned later = starts & ~((2u << p) - 1u);  // starts after this one (p <= 31: 2u << 31 wraps to 0)
+    const int end = later ? __ffs(later) - 1 : __popc(validm);  // valid positions are a prefix
+    const int cnt = end - p;
+    W.grp_slot[gid] = ki;
+    W.grp_start[gid] = p;
+    W.grp_count[gid] = cnt;
+  }
+  // (group, pass) list in group order: group g's passes start after all earlier groups' passes
+  const bool st = valid && ki != kprev;
+  int npass = 0;
+  if (st) {
+    const unsigned later = starts & ~((2u << p) - 1u);
+    const int end = later ? __ffs(later) - 1 : __popc(validm);
+    npass = (end - p + TOK - 1) / TOK;
+  }
+  int before = npass;  // inclusive prefix over lanes
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, before, o);
+    if (p >= o) before += v;
+  }
+  const int total = __shfl_sync(0xffffffffu, before, 31);
+  if (st) {
+    const int gid = __popc(starts & ((1u << p) - 1u));
+    for (int pp = 0; pp < npass; ++pp) W.gp_list[before - npass + pp] = gid << 8 | pp;
+  }
+  if (p == 0) {
+    W.n_groups[0] = ngroups;
+    W.n_gp[0] = total;
+    W.next_unit[0] = 0;
+    W.next_unit[1] = 0;
+  }
+}
+
 __global__ void __launch_bounds__(1024) count_group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {
   extern __shared__ int cs[];  // [nslots] counts, then [nslots] group starts
   __shared__ int rank_in[MAX_PAIRS];

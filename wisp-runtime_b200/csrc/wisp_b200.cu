@@ -498,7 +498,8 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   W.xp = batched::ws_xp(workspace, N * k, H, I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms();
-  cudaError_t e = nslots <= batched::CS_MAX_SLOTS
+  cudaError_t e = N * k <= batched::SMALL_PAIRS ? launch_pdl(batched::small_group_kernel, 1, 32, 0, s, meta, N, k, nslots, W)
+                  : nslots <= batched::CS_MAX_SLOTS
                       ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W)
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
@@ -651,7 +652,8 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   if (rows) gptoss_rows_splits(P, H, I, ns0, ns1);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms() * 2;
-  cudaError_t e = nslots <= batched::CS_MAX_SLOTS
+  cudaError_t e = N * k <= batched::SMALL_PAIRS ? launch_pdl(batched::small_group_kernel, 1, 32, 0, s, meta, N, k, nslots, W.g)
+                  : nslots <= batched::CS_MAX_SLOTS
                       ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W.g)
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
 #define WISP_GPTOSS(B)                                                                                                      \
