@@ -121,3 +121,28 @@ def test_invalid_slot_skipped_and_flagged():
     want = O.moe_batched_ref(pool.cpu().numpy(), sel, rw, _np(x), n, H, I, bits, G)
     assert _rel(_np(out), want) < TOL
     _lib.device_status(0, clear=True)
+
+
+@pytest.mark.parametrize("N,k", [(16, 2), (11, 3)])
+def test_grouping_either_side_of_the_warp_path(N, k):
+    """32 pairs are grouped by one warp, 33 by the one-CTA counting sort; both against the oracle, with
+    repeated experts (several tokens per group) and one padded pair."""
+    from wisp import kernels, quant
+
+    H, I, E, G, bits = 256, 128, 6, 128, 4
+    n = H * I
+    gen = torch.Generator(device="cuda").manual_seed(N * k)
+    pool = quant.quantize_batch((torch.randn(E, 3, n, device="cuda", generator=gen) * 0.02).to(torch.bfloat16), bits, G)
+    x = torch.randn(N, H, device="cuda", generator=gen).to(torch.bfloat16)
+    rng = np.random.default_rng(N * k)
+    sel = np.stack([rng.choice(E, k, replace=False) for _ in range(N)]).astype(np.int64)
+    rw = rng.uniform(0.1, 1.0, (N, k)).astype(np.float32)
+    meta_np = np.concatenate([sel.astype(np.float32), rw], 1)
+    meta_np[N - 1, k - 1] = -1.0  # a padded pair: skipped, contributes nothing
+    rw_ref = rw.copy()
+    rw_ref[N - 1, k - 1] = 0.0
+    sel_ref = sel.copy()
+    sel_ref[N - 1, k - 1] = sel[N - 1, 0]
+    out = kernels.moe_batched(pool, torch.from_numpy(meta_np).cuda().contiguous(), x, k, n, H, I, bits, G)
+    want = O.moe_batched_ref(pool.cpu().numpy(), sel_ref, rw_ref, _np(x), n, H, I, bits, G)
+    assert _rel(_np(out), want) < TOL
