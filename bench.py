@@ -41,6 +41,9 @@ EP_BATCH = 64  # moe-ep: tokens per step over all ranks (config 4 batch)
 NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
 # DRAM read + write of the batched gate/up and down grids for one 64-token Zipf(1.1) layer (ncu)
 NCU_TRAFFIC_BATCHED_LAYER = 96_768_256 + 3_038_720 + 48_437_504 + 489_472
+# DRAM bytes of the two gpt-oss GEMVs (gate_up + down) of one 20b layer at one token (4 experts), one ncu capture
+# (profiles/moe_gptoss_rows_q4_20b_layer_full.md)
+NCU_TRAFFIC_GPTOSS_LAYER_BS1 = 35_287_552 + 17_679_872
 
 
 GO_L, GO_H, GO_I, GO_E, GO_K = 24, 2880, 2880, 32, 4  # gpt-oss-20b MoE shape (config 5)
@@ -697,7 +700,8 @@ class GptOssStack:
         bytes_layer = self.distinct * self.nb + 2 * self.N * GO_H * 2
         us = ms_per_step / GO_L * 1e3
         ach = bytes_layer / (us * 1e-6) / 1e9
-        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "traffic": None,
+        traffic = NCU_TRAFFIC_GPTOSS_LAYER_BS1 if self.N == 1 and self.bits == 4 else None
+        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "traffic": traffic,
                 "kernel": "wisp_moe_gptoss (grouping, gate_up GEMV, activation, down GEMV, combine) per layer, timed as "
                 "the step time / layers (RMSNorm included)", "bytes_per_call": bytes_layer, "us_per_call": us,
                 "peak_source": peak_src}
