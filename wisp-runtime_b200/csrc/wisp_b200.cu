@@ -547,13 +547,17 @@ static int gptoss_splits(int P, int64_t I) {
   return int(s < 1 ? 1 : (s > 32 ? 32 : s));
 }
 
-// K splits of the row-streaming GEMVs (gate_up, down): about four (pass, split, slab) units per CTA of
-// the grid (2 per SM), estimating the 8-token passes as min(pairs, 32); every split keeps >= 1 k-step
+// K splits of the row-streaming GEMVs (gate_up, down): two (pass, split, slab) units per CTA of the grid
+// (2 per SM) for fewer than 8 passes, three otherwise, estimating the 8-token passes as min(pairs, 32);
+// every split keeps >= 1 k-step.  More units balance the CTAs better but leave more split partials to
+// sum: per gpt-oss-20b layer 43.0 / 44.5 / 45.4 / 49.7 us at one token for 2 / 3 / 4 / 6 units per CTA,
+// 261 / 251 / 258 / 266 us at 32 tokens.
 static void gptoss_rows_splits(int P, int64_t H, int64_t I, int& ns0, int& ns1) {
   const int64_t passes = P < 1 ? 1 : (P < 32 ? P : 32), ctas = 2 * int64_t(num_sms());
+  const int64_t per = passes < 8 ? 2 : 3;
   auto pick = [&](int64_t ncol, int64_t K) {
     const int64_t slabs = (ncol + gptoss::rows::SLAB - 1) / gptoss::rows::SLAB, kst = K / 16 > 0 ? K / 16 : 1;
-    const int64_t sp = (4 * ctas + passes * slabs - 1) / (passes * slabs);
+    const int64_t sp = (per * ctas + passes * slabs - 1) / (passes * slabs);
     return int(sp < 1 ? 1 : (sp > kst ? kst : sp));
   };
   ns0 = pick(2 * I, H);
