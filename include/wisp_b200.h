@@ -201,7 +201,12 @@ int64_t wisp_moe_gptoss_workspace_bytes(int N, int k, int64_t H, int64_t I);
  * input-major, wisp.quant layout (H == I); meta fp32 [N, 2k] = per token [k slots | k weights],
  * experts int32 [N, k] = the expert ids (bias rows), gate_up_bias bf16 [E, 2I], down_bias bf16 [E, H].
  * out[t] = sum_j w[t,j] * (bf16(a . W_d) + b_d), a = (clamp(up, -7, 7) + 1) * g * sigmoid(1.702 g),
- * g = min(gate, 7), [gate | up] = bf16(x . W_gu) + b_gu (interleaved).  Dequant bit-exact (bf16(q*s+m)).
+ * g = min(gate, 7), [gate | up] = bf16(x . W_gu) + b_gu (interleaved).
+ * 4-bit codes with power-of-two groups >= 64 and 64 | H stream rows through tensor-map TMA boxes into
+ * fp16 tensor-core MMAs: weights enter as q*s + m exactly and s*x, m*x are rounded to fp16 (0.2-0.3%
+ * from the reference's bf16(q*s+m) matmul on its own fixtures); other formats dequantize bit-exactly
+ * (bf16(q*s+m)) in a column kernel.  pool, x: 16-byte aligned; out and both biases: 8-byte aligned.
+ * Results are bitwise repeatable (split sums in a fixed order).
  * Replaces the reference's PagedGptOssBlock expert math (wisp/gptoss.py:107-143: dequant + bmm). */
 int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, const int32_t* experts, int N, int k,
                     const uint16_t* x, int64_t H, int64_t I, int bits, int group, const uint16_t* gate_up_bias,
