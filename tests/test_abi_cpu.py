@@ -57,3 +57,26 @@ def test_invalid_arguments_fail_on_host_without_a_gpu():
     assert b"NULL" in L.wisp_last_error()
     with pytest.raises(_lib.WispError, match="bits must be"):
         _lib.call("wisp_moe_decode", 16, 8, 2506752, 16, 8, 16, 2048, 768, 5, 128, 16, 8 * 768, 16, None)
+
+
+def test_gptoss_alignment_checks_run_on_host():
+    """The gpt-oss entry point rejects an output or bias pointer that is not 8-byte aligned (its
+    reductions store and load 8-byte vectors) before touching the device."""
+    from oracle import wisp_oracle as O
+
+    H = I = 256
+    nb = O.expert_nbytes(H * I, 4, 128)
+    args = dict(pool=4096, nslots=8, nbytes=nb, meta=4096, experts=4096, N=1, k=2, x=4096, H=H, I=I, bits=4, group=128,
+                gub=4096, db=4096, ws=4096, wsb=1 << 30, out=4096, stream=None)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return _lib.call("wisp_moe_gptoss", a["pool"], a["nslots"], a["nbytes"], a["meta"], a["experts"], a["N"], a["k"],
+                         a["x"], a["H"], a["I"], a["bits"], a["group"], a["gub"], a["db"], a["ws"], a["wsb"], a["out"],
+                         a["stream"])
+
+    for bad in (dict(out=4098), dict(gub=4100), dict(db=4102)):
+        with pytest.raises(_lib.WispError, match="8-byte aligned"):
+            call(**bad)
+    with pytest.raises(_lib.WispError, match="16-byte aligned"):
+        call(x=4104)
