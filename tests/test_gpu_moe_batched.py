@@ -146,3 +146,22 @@ def test_grouping_either_side_of_the_warp_path(N, k):
     out = kernels.moe_batched(pool, torch.from_numpy(meta_np).cuda().contiguous(), x, k, n, H, I, bits, G)
     want = O.moe_batched_ref(pool.cpu().numpy(), sel_ref, rw_ref, _np(x), n, H, I, bits, G)
     assert _rel(_np(out), want) < TOL
+
+
+def test_reference_named_batched_entry():
+    """moe_decode_qb (the reference's planned batched name) is the batched kernel, and each of its rows
+    agrees with the bs=1 moe_decode_q4_fast of that token."""
+    from wisp import kernels, quant
+
+    H, I, E, k, G, N = 256, 128, 8, 2, 128, 3
+    n = H * I
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    pool = quant.quantize_batch((torch.randn(E, 3, n, device="cuda", generator=gen) * 0.02).to(torch.bfloat16), 4, G)
+    x = torch.randn(N, H, device="cuda", generator=gen).to(torch.bfloat16)
+    sel = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(t))[:k] for t in range(N)]).float()
+    meta = torch.cat([sel, torch.full((N, k), 0.5)], 1).cuda().contiguous()
+    got = kernels.moe_decode_qb(pool, meta, x, k, n, H, I, block_gu=16)
+    assert torch.equal(got.view(torch.int16), kernels.moe_batched(pool, meta, x, k, n, H, I, 4, G).view(torch.int16))
+    for t in range(N):
+        one = kernels.moe_decode_q4_fast(pool, meta[t].contiguous(), x[t], k, n, H, I)
+        assert _rel(_np(got)[t], _np(one)) < TOL

@@ -413,6 +413,14 @@ def moe_decode_q2_fast(pool, meta, x, k, n, H, I, group=128, block_gu=8, block_d
     return moe_decode_fast(pool, meta, x, k, n, H, I, 2, group)
 
 
+def moe_decode_qb(pool, meta, x, k, n, H, I, bits=4, group=128, out=None, workspace=None, **tuning):
+    """Batched MoE decode of N tokens in the reference's naming (the batched entry it plans beside the
+    bs=1 ``moe_decode_q*_fast``): meta fp32 [N, 2k] = per token [slots | weights], x bf16 [N, H] ->
+    bf16 [N, H].  The reference's own batched path is dequant + bmm / per-expert MLPs
+    (wisp/moe.py:122-137); tuning keyword arguments are accepted and ignored, like the bs=1 names'."""
+    return moe_batched(pool, meta, x, k, n, H, I, bits, group, out=out, workspace=workspace)
+
+
 def moe_decode_q4(pool, slots, x, w, n, H, I, group=128, block_r=32, num_warps=4):
     """pool uint8 [nslots, nbytes] (4-bit experts); slots int64 [k]; x [H] bf16; w [k] routing weights.
     Returns [H] in x.dtype.  Reference: wisp/kernels.py:115-137."""
