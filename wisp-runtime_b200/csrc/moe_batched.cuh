@@ -238,11 +238,11 @@ __device__ __forceinline__ void block_scan2(int a, int g, int& ea, int& eg, int&
 // which is what the one-CTA kernels spend their time on for a handful of pairs.
 constexpr int SMALL_PAIRS = 32;
 static_assert(NT_MAX == 1, "the warp grouping lists passes in group order (no token-tile buckets)");
-__global__ void __launch_bounds__(32) small_group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {
-  __shared__ int key_at[SMALL_PAIRS];
-  const int P = N * k, p = threadIdx.x;
-  pdl_wait();
-  pdl_launch_dependents();  // the next grid may launch now; its own wait covers this whole grid
+// one warp (lane = threadIdx.x % 32) writes the grouping of P = N * k <= 32 pairs into W; key_at is 32 ints of
+// the warp's shared memory; W's arrays may be shared or global memory (next_unit is skipped when null)
+__device__ __forceinline__ void warp_group(const float* __restrict__ meta, int N, int k, int64_t nslots, const Ws& W,
+                                           int* key_at) {
+  const int P = N * k, p = threadIdx.x & 31;
   int sl = -1;
   if (p < P) {
     const int tk = p / k, j = p - tk * k;
@@ -299,9 +299,19 @@ __global__ void __launch_bounds__(32) small_group_kernel(const float* __restrict
   if (p == 0) {
     W.n_groups[0] = ngroups;
     W.n_gp[0] = total;
-    W.next_unit[0] = 0;
-    W.next_unit[1] = 0;
+    if (W.next_unit) {
+      W.next_unit[0] = 0;
+      W.next_unit[1] = 0;
+    }
   }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(32) small_group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {
+  __shared__ int key_at[SMALL_PAIRS];
+  pdl_wait();
+  pdl_launch_dependents();  // the next grid may launch now; its own wait covers this whole grid
+  warp_group(meta, N, k, nslots, W, key_at);
 }
 
 __global__ void __launch_bounds__(1024) count_group_kernel(const float* __restrict__ meta, int N, int k, int64_t nslots, Ws W) {

@@ -320,6 +320,9 @@ __global__ void __launch_bounds__(RED_THREADS) combine_kernel(const float* __res
 // t + 12 (t = lane % 4), which with the 288-byte row pitch fall in disjoint banks.  Two CTAs per SM
 // (18 consumer warps, 8 stages in flight) measured 50 us per gpt-oss-20b layer at one token against
 // 62 us for one CTA of 15 consumer warps on 960-column slabs, and 52 us for four CTAs of 5.
+// With `fuse_group` (at most 32 pairs) the gate_up grid groups the pairs itself: every CTA's producer
+// warp ranks them into shared memory and CTA 0 also writes the grouping to the workspace for the
+// activation, down and combine grids, so no grouping grid runs before it.
 // Units (8-token pass, K split, slab) are dealt round-robin, so neighbouring CTAs read the slabs of
 // the same rows at about the same time; the producer decodes a pass (slot, positions, token rows)
 // only when it changes.  Each unit writes its own split partial, summed in a fixed order by the
@@ -342,7 +345,8 @@ constexpr int SCALE_BYTES = SR * SWS;
 constexpr int X_BYTES = 8 * XP * 2;
 constexpr int STAGE_BYTES = CODE_BYTES + SCALE_BYTES + X_BYTES;
 constexpr int META = 12;                   // ints of stage metadata
-constexpr int SMEM = STAGES * STAGE_BYTES + STAGES * 2 * 8 + STAGES * META * 4;
+constexpr int GRP_INTS = 256;              // in-kernel grouping (<= 32 pairs): 7 arrays of 32, n_groups, n_gp
+constexpr int SMEM = STAGES * STAGE_BYTES + STAGES * 2 * 8 + STAGES * META * 4 + GRP_INTS * 4;
 static_assert(batched::TOK == 8, "a unit is one 8-token pass of the grouping");
 static_assert(STAGE_BYTES % 128 == 0 && (BOX_ROWS * PITCH) % 128 == 0, "128-byte aligned tensor boxes");
 static_assert(SLAB / 8 <= 256, "a tensor box is at most 256 elements wide");
@@ -409,11 +413,13 @@ __device__ __forceinline__ Geo geo(const MoeShape& S) {
 
 template <int MAT>
 __global__ void __launch_bounds__(THREADS, 2) rows_kernel(const __grid_constant__ CUtensorMap tmap, const uint8_t* __restrict__ pool,
-                                                          MoeShape S, int P, int nsplit, const uint16_t* __restrict__ x, Ws W) {
+                                                          MoeShape S, int P, int nsplit, const uint16_t* __restrict__ x, Ws W,
+                                                          const float* __restrict__ meta_in, int N, int fuse_group) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   int* meta = reinterpret_cast<int*>(empty + STAGES);
+  int* grp = meta + STAGES * META;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int b = 0; b < STAGES; ++b) {
@@ -429,7 +435,41 @@ __global__ void __launch_bounds__(THREADS, 2) rows_kernel(const __grid_constant_
   const int64_t wd = (2 * int64_t(S.I) > S.H ? 2 * int64_t(S.I) : S.H);
 
   if (warp == CONS) {  // ---------------- producer ----------------
-    const int64_t total = int64_t(W.g.n_gp[0]) * G.nslab * nsplit;
+    batched::Ws g = W.g;  // where this warp reads the grouping
+    if (fuse_group) {
+      batched::Ws sg = W.g;
+      sg.order = grp + 32;
+      sg.posof = grp + 64;
+      sg.grp_slot = grp + 96;
+      sg.grp_start = grp + 128;
+      sg.grp_count = grp + 160;
+      sg.gp_list = grp + 192;
+      sg.n_groups = grp + 224;
+      sg.n_gp = grp + 225;
+      sg.next_unit = nullptr;
+      batched::warp_group(meta_in, N, S.k, S.nslots, sg, grp);
+      if (blockIdx.x == 0) {  // publish for the later grids (they wait for this grid's completion)
+        const int ng = sg.n_groups[0], ngp = sg.n_gp[0];
+        if (lane < P) {
+          W.g.order[lane] = sg.order[lane];
+          W.g.posof[lane] = sg.posof[lane];
+        }
+        if (lane < ng) {
+          W.g.grp_slot[lane] = sg.grp_slot[lane];
+          W.g.grp_start[lane] = sg.grp_start[lane];
+          W.g.grp_count[lane] = sg.grp_count[lane];
+        }
+        if (lane < ngp) W.g.gp_list[lane] = sg.gp_list[lane];
+        if (lane == 0) {
+          W.g.n_groups[0] = ng;
+          W.g.n_gp[0] = ngp;
+          W.g.next_unit[0] = 0;
+          W.g.next_unit[1] = 0;
+        }
+      }
+      g = sg;
+    }
+    const int64_t total = int64_t(g.n_gp[0]) * G.nslab * nsplit;
     int stage = 0, cur = -1, slot = 0, pos0 = 0, nt = 0;
     const uint16_t* xr = x;  // lane t < nt: the activation row of token t of the pass
     for (int64_t u = blockIdx.x;; u += gridDim.x) {
@@ -441,13 +481,13 @@ __global__ void __launch_bounds__(THREADS, 2) rows_kernel(const __grid_constant_
         sp = int(rest % nsplit);
         const int gpi = int(rest / nsplit);
         if (gpi != cur) {
-          const int gp = W.g.gp_list[gpi];
-          const int grp = gp >> 8, t0 = (gp & 255) * 8, cnt = W.g.grp_count[grp];
-          slot = W.g.grp_slot[grp];
-          pos0 = W.g.grp_start[grp] + t0;
+          const int gp = g.gp_list[gpi];
+          const int gr = gp >> 8, t0 = (gp & 255) * 8, cnt = g.grp_count[gr];
+          slot = g.grp_slot[gr];
+          pos0 = g.grp_start[gr] + t0;
           nt = cnt - t0 < 8 ? cnt - t0 : 8;
           if (lane < nt)
-            xr = MAT == 0 ? x + int64_t(W.g.order[pos0 + lane] / S.k) * S.H : W.act + int64_t(pos0 + lane) * S.I;
+            xr = MAT == 0 ? x + int64_t(g.order[pos0 + lane] / S.k) * S.H : W.act + int64_t(pos0 + lane) * S.I;
           cur = gpi;
         }
         ks0 = int(int64_t(G.kst) * sp / nsplit);

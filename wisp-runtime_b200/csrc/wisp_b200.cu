@@ -656,7 +656,10 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   if (rows) gptoss_rows_splits(P, H, I, ns0, ns1);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = num_sms() * 2;
-  cudaError_t e = N * k <= batched::SMALL_PAIRS ? launch_pdl(batched::small_group_kernel, 1, 32, 0, s, meta, N, k, nslots, W.g)
+  // the row path groups up to 32 pairs inside its gate_up grid
+  const int fuse_group = rows && N * k <= batched::SMALL_PAIRS ? 1 : 0;
+  cudaError_t e = fuse_group ? cudaSuccess
+                  : N * k <= batched::SMALL_PAIRS ? launch_pdl(batched::small_group_kernel, 1, 32, 0, s, meta, N, k, nslots, W.g)
                   : nslots <= batched::CS_MAX_SLOTS
                       ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W.g)
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
@@ -667,10 +670,12 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   if (rows) {
     const int rgrid = 2 * num_sms();  // two CTAs per SM (shared memory and registers)
     if (e == cudaSuccess)
-      e = launch_pdl(gptoss::rows::rows_kernel<0>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map0, pool, S, P, ns0, x, W);
+      e = launch_pdl(gptoss::rows::rows_kernel<0>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map0, pool, S, P, ns0, x, W,
+                     meta, N, fuse_group);
     if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W);
     if (e == cudaSuccess)
-      e = launch_pdl(gptoss::rows::rows_kernel<1>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map1, pool, S, P, ns1, x, W);
+      e = launch_pdl(gptoss::rows::rows_kernel<1>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map1, pool, S, P, ns1, x, W,
+                     meta, N, 0);
   } else {
     switch (bits) {
       case 8: WISP_GPTOSS(8) break;
