@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wisp|reference] [--bits 4]
                     [--workload decoder|moe-stack] [--layers 48]
 
-Workload ``decoder`` (default; BASELINE config 3 with every expert resident): greedy bs=1 decode of a
+Workload ``decoder`` (default; the Qwen3-30B-A3B bs=1 decode benchmark, expert cache capped at
+``--cache-frac`` 0.4 of the experts with device-side paging): greedy bs=1 decode of a
 Qwen3-30B-A3B-shaped random-init model (48 layers, hidden 2048, 32 query / 4 KV heads x 128, rotary
 base 1e6, RMSNorm eps 1e-6, vocab 151936, 128 experts top-8, intermediate 768, 4-bit g128 experts,
 bf16 attention and embeddings).  A 512-token seeded prompt is run first; one step = one generated

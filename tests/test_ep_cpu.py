@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch/combine (the exchange steps of BASELINE config 4) on CPU: world_size-2 gloo
+"""Expert-parallel dispatch/combine (the exchange steps of 64-token expert-parallel decode) on CPU: world_size-2 gloo
 ranks, each with its own tokens and half of the experts, against the same MoE computed on one process.
 The expert compute is a dense fp32 stand-in; the GPU path swaps in the batched MoE kernel."""
 

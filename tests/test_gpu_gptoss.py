@@ -1,4 +1,4 @@
-"""GPU parity of the gpt-oss expert kernels through the C ABI: against the reference
+"""GPU parity of the gpt-oss expert kernels (gpt-oss-20b shape) through the C ABI: against the reference
 PagedGptOssBlock outputs (fixture gptoss.npz: its decode branch N=1 and grouped branch N=5) and the
 oracle at the gpt-oss-20b layer shape (H = I = 2880, 32 experts, top-4) for N = 1 and 32."""
 

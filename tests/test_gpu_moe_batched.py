@@ -1,5 +1,5 @@
-"""GPU parity of the batched MoE (N tokens, each its own top-k; BASELINE config 2 at N = 1, 4, 16 and
-the bs=64 shape of config 4) through the C ABI: against the reference PagedMoEBlock outputs
+"""GPU parity of the batched MoE (N tokens, each its own top-k; N = 1, 4, 16 and the 64-token
+expert-parallel shape) through the C ABI: against the reference PagedMoEBlock outputs
 (fixture moe_block.npz, both of its branches), the oracle's fp32 batched reference at the Qwen3 layer
 shape, and the bs=1 kernels."""
 

@@ -1,4 +1,4 @@
-// Expert-parallel pack / unpack around the all-to-all exchanges of batched decode.
+// Expert-parallel pack / unpack around the all-to-all exchanges of batched decode (64 tokens per step over all ranks).
 // The experts of a layer are split contiguously over `world` ranks (E_local each); a (token, choice)
 // pair goes to rank sel / E_local.  Buffers have a fixed capacity C per destination, so every shape is
 // static and the exchange can live in a CUDA graph.

@@ -1,4 +1,4 @@
-// Batched MoE decode: N tokens, each with its own top-k experts (BASELINE configs 2 and 4; the
+// Batched MoE decode: N tokens, each with its own top-k experts (N = 1 to 64 per step; the
 // reference's bs > 1 branch, wisp/moe.py:62-137: unique experts, dequant, per-expert MLP, weighted
 // index_add).  The (token, choice) pairs are grouped by slot on the device, so every routed expert's
 // weights are read once per call however many tokens chose it, and the per-expert products run on the

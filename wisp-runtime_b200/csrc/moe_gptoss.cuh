@@ -1,4 +1,5 @@
-// gpt-oss experts (the reference's PagedGptOssBlock, wisp/gptoss.py:107-143).
+// gpt-oss experts (gpt-oss-20b: H = I = 2880, 32 experts, top-4; the reference's PagedGptOssBlock,
+// wisp/gptoss.py:107-143).
 //
 // An expert is gate_up [H, 2I] (gate and up interleaved along the output axis) and down [I, H], both
 // stored input-major, plus biases, packed as the flat [gate_up | down] code stream of the wisp.quant

@@ -1,4 +1,4 @@
-"""Expert parallelism for batched decode: the experts of every layer are split
+"""Expert parallelism for batched decode (64 tokens per step over all ranks): the experts of every layer are split
 contiguously over the ranks of a process group (E / P each); every rank keeps its own tokens
 (data-parallel attention), and per MoE layer
 
