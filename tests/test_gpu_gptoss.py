@@ -87,7 +87,7 @@ def test_gptoss_20b_layer_vs_oracle(N):
     assert _rel(_np(out)[tok], want) < 1e-2
 
 
-def _layer_case(H, bits, G, N, E, k, seed, hot=None):
+def _layer_case(H, bits, G, N, E, k, seed, hot=None, top=False):
     """One gpt-oss layer of shape H = I through the library and the oracle on a sample of tokens, and the
     same call twice (bitwise equal). `hot` routes every token to experts drawn from the first `hot`
     ids, so each expert's tokens span several 8-token passes."""
@@ -99,6 +99,8 @@ def _layer_case(H, bits, G, N, E, k, seed, hot=None):
     logits = torch.randn(N, E, device="cuda", generator=gen)
     if hot is not None:
         logits[:, hot:] -= 100.0
+    if top:  # only the last k + 2 experts of the pool can win
+        logits[:, : E - k - 2] -= 100.0
     experts, w = _route(logits.to(torch.bfloat16), k)
     used = torch.unique(experts.long()).tolist()
     nb = quant.expert_nbytes(n, bits, G)
@@ -134,3 +136,8 @@ def test_row_path_ragged_slab_and_groups(G):
 def test_row_path_many_passes():
     """24 tokens on 3 hot experts: each expert's tokens span several 8-token passes."""
     assert _layer_case(512, 4, 128, N=24, E=16, k=2, seed=7, hot=3) < 1e-2
+
+
+def test_row_path_last_slots_of_a_larger_pool():
+    """Experts in the last slots of a 64-slot pool: the tensor maps' slot coordinate at its far end."""
+    assert _layer_case(512, 4, 128, N=3, E=64, k=2, seed=5, top=True) < 1e-2
