@@ -222,8 +222,13 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
  *   - Nothing in the array needs to start at zero: each call writes all k*I values before reading them.
  *   - The array is one per device and shared by every call on that device: two calls that can run at
  *     the same time (different streams, or threads without ordering) race on it.  Order them.
- *   - The array's address is looked up once per device (cudaGetSymbolAddress, with that device
- *     current); make the first call on each device outside stream capture.
+ *   - The array's device address belongs to a CUDA context.  The first call made in a context looks
+ *     it up (cudaGetSymbolAddress, with that context current) and remembers it under the context's
+ *     unique id (cuCtxGetId); later calls in the same context reuse it.  A context rebuilt by
+ *     cudaDeviceReset, or a second context on the same device, has its own array and gets its own
+ *     lookup on its first call.  Make the first call in each context outside stream capture.
+ *   - The array's name in host code is only a host-side stand-in for the symbol, not a device
+ *     address; the library passes the looked-up address to its kernels.
  * No counterpart in the reference (its kernels allocate their intermediate with torch.empty). */
 #define WISP_MOE_NOALLOC_MAX_SCRATCH 65536
 int wisp_moe_decode_noalloc(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,

@@ -1,11 +1,13 @@
 // libwisp_b200.so: the C ABI declared in include/wisp_b200.h.  One translation unit (the kernels live
 // in the included .cuh files) so the per-device status word is a single __device__ symbol.
+#include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <cstring>
 #include <mutex>
 
 #include "common.cuh"
+#include "ctx_cache.h"
 #include "decode_ops.cuh"
 #include "decoder.cuh"
 #include "dense.cuh"
@@ -307,27 +309,66 @@ static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, 
 }
 
 // ---- built-in scratch of wisp_moe_decode_noalloc -------------------------------------------------
-// One array per device (a __device__ variable exists once in every context that loads the module).
+// One instance per CUDA context that loads this module.  Its device address is looked up with
+// cudaGetSymbolAddress and remembered per context, keyed on the context's unique id (cuCtxGetId), so
+// a context rebuilt by cudaDeviceReset or a second context on the same device gets its own lookup.
 static __device__ __align__(256) float g_noalloc_scratch[WISP_MOE_NOALLOC_MAX_SCRATCH];
-constexpr int kMaxDevices = 64;
 static std::mutex g_noalloc_mu;
-static float* g_noalloc_ptr[kMaxDevices] = {};
+static wisp::ContextAddressTable<64> g_noalloc_addr;
 
-// address of the current device's array, looked up once per device with that device current
+struct CtxApi {
+  PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  PFN_cuCtxGetId_v12000 get_id = nullptr;
+};
+
+static const CtxApi& ctx_api() {
+  static CtxApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      api.get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      api.get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  return api;
+}
+
+// unique id of the calling thread's current context; 0 when there is none yet
+static int current_ctx_id(uint64_t* id) {
+  const CtxApi& api = ctx_api();
+  if (!api.get_current || !api.get_id) return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cuCtxGetCurrent / cuCtxGetId unavailable");
+  CUcontext ctx = nullptr;
+  if (api.get_current(&ctx) != CUDA_SUCCESS) return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cuCtxGetCurrent failed");
+  *id = 0;
+  if (!ctx) return WISP_OK;
+  unsigned long long v = 0;
+  if (api.get_id(ctx, &v) != CUDA_SUCCESS) return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cuCtxGetId failed");
+  *id = uint64_t(v);
+  return WISP_OK;
+}
+
+// the current context's array, looked up on the first call made in that context
 static int noalloc_scratch(float** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_noalloc: device %d >= %d", dev, kMaxDevices);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
+  uint64_t id = 0;
+  int rc = current_ctx_id(&id);
+  if (rc) return rc;
+  void* p = id ? g_noalloc_addr.find(id) : nullptr;
+  if (!p) {
+    // also makes the runtime bind the device's primary context when no context is current yet
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return fail(WISP_ERR_CUDA, "wisp_moe_decode_noalloc: cudaGetSymbolAddress on device %d: %s", dev, cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+    if (!id && (rc = current_ctx_id(&id))) return rc;
+    if (id) g_noalloc_addr.put(id, p);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = static_cast<float*>(p);
   return WISP_OK;
 }
 
