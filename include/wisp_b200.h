@@ -265,6 +265,15 @@ int wisp_qk_norm_rope_kv(const uint16_t* qkv, int Hq, int Hk, int D, const uint1
                          const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos, int64_t tmax, uint16_t* q_out,
                          uint16_t* k_cache, uint16_t* v_cache, void* stream);
 
+/* wisp_qk_norm_rope_kv for T consecutive tokens (a prefill chunk): token t's [q | k | v] heads at
+ * qkv + t*qkv_stride go to position *pos0 + t -- q to q_out [T, Hq, D], k and v into the caches.
+ * Positions outside [0, tmax) write nothing and set WISP_STATUS_BAD_POS.  1 <= T <= 65535.
+ * Replaces the per-chunk q_norm / k_norm, apply_rotary_pos_emb and cache copies of the reference's
+ * chunked prefill (wisp/graphdec.py:122-130). */
+int wisp_qk_norm_rope_kv_rows(const uint16_t* qkv, int T, int64_t qkv_stride, int Hq, int Hk, int D, const uint16_t* qn_w,
+                              const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos0,
+                              int64_t tmax, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream);
+
 /* fp32 elements of the workspace wisp_gqa_decode_attn needs (host-only; -1 for a bad shape). */
 int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax);
 

@@ -19,13 +19,20 @@ Every fixture is produced by the reference's own public functions:
                   per-expert branch N>4, wisp/moe.py:62-137), 4/3/2-bit
   gptoss.npz      wisp.gptoss.PagedGptOssBlock.forward on a CPU stand-in cache (wisp/gptoss.py:111-143)
   attn.npz        the graph decoder's masked GQA SDPA (wisp/graphdec.py:169-175)
+  cache_trace.npz decisions of wisp.cache_core.CacheCore (wisp/cache_core.py:15-149) on seeded
+                  operation sequences: ensure / split / admit / acquire / resized under lru, wsa and
+                  static, with the resulting slots, page-ins, residency and statistics
+
+    python tests/golden/make_golden.py [generator ...]   (default: all; e.g. `cache_trace`)
 """
 
 import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"
-REF = os.environ.get("WISP_REFERENCE", "/root/reference")
+REF = os.environ.get("WISP_REFERENCE")
+if not REF:
+    sys.exit("set WISP_REFERENCE to the reference source tree (the directory holding its wisp/ package)")
 sys.path.insert(0, REF)
 
 import numpy as np  # noqa: E402
@@ -285,13 +292,77 @@ def gen_attn():
     )
 
 
+def gen_cache_trace():
+    """Seeded operation sequences run through the reference CacheCore; every result is recorded so a
+    reimplementation can be replayed against them.  Keys are layer * E + expert with Zipf-biased
+    experts (a few hot ones), k distinct experts per call."""
+    import json
+
+    from wisp.cache_core import CacheCore
+
+    L, E, k = 4, 32, 4
+    cases = [
+        dict(name="lru", nslots=24, policy="lru", decay=0.9995, n_static=0, admit_after=2.0, steps=500, seed=11),
+        dict(name="wsa", nslots=24, policy="wsa", decay=0.97, n_static=0, admit_after=2.0, steps=500, seed=12),
+        # decay 0.5: the growing increment passes 1e100 after ~333 steps, so the renormalisation runs
+        dict(name="wsa_renorm", nslots=20, policy="wsa", decay=0.5, n_static=0, admit_after=1.5, steps=800, seed=13),
+        dict(name="static", nslots=24, policy="static", decay=0.99, n_static=8, admit_after=2.0, steps=400, seed=14),
+        dict(name="lru_tight", nslots=9, policy="lru", decay=0.9995, n_static=0, admit_after=2.0, steps=400, seed=15),
+    ]
+    out = []
+    for c in cases:
+        rng = np.random.default_rng(c["seed"])
+        pop = 1.0 / np.arange(1, E + 1) ** 1.1
+        pop /= pop.sum()
+        perm = [rng.permutation(E) for _ in range(L)]
+        core = CacheCore(c["nslots"], c["policy"], c["decay"], c["n_static"], c["admit_after"])
+        ops = []
+        if c["n_static"]:
+            keys = [int(l * E + perm[l][0]) for l in range(L)] + [int(l * E + perm[l][1]) for l in range(L)]
+            keys = keys[: c["n_static"]]
+            ops.append(dict(op="preload", keys=keys, res=[list(p) for p in core.preload(keys)]))
+        for t in range(c["steps"]):
+            l = t % L
+            ex = rng.choice(E, k, replace=False, p=pop)
+            keys = [int(l * E + perm[l][e]) for e in ex]
+            r = rng.random()
+            try:
+                if r < 0.6:
+                    slots, loads = core.ensure(keys)
+                    ops.append(dict(op="ensure", keys=keys, res=[[int(s) for s in slots], [list(map(int, p)) for p in loads]]))
+                elif r < 0.8:
+                    hk, hs, mk = core.split(keys)
+                    ops.append(dict(op="split", keys=keys, res=[list(map(int, hk)), list(map(int, hs)), list(map(int, mk))]))
+                elif r < 0.9:
+                    prot = sorted({int(s) for s in rng.choice(core.nslots, 3, replace=False)})
+                    s = core.admit(keys[0], set(prot))
+                    ops.append(dict(op="admit", keys=keys[:1], prot=prot, res=-1 if s is None else int(s)))
+                elif r < 0.985 or c["n_static"]:
+                    prot = sorted({int(s) for s in rng.choice(core.nslots, 2, replace=False)})
+                    if core.lookup(keys[0]) is None:
+                        s = core.acquire(keys[0], set(prot))
+                        ops.append(dict(op="acquire", keys=keys[:1], prot=prot, res=int(s)))
+                    else:
+                        ops.append(dict(op="lookup", keys=keys[:1], res=int(core.lookup(keys[0]))))
+                else:
+                    n2 = int(rng.integers(max(k, c["nslots"] // 2), c["nslots"] + 8))
+                    core, loads = core.resized(n2)
+                    ops.append(dict(op="resized", n=n2, res=[list(map(int, p)) for p in loads]))
+            except RuntimeError as e:
+                ops.append(dict(op="error", keys=keys, msg=str(e)))
+                break
+            ops[-1]["resident"] = sorted([int(a), int(b)] for a, b in core.key2slot.items())
+            ops[-1]["stats"] = dict(core.stats)
+        out.append(dict(case=c, ops=ops))
+    np.savez_compressed(os.path.join(OUT, "cache_trace.npz"), trace=np.array(json.dumps(out)))
+
+
+GENERATORS = dict(quant=gen_quant, kernels=gen_kernels, rope_norm=gen_rope_norm, moe_block=gen_moe_block,
+                  gptoss=gen_gptoss, attn=gen_attn, cache_trace=gen_cache_trace)
+
 if __name__ == "__main__":
-    gen_quant()
-    gen_kernels()
-    gen_rope_norm()
-    gen_moe_block()
-    gen_gptoss()
-    gen_attn()
+    for name in sys.argv[1:] or list(GENERATORS):
+        GENERATORS[name]()
     for f in sorted(os.listdir(OUT)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(OUT, f)))

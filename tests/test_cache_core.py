@@ -128,3 +128,58 @@ def test_plan_token_hot_admission():
     assert loads == []  # seen once
     _, loads = plan_token(core, [[1]], 8, set(), admit="hot")
     assert loads == [(1, 0)]  # seen twice: admitted
+
+
+def _replay(case, ops):
+    core = CacheCore(case["nslots"], case["policy"], case["decay"], case["n_static"], case["admit_after"])
+    for i, op in enumerate(ops):
+        kind, where = op["op"], f"{case['name']} op {i} ({op['op']})"
+        if kind == "preload":
+            assert [list(p) for p in core.preload(op["keys"])] == op["res"], where
+        elif kind == "ensure":
+            slots, loads = core.ensure(op["keys"])
+            assert [slots, [list(p) for p in loads]] == op["res"], where
+        elif kind == "split":
+            assert [list(r) for r in core.split(op["keys"])] == op["res"], where
+        elif kind == "admit":
+            s = core.admit(op["keys"][0], set(op["prot"]))
+            assert (-1 if s is None else s) == op["res"], where
+        elif kind == "acquire":
+            assert core.lookup(op["keys"][0]) is None, where
+            assert core.acquire(op["keys"][0], set(op["prot"])) == op["res"], where
+        elif kind == "lookup":
+            assert core.lookup(op["keys"][0]) == op["res"], where
+        elif kind == "resized":
+            core, loads = core.resized(op["n"])
+            assert [list(p) for p in loads] == op["res"], where
+        elif kind == "error":
+            with pytest.raises(RuntimeError):
+                core.ensure(op["keys"])
+            return core
+        if "resident" in op:  # recorded after every operation but the initial preload
+            assert sorted([k, s] for k, s in core.key2slot.items()) == op["resident"], where
+            assert core.stats == op["stats"], where
+    return core
+
+
+def test_decisions_equal_reference_traces(golden):
+    """Seeded operation sequences recorded from the reference CacheCore (tests/golden/make_golden.py,
+    gen_cache_trace): lru, wsa, wsa with the frequency renormalisation crossed (decay 0.5), static with
+    a pinned region, and a tight lru pool; ensure / split / admit / acquire / resized.  Every returned
+    slot and page-in, the residency after each operation and the statistics must be equal."""
+    import json
+
+    trace = json.loads(str(golden("cache_trace")["trace"]))
+    assert {t["case"]["name"] for t in trace} == {"lru", "wsa", "wsa_renorm", "static", "lru_tight"}
+    for t in trace:
+        core = _replay(t["case"], t["ops"])
+        if t["case"]["name"] == "wsa_renorm":
+            assert core.tick > 400  # 2**tick passed 1e100: the renormalisation ran
+
+
+def test_table_is_the_device_layout():
+    c = CacheCore(3)
+    c.ensure([5, 9])
+    t = c.table(12)
+    assert t.dtype == np.int32 and t.shape == (12,)
+    assert t[5] == 0 and t[9] == 1 and (np.delete(t, [5, 9]) == -1).all()

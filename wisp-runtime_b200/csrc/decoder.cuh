@@ -22,23 +22,27 @@ constexpr int MAX_D = 128;      // head_dim limit of the attention kernels
 constexpr int MAX_G = 8;        // query heads per KV head (attention)
 
 // ---- per-head RMSNorm + rotary + cache write -----------------------------------------------------
-// qkv: [Hq*D | Hk*D | Hk*D] bf16 (q heads, k heads, v heads).  One warp per head.
+// qkv: per token [Hq*D | Hk*D | Hk*D] bf16 (q heads, k heads, v heads), token t at qkv + t*qkv_stride.
+// One warp per head; grid y = token: token t sits at position *pos_ptr + t, its q goes to
+// q_out + t*Hq*D.  (One token per decode step; a chunk of prompt tokens in the prefill.)
 __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq, int Hk, int D,
                                        const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w, float eps,
                                        const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t,
                                        const int64_t* __restrict__ pos_ptr, int64_t tmax, uint16_t* __restrict__ q_out,
-                                       uint16_t* __restrict__ kc, uint16_t* __restrict__ vc) {
+                                       uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int64_t qkv_stride) {
   __shared__ float xs[8][QK_MAX_D];
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.x * (blockDim.x >> 5) + wib;
   pdl_wait();
   pdl_launch_dependents();
   if (head >= Hq + 2 * Hk) return;
-  const int64_t pos = *pos_ptr;
+  const int64_t pos = *pos_ptr + blockIdx.y;
   if (pos < 0 || pos >= tmax) {
     if (lane == 0 && head == 0) flag(WISP_STATUS_BAD_POS);
     return;
   }
+  qkv += int64_t(blockIdx.y) * qkv_stride;
+  q_out += int64_t(blockIdx.y) * Hq * D;
   const uint16_t* src = qkv + int64_t(head) * D;
   if (head >= Hq + Hk) {  // v: straight into the cache
     const int hv = head - Hq - Hk;

@@ -249,7 +249,7 @@ static int num_sms() {
 }
 
 template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int block, size_t smem, cudaStream_t s, Args... args) {
   // dynamic shared memory beyond the default 48 KB window (static + dynamic) needs the opt-in
   if (smem > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (smem > 48 * 1024) {
@@ -258,7 +258,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, int block, size_
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -788,9 +788,24 @@ int wisp_qk_norm_rope_kv(const uint16_t* qkv, int Hq, int Hk, int D, const uint1
   WISP_REQUIRE(Hq > 0 && Hk > 0 && D > 0 && D % 2 == 0 && D <= dec::QK_MAX_D && tmax > 0, "wisp_qk_norm_rope_kv: bad shape");
   const int heads = Hq + 2 * Hk;
   const cudaError_t e = launch_pdl(dec::qk_norm_rope_kv_kernel, (heads + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream), qkv, Hq,
-                                   Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax, q_out, k_cache, v_cache);
+                                   Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax, q_out, k_cache, v_cache, int64_t(0));
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_qk_norm_rope_kv: %s", cudaGetErrorString(e));
   return check_launch("qk_norm_rope_kv");
+}
+
+int wisp_qk_norm_rope_kv_rows(const uint16_t* qkv, int T, int64_t qkv_stride, int Hq, int Hk, int D, const uint16_t* qn_w,
+                              const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos0,
+                              int64_t tmax, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream) {
+  WISP_REQUIRE(qkv && qn_w && kn_w && cos_t && sin_t && pos0 && q_out && k_cache && v_cache,
+               "wisp_qk_norm_rope_kv_rows: NULL pointer");
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && D > 0 && D % 2 == 0 && D <= dec::QK_MAX_D && tmax > 0, "wisp_qk_norm_rope_kv_rows: bad shape");
+  WISP_REQUIRE(T >= 1 && T <= 65535 && qkv_stride >= int64_t(Hq + 2 * Hk) * D,
+               "wisp_qk_norm_rope_kv_rows: need 1 <= T <= 65535 and qkv_stride >= (Hq + 2 Hk) D");
+  const int heads = Hq + 2 * Hk;
+  const cudaError_t e = launch_pdl(dec::qk_norm_rope_kv_kernel, dim3((heads + 7) / 8, T), 256, 0, static_cast<cudaStream_t>(stream),
+                                   qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos0, tmax, q_out, k_cache, v_cache, qkv_stride);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_qk_norm_rope_kv_rows: %s", cudaGetErrorString(e));
+  return check_launch("qk_norm_rope_kv_rows");
 }
 
 int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {

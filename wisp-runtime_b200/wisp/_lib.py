@@ -57,6 +57,7 @@ SIGNATURES = {
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
     "wisp_gemv": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P]),
     "wisp_qk_norm_rope_kv": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _P, _P]),
+    "wisp_qk_norm_rope_kv_rows": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _P, _P]),
     "wisp_attn_workspace_floats": (_L, [_I, _I, _I, _L]),
     "wisp_gqa_decode_attn": (_I, [_P, _I, _I, _I, _P, _P, _L, _P, _F, _P, _P, _P]),
     "wisp_attn_decode": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _F, _P, _P]),

@@ -1,21 +1,37 @@
-"""Slot bookkeeping of the expert cache (drop-in for the reference ``wisp.cache_core``).
+"""Slot bookkeeping of the expert cache (drop-in for the reference ``wisp.cache_core.CacheCore``).
 
 Keys are ints, ``layer * n_experts + expert``.  Slots [0, n_static) hold a pinned resident set (the
 'static' profile-then-pin policy); slots [n_static, nslots) are managed by the dynamic policy:
 
-  lru     evict the least recently used slot
-  wsa     evict the lowest exponentially-decayed access frequency (working-set style)
-  static  nothing dynamic beyond the pinned set (misses still need a dynamic slot)
+  lru     evict the slot used longest ago
+  wsa     evict the slot whose key has the lowest exponentially decayed use frequency
+  static  nothing dynamic beyond the pinned set (misses still take a dynamic slot)
 
-Semantics follow wisp/cache_core.py (CacheCore: ensure / split / admit / preload / acquire / resized,
-hit / miss / eviction statistics); no torch here, so the host logic is tested on CPU.
+The structure is the host half of the device slot table that the MoE kernels read
+(``wisp_moe_decode_paged``): residency is a dense int array over the key space, ``slot_of[key]`` =
+slot or -1, exactly the layout of the int32 table on the GPU (``table()`` hands it over), plus its
+inverse ``owner[slot]``.  Around it:
+
+  - ``rank[slot]``: the eviction order of the policy -- the clock tick of the slot's last use (lru) or
+    its key's decayed frequency at that use (wsa, static); the eviction victim is the lowest rank
+    outside the protected slots, ties going to the lower slot.
+  - ``heat[key]``: decayed use frequency.  Decay is lazy: a use adds the current ``unit`` and every
+    clock step multiplies ``unit`` by 1/decay, so older uses weigh decay^age relative to new ones
+    without touching every key per step; before ``unit`` overflows, every heat value and ``unit`` are
+    divided by 1e100 together (ratios, hence decisions, are unchanged).
+  - ``fill``: slots [fill, nslots) have never been used; a miss takes the lowest of them before any
+    eviction (slots only become free again through ``resized``).
+
+Decisions -- which slot a key gets, what is evicted, hit/miss/eviction counts -- are those of the
+reference policy (wisp/cache_core.py:15-149); ``tests/test_cache_core.py`` replays operation traces
+recorded from the reference against this class.  No torch here: the host logic runs on CPU.
 """
 
 from __future__ import annotations
 
-from collections import defaultdict
-
 import numpy as np
+
+_RENORM = 1e100
 
 
 class CacheCore:
@@ -26,125 +42,179 @@ class CacheCore:
             raise AssertionError("n_static must be within [0, nslots]")
         self.nslots, self.policy, self.decay = int(nslots), policy, float(decay)
         self.n_static, self.admit_after = int(n_static), float(admit_after)
-        self.slot_key = np.full(self.nslots, -1, dtype=np.int64)
-        self.last = np.zeros(self.nslots)  # tick of the last use (lru)
-        self.score = np.zeros(self.nslots)  # decayed frequency at the last use (wsa)
-        self.key2slot = {}
-        self.free = list(range(self.nslots - 1, self.n_static - 1, -1))  # pop() hands out low slots first
-        self.tick, self.inc = 0, 1.0
-        self.freq = defaultdict(float)
+        self.owner = np.full(self.nslots, -1, dtype=np.int64)  # key held by each slot, -1 = empty
+        self.rank = np.zeros(self.nslots)  # eviction rank of each slot (see module docstring)
+        self.slot_of = np.full(0, -1, dtype=np.int64)  # key -> slot (-1: not resident), grown on demand
+        self.heat = np.zeros(0)  # key -> decayed use frequency, in units of `unit`
+        self.fill = self.n_static  # first never-used dynamic slot
+        self.tick, self.unit = 0, 1.0
         self.stats = dict(hits=0, misses=0, evictions=0, calls=0)
-        self.last_evicted = None  # key that the last acquire() evicted (None: it took a free slot)
+        self.last_evicted = None  # key the last acquire() evicted (None: it took a never-used slot)
 
-    # ---- clock and frequency --------------------------------------------------------------------
+    # ---- key space ----------------------------------------------------------------------------------
+    def _grow(self, top):
+        """Make key `top` addressable."""
+        if top < self.slot_of.size:
+            return
+        n = max(top + 1, 2 * self.slot_of.size, 64)
+        so = np.full(n, -1, dtype=np.int64)
+        so[: self.slot_of.size] = self.slot_of
+        he = np.zeros(n)
+        he[: self.heat.size] = self.heat
+        self.slot_of, self.heat = so, he
+
+    def _keys(self, keys):
+        ks = np.asarray(keys, dtype=np.int64).reshape(-1)
+        if ks.size:
+            if ks.min() < 0:
+                raise AssertionError("keys must be non-negative")
+            self._grow(int(ks.max()))
+        return ks
+
+    def _use_rank(self, key):
+        return float(self.tick) if self.policy == "lru" else float(self.heat[key])
+
+    # ---- clock and frequency ------------------------------------------------------------------------
     def step(self):
-        """One routing decision: advance the clock; frequencies decay by ``decay`` per step (kept as a
-        growing increment, renormalised before it overflows)."""
+        """One routing decision: advance the clock (frequencies age by one decay factor)."""
         self.tick += 1
-        self.inc /= self.decay
-        if self.inc > 1e100:
-            for k in self.freq:
-                self.freq[k] /= 1e100
-            self.score /= 1e100
-            self.inc /= 1e100
+        self.unit /= self.decay
+        if self.unit > _RENORM:
+            self.heat /= _RENORM
+            if self.policy != "lru":
+                self.rank /= _RENORM
+            self.unit /= _RENORM
 
     def note(self, keys):
-        for k in keys:
-            self.freq[k] += self.inc
-            s = self.key2slot.get(k)
-            if s is not None:
-                self.last[s] = self.tick
-                self.score[s] = self.freq[k]
+        """Record one use of each key (a key listed twice counts twice); resident keys' slots move up
+        in the eviction order."""
+        ks = self._keys(keys)
+        if not ks.size:
+            return
+        np.add.at(self.heat, ks, self.unit)
+        s = self.slot_of[ks]
+        live = s >= 0
+        if live.any():
+            if self.policy == "lru":
+                self.rank[s[live]] = float(self.tick)
+            else:
+                self.rank[s[live]] = self.heat[ks[live]]
 
     def norm_freq(self, k):
-        return self.freq.get(k, 0.0) / self.inc
+        return float(self.heat[k]) / self.unit if 0 <= k < self.heat.size else 0.0
 
     def should_admit(self, k):
         return self.norm_freq(k) >= self.admit_after
 
-    # ---- residency ----------------------------------------------------------------------------------
+    # ---- residency -----------------------------------------------------------------------------------
     def lookup(self, k):
-        return self.key2slot.get(k)
+        if 0 <= k < self.slot_of.size:
+            s = int(self.slot_of[k])
+            return s if s >= 0 else None
+        return None
+
+    @property
+    def key2slot(self):
+        """Resident keys as a {key: slot} dict (a snapshot)."""
+        ks = np.flatnonzero(self.slot_of >= 0)
+        return {int(k): int(self.slot_of[k]) for k in ks}
+
+    @property
+    def free(self):
+        """Never-used slots, in the order a list's pop() would hand them out (the last one first)."""
+        return list(range(self.nslots - 1, self.fill - 1, -1))
+
+    def table(self, size=None):
+        """The residency table key -> slot (-1: not resident) as int32, ``size`` keys long (the layout
+        of the device slot table)."""
+        n = self.slot_of.size if size is None else int(size)
+        t = np.full(n, -1, dtype=np.int32)
+        m = min(n, self.slot_of.size)
+        t[:m] = self.slot_of[:m]
+        return t
+
+    def _place(self, key, s):
+        self.owner[s] = key
+        self.slot_of[key] = s
+        self.rank[s] = self._use_rank(key)
 
     def preload(self, keys):
         """Pin ``keys`` into the static region, in order; returns the (key, slot) copies to issue."""
         if len(keys) > self.n_static:
             raise AssertionError("more preload keys than static slots")
+        self._keys(keys)
         out = []
         for s, k in enumerate(keys):
-            self.slot_key[s] = k
-            self.key2slot[k] = s
+            k = int(k)
+            self.owner[s] = k
+            self.slot_of[k] = s
             out.append((k, s))
         return out
 
     def acquire(self, key, protected):
-        """A slot for ``key``: a free one, else the dynamic slot the policy ranks lowest outside
-        ``protected`` (slots the current request already uses)."""
+        """A slot for ``key``: the lowest never-used slot, else the dynamic slot ranked lowest by the
+        policy outside ``protected`` (slots the current request already uses)."""
+        key = int(key)
+        self._grow(key)
         self.last_evicted = None
-        if self.free:
-            s = self.free.pop()
+        if self.fill < self.nslots:
+            s = self.fill
+            self.fill += 1
         else:
-            base = self.n_static
-            rank = (self.last if self.policy == "lru" else self.score)[base:].copy()
-            for p in protected:
-                if p >= base:
-                    rank[p - base] = np.inf
-            j = int(np.argmin(rank))
-            if not np.isfinite(rank[j]):
+            lo = self.n_static
+            cand = self.rank[lo:].copy()
+            p = np.fromiter((q - lo for q in protected if lo <= q < self.nslots), dtype=np.int64)
+            cand[p] = np.inf
+            j = int(np.argmin(cand)) if cand.size else 0
+            if not cand.size or not np.isfinite(cand[j]):
                 raise RuntimeError("no evictable slot: dynamic region smaller than the working request")
-            s = base + j
-            self.last_evicted = int(self.slot_key[s])
-            del self.key2slot[self.last_evicted]
+            s = lo + j
+            victim = int(self.owner[s])
+            self.slot_of[victim] = -1
+            self.last_evicted = victim
             self.stats["evictions"] += 1
-        self.slot_key[s] = key
-        self.key2slot[key] = s
-        self.last[s] = self.tick
-        self.score[s] = self.freq[key]
+        self._place(key, s)
         return s
 
-    # ---- policies ----------------------------------------------------------------------------------
+    # ---- policies ------------------------------------------------------------------------------------
     def ensure(self, keys):
         """Transfer policy: every key becomes resident.  Returns (slots aligned with keys, [(key, slot)]
         copies to issue for the misses)."""
         self.step()
         self.note(keys)
         self.stats["calls"] += 1
-        slots, loads, prot = [None] * len(keys), [], set()
-        for i, k in enumerate(keys):
-            s = self.key2slot.get(k)
-            if s is not None:
-                slots[i] = s
-                prot.add(s)
-                self.stats["hits"] += 1
-        for i, k in enumerate(keys):
-            if slots[i] is None:
-                s = self.acquire(k, prot)
-                slots[i] = s
-                prot.add(s)
+        ks = self._keys(keys)
+        got = self.slot_of[ks].copy()
+        hit = got >= 0
+        self.stats["hits"] += int(hit.sum())
+        busy = set(int(s) for s in got[hit])
+        loads = []
+        for i in np.flatnonzero(~hit):
+            k = int(ks[i])
+            s = self.lookup(k)  # a key listed twice: the first listing made it resident
+            if s is None:
+                s = self.acquire(k, busy)
                 loads.append((k, s))
                 self.stats["misses"] += 1
-        return slots, loads
+            busy.add(s)
+            got[i] = s
+        return [int(s) for s in got], loads
 
     def split(self, keys):
         """Hybrid policy: (hit keys, hit slots, miss keys); nothing is loaded."""
         self.step()
         self.note(keys)
         self.stats["calls"] += 1
-        hk, hs, mk = [], [], []
-        for k in keys:
-            s = self.key2slot.get(k)
-            if s is None:
-                mk.append(k)
-            else:
-                hk.append(k)
-                hs.append(s)
-        self.stats["hits"] += len(hk)
-        self.stats["misses"] += len(mk)
-        return hk, hs, mk
+        ks = self._keys(keys)
+        got = self.slot_of[ks]
+        hit = got >= 0
+        self.stats["hits"] += int(hit.sum())
+        self.stats["misses"] += int((~hit).sum())
+        return [int(k) for k in ks[hit]], [int(s) for s in got[hit]], [int(k) for k in ks[~hit]]
 
     def admit(self, key, protected):
-        """Bring a key computed elsewhere into the cache when it is hot enough; slot or None."""
-        if key in self.key2slot or not self.should_admit(key):
+        """Bring a key served elsewhere into the cache once it is hot enough; slot or None."""
+        if self.lookup(key) is not None or not self.should_admit(key):
             return None
         try:
             return self.acquire(key, protected)
@@ -152,21 +222,23 @@ class CacheCore:
             return None
 
     def resized(self, nslots):
-        """A new core of ``nslots`` keeping the hottest resident keys (lru: most recent, wsa: highest
-        score).  Returns (core, [(key, new_slot)]) -- the copies into the new pool."""
+        """A new core of ``nslots`` keeping the highest-ranked resident keys (lru: most recently used,
+        wsa: most frequent; equal ranks keep slot order).  Returns (core, [(key, new_slot)]) -- the
+        copies into the new pool, in new-slot order."""
         if self.n_static:
             raise AssertionError("resize is not supported with a static region")
         nc = CacheCore(nslots, self.policy, self.decay, 0, self.admit_after)
-        nc.tick, nc.inc, nc.freq, nc.stats = self.tick, self.inc, self.freq, self.stats
-        resident = [s for s in range(self.nslots) if self.slot_key[s] >= 0]
-        rank = self.last if self.policy == "lru" else self.score
-        resident.sort(key=lambda s: -rank[s])
+        nc.tick, nc.unit, nc.stats = self.tick, self.unit, self.stats
+        nc.slot_of = np.full(self.slot_of.size, -1, dtype=np.int64)
+        nc.heat = self.heat  # the frequency history carries over
+        live = np.flatnonzero(self.owner >= 0)
+        order = live[np.argsort(-self.rank[live], kind="stable")][: nc.nslots]
         loads = []
-        for s in resident[:nslots]:
-            k = int(self.slot_key[s])
-            ns = nc.free.pop()
-            nc.slot_key[ns] = k
-            nc.key2slot[k] = ns
-            nc.last[ns], nc.score[ns] = self.last[s], self.score[s]
+        for ns, s in enumerate(order):
+            k = int(self.owner[s])
+            nc.owner[ns] = k
+            nc.slot_of[k] = ns
+            nc.rank[ns] = self.rank[s]
             loads.append((k, ns))
+        nc.fill = len(order)
         return nc, loads

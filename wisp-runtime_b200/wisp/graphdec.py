@@ -6,29 +6,68 @@ depends on the current length.  The reference cuts a token at its 48 host decisi
 and records the pieces between them; with the experts resident (or a device-side slot table) there
 is no host decision, so a whole token is one graph:
 
-    embed -> per layer: [RMSNorm+qkv GEMV] [q/k norm, rotary, cache write] [attention split, combine]
-                        [o GEMV + residual] [RMSNorm+router GEMV] [top-k -> meta] [MoE gate/up, down]
+    embed -> per layer: [RMSNorm+qkv GEMV] [q/k norm, rotary, cache write, attention]
+                        [o GEMV + residual] [RMSNorm+router GEMV] [MoE gate/up (top-k inside), down]
           -> [residual + final RMSNorm + lm_head GEMV] [argmax]
 
 Each kernel is launched with programmatic dependent launch, so its prologue (and the weight stream of
 the GEMVs) overlaps the tail of the kernel before it.  ``greedy`` appends the position/token update
 to the graph, so a whole generation runs with no host round trip per token.
+
+Two constructors:
+
+  GraphDecoder(weights: DecoderWeights, tmax=...)   the weights in the layout the kernels stream
+  GraphDecoder(model, rt, tmax)                     the reference's form: an HF Qwen3-MoE model (its
+                                                    MoE blocks attached or not) whose experts live in
+                                                    ``rt.cache`` / ``rt.store``; residency is a device
+                                                    slot table, misses are read from the pinned host
+                                                    store and paged in one token behind
+
+``prefill`` runs the prompt in chunks (the reference's chunked prefill, wisp/graphdec.py:99-152): per
+layer the q/k/v, o and router products as GEMMs over the chunk, q/k RMSNorm + rotary + cache write
+for all its tokens in one kernel, causal attention over the cache, and the batched MoE kernel.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 
 from . import kernels
 from .model import DecoderWeights, rotary_tables
 
 
+def _get_kv(pk, i):
+    """(keys, values) [1, Hk, T, D] of layer i from an HF cache object or a legacy tuple list."""
+    if hasattr(pk, "layers"):
+        return pk.layers[i].keys, pk.layers[i].values
+    if hasattr(pk, "key_cache"):
+        return pk.key_cache[i], pk.value_cache[i]
+    return pk[i][0], pk[i][1]
+
+
 class GraphDecoder:
-    def __init__(self, w: DecoderWeights, tmax=2048, use_graph=True, slot_table=None, pool=None, store_host=None):
+    def __init__(self, w, rt=None, tmax=2048, use_graph=True, slot_table=None, pool=None, store_host=None, pager=None):
+        self.model, self.rt = None, rt
+        if not isinstance(w, DecoderWeights):  # the reference's GraphDecoder(model, rt, tmax)
+            self.model = w
+            if rt is None or getattr(rt, "cache", None) is None:
+                raise kernels.WispError("GraphDecoder(model, rt, tmax): the experts come from rt.cache")
+            cache = rt.cache
+            st = cache.store
+            if cache.decode_on_load or st.bits not in (4, 3, 2):
+                raise kernels.WispError("GraphDecoder(model, rt): needs packed 4/3/2-bit slots (no decode_on_load)")
+            from .cache import SlotTablePager
+
+            w = DecoderWeights.from_hf(self.model, None, bits=st.bits, group=st.group)
+            self.cache = cache
+            pager = SlotTablePager(cache)
+            slot_table, pool, store_host = pager.table, cache.gpu, st.host
         cfg = w.cfg
         self.w, self.cfg = w, cfg
         self.pool = w.pool if pool is None else pool
         self.store_host = store_host  # pinned host store: non-resident experts are read from it
+        self.pager = pager
         dev = w.embed.device
         self.dev = dev
         self.L, self.H = cfg.layers, cfg.hidden
@@ -41,7 +80,7 @@ class GraphDecoder:
         d = dict(device=dev, dtype=bf)
         self.kc = torch.zeros(self.L, self.Hk, self.tmax, self.D, **d)
         self.vc = torch.zeros(self.L, self.Hk, self.tmax, self.D, **d)
-        self.cos, self.sin = rotary_tables(self.D, self.tmax, cfg.rope_theta, dev)
+        self.cos, self.sin = self._rotary(self.tmax)
         self.ctl = torch.zeros(2, dtype=torch.int64, device=dev)  # [token, position]
         self.h_emb = torch.zeros(H, **d)
         self.h_res = torch.zeros(H, **d)  # residual stream entering a layer
@@ -63,8 +102,24 @@ class GraphDecoder:
         self.scale = self.D ** -0.5
         self.pos = 0
         self.graph = self.greedy_graph = None
+        if self.pager is not None:  # routing rows of the last tokens, for the policy one token behind
+            self.rows_host = [torch.zeros(self.L, 2 * self.k, dtype=torch.float32, pin_memory=True) for _ in range(2)]
+            self.turn = 0
+            self.waiting = None  # (rows_host index, event) of the last replayed token, not yet planned
         # router top-k folded into the MoE kernels where the tensor-core MoE path takes the shape
         self.routed_moe = self._try_routed_moe()
+
+    def _rotary(self, tmax):
+        """cos / sin [tmax, D] bf16: the HF model's own rotary embedding when there is a model, else the
+        rotate-half tables of the configured base."""
+        if self.model is not None and hasattr(self.model.model, "rotary_emb"):
+            pos = torch.arange(tmax, device=self.dev)[None]
+            cos, sin = self.model.model.rotary_emb(torch.zeros(1, 1, self.H, device=self.dev, dtype=torch.bfloat16), pos)
+            return cos[0].to(torch.bfloat16).contiguous(), sin[0].to(torch.bfloat16).contiguous()
+        return rotary_tables(self.D, tmax, self.cfg.rope_theta, self.dev)
+
+    def _out_logits(self):
+        return self.logits.view(1, -1) if self.model is not None else self.logits
 
     # ---------------------------------------------------------------------------------------------
     def _layer(self, l):
@@ -179,16 +234,27 @@ class GraphDecoder:
 
     # ---------------------------------------------------------------------------------------------
     @torch.no_grad()
-    def load_kv(self, k, v, T):
-        """Context of T positions: k, v [L, Hk, T, D] (e.g. from an HF prefill)."""
-        assert T < self.tmax, f"context {T} >= tmax {self.tmax}"
-        self.kc[:, :, :T].copy_(k)
-        self.vc[:, :, :T].copy_(v)
-        self.pos = T
+    def load_kv(self, pk, v=None, T=None):
+        """Hand over a context of T positions: ``load_kv(hf_cache, T)`` (the reference's form, an HF
+        cache object or per-layer (k, v) pairs of [1, Hk, T, D]) or ``load_kv(k, v, T)`` with
+        k, v [L, Hk, T, D]."""
+        if T is None:  # load_kv(pk, T)
+            T = int(v)
+            assert T < self.tmax, f"context {T} >= tmax {self.tmax}"
+            for i in range(self.L):
+                k_i, v_i = _get_kv(pk, i)
+                self.kc[i, :, :T].copy_(k_i.reshape(self.Hk, -1, self.D)[:, :T])
+                self.vc[i, :, :T].copy_(v_i.reshape(self.Hk, -1, self.D)[:, :T])
+        else:
+            assert T < self.tmax, f"context {T} >= tmax {self.tmax}"
+            self.kc[:, :, :T].copy_(pk)
+            self.vc[:, :, :T].copy_(v)
+        self.pos = int(T)
 
     @torch.no_grad()
     def next(self, token):
-        """token: LongTensor [1] on the device -> logits [V] (bf16) for the following position."""
+        """token: LongTensor [1] on the device -> logits (bf16 [V]; [1, V] for a model-built decoder)
+        for the following position."""
         assert self.pos < self.tmax, "context full"
         if self.use_graph and self.graph is None:
             self.capture()
@@ -199,15 +265,9 @@ class GraphDecoder:
         else:
             self._step()
         self.pos += 1
-        return self.logits
-
-    @torch.no_grad()
-    def prefill(self, ids):
-        """Run prompt tokens one decode step each (positions pos, pos+1, ...); returns the last logits."""
-        logits = None
-        for t in ids.reshape(-1):
-            logits = self.next(t.reshape(1))
-        return logits
+        if self.pager is not None:
+            self._after_replay()
+        return self._out_logits()
 
     @torch.no_grad()
     def greedy(self, token, steps):
@@ -222,8 +282,154 @@ class GraphDecoder:
         for i in range(steps):
             self.greedy_graph.replay()
             out[i : i + 1].copy_(self.next_token)
+            if self.pager is not None:
+                self._after_replay()
         self.pos += steps
         return out
+
+    @torch.no_grad()
+    def step_greedy(self):
+        """One greedy token from the device-side token and position (no host input)."""
+        if self.greedy_graph is None:
+            self.capture()
+        self.greedy_graph.replay()
+        self.pos += 1
+        if self.pager is not None:
+            self._after_replay()
+
+    # ---- chunked prefill -------------------------------------------------------------------------
+    @torch.no_grad()
+    def prefill(self, ids, start=None, chunk=None):
+        """Run prompt tokens ``ids`` at positions start .. start + T - 1 (default: the current position,
+        so earlier context is reused), writing K/V straight into the static cache, in chunks of at most
+        ``chunk`` tokens (<= 2048 / top_k, the batched MoE kernel's pair limit).  Returns the logits of
+        the last token.  Reference: wisp/graphdec.py:99-152."""
+        start = self.pos if start is None else int(start)
+        ids = ids.reshape(-1).to(self.dev)
+        n = ids.numel()
+        assert start + n <= self.tmax, f"context {start + n} > capacity {self.tmax}"
+        if self.pager is not None:
+            self.flush()  # every page-in landed and published: residency is settled
+        most = max(1, 2048 // self.k)
+        chunk = most if chunk is None else max(1, min(int(chunk), most))
+        for c0 in range(0, n, chunk):
+            self._prefill_chunk(ids[c0 : c0 + chunk], start + c0)
+        self.pos = start + n
+        return self._out_logits()
+
+    def _chunk_moe(self, l, sel, rw, xn):
+        """MoE of the chunk's tokens in layer l (routing sel [T, k], rw fp32 [T, k]) with the batched
+        kernel.  Its experts must be resident in the pool it reads: with an expert cache they are paged
+        in as one request per layer, or in groups the pool can hold (pairs outside a group carry slot
+        -1, and the groups' outputs are summed) when the layer's working set is larger than the cache."""
+        c, H, I, k = self.cfg, self.H, self.I, self.k
+        cache = getattr(self, "cache", None)
+        if cache is None:
+            slots = (sel + l * self.E).float() if self.slot_table is None else self.slot_table[sel + l * self.E].float()
+            meta = torch.cat([slots, rw], 1).contiguous()
+            return kernels.moe_batched(self.pool, meta, xn, k, H * I, H, I, c.bits, c.group)
+        base = l * self.E
+        sel_c = sel.cpu()
+        uniq = torch.unique(sel_c).tolist()
+        room = max(1, cache.core.nslots - cache.core.n_static)
+        out = None
+        for i in range(0, len(uniq), room):
+            group = uniq[i : i + room]
+            slot_of = torch.full((self.E,), -1.0)
+            slot_of[group] = torch.tensor(cache.ensure([base + e for e in group]), dtype=torch.float32)
+            slots = slot_of[sel_c].to(self.dev, non_blocking=True)
+            meta = torch.cat([slots, torch.where(slots >= 0, rw, torch.zeros_like(rw))], 1).contiguous()
+            y = kernels.moe_batched(cache.gpu, meta, xn, k, H * I, H, I, c.bits, c.group)
+            out = y if out is None else out + y
+        return out
+
+    def _prefill_chunk(self, part, s0):
+        c, w = self.cfg, self.w
+        T, H, Hq, Hk, D, k = part.numel(), self.H, self.Hq, self.Hk, self.D, self.k
+        pos0 = torch.full((1,), s0, dtype=torch.int64, device=self.dev)
+        S = s0 + T
+        mask = torch.arange(S, device=self.dev)[None, :] <= (s0 + torch.arange(T, device=self.dev))[:, None]
+        h = w.embed.index_select(0, part)  # [T, H]
+        for l in range(self.L):
+            lw = w.layers[l]
+            xn = kernels.rmsnorm(h, lw["in_norm"], c.eps)
+            qkv = xn @ lw["wqkv"].t()
+            q = kernels.qk_norm_rope_kv_rows(qkv, Hq, Hk, D, lw["q_norm"], lw["k_norm"], c.eps, self.cos, self.sin, pos0,
+                                            self.kc[l], self.vc[l])
+            o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], self.kc[l, :, :S][None], self.vc[l, :, :S][None],
+                                               attn_mask=mask, scale=self.scale, enable_gqa=True)
+            h = h + o[0].transpose(0, 1).reshape(T, Hq * D) @ lw["wo"].t()
+            xn2 = kernels.rmsnorm(h, lw["post_norm"], c.eps)
+            p = F.softmax(xn2 @ lw["router"].t(), dim=-1, dtype=torch.float32)
+            rw, sel = torch.topk(p, k, dim=-1)
+            if c.norm_topk:
+                rw = rw / rw.sum(-1, keepdim=True)
+            h = h + self._chunk_moe(l, sel, rw.to(torch.bfloat16).float(), xn2)
+        kernels.gemv(w.lm_head, h[-1].contiguous(), norm_w=w.final_norm, eps=c.eps, out=self.logits)
+
+    # ---- capacity ----------------------------------------------------------------------------------
+    @torch.no_grad()
+    def resize(self, tmax):
+        """Change the context capacity, keeping the first ``pos`` positions; graphs are re-captured on
+        the next step.  Reference: wisp/graphdec.py:87-97."""
+        tmax = (tmax + 63) // 64 * 64
+        if tmax == self.tmax:
+            return
+        if self.pager is not None:
+            self.flush()
+        torch.cuda.synchronize()
+        keep = min(self.pos, tmax)
+        d = dict(device=self.dev, dtype=torch.bfloat16)
+        kc = torch.zeros(self.L, self.Hk, tmax, self.D, **d)
+        vc = torch.zeros(self.L, self.Hk, tmax, self.D, **d)
+        kc[:, :, :keep].copy_(self.kc[:, :, :keep])
+        vc[:, :, :keep].copy_(self.vc[:, :, :keep])
+        self.kc, self.vc = kc, vc
+        self.tmax, self.pos = tmax, keep
+        self.cos, self.sin = self._rotary(tmax)
+        self.attn_ws = kernels.attn_workspace(self.Hq, self.Hk, self.D, tmax, self.dev)
+        self.graph = self.greedy_graph = None
+        torch.cuda.empty_cache()
+
+    # ---- paging one token behind (decoders with a SlotTablePager) ----------------------------------
+    def _after_replay(self):
+        i = self.turn
+        self.turn ^= 1
+        self.rows_host[i].copy_(self.rows, non_blocking=True)
+        evt = torch.cuda.Event()
+        evt.record()
+        prev, self.waiting = self.waiting, (i, evt)
+        if prev is not None:
+            self._plan(*prev)
+
+    def _plan(self, j, e):
+        e.synchronize()  # that token has finished; the one replayed after it keeps the GPU busy
+        rows = self.rows_host[j][:, : self.k].to(torch.int64).tolist()
+        self.pager.apply(rows)
+        if self.rt is not None:
+            st = self.rt.stats
+            st["layer_calls"] += self.L
+            st["gpu_experts"] += self.L * self.k
+            if self.rt.recorder is not None:
+                import numpy as np
+
+                for l, r in enumerate(rows):
+                    self.rt.recorder.append((l, np.array([r])))
+
+    @torch.no_grad()
+    def flush(self):
+        """Run the policy on the last replayed token and wait for every page-in."""
+        if self.pager is None:
+            return
+        if self.waiting is not None:
+            j, e = self.waiting
+            self.waiting = None
+            self._plan(j, e)
+        self.pager.drain()
+
+    def host_reads_total(self):
+        """Experts read from the host store so far (synchronises)."""
+        return int(self.miss_count.item()) if self.miss_count is not None else 0
 
 
 class PagedGraphDecoder(GraphDecoder):
@@ -384,50 +590,6 @@ class DevicePagedDecoder(GraphDecoder):
         from .cache import SlotTablePager
 
         self.cache = cache
-        self.pager = SlotTablePager(cache, admit)
-        super().__init__(w, tmax=tmax, use_graph=True, slot_table=self.pager.table, pool=cache.gpu,
-                         store_host=cache.store.host)
-        self.rows_host = [torch.zeros(self.L, 2 * self.k, dtype=torch.float32, pin_memory=True) for _ in range(2)]
-        self.turn = 0
-        self.waiting = None  # (rows_host index, event) of the last replayed token, not yet planned
-
-    def _after_replay(self):
-        i = self.turn
-        self.turn ^= 1
-        self.rows_host[i].copy_(self.rows, non_blocking=True)
-        evt = torch.cuda.Event()
-        evt.record()
-        prev, self.waiting = self.waiting, (i, evt)
-        if prev is not None:
-            j, e = prev
-            e.synchronize()  # the token before this one has finished; this one keeps the GPU busy
-            self.pager.apply(self.rows_host[j][:, : self.k].to(torch.int64).tolist())
-
-    @torch.no_grad()
-    def next(self, token):
-        logits = super().next(token)
-        self._after_replay()
-        return logits
-
-    @torch.no_grad()
-    def step_greedy(self):
-        """One greedy token from the device-side token and position (no host input)."""
-        if self.greedy_graph is None:
-            self.capture()
-        self.greedy_graph.replay()
-        self.pos += 1
-        self._after_replay()
-
-    @torch.no_grad()
-    def flush(self):
-        """Run the policy on the last replayed token and wait for every page-in."""
-        if self.waiting is not None:
-            j, e = self.waiting
-            self.waiting = None
-            e.synchronize()
-            self.pager.apply(self.rows_host[j][:, : self.k].to(torch.int64).tolist())
-        self.pager.drain()
-
-    def host_reads_total(self):
-        """Experts read from the host store so far (synchronises)."""
-        return int(self.miss_count.item())
+        pager = SlotTablePager(cache, admit)
+        super().__init__(w, tmax=tmax, use_graph=True, slot_table=pager.table, pool=cache.gpu,
+                         store_host=cache.store.host, pager=pager)

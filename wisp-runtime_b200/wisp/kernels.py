@@ -37,6 +37,7 @@ __all__ = [
     "rmsnorm",
     "gemv",
     "qk_norm_rope_kv",
+    "qk_norm_rope_kv_rows",
     "gqa_decode_attn",
     "attn_decode",
     "router_topk",
@@ -527,6 +528,23 @@ def qk_norm_rope_kv(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, k_cache,
     _lib.call(
         "wisp_qk_norm_rope_kv", qkv.data_ptr(), Hq, Hk, D, qn_w.data_ptr(), kn_w.data_ptr(), float(eps), cos_t.data_ptr(),
         sin_t.data_ptr(), pos.data_ptr(), tmax, q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _stream(qkv),
+    )
+    return q_out
+
+
+def qk_norm_rope_kv_rows(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos0, k_cache, v_cache, q_out=None):
+    """qk_norm_rope_kv for the T tokens of ``qkv`` [T, (Hq + 2 Hk) D] at positions *pos0 .. *pos0 + T - 1
+    (``pos0`` an int64 device scalar) -> q [T, Hq, D]; K/V rows go into the caches [Hk, tmax, D]."""
+    _need_cuda(qkv, pos0)
+    _bf16(qkv, qn_w, kn_w, cos_t, sin_t, k_cache, v_cache)
+    T = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=qkv.device)
+    tmax = k_cache.shape[-2]
+    _lib.call(
+        "wisp_qk_norm_rope_kv_rows", qkv.data_ptr(), T, qkv.stride(0), Hq, Hk, D, qn_w.data_ptr(), kn_w.data_ptr(), float(eps),
+        cos_t.data_ptr(), sin_t.data_ptr(), pos0.data_ptr(), tmax, q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        _stream(qkv),
     )
     return q_out
 

@@ -108,7 +108,10 @@ class DecoderWeights:
     @torch.no_grad()
     def from_hf(model, experts, bits=4, group=128, device="cuda"):
         """Weights of an HF Qwen3-MoE causal LM.  ``experts(l)`` returns the layer's expert weights as
-        three tensors gate [E, I, H], up [E, I, H], down [E, H, I]; they are quantized into the pool."""
+        three tensors gate [E, I, H], up [E, I, H], down [E, H, I]; they are quantized into the pool.
+        With ``experts=None`` only the dense weights are taken (the experts live in an expert store)
+        and ``pool`` is None.  The router is ``layer.mlp.gate.weight`` (an HF gate or router module,
+        or the gate a PagedMoEBlock kept)."""
         hc = model.config
         cfg = DecoderConfig(
             vocab=hc.vocab_size,
@@ -138,7 +141,7 @@ class DecoderWeights:
         w.final_norm = t(m.norm.weight)
         E, n = cfg.experts, cfg.hidden * cfg.moe_inter
         w.nbytes = quant.expert_nbytes(n, bits, group)
-        w.pool = torch.empty((cfg.layers * E, w.nbytes), dtype=torch.uint8, device=device)
+        w.pool = None if experts is None else torch.empty((cfg.layers * E, w.nbytes), dtype=torch.uint8, device=device)
         for l, layer in enumerate(m.layers):
             at = layer.self_attn
             w.layers.append(
@@ -152,6 +155,8 @@ class DecoderWeights:
                     router=t(layer.mlp.gate.weight),
                 )
             )
+            if experts is None:
+                continue
             gate, up, down = experts(l)
             w3 = torch.stack([gate.reshape(E, n), up.reshape(E, n), down.reshape(E, n)], 1).to(device=device, dtype=torch.float32)
             w.pool[l * E : (l + 1) * E].copy_(quant.quantize_batch(w3, bits, group))
