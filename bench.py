@@ -48,6 +48,7 @@ NCU_TRAFFIC_GPTOSS_LAYER_BS1 = 35_287_552 + 17_679_872
 
 
 GO_L, GO_H, GO_I, GO_E, GO_K = 24, 2880, 2880, 32, 4  # gpt-oss-20b MoE shape (config 5)
+TIMELINE_TOKENS = 24  # decoder with device paging: untimed steps traced with CUDA events after the timed ones
 
 
 def parse():
@@ -68,6 +69,14 @@ def parse():
                     "the MoE kernels, page-ins one token behind (device), or the reference's per-layer host "
                     "decision with page-in before use (host)")
     ap.add_argument("--no-prefetch", action="store_true", help="host paging: no next-layer expert prefetch")
+    ap.add_argument("--tokens", default="forced", choices=["forced", "greedy"],
+                    help="decoder: the token each step decodes -- a seeded random token stream (teacher forcing, so "
+                    "routing keeps moving the way a real prompt stream does) or the model's own greedy choice (a "
+                    "random-init model settles into a fixed loop and hardly pages)")
+    ap.add_argument("--admit", default="hot", choices=["all", "hot"],
+                    help="decoder, device paging: page every miss in (all) or only experts whose decayed use "
+                    "frequency reached the cache's admit threshold (hot); misses are read from the pinned host "
+                    "store either way")
     ap.add_argument("--transport", default="auto", choices=["auto", "nccl", "p2p"],
                     help="moe-ep exchange: NCCL all-to-alls or kernel stores into peer memory (auto: p2p when N > 1)")
     a = ap.parse_args()
@@ -88,8 +97,9 @@ def workload_config(a, n):
             res, graph = "all experts resident", "(whole-token CUDA graph)"
         elif a.paging == "device":
             res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU; residency in a device slot "
-                   "table, non-resident experts read by the MoE kernels from the pinned host store, page-ins decided "
-                   "one token behind and copied with cudaMemcpyAsync on a side stream)")
+                   "table, non-resident experts read by the MoE kernels from the pinned host store, page-ins "
+                   f"({'every miss' if a.admit == 'all' else 'experts that turned hot'}) decided one token behind and "
+                   "copied with cudaMemcpyAsync on a side stream)")
             graph = "(whole-token CUDA graph)"
         else:
             res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU, pinned host store, "
@@ -98,7 +108,8 @@ def workload_config(a, n):
         return {
             "workload": f"qwen3-30b-a3b greedy decode bs=1: {L} layers, 32q/4kv heads x 128, {E} experts top-{K_TOP}, "
             f"{a.bits}-bit g{G} experts, {res}, bf16 attention/embeddings, vocab {VOCAB}, "
-            f"{a.prompt}-token seeded prompt then one token per step " + graph,
+            f"{a.prompt}-token seeded prompt (chunked prefill) then one token per step, "
+            + ("teacher-forced from a seeded random token stream " if a.tokens == "forced" else "greedy ") + graph,
             "model": "Qwen3-30B-A3B-shaped (random init)",
             "global_batch": n,
             "seq_len": a.prompt,
@@ -330,12 +341,24 @@ def _cpu_weights(bits, attention, context):
     return _CPU_WEIGHTS[key]
 
 
+_CPU_POOL = None
+
+
+def cpu_pool():
+    """One thread per host core, kept for the whole run (numpy releases the GIL in its kernels)."""
+    global _CPU_POOL
+    if _CPU_POOL is None:
+        from concurrent.futures import ThreadPoolExecutor
+
+        _CPU_POOL = ThreadPoolExecutor(max_workers=os.cpu_count() or 1)
+    return _CPU_POOL
+
+
 def cpu_layer_sample(bits, seed=0, attention=False, context=512):
     """One layer, one token, on the CPU with the oracle (dequantize -> fp32 matmul; experts in
     parallel over the host cores): the fused MoE, plus (attention=True) RMSNorm, q/k/v/o projections,
     GQA attention over ``context`` cached positions and the router.  Returns (seconds, threads)."""
     import numpy as np
-    from concurrent.futures import ThreadPoolExecutor
 
     from oracle import wisp_oracle as O
 
@@ -345,25 +368,24 @@ def cpu_layer_sample(bits, seed=0, attention=False, context=512):
     x = rng.standard_normal(H).astype(np.float32)
     w = np.full(K_TOP, 1.0 / K_TOP, np.float32)
     nw = np.ones(H, np.float32)
-    threads = os.cpu_count() or 1
 
     def one(j):
         gm, um, dm = O.expert_weights(wt["pool"], j, n, bits, G, H, I)
         return w[j] * (dm @ (O.silu(gm @ x) * (um @ x)))
 
-    with ThreadPoolExecutor(max_workers=threads) as ex:
-        t0 = time.perf_counter()
-        if attention:
-            xn = O.rmsnorm(x, nw)
-            qkv = wt["wqkv"] @ xn
-            q = qkv[: HQ * D].reshape(HQ, D)
-            att = O.gqa_decode_attention(q, wt["kc"], wt["vc"], context - 1, D**-0.5)
-            hm = x + wt["wo"] @ att.reshape(-1)
-            O.router_topk((wt["wr"] @ O.rmsnorm(hm, nw))[None], K_TOP)
-        out = sum(ex.map(one, range(K_TOP)))
-        dt = time.perf_counter() - t0
+    ex = cpu_pool()
+    t0 = time.perf_counter()
+    if attention:
+        xn = O.rmsnorm(x, nw)
+        qkv = wt["wqkv"] @ xn
+        q = qkv[: HQ * D].reshape(HQ, D)
+        att = O.gqa_decode_attention(q, wt["kc"], wt["vc"], context - 1, D**-0.5)
+        hm = x + wt["wo"] @ att.reshape(-1)
+        O.router_topk((wt["wr"] @ O.rmsnorm(hm, nw))[None], K_TOP)
+    out = sum(ex.map(one, range(K_TOP)))
+    dt = time.perf_counter() - t0
     assert np.isfinite(out).all()
-    return dt, threads
+    return dt, os.cpu_count() or 1
 
 
 def cpu_head_sample(seed=0, frac=16):
@@ -382,96 +404,107 @@ def cpu_head_sample(seed=0, frac=16):
     return dt * frac
 
 
-def cpu_ep_tok_s(a, seed=0, distinct=60.0, sample_experts=4):
-    """Batched tokens/s of the CPU path: the oracle's per-expert cost (dequantize + fp32 MLP for the
-    average number of tokens an expert receives), measured on a few experts, times the distinct experts
-    of a layer, times L, for EP_BATCH tokens."""
+def _parallel_expert_cost(fn, m):
+    """Wall time of m expert computations run in parallel on the host cores, per expert."""
+    ex = cpu_pool()
+    t0 = time.perf_counter()
+    list(ex.map(fn, range(m)))
+    return (time.perf_counter() - t0) / m
+
+
+def cpu_sample(a, seed=0, distinct=60.0):
+    """One bounded sample of the workload on the CPU path (the reference's algorithm restated in numpy:
+    dequantize, then fp32 products), on every host core.  Returns (sample seconds, tokens/s that the
+    sample implies for the whole step, cores, what the sample was)."""
     import numpy as np
 
     from oracle import wisp_oracle as O
 
-    rng = np.random.default_rng(seed)
-    n = H * I
-    toks = max(1, int(round(EP_BATCH * K_TOP / distinct)))
-    pool = np.stack([O.quantize((rng.standard_normal((3, n)) * 0.02).astype(np.float32), a.bits, G) for _ in range(sample_experts)])
-    x = rng.standard_normal((toks, H)).astype(np.float32)
-    t0 = time.perf_counter()
-    for j in range(sample_experts):
-        gm, um, dm = O.expert_weights(pool, j, n, a.bits, G, H, I)
-        y = (O.silu(x @ gm.T) * (x @ um.T)) @ dm.T
-    per_expert = (time.perf_counter() - t0) / sample_experts
-    assert np.isfinite(y).all()
-    step = per_expert * distinct * L
-    return EP_BATCH / step, 1, (f"oracle per-expert cost (dequantize + fp32 MLP of {toks} tokens) on {sample_experts} "
-                               f"experts x {distinct:.0f} distinct experts per layer x {L} layers, {EP_BATCH} tokens per step")
-
-
-def cpu_gptoss_tok_s(a, seed=0, distinct=4.0):
-    """Tokens/s of the CPU path for the gpt-oss MoE stack: the oracle's gpt-oss expert (dequantize,
-    x W_gu + b, clamped SwiGLU, . W_d + b) on one sampled expert for the average number of tokens an
-    expert receives, times the distinct experts of a layer, times the layers."""
-    import numpy as np
-
-    from oracle import wisp_oracle as O
-
-    rng = np.random.default_rng(seed)
-    n = GO_H * GO_I
-    toks = max(1, int(round(a.batch * GO_K / distinct)))
-    pool = O.quantize((rng.standard_normal((3, n)) * 0.02).astype(np.float32), a.bits, G)[None]
-    gub = np.zeros((1, 2 * GO_I), np.uint16)
-    db = np.zeros((1, GO_H), np.uint16)
-    x = rng.standard_normal((toks, GO_H)).astype(np.float32)
-    t0 = time.perf_counter()
-    y = O.gptoss_ref(pool, np.zeros((toks, 1), np.int64), np.ones((toks, 1), np.float32), x, GO_H, GO_I, a.bits, G, gub, db)
-    per_expert = time.perf_counter() - t0
-    assert np.isfinite(y).all()
-    step = per_expert * distinct * GO_L
-    return a.batch / step, 1, (f"oracle gpt-oss expert (dequantize + fp32 MLP of {toks} token(s)) on 1 expert x "
-                               f"{distinct:.1f} distinct experts per layer x {GO_L} layers, {a.batch} token(s) per step")
-
-
-def cpu_tok_s(a, seed=0, distinct=60.0):
-    """Tokens/s of the CPU path, extrapolated from one sampled layer (x L) and a sampled lm_head."""
-    if a.workload == "moe-ep":
-        return cpu_ep_tok_s(a, seed, distinct)
-    if a.workload == "gptoss-moe":
-        return cpu_gptoss_tok_s(a, seed, distinct if distinct < 60.0 else float(min(GO_E, a.batch * GO_K)))
+    threads = os.cpu_count() or 1
     if a.workload == "decoder":
-        dt, threads = cpu_layer_sample(a.bits, seed=seed, attention=True, context=a.prompt)
-        return 1.0 / (dt * L + cpu_head_sample(seed)), threads, (
-            f"1 decoder layer (RMSNorm, q/k/v/o projections, GQA attention over {a.prompt} positions, router, "
-            f"8 experts) + 1/16 of lm_head on the oracle, extrapolated x{L} layers and x16 rows"
-        )
-    dt, threads = cpu_layer_sample(a.bits, seed=seed)
-    return 1.0 / (dt * L), threads, f"1 MoE layer (8 experts, 1 token) on the oracle, extrapolated x{L} layers"
+        dt, _ = cpu_layer_sample(a.bits, seed=seed, attention=True, context=a.prompt)
+        head = cpu_head_sample(seed)
+        return dt, 1.0 / (dt * L + head), threads, (
+            f"one decoder layer of one token (RMSNorm, q/k/v/o projections, GQA attention over {a.prompt} positions, "
+            f"router, 8 experts in parallel) per sample; token time = {L} x the layer + lm_head (1/16 of its rows timed, x16)")
+    if a.workload == "moe-stack":
+        dt, _ = cpu_layer_sample(a.bits, seed=seed)
+        return dt, 1.0 / (dt * L), threads, f"one MoE layer (8 experts in parallel, 1 token) per sample; token time = {L} x the layer"
+    rng = np.random.default_rng(seed)
+    if a.workload == "moe-ep":
+        n = H * I
+        toks = max(1, int(round(EP_BATCH * K_TOP / distinct)))
+        wt = _cpu_weights(a.bits, False, 0)
+        x = rng.standard_normal((toks, H)).astype(np.float32)
+
+        def one(j):
+            gm, um, dm = O.expert_weights(wt["pool"], j % K_TOP, n, a.bits, G, H, I)
+            return (O.silu(x @ gm.T) * (x @ um.T)) @ dm.T
+
+        m = max(K_TOP, threads)
+        per = _parallel_expert_cost(one, m)
+        return per * m, EP_BATCH / (per * distinct * L), threads, (
+            f"{m} experts in parallel (dequantize + fp32 MLP of the {toks} tokens an expert receives on average) per "
+            f"sample; step time = per-expert time x {distinct:.0f} distinct experts per layer x {L} layers, {EP_BATCH} tokens")
+    # gptoss-moe
+    n = GO_H * GO_I
+    dist_go = distinct if distinct < 60.0 else float(min(GO_E, a.batch * GO_K))
+    toks = max(1, int(round(a.batch * GO_K / dist_go)))
+    if "gptoss" not in _CPU_WEIGHTS:
+        _CPU_WEIGHTS["gptoss"] = O.quantize((np.random.default_rng(77).standard_normal((3, n)) * 0.02).astype(np.float32),
+                                            a.bits, G)[None]
+    pool = _CPU_WEIGHTS["gptoss"]
+    gub, db = np.zeros((1, 2 * GO_I), np.uint16), np.zeros((1, GO_H), np.uint16)
+    x = rng.standard_normal((toks, GO_H)).astype(np.float32)
+
+    def one(j):
+        return O.gptoss_ref(pool, np.zeros((toks, 1), np.int64), np.ones((toks, 1), np.float32), x, GO_H, GO_I, a.bits, G,
+                            gub, db)
+
+    m = max(GO_K, threads)
+    per = _parallel_expert_cost(one, m)
+    return per * m, a.batch / (per * dist_go * GO_L), threads, (
+        f"{m} gpt-oss experts in parallel (dequantize + fp32 MLP of {toks} token(s)) per sample; step time = per-expert "
+        f"time x {dist_go:.1f} distinct experts per layer x {GO_L} layers, {a.batch} token(s) per step")
 
 
-CPU_SAMPLES = 5  # timed CPU samples per reference run (about a second each on 16 cores)
+def cpu_tok_s(a, seed=0, distinct=60.0, samples=2):
+    """The CPU baseline of the wisp arm's line: one warm-up sample, then the mean of ``samples``."""
+    cpu_sample(a, seed, distinct)
+    got = [cpu_sample(a, seed + 1 + i, distinct) for i in range(samples)]
+    return statistics.mean(g[1] for g in got), got[0][2], got[0][3] + f"; mean of {samples} samples after 1 warm-up"
+
+
+CPU_SAMPLES = 8  # most timed CPU samples per reference run (a decoder-layer sample takes about a second)
 
 
 def run_reference(a, rank):
-    """The reference arm: the CPU path on the host cores, one warm-up sample and up to CPU_SAMPLES
-    timed samples (each one sampled layer, extrapolated), so the run ends within a few minutes."""
+    """The reference arm: the CPU path on every host core, ``--warmup`` (at most 2) untimed samples, then
+    ``--steps`` (at most CPU_SAMPLES) timed samples; each sample is one bounded piece of a step (a
+    decoder layer, an MoE layer, a batch of experts), and ``value`` is the tokens/s those samples imply
+    for whole steps.  ``steps`` and ``ms_per_step`` report the samples actually timed."""
     if rank != 0:
         return
-    vals = []
-    threads, sample = os.cpu_count() or 1, ""
-    nt = min(a.steps, CPU_SAMPLES)
-    for i in range(1 + nt):
-        v, threads, sample = cpu_tok_s(a, seed=i)
-        if i >= 1:
-            vals.append(v)
-    sample += f"; mean of {nt} timed samples after 1 warm-up"
-    tok_s = statistics.mean(vals)
+    warm = max(1, min(a.warmup, 2))
+    nt = max(1, min(a.steps, CPU_SAMPLES))
+    for i in range(warm):
+        cpu_sample(a, seed=i)
+    t0 = time.perf_counter()
+    got = [cpu_sample(a, seed=warm + i) for i in range(nt)]
+    wall = time.perf_counter() - t0
+    tok_s = statistics.mean(g[1] for g in got)
+    threads, sample = got[0][2], got[0][3] + f"; mean of {nt} timed samples after {warm} untimed"
     line = {
         "impl": "reference",
         "metric": metric_name(a),
         "value": tok_s,
         "unit": "tok/s",
         "n_gpus": a.gpus,
-        "steps": a.steps,
-        "warmup": a.warmup,
-        "ms_per_step": 1e3 / tok_s,
+        "steps": nt,
+        "warmup": warm,
+        "ms_per_step": 1e3 * statistics.mean(g[0] for g in got),
+        "step_is_sample": True,
+        "timed_s": wall,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -715,8 +748,8 @@ class GptOssStack:
 # decoder workload
 # ------------------------------------------------------------------------------------------------
 class DecodeBench:
-    """Greedy bs=1 decode: the whole-token graph (GraphDecoder.greedy_graph) with every expert
-    resident, or the segmented paged decoder (PagedGraphDecoder) with a capped expert cache."""
+    """Greedy or teacher-forced bs=1 decode: the whole-token graph (GraphDecoder / DevicePagedDecoder)
+    or the segmented paged decoder (PagedGraphDecoder, the reference's per-layer host decision)."""
 
     def __init__(self, a, device, seed):
         import torch
@@ -725,10 +758,13 @@ class DecodeBench:
         from wisp.model import DecoderConfig, DecoderWeights
 
         cfg = DecoderConfig(layers=L, bits=a.bits)
+        self.a = a
         self.w = DecoderWeights.random(cfg, device=device, seed=seed)
-        need = a.prompt + 2 * (a.warmup + a.steps) + 16
+        n_steps = a.warmup + 2 * a.steps + 3 + TIMELINE_TOKENS
+        need = a.prompt + n_steps + 16
         self.paged = a.cache_frac < 1.0
         self.device_paged = self.paged and a.paging == "device"
+        self.forced = a.tokens == "forced"
         if self.paged:
             from wisp.cache import ExpertCache
             from wisp.store import ExpertStore
@@ -738,29 +774,43 @@ class DecodeBench:
             torch.cuda.empty_cache()
             self.cache = ExpertCache(store, nslots=int(a.cache_frac * L * E), device=device)
             if self.device_paged:
-                self.dec = DevicePagedDecoder(self.w, self.cache, tmax=need)
+                self.dec = DevicePagedDecoder(self.w, self.cache, tmax=need, admit=a.admit)
             else:
                 self.dec = PagedGraphDecoder(self.w, self.cache, tmax=need, prefetch=not a.no_prefetch)
         else:
             self.dec = GraphDecoder(self.w, tmax=need)
         g = torch.Generator(device=device).manual_seed(seed)
         self.prompt = torch.randint(0, cfg.vocab, (a.prompt,), device=device, generator=g)
+        # the token stream of the forced steps (seeded random ids, like a prompt being read)
+        self.stream = torch.randint(0, cfg.vocab, (n_steps,), device=device, generator=g)
+        self.stream_host = self.stream.cpu().pin_memory()
+        self.i = 0
+        t0 = time.perf_counter()
         self.dec.prefill(self.prompt)
+        torch.cuda.synchronize()
+        self.prefill_s = time.perf_counter() - t0
         self.tok = self.dec.logits.argmax().reshape(1)
         self.dec.ctl[0:1].copy_(self.tok)
         self.dec.ctl[1].fill_(self.dec.pos)
+        if self.dec.graph is None:
+            self.dec.capture()
         if self.paged:
-            self.stats0 = dict(self.cache.stats), self.cache.bytes_h2d
+            self.stats0 = dict(self.cache.stats), self.cache.bytes_h2d, self.cache.n_loads
         if self.device_paged:
             self.reads0 = self.dec.host_reads_total()
+        self.tokens0 = self.dec.pos
 
     def launches_per_step(self):
-        return self.dec.kernels_per_step()  # embed; per layer 3 GEMVs, attention, top-k, MoE x2; lm_head; argmax x2
+        return self.dec.kernels_per_step()  # embed; per layer 3 GEMVs, attention, MoE x2; lm_head; argmax x2
 
     def step(self, t):
-        """One generated token: the step graph plus the on-device token/position update (paged: the
-        L + 1 segments with the host's paging decisions between them)."""
-        if self.device_paged:
+        """One decoded token: the step graph (teacher-forced: this step's token from the device stream;
+        greedy: the previous step's choice, advanced inside the graph); paged decoders add their host
+        work (the policy one token behind, or the L + 1 segments with per-layer decisions)."""
+        if self.forced:
+            self.dec.next(self.stream[self.i : self.i + 1])
+            self.i += 1
+        elif self.device_paged:
             self.dec.step_greedy()
         elif self.paged:
             self.dec.next(self.dec.next_token)
@@ -770,21 +820,32 @@ class DecodeBench:
     def e2e_inputs(self):
         import torch
 
-        return torch.zeros(1, dtype=torch.int64).pin_memory(), torch.zeros(1, dtype=torch.int64).pin_memory()
+        return self.stream_host, torch.zeros(1, dtype=torch.int64).pin_memory()
 
     def step_e2e(self, t, inp):
-        """Public-API step from host buffers: the token H2D, one decode step (which also advances the
-        position), the next token D2H."""
+        """Public-API step from host buffers: the token H2D, one decode step, the chosen next token D2H."""
         tok_host, out_host = inp
-        if self.device_paged:
-            self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
-            self.dec.step_greedy()
+        d = self.dec
+        if self.forced:
+            if self.paged and not self.device_paged:
+                d.next(tok_host[self.i : self.i + 1].to(d.dev, non_blocking=True))
+            else:
+                d.ctl[0:1].copy_(tok_host[self.i : self.i + 1], non_blocking=True)
+                d.ctl[1].fill_(d.pos)
+                d.graph.replay()
+                d.pos += 1
+                if d.pager is not None:
+                    d._after_replay()
+            self.i += 1
+        elif self.device_paged:
+            d.ctl[0:1].copy_(tok_host[0:1], non_blocking=True)
+            d.step_greedy()
         elif self.paged:
-            self.dec.next(tok_host.to(self.dec.dev, non_blocking=True))
+            d.next(tok_host[0:1].to(d.dev, non_blocking=True))
         else:
-            self.dec.ctl[0:1].copy_(tok_host, non_blocking=True)
-            self.dec.greedy_graph.replay()
-        out_host.copy_(self.dec.next_token, non_blocking=True)
+            d.ctl[0:1].copy_(tok_host[0:1], non_blocking=True)
+            d.greedy_graph.replay()
+        out_host.copy_(d.next_token, non_blocking=True)
 
     def e2e_bytes(self):
         return 8, 8
@@ -792,21 +853,84 @@ class DecodeBench:
     def pool(self):
         return (self.cache.gpu if self.paged else self.w.pool), self.w.nbytes
 
-    def paging_stats(self, tokens):
+    def paging_stats(self, value_tok_s):
+        """Hit rate and PCIe traffic per token over the decode steps so far, the measured pinned H2D
+        bandwidth and the PCIe floor it sets (bytes that must cross PCIe per token / H2D GB/s)."""
         if not self.paged:
             return None
-        st0, b0 = self.stats0
+        tokens = self.dec.pos - self.tokens0
+        st0, b0, n0 = self.stats0
         st = self.cache.stats
         hits, misses = st["hits"] - st0["hits"], st["misses"] - st0["misses"]
+        nb = self.w.nbytes
+        page_ins = (self.cache.n_loads - n0) / tokens
         out = {
             "slots": self.cache.nslots,
+            "tokens": tokens,
             "hit_rate": hits / max(1, hits + misses),
+            "misses_per_token": misses / tokens,
+            "page_ins_per_token": page_ins,
             "h2d_mb_per_token": (self.cache.bytes_h2d - b0) / tokens / 1e6,
             "mode": "device slot table" if self.device_paged else "per-layer host decision",
+            "admit": self.a.admit if self.device_paged else "all",
+            "token_stream": self.a.tokens,
         }
+        pcie_bytes = (self.cache.bytes_h2d - b0) / tokens
         if self.device_paged:
-            out["host_store_expert_reads_per_token"] = (self.dec.host_reads_total() - self.reads0) / tokens
+            reads = (self.dec.host_reads_total() - self.reads0) / tokens
+            out["host_store_expert_reads_per_token"] = reads
+            out["host_read_mb_per_token"] = reads * nb / 1e6
+            pcie_bytes += reads * nb
+        gbs = measure_h2d_gbs()
+        out["pcie_mb_per_token"] = pcie_bytes / 1e6
+        out["pinned_h2d_gbs"] = gbs
+        out["pcie_floor_tok_s"] = gbs * 1e9 / pcie_bytes if pcie_bytes > 0 else None
+        out["frac_of_pcie_floor"] = value_tok_s / out["pcie_floor_tok_s"] if out["pcie_floor_tok_s"] else None
         return out
+
+    def timeline(self, tokens=None):
+        """CUDA-event timeline of ``tokens`` more forced decode steps (untimed): per step the compute
+        stream's interval, per page-in batch the copy stream's; returns how much of the copy time ran
+        while a step was computing."""
+        import torch
+
+        if not self.device_paged or not self.forced:
+            return None
+        tokens = tokens or TIMELINE_TOKENS
+        cache = self.cache
+        cache.timeline = []
+        st = torch.cuda.current_stream()
+        base = torch.cuda.Event(enable_timing=True)
+        base.record(st)
+        steps = []
+        for _ in range(tokens):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            self.step(0)
+            e1.record(st)
+            steps.append((e0, e1))
+        self.dec.flush()
+        torch.cuda.synchronize()
+        comp = [(base.elapsed_time(a), base.elapsed_time(b)) for a, b in steps]
+        copies = [(base.elapsed_time(a), base.elapsed_time(b), nbytes) for a, b, nbytes in cache.timeline]
+        cache.timeline = None
+        copy_ms = sum(b - a for a, b, _ in copies)
+        overl = 0.0
+        for a, b, _ in copies:
+            for c, d in comp:
+                overl += max(0.0, min(b, d) - max(a, c))
+        return {
+            "tokens": tokens,
+            "span_ms": comp[-1][1] - comp[0][0],
+            "compute_ms": sum(d - c for c, d in comp),
+            "page_in_batches": len(copies),
+            "page_in_mb": sum(n for _, _, n in copies) / 1e6,
+            "copy_ms": copy_ms,
+            "copy_gbs": sum(n for _, _, n in copies) / (copy_ms * 1e-3) / 1e9 if copy_ms > 0 else None,
+            "copy_overlapped_frac": overl / copy_ms if copy_ms > 0 else None,
+            "steps_ms": [round(d - c, 3) for c, d in comp],
+            "copies_ms": [(round(a, 3), round(b, 3)) for a, b, _ in copies],
+        }
 
     def release(self):
         self.dec.graph = self.dec.greedy_graph = None
@@ -819,6 +943,23 @@ class DecodeBench:
         router = cfg.experts * cfg.hidden * 2
         kv = 2 * cfg.kv_heads * ctx * cfg.head_dim * 2
         return L * (attn + router + K_TOP * self.w.nbytes + kv) + cfg.vocab * cfg.hidden * 2 + cfg.hidden * 2
+
+
+def measure_h2d_gbs(mb=256, reps=5):
+    """Pinned host -> device copy bandwidth (cudaMemcpyAsync of ``mb`` MB, best of ``reps``, CUDA events)."""
+    import torch
+
+    src = torch.empty(mb << 20, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(mb << 20, dtype=torch.uint8, device="cuda")
+    best = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(src, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        best = max(best, src.numel() / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+    return best
 
 
 # ------------------------------------------------------------------------------------------------
@@ -999,7 +1140,13 @@ def main():
     ms_e2e = e2.elapsed_time(e3)
     clk = clocks.stop()
     if a.workload == "decoder" and bench.paged:
-        paging = bench.paging_stats(a.warmup + 2 * a.steps + 3)
+        paging = bench.paging_stats(a.steps / (ms * 1e-3))
+        tl = bench.timeline()
+        if tl is not None:
+            paging["timeline"] = {k: v for k, v in tl.items() if k not in ("steps_ms", "copies_ms")}
+            if os.environ.get("WISP_TIMELINE_OUT"):
+                with open(os.environ["WISP_TIMELINE_OUT"], "w") as f:
+                    json.dump(tl, f)
     if a.workload in ("gptoss-moe", "moe-ep"):
         peak, src = load_peaks()
         src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
@@ -1038,6 +1185,8 @@ def main():
             "gpu_launches": bench.launches_per_step() * a.steps,
             "clocks": clk,
         }
+        if a.workload == "decoder":
+            line["prefill_s"] = bench.prefill_s
         if a.workload == "decoder" and bench.paged:
             line["paging"] = paging
         if a.workload == "gptoss-moe":

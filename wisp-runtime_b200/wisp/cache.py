@@ -53,6 +53,7 @@ class ExpertCache:
         self.n_loads = 0
         self.n_copies = 0  # cudaMemcpyAsync calls issued (runs of rows)
         self._table = None
+        self.timeline = None  # a list: (start event, end event, bytes) of every page-in batch on the copy stream
         if n_static:
             assert preload_keys is not None and len(preload_keys) <= n_static
             self._issue(self.core.preload(list(preload_keys)))
@@ -82,6 +83,9 @@ class ExpertCache:
         host = self.store.host
         with torch.cuda.stream(self.copy_stream):
             self.copy_stream.wait_event(after)
+            if self.timeline is not None:
+                t0 = torch.cuda.Event(enable_timing=True)
+                t0.record(self.copy_stream)
             if not self.decode_on_load:
                 for k0, s0, n in self._runs(pairs):
                     self.gpu[s0 : s0 + n].copy_(host[k0 : k0 + n], non_blocking=True)
@@ -92,8 +96,10 @@ class ExpertCache:
                 keys = torch.tensor([k for k, _ in pairs], dtype=torch.int64).pin_memory()
                 slots = torch.tensor([s for _, s in pairs], dtype=torch.int32).pin_memory()
                 self._table.index_copy_(0, keys.to(self.device, non_blocking=True), slots.to(self.device, non_blocking=True))
-            done = torch.cuda.Event()
+            done = torch.cuda.Event(enable_timing=self.timeline is not None)
             done.record(self.copy_stream)
+        if self.timeline is not None:
+            self.timeline.append((t0, done, len(pairs) * self.store.nbytes))
         self.evt = done
         self.bytes_h2d += len(pairs) * self.store.nbytes
         self.n_loads += len(pairs)
