@@ -36,6 +36,7 @@ extern "C" {
 #define WISP_STATUS_BAD_POS 0x2u     /* a position outside the KV capacity was skipped */
 #define WISP_STATUS_WAIT_TIMEOUT 0x4u /* a bounded device-side wait gave up */
 #define WISP_STATUS_BAD_ROUTE 0x8u   /* a routing entry (expert id / token index) was out of range */
+#define WISP_STATUS_RANGE 0x10u      /* a value outside the fp16 range met an fp16 operand and was saturated */
 
 #define WISP_DTYPE_F32 0
 #define WISP_DTYPE_BF16 1
@@ -148,6 +149,19 @@ int64_t wisp_moe_batched_workspace_bytes(int N, int k, int64_t H, int64_t I);
 int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
                      int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
                      void* stream);
+
+/* wisp_moe_batched with an explicit path: 0 = automatic (what wisp_moe_batched does), 1 = the warp-level
+ * tensor-core kernels (mma.sync; any supported format), 2 = the 5th-generation tensor cores: per
+ * (expert, 128 weight rows, up to 128 tokens) one CTA streams the packed codes through TMA tensor
+ * loads, dequantizes them once into fp16 (q*s + m with a single rounding) in the 128-byte-swizzled
+ * K-major layout, and one thread issues tcgen05.mma (M = 128, N = the expert's tokens, fp32
+ * accumulators in TMEM) for gate and up, then down; the activations and the intermediate enter as
+ * fp16 (values outside fp16's range saturate and set WISP_STATUS_RANGE).  Path 2 needs 4-bit or
+ * 2-bit codes and groups a multiple of 128 dividing H and I (WISP_ERR_UNSUPPORTED otherwise).
+ * Automatic = 2 when it applies, else 1.  Same replacement as wisp_moe_batched (wisp/moe.py:62-137). */
+int wisp_moe_batched_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
+                             int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
+                             int variant, void* stream);
 
 /* ---- expert parallelism (batched decode over ranks) ------------------------------------------------ */
 /* Pack for the dispatch all-to-all: pair p = t*k + j of this rank's N tokens (sel: int64 [N, k] global

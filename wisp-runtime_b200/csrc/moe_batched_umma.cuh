@@ -1,0 +1,530 @@
+// Batched MoE expert products on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for
+// 4-bit and 2-bit codes with quantization groups of a multiple of 128 (the reference's bs > 1 branch,
+// wisp/moe.py:62-137: unique experts, dequant, per-expert MLP, weighted index_add).
+//
+// Work item = (group of pairs routed to one slot, N tile of up to NMAX of its tokens, tile of BM = 128
+// weight rows).  Per item the whole K range streams through shared memory in BK = 64 slices:
+//
+//   warp 0      producer: TMA tensor loads of the slice's packed codes (one 128-row box per matrix),
+//               of the tokens' activation rows (fp16, 128-byte swizzled boxes of 32 rows), and per item
+//               one bulk copy of the tile's scales and mins
+//   warps 2-9   dequantize the codes into the MMA's A operand: per 8 codes one LOP3 builds fp16 pairs
+//               1024 + q, one HSUB2 makes q exact, one HFMA2 applies scale and min (a single rounding of
+//               q*s + m to fp16: closer to the exact weight than the reference's bf16(q*s + m)); the
+//               tile is written in the K-major 128-byte-swizzled layout the tensor core reads
+//   warp 1      one thread issues tcgen05.mma (kind::f16, M = 128, N = the item's tokens rounded up to
+//               32, K = 16 per instruction) for gate and up (or down) into TMEM, and commits each
+//               stage back to the producer and the dequantizers
+//   warps 2-9   epilogue: tcgen05.ld of the accumulators; gate/up -> a = silu(g)*u as fp16 rows of the
+//               intermediate (pair-permuted, the down pass's activation operand); down -> fp32 rows of
+//               y that the combine kernel sums per token in a fixed order
+//
+// Each code word is read from HBM once per item, however many tokens the expert received (up to
+// NMAX per N tile), and it is unpacked once.  Inside a code word the MMA's K order is the pair order
+// (codes i and i + W/2 of a W-code word sit side by side); the activations are staged in the same
+// order, so the products are the plain dot products.
+//
+// No TMA multicast, no clusters: the kernels run on one GPU's own memory.  Every wait on an
+// mbarrier is bounded; a wait that gives up flags WISP_STATUS_WAIT_TIMEOUT and makes every role
+// leave its loop, the producer waits for its copies in flight, the MMA thread for its MMAs, and the
+// TMEM is released before the CTA exits.
+#pragma once
+#include "common.cuh"
+#include "moe_batched.cuh"
+#include "moe_decode.cuh"
+#include "tma.cuh"
+
+namespace wisp {
+namespace umma {
+
+constexpr int BM = 128;       // weight rows per tile (MMA M)
+constexpr int BK = 64;        // K per stage: 64 fp16 = one 128-byte swizzle row
+constexpr int NMAX = 128;     // tokens per N tile (MMA N <= 128)
+constexpr int BOXR = 32;      // token rows per activation box; MMA N is a multiple of it
+constexpr int CST = 4;        // code stages
+constexpr int AST = 2;        // dequantized A stages
+constexpr int BST = 3;        // activation stages
+constexpr int DQ_WARPS = 8;   // dequantizing / epilogue warps (warps 2..9)
+constexpr int THREADS = (2 + DQ_WARPS) * 32;
+constexpr uint32_t TMEM_COLS = 256;  // gate at column 0, up at column NMAX
+
+template <int BITS, int MAT>
+struct Cfg {
+  static constexpr int NMAT = MAT == 0 ? 2 : 1;
+  static constexpr int CODE_ROW = BK * BITS / 8;            // code bytes of one row per stage
+  static constexpr int CODE_MAT = BM * CODE_ROW;
+  static constexpr int CODE_STAGE = NMAT * CODE_MAT;
+  static constexpr int A_MAT = BM * BK * 2;                 // 16 KB
+  static constexpr int A_STAGE = NMAT * A_MAT;
+  static constexpr int B_STAGE = NMAX * BK * 2;             // 16 KB
+  static constexpr int OFF_A = 0;                           // 1024-aligned pieces first
+  static constexpr int OFF_B = OFF_A + AST * A_STAGE;
+  static constexpr int OFF_C = OFF_B + BST * B_STAGE;
+  static constexpr int OFF_S = OFF_C + CST * CODE_STAGE;    // scales/mins: 2 item buffers
+  static __host__ __device__ constexpr int scale_bytes(int gpr) { return NMAT * 2 * BM * gpr * 2; }
+};
+
+template <int BITS, int MAT>
+__host__ __device__ inline int64_t smem_bytes(int gpr) {
+  using C = Cfg<BITS, MAT>;
+  const int64_t sc = (C::scale_bytes(gpr) + 127) / 128 * 128;
+  // + barriers (2 CST + 2 AST + 2 BST + 4 + 3) * 8, the TMEM address, the abort flag, 1 KB alignment slack
+  return C::OFF_S + 2 * sc + 256 + 1024;
+}
+
+// ---- tcgen05 / TMA wrappers --------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, fp16 inputs, fp32 accumulation
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 16 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// shared-memory matrix descriptor: K-major operand in the 128-byte swizzled canonical layout (rows of
+// 128 bytes, 8-row atoms of 1 KB stacked at a stride of 1 KB), Blackwell descriptor version 1
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+// instruction descriptor of kind::f16: fp32 accumulator, fp16 A and B, both K-major, M = 128, N = n
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+// bounded wait by a whole warp (every lane polls, the answer is the same on every lane); it also gives
+// up as soon as another role raised the CTA's abort flag
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  for (unsigned it = 0; it < WAIT_LIMIT; ++it) {
+    if (__all_sync(0xFFFFFFFFu, mbar_try_wait(bar, parity))) return true;
+    if ((it & 127) == 127 && __any_sync(0xFFFFFFFFu, *abort != 0)) return false;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    flag(WISP_STATUS_WAIT_TIMEOUT);
+    *abort = 1;
+  }
+  __syncwarp();
+  return false;
+}
+
+// fp16 pair of codes (i, i + W/2) of word w: 1024 + q each, then q exact
+template <int BITS>
+__device__ __forceinline__ uint32_t q_pair(uint32_t w, int i) {
+  constexpr uint32_t mask = BITS == 4 ? 0x000F000Fu : 0x00030003u;
+  uint32_t h;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(h) : "r"(w >> (BITS * i)), "r"(mask), "r"(0x64006400u));  // (a & b) | c
+  const __half2 q = __hsub2(*reinterpret_cast<__half2*>(&h), __half2(__float2half_rn(1024.0f), __float2half_rn(1024.0f)));
+  return *reinterpret_cast<const uint32_t*>(&q);
+}
+__device__ __forceinline__ uint32_t deq2(uint32_t q, __half2 s, __half2 m) {
+  const __half2 v = __hfma2(*reinterpret_cast<__half2*>(&q), s, m);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+struct Item {
+  int grp, nt, rt;
+};
+
+__device__ __forceinline__ Item item_of(int i, int rtiles, int maxnt) {
+  Item it;
+  it.rt = i % rtiles;
+  const int j = i / rtiles;
+  it.nt = j % maxnt;
+  it.grp = j / maxnt;
+  return it;
+}
+
+// byte offset of 16-byte chunk `ch` of row r in a 128-row, 128-byte-row swizzled tile
+__device__ __forceinline__ uint32_t sw128_off(int r, int ch) { return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4)); }
+
+// ---- activation staging: the tokens' rows in group order, fp16, pair-permuted ---------------------------
+// xh[p] = x[order[p] / k] for every sorted position p; inside each code word's span of W = 32/BITS
+// elements, element i goes to 2i (i < W/2) or 2(i - W/2) + 1.  bf16 -> fp16 is exact inside fp16's range.
+template <int BITS>
+__global__ void stage_rows_kernel(const uint16_t* __restrict__ x, int P, int k, int64_t H, batched::Ws W, uint16_t* __restrict__ xh) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t per = H / 16;  // 16 elements (two code words at 4 bit, one at 2 bit) per item
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(P) * per; i += int64_t(gridDim.x) * blockDim.x) {
+    const int p = int(i / per);
+    const int64_t q = i - int64_t(p) * per;
+    const int t = W.order[p] / k;
+    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(t) * H + 16 * q);
+    const uint4 a = src[0], b = src[1];
+    const uint32_t in[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[2 * j] = __uint_as_float(in[j] << 16);
+      v[2 * j + 1] = __uint_as_float(in[j] & 0xFFFF0000u);
+    }
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // output positions 2j, 2j+1 hold elements (e0, e1) of the word span
+      int e0, e1;
+      if (BITS == 4) {
+        const int w = j >> 2, i2 = j & 3;  // word w covers elements 8w..8w+7
+        e0 = 8 * w + i2;
+        e1 = 8 * w + i2 + 4;
+      } else {
+        e0 = j;
+        e1 = j + 8;
+      }
+      const __half2 h = __floats2half2_rn(v[e0], v[e1]);
+      o[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(xh + int64_t(p) * H + 16 * q);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// ---- the tensor-core grouped GEMM ------------------------------------------------------------------------
+// MAT 0: gate/up rows [I] of every item's expert against the staged token rows (mapB over xh [P][H]),
+//        a = silu(gate) * up -> ah [P][I] fp16, pair-permuted
+// MAT 2: down rows [H] against ah (mapB over ah [P][I]) -> y [P][H] fp32
+// mapC: 3-D map (code bytes of a row, rows, slots) of the codes of gate+up (2I rows) or down (H rows)
+template <int BITS, int MAT>
+__global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_constant__ CUtensorMap mapC,
+                                                                  const __grid_constant__ CUtensorMap mapB,
+                                                                  const uint8_t* __restrict__ pool, MoeShape S, batched::Ws W,
+                                                                  uint16_t* __restrict__ ah) {
+  using C = Cfg<BITS, MAT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int K = MAT == 0 ? S.H : S.I;
+  const int rows = MAT == 0 ? S.I : S.H;
+  const int KT = K / BK;
+  const int gpr = K / S.group;                      // quantization groups per row
+  const int sc_bytes = (C::scale_bytes(gpr) + 127) / 128 * 128;
+  uint8_t* sA = smem + C::OFF_A;
+  uint8_t* sB = smem + C::OFF_B;
+  uint8_t* sC = smem + C::OFF_C;
+  uint8_t* sS = smem + C::OFF_S;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sS + 2 * sc_bytes);
+  uint64_t* code_full = bars;
+  uint64_t* code_empty = code_full + CST;
+  uint64_t* a_full = code_empty + CST;
+  uint64_t* a_empty = a_full + AST;
+  uint64_t* b_full = a_empty + AST;
+  uint64_t* b_empty = b_full + BST;
+  uint64_t* sc_full = b_empty + BST;    // [2]
+  uint64_t* sc_empty = sc_full + 2;     // [2]
+  uint64_t* acc_full = sc_empty + 2;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ int s_maxcnt;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < CST; ++i) {
+      mbar_init(code_full + i, 1);
+      mbar_init(code_empty + i, DQ_WARPS);
+    }
+    for (int i = 0; i < AST; ++i) {
+      mbar_init(a_full + i, DQ_WARPS);
+      mbar_init(a_empty + i, 1);
+    }
+    for (int i = 0; i < BST; ++i) {
+      mbar_init(b_full + i, 1);
+      mbar_init(b_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(sc_full + i, 1);
+      mbar_init(sc_empty + i, DQ_WARPS);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, DQ_WARPS);
+    mbar_init(mma_done, 1);
+    *abort = 0;
+    s_maxcnt = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {  // TMEM for the accumulators (the whole warp allocates)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  pdl_wait();  // the grouping (and, for MAT 2, the gate/up pass) has finished
+  pdl_launch_dependents();
+  const int ngr = W.n_groups[0];
+  __syncthreads();
+  for (int g = threadIdx.x; g < ngr; g += blockDim.x) atomicMax(&s_maxcnt, W.grp_count[g]);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int maxnt = (s_maxcnt + NMAX - 1) / NMAX;
+  const int rtiles = rows / BM;
+  const int nitems = ngr * maxnt * rtiles;
+
+  if (warp == 0) {
+    // ================= producer (the whole warp loops, lane 0 issues) =================
+    uint32_t cs = 0, cph = 0, bs = 0, bph = 0, ss = 0, sph = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+      const Item it = item_of(i, rtiles, maxnt);
+      const int cnt = W.grp_count[it.grp];
+      if (it.nt * NMAX >= cnt) continue;
+      const int slot = W.grp_slot[it.grp];
+      const int row0 = W.grp_start[it.grp] + it.nt * NMAX;
+      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
+      const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
+      const int r0 = it.rt * BM;
+      // scales and mins of the tile's rows: one contiguous run per (matrix, kind)
+      ok = warp_wait(sc_empty + ss, sph ^ 1, abort);
+      if (!ok) break;
+      if (lane == 0) {
+        const uint32_t run = uint32_t(BM * gpr * 2);
+        mbar_expect_tx(sc_full + ss, run * 2 * C::NMAT);
+        const uint8_t* base = pool + int64_t(slot) * S.nbytes;
+#pragma unroll
+        for (int m = 0; m < C::NMAT; ++m) {
+          const int mat = MAT == 0 ? m : 2;
+          const int64_t gi0 = (int64_t(mat) * S.H * S.I + int64_t(r0) * K) / S.group;
+          bulk_g2s(sS + ss * sc_bytes + (2 * m) * run, base + S.ncode + 2 * gi0, run, sc_full + ss);
+          bulk_g2s(sS + ss * sc_bytes + (2 * m + 1) * run, base + S.ncode + 2 * (S.ng + gi0), run, sc_full + ss);
+        }
+      }
+      __syncwarp();
+      ss ^= 1;
+      if (ss == 0) sph ^= 1;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        ok = warp_wait(code_empty + cs, cph ^ 1, abort);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_expect_tx(code_full + cs, C::CODE_STAGE);
+          tma_load_3d(sC + cs * C::CODE_STAGE, &mapC, kt * C::CODE_ROW, r0, slot, code_full + cs);
+          if (MAT == 0) tma_load_3d(sC + cs * C::CODE_STAGE + C::CODE_MAT, &mapC, kt * C::CODE_ROW, S.I + r0, slot, code_full + cs);
+        }
+        __syncwarp();
+        if (++cs == CST) cs = 0, cph ^= 1;
+        ok = warp_wait(b_empty + bs, bph ^ 1, abort);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_expect_tx(b_full + bs, uint32_t(NT * BK * 2));
+          for (int j = 0; j < NT / BOXR; ++j)
+            tma_load_2d(sB + bs * C::B_STAGE + j * BOXR * BK * 2, &mapB, kt * BK, row0 + j * BOXR, b_full + bs);
+        }
+        __syncwarp();
+        if (++bs == BST) bs = 0, bph ^= 1;
+      }
+    }
+    // copies still in flight land before the CTA can exit: wait for the last arming of every stage
+    // (bounded, ignoring the abort flag; a phase that already completed passes at once)
+    if (lane == 0) {
+      for (int j = 0; j < CST; ++j) {
+        cs = cs == 0 ? CST - 1 : cs - 1;
+        if (cs == CST - 1) cph ^= 1;
+        mbar_wait(code_full + cs, cph);
+      }
+      for (int j = 0; j < BST; ++j) {
+        bs = bs == 0 ? BST - 1 : bs - 1;
+        if (bs == BST - 1) bph ^= 1;
+        mbar_wait(b_full + bs, bph);
+      }
+      for (int j = 0; j < 2; ++j) {
+        ss ^= 1;
+        if (ss == 1) sph ^= 1;
+        mbar_wait(sc_full + ss, sph);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ================= MMA issuer (the whole warp loops, lane 0 issues) =================
+    uint32_t as = 0, aph = 0, bs = 0, bph = 0, eph = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+      const Item it = item_of(i, rtiles, maxnt);
+      const int cnt = W.grp_count[it.grp];
+      if (it.nt * NMAX >= cnt) continue;
+      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
+      const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
+      const uint32_t idesc = idesc_f16(NT);
+      ok = warp_wait(acc_empty, eph ^ 1, abort);  // the epilogue has read the previous item's accumulators
+      if (!ok) break;
+      eph ^= 1;
+      for (int kt = 0; kt < KT; ++kt) {
+        ok = warp_wait(a_full + as, aph, abort) && warp_wait(b_full + bs, bph, abort);
+        if (!ok) break;
+        if (lane == 0) {
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + as * C::A_STAGE), b0 = smem_u32(sB + bs * C::B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t bd = sdesc_sw128(b0 + kk * 32);
+            const uint32_t acc = (kt | kk) != 0;
+            tc_mma(tmem, sdesc_sw128(a0 + kk * 32), bd, idesc, acc);
+            if (MAT == 0) tc_mma(tmem + NMAX, sdesc_sw128(a0 + C::A_MAT + kk * 32), bd, idesc, acc);
+          }
+          tc_commit(a_empty + as);  // arrives once these MMAs have read the stage
+          tc_commit(b_empty + bs);
+        }
+        __syncwarp();
+        if (++as == AST) as = 0, aph ^= 1;
+        if (++bs == BST) bs = 0, bph ^= 1;
+      }
+      if (ok && lane == 0) tc_commit(acc_full);
+      __syncwarp();
+    }
+    if (lane == 0) {
+      tc_commit(mma_done);  // every MMA issued so far has completed
+      mbar_wait(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ================= dequantize + epilogue =================
+    const int d = threadIdx.x - 64;      // 0..255
+    constexpr int WPR = BK * BITS / 32;  // code words per row per stage: 8 (4-bit), 4 (2-bit)
+    constexpr int RPT = BM * WPR / (DQ_WARPS * 32);  // rows per thread per matrix: 4 / 2
+    const int wc = d % WPR, rb = d / WPR;
+    constexpr int RSTEP = DQ_WARPS * 32 / WPR;  // 32 / 64
+    uint32_t cs = 0, cph = 0, as = 0, aph = 0, ss = 0, sph = 0, eph = 0;
+    const int q4 = warp & 3;                // TMEM lane quarter this warp may read
+    const int chalf = (warp - 2) >> 2;      // column half of the epilogue
+    bool ok = true;
+    for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+      const Item it = item_of(i, rtiles, maxnt);
+      const int cnt = W.grp_count[it.grp];
+      if (it.nt * NMAX >= cnt) continue;
+      const int row0 = W.grp_start[it.grp] + it.nt * NMAX;
+      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
+      const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
+      const int r0 = it.rt * BM;
+      ok = warp_wait(sc_full + ss, sph, abort);
+      if (!ok) break;
+      const __half* scl = reinterpret_cast<const __half*>(sS + ss * sc_bytes);
+      for (int kt = 0; kt < KT; ++kt) {
+        ok = warp_wait(code_full + cs, cph, abort) && warp_wait(a_empty + as, aph ^ 1, abort);
+        if (!ok) break;
+        const int gcol = kt * BK / S.group;  // the stage's quantization group within the row
+        const uint8_t* cst = sC + cs * C::CODE_STAGE;
+        uint8_t* ast = sA + as * C::A_STAGE;
+#pragma unroll
+        for (int m = 0; m < C::NMAT; ++m) {
+#pragma unroll
+          for (int j = 0; j < RPT; ++j) {
+            const int r = rb + RSTEP * j;
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(cst + m * C::CODE_MAT + r * C::CODE_ROW + 4 * wc);
+            const __half sv = scl[((2 * m) * BM + r) * gpr + gcol], mv = scl[((2 * m + 1) * BM + r) * gpr + gcol];
+            const __half2 s2 = __half2(sv, sv), m2 = __half2(mv, mv);
+            if (BITS == 4) {
+              uint4 o;
+              o.x = deq2(q_pair<4>(w, 0), s2, m2);
+              o.y = deq2(q_pair<4>(w, 1), s2, m2);
+              o.z = deq2(q_pair<4>(w, 2), s2, m2);
+              o.w = deq2(q_pair<4>(w, 3), s2, m2);
+              *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, wc)) = o;
+            } else {
+              uint4 o0, o1;
+              o0.x = deq2(q_pair<2>(w, 0), s2, m2);
+              o0.y = deq2(q_pair<2>(w, 1), s2, m2);
+              o0.z = deq2(q_pair<2>(w, 2), s2, m2);
+              o0.w = deq2(q_pair<2>(w, 3), s2, m2);
+              o1.x = deq2(q_pair<2>(w, 4), s2, m2);
+              o1.y = deq2(q_pair<2>(w, 5), s2, m2);
+              o1.z = deq2(q_pair<2>(w, 6), s2, m2);
+              o1.w = deq2(q_pair<2>(w, 7), s2, m2);
+              *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, 2 * wc)) = o0;
+              *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, 2 * wc + 1)) = o1;
+            }
+          }
+        }
+        fence_proxy_async();  // the generic-proxy stores become visible to the tensor core
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive1(a_full + as);
+          mbar_arrive1(code_empty + cs);
+        }
+        if (++cs == CST) cs = 0, cph ^= 1;
+        if (++as == AST) as = 0, aph ^= 1;
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive1(sc_empty + ss);
+      ss ^= 1;
+      if (ss == 0) sph ^= 1;
+      // ---- epilogue ----
+      ok = warp_wait(acc_full, eph, abort);
+      if (!ok) break;
+      eph ^= 1;
+      tc_fence_after();
+      const int r = r0 + 32 * q4 + lane;  // this thread's weight row (its TMEM lane)
+      const uint32_t lane_base = tmem + (uint32_t(32 * q4) << 16);
+      for (int c0 = 16 * chalf; c0 < NT; c0 += 32) {
+        uint32_t g[16];
+        tc_ld16(lane_base + c0, g);
+        if (MAT == 0) {
+          uint32_t u[16];
+          tc_ld16(lane_base + NMAX + c0, u);
+          tc_wait_ld();
+          const int pr = batched::perm_pos<BITS>(r);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (c0 + c < ntok) {
+              float a = silu_mul(__uint_as_float(g[c]), __uint_as_float(u[c]));
+              if (!(fabsf(a) <= 65504.0f)) {  // outside fp16 (or NaN): saturate and say so
+                flag(WISP_STATUS_RANGE);
+                a = a != a ? 0.0f : copysignf(65504.0f, a);
+              }
+              const __half h = __float2half_rn(a);
+              ah[int64_t(row0 + c0 + c) * S.I + pr] = *reinterpret_cast<const uint16_t*>(&h);
+            }
+          }
+        } else {
+          tc_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            if (c0 + c < ntok) W.y[int64_t(row0 + c0 + c) * S.H + r] = __uint_as_float(g[c]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive1(acc_empty);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+}  // namespace umma
+}  // namespace wisp

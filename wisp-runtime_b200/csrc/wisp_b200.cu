@@ -15,6 +15,7 @@
 #include "moe_decode_v4.cuh"
 #include "moe_decode_v5.cuh"
 #include "moe_batched.cuh"
+#include "moe_batched_umma.cuh"
 #include "moe_gptoss.cuh"
 #include "ep.cuh"
 #include "quant.cuh"
@@ -523,10 +524,86 @@ int64_t wisp_moe_batched_workspace_bytes(int N, int k, int64_t H, int64_t I) {
   return batched::ws_bytes(N * k, H, I);
 }
 
-int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
-                     int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
-                     void* stream) {
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library does not link libcuda)
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// the tensor-core (tcgen05) grouped GEMM: 4-bit or 2-bit codes, groups a multiple of 128 dividing the rows
+static bool umma_batched_ok(const MoeShape& S, int bits) {
+  return (bits == 4 || bits == 2) && S.group % 128 == 0 && S.H % 128 == 0 && S.I % 128 == 0 && S.H % S.group == 0 &&
+         S.I % S.group == 0 && S.nslots < (int64_t(1) << 31);
+}
+
+// 3-D map (code bytes of a row, rows, slots) over one matrix run of every slot, boxes of BK codes x 128 rows
+static bool umma_code_map(CUtensorMap* m, const uint8_t* base, int64_t nslots, int64_t nbytes, int64_t rowbytes, int64_t rows, int bits) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tmap_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {cuuint64_t(rowbytes), cuuint64_t(rows), cuuint64_t(nslots)};
+  cuuint64_t strides[2] = {cuuint64_t(rowbytes), cuuint64_t(nbytes)};
+  cuuint32_t box[3] = {cuuint32_t(umma::BK * bits / 8), cuuint32_t(umma::BM), 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D map over fp16 rows [P][K] (the staged tokens or the intermediate), 128-byte swizzled boxes of 64 x 32
+static bool umma_row_map(CUtensorMap* m, const uint16_t* base, int64_t K, int64_t P) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tmap_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(P)};
+  cuuint64_t strides[1] = {cuuint64_t(K * 2)};
+  cuuint32_t box[2] = {cuuint32_t(umma::BK), cuuint32_t(umma::BOXR)};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// staging, gate/up and down on the tensor cores (after the grouping); false if a tensor map cannot be encoded
+static int umma_batched_launch(const uint8_t* pool, const MoeShape& S, int bits, const uint16_t* x, int N, int k, batched::Ws W,
+                               cudaStream_t s, bool& launched) {
+  launched = false;
+  const int P = N * k;
+  CUtensorMap mc0, mc2, mb0, mb2;
+  if (!umma_code_map(&mc0, pool, S.nslots, S.nbytes, int64_t(S.H) * bits / 8, 2 * int64_t(S.I), bits) ||
+      !umma_code_map(&mc2, pool + 2 * S.mat_bytes, S.nslots, S.nbytes, int64_t(S.I) * bits / 8, S.H, bits) ||
+      !umma_row_map(&mb0, W.xp, S.H, P) || !umma_row_map(&mb2, W.a, S.I, P))
+    return WISP_OK;
+  const int grid = num_sms();
+  const int64_t items = int64_t(P) * (S.H / 16);
+  const int sgrid = int(items / 256 + 1 < int64_t(grid) * 8 ? items / 256 + 1 : int64_t(grid) * 8);
+  const size_t sm0 = size_t(bits == 4 ? umma::smem_bytes<4, 0>(S.H / S.group) : umma::smem_bytes<2, 0>(S.H / S.group));
+  const size_t sm2 = size_t(bits == 4 ? umma::smem_bytes<4, 2>(S.I / S.group) : umma::smem_bytes<2, 2>(S.I / S.group));
+  if (sm0 > 227 * 1024 || sm2 > 227 * 1024) return WISP_OK;
+  cudaError_t e = cudaSuccess;
+#define WISP_UMMA(B)                                                                                                   \
+  e = launch_pdl(umma::stage_rows_kernel<B>, sgrid, 256, 0, s, x, P, k, int64_t(S.H), W, W.xp);                          \
+  if (e == cudaSuccess) e = launch_pdl(umma::grouped_umma_kernel<B, 0>, grid, umma::THREADS, sm0, s, mc0, mb0, pool, S, W, W.a); \
+  if (e == cudaSuccess) e = launch_pdl(umma::grouped_umma_kernel<B, 2>, grid, umma::THREADS, sm2, s, mc2, mb2, pool, S, W, W.a);
+  if (bits == 4) {
+    WISP_UMMA(4)
+  } else {
+    WISP_UMMA(2)
+  }
+#undef WISP_UMMA
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched (tensor-core path): %s", cudaGetErrorString(e));
+  launched = true;
+  return WISP_OK;
+}
+
+int wisp_moe_batched_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
+                             int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
+                             int variant, void* stream) {
   WISP_REQUIRE(N >= 1 && k >= 1 && int64_t(N) * k <= batched::MAX_PAIRS, "wisp_moe_batched: need 1 <= N*k <= %d", batched::MAX_PAIRS);
+  WISP_REQUIRE(variant >= 0 && variant <= 2, "wisp_moe_batched_variant: variant must be 0, 1 or 2");
   MoeShape S;
   int rc = moe_shape(pool, nslots, nbytes, meta, k, x, H, I, bits, group, reinterpret_cast<const float*>(workspace), out, S);
   if (rc) return rc;
@@ -535,6 +612,8 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   WISP_REQUIRE(workspace_bytes >= batched::ws_bytes(N * k, H, I), "wisp_moe_batched: workspace of %lld bytes is too small (%lld needed)",
                (long long)workspace_bytes, (long long)batched::ws_bytes(N * k, H, I));
   WISP_REQUIRE(aligned(workspace, 256), "wisp_moe_batched: workspace must be 256-byte aligned");
+  if (variant == 2 && !umma_batched_ok(S, bits))
+    return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_batched: the tensor-core path needs 4-bit or 2-bit codes and groups a multiple of 128");
   batched::Ws W = batched::ws_carve(workspace, N * k, I);
   W.xp = batched::ws_xp(workspace, N * k, H, I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -544,10 +623,17 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
                       ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W)
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
+  bool done = false;
+  if (variant != 1 && umma_batched_ok(S, bits)) {
+    rc = umma_batched_launch(pool, S, bits, x, N, k, W, s, done);
+    if (rc) return rc;
+    if (!done && variant == 2) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_batched: tensor maps of the tensor-core path unavailable");
+  }
   // 4-bit and 2-bit codes with 128-multiple groups go straight into the MMA (two CTAs per SM, units
   // taken from a counter); 3-bit, 8-bit and finer groups dequantize to bf16 first
   const bool nib = (bits == 4 || bits == 2) && group % 128 == 0;
-  if (nib) {
+  if (done) {
+  } else if (nib) {
     const size_t sm_gu = size_t(batched::nib_stage_bytes(H)), sm_dn = size_t(batched::nib_stage_bytes(I));
     const int64_t nwords = int64_t(N) * H / (32 / bits);
     const int pgrid = int(nwords / 256 + 1 < int64_t(grid) * 4 ? nwords / 256 + 1 : int64_t(grid) * 4);
@@ -577,6 +663,12 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   if (e == cudaSuccess) e = launch_pdl(batched::combine_kernel, grid * 4, 256, 0, s, meta, N, k, H, W, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
   return check_launch("moe_batched");
+}
+
+int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
+                     int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
+                     void* stream) {
+  return wisp_moe_batched_variant(pool, nslots, nbytes, meta, N, k, x, H, I, bits, group, workspace, workspace_bytes, out, 0, stream);
 }
 
 // K splits of the gpt-oss GEMVs: enough (group, column tile, split) units for about four per warp of
@@ -620,19 +712,6 @@ static int gptoss_ws_splits(int P, int64_t H, int64_t I) {
   const int c = gptoss_splits(P, I);
   const int r = ns0 > ns1 ? ns0 : ns1;
   return c > r ? c : r;
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (the library does not link libcuda)
-static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
 }
 
 // the 3-D map (row words, rows, slots) of one gpt-oss matrix across the pool, boxes of one slab x 16 rows

@@ -14,7 +14,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("WISP_B200_LIB", os.path.join(os.path.dirname(_HERE), "lib", "libwisp_b200.so"))
 
 WISP_OK, WISP_ERR_INVALID, WISP_ERR_CUDA, WISP_ERR_UNSUPPORTED = 0, 1, 2, 3
-STATUS_BAD_SLOT, STATUS_BAD_POS, STATUS_WAIT_TIMEOUT, STATUS_BAD_ROUTE = 0x1, 0x2, 0x4, 0x8
+STATUS_BAD_SLOT, STATUS_BAD_POS, STATUS_WAIT_TIMEOUT, STATUS_BAD_ROUTE, STATUS_RANGE = 0x1, 0x2, 0x4, 0x8, 0x10
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 MOE_NOALLOC_MAX_SCRATCH = 65536  # WISP_MOE_NOALLOC_MAX_SCRATCH: fp32 values of k*I
 ARGMAX_WORKSPACE = 256  # WISP_ARGMAX_WORKSPACE: u64 entries
@@ -40,6 +40,7 @@ SIGNATURES = {
     "wisp_moe_decode_paged": (_I, [_P, _L, _L, _P, _I, _I, _I, _P, _L, _P, _L, _P, _P, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
     "wisp_moe_batched_workspace_bytes": (_L, [_I, _I, _L, _L]),
     "wisp_moe_batched": (_I, [_P, _L, _L, _P, _I, _I, _P, _L, _L, _I, _I, _P, _L, _P, _P]),
+    "wisp_moe_batched_variant": (_I, [_P, _L, _L, _P, _I, _I, _P, _L, _L, _I, _I, _P, _L, _P, _I, _P]),
     "wisp_moe_gptoss_workspace_bytes": (_L, [_I, _I, _L, _L]),
     "wisp_moe_gptoss": (_I, [_P, _L, _L, _P, _P, _I, _I, _P, _L, _L, _I, _I, _P, _P, _P, _L, _P, _P]),
     "wisp_ep_dispatch": (_I, [_P, _I, _L, _P, _I, _I, _I, _L, _L, _P, _P, _P, _P]),

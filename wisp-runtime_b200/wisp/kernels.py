@@ -187,8 +187,9 @@ def moe_batched_workspace(N, k, H, I, device):
     return torch.empty(nb, dtype=torch.uint8, device=device)
 
 
-def moe_batched(pool, meta, x, k, n, H, I, bits, group=128, out=None, workspace=None):
-    """MoE of N tokens (x bf16 [N, H], meta fp32 [N, 2k] = per token [slots | weights]) -> bf16 [N, H]."""
+def moe_batched(pool, meta, x, k, n, H, I, bits, group=128, out=None, workspace=None, variant=0):
+    """MoE of N tokens (x bf16 [N, H], meta fp32 [N, 2k] = per token [slots | weights]) -> bf16 [N, H].
+    ``variant``: 0 automatic, 1 warp-level tensor-core kernels, 2 tcgen05 (4/2-bit, groups of 128k)."""
     assert H % group == 0 and I % group == 0 and n == H * I
     _need_cuda(pool, meta, x)
     _bf16(x)
@@ -199,8 +200,8 @@ def moe_batched(pool, meta, x, k, n, H, I, bits, group=128, out=None, workspace=
     if out is None:
         out = torch.empty((N, H), dtype=torch.bfloat16, device=x.device)
     _lib.call(
-        "wisp_moe_batched", pool.data_ptr(), pool.shape[0], pool.shape[1], meta.data_ptr(), N, k, x.data_ptr(), H, I, bits,
-        group, workspace.data_ptr(), workspace.numel(), out.data_ptr(), _stream(x),
+        "wisp_moe_batched_variant", pool.data_ptr(), pool.shape[0], pool.shape[1], meta.data_ptr(), N, k, x.data_ptr(), H, I,
+        bits, group, workspace.data_ptr(), workspace.numel(), out.data_ptr(), int(variant), _stream(x),
     )
     return out
 
