@@ -190,3 +190,60 @@ def test_p2p_wait_runs_out_and_reports():
 
 def _stream0():
     return torch.cuda.current_stream(0).cuda_stream
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_emulated_ranks_kernel_path_matches_oracle(world):
+    """``world`` ranks emulated on one GPU, 32 tokens in total: each rank's pairs go through
+    wisp_ep_dispatch (its routing rows, capacity slots and src_pos bit-exact with dispatch_plan, the
+    rows equal to the token rows), the all-to-all is a permutation of the send buffers, each rank runs
+    the batched MoE on its own contiguous slice of the experts, the results travel back and
+    wisp_ep_combine sums them -- the whole against the oracle's batched MoE over all tokens."""
+    import numpy as np
+
+    from oracle import wisp_oracle as O
+    from wisp import _lib, kernels, quant
+    from wisp.ep import dispatch_plan
+
+    dev = torch.device("cuda", 0)
+    Hs, Is, Es, Ks, Ntot, bits, G = 256, 128, 16, 4, 32, 4, 128
+    n = Hs * Is
+    El, Nr = Es // world, Ntot // world
+    C = Nr * Ks
+    gen = torch.Generator(device="cuda").manual_seed(world)
+    pool = quant.quantize_batch((torch.randn(Es, 3, n, device=dev, generator=gen) * 0.05).to(torch.bfloat16), bits, G)
+    x = torch.randn(Ntot, Hs, device=dev, generator=gen).to(torch.bfloat16)
+    logits = torch.randn(Ntot, Es, device=dev, generator=gen)
+    sel_np, rw_np = O.router_topk(logits.to(torch.bfloat16).float().cpu().numpy(), Ks)
+    sel = torch.from_numpy(sel_np).to(dev).contiguous()
+    w = torch.from_numpy(rw_np).to(dev).float().contiguous()
+    _lib.device_status(0)
+    sends, metas, srcs = [], [], []
+    for r in range(world):
+        xr, sr = x[r * Nr : (r + 1) * Nr].contiguous(), sel[r * Nr : (r + 1) * Nr].contiguous()
+        sx = torch.zeros(world, C, Hs, dtype=torch.bfloat16, device=dev)
+        sm = torch.zeros(world, C, 2, dtype=torch.float32, device=dev)
+        sp = torch.zeros(Nr * Ks, dtype=torch.int32, device=dev)
+        kernels.ep_dispatch(xr, sr, El, world, C, 0, sx, sm, sp)
+        dest, cap, meta, src_pos = dispatch_plan(sr.cpu(), El, world, C, 0)
+        assert torch.equal(sm.cpu(), meta) and torch.equal(sp.cpu(), src_pos), r
+        assert torch.equal(sx[dest, cap].cpu(), xr.cpu()[torch.arange(Nr * Ks) // Ks]), r
+        sends.append(sx)
+        metas.append(sm)
+        srcs.append(sp)
+    ys = []
+    for d in range(world):  # rank d receives block d of every source, runs its experts (slots 0..El-1)
+        rx = torch.stack([sends[s][d] for s in range(world)]).view(world * C, Hs).contiguous()
+        rm = torch.stack([metas[s][d] for s in range(world)]).view(world * C, 2).contiguous()
+        ys.append(kernels.moe_batched(pool[d * El : (d + 1) * El].contiguous(), rm, rx, 1, n, Hs, Is, bits, G))
+    outs = []
+    for s in range(world):  # results of source s come back from every rank d
+        back = torch.stack([ys[d][s * C : (s + 1) * C] for d in range(world)]).view(world * C, Hs).contiguous()
+        out = torch.empty(Nr, Hs, dtype=torch.bfloat16, device=dev)
+        kernels.ep_combine(back, srcs[s], w[s * Nr : (s + 1) * Nr].contiguous(), out)
+        outs.append(out)
+    got = torch.cat(outs).float().cpu().numpy()
+    want = O.moe_batched_ref(pool.cpu().numpy(), sel_np, rw_np, O.bf16_bits_to_f32(x.view(torch.int16).cpu().numpy().view(np.uint16)),
+                             n, Hs, Is, bits, G)
+    assert float(np.abs(got - want).max() / np.abs(want).max()) < 1e-2
+    assert _lib.device_status(0) == 0

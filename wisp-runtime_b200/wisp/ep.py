@@ -147,6 +147,42 @@ class ExpertParallelMoE:
         return kernels.ep_combine(y, self.src_pos, w.contiguous(), self.out)
 
 
+def dispatch_plan(sel, E_local, world, capacity, slot_base):
+    """The bookkeeping of the kernel-path dispatch as plain tensor operations (any device): exactly what
+    wisp_ep_dispatch writes besides the token rows.  For pair p = t*k + j of this rank's tokens
+    (sel int64 [N, k] global expert ids): destination d = sel // E_local, capacity slot c = the pair's
+    rank among the pairs bound for d (pair order).  Returns
+
+      dest, cap  int64 [N*k]
+      meta       fp32 [world, capacity, 2]: [slot_base + sel - d*E_local, 1] at (d, c), [-1, 0] elsewhere
+                 (the receiver's batched-MoE routing rows, k = 1)
+      src_pos    int32 [N*k] = d*capacity + c (where the pair's result comes back)"""
+    sel = sel.reshape(-1)
+    P = sel.numel()
+    if P > capacity:
+        raise ValueError(f"capacity {capacity} is below the {P} pairs of this rank")
+    dest = sel // E_local
+    onehot = (dest[:, None] == torch.arange(world, device=sel.device)[None, :]).to(torch.int64)
+    cap = (torch.cumsum(onehot, 0) - 1).gather(1, dest[:, None])[:, 0]
+    meta = torch.zeros(world, capacity, 2, dtype=torch.float32, device=sel.device)
+    meta[..., 0] = -1.0
+    meta[dest, cap, 0] = (slot_base + sel - dest * E_local).to(torch.float32)
+    meta[dest, cap, 1] = 1.0
+    src_pos = (dest * capacity + cap).to(torch.int32)
+    return dest, cap, meta, src_pos
+
+
+def combine_plan(y_back, src_pos, w):
+    """What wisp_ep_combine computes, in fp32: out[t] = sum_j w[t, j] * y_back[src_pos[t*k + j]], the
+    choices summed in order (y_back [world * capacity, H], w fp32 [N, k])."""
+    N, k = w.shape
+    rows = y_back.reshape(-1, y_back.shape[-1])[src_pos.long()].float().view(N, k, -1)
+    out = torch.zeros(N, rows.shape[-1], dtype=torch.float32, device=rows.device)
+    for j in range(k):
+        out += w[:, j : j + 1].float() * rows[:, j]
+    return out
+
+
 def batched_expert_fn(pool, layer_slots, n, H, I, bits, group):
     """expert_fn running this rank's experts with the batched MoE kernel: local id e of layer l is slot
     layer_slots(l, e) of ``pool``; every received pair gets weight 1 (the source applies w).  Takes the
