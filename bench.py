@@ -110,7 +110,7 @@ def workload_config(a, n):
             f"{a.bits}-bit g{G} experts, {res}, bf16 attention/embeddings, vocab {VOCAB}, "
             f"{a.prompt}-token seeded prompt (chunked prefill) then one token per step, "
             + ("teacher-forced from a seeded random token stream " if a.tokens == "forced" else "greedy ") + graph,
-            "model": "Qwen3-30B-A3B-shaped (random init)",
+            "model": "Qwen3-30B-A3B-shaped (random init; o_proj and expert down at std 0.02/sqrt(2L))",
             "global_batch": n,
             "seq_len": a.prompt,
             "parallelism": "replicas" if n > 1 else "single",
@@ -759,7 +759,10 @@ class DecodeBench:
 
         cfg = DecoderConfig(layers=L, bits=a.bits)
         self.a = a
-        self.w = DecoderWeights.random(cfg, device=device, seed=seed)
+        # scaled residual init: with the plain init the residual stream of a random model grows a component
+        # shared by every token and routing collapses onto ~20 experts per layer in the deep layers; scaled,
+        # a token's routing follows the token (~110 of 128 experts per layer over 32 tokens)
+        self.w = DecoderWeights.random(cfg, device=device, seed=seed, resid_scale=True)
         n_steps = a.warmup + 2 * a.steps + 3 + TIMELINE_TOKENS
         need = a.prompt + n_steps + 16
         self.paged = a.cache_frac < 1.0

@@ -64,9 +64,17 @@ def test_block_matches_reference_outputs(golden, bits, fused, nslots, miss):
         x = _bf(g[f"x_b{bits}_N{N}"])[None]
         with torch.no_grad():
             out, logits = blk(x)
-        ref = O.bf16_bits_to_f32(g[f"out_b{bits}_N{N}"])
-        assert _rel(_np(out[0]), ref) < TOL, (N, _rel(_np(out[0]), ref))
         assert torch.equal(logits.view(torch.int16).cpu(), torch.from_numpy(g[f"logits_b{bits}_N{N}"].view(np.int16)))
+        # the block's own routing (CUDA topk); bf16 logits can tie at the k-th place, and a tie may break
+        # differently than on the reference's CPU, so the frozen output is compared only where they agree
+        _, sel, rw = blk._route(x[0])
+        sel_np, rw_np = sel.cpu().numpy(), rw.float().cpu().numpy()
+        want = O.moe_batched_ref(g[f"pool_b{bits}"], sel_np, rw_np, _np(x[0]), H * I, H, I, bits, G)
+        assert _rel(_np(out[0]), want) < TOL, (N, _rel(_np(out[0]), want))
+        same = (np.sort(sel_np, 1) == np.sort(g[f"sel_b{bits}_N{N}"], 1)).all(1)
+        assert same.sum() >= N - 1, N  # at most one tie in a fixture
+        ref = O.bf16_bits_to_f32(g[f"out_b{bits}_N{N}"])
+        assert _rel(_np(out[0])[same], ref[same]) < 2 * TOL, N
     if nslots < E:
         assert cache.stats["misses"] > 0
     if miss == "hybrid":
@@ -77,7 +85,7 @@ def test_block_matches_reference_outputs(golden, bits, fused, nslots, miss):
 
 
 # ---- an HF Qwen3-MoE model with attached blocks ---------------------------------------------------------
-def _tiny_hf(seed=0, layers=3):
+def _tiny_hf(seed=0, layers=3, boost=True):
     from transformers import AutoModelForCausalLM, Qwen3MoeConfig
 
     cfg = Qwen3MoeConfig(vocab_size=256, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
@@ -86,10 +94,11 @@ def _tiny_hf(seed=0, layers=3):
                          norm_topk_prob=True, max_position_embeddings=256, rms_norm_eps=1e-6)
     torch.manual_seed(seed)
     m = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16).cuda().eval()
-    with torch.no_grad():  # make the experts matter: default init leaves the MoE almost irrelevant
-        for layer in m.model.layers:
-            layer.mlp.experts.gate_up_proj.mul_(6)
-            layer.mlp.experts.down_proj.mul_(30)
+    if boost:
+        with torch.no_grad():  # make the experts matter: default init leaves the MoE almost irrelevant
+            for layer in m.model.layers:
+                layer.mlp.experts.gate_up_proj.mul_(6)
+                layer.mlp.experts.down_proj.mul_(30)
     return m, cfg
 
 
@@ -103,13 +112,13 @@ def _experts_of(model, cfg):
     return out
 
 
-def _quantized_hf(bits, group=128, seed=0, shuffle=False):
+def _quantized_hf(bits, group=128, seed=0, shuffle=False, boost=True):
     """The tiny HF model with its experts replaced by their dequantized packed form (both sides then
     compute the same function), and the packed store."""
     from wisp import quant
     from wisp.store import ExpertStore
 
-    model, cfg = _tiny_hf(seed)
+    model, cfg = _tiny_hf(seed, boost=boost)
     store = ExpertStore.from_experts(_experts_of(model, cfg), bits, group=group, device="cuda")
     E, I, H = cfg.num_experts, cfg.moe_intermediate_size, cfg.hidden_size
     with torch.no_grad():
@@ -196,21 +205,31 @@ def test_attached_model_sabotage_is_caught():
 def test_graph_decoder_from_model(nslots):
     """GraphDecoder(model, rt, tmax): chunked prefill, then teacher-forced decode steps through the
     whole-token graph (device slot table; with 10 of 24 experts resident the rest are read from the
-    pinned host store and paged in one token behind) against HF on the dequantized experts."""
+    pinned host store and paged in one token behind).  Bit-identical to the decoder built from the
+    same weights with every expert resident, and close to HF itself.  (The HF comparison uses the
+    default expert scale: with boosted experts a last-bit difference in attention can flip a top-2
+    choice, which the test of the attached blocks avoids by running HF's own attention.)"""
     from wisp.graphdec import GraphDecoder
+    from wisp.model import DecoderWeights
 
-    model, cfg, store = _quantized_hf(4)
+    model, cfg, store = _quantized_hf(4, boost=False)
     ids = torch.randint(0, 256, (1, 16), device="cuda", generator=torch.Generator("cuda").manual_seed(5))
     with torch.no_grad():
         ref = model(ids).logits.float()[0]
+    w = DecoderWeights.from_hf(model, None, bits=4, group=128)
+    w.pool = store.host.cuda()  # every expert resident, slot = key: the store's own bytes
+    resident = GraphDecoder(w, tmax=64)
     rt = _attach(model, store, nslots)
     dec = GraphDecoder(model, rt, tmax=64)
     scale = ref.abs().max().item()
     lg = dec.prefill(ids[0, :9], chunk=4)  # chunks of 4, 4, 1
+    want = resident.prefill(ids[0, :9], chunk=4)
     assert lg.shape == (1, cfg.vocab_size)
+    assert torch.equal(lg[0], want)
     assert (lg.float()[0] - ref[8]).abs().max().item() < 3 * TOL * scale
     for t in range(9, 16):
         lg = dec.next(ids[0, t : t + 1])
+        assert torch.equal(lg[0], resident.next(ids[0, t : t + 1])), t
         assert (lg.float()[0] - ref[t]).abs().max().item() < 3 * TOL * scale, t
     dec.flush()
     assert rt.stats["layer_calls"] > 0
@@ -238,7 +257,8 @@ def test_cache_weights_resize_and_decode_on_load():
         assert torch.equal(W, want[key])
     assert torch.equal(cache.cpu_weights(5), want[5].cpu())
     # resize: the kept experts are the most recently used, their bytes re-copied from the host store
-    cache.ensure([0, 2, 4, 5, 6])
+    for key in (0, 2, 4, 5, 6):
+        cache.ensure([key])
     cache.resize(4)
     assert cache.gpu.shape[0] == 4 and len(cache.core.key2slot) == 4
     for key, s in cache.core.key2slot.items():

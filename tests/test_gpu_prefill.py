@@ -84,7 +84,10 @@ def test_prefill_with_a_capped_cache():
     lb = b.prefill(ids)
     assert _close(la, lb, 1e-2)
     assert cache.stats["misses"] > 0
-    # decode continues bit-identically afterwards (the paged decode path is bit-identical to resident)
+    # the paged prefill sums groups of experts in bf16, so its cache differs from the resident one by
+    # rounding; with the same cache contents the paged decode steps are bit-identical to the resident ones
+    b.kc.copy_(a.kc)
+    b.vc.copy_(a.vc)
     t = la.argmax().reshape(1)
     for _ in range(4):
         x, y = a.next(t).clone(), b.next(t)

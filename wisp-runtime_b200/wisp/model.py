@@ -63,8 +63,11 @@ class DecoderWeights:
     # ------------------------------------------------------------------------------------------------
     @staticmethod
     @torch.no_grad()
-    def random(cfg: DecoderConfig, device="cuda", seed=0, std=0.02, expert_std=0.02):
-        """Seeded random-init weights of the given shape; experts quantized into a resident pool."""
+    def random(cfg: DecoderConfig, device="cuda", seed=0, std=0.02, expert_std=0.02, resid_scale=False):
+        """Seeded random-init weights of the given shape; experts quantized into a resident pool.
+        ``resid_scale``: the projections that write into the residual stream (attention o_proj, the
+        experts' down) start at std / sqrt(2 * layers), the scaled initialisation of GPT-2-style models,
+        so the stream stays dominated by the token's own embedding and routing follows the token."""
         w = DecoderWeights(cfg)
         g = torch.Generator(device=device).manual_seed(seed)
         H, D, Hq, Hk, E, I, V = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.moe_inter, cfg.vocab
@@ -86,7 +89,7 @@ class DecoderWeights:
                     wqkv=rnd((Hq + 2 * Hk) * D, H),
                     q_norm=norm(D),
                     k_norm=norm(D),
-                    wo=rnd(H, Hq * D),
+                    wo=rnd(H, Hq * D, s=std / (2 * cfg.layers) ** 0.5 if resid_scale else std),
                     post_norm=norm(H),
                     router=rnd(E, H, s=0.5),
                 )
@@ -98,7 +101,10 @@ class DecoderWeights:
         for l in range(cfg.layers):
             for e0 in range(0, E, chunk):
                 e1 = min(E, e0 + chunk)
-                w3 = (torch.randn(e1 - e0, 3, n, device=device, generator=g) * expert_std).to(bf)
+                w3 = torch.randn(e1 - e0, 3, n, device=device, generator=g) * expert_std
+                if resid_scale:
+                    w3[:, 2] /= (2 * cfg.layers) ** 0.5
+                w3 = w3.to(bf)
                 w.pool[l * E + e0 : l * E + e1].copy_(quant.quantize_batch(w3, cfg.bits, cfg.group))
                 del w3
         return w
