@@ -73,10 +73,10 @@ def parse():
                     help="decoder: the token each step decodes -- a seeded random token stream (teacher forcing, so "
                     "routing keeps moving the way a real prompt stream does) or the model's own greedy choice (a "
                     "random-init model settles into a fixed loop and hardly pages)")
-    ap.add_argument("--admit", default="hot", choices=["all", "hot"],
-                    help="decoder, device paging: page every miss in (all) or only experts whose decayed use "
-                    "frequency reached the cache's admit threshold (hot); misses are read from the pinned host "
-                    "store either way")
+    ap.add_argument("--admit", default="lfu", choices=["all", "hot", "lfu", "none"],
+                    help="decoder, device paging: page every miss in (all), only experts whose decayed use "
+                    "frequency reached the cache's admit threshold (hot), only experts used more often than the "
+                    "one they would evict (lfu), or none; misses are read from the pinned host store either way")
     ap.add_argument("--transport", default="auto", choices=["auto", "nccl", "p2p"],
                     help="moe-ep exchange: NCCL all-to-alls or kernel stores into peer memory (auto: p2p when N > 1)")
     a = ap.parse_args()
@@ -98,7 +98,7 @@ def workload_config(a, n):
         elif a.paging == "device":
             res = (f"expert cache capped at {a.cache_frac:.0%} of the {L * E} experts (LRU; residency in a device slot "
                    "table, non-resident experts read by the MoE kernels from the pinned host store, page-ins "
-                   f"({'every miss' if a.admit == 'all' else 'experts that turned hot'}) decided one token behind and "
+                   f"({dict(all='every miss', hot='experts that turned hot', lfu='misses used more often than the expert they would evict', none='none')[a.admit]}) decided one token behind and "
                    "copied with cudaMemcpyAsync on a side stream)")
             graph = "(whole-token CUDA graph)"
         else:

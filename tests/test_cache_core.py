@@ -183,3 +183,31 @@ def test_table_is_the_device_layout():
     t = c.table(12)
     assert t.dtype == np.int32 and t.shape == (12,)
     assert t[5] == 0 and t[9] == 1 and (np.delete(t, [5, 9]) == -1).all()
+
+
+def test_victim_matches_acquire():
+    c = CacheCore(3)
+    assert c.victim(set()) == (0, -1)
+    c.ensure([1, 2, 3])
+    c.ensure([2])
+    c.ensure([3])
+    s, k = c.victim(set())
+    assert (s, k) == (c.key2slot[1], 1)  # least recently used
+    assert c.victim({0, 1, 2}) is None
+    assert c.acquire(9, set()) == s and 1 not in c.key2slot
+
+
+def test_plan_token_lfu_and_none_admission():
+    from wisp.cache import plan_token
+
+    core = CacheCore(2, decay=1.0)
+    plan_token(core, [[0, 1]], 8, set(), admit="all")  # keys 0, 1 resident, used once
+    for _ in range(3):
+        plan_token(core, [[0]], 8, set(), admit="all")  # key 0 used 4 times
+    _, loads = plan_token(core, [[5]], 8, set(), admit="lfu")  # 5 (used once) would evict 1 (once): no
+    assert loads == []
+    for _ in range(2):
+        plan_token(core, [[5]], 8, set(), admit="none")  # still served from the host
+    assert 5 not in core.key2slot
+    _, loads = plan_token(core, [[5]], 8, set(), admit="lfu")  # 4 uses against 1: admitted over key 1
+    assert loads == [(5, core.key2slot[5])] and 1 not in core.key2slot and 0 in core.key2slot

@@ -258,6 +258,9 @@ class ExpertCache:
         return self.core.stats
 
 
+LFU_MARGIN = 1.25  # admit="lfu": a miss replaces a resident expert only when used this much more often
+
+
 def plan_token(core, rows, experts, busy, admit="all"):
     """Cache policy for one decoded token whose routing is already known (``rows[l]`` = the experts
     layer l chose): per layer, in order, one clock tick and the hit / miss counts of the reference's
@@ -265,8 +268,12 @@ def plan_token(core, rows, experts, busy, admit="all"):
     -- a slot acquired, evicting the policy's victim -- when a slot outside this layer's resident
     experts and ``busy`` (slots whose page-in is still in flight, grown by this call) can be had; with
     admit="hot" only keys whose decayed frequency reached ``core.admit_after`` (the hybrid policy's
-    admit_async, wisp/cache.py:96-104).  Returns (evicted keys, [(key, slot)] page-ins)."""
-    if admit not in ("all", "hot"):
+    admit_async, wisp/cache.py:96-104); with admit="lfu" only keys whose decayed use frequency is
+    LFU_MARGIN times that of the expert they would evict (TinyLFU-style admission: under routing with
+    little reuse a page-in that is evicted before its next use only costs PCIe bandwidth, since the
+    MoE kernels read a non-resident expert from host memory anyway); admit="none" never pages in (the
+    residency stays what it was, a pinned working set).  Returns (evicted keys, [(key, slot)] page-ins)."""
+    if admit not in ("all", "hot", "lfu", "none"):
         raise AssertionError(admit)
     evicted, loads = [], []
     for l, row in enumerate(rows):
@@ -284,8 +291,12 @@ def plan_token(core, rows, experts, busy, admit="all"):
         core.stats["hits"] += len(keys) - len(miss)
         core.stats["misses"] += len(miss)
         for k in miss:
-            if admit == "hot" and not core.should_admit(k):
+            if admit == "none" or (admit == "hot" and not core.should_admit(k)):
                 continue
+            if admit == "lfu":
+                v = core.victim(prot)
+                if v is None or (v[1] >= 0 and core.norm_freq(k) <= LFU_MARGIN * core.norm_freq(v[1])):
+                    continue
             try:
                 s = core.acquire(k, prot)
             except RuntimeError:  # every candidate is in use or in flight: stays host-served for now

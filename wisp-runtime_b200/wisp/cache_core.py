@@ -151,6 +151,22 @@ class CacheCore:
             out.append((k, s))
         return out
 
+    def victim(self, protected):
+        """The slot ``acquire`` would take next and the key it would evict from it: (slot, -1) while
+        never-used slots remain, None when every dynamic slot is protected."""
+        if self.fill < self.nslots:
+            return self.fill, -1
+        lo = self.n_static
+        cand = self.rank[lo:].copy()
+        p = np.fromiter((q - lo for q in protected if lo <= q < self.nslots), dtype=np.int64)
+        cand[p] = np.inf
+        if not cand.size:
+            return None
+        j = int(np.argmin(cand))
+        if not np.isfinite(cand[j]):
+            return None
+        return lo + j, int(self.owner[lo + j])
+
     def acquire(self, key, protected):
         """A slot for ``key``: the lowest never-used slot, else the dynamic slot ranked lowest by the
         policy outside ``protected`` (slots the current request already uses)."""
