@@ -77,6 +77,8 @@ def parse():
                     help="decoder, device paging: page every miss in (all), only experts whose decayed use "
                     "frequency reached the cache's admit threshold (hot), only experts used more often than the "
                     "one they would evict (lfu), or none; misses are read from the pinned host store either way")
+    ap.add_argument("--batched-path", default="auto", choices=["auto", "mma", "tcgen05"],
+                    help="moe-ep: the batched MoE kernels (auto = tcgen05 for 4/2-bit codes; mma = the warp-level path)")
     ap.add_argument("--transport", default="auto", choices=["auto", "nccl", "p2p"],
                     help="moe-ep exchange: NCCL all-to-alls or kernel stores into peer memory (auto: p2p when N > 1)")
     a = ap.parse_args()
@@ -134,7 +136,8 @@ def workload_config(a, n):
             f"over {n} GPU(s) ({E // n} per layer each), "
             + ("dispatch and combine as kernel stores into peer memory (CUDA IPC over NVLink, flags)"
                if (a.transport == "p2p" or (a.transport == "auto" and n > 1)) else "NCCL all-to-all dispatch and combine")
-            + ", rmsnorm+residual between layers (no attention)",
+            + ", rmsnorm+residual between layers (no attention), batched expert products on "
+            + ("the warp-level tensor-core kernels" if a.batched_path == "mma" else "tcgen05 (TMEM accumulators)"),
             "model": "Qwen3-30B-A3B-shaped (random init)",
             "global_batch": EP_BATCH,
             "seq_len": 1,
@@ -1001,7 +1004,8 @@ class EPStack:
         self.distinct = float(torch.tensor([len(torch.unique(sel[l])) for l in range(L)]).float().mean())
         self.norm_w = (1.0 + 0.1 * torch.randn(L, H, device=device, generator=g)).to(torch.bfloat16)
         self.x0 = torch.randn(self.N, H, device=device, generator=gen).to(torch.bfloat16)
-        fn = batched_expert_fn(self.pool, lambda l, e: l * self.El + e, n, H, I, a.bits, G)
+        fn = batched_expert_fn(self.pool, lambda l, e: l * self.El + e, n, H, I, a.bits, G,
+                               variant={"auto": 0, "mma": 1, "tcgen05": 2}[a.batched_path])
         self.transport = a.transport if a.transport != "auto" else ("p2p" if world > 1 else "nccl")
         assert self.transport == "nccl" or L % 2 == 0, "the p2p buffer sets alternate per layer: use an even layer count"
         self.ep = ExpertParallelMoE(E, K_TOP, H, self.N, fn, device=device, slot_base=lambda l: l * self.El,

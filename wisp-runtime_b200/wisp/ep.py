@@ -183,7 +183,7 @@ def combine_plan(y_back, src_pos, w):
     return out
 
 
-def batched_expert_fn(pool, layer_slots, n, H, I, bits, group):
+def batched_expert_fn(pool, layer_slots, n, H, I, bits, group, variant=0):
     """expert_fn running this rank's experts with the batched MoE kernel: local id e of layer l is slot
     layer_slots(l, e) of ``pool``; every received pair gets weight 1 (the source applies w).  Takes the
     receiver meta rows [slot, 1] (kernel mode) or local ids (-1 = unused capacity)."""
@@ -191,11 +191,11 @@ def batched_expert_fn(pool, layer_slots, n, H, I, bits, group):
 
     def fn(xr, ids_or_meta, layer):
         if ids_or_meta.dim() == 2:  # meta rows from wisp_ep_dispatch
-            return kernels.moe_batched(pool, ids_or_meta, xr, 1, n, H, I, bits, group)
+            return kernels.moe_batched(pool, ids_or_meta, xr, 1, n, H, I, bits, group, variant=variant)
         ids = ids_or_meta
         base = float(layer_slots(layer, 0))
         slots = torch.where(ids >= 0, ids + base, torch.full_like(ids, -1.0))
         meta = torch.stack([slots, torch.ones_like(ids)], 1).contiguous()
-        return kernels.moe_batched(pool, meta, xr.contiguous(), 1, n, H, I, bits, group)
+        return kernels.moe_batched(pool, meta, xr.contiguous(), 1, n, H, I, bits, group, variant=variant)
 
     return fn
