@@ -288,6 +288,30 @@ int wisp_qk_norm_rope_kv_rows(const uint16_t* qkv, int T, int64_t qkv_stride, in
                               const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos0,
                               int64_t tmax, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream);
 
+/* One decode token of each of B sequences: qkv row b (at qkv + b*qkv_stride) is sequence b's token at
+ * position pos[b] (int64 [B] on the device); q goes to q_out [B, Hq, D], k and v into row pos[b] of
+ * sequence b's caches (k_cache, v_cache [B, Hk, tmax, D]).  qn_w and kn_w NULL: no per-head RMSNorm
+ * (models without q/k norms, e.g. gpt-oss), only the rotary embedding.
+ * Replaces the per-sequence q/k norm, rotary and cache writes of a batched HF decode step
+ * (wisp/graphdec.py:160-170 per sequence). */
+int wisp_qk_norm_rope_kv_batched(const uint16_t* qkv, int B, int64_t qkv_stride, int Hq, int Hk, int D, const uint16_t* qn_w,
+                                 const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos,
+                                 int64_t tmax, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream);
+
+/* fp32 elements of the workspace wisp_gqa_decode_attn_batched needs (host-only; -1 for a bad shape). */
+int64_t wisp_attn_batched_workspace_floats(int B, int Hq, int Hk, int D, int64_t tmax);
+
+/* GQA decode attention of one token of each of B sequences: q [B, Hq, D] over positions [lo, pos[b]] of
+ * sequence b's caches [B, Hk, tmax, D], lo = pos[b] - window + 1 (0 when window == 0: full attention);
+ * softmax(scale * q.k) in fp32, with sinks (fp32 [Hq], nullable) as one extra logit per head that
+ * enters the normalisation only; out [B, Hq, D] bf16.  Split over chunks of 64 positions, then one
+ * combine launch.  Hq/Hk <= 8, D % 32 == 0, D <= 128.
+ * Replaces the masked SDPA of a batched decode step, with the sliding windows and attention sinks of
+ * gpt-oss attention (the HF GptOssAttention the reference's gpt-oss runs, wisp/gptoss.py:146-183). */
+int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache,
+                                 int64_t tmax, const int64_t* pos, int window, const float* sinks, float scale, float* workspace,
+                                 int64_t workspace_floats, uint16_t* out, void* stream);
+
 /* fp32 elements of the workspace wisp_gqa_decode_attn needs (host-only; -1 for a bad shape). */
 int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax);
 

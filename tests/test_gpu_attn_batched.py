@@ -1,0 +1,90 @@
+"""Batched decode attention and the batched q/k norm + rotary + cache write (one token of each of B
+sequences, each with its own position and cache), through the C ABI: against an fp32 restatement of
+masked softmax attention with gpt-oss's sliding window and attention sinks (the HF GptOssAttention
+math), and against the single-sequence kernels."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2  # relative to max |reference| (bf16 output)
+
+
+def _ref_attn(q, kc, vc, pos, scale, window, sinks):
+    """fp32: out[b, head] = sum_t p_t v_t over t in [lo, pos[b]], p = softmax over those scores plus an
+    optional per-head sink logit that takes part in the normalisation only."""
+    B, Hq, D = q.shape
+    Hk = kc.shape[1]
+    G = Hq // Hk
+    out = torch.zeros(B, Hq, D)
+    for b in range(B):
+        p = int(pos[b])
+        lo = max(0, p - window + 1) if window > 0 else 0
+        for hd in range(Hq):
+            k = kc[b, hd // G, lo : p + 1].float()
+            v = vc[b, hd // G, lo : p + 1].float()
+            s = (k @ q[b, hd].float()) * scale
+            if sinks is not None:
+                s = torch.cat([s, sinks[hd : hd + 1].float()])
+            w = torch.softmax(s, 0)[: k.shape[0]]
+            out[b, hd] = w @ v
+    return out
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("window,use_sinks", [(0, False), (128, True), (100, False), (0, True)])
+def test_batched_attention_matches_reference(D, window, use_sinks):
+    from wisp import _lib, kernels
+
+    g = torch.Generator(device="cuda").manual_seed(D + window)
+    B, Hq, Hk, tmax = 4, 8, 2, 320
+    q = torch.randn(B, Hq, D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    pos = torch.tensor([0, 63, 191, 319], dtype=torch.int64, device="cuda")  # chunk edges and the last slot
+    sinks = torch.randn(Hq, device="cuda", generator=g).float() * 2 if use_sinks else None
+    scale = D ** -0.5
+    _lib.device_status(0)
+    out = kernels.gqa_decode_attn_batched(q, Hq, Hk, D, kc, vc, pos, scale, window=window, sinks=sinks)
+    ref = _ref_attn(q.cpu(), kc.cpu(), vc.cpu(), pos.cpu(), scale, window, None if sinks is None else sinks.cpu())
+    err = (out.float().cpu() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < TOL, err
+    assert _lib.device_status(0) == 0
+    if window == 0 and not use_sinks:  # one sequence at a time through the single-sequence entry point: the same bits
+        for b in range(B):
+            one = kernels.gqa_decode_attn(q[b].reshape(-1).contiguous(), Hq, Hk, D, kc[b].contiguous(), vc[b].contiguous(),
+                                          pos[b : b + 1], scale)
+            assert torch.equal(one.view(Hq, D), out[b]), b
+
+
+@pytest.mark.parametrize("norm", [True, False])
+def test_batched_rope_kv_write(norm):
+    from wisp import kernels
+    from wisp.model import rotary_tables
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    B, Hq, Hk, D, tmax = 3, 8, 2, 64, 96
+    qkv = torch.randn(B, (Hq + 2 * Hk) * D, device="cuda", generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16) if norm else None
+    kn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16) if norm else None
+    cos, sin = rotary_tables(D, tmax, 150000.0, "cuda")
+    pos = torch.tensor([5, 0, 95], dtype=torch.int64, device="cuda")
+    kc = torch.zeros(B, Hk, tmax, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q = kernels.qk_norm_rope_kv_batched(qkv, Hq, Hk, D, qn, kn, 1e-6, cos, sin, pos, kc, vc)
+    for b in range(B):
+        p = int(pos[b])
+        v = qkv[b, (Hq + Hk) * D :].view(Hk, D)
+        assert torch.equal(vc[b, :, p], v)
+        if norm:  # the single-token kernel on that sequence's cache gives the same bits
+            kc1 = torch.zeros(Hk, tmax, D, dtype=torch.bfloat16, device="cuda")
+            vc1 = torch.zeros_like(kc1)
+            q1 = kernels.qk_norm_rope_kv(qkv[b].contiguous(), Hq, Hk, D, qn, kn, 1e-6, cos, sin, pos[b : b + 1], kc1, vc1)
+            assert torch.equal(q1.view(Hq, D), q[b]) and torch.equal(kc1[:, p], kc[b, :, p])
+        else:  # plain rotate-half rotary in fp32
+            x = qkv[b, : Hq * D].view(Hq, D).float()
+            rot = torch.cat([-x[:, D // 2 :], x[:, : D // 2]], 1)
+            want = x * cos[p].float() + rot * sin[p].float()
+            assert (q[b].float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+        others = [t for t in range(tmax) if t != p]
+        assert (kc[b, :, others] == 0).all()  # nothing else of that cache was written

@@ -23,26 +23,32 @@ constexpr int MAX_G = 8;        // query heads per KV head (attention)
 
 // ---- per-head RMSNorm + rotary + cache write -----------------------------------------------------
 // qkv: per token [Hq*D | Hk*D | Hk*D] bf16 (q heads, k heads, v heads), token t at qkv + t*qkv_stride.
-// One warp per head; grid y = token: token t sits at position *pos_ptr + t, its q goes to
-// q_out + t*Hq*D.  (One token per decode step; a chunk of prompt tokens in the prefill.)
+// One warp per head; grid y = token t, at position pos_ptr[t * pos_step] + t * pos_inc, writing the
+// caches at kc/vc + t * kv_bstride; its q goes to q_out + t*Hq*D.  One token per decode step
+// (pos_step 0); a chunk of one sequence's prompt (pos_step 0, pos_inc 1); one token of each of
+// several sequences (pos_step 1, pos_inc 0, kv_bstride = one sequence's cache).  qn_w == nullptr:
+// no per-head RMSNorm (models without q/k norms).
 __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq, int Hk, int D,
                                        const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w, float eps,
                                        const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t,
                                        const int64_t* __restrict__ pos_ptr, int64_t tmax, uint16_t* __restrict__ q_out,
-                                       uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int64_t qkv_stride) {
+                                       uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int64_t qkv_stride, int pos_step,
+                                       int pos_inc, int64_t kv_bstride) {
   __shared__ float xs[8][QK_MAX_D];
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.x * (blockDim.x >> 5) + wib;
   pdl_wait();
   pdl_launch_dependents();
   if (head >= Hq + 2 * Hk) return;
-  const int64_t pos = *pos_ptr + blockIdx.y;
+  const int64_t pos = pos_ptr[int64_t(blockIdx.y) * pos_step] + int64_t(blockIdx.y) * pos_inc;
   if (pos < 0 || pos >= tmax) {
     if (lane == 0 && head == 0) flag(WISP_STATUS_BAD_POS);
     return;
   }
   qkv += int64_t(blockIdx.y) * qkv_stride;
   q_out += int64_t(blockIdx.y) * Hq * D;
+  kc += int64_t(blockIdx.y) * kv_bstride;
+  vc += int64_t(blockIdx.y) * kv_bstride;
   const uint16_t* src = qkv + int64_t(head) * D;
   if (head >= Hq + Hk) {  // v: straight into the cache
     const int hv = head - Hq - Hk;
@@ -63,7 +69,8 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq,
   const float inv = rsqrtf(ss / float(D) + eps);
   __syncwarp();
   // HF RMSNorm: weight * bf16(x * rsqrt(mean(x^2) + eps)), rounded to bf16
-  for (int i = lane; i < D; i += 32) x[i] = bf16_to_f32(f32_to_bf16(bf16_to_f32(w[i]) * bf16_to_f32(f32_to_bf16(x[i] * inv))));
+  if (w)
+    for (int i = lane; i < D; i += 32) x[i] = bf16_to_f32(f32_to_bf16(bf16_to_f32(w[i]) * bf16_to_f32(f32_to_bf16(x[i] * inv))));
   __syncwarp();
   const uint16_t* cs = cos_t + pos * D;
   const uint16_t* sn = sin_t + pos * D;
@@ -79,24 +86,36 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq,
 // grid (Hk, tmax / CHUNK): CTA (h, c) covers positions [c*CHUNK, min((c+1)*CHUNK, pos+1)) for the
 // G = Hq/Hk query heads of KV head h.  Partial record per (h, c, g): D unnormalised outputs, then
 // the running max and the sum of exponentials.
+// grid (Hk, chunks, batch): sequence b = blockIdx.z has its query at q + b*Hq*D, its caches at
+// kc/vc + b*kv_bstride and its position at pos_ptr[b]; window > 0 keeps only positions
+// (pos - window, pos] (sliding-window attention).  Records: part[((b*Hk + h)*chunks + c)*G + g].
+__device__ __forceinline__ int64_t window_lo(int64_t pos, int window) {
+  return window > 0 && pos - window + 1 > 0 ? pos - window + 1 : 0;
+}
+
 __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t* __restrict__ q, int Hq, int Hk, int D,
                                                                   const uint16_t* __restrict__ kc,
                                                                   const uint16_t* __restrict__ vc, int64_t tmax,
                                                                   const int64_t* __restrict__ pos_ptr, float scale,
-                                                                  float* __restrict__ part) {
+                                                                  float* __restrict__ part, int64_t kv_bstride, int window) {
   __shared__ float qs[MAX_G][MAX_D];
   __shared__ float ps[MAX_G][CHUNK];
   __shared__ float red[ATTN_THREADS / 32][MAX_G][MAX_D];  // per-warp P V sums, lane-major
-  const int h = blockIdx.x, c = blockIdx.y;
+  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int G = Hq / Hk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = ATTN_THREADS / 32;
   pdl_wait();
   pdl_launch_dependents();
-  const int64_t pos = *pos_ptr;
+  const int64_t pos = pos_ptr[b];
   if (pos < 0 || pos >= tmax) return;  // flagged by the cache-write kernel
-  const int64_t t0 = int64_t(c) * CHUNK;
-  if (t0 > pos) return;  // beyond the current length: the combine never reads this record
-  const int n = int((pos + 1 - t0) < CHUNK ? (pos + 1 - t0) : CHUNK);
+  const int64_t lo = window_lo(pos, window);
+  const int64_t t0 = int64_t(c) * CHUNK > lo ? int64_t(c) * CHUNK : lo;
+  if (t0 > pos || t0 >= int64_t(c + 1) * CHUNK) return;  // outside [lo, pos]: the combine never reads this record
+  const int n = int((pos + 1 - t0) < int64_t(c + 1) * CHUNK - t0 ? (pos + 1 - t0) : int64_t(c + 1) * CHUNK - t0);
+  q += int64_t(b) * Hq * D;
+  kc += int64_t(b) * kv_bstride;
+  vc += int64_t(b) * kv_bstride;
+  part += int64_t(b) * Hk * gridDim.y * G * (D + 2);
   // q of the G heads, pre-scaled, fp32
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i / D][i % D] = bf16_to_f32(q[(int64_t(h) * G) * D + i]) * scale;
   __syncthreads();
@@ -170,26 +189,31 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
   }
 }
 
-// one CTA per query head: out = sum_c O_c e^(m_c - M) / sum_c l_c e^(m_c - M)
+// one CTA per (query head, sequence): out = sum_c O_c e^(m_c - M) / (sum_c l_c e^(m_c - M) [+ e^(sink - M)]);
+// sinks (fp32 [Hq], nullable) are per-head logits that take part in the softmax's normalisation but
+// contribute no value (attention sinks)
 __global__ void attn_combine_kernel(const float* __restrict__ part, int Hq, int Hk, int D, int nchunk_max,
-                                    const int64_t* __restrict__ pos_ptr, int64_t tmax, uint16_t* __restrict__ out) {
-  const int head = blockIdx.x;
+                                    const int64_t* __restrict__ pos_ptr, int64_t tmax, uint16_t* __restrict__ out, int window,
+                                    const float* __restrict__ sinks) {
+  const int head = blockIdx.x, b = blockIdx.y;
   const int G = Hq / Hk, h = head / G, g = head % G;
   pdl_wait();
   pdl_launch_dependents();
-  const int64_t pos = *pos_ptr;
+  const int64_t pos = pos_ptr[b];
   if (pos < 0 || pos >= tmax) return;
-  const int nc = int(pos / CHUNK) + 1;
-  float M = -INFINITY;
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, part[((int64_t(h) * nchunk_max + c) * G + g) * (D + 2) + D]);
-  float Ls = 0.0f;
-  for (int c = 0; c < nc; ++c) {
+  part += int64_t(b) * Hk * nchunk_max * G * (D + 2);
+  out += int64_t(b) * Hq * D;
+  const int c0 = int(window_lo(pos, window) / CHUNK), nc = int(pos / CHUNK) + 1;
+  float M = sinks ? sinks[head] : -INFINITY;
+  for (int c = c0; c < nc; ++c) M = fmaxf(M, part[((int64_t(h) * nchunk_max + c) * G + g) * (D + 2) + D]);
+  float Ls = sinks ? __expf(sinks[head] - M) : 0.0f;
+  for (int c = c0; c < nc; ++c) {
     const float* rec = part + ((int64_t(h) * nchunk_max + c) * G + g) * (D + 2);
     Ls += rec[D + 1] * __expf(rec[D] - M);
   }
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float o = 0.0f;
-    for (int c = 0; c < nc; ++c) {
+    for (int c = c0; c < nc; ++c) {
       const float* rec = part + ((int64_t(h) * nchunk_max + c) * G + g) * (D + 2);
       o += rec[d] * __expf(rec[D] - M);
     }

@@ -5,19 +5,22 @@
 // Work item = (group of pairs routed to one slot, N tile of up to NMAX of its tokens, tile of BM = 128
 // weight rows).  Per item the whole K range streams through shared memory in BK = 64 slices:
 //
-//   warp 0      producer: TMA tensor loads of the slice's packed codes (one 128-row box per matrix),
-//               of the tokens' activation rows (fp16, 128-byte swizzled boxes of 32 rows), and per item
-//               one bulk copy of the tile's scales and mins
-//   warps 2-9   dequantize the codes into the MMA's A operand: per 8 codes one LOP3 builds fp16 pairs
+//   warp 0      code producer: TMA tensor loads of the slice's packed codes (one 128-row box per
+//               matrix), per item one bulk copy of the tile's scales and mins and an L2 prefetch of the
+//               item's (and the next item's) code rows
+//   warp 22     activation producer: the tokens' activation rows (fp16, 128-byte swizzled boxes of 32
+//               rows); a ring of its own, so the code ring runs ahead of the tensor core by its full depth
+//   warps 2-17  dequantize the codes into the MMA's A operand: per 8 codes one LOP3 builds fp16 pairs
 //               1024 + q, one HSUB2 makes q exact, one HFMA2 applies scale and min (a single rounding of
 //               q*s + m to fp16: closer to the exact weight than the reference's bf16(q*s + m)); the
 //               tile is written in the K-major 128-byte-swizzled layout the tensor core reads
 //   warp 1      one thread issues tcgen05.mma (kind::f16, M = 128, N = the item's tokens rounded up to
 //               32, K = 16 per instruction) for gate and up (or down) into TMEM, and commits each
 //               stage back to the producer and the dequantizers
-//   warps 2-9   epilogue: tcgen05.ld of the accumulators; gate/up -> a = silu(g)*u as fp16 rows of the
+//   warps 18-21 epilogue: tcgen05.ld of the accumulators; gate/up -> a = silu(g)*u as fp16 rows of the
 //               intermediate (pair-permuted, the down pass's activation operand); down -> fp32 rows of
-//               y that the combine kernel sums per token in a fixed order
+//               y that the combine kernel sums per token in a fixed order.  Two accumulator buffers in
+//               TMEM let this run while the other warps stream the next item.
 //
 // Each code word is read from HBM once per item, however many tokens the expert received (up to
 // NMAX per N tile), and it is unpacked once.  Inside a code word the MMA's K order is the pair order
@@ -39,14 +42,24 @@ namespace umma {
 
 constexpr int BM = 128;       // weight rows per tile (MMA M)
 constexpr int BK = 64;        // K per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int NMAX = 128;     // tokens per N tile (MMA N <= 128)
+constexpr int NMAX = 64;      // tokens per N tile (MMA N <= 64; an expert with more tokens takes several tiles)
 constexpr int BOXR = 32;      // token rows per activation box; MMA N is a multiple of it
 constexpr int CST = 4;        // code stages
-constexpr int AST = 2;        // dequantized A stages
-constexpr int BST = 3;        // activation stages
-constexpr int DQ_WARPS = 8;   // dequantizing / epilogue warps (warps 2..9)
-constexpr int THREADS = (2 + DQ_WARPS) * 32;
-constexpr uint32_t TMEM_COLS = 256;  // gate at column 0, up at column NMAX
+constexpr int AST = 3;        // dequantized A stages
+constexpr int BST = 6;        // activation stages
+constexpr int DQ_WARPS = 16;  // dequantizing warps (warps 2..17)
+constexpr int EPI_WARPS = 4;  // epilogue warps (warps 18..21: one per TMEM lane quarter)
+constexpr int EPI0 = 2 + DQ_WARPS;
+constexpr int BPROD = EPI0 + EPI_WARPS;  // warp 22: activation producer
+constexpr int THREADS = (BPROD + 1) * 32;
+// two accumulator buffers, so the epilogue of one item overlaps the main loop of the next; inside one,
+// every matrix has two accumulators that alternate over the K steps (two independent MMA chains per
+// matrix instead of one: with the few tokens of an expert each MMA is short and a single chain waits on
+// the previous MMA's result): gate/up [gate0 | gate1 | up0 | up1] of NMAX columns, down [down0 | down1]
+template <int MAT>
+constexpr uint32_t acc_cols() { return MAT == 0 ? 4 * NMAX : 2 * NMAX; }
+template <int MAT>
+constexpr uint32_t tmem_cols() { return 2 * acc_cols<MAT>(); }
 
 template <int BITS, int MAT>
 struct Cfg {
@@ -56,7 +69,7 @@ struct Cfg {
   static constexpr int CODE_STAGE = NMAT * CODE_MAT;
   static constexpr int A_MAT = BM * BK * 2;                 // 16 KB
   static constexpr int A_STAGE = NMAT * A_MAT;
-  static constexpr int B_STAGE = NMAX * BK * 2;             // 16 KB
+  static constexpr int B_STAGE = NMAX * BK * 2;             // 8 KB
   static constexpr int OFF_A = 0;                           // 1024-aligned pieces first
   static constexpr int OFF_B = OFF_A + AST * A_STAGE;
   static constexpr int OFF_C = OFF_B + BST * B_STAGE;
@@ -68,7 +81,7 @@ template <int BITS, int MAT>
 __host__ __device__ inline int64_t smem_bytes(int gpr) {
   using C = Cfg<BITS, MAT>;
   const int64_t sc = (C::scale_bytes(gpr) + 127) / 128 * 128;
-  // + barriers (2 CST + 2 AST + 2 BST + 4 + 3) * 8, the TMEM address, the abort flag, 1 KB alignment slack
+  // + barriers (2 CST + 2 AST + 2 BST + 4 + 5) * 8, the TMEM address, the abort flag, 1 KB alignment slack
   return C::OFF_S + 2 * sc + 256 + 1024;
 }
 
@@ -243,9 +256,9 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
   uint64_t* b_empty = b_full + BST;
   uint64_t* sc_full = b_empty + BST;    // [2]
   uint64_t* sc_empty = sc_full + 2;     // [2]
-  uint64_t* acc_full = sc_empty + 2;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* mma_done = acc_empty + 1;
+  uint64_t* acc_full = sc_empty + 2;    // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   __shared__ int s_maxcnt;
@@ -268,15 +281,17 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
       mbar_init(sc_full + i, 1);
       mbar_init(sc_empty + i, DQ_WARPS);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, DQ_WARPS);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, EPI_WARPS);
+    }
     mbar_init(mma_done, 1);
     *abort = 0;
     s_maxcnt = 0;
     mbar_fence_init();
   }
   if (warp == 1) {  // TMEM for the accumulators (the whole warp allocates)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(tmem_cols<MAT>())
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -295,17 +310,38 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
 
   if (warp == 0) {
     // ================= producer (the whole warp loops, lane 0 issues) =================
-    uint32_t cs = 0, cph = 0, bs = 0, bph = 0, ss = 0, sph = 0;
+    uint32_t cs = 0, cph = 0, ss = 0, sph = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
       const Item it = item_of(i, rtiles, maxnt);
       const int cnt = W.grp_count[it.grp];
       if (it.nt * NMAX >= cnt) continue;
       const int slot = W.grp_slot[it.grp];
-      const int row0 = W.grp_start[it.grp] + it.nt * NMAX;
-      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
-      const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
       const int r0 = it.rt * BM;
+      // the item's code rows (one contiguous range per matrix) and the next item's, pulled into L2 now so
+      // the per-stage tensor loads below hit L2 instead of paying HBM latency one small stage at a time
+      if (lane < 2 * C::NMAT) {
+        const int which = lane / C::NMAT, m = lane % C::NMAT;
+        int ii = i;
+        if (which) {  // the next item this CTA takes that has tokens
+          ii = -1;
+          for (int jn = i + int(gridDim.x); jn < nitems; jn += gridDim.x) {
+            const Item nx = item_of(jn, rtiles, maxnt);
+            if (nx.nt * NMAX < W.grp_count[nx.grp]) {
+              ii = jn;
+              break;
+            }
+          }
+        }
+        if (ii >= 0) {
+          const Item px = item_of(ii, rtiles, maxnt);
+          const int mat = MAT == 0 ? m : 2;
+          const int64_t rb = int64_t(K) * BITS / 8;
+          prefetch_l2(pool + int64_t(W.grp_slot[px.grp]) * S.nbytes + mat * S.mat_bytes + int64_t(px.rt) * BM * rb,
+                      uint32_t(BM * rb));
+        }
+      }
+      __syncwarp();
       // scales and mins of the tile's rows: one contiguous run per (matrix, kind)
       ok = warp_wait(sc_empty + ss, sph ^ 1, abort);
       if (!ok) break;
@@ -334,15 +370,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
         }
         __syncwarp();
         if (++cs == CST) cs = 0, cph ^= 1;
-        ok = warp_wait(b_empty + bs, bph ^ 1, abort);
-        if (!ok) break;
-        if (lane == 0) {
-          mbar_expect_tx(b_full + bs, uint32_t(NT * BK * 2));
-          for (int j = 0; j < NT / BOXR; ++j)
-            tma_load_2d(sB + bs * C::B_STAGE + j * BOXR * BK * 2, &mapB, kt * BK, row0 + j * BOXR, b_full + bs);
-        }
-        __syncwarp();
-        if (++bs == BST) bs = 0, bph ^= 1;
       }
     }
     // copies still in flight land before the CTA can exit: wait for the last arming of every stage
@@ -353,11 +380,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
         if (cs == CST - 1) cph ^= 1;
         mbar_wait(code_full + cs, cph);
       }
-      for (int j = 0; j < BST; ++j) {
-        bs = bs == 0 ? BST - 1 : bs - 1;
-        if (bs == BST - 1) bph ^= 1;
-        mbar_wait(b_full + bs, bph);
-      }
       for (int j = 0; j < 2; ++j) {
         ss ^= 1;
         if (ss == 1) sph ^= 1;
@@ -367,7 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
     __syncwarp();
   } else if (warp == 1) {
     // ================= MMA issuer (the whole warp loops, lane 0 issues) =================
-    uint32_t as = 0, aph = 0, bs = 0, bph = 0, eph = 0;
+    uint32_t as = 0, aph = 0, bs = 0, bph = 0, eph0 = 0, eph1 = 0, buf = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
       const Item it = item_of(i, rtiles, maxnt);
@@ -376,9 +398,12 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
       const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
       const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
       const uint32_t idesc = idesc_f16(NT);
-      ok = warp_wait(acc_empty, eph ^ 1, abort);  // the epilogue has read the previous item's accumulators
+      // the epilogue has read what this buffer held two items ago
+      uint32_t& eph = buf ? eph1 : eph0;
+      ok = warp_wait(acc_empty + buf, eph ^ 1, abort);
       if (!ok) break;
       eph ^= 1;
+      const uint32_t d0 = tmem + buf * acc_cols<MAT>();
       for (int kt = 0; kt < KT; ++kt) {
         ok = warp_wait(a_full + as, aph, abort) && warp_wait(b_full + bs, bph, abort);
         if (!ok) break;
@@ -388,9 +413,10 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t bd = sdesc_sw128(b0 + kk * 32);
-            const uint32_t acc = (kt | kk) != 0;
-            tc_mma(tmem, sdesc_sw128(a0 + kk * 32), bd, idesc, acc);
-            if (MAT == 0) tc_mma(tmem + NMAX, sdesc_sw128(a0 + C::A_MAT + kk * 32), bd, idesc, acc);
+            const uint32_t acc = kt != 0 || kk >= 2;  // each of the two accumulators starts at its first K step
+            const uint32_t half = (kk & 1) * NMAX;
+            tc_mma(d0 + half, sdesc_sw128(a0 + kk * 32), bd, idesc, acc);
+            if (MAT == 0) tc_mma(d0 + 2 * NMAX + half, sdesc_sw128(a0 + C::A_MAT + kk * 32), bd, idesc, acc);
           }
           tc_commit(a_empty + as);  // arrives once these MMAs have read the stage
           tc_commit(b_empty + bs);
@@ -399,40 +425,49 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
         if (++as == AST) as = 0, aph ^= 1;
         if (++bs == BST) bs = 0, bph ^= 1;
       }
-      if (ok && lane == 0) tc_commit(acc_full);
+      if (ok && lane == 0) tc_commit(acc_full + buf);
       __syncwarp();
+      buf ^= 1;
     }
     if (lane == 0) {
       tc_commit(mma_done);  // every MMA issued so far has completed
       mbar_wait(mma_done, 0);
     }
     __syncwarp();
-  } else {
-    // ================= dequantize + epilogue =================
-    const int d = threadIdx.x - 64;      // 0..255
+  } else if (warp < EPI0) {
+    // ================= dequantize =================
+    const int d = threadIdx.x - 64;      // 0 .. 32 DQ_WARPS - 1
     constexpr int WPR = BK * BITS / 32;  // code words per row per stage: 8 (4-bit), 4 (2-bit)
-    constexpr int RPT = BM * WPR / (DQ_WARPS * 32);  // rows per thread per matrix: 4 / 2
+    constexpr int RPT = BM * WPR / (DQ_WARPS * 32);  // rows per thread per matrix: 2 / 1
     const int wc = d % WPR, rb = d / WPR;
-    constexpr int RSTEP = DQ_WARPS * 32 / WPR;  // 32 / 64
-    uint32_t cs = 0, cph = 0, as = 0, aph = 0, ss = 0, sph = 0, eph = 0;
-    const int q4 = warp & 3;                // TMEM lane quarter this warp may read
-    const int chalf = (warp - 2) >> 2;      // column half of the epilogue
+    constexpr int RSTEP = DQ_WARPS * 32 / WPR;  // 64 / 128
+    uint32_t cs = 0, cph = 0, as = 0, aph = 0, ss = 0, sph = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
       const Item it = item_of(i, rtiles, maxnt);
       const int cnt = W.grp_count[it.grp];
       if (it.nt * NMAX >= cnt) continue;
-      const int row0 = W.grp_start[it.grp] + it.nt * NMAX;
-      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
-      const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
-      const int r0 = it.rt * BM;
       ok = warp_wait(sc_full + ss, sph, abort);
       if (!ok) break;
       const __half* scl = reinterpret_cast<const __half*>(sS + ss * sc_bytes);
+      __half2 s2[C::NMAT][RPT], m2[C::NMAT][RPT];
+      int gcur = -1;
       for (int kt = 0; kt < KT; ++kt) {
         ok = warp_wait(code_full + cs, cph, abort) && warp_wait(a_empty + as, aph ^ 1, abort);
         if (!ok) break;
         const int gcol = kt * BK / S.group;  // the stage's quantization group within the row
+        if (gcol != gcur) {  // scales and mins stay in registers for the stages of one group
+          gcur = gcol;
+#pragma unroll
+          for (int m = 0; m < C::NMAT; ++m)
+#pragma unroll
+            for (int j = 0; j < RPT; ++j) {
+              const int r = rb + RSTEP * j;
+              const __half sv = scl[((2 * m) * BM + r) * gpr + gcol], mv = scl[((2 * m + 1) * BM + r) * gpr + gcol];
+              s2[m][j] = __half2(sv, sv);
+              m2[m][j] = __half2(mv, mv);
+            }
+        }
         const uint8_t* cst = sC + cs * C::CODE_STAGE;
         uint8_t* ast = sA + as * C::A_STAGE;
 #pragma unroll
@@ -441,25 +476,24 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
           for (int j = 0; j < RPT; ++j) {
             const int r = rb + RSTEP * j;
             const uint32_t w = *reinterpret_cast<const uint32_t*>(cst + m * C::CODE_MAT + r * C::CODE_ROW + 4 * wc);
-            const __half sv = scl[((2 * m) * BM + r) * gpr + gcol], mv = scl[((2 * m + 1) * BM + r) * gpr + gcol];
-            const __half2 s2 = __half2(sv, sv), m2 = __half2(mv, mv);
+            const __half2 sj = s2[m][j], mj = m2[m][j];
             if (BITS == 4) {
               uint4 o;
-              o.x = deq2(q_pair<4>(w, 0), s2, m2);
-              o.y = deq2(q_pair<4>(w, 1), s2, m2);
-              o.z = deq2(q_pair<4>(w, 2), s2, m2);
-              o.w = deq2(q_pair<4>(w, 3), s2, m2);
+              o.x = deq2(q_pair<4>(w, 0), sj, mj);
+              o.y = deq2(q_pair<4>(w, 1), sj, mj);
+              o.z = deq2(q_pair<4>(w, 2), sj, mj);
+              o.w = deq2(q_pair<4>(w, 3), sj, mj);
               *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, wc)) = o;
             } else {
               uint4 o0, o1;
-              o0.x = deq2(q_pair<2>(w, 0), s2, m2);
-              o0.y = deq2(q_pair<2>(w, 1), s2, m2);
-              o0.z = deq2(q_pair<2>(w, 2), s2, m2);
-              o0.w = deq2(q_pair<2>(w, 3), s2, m2);
-              o1.x = deq2(q_pair<2>(w, 4), s2, m2);
-              o1.y = deq2(q_pair<2>(w, 5), s2, m2);
-              o1.z = deq2(q_pair<2>(w, 6), s2, m2);
-              o1.w = deq2(q_pair<2>(w, 7), s2, m2);
+              o0.x = deq2(q_pair<2>(w, 0), sj, mj);
+              o0.y = deq2(q_pair<2>(w, 1), sj, mj);
+              o0.z = deq2(q_pair<2>(w, 2), sj, mj);
+              o0.w = deq2(q_pair<2>(w, 3), sj, mj);
+              o1.x = deq2(q_pair<2>(w, 4), sj, mj);
+              o1.y = deq2(q_pair<2>(w, 5), sj, mj);
+              o1.z = deq2(q_pair<2>(w, 6), sj, mj);
+              o1.w = deq2(q_pair<2>(w, 7), sj, mj);
               *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, 2 * wc)) = o0;
               *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, 2 * wc + 1)) = o1;
             }
@@ -479,25 +513,72 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
       if (lane == 0) mbar_arrive1(sc_empty + ss);
       ss ^= 1;
       if (ss == 0) sph ^= 1;
-      // ---- epilogue ----
-      ok = warp_wait(acc_full, eph, abort);
+    }
+  } else if (warp == BPROD) {
+    // ================= activation producer (the whole warp loops, lane 0 issues) =================
+    uint32_t bs = 0, bph = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+      const Item it = item_of(i, rtiles, maxnt);
+      const int cnt = W.grp_count[it.grp];
+      if (it.nt * NMAX >= cnt) continue;
+      const int row0 = W.grp_start[it.grp] + it.nt * NMAX;
+      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
+      const int NT = (ntok + BOXR - 1) / BOXR * BOXR;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        ok = warp_wait(b_empty + bs, bph ^ 1, abort);
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_expect_tx(b_full + bs, uint32_t(NT * BK * 2));
+          for (int j = 0; j < NT / BOXR; ++j)
+            tma_load_2d(sB + bs * C::B_STAGE + j * BOXR * BK * 2, &mapB, kt * BK, row0 + j * BOXR, b_full + bs);
+        }
+        __syncwarp();
+        if (++bs == BST) bs = 0, bph ^= 1;
+      }
+    }
+    if (lane == 0) {  // copies in flight land before the CTA can exit
+      for (int j = 0; j < BST; ++j) {
+        bs = bs == 0 ? BST - 1 : bs - 1;
+        if (bs == BST - 1) bph ^= 1;
+        mbar_wait(b_full + bs, bph);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ================= epilogue =================
+    const int q4 = warp & 3;  // the TMEM lane quarter this warp may read
+    uint32_t eph0 = 0, eph1 = 0, buf = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+      const Item it = item_of(i, rtiles, maxnt);
+      const int cnt = W.grp_count[it.grp];
+      if (it.nt * NMAX >= cnt) continue;
+      const int row0 = W.grp_start[it.grp] + it.nt * NMAX;
+      const int ntok = cnt - it.nt * NMAX < NMAX ? cnt - it.nt * NMAX : NMAX;
+      const int r0 = it.rt * BM;
+      uint32_t& eph = buf ? eph1 : eph0;
+      ok = warp_wait(acc_full + buf, eph, abort);
       if (!ok) break;
       eph ^= 1;
       tc_fence_after();
       const int r = r0 + 32 * q4 + lane;  // this thread's weight row (its TMEM lane)
-      const uint32_t lane_base = tmem + (uint32_t(32 * q4) << 16);
-      for (int c0 = 16 * chalf; c0 < NT; c0 += 32) {
-        uint32_t g[16];
+      const uint32_t lane_base = tmem + (uint32_t(32 * q4) << 16) + buf * acc_cols<MAT>();
+      const int pr = batched::perm_pos<BITS>(r);
+      for (int c0 = 0; c0 < ntok; c0 += 16) {
+        uint32_t g[16], g1[16];
         tc_ld16(lane_base + c0, g);
+        tc_ld16(lane_base + NMAX + c0, g1);
         if (MAT == 0) {
-          uint32_t u[16];
-          tc_ld16(lane_base + NMAX + c0, u);
+          uint32_t u[16], u1[16];
+          tc_ld16(lane_base + 2 * NMAX + c0, u);
+          tc_ld16(lane_base + 3 * NMAX + c0, u1);
           tc_wait_ld();
-          const int pr = batched::perm_pos<BITS>(r);
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             if (c0 + c < ntok) {
-              float a = silu_mul(__uint_as_float(g[c]), __uint_as_float(u[c]));
+              const float gs = __uint_as_float(g[c]) + __uint_as_float(g1[c]), us = __uint_as_float(u[c]) + __uint_as_float(u1[c]);
+              float a = silu_mul(gs, us);
               if (!(fabsf(a) <= 65504.0f)) {  // outside fp16 (or NaN): saturate and say so
                 flag(WISP_STATUS_RANGE);
                 a = a != a ? 0.0f : copysignf(65504.0f, a);
@@ -510,19 +591,20 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
           tc_wait_ld();
 #pragma unroll
           for (int c = 0; c < 16; ++c)
-            if (c0 + c < ntok) W.y[int64_t(row0 + c0 + c) * S.H + r] = __uint_as_float(g[c]);
+            if (c0 + c < ntok) W.y[int64_t(row0 + c0 + c) * S.H + r] = __uint_as_float(g[c]) + __uint_as_float(g1[c]);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive1(acc_empty);
+      if (lane == 0) mbar_arrive1(acc_empty + buf);
+      buf ^= 1;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols<MAT>()) : "memory");
   }
 }
 

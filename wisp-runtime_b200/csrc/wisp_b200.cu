@@ -867,7 +867,8 @@ int wisp_qk_norm_rope_kv(const uint16_t* qkv, int Hq, int Hk, int D, const uint1
   WISP_REQUIRE(Hq > 0 && Hk > 0 && D > 0 && D % 2 == 0 && D <= dec::QK_MAX_D && tmax > 0, "wisp_qk_norm_rope_kv: bad shape");
   const int heads = Hq + 2 * Hk;
   const cudaError_t e = launch_pdl(dec::qk_norm_rope_kv_kernel, (heads + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream), qkv, Hq,
-                                   Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax, q_out, k_cache, v_cache, int64_t(0));
+                                   Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax, q_out, k_cache, v_cache, int64_t(0), 0, 1,
+                                   int64_t(0));
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_qk_norm_rope_kv: %s", cudaGetErrorString(e));
   return check_launch("qk_norm_rope_kv");
 }
@@ -882,9 +883,26 @@ int wisp_qk_norm_rope_kv_rows(const uint16_t* qkv, int T, int64_t qkv_stride, in
                "wisp_qk_norm_rope_kv_rows: need 1 <= T <= 65535 and qkv_stride >= (Hq + 2 Hk) D");
   const int heads = Hq + 2 * Hk;
   const cudaError_t e = launch_pdl(dec::qk_norm_rope_kv_kernel, dim3((heads + 7) / 8, T), 256, 0, static_cast<cudaStream_t>(stream),
-                                   qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos0, tmax, q_out, k_cache, v_cache, qkv_stride);
+                                   qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos0, tmax, q_out, k_cache, v_cache, qkv_stride, 0, 1,
+                                   int64_t(0));
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_qk_norm_rope_kv_rows: %s", cudaGetErrorString(e));
   return check_launch("qk_norm_rope_kv_rows");
+}
+
+int wisp_qk_norm_rope_kv_batched(const uint16_t* qkv, int B, int64_t qkv_stride, int Hq, int Hk, int D, const uint16_t* qn_w,
+                                 const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, const int64_t* pos,
+                                 int64_t tmax, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream) {
+  WISP_REQUIRE(qkv && cos_t && sin_t && pos && q_out && k_cache && v_cache, "wisp_qk_norm_rope_kv_batched: NULL pointer");
+  WISP_REQUIRE((qn_w == nullptr) == (kn_w == nullptr), "wisp_qk_norm_rope_kv_batched: give both norm weights or neither");
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && D > 0 && D % 2 == 0 && D <= dec::QK_MAX_D && tmax > 0, "wisp_qk_norm_rope_kv_batched: bad shape");
+  WISP_REQUIRE(B >= 1 && B <= 65535 && qkv_stride >= int64_t(Hq + 2 * Hk) * D,
+               "wisp_qk_norm_rope_kv_batched: need 1 <= B <= 65535 and qkv_stride >= (Hq + 2 Hk) D");
+  const int heads = Hq + 2 * Hk;
+  const cudaError_t e = launch_pdl(dec::qk_norm_rope_kv_kernel, dim3((heads + 7) / 8, B), 256, 0, static_cast<cudaStream_t>(stream),
+                                   qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, tmax, q_out, k_cache, v_cache, qkv_stride, 1, 0,
+                                   int64_t(Hk) * tmax * D);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_qk_norm_rope_kv_batched: %s", cudaGetErrorString(e));
+  return check_launch("qk_norm_rope_kv_batched");
 }
 
 int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {
@@ -909,11 +927,41 @@ int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, dec::attn_split_kernel, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, dec::attn_split_kernel, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
+                                     int64_t(0), 0);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
-  e = launch_pdl(dec::attn_combine_kernel, Hq, 128, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out);
+  e = launch_pdl(dec::attn_combine_kernel, Hq, 128, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, 0,
+                 (const float*)nullptr);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_attn");
+}
+
+int64_t wisp_attn_batched_workspace_floats(int B, int Hq, int Hk, int D, int64_t tmax) {
+  if (B < 1 || Hq <= 0 || Hk <= 0 || D <= 0 || tmax <= 0 || Hq % Hk) return -1;
+  return int64_t(B) * Hk * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * (D + 2);
+}
+
+int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache,
+                                 int64_t tmax, const int64_t* pos, int window, const float* sinks, float scale, float* workspace,
+                                 int64_t workspace_floats, uint16_t* out, void* stream) {
+  WISP_REQUIRE(q && k_cache && v_cache && pos && workspace && out, "wisp_gqa_decode_attn_batched: NULL pointer");
+  WISP_REQUIRE(B >= 1 && B <= 65535, "wisp_gqa_decode_attn_batched: need 1 <= B <= 65535");
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && Hq % Hk == 0 && Hq / Hk <= dec::MAX_G,
+               "wisp_gqa_decode_attn_batched: need Hq a multiple of Hk, Hq/Hk <= %d", dec::MAX_G);
+  WISP_REQUIRE(D > 0 && D % 32 == 0 && D <= dec::MAX_D && tmax > 0, "wisp_gqa_decode_attn_batched: need D a multiple of 32, <= %d",
+               dec::MAX_D);
+  WISP_REQUIRE(window >= 0, "wisp_gqa_decode_attn_batched: window must be >= 0");
+  WISP_REQUIRE(workspace_floats >= wisp_attn_batched_workspace_floats(B, Hq, Hk, D, tmax),
+               "wisp_gqa_decode_attn_batched: workspace of %lld floats is too small", (long long)workspace_floats);
+  const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_pdl(dec::attn_split_kernel, dim3(Hk, nchunk, B), dec::ATTN_THREADS, 0, s, q, Hq, Hk, D, k_cache, v_cache, tmax,
+                             pos, scale, workspace, int64_t(Hk) * tmax * D, window);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
+  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), 128, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, window,
+                 sinks);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
+  return check_launch("gqa_decode_attn_batched");
 }
 
 int wisp_attn_decode(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t* qn_w, const uint16_t* kn_w, float eps,

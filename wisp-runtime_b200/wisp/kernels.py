@@ -38,6 +38,8 @@ __all__ = [
     "gemv",
     "qk_norm_rope_kv",
     "qk_norm_rope_kv_rows",
+    "qk_norm_rope_kv_batched",
+    "gqa_decode_attn_batched",
     "gqa_decode_attn",
     "attn_decode",
     "router_topk",
@@ -548,6 +550,50 @@ def qk_norm_rope_kv_rows(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos0, k_
         _stream(qkv),
     )
     return q_out
+
+
+def qk_norm_rope_kv_batched(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, k_cache, v_cache, q_out=None):
+    """One token of each of B sequences: qkv [B, (Hq + 2 Hk) D] at positions pos (int64 [B] on the device)
+    -> q [B, Hq, D]; K/V rows go into the caches [B, Hk, tmax, D].  qn_w = kn_w = None: no q/k norm."""
+    _need_cuda(qkv, pos)
+    _bf16(qkv, cos_t, sin_t, k_cache, v_cache)
+    B = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=qkv.device)
+    tmax = k_cache.shape[-2]
+    _lib.call(
+        "wisp_qk_norm_rope_kv_batched", qkv.data_ptr(), B, qkv.stride(0), Hq, Hk, D, _ptr(qn_w), _ptr(kn_w), float(eps),
+        cos_t.data_ptr(), sin_t.data_ptr(), pos.data_ptr(), tmax, q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        _stream(qkv),
+    )
+    return q_out
+
+
+def attn_batched_workspace(B, Hq, Hk, D, tmax, device):
+    nf = _lib.lib().wisp_attn_batched_workspace_floats(B, Hq, Hk, D, tmax)
+    if nf < 0:
+        raise WispError("attn_batched_workspace: bad shape")
+    return torch.empty(nf, dtype=torch.float32, device=device)
+
+
+def gqa_decode_attn_batched(q, Hq, Hk, D, k_cache, v_cache, pos, scale, window=0, sinks=None, workspace=None, out=None):
+    """q [B, Hq, D] (one token per sequence) over sequence b's cached positions up to pos[b] (int64 [B]),
+    the last ``window`` of them when window > 0; ``sinks`` fp32 [Hq] per-head softmax sinks -> [B, Hq, D]."""
+    _need_cuda(q, k_cache, v_cache, pos)
+    _bf16(q, k_cache, v_cache)
+    B = q.shape[0]
+    tmax = k_cache.shape[-2]
+    if workspace is None:
+        workspace = attn_batched_workspace(B, Hq, Hk, D, tmax, q.device)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    if sinks is not None and (sinks.dtype != torch.float32 or not sinks.is_contiguous()):
+        raise WispError("sinks must be contiguous float32")
+    _lib.call(
+        "wisp_gqa_decode_attn_batched", q.data_ptr(), B, Hq, Hk, D, k_cache.data_ptr(), v_cache.data_ptr(), tmax, pos.data_ptr(),
+        int(window), _ptr(sinks), float(scale), workspace.data_ptr(), workspace.numel(), out.data_ptr(), _stream(q),
+    )
+    return out
 
 
 def attn_workspace(Hq, Hk, D, tmax, device):
