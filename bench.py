@@ -38,16 +38,16 @@ HQ, HK, D, VOCAB = 32, 4, 128, 151936
 N_ROUTES = 16  # moe-stack: distinct seeded routings (tokens) cycled through by the timed steps
 EP_BATCH = 64  # moe-ep: tokens per step over all ranks (config 4 batch)
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up + one down launch (4-bit, this shape),
-# from the ncu capture summarised in profiles/moe_decode_q4_qwen3_gate_up_down_full.md
+# from one ncu capture of the fused decode kernels
 NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
 # DRAM read + write of the batched gate/up and down grids for one 64-token Zipf(1.1) layer (ncu)
 NCU_TRAFFIC_BATCHED_LAYER = 96_768_256 + 3_038_720 + 48_437_504 + 489_472
 # DRAM bytes of the two gpt-oss GEMVs (gate_up + down) of one 20b layer at one token (4 experts), one ncu capture
-# (profiles/moe_gptoss_rows_q4_20b_layer_full.md)
 NCU_TRAFFIC_GPTOSS_LAYER_BS1 = 35_287_552 + 17_679_872
 
 
 GO_L, GO_H, GO_I, GO_E, GO_K = 24, 2880, 2880, 32, 4  # gpt-oss-20b MoE shape (config 5)
+GO_PROMPT, GO_VOCAB, GO_HQ, GO_HK, GO_D, GO_WINDOW = 256, 201088, 64, 8, 64, 128  # gpt-oss-20b decoder (config 5)
 TIMELINE_TOKENS = 24  # decoder with device paging: untimed steps traced with CUDA events after the timed ones
 
 
@@ -58,8 +58,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
-    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack", "moe-ep", "gptoss-moe"])
-    ap.add_argument("--batch", type=int, default=1, help="gptoss-moe: tokens per step (config 5: 1 or 32)")
+    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack", "moe-ep", "gptoss-moe", "gptoss"])
+    ap.add_argument("--batch", type=int, default=1, help="gptoss, gptoss-moe: sequences (tokens) per step (config 5: 1 or 32)")
     ap.add_argument("--layers", type=int, default=48, help="layers (48 = the model; fewer = a small ncu case)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--cache-frac", type=float, default=0.4,
@@ -89,7 +89,7 @@ def parse():
 
 def metric_name(a):
     return {"decoder": "decode tok/s", "moe-stack": "moe decode tok/s", "moe-ep": "batched moe tok/s",
-            "gptoss-moe": "moe decode tok/s"}[a.workload]
+            "gptoss-moe": "moe decode tok/s", "gptoss": "decode tok/s"}[a.workload]
 
 
 def workload_config(a, n):
@@ -128,6 +128,19 @@ def workload_config(a, n):
             "seq_len": 1,
             "parallelism": "replicas" if n > 1 else "single",
             "l2": f"expert working set {GO_L * GO_E * 13.2:.0f} MB >> 126 MB L2; no flush",
+        }
+    if a.workload == "gptoss":
+        return {
+            "workload": f"gpt-oss-20b greedy decode, {a.batch} sequence(s) per step: {GO_L} layers, hidden {GO_H}, "
+            f"{GO_HQ}q/{GO_HK}kv heads x {GO_D} with biases and per-head attention sinks, sliding window {GO_WINDOW} on "
+            f"alternate layers, YaRN rotary, {GO_E} experts top-{GO_K} of intermediate {GO_I} (clamped SwiGLU, biases), "
+            f"{a.bits}-bit g{G} experts all resident, bf16 attention/embeddings, vocab {GO_VOCAB}, {GO_PROMPT}-token seeded "
+            "prompt per sequence, then one greedy token per sequence per step (whole-step CUDA graph)",
+            "model": "gpt-oss-20b-shaped (random init; o_proj and expert down at std 0.02/sqrt(2L))",
+            "global_batch": a.batch * n,
+            "seq_len": GO_PROMPT,
+            "parallelism": "replicas" if n > 1 else "single",
+            "l2": "working set per step (lm_head 1.16 GB + experts) >> 126 MB L2; no flush",
         }
     if a.workload == "moe-ep":
         return {
@@ -449,6 +462,8 @@ def cpu_sample(a, seed=0, distinct=60.0):
         return per * m, EP_BATCH / (per * distinct * L), threads, (
             f"{m} experts in parallel (dequantize + fp32 MLP of the {toks} tokens an expert receives on average) per "
             f"sample; step time = per-expert time x {distinct:.0f} distinct experts per layer x {L} layers, {EP_BATCH} tokens")
+    if a.workload == "gptoss":
+        return cpu_gptoss_sample(a, seed, distinct)
     # gptoss-moe
     n = GO_H * GO_I
     dist_go = distinct if distinct < 60.0 else float(min(GO_E, a.batch * GO_K))
@@ -469,6 +484,66 @@ def cpu_sample(a, seed=0, distinct=60.0):
     return per * m, a.batch / (per * dist_go * GO_L), threads, (
         f"{m} gpt-oss experts in parallel (dequantize + fp32 MLP of {toks} token(s)) per sample; step time = per-expert "
         f"time x {dist_go:.1f} distinct experts per layer x {GO_L} layers, {a.batch} token(s) per step")
+
+
+def cpu_gptoss_sample(a, seed, distinct):
+    """One gpt-oss decoder layer for ``a.batch`` sequences on the host cores: RMSNorm, q/k/v projections with
+    biases, GQA attention with sinks over the context (the window on sliding layers), o projection, router,
+    the distinct experts of the layer (dequantize + fp32 clamped-SwiGLU MLP) in parallel; step time =
+    24 x the layer + the lm_head over the vocabulary (1/16 of its rows timed)."""
+    import numpy as np
+
+    from oracle import wisp_oracle as O
+
+    rng = np.random.default_rng(seed)
+    B = a.batch
+    n = GO_H * GO_I
+    if "gptoss_dec" not in _CPU_WEIGHTS:
+        r = np.random.default_rng(78)
+        qkv = (GO_HQ + 2 * GO_HK) * GO_D
+        _CPU_WEIGHTS["gptoss_dec"] = dict(
+            pool=O.quantize((r.standard_normal((3, n)) * 0.02).astype(np.float32), a.bits, G)[None],
+            wqkv=(r.standard_normal((qkv, GO_H)) * 0.02).astype(np.float32), bqkv=np.zeros(qkv, np.float32),
+            wo=(r.standard_normal((GO_H, GO_HQ * GO_D)) * 0.02).astype(np.float32),
+            wr=(r.standard_normal((GO_E, GO_H)) * 0.02).astype(np.float32),
+            kc=r.standard_normal((GO_HK, GO_PROMPT, GO_D)).astype(np.float32),
+            vc=r.standard_normal((GO_HK, GO_PROMPT, GO_D)).astype(np.float32),
+            head=(r.standard_normal((GO_VOCAB // 16, GO_H)) * 0.02).astype(np.float32))
+    wt = _CPU_WEIGHTS["gptoss_dec"]
+    dist_go = distinct if distinct < 60.0 else float(min(GO_E, B * GO_K))
+    toks = max(1, int(round(B * GO_K / dist_go)))
+    gub, db = np.zeros((1, 2 * GO_I), np.uint16), np.zeros((1, GO_H), np.uint16)
+    x = rng.standard_normal((B, GO_H)).astype(np.float32)
+    xe = rng.standard_normal((toks, GO_H)).astype(np.float32)
+    nw = np.ones(GO_H, np.float32)
+    ex = cpu_pool()
+
+    def attn(b, window):
+        xn = O.rmsnorm(x[b], nw)
+        q = (wt["wqkv"] @ xn + wt["bqkv"])[: GO_HQ * GO_D].reshape(GO_HQ, GO_D)
+        lo = GO_PROMPT - window if window else 0
+        att = O.gqa_decode_attention(q, wt["kc"][:, lo:], wt["vc"][:, lo:], GO_PROMPT - lo - 1, GO_D ** -0.5)
+        hm = x[b] + wt["wo"] @ att.reshape(-1)
+        O.router_topk((wt["wr"] @ O.rmsnorm(hm, nw))[None], GO_K)
+
+    def expert(j):
+        return O.gptoss_ref(wt["pool"], np.zeros((toks, 1), np.int64), np.ones((toks, 1), np.float32), xe, GO_H, GO_I, a.bits,
+                            G, gub, db)
+
+    t0 = time.perf_counter()
+    for window in (GO_WINDOW, 0):  # one sliding and one full layer
+        list(ex.map(lambda b: attn(b, window), range(B)))
+    dense = (time.perf_counter() - t0) / 2
+    m = max(GO_K, min(int(round(dist_go)), os.cpu_count() or 1))
+    per = _parallel_expert_cost(expert, m)
+    t0 = time.perf_counter()
+    wt["head"] @ O.rmsnorm(x, nw).T
+    head = (time.perf_counter() - t0) * 16
+    step = GO_L * (dense + per * dist_go) + head
+    return step, B / step, os.cpu_count() or 1, (
+        f"per sample: {B} sequence(s) through the attention part of one sliding and one full layer (context "
+        f"{GO_PROMPT}), {m} experts in parallel (dequantize + fp32 MLP of {toks} token(s)), lm_head over 1/16 of the vocabulary; "
+        f"step time = {GO_L} x (attention part + per-expert time x {dist_go:.1f} distinct experts) + 16 x the lm_head share")
 
 
 def cpu_tok_s(a, seed=0, distinct=60.0, samples=2):
@@ -745,6 +820,90 @@ class GptOssStack:
 
     def release(self):
         self.graphs = []
+
+
+# ------------------------------------------------------------------------------------------------
+# gptoss workload (config 5: the whole gpt-oss-20b-shaped decoder, bs 1 or 32)
+# ------------------------------------------------------------------------------------------------
+class GptOssDecodeBench:
+    """``a.batch`` sequences decoded greedily through GptOssDecoder (one CUDA graph per step) after a
+    256-token seeded prompt per sequence."""
+
+    def __init__(self, a, device, seed):
+        import torch
+
+        from wisp.gptoss_decoder import GptOssDecoder, GptOssDecoderConfig, GptOssWeights
+
+        self.a, self.B = a, a.batch
+        cfg = GptOssDecoderConfig(bits=a.bits, group=G)
+        t0 = time.perf_counter()
+        self.w = GptOssWeights.random(cfg, device=device, seed=seed)
+        torch.cuda.synchronize()
+        self.build_s = time.perf_counter() - t0
+        tmax = GO_PROMPT + 2 * a.warmup + 2 * a.steps + 16
+        self.dec = GptOssDecoder(self.w, batch=self.B, tmax=tmax)
+        self.nb = self.w.nbytes
+        g = torch.Generator().manual_seed(1000 + seed)
+        ids = torch.randint(0, cfg.vocab, (self.B, GO_PROMPT), generator=g).to(device)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        self.dec.prompt(ids)
+        torch.cuda.synchronize()
+        self.prefill_s = time.perf_counter() - t0
+        self.distinct_seen = []
+
+    def step(self, t):
+        self.dec.step()
+
+    def record_routes(self):
+        import torch
+
+        r = self.dec.routes
+        self.distinct_seen.append(sum(torch.unique(r[l]).numel() for l in range(r.shape[0])) / r.shape[0])
+
+    @property
+    def distinct(self):
+        return statistics.mean(self.distinct_seen) if self.distinct_seen else float(min(GO_E, self.B * GO_K))
+
+    def launches_per_step(self):
+        """This package's kernels per step (torch's top-k / softmax / index ops not counted)."""
+        per_layer = (3 if self.B == 1 else 2) + 1 + 2 + 5  # projections or norms, rotary+cache, attention, moe_gptoss
+        return GO_L * per_layer + (3 if self.B == 1 else 1)
+
+    def e2e_inputs(self):
+        import torch
+
+        return (torch.randint(0, GO_VOCAB, (self.B,), generator=torch.Generator().manual_seed(9)).pin_memory(),
+                torch.empty(self.B, dtype=torch.int64).pin_memory())
+
+    def step_e2e(self, t, inp):
+        tok_host, out_host = inp
+        self.dec.tokens.copy_(tok_host, non_blocking=True)
+        self.dec.graph.replay()
+        out_host.copy_(self.dec.next_token, non_blocking=True)
+
+    def e2e_bytes(self):
+        return 8 * self.B, 8 * self.B
+
+    def step_bytes(self, ctx):
+        """Algorithmic bytes of one step: every dense weight once, the distinct experts of each layer,
+        the embedding rows, and each sequence's cached K/V over its window."""
+        d = GO_HQ * GO_D
+        qkv = (GO_HQ + 2 * GO_HK) * GO_D
+        dense = GO_L * 2 * (qkv * GO_H + qkv + GO_H * d + GO_H + GO_E * GO_H + GO_E + 4 * GO_H + GO_E * 3 * GO_I)
+        dense += 2 * GO_VOCAB * GO_H + 2 * GO_H + self.B * 2 * GO_H
+        kv = sum(self.B * 2 * GO_HK * GO_D * 2 * (min(ctx, GO_WINDOW) if l % 2 == 0 else ctx) for l in range(GO_L))
+        return dense + GO_L * self.distinct * self.nb + kv
+
+    def roofline(self, ms_per_step, peak, peak_src, ctx):
+        b = self.step_bytes(ctx)
+        ach = b / (ms_per_step * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "traffic": None,
+                "kernel": "whole decode step (every kernel of the graph): algorithmic bytes per step / step time",
+                "bytes_per_call": b, "us_per_call": ms_per_step * 1e3, "peak_source": peak_src}
+
+    def release(self):
+        self.dec.graph = None
 
 
 # ------------------------------------------------------------------------------------------------
@@ -1065,7 +1224,7 @@ class EPStack:
         us = ms_per_step / L * 1e3
         ach = bytes_layer / (us * 1e-6) / 1e9
         return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                # ncu, gate/up + down grids of one 64-token Zipf(1.1) layer (profiles/moe_batched_q4_zipf64_gate_up_down_full.md)
+                # ncu, gate/up + down grids of one 64-token Zipf(1.1) layer
                 "traffic": NCU_TRAFFIC_BATCHED_LAYER if world == 1 else None,
                 "kernel": "batched MoE layer (dispatch, grouping, gate/up and down grids, combine) per GPU, timed as the "
                 "step time / layers", "bytes_per_call": bytes_layer, "us_per_call": us, "peak_source": peak_src}
@@ -1100,6 +1259,9 @@ def main():
         bench = EPStack(a, dev, rank, world)
         bench.capture()
         pool, nbytes = bench.pool, bench.nb
+    elif a.workload == "gptoss":
+        bench = GptOssDecodeBench(a, dev, seed=rank)
+        pool, nbytes = None, bench.nb
     elif a.workload == "gptoss-moe":
         bench = GptOssStack(a, dev, seed=rank)
         bench.capture()
@@ -1131,6 +1293,8 @@ def main():
     barrier()
     clocks.window(w0, time.perf_counter())
     ms = e0.elapsed_time(e1)
+    if a.workload == "gptoss":
+        bench.record_routes()
     # e2e: host buffers, copies inside the timed region
     inp = bench.e2e_inputs()
     for t in range(3):
@@ -1154,7 +1318,11 @@ def main():
             if os.environ.get("WISP_TIMELINE_OUT"):
                 with open(os.environ["WISP_TIMELINE_OUT"], "w") as f:
                     json.dump(tl, f)
-    if a.workload in ("gptoss-moe", "moe-ep"):
+    if a.workload == "gptoss":
+        peak, src = load_peaks()
+        src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
+        roof = bench.roofline(ms / a.steps, peak, src, GO_PROMPT + a.warmup + a.steps)
+    elif a.workload in ("gptoss-moe", "moe-ep"):
         peak, src = load_peaks()
         src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
         roof = bench.roofline(ms / a.steps, peak, src) if a.workload == "gptoss-moe" else bench.roofline(ms / a.steps, peak, src, world)
@@ -1169,8 +1337,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = t.tolist()
     if rank == 0:
-        cpu_v, cores, sample = cpu_tok_s(a, distinct=bench.distinct if a.workload in ("moe-ep", "gptoss-moe") else 60.0)
-        tok = a.steps * (EP_BATCH if a.workload == "moe-ep" else (a.batch * world if a.workload == "gptoss-moe" else world))
+        cpu_v, cores, sample = cpu_tok_s(a, distinct=bench.distinct if a.workload in ("moe-ep", "gptoss-moe", "gptoss") else 60.0)
+        tok = a.steps * (EP_BATCH if a.workload == "moe-ep" else (a.batch * world if a.workload in ("gptoss-moe", "gptoss") else world))
         h2d, d2h = bench.e2e_bytes()
         line = {
             "metric": metric_name(a),
@@ -1192,8 +1360,11 @@ def main():
             "gpu_launches": bench.launches_per_step() * a.steps,
             "clocks": clk,
         }
-        if a.workload == "decoder":
+        if a.workload in ("decoder", "gptoss"):
             line["prefill_s"] = bench.prefill_s
+        if a.workload == "gptoss":
+            line["distinct_experts_per_layer"] = bench.distinct
+            line["prefill"] = f"{GO_PROMPT} prompt tokens per sequence fed one position per graph step"
         if a.workload == "decoder" and bench.paged:
             line["paging"] = paging
         if a.workload == "gptoss-moe":

@@ -1,0 +1,100 @@
+"""The gpt-oss-shaped decoder (one CUDA graph per step, B sequences at their own positions) against the
+fp32 restatement of HF GptOss decoding (tests/_gptoss_ref.py, pinned to transformers on the CPU) on the
+decoder's own weights, the experts dequantized from the packed pool.  Routing is forced to the decoder's
+choice (experts and weights) in the reference: the decoder's router logits are bf16, as in HF, and a near-tie
+that bf16 rounding flips, or the percent-level weight change the bf16 logit step makes, would mask every
+other difference; the test bounds how often the two routings disagree and how far the weights move.  Small config: 3 layers (sliding window 8 on layers 0
+and 2), 8 / 2 heads of 64, 8 experts top-4 of H = I = 640, 20 steps past the window."""
+
+import pytest
+import torch
+
+from _gptoss_ref import RefGptOss
+
+pytestmark = pytest.mark.gpu
+TOL = 3e-2  # max |logit error| / max |logit| (bf16 activations, 4-bit experts dequantized alike)
+
+
+def _cfg():
+    from wisp.gptoss_decoder import GptOssDecoderConfig
+
+    return GptOssDecoderConfig(vocab=512, hidden=640, layers=3, heads=8, kv_heads=2, head_dim=64, experts=8, top_k=4, inter=640,
+                               window=8)
+
+
+def _ref_params(w):
+    from wisp import quant
+
+    c = w.cfg
+    H, I, D, Hq, Hk = c.hidden, c.inter, c.head_dim, c.heads, c.kv_heads
+    f = lambda t: t.float().cpu()
+    p = dict(embed=f(w.embed), lm_head=f(w.lm_head), final_norm=f(w.final_norm), layers=[])
+    for l, lw in enumerate(w.layers):
+        q, k, v = f(lw["wqkv"]).split([Hq * D, Hk * D, Hk * D])
+        bq, bk, bv = f(lw["bqkv"]).split([Hq * D, Hk * D, Hk * D])
+        w3 = quant.dequant(w.pool[l * c.experts : (l + 1) * c.experts], H * I, c.bits, c.group).float().cpu()
+        p["layers"].append(dict(
+            in_norm=f(lw["in_norm"]), post_norm=f(lw["post_norm"]), wq=q, bq=bq, wk=k, bk=bk, wv=v, bv=bv, wo=f(lw["wo"]),
+            bo=f(lw["bo"]), sinks=f(lw["sinks"]), router=f(lw["router"]), router_b=f(lw["router_b"]),
+            gate_up=torch.cat([w3[:, 0], w3[:, 1]], 1).view(c.experts, H, 2 * I), gub=f(lw["gub"]),
+            down=w3[:, 2].reshape(c.experts, I, H), db=f(lw["db"])))
+    return p
+
+
+@pytest.fixture(scope="module")
+def weights():
+    from wisp.gptoss_decoder import GptOssWeights
+
+    return GptOssWeights.random(_cfg(), seed=1, expert_std=0.05)
+
+
+@pytest.mark.parametrize("B,start", [(1, [0]), (3, [0, 5, 2])])
+def test_decoder_matches_reference(weights, B, start):
+    from wisp import _lib
+    from wisp.gptoss_decoder import GptOssDecoder, gptoss_rotary_half
+
+    cfg = weights.cfg
+    dec = GptOssDecoder(weights, batch=B, tmax=64)
+    dec.pos.copy_(torch.tensor(start, device="cuda"))
+    cos, sin = gptoss_rotary_half(cfg, dec.tmax, "cpu")
+    ref = RefGptOss(_ref_params(weights), cfg, cos, sin, B, dec.tmax)
+    g = torch.Generator().manual_seed(B)
+    agree = total = 0
+    errs = []
+    _lib.device_status(0)
+    for t in range(20):
+        tok = torch.randint(0, cfg.vocab, (B,), generator=g) if t < 12 else dec.next_token.cpu()  # prompt, then greedy
+        pos = torch.tensor(start) + t
+        got = dec.step(tok.cuda()).float().cpu()
+        forced = (dec.routes.cpu(), dec.rweights.float().cpu())
+        saved = (ref.kc.clone(), ref.vc.clone())
+        _, own, own_w = ref.step(tok, pos)  # the reference's own routing on the same inputs, then its caches put back
+        ref.kc, ref.vc = saved
+        want, _, _ = ref.step(tok, pos, force=forced)
+        errs.append((got - want).abs().max().item() / want.abs().max().item())
+        assert torch.equal(dec.next_token.cpu(), got.argmax(-1)), t
+        for a, b, wa, wb in zip(forced[0].view(-1, cfg.top_k), own.view(-1, cfg.top_k), forced[1].view(-1, cfg.top_k),
+                                own_w.view(-1, cfg.top_k)):
+            agree += len(set(a.tolist()) & set(b.tolist()))
+            if torch.equal(a, b):  # same experts in the same order: the weights agree to bf16 rounding of the logits
+                assert (wa - wb).abs().max().item() < 0.05, (wa, wb)
+        total += forced[0].numel()
+    assert _lib.device_status(0) == 0
+    assert max(errs) < TOL, errs
+    assert agree / total > 0.9, agree / total
+    assert dec.pos.cpu().tolist() == [s + 20 for s in start]
+
+
+def test_graph_matches_eager(weights):
+    """The captured graph and eager launches of the same step give the same bits."""
+    from wisp.gptoss_decoder import GptOssDecoder
+
+    a = GptOssDecoder(weights, batch=2, tmax=64, use_graph=True)
+    b = GptOssDecoder(weights, batch=2, tmax=64, use_graph=False)
+    ids = torch.randint(0, weights.cfg.vocab, (2, 10), generator=torch.Generator().manual_seed(5)).cuda()
+    for t in range(10):
+        la = a.step(ids[:, t].contiguous()).clone()
+        lb = b.step(ids[:, t].contiguous()).clone()
+        assert torch.equal(la, lb), t
+    # the graph's capture warm-up wrote the last cache slot, which a step overwrites before it is read
+    assert torch.equal(a.kc[..., :10, :], b.kc[..., :10, :]) and torch.equal(a.vc[..., :10, :], b.vc[..., :10, :])
