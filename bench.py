@@ -150,7 +150,7 @@ def workload_config(a, n):
             + ("dispatch and combine as kernel stores into peer memory (CUDA IPC over NVLink, flags)"
                if (a.transport == "p2p" or (a.transport == "auto" and n > 1)) else "NCCL all-to-all dispatch and combine")
             + ", rmsnorm+residual between layers (no attention), batched expert products on "
-            + ("the warp-level tensor-core kernels" if a.batched_path == "mma" else "tcgen05 (TMEM accumulators)"),
+            + ("tcgen05 (TMEM accumulators)" if a.batched_path == "tcgen05" else "the warp-level tensor-core kernels"),
             "model": "Qwen3-30B-A3B-shaped (random init)",
             "global_batch": EP_BATCH,
             "seq_len": 1,
@@ -866,9 +866,12 @@ class GptOssDecodeBench:
         return statistics.mean(self.distinct_seen) if self.distinct_seen else float(min(GO_E, self.B * GO_K))
 
     def launches_per_step(self):
-        """This package's kernels per step (torch's top-k / softmax / index ops not counted)."""
-        per_layer = (3 if self.B == 1 else 2) + 1 + 2 + 5  # projections or norms, rotary+cache, attention, moe_gptoss
-        return GO_L * per_layer + (3 if self.B == 1 else 1)
+        """This package's kernels per step (cuBLAS GEMMs, torch's adds and argmax at B > 1 not counted).
+        Per layer: B = 1: two GEMVs, rotary + cache write, attention (2), router, wisp_moe_gptoss (4: the
+        gate_up grid groups the pairs itself); B > 1: RMSNorm, rotary, attention (2), router, wisp_moe_gptoss
+        (5 with its grouping grid).  Per step: embedding, final RMSNorm, lm_head GEMV, argmax (2) at B = 1;
+        the final RMSNorm at B > 1."""
+        return GO_L * 10 + (5 if self.B == 1 else 1)
 
     def e2e_inputs(self):
         import torch

@@ -152,13 +152,14 @@ int wisp_moe_batched(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
 
 /* wisp_moe_batched with an explicit path: 0 = automatic (what wisp_moe_batched does), 1 = the warp-level
  * tensor-core kernels (mma.sync; any supported format), 2 = the 5th-generation tensor cores: per
- * (expert, 128 weight rows, up to 128 tokens) one CTA streams the packed codes through TMA tensor
+ * (expert, 128 weight rows, up to 64 tokens) one CTA streams the packed codes through TMA tensor
  * loads, dequantizes them once into fp16 (q*s + m with a single rounding) in the 128-byte-swizzled
  * K-major layout, and one thread issues tcgen05.mma (M = 128, N = the expert's tokens, fp32
  * accumulators in TMEM) for gate and up, then down; the activations and the intermediate enter as
  * fp16 (values outside fp16's range saturate and set WISP_STATUS_RANGE).  Path 2 needs 4-bit or
  * 2-bit codes and groups a multiple of 128 dividing H and I (WISP_ERR_UNSUPPORTED otherwise).
- * Automatic = 2 when it applies, else 1.  Same replacement as wisp_moe_batched (wisp/moe.py:62-137). */
+ * Automatic = 1 (measured faster on the 64-token Zipf layer).  Same replacement as wisp_moe_batched
+ * (wisp/moe.py:62-137). */
 int wisp_moe_batched_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int N, int k, const uint16_t* x,
                              int64_t H, int64_t I, int bits, int group, void* workspace, int64_t workspace_bytes, uint16_t* out,
                              int variant, void* stream);
@@ -270,6 +271,14 @@ int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t
 int wisp_gemv(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const uint16_t* x_add, uint16_t* x_sum_out,
               const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* res, uint16_t* y, void* stream);
 
+/* wisp_gemv with a bias: y[n] = bf16(W[n,:] . x' + bias[n]) (fp32 sum and bias, one rounding, as a bf16
+ * nn.Linear with bias gives), then y[n] = bf16(res[n] + y[n]) when res is given.  bias may be NULL.
+ * Replaces the biased projections of gpt-oss attention (q/k/v/o with attention_bias, HF
+ * GptOssAttention as loaded by wisp/gptoss.py:146-183). */
+int wisp_gemv_bias(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const uint16_t* x_add, uint16_t* x_sum_out,
+                   const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* bias, const uint16_t* res, uint16_t* y,
+                   void* stream);
+
 /* Per-head RMSNorm of the q and k heads of qkv = [Hq*D | Hk*D | Hk*D] (weights qn_w, kn_w [D]),
  * rotate-half rotary with cos/sin rows `*pos` of the [tmax, D] tables (fp32 math, one rounding), q to
  * q_out [Hq, D], k and v into row `*pos` of the caches [Hk, tmax, D].  *pos outside [0, tmax) writes
@@ -341,6 +350,19 @@ int wisp_attn_decode(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t*
  * Replaces wisp/graphdec.py:177-182 and wisp/moe.py:67-72 (softmax, topk, renormalise, bf16). */
 int wisp_router_topk(const uint16_t* logits, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* row,
                      float* meta, void* stream);
+
+/* Router of B tokens in one launch, one CTA per token: xn = RMSNorm(x[b]) * norm_w (wisp_rmsnorm's
+ * rounding; norm_w NULL: xn = x) stored to xn_out [B, H] (nullable), logits[e] = bf16(xn . W[e] + bias[e])
+ * (W [E, H] bf16, bias [E] nullable; fp32 sum, one rounding), then wisp_router_topk's selection and
+ * weights (norm_topk 0, 1 or 2).  meta [B, 2k] = [k slots | k weights] (slot = slot_table[base + e]
+ * or base + e); experts [B, k] int32 expert ids (nullable); row [B, 2k] fp32 [k ids | k weights]
+ * (nullable).  H % 8 == 0, H <= 8192, E <= 1024, k <= 32; x, W, norm_w, xn_out 16-byte aligned.
+ * Replaces the router of a batched decode step: gpt-oss (post-attention RMSNorm, F.linear with bias,
+ * topk, softmax over the k: wisp/gptoss.py:116-123) and Qwen3-MoE (gate, softmax, topk, renormalise:
+ * wisp/moe.py:67-72). */
+int wisp_router_rows(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* W,
+                     const uint16_t* bias, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* meta,
+                     int32_t* experts, float* row, void* stream);
 
 /* out [H] = table[*token] (bf16 rows, H % 8 == 0).  *token outside [0, V) sets WISP_STATUS_BAD_ROUTE. */
 int wisp_embed(const uint16_t* table, int64_t V, int64_t H, const int64_t* token, uint16_t* out, void* stream);

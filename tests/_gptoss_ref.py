@@ -56,10 +56,9 @@ class RefGptOss:
     def _moe(self, l, x, force=None):
         c, lw = self.c, self.p["layers"][l]
         logits = x @ lw["router"].T + lw["router_b"]
-        tv, ti = torch.topk(logits, c.top_k, dim=-1)
-        w = torch.softmax(tv, -1)
-        if force is not None:
-            ti, w = force[0].to(torch.int64), force[1].float()
+        tv, own = torch.topk(logits, c.top_k, dim=-1)
+        own_w = torch.softmax(tv, -1)
+        ti, w = (own, own_w) if force is None else (force[0].to(torch.int64), force[1].float())
         y = torch.zeros_like(x)
         for t in range(x.shape[0]):
             for j in range(c.top_k):
@@ -69,11 +68,12 @@ class RefGptOss:
                 up = gu[1::2].clamp(-7.0, 7.0)
                 act = (up + 1) * gate * torch.sigmoid(gate * 1.702)
                 y[t] += w[t, j] * (act @ lw["down"][e] + lw["db"][e])
-        return y, ti, w
+        return y, own, own_w
 
     @torch.no_grad()
     def step(self, tokens, pos, force=None):
-        """tokens [B], pos [B] -> (logits [B, V], routes [L, B, k], weights [L, B, k])."""
+        """tokens [B], pos [B] -> (logits [B, V], routes [L, B, k], weights [L, B, k]); the routes and weights
+        are the reference's own top-k and softmax at each layer, also when ``force`` replaced them."""
         c, p = self.c, self.p
         h = p["embed"][tokens]
         routes, weights = [], []

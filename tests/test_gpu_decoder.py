@@ -17,17 +17,19 @@ class PoolMoE(nn.Module):
     """HF-side MoE block: the layer's router + experts dequantized from the packed pool (the math of
     the reference PagedMoEBlock's non-fused path, wisp/moe.py:62-137, in fp32)."""
 
-    def __init__(self, gate_w, pool, layer, cfg):
+    def __init__(self, gate_w, pool, layer, cfg, gate_b=None):
         super().__init__()
         from wisp import quant
 
         E, H, I = cfg.experts, cfg.hidden, cfg.moe_inter
-        self.gate = nn.Linear(H, E, bias=False).to(device=gate_w.device, dtype=gate_w.dtype)
+        self.gate = nn.Linear(H, E, bias=gate_b is not None).to(device=gate_w.device, dtype=gate_w.dtype)
         self.gate.weight.data.copy_(gate_w)
+        if gate_b is not None:
+            self.gate.bias.data.copy_(gate_b)
         deq = quant.dequant(pool[layer * E : (layer + 1) * E], H * I, cfg.bits, cfg.group).float()
         self.wg, self.wu, self.wd = deq[:, 0].view(E, I, H), deq[:, 1].view(E, I, H), deq[:, 2].view(E, H, I)
         self.k, self.norm_topk = cfg.top_k, cfg.norm_topk
-        self.forced = None  # (experts, weights) of one token: replay another router's choice
+        self.forced = None  # (experts, weights) of one token ([k]) or of every token ([N, k]): replay another router's choice
         self.margin = 0.0  # how far the replayed choice is from HF's own top-k (probability units)
 
     def forward(self, h):
@@ -37,13 +39,17 @@ class PoolMoE(nn.Module):
         if self.norm_topk:
             rw = rw / rw.sum(-1, keepdim=True)
         rw = rw.to(x.dtype).float()
-        if self.forced is not None and x.shape[0] == 1:
+        if self.forced is not None:
             fsel, frw = self.forced
-            chosen = torch.zeros_like(p[0], dtype=torch.bool)
-            chosen[fsel] = True
-            # > 0 when an expert outside HF's own choice beats one inside it
-            self.margin = max(0.0, (p[0][~chosen].max() - p[0][chosen].min()).item())
-            sel, rw = fsel[None], frw[None].float()
+            fsel, frw = (fsel[None], frw[None]) if fsel.dim() == 1 else (fsel, frw)
+            assert fsel.shape[0] == x.shape[0]
+            self.margin = 0.0
+            for i in range(x.shape[0]):
+                chosen = torch.zeros_like(p[i], dtype=torch.bool)
+                chosen[fsel[i]] = True
+                # > 0 when an expert outside HF's own choice beats one inside it
+                self.margin = max(self.margin, (p[i][~chosen].max() - p[i][chosen].min()).item())
+            sel, rw = fsel, frw.float()
         out = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
         xf = x.float()
         for i in range(x.shape[0]):

@@ -72,6 +72,61 @@ def test_gemv_fused_residual_norm(K):
     assert (y.float() - ref).abs().max().item() <= 2.0**-6 * ref.abs().max().item()
 
 
+@pytest.mark.parametrize("N,K", [(5120, 2880), (2880, 4096)])
+def test_gemv_bias_and_residual(N, K):
+    """y = bf16(res + bf16(W x + bias)): the biased gpt-oss projections (fp32 sum and bias, one rounding)."""
+    from wisp import kernels
+
+    g = _gen(N + 7)
+    W = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(K, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(N, device="cuda", generator=g).to(torch.bfloat16)
+    res = torch.randn(N, device="cuda", generator=g).to(torch.bfloat16)
+    lin = (W.float() @ x.float() + b.float()).to(torch.bfloat16).float()
+    y = kernels.gemv(W, x, bias=b)
+    assert (y.float() - lin).abs().max().item() <= 2.0**-7 * lin.abs().max().item()
+    y2 = kernels.gemv(W, x, bias=b, res=res)
+    want = (res.float() + y.float()).to(torch.bfloat16)
+    assert torch.equal(y2, want)  # the residual add is one bf16 add on the same biased product
+
+
+@pytest.mark.parametrize("B,H,E,k,mode", [(1, 2880, 32, 4, "selected"), (32, 2880, 32, 4, "selected"), (5, 2048, 128, 8, True),
+                                          (3, 64, 8, 2, False)])
+def test_router_rows(B, H, E, k, mode):
+    """RMSNorm + biased gate + top-k + weights for B tokens in one launch, against torch fp32 with the
+    kernel's rounding steps; the selection and weights also against the single-token router kernel on
+    the same logits."""
+    from wisp import kernels
+
+    g = _gen(B * 1000 + E)
+    x = torch.randn(B, H, device="cuda", generator=g).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
+    W = (torch.randn(E, H, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(E, device="cuda", generator=g) * 0.1).to(torch.bfloat16) if mode == "selected" else None
+    xn = torch.empty_like(x)
+    experts = torch.empty(B, k, dtype=torch.int32, device="cuda")
+    row = torch.empty(B, 2 * k, dtype=torch.float32, device="cuda")
+    meta = kernels.router_rows(x, W, k, mode, norm_w=nw, eps=1e-5, bias=bias, xn_out=xn, base=7 * E, experts=experts, row=row)
+    xs = x.float()
+    inv = torch.rsqrt((xs * xs).mean(-1, keepdim=True) + 1e-5)
+    xn_ref = (nw.float() * (xs * inv).to(torch.bfloat16).float()).to(torch.bfloat16)
+    assert (xn.float() - xn_ref.float()).abs().max().item() <= 2.0**-7 * xn_ref.float().abs().max().item()
+    logits = xn.float() @ W.float().t() + (0 if bias is None else bias.float())
+    lg = logits.to(torch.bfloat16)
+    for b in range(B):
+        want = torch.empty(2 * k, dtype=torch.float32, device="cuda")
+        kernels.router_topk(lg[b].contiguous(), k, mode, row=want)
+        # the kernel's own logits may differ from torch's by one bf16 step; compare where the top-k has
+        # no near-tie at that resolution
+        srt = lg[b].float().sort(descending=True).values
+        if (srt[k - 1] - srt[k]).abs().item() > 2 * 2.0**-7 * srt[0].abs().item():
+            assert set(row[b, :k].long().tolist()) == set(want[:k].long().tolist()), b
+            assert (row[b, k:].sort().values - want[k:].sort().values).abs().max().item() <= 0.02
+    assert torch.equal(experts.long(), row[:, :k].long())
+    assert torch.equal(meta[:, :k].long(), row[:, :k].long() + 7 * E) and torch.equal(meta[:, k:], row[:, k:])
+    assert torch.allclose(row[:, k:].sum(-1), torch.ones(B, device="cuda"), atol=2e-2) or mode is False
+
+
 def test_gemv_rejects_aliasing():
     from wisp import kernels
     from wisp._lib import WispError

@@ -12,7 +12,7 @@ import torch
 from _gptoss_ref import RefGptOss
 
 pytestmark = pytest.mark.gpu
-TOL = 3e-2  # max |logit error| / max |logit| (bf16 activations, 4-bit experts dequantized alike)
+TOL = 2e-2  # max |logit error| / max |logit| (bf16 activations, 4-bit experts dequantized alike; measured <= 1e-2)
 
 
 def _cfg():
@@ -67,17 +67,14 @@ def test_decoder_matches_reference(weights, B, start):
         pos = torch.tensor(start) + t
         got = dec.step(tok.cuda()).float().cpu()
         forced = (dec.routes.cpu(), dec.rweights.float().cpu())
-        saved = (ref.kc.clone(), ref.vc.clone())
-        _, own, own_w = ref.step(tok, pos)  # the reference's own routing on the same inputs, then its caches put back
-        ref.kc, ref.vc = saved
-        want, _, _ = ref.step(tok, pos, force=forced)
+        want, own, own_w = ref.step(tok, pos, force=forced)  # own: the reference's top-k on the same layer inputs
         errs.append((got - want).abs().max().item() / want.abs().max().item())
         assert torch.equal(dec.next_token.cpu(), got.argmax(-1)), t
         for a, b, wa, wb in zip(forced[0].view(-1, cfg.top_k), own.view(-1, cfg.top_k), forced[1].view(-1, cfg.top_k),
                                 own_w.view(-1, cfg.top_k)):
             agree += len(set(a.tolist()) & set(b.tolist()))
             if torch.equal(a, b):  # same experts in the same order: the weights agree to bf16 rounding of the logits
-                assert (wa - wb).abs().max().item() < 0.05, (wa, wb)
+                assert (wa - wb).abs().max().item() < 0.02, (wa, wb)
         total += forced[0].numel()
     assert _lib.device_status(0) == 0
     assert max(errs) < TOL, errs

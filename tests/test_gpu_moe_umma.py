@@ -75,7 +75,7 @@ def test_qwen3_layer_paths_match_oracle(bits, N, zipf):
 
 @pytest.mark.parametrize("bits", [4, 2])
 def test_expert_with_several_token_tiles(bits):
-    """One expert receives 300 tokens (N tiles of 128, 128 and 44), another 17, with k = 1."""
+    """One expert receives 300 tokens (four N tiles of 64 and one of 44), another 17, with k = 1."""
     from wisp import _lib, kernels
 
     H, I, E, k, G = 256, 128, 4, 1, 128

@@ -10,10 +10,13 @@
 // The position and the token are read from device memory, so one captured graph serves every step.
 #pragma once
 #include "common.cuh"
+#include "dense.cuh"
 #include "tma.cuh"
 
 namespace wisp {
 namespace dec {
+using dense::bf_hi;
+using dense::bf_lo;
 
 constexpr int CHUNK = 64;       // positions per attention CTA
 constexpr int ATTN_THREADS = 128;
@@ -98,9 +101,15 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
                                                                   const uint16_t* __restrict__ vc, int64_t tmax,
                                                                   const int64_t* __restrict__ pos_ptr, float scale,
                                                                   float* __restrict__ part, int64_t kv_bstride, int window) {
-  __shared__ float qs[MAX_G][MAX_D];
+  // the chunk's K and V rows are contiguous in the cache ([Hk, tmax, D] per sequence): both are copied
+  // into shared memory first with 16-byte loads all in flight at once, so the score and P V loops
+  // below wait on shared-memory latency instead of one dependent HBM load per position
+  __shared__ __align__(16) uint16_t kvs[2][CHUNK * MAX_D];
+  __shared__ __align__(16) float qs[MAX_G][MAX_D];
   __shared__ float ps[MAX_G][CHUNK];
-  __shared__ float red[ATTN_THREADS / 32][MAX_G][MAX_D];  // per-warp P V sums, lane-major
+  // per-warp P V sums, lane-major; they reuse the K rows, which are dead once the scores are taken
+  static_assert(sizeof(float) * (ATTN_THREADS / 32) * MAX_G * MAX_D <= sizeof(uint16_t) * CHUNK * MAX_D, "red fits in K");
+  float (*red)[MAX_G][MAX_D] = reinterpret_cast<float (*)[MAX_G][MAX_D]>(&kvs[0][0]);
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int G = Hq / Hk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = ATTN_THREADS / 32;
@@ -116,24 +125,62 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
   kc += int64_t(b) * kv_bstride;
   vc += int64_t(b) * kv_bstride;
   part += int64_t(b) * Hk * gridDim.y * G * (D + 2);
+  {
+    const uint4* kg = reinterpret_cast<const uint4*>(kc + (int64_t(h) * tmax + t0) * D);
+    const uint4* vg = reinterpret_cast<const uint4*>(vc + (int64_t(h) * tmax + t0) * D);
+    uint4* ks4 = reinterpret_cast<uint4*>(&kvs[0][0]);
+    uint4* vs4 = reinterpret_cast<uint4*>(&kvs[1][0]);
+    const int nv = n * D / 8;  // 16-byte pieces of n rows (D % 32 == 0)
+    constexpr int PER = CHUNK * MAX_D / 8 / ATTN_THREADS;
+    uint4 kr[PER], vr[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = threadIdx.x + j * ATTN_THREADS;
+      if (i < nv) {
+        kr[j] = kg[i];
+        vr[j] = vg[i];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = threadIdx.x + j * ATTN_THREADS;
+      if (i < nv) {
+        ks4[i] = kr[j];
+        vs4[i] = vr[j];
+      }
+    }
+  }
   // q of the G heads, pre-scaled, fp32
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i / D][i % D] = bf16_to_f32(q[(int64_t(h) * G) * D + i]) * scale;
   __syncthreads();
-  const uint16_t* kb = kc + (int64_t(h) * tmax + t0) * D;
-  const uint16_t* vb = vc + (int64_t(h) * tmax + t0) * D;
+  const uint16_t* kb = &kvs[0][0];
+  const uint16_t* vb = &kvs[1][0];
   const int dpl = D / 32;  // elements of a row per lane (D % 32 == 0, D <= MAX_D)
-  // scores: warp w takes positions w, w + 4, ...; lanes split the row
-  for (int t = warp; t < n; t += nw) {
-    float kv[MAX_D / 32];
+  // scores: each thread takes whole dot products, positions lane, lane + 32 and heads warp, warp + 4, ...
+  // (no cross-lane reductions on the critical path); lane l starts its row at word l, so the lanes of a
+  // warp read distinct banks of their different rows
+  {
+    const int hw = D / 2;  // 32-bit words (bf16 pairs) of a row
+    for (int g = warp; g < G; g += nw) {
+      const float2* qg = reinterpret_cast<const float2*>(&qs[g][0]);
 #pragma unroll
-    for (int e = 0; e < MAX_D / 32; ++e) kv[e] = e < dpl ? bf16_to_f32(kb[int64_t(t) * D + lane * dpl + e]) : 0.0f;
-    for (int g = 0; g < G; ++g) {
-      float s = 0.0f;
-#pragma unroll
-      for (int e = 0; e < MAX_D / 32; ++e)
-        if (e < dpl) s = fmaf(qs[g][lane * dpl + e], kv[e], s);
-      s = warp_sum(s);
-      if (lane == 0) ps[g][t] = s;
+      for (int i = 0; i < CHUNK / 32; ++i) {
+        const int t = lane + 32 * i;
+        if (t < n) {
+          const uint32_t* kr = reinterpret_cast<const uint32_t*>(kb + t * D);
+          float s0 = 0.0f, s1 = 0.0f;
+          int j = lane % hw;
+#pragma unroll 8
+          for (int c = 0; c < hw; ++c) {
+            const uint32_t kv = kr[j];
+            const float2 qv = qg[j];
+            s0 = fmaf(qv.x, bf_lo(kv), s0);
+            s1 = fmaf(qv.y, bf_hi(kv), s1);
+            j = j + 1 == hw ? 0 : j + 1;
+          }
+          ps[g][t] = s0 + s1;
+        }
+      }
     }
   }
   __syncthreads();
@@ -165,7 +212,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
   for (int t = warp; t < n; t += nw) {
     float vv[MAX_D / 32];
 #pragma unroll
-    for (int e = 0; e < MAX_D / 32; ++e) vv[e] = e < dpl ? bf16_to_f32(vb[int64_t(t) * D + lane * dpl + e]) : 0.0f;
+    for (int e = 0; e < MAX_D / 32; ++e) vv[e] = e < dpl ? bf16_to_f32(vb[t * D + lane * dpl + e]) : 0.0f;
 #pragma unroll
     for (int g = 0; g < MAX_G; ++g) {
       if (g < G) {
@@ -490,18 +537,13 @@ __global__ void __launch_bounds__(FTHREADS)
 // -> bf16.  row (nullable) = [experts as float..., weights...]; meta = [slots..., weights...] with
 // slot = slot_table[base + e] when a table is given (a negative entry is passed through and the MoE
 // kernels skip and flag it), else base + e.
-__global__ void router_topk_kernel(const uint16_t* __restrict__ logits, int E, int k, int norm_topk,
-                                   const int32_t* __restrict__ slot_table, int64_t base, float* __restrict__ row,
-                                   float* __restrict__ meta) {
-  __shared__ float p[1024];
-  const int lane = threadIdx.x;
-  pdl_wait();
-  pdl_launch_dependents();
+// Top-k of one token's router logits held (as fp32 values of bf16 logits) in p[0..E) of shared memory,
+// by one warp; p is overwritten.  norm_topk 0: softmax over all E in fp32, the k largest; 1: the same,
+// renormalised over the k; 2 (gpt-oss, wisp/gptoss.py:122-123): softmax over the k selected logits
+// only.  Lane j < k gets the j-th expert (ties: lower expert id) and its weight rounded to bf16.
+__device__ __forceinline__ void topk_weights(float* p, int E, int k, int norm_topk, int lane, int& sele, float& w) {
   float m = -INFINITY;
-  for (int e = lane; e < E; e += 32) {
-    p[e] = bf16_to_f32(logits[e]);
-    m = fmaxf(m, p[e]);
-  }
+  for (int e = lane; e < E; e += 32) m = fmaxf(m, p[e]);
   m = warp_max(m);
   float s = 0.0f;
   for (int e = lane; e < E; e += 32) {
@@ -513,7 +555,7 @@ __global__ void router_topk_kernel(const uint16_t* __restrict__ logits, int E, i
   for (int e = lane; e < E; e += 32) p[e] = p[e] / s;
   __syncwarp();
   float selw = 0.0f, tot = 0.0f;
-  int sele = 0;
+  sele = 0;
   for (int j = 0; j < k; ++j) {
     float bv = -1.0f;
     int be = E;
@@ -530,18 +572,31 @@ __global__ void router_topk_kernel(const uint16_t* __restrict__ logits, int E, i
     if (lane == 0) p[be] = -2.0f;
     __syncwarp();
   }
-  // norm_topk 2 (gpt-oss, wisp/gptoss.py:122-123): softmax over the k selected logits only
+  // norm_topk 2: p = e^(l - m) / s is monotone in l, so the selected probabilities give back the
+  // logits' ratios: e^(l_j - l_max) = p_j / p_max
   float sm_w = 0.0f;
   if (norm_topk == 2) {
-    // p = e^(l - m) / s is monotone in l, so the selected probabilities give back the logits' ratios:
-    // e^(l_j - l_max) = p_j / p_max
     const float pmax = __shfl_sync(0xffffffffu, selw, 0);  // the first pick is the largest
-    float r = lane < k ? selw / pmax : 0.0f;
-    float rs = warp_sum(r);
+    const float r = lane < k ? selw / pmax : 0.0f;
+    const float rs = warp_sum(r);
     sm_w = r / rs;
   }
+  w = bf16_to_f32(f32_to_bf16(norm_topk == 2 ? sm_w : (norm_topk ? selw / tot : selw)));
+}
+
+__global__ void router_topk_kernel(const uint16_t* __restrict__ logits, int E, int k, int norm_topk,
+                                   const int32_t* __restrict__ slot_table, int64_t base, float* __restrict__ row,
+                                   float* __restrict__ meta) {
+  __shared__ float p[1024];
+  const int lane = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int e = lane; e < E; e += 32) p[e] = bf16_to_f32(logits[e]);
+  __syncwarp();
+  int sele;
+  float w;
+  topk_weights(p, E, k, norm_topk, lane, sele, w);
   if (lane < k) {
-    const float w = bf16_to_f32(f32_to_bf16(norm_topk == 2 ? sm_w : (norm_topk ? selw / tot : selw)));
     if (row) {
       row[lane] = float(sele);
       row[k + lane] = w;
@@ -549,6 +604,100 @@ __global__ void router_topk_kernel(const uint16_t* __restrict__ logits, int E, i
     const int64_t slot = slot_table ? int64_t(slot_table[base + sele]) : base + sele;
     meta[lane] = float(slot);
     meta[k + lane] = w;
+  }
+}
+
+// ---- the router of B tokens in one launch: RMSNorm, gate logits, top-k ------------------------------
+// One CTA per token b: xn = RMSNorm(x[b]) * norm_w (the rounding of wisp_rmsnorm; stored to xn_out,
+// the experts' input), logits[e] = bf16(xn . W[e] + bias[e]) in fp32 (one rounding, as a bf16 linear
+// layer with bias gives), then topk_weights.  Writes meta[b] = [k slots | k weights] (slot =
+// slot_table[base + e] or base + e), experts[b] = the k expert ids (int32, nullable) and row[b] =
+// [k ids | k weights] in fp32 (nullable).  H % 8 == 0, H <= ROUTER_MAX_H, E <= 1024, k <= 32.
+constexpr int ROUTER_THREADS = 1024;  // one warp per expert for E <= 32: a row's loads are all in flight at once
+constexpr int ROUTER_MAX_H = 8192;
+__global__ void __launch_bounds__(ROUTER_THREADS) router_rows_kernel(
+    const uint16_t* __restrict__ x, int64_t H, const uint16_t* __restrict__ norm_w, float eps, uint16_t* __restrict__ xn_out,
+    const uint16_t* __restrict__ W, const uint16_t* __restrict__ bias, int E, int k, int norm_topk,
+    const int32_t* __restrict__ slot_table, int64_t base, float* __restrict__ meta, int32_t* __restrict__ experts,
+    float* __restrict__ row) {
+  __shared__ __align__(16) uint16_t xs[ROUTER_MAX_H];
+  __shared__ float p[1024];
+  __shared__ float red[ROUTER_THREADS / 32];
+  const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NW = ROUTER_THREADS / 32;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t nch = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(b) * H);
+  float ss = 0.0f;
+  for (int64_t c = threadIdx.x; c < nch; c += ROUTER_THREADS) {
+    const uint4 v = xr[c];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss += bf_lo(w4[i]) * bf_lo(w4[i]) + bf_hi(w4[i]) * bf_hi(w4[i]);
+    reinterpret_cast<uint4*>(xs)[c] = v;
+  }
+  if (norm_w) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) tot += red[w];
+    const float inv = rsqrtf(tot / float(H) + eps);
+    for (int64_t c = threadIdx.x; c < nch; c += ROUTER_THREADS) {
+      const uint4 v = reinterpret_cast<const uint4*>(xs)[c];
+      const uint4 wv = reinterpret_cast<const uint4*>(norm_w)[c];
+      const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = bf_lo(ww[i]) * bf16_to_f32(f32_to_bf16(bf_lo(xv[i]) * inv));
+        const float hi = bf_hi(ww[i]) * bf16_to_f32(f32_to_bf16(bf_hi(xv[i]) * inv));
+        o[i] = uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
+      }
+      const uint4 on = make_uint4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<uint4*>(xs)[c] = on;
+      if (xn_out) reinterpret_cast<uint4*>(xn_out + int64_t(b) * H)[c] = on;
+    }
+  } else if (xn_out) {
+    for (int64_t c = threadIdx.x; c < nch; c += ROUTER_THREADS)
+      reinterpret_cast<uint4*>(xn_out + int64_t(b) * H)[c] = reinterpret_cast<const uint4*>(xs)[c];
+  }
+  __syncthreads();
+  // gate logits: warp w takes experts w, w + NW, ...; lanes split the row
+  const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
+  for (int e = warp; e < E; e += NW) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + int64_t(e) * H);
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 8
+    for (int64_t c = lane; c < nch; c += 32) {
+      const uint4 w = __ldg(wr + c), xv4 = xs4[c];
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w}, xv[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        a0 = fmaf(bf_lo(wv[q]), bf_lo(xv[q]), a0);
+        a1 = fmaf(bf_hi(wv[q]), bf_hi(xv[q]), a1);
+      }
+    }
+    const float acc = warp_sum(a0 + a1);
+    if (lane == 0) p[e] = bf16_to_f32(f32_to_bf16(acc + (bias ? bf16_to_f32(bias[e]) : 0.0f)));
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int sele;
+    float w;
+    topk_weights(p, E, k, norm_topk, lane, sele, w);
+    if (lane < k) {
+      const int64_t slot = slot_table ? int64_t(slot_table[base + sele]) : base + sele;
+      meta[int64_t(b) * 2 * k + lane] = float(slot);
+      meta[int64_t(b) * 2 * k + k + lane] = w;
+      if (experts) experts[int64_t(b) * k + lane] = sele;
+      if (row) {
+        row[int64_t(b) * 2 * k + lane] = float(sele);
+        row[int64_t(b) * 2 * k + k + lane] = w;
+      }
+    }
   }
 }
 

@@ -9,7 +9,7 @@
 //
 // Fused around the product (all optional): x := bf16(x + x_add) (the residual add of the previous
 // sub-layer, stored once to x_sum_out), x := RMSNorm(x) * norm_w (stored once to xn_out), and
-// y := bf16(res + bf16(W x)) (this sub-layer's residual add).  Every CTA reads all of x while CTA 0
+// y := bf16(res + bf16(W x [+ bias])) (the layer's bias and this sub-layer's residual add).  Every CTA reads all of x while CTA 0
 // writes x_sum_out / xn_out and all CTAs write y, so none of those may alias x or x_add; y may
 // alias res (each row is read and written by the same thread).
 #pragma once
@@ -35,6 +35,7 @@ struct GemvArgs {
   uint16_t* xn_out;       // nullable (written by CTA 0)
   const uint16_t* res;    // nullable
   uint16_t* y;
+  const uint16_t* bias;   // nullable: y = bf16(W x + bias) before the residual add
 };
 
 struct GemvLayout {
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemv_kernel(GemvArgs A) {
       const float acc = warp_sum(acc0 + acc1);
       if (lane == 0) {
         const int64_t n = n0 + r0 + r;
-        float out = bf16_to_f32(f32_to_bf16(acc));
+        float out = bf16_to_f32(f32_to_bf16(A.bias ? acc + bf16_to_f32(A.bias[n]) : acc));
         if (A.res) out = bf16_to_f32(A.res[n]) + out;
         A.y[n] = f32_to_bf16(out);
       }

@@ -623,8 +623,11 @@ int wisp_moe_batched_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes
                       ? launch_pdl(batched::count_group_kernel, 1, 1024, batched::count_group_smem(nslots), s, meta, N, k, nslots, W)
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_batched: %s", cudaGetErrorString(e));
+  // variant 0 (automatic) takes the warp-level kernels below: on the 64-token Zipf(1.1) layer of the
+  // Qwen3-30B-A3B shape they measured 118.7 us against 132 us for the tcgen05 pipeline, whose stages are
+  // bound by the per-stage latency of dequantizing into shared memory and of the small-N MMAs
   bool done = false;
-  if (variant != 1 && umma_batched_ok(S, bits)) {
+  if (variant == 2 && umma_batched_ok(S, bits)) {
     rc = umma_batched_launch(pool, S, bits, x, N, k, W, s, done);
     if (rc) return rc;
     if (!done && variant == 2) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_batched: tensor maps of the tensor-core path unavailable");
@@ -778,6 +781,10 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
   const int grid = num_sms() * 2;
   // the row path groups up to 32 pairs inside its gate_up grid
   const int fuse_group = rows && N * k <= batched::SMALL_PAIRS ? 1 : 0;
+  // reduction shapes of the activation and combine grids (see gptoss::RED_THREADS)
+  const bool act_wide = P <= 8 && ns0 > 4;
+  auto act = act_wide ? gptoss::act_kernel<16> : gptoss::act_kernel<1>;
+  auto cmb = ns1 > 16 ? gptoss::combine_kernel<32> : (N <= 2 && ns1 > 4 ? gptoss::combine_kernel<16> : gptoss::combine_kernel<1>);
   cudaError_t e = fuse_group ? cudaSuccess
                   : N * k <= batched::SMALL_PAIRS ? launch_pdl(batched::small_group_kernel, 1, 32, 0, s, meta, N, k, nslots, W.g)
                   : nslots <= batched::CS_MAX_SLOTS
@@ -785,14 +792,14 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
                       : launch_pdl(batched::group_kernel, 1, 1024, 0, s, meta, N, k, nslots, W.g);
 #define WISP_GPTOSS(B)                                                                                                      \
   if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 0>, grid, gptoss::THREADS, 0, s, pool, S, P, ns0, x, W);         \
-  if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W); \
+  if (e == cudaSuccess) e = launch_pdl(act, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W);             \
   if (e == cudaSuccess) e = launch_pdl(gptoss::gemv_kernel<B, 1>, grid, gptoss::THREADS, 0, s, pool, S, P, ns1, x, W);
   if (rows) {
     const int rgrid = 2 * num_sms();  // two CTAs per SM (shared memory and registers)
     if (e == cudaSuccess)
       e = launch_pdl(gptoss::rows::rows_kernel<0>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map0, pool, S, P, ns0, x, W,
                      meta, N, fuse_group);
-    if (e == cudaSuccess) e = launch_pdl(gptoss::act_kernel, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W);
+    if (e == cudaSuccess) e = launch_pdl(act, grid, gptoss::RED_THREADS, 0, s, S, P, ns0, experts, gate_up_bias, W);
     if (e == cudaSuccess)
       e = launch_pdl(gptoss::rows::rows_kernel<1>, rgrid, gptoss::rows::THREADS, gptoss::rows::SMEM, s, map1, pool, S, P, ns1, x, W,
                      meta, N, 0);
@@ -805,9 +812,7 @@ int wisp_moe_gptoss(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
     }
   }
 #undef WISP_GPTOSS
-  if (e == cudaSuccess)
-    e = ns1 > 16 ? launch_pdl(gptoss::combine_kernel<32>, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out)
-                 : launch_pdl(gptoss::combine_kernel<16>, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out);
+  if (e == cudaSuccess) e = launch_pdl(cmb, grid, gptoss::RED_THREADS, 0, s, meta, N, k, S, ns1, experts, down_bias, W, out);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_moe_gptoss: %s", cudaGetErrorString(e));
   return check_launch("moe_gptoss");
 }
@@ -840,6 +845,12 @@ int wisp_rope_decode(const uint16_t* q, int64_t q_stride, int Hq, const uint16_t
 
 int wisp_gemv(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const uint16_t* x_add, uint16_t* x_sum_out,
               const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* res, uint16_t* y, void* stream) {
+  return wisp_gemv_bias(W, N, K, x, x_add, x_sum_out, norm_w, eps, xn_out, nullptr, res, y, stream);
+}
+
+int wisp_gemv_bias(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const uint16_t* x_add, uint16_t* x_sum_out,
+                   const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* bias, const uint16_t* res, uint16_t* y,
+                   void* stream) {
   WISP_REQUIRE(W && x && y, "wisp_gemv: NULL pointer");
   WISP_REQUIRE(N > 0 && K > 0 && K % 8 == 0 && K <= 4096, "wisp_gemv: need N > 0, K a multiple of 8 and <= 4096 (N=%lld K=%lld)",
                (long long)N, (long long)K);
@@ -850,7 +861,7 @@ int wisp_gemv(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, const 
   WISP_REQUIRE(y != x && y != x_add && (!x_sum_out || (x_sum_out != x && x_sum_out != x_add)) &&
                    (!xn_out || (xn_out != x && xn_out != x_add)),
                "wisp_gemv: y, x_sum_out and xn_out must not alias x or x_add");
-  dense::GemvArgs A{W, N, K, x, x_add, x_sum_out, norm_w, eps, xn_out, res, y};
+  dense::GemvArgs A{W, N, K, x, x_add, x_sum_out, norm_w, eps, xn_out, res, y, bias};
   const dense::GemvLayout L = dense::gemv_layout(K);
   const int grid = int(N < num_sms() ? N : num_sms());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -916,6 +927,7 @@ int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_
   WISP_REQUIRE(Hq > 0 && Hk > 0 && Hq % Hk == 0 && Hq / Hk <= dec::MAX_G, "wisp_gqa_decode_attn: need Hq a multiple of Hk, Hq/Hk <= %d",
                dec::MAX_G);
   WISP_REQUIRE(D > 0 && D % 32 == 0 && D <= dec::MAX_D && tmax > 0, "wisp_gqa_decode_attn: need D a multiple of 32, <= %d", dec::MAX_D);
+  WISP_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16), "wisp_gqa_decode_attn: caches must be 16-byte aligned");
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaLaunchConfig_t cfg = {};
@@ -951,6 +963,7 @@ int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D
   WISP_REQUIRE(D > 0 && D % 32 == 0 && D <= dec::MAX_D && tmax > 0, "wisp_gqa_decode_attn_batched: need D a multiple of 32, <= %d",
                dec::MAX_D);
   WISP_REQUIRE(window >= 0, "wisp_gqa_decode_attn_batched: window must be >= 0");
+  WISP_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16), "wisp_gqa_decode_attn_batched: caches must be 16-byte aligned");
   WISP_REQUIRE(workspace_floats >= wisp_attn_batched_workspace_floats(B, Hq, Hk, D, tmax),
                "wisp_gqa_decode_attn_batched: workspace of %lld floats is too small", (long long)workspace_floats);
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
@@ -1018,6 +1031,23 @@ int wisp_router_topk(const uint16_t* logits, int E, int k, int norm_topk, const 
                                    slot_table, base, row, meta);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_router_topk: %s", cudaGetErrorString(e));
   return check_launch("router_topk");
+}
+
+int wisp_router_rows(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* W,
+                     const uint16_t* bias, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* meta,
+                     int32_t* experts, float* row, void* stream) {
+  WISP_REQUIRE(x && W && meta, "wisp_router_rows: NULL pointer");
+  WISP_REQUIRE(B >= 1 && B <= 65535, "wisp_router_rows: need 1 <= B <= 65535");
+  WISP_REQUIRE(H > 0 && H % 8 == 0 && H <= dec::ROUTER_MAX_H, "wisp_router_rows: need H a multiple of 8, <= %d", dec::ROUTER_MAX_H);
+  WISP_REQUIRE(E > 0 && E <= 1024 && k >= 1 && k <= 32 && k <= E, "wisp_router_rows: need 1 <= k <= min(E, 32), E <= 1024");
+  WISP_REQUIRE(norm_topk >= 0 && norm_topk <= 2, "wisp_router_rows: norm_topk must be 0, 1 or 2");
+  WISP_REQUIRE(aligned(x, 16) && aligned(W, 16) && (!norm_w || aligned(norm_w, 16)) && (!xn_out || aligned(xn_out, 16)),
+               "wisp_router_rows: x, W, norm_w and xn_out must be 16-byte aligned");
+  WISP_REQUIRE(xn_out != x, "wisp_router_rows: xn_out must not alias x");
+  const cudaError_t e = launch_pdl(dec::router_rows_kernel, B, dec::ROUTER_THREADS, 0, static_cast<cudaStream_t>(stream), x, H, norm_w,
+                                   eps, xn_out, W, bias, E, k, norm_topk, slot_table, base, meta, experts, row);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_router_rows: %s", cudaGetErrorString(e));
+  return check_launch("router_rows");
 }
 
 int wisp_embed(const uint16_t* table, int64_t V, int64_t H, const int64_t* token, uint16_t* out, void* stream) {

@@ -57,6 +57,7 @@ SIGNATURES = {
     "wisp_moe_decode_noalloc": (_I, [_P, _L, _L, _P, _I, _P, _L, _L, _I, _I, _P, _P]),
     "wisp_rope_decode": (_I, [_P, _L, _I, _P, _L, _I, _I, _P, _P, _P, _P, _P]),
     "wisp_gemv": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P]),
+    "wisp_gemv_bias": (_I, [_P, _L, _L, _P, _P, _P, _P, _F, _P, _P, _P, _P, _P]),
     "wisp_qk_norm_rope_kv": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _P, _P]),
     "wisp_qk_norm_rope_kv_rows": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _P, _P]),
     "wisp_attn_workspace_floats": (_L, [_I, _I, _I, _L]),
@@ -66,6 +67,7 @@ SIGNATURES = {
     "wisp_gqa_decode_attn": (_I, [_P, _I, _I, _I, _P, _P, _L, _P, _F, _P, _P, _P]),
     "wisp_attn_decode": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _F, _P, _P]),
     "wisp_router_topk": (_I, [_P, _I, _I, _I, _P, _L, _P, _P, _P]),
+    "wisp_router_rows": (_I, [_P, _I, _L, _P, _F, _P, _P, _P, _I, _I, _I, _P, _L, _P, _P, _P, _P]),
     "wisp_embed": (_I, [_P, _L, _L, _P, _P, _P]),
     "wisp_argmax": (_I, [_P, _L, _P, _P, _P]),
     "wisp_rmsnorm": (_I, [_P, _P, _P, _P, _L, _L, _F, _P, _P]),

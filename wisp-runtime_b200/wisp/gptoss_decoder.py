@@ -15,10 +15,11 @@ The reference runs gpt-oss through HF modules with its paged expert block swappe
     h   = h + sum_j w_j * (act(x W_gu_j + b_gu_j) W_d_j + b_d_j)   (clamped SwiGLU, wisp_moe_gptoss)
     out = RMSNorm(h) W_lm^T -> greedy argmax
 
-Kernels: RMSNorm, the q/k rotary + cache write and the batched GQA decode attention with sinks and
-windows, the gpt-oss expert kernels (wisp_moe_gptoss) are this package's; at one sequence the
-projections are the GEMV kernel (bias as its residual term, norm and residual adds fused), for several
-sequences they are cuBLAS GEMMs over the batch.
+Kernels: this package's RMSNorm (with the residual add fused), q/k rotary + cache write, batched GQA
+decode attention with sinks and windows, the fused router (RMSNorm, biased gate, top-k, softmax over
+the k: one launch for all sequences) and the gpt-oss expert kernels (wisp_moe_gptoss).  At one sequence
+the q/k/v and o projections are the GEMV kernel with the previous residual add, the RMSNorm, the bias
+and the next residual add fused; for several sequences they are cuBLAS GEMMs over the batch.
 """
 
 from __future__ import annotations
@@ -160,11 +161,11 @@ class GptOssDecoder:
         self.qkv = torch.zeros(B, (self.Hq + 2 * self.Hk) * self.D, **d)
         self.att = torch.zeros(B, self.Hq, self.D, **d)
         self.moe = torch.zeros(B, self.H, **d)
-        self.rlog = torch.zeros(B, self.E, **d)
         self.logits = torch.zeros(B, cfg.vocab, **d)
         self.next_token = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.routes = torch.zeros(self.L, B, self.k, dtype=torch.int64, device=dev)  # chosen experts per layer
-        self.rweights = torch.zeros(self.L, B, self.k, **d)  # and their weights (bf16 softmax over the chosen logits)
+        self.meta = torch.zeros(B, 2 * self.k, dtype=torch.float32, device=dev)  # [slots | weights] of the layer
+        self.experts = torch.zeros(B, self.k, dtype=torch.int32, device=dev)
+        self.rrow = torch.zeros(self.L, B, 2 * self.k, dtype=torch.float32, device=dev)  # per layer [experts | weights]
         self.attn_ws = kernels.attn_batched_workspace(B, self.Hq, self.Hk, self.D, self.tmax, dev)
         self.moe_ws = torch.empty(_lib.lib().wisp_moe_gptoss_workspace_bytes(B, self.k, self.H, self.I), dtype=torch.uint8,
                                   device=dev)
@@ -174,50 +175,56 @@ class GptOssDecoder:
         self.graph = None
         self.steps = 0
 
-    # ---- one token of every sequence -----------------------------------------------------------------
-    def _proj(self, W, x, bias=None, res=None, out=None, norm_w=None, xn_out=None):
-        """out = [res +] (norm(x) W^T + bias): the GEMV kernel for one sequence, cuBLAS for several."""
-        if self.B == 1:
-            if bias is not None and res is not None:  # y = res + (W x + b): the bias first, then the residual
-                kernels.gemv(W, x[0], norm_w=norm_w, eps=self.cfg.eps, xn_out=None if xn_out is None else xn_out[0],
-                             res=bias, out=self.tmp[0])
-                torch.add(res, self.tmp, out=out)
-                return out
-            kernels.gemv(W, x[0], norm_w=norm_w, eps=self.cfg.eps, xn_out=None if xn_out is None else xn_out[0],
-                         res=bias if res is None else res[0], out=out[0])
-            return out
-        if norm_w is not None:
-            x = kernels.rmsnorm(x, norm_w, self.cfg.eps, out=xn_out)
-        y = torch.addmm(bias, x, W.t()) if bias is not None else x @ W.t()
-        if res is not None:
-            y = res + y
-        out.copy_(y)
-        return out
+    @property
+    def routes(self):
+        """The experts each layer chose for each sequence in the last step, int64 [L, B, k]."""
+        return self.rrow[..., : self.k].long()
 
+    @property
+    def rweights(self):
+        """Their weights (bf16 softmax over the chosen logits, held in fp32), [L, B, k]."""
+        return self.rrow[..., self.k :]
+
+    # ---- one token of every sequence -----------------------------------------------------------------
     def _layer(self, l):
-        c, lw, B = self.cfg, self.w.layers[l], self.B
-        self._proj(lw["wqkv"], self.h, bias=lw["bqkv"], out=self.qkv, norm_w=lw["in_norm"], xn_out=self.xn)
-        q = kernels.qk_norm_rope_kv_batched(self.qkv, self.Hq, self.Hk, self.D, None, None, c.eps, self.cos, self.sin, self.pos,
+        """Attention then MoE of layer l.  The residual stream arrives as h (layer 0) or as h_mid + moe
+        of the previous layer, whose sum is formed inside this layer's first kernel (stored to h)."""
+        c, lw, B, eps = self.cfg, self.w.layers[l], self.B, self.cfg.eps
+        if B == 1:
+            if l == 0:
+                kernels.gemv(lw["wqkv"], self.h[0], norm_w=lw["in_norm"], eps=eps, bias=lw["bqkv"], out=self.qkv[0])
+            else:
+                kernels.gemv(lw["wqkv"], self.h_mid[0], x_add=self.moe[0], x_sum_out=self.h[0], norm_w=lw["in_norm"], eps=eps,
+                             bias=lw["bqkv"], out=self.qkv[0])
+        else:
+            if l == 0:
+                kernels.rmsnorm(self.h, lw["in_norm"], eps, out=self.xn)
+            else:
+                kernels.rmsnorm(self.h_mid, lw["in_norm"], eps, delta=self.moe, sum_out=self.h, out=self.xn)
+            torch.addmm(lw["bqkv"], self.xn, lw["wqkv"].t(), out=self.qkv)
+        q = kernels.qk_norm_rope_kv_batched(self.qkv, self.Hq, self.Hk, self.D, None, None, eps, self.cos, self.sin, self.pos,
                                             self.kc[l], self.vc[l])
         window = c.window if c.layer_types[l] == "sliding_attention" else 0
         kernels.gqa_decode_attn_batched(q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], self.pos, self.scale, window=window,
                                         sinks=lw["sinks"], workspace=self.attn_ws, out=self.att)
-        self._proj(lw["wo"], self.att.view(B, -1), bias=lw["bo"], res=self.h, out=self.h_mid)
-        self._proj(lw["router"], self.h_mid, bias=lw["router_b"], out=self.rlog, norm_w=lw["post_norm"], xn_out=self.xn)
-        tv, ti = torch.topk(self.rlog, self.k, dim=-1)
-        sc = torch.softmax(tv, dim=-1, dtype=tv.dtype)
-        self.routes[l].copy_(ti)
-        self.rweights[l].copy_(sc)
-        meta = torch.cat([(ti + l * self.E).float(), sc.float()], 1).contiguous()
-        kernels.moe_gptoss(self.w.pool, meta, ti.to(torch.int32).contiguous(), self.xn, self.k, self.H, self.I, c.bits,
-                           lw["gub"], lw["db"], c.group, out=self.moe, workspace=self.moe_ws)
-        torch.add(self.h_mid, self.moe, out=self.h)
+        if B == 1:
+            kernels.gemv(lw["wo"], self.att.view(-1), bias=lw["bo"], res=self.h[0], out=self.h_mid[0])
+        else:
+            torch.addmm(lw["bo"], self.att.view(B, -1), lw["wo"].t(), out=self.tmp)
+            torch.add(self.h, self.tmp, out=self.h_mid)
+        kernels.router_rows(self.h_mid, lw["router"], self.k, "selected", norm_w=lw["post_norm"], eps=eps, bias=lw["router_b"],
+                            xn_out=self.xn, base=l * self.E, meta=self.meta, experts=self.experts, row=self.rrow[l])
+        kernels.moe_gptoss(self.w.pool, self.meta, self.experts, self.xn, self.k, self.H, self.I, c.bits, lw["gub"], lw["db"],
+                           c.group, out=self.moe, workspace=self.moe_ws)
 
     def _step(self):
-        torch.index_select(self.w.embed, 0, self.tokens, out=self.h)
+        if self.B == 1:
+            kernels.embed(self.w.embed, self.tokens, out=self.h[0])
+        else:
+            torch.index_select(self.w.embed, 0, self.tokens, out=self.h)
         for l in range(self.L):
             self._layer(l)
-        xf = kernels.rmsnorm(self.h, self.w.final_norm, self.cfg.eps)
+        xf = kernels.rmsnorm(self.h_mid, self.w.final_norm, self.cfg.eps, delta=self.moe, sum_out=self.h, out=self.xn)
         if self.B == 1:
             kernels.gemv(self.w.lm_head, xf[0], out=self.logits[0])
             kernels.argmax(self.logits[0], workspace=self.argmax_ws, out=self.next_token[0:1])

@@ -507,17 +507,24 @@ def _bf16(*ts):
             raise WispError("contiguous bfloat16 tensors expected")
 
 
-def gemv(W, x, x_add=None, x_sum_out=None, norm_w=None, eps=1e-6, xn_out=None, res=None, out=None):
-    """y = W x' (W [N, K] bf16, one token), x' = rmsnorm(x + x_add) as requested; see wisp_gemv."""
+def gemv(W, x, x_add=None, x_sum_out=None, norm_w=None, eps=1e-6, xn_out=None, res=None, out=None, bias=None):
+    """y = [res +] (W x' [+ bias]) (W [N, K] bf16, one token), x' = rmsnorm(x + x_add) as requested; see
+    wisp_gemv / wisp_gemv_bias."""
     _need_cuda(W, x)
-    _bf16(W, x, x_add, x_sum_out, norm_w, xn_out, res, out)
+    _bf16(W, x, x_add, x_sum_out, norm_w, xn_out, res, out, bias)
     N, K = W.shape
     if out is None:
         out = torch.empty(N, dtype=torch.bfloat16, device=x.device)
-    _lib.call(
-        "wisp_gemv", W.data_ptr(), N, K, x.data_ptr(), _ptr(x_add), _ptr(x_sum_out), _ptr(norm_w), float(eps),
-        _ptr(xn_out), _ptr(res), out.data_ptr(), _stream(x),
-    )
+    if bias is None:
+        _lib.call(
+            "wisp_gemv", W.data_ptr(), N, K, x.data_ptr(), _ptr(x_add), _ptr(x_sum_out), _ptr(norm_w), float(eps),
+            _ptr(xn_out), _ptr(res), out.data_ptr(), _stream(x),
+        )
+    else:
+        _lib.call(
+            "wisp_gemv_bias", W.data_ptr(), N, K, x.data_ptr(), _ptr(x_add), _ptr(x_sum_out), _ptr(norm_w), float(eps),
+            _ptr(xn_out), bias.data_ptr(), _ptr(res), out.data_ptr(), _stream(x),
+        )
     return out
 
 
@@ -649,6 +656,28 @@ def router_topk(logits, k, norm_topk=True, slot_table=None, base=0, row=None, me
     _lib.call(
         "wisp_router_topk", logits.data_ptr(), E, k, mode, _ptr(slot_table), int(base), _ptr(row),
         meta.data_ptr(), _stream(logits),
+    )
+    return meta
+
+
+def router_rows(x, W, k, norm_topk, norm_w=None, eps=1e-6, bias=None, xn_out=None, slot_table=None, base=0, meta=None,
+                experts=None, row=None):
+    """Router of B tokens (x bf16 [B, H]) in one launch: RMSNorm (norm_w), gate logits W [E, H] (+ bias),
+    top-k and weights (norm_topk 0 / 1 / 2 as in router_topk) -> meta fp32 [B, 2k] = [slots | weights];
+    optionally experts int32 [B, k], row fp32 [B, 2k] = [ids | weights], xn_out = the normed rows."""
+    _need_cuda(x, W)
+    _bf16(x, W, norm_w, bias, xn_out)
+    B, H = x.shape
+    E = W.shape[0]
+    if meta is None:
+        meta = torch.empty((B, 2 * k), dtype=torch.float32, device=x.device)
+    mode = 2 if norm_topk == "selected" else (1 if norm_topk else 0)
+    for t, dt in ((slot_table, torch.int32), (experts, torch.int32), (row, torch.float32), (meta, torch.float32)):
+        if t is not None and (t.dtype != dt or not t.is_contiguous()):
+            raise WispError("router_rows: slot_table / experts int32, meta / row float32, contiguous")
+    _lib.call(
+        "wisp_router_rows", x.data_ptr(), B, H, _ptr(norm_w), float(eps), _ptr(xn_out), W.data_ptr(), _ptr(bias), E, k, int(mode),
+        _ptr(slot_table), int(base), meta.data_ptr(), _ptr(experts), _ptr(row), _stream(x),
     )
     return meta
 
