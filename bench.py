@@ -47,6 +47,7 @@ NCU_TRAFFIC_GPTOSS_LAYER_BS1 = 35_287_552 + 17_679_872
 
 
 GO_L, GO_H, GO_I, GO_E, GO_K = 24, 2880, 2880, 32, 4  # gpt-oss-20b MoE shape (config 5)
+QB_CONTEXT = 4096  # qwen-batched: KV context of every sequence when the timed steps start (config 4)
 GO_PROMPT, GO_VOCAB, GO_HQ, GO_HK, GO_D, GO_WINDOW = 256, 201088, 64, 8, 64, 128  # gpt-oss-20b decoder (config 5)
 TIMELINE_TOKENS = 24  # decoder with device paging: untimed steps traced with CUDA events after the timed ones
 
@@ -58,7 +59,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="wisp", choices=["wisp", "reference"])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 3, 2])
-    ap.add_argument("--workload", default="decoder", choices=["decoder", "moe-stack", "moe-ep", "gptoss-moe", "gptoss"])
+    ap.add_argument("--workload", default="decoder",
+                    choices=["decoder", "moe-stack", "moe-ep", "gptoss-moe", "gptoss", "qwen-batched"])
     ap.add_argument("--batch", type=int, default=1, help="gptoss, gptoss-moe: sequences (tokens) per step (config 5: 1 or 32)")
     ap.add_argument("--layers", type=int, default=48, help="layers (48 = the model; fewer = a small ncu case)")
     ap.add_argument("--prompt", type=int, default=512)
@@ -89,7 +91,7 @@ def parse():
 
 def metric_name(a):
     return {"decoder": "decode tok/s", "moe-stack": "moe decode tok/s", "moe-ep": "batched moe tok/s",
-            "gptoss-moe": "moe decode tok/s", "gptoss": "decode tok/s"}[a.workload]
+            "gptoss-moe": "moe decode tok/s", "gptoss": "decode tok/s", "qwen-batched": "decode tok/s"}[a.workload]
 
 
 def workload_config(a, n):
@@ -128,6 +130,21 @@ def workload_config(a, n):
             "seq_len": 1,
             "parallelism": "replicas" if n > 1 else "single",
             "l2": f"expert working set {GO_L * GO_E * 13.2:.0f} MB >> 126 MB L2; no flush",
+        }
+    if a.workload == "qwen-batched":
+        return {
+            "workload": f"qwen3-30b-a3b batched greedy decode (config 4): {EP_BATCH} sequences in total, KV context "
+            f"{QB_CONTEXT} each (seeded synthetic K/V, then one token per sequence per step), {L} layers, 32q/4kv heads x 128, "
+            f"{E} experts top-{K_TOP}, {a.bits}-bit g{G} experts all resident, router logits biased to Zipf(1.1) expert "
+            f"popularity, experts sharded expert-parallel over {n} GPU(s) ({E // n} per layer each)"
+            + (", dispatch / combine as kernel stores into peer memory" if n > 1 and a.transport in ("auto", "p2p")
+               else (", NCCL all-to-all dispatch / combine" if n > 1 else ""))
+            + f", attention data-parallel ({EP_BATCH // n} sequences per GPU), whole-step CUDA graph",
+            "model": "Qwen3-30B-A3B-shaped (random init; o_proj and expert down at std 0.02/sqrt(2L))",
+            "global_batch": EP_BATCH,
+            "seq_len": QB_CONTEXT,
+            "parallelism": f"ep{n}+dp{n}",
+            "l2": "KV cache read per step (537 MB per layer at 64 x 4096) >> 126 MB L2; no flush",
         }
     if a.workload == "gptoss":
         return {
@@ -464,6 +481,8 @@ def cpu_sample(a, seed=0, distinct=60.0):
             f"sample; step time = per-expert time x {distinct:.0f} distinct experts per layer x {L} layers, {EP_BATCH} tokens")
     if a.workload == "gptoss":
         return cpu_gptoss_sample(a, seed, distinct)
+    if a.workload == "qwen-batched":
+        return cpu_batched_sample(a, seed, distinct)
     # gptoss-moe
     n = GO_H * GO_I
     dist_go = distinct if distinct < 60.0 else float(min(GO_E, a.batch * GO_K))
@@ -484,6 +503,49 @@ def cpu_sample(a, seed=0, distinct=60.0):
     return per * m, a.batch / (per * dist_go * GO_L), threads, (
         f"{m} gpt-oss experts in parallel (dequantize + fp32 MLP of {toks} token(s)) per sample; step time = per-expert "
         f"time x {dist_go:.1f} distinct experts per layer x {GO_L} layers, {a.batch} token(s) per step")
+
+
+def cpu_batched_sample(a, seed, distinct, seqs=4):
+    """Config 4 on the host cores: the attention part of one layer (RMSNorm, q/k/v projections, GQA over
+    QB_CONTEXT positions, o projection, router) for ``seqs`` of the 64 sequences, scaled to 64; the
+    distinct experts of a layer (dequantize + fp32 MLP of the tokens one expert receives on average) in
+    parallel; step time = L x (attention part + experts) + the lm_head of 64 tokens (1/16 of its rows)."""
+    import numpy as np
+
+    from oracle import wisp_oracle as O
+
+    wt = _cpu_weights(a.bits, True, QB_CONTEXT)
+    rng = np.random.default_rng(seed)
+    n = H * I
+    nw = np.ones(H, np.float32)
+    ex = cpu_pool()
+    x = rng.standard_normal((seqs, H)).astype(np.float32)
+
+    def attn(b):
+        xn = O.rmsnorm(x[b], nw)
+        q = (wt["wqkv"] @ xn)[: HQ * D].reshape(HQ, D)
+        att = O.gqa_decode_attention(q, wt["kc"], wt["vc"], QB_CONTEXT - 1, D ** -0.5)
+        hm = x[b] + wt["wo"] @ att.reshape(-1)
+        O.router_topk((wt["wr"] @ O.rmsnorm(hm, nw))[None], K_TOP)
+
+    t0 = time.perf_counter()
+    list(ex.map(attn, range(seqs)))
+    dense = (time.perf_counter() - t0) * EP_BATCH / seqs
+    toks = max(1, int(round(EP_BATCH * K_TOP / distinct)))
+    xe = rng.standard_normal((toks, H)).astype(np.float32)
+
+    def one(j):
+        gm, um, dm = O.expert_weights(wt["pool"], j % K_TOP, n, a.bits, G, H, I)
+        return (O.silu(xe @ gm.T) * (xe @ um.T)) @ dm.T
+
+    m = max(K_TOP, os.cpu_count() or 1)
+    per = _parallel_expert_cost(one, m)
+    head = cpu_head_sample(seed) * EP_BATCH
+    step = L * (dense + per * distinct) + head
+    return step, EP_BATCH / step, os.cpu_count() or 1, (
+        f"per sample: the attention part of one layer for {seqs} sequences at context {QB_CONTEXT} (x {EP_BATCH // seqs}), "
+        f"{m} experts in parallel (dequantize + fp32 MLP of {toks} tokens); step time = {L} x (attention part + per-expert "
+        f"time x {distinct:.0f} distinct experts) + the lm_head of {EP_BATCH} tokens")
 
 
 def cpu_gptoss_sample(a, seed, distinct):
@@ -820,6 +882,110 @@ class GptOssStack:
 
     def release(self):
         self.graphs = []
+
+
+# ------------------------------------------------------------------------------------------------
+# qwen-batched workload (config 4: 64 sequences at KV context 4096, experts expert-parallel)
+# ------------------------------------------------------------------------------------------------
+class QwenBatchedBench:
+    """EP_BATCH sequences over all ranks (EP_BATCH / world each) decoded greedily through BatchedDecoder:
+    every sequence's cache holds QB_CONTEXT seeded positions when the timed steps start; the router
+    logits carry a Zipf(1.1) popularity bias; with world > 1 the experts are split over the ranks."""
+
+    def __init__(self, a, device, rank, world):
+        import torch
+
+        from wisp.batched_decoder import BatchedDecoder, zipf_bias
+        from wisp.ep import ExpertParallelMoE, batched_expert_fn
+        from wisp.model import DecoderConfig, DecoderWeights
+
+        assert EP_BATCH % world == 0 and E % world == 0
+        self.B, self.El, self.world = EP_BATCH // world, E // world, world
+        cfg = DecoderConfig(layers=L, bits=a.bits)
+        local = None if world == 1 else (rank * self.El, self.El)
+        self.w = DecoderWeights.random(cfg, device=device, seed=0, resid_scale=True, local_experts=local, router_std=H ** -0.5)
+        self.nb = self.w.nbytes
+        variant = {"auto": 0, "mma": 1, "tcgen05": 2}[a.batched_path]
+        self.ep = None
+        if world > 1:
+            fn = batched_expert_fn(self.w.pool, lambda l, e: l * self.El + e, H * I, H, I, a.bits, G, variant=variant)
+            transport = a.transport if a.transport != "auto" else "p2p"
+            self.ep = ExpertParallelMoE(E, K_TOP, H, self.B, fn, device=device, slot_base=lambda l: l * self.El,
+                                        transport=transport)
+        tmax = QB_CONTEXT + 2 * (a.warmup + a.steps) + 64
+        self.dec = BatchedDecoder(self.w, batch=self.B, tmax=tmax, ep=self.ep, expert_bias=zipf_bias(L, E, device=device),
+                                  variant=variant)
+        g = torch.Generator(device=device).manual_seed(100 + rank)
+        for l in range(L):  # seeded synthetic context
+            self.dec.kc[l, :, :, :QB_CONTEXT].normal_(generator=g)
+            self.dec.vc[l, :, :, :QB_CONTEXT].normal_(generator=g)
+        self.dec.pos.fill_(QB_CONTEXT)
+        self.dec.tokens.copy_(torch.randint(0, VOCAB, (self.B,), device=device, generator=g))
+        self.dec.next_token.copy_(self.dec.tokens)
+        self.dec.capture()
+        self.prefill_s = 0.0
+        self.distinct_seen = []
+
+    def step(self, t):
+        self.dec.step()
+
+    def record_routes(self):
+        import torch
+
+        r = self.dec.routes  # this rank's sequences; the distinct experts of the whole batch need every rank
+        if self.world > 1:
+            import torch.distributed as dist
+
+            allr = [torch.empty_like(r) for _ in range(self.world)]
+            dist.all_gather(allr, r.contiguous())
+            r = torch.cat(allr, 1)
+        self.distinct_seen.append(sum(torch.unique(r[l]).numel() for l in range(L)) / L)
+
+    @property
+    def distinct(self):
+        return statistics.mean(self.distinct_seen) if self.distinct_seen else 50.0
+
+    def launches_per_step(self):
+        """This package's kernels per step (cuBLAS GEMMs, torch's adds, copies and argmax not counted): per
+        layer RMSNorm, rotary + cache write, attention (2), router, and the batched MoE (grouping, permute,
+        gate/up, down, combine: 5) or, expert-parallel, dispatch + batched MoE + combine (7, 9 with the
+        peer-memory transport); the final RMSNorm."""
+        per = 5 + (5 if self.world == 1 else (9 if self.ep.p2p is not None else 7))
+        return L * per + 1
+
+    def e2e_inputs(self):
+        import torch
+
+        return (torch.randint(0, VOCAB, (self.B,), generator=torch.Generator().manual_seed(9)).pin_memory(),
+                torch.empty(self.B, dtype=torch.int64).pin_memory())
+
+    def step_e2e(self, t, inp):
+        tok_host, out_host = inp
+        self.dec.tokens.copy_(tok_host, non_blocking=True)
+        self.dec.graph.replay()
+        out_host.copy_(self.dec.next_token, non_blocking=True)
+
+    def e2e_bytes(self):
+        return 8 * self.B, 8 * self.B
+
+    def step_bytes(self, ctx):
+        """Algorithmic bytes one GPU moves per step: every dense weight once, its share of the distinct
+        experts of each layer, and its sequences' K/V over the context."""
+        dense = L * 2 * ((HQ + 2 * HK) * D * H + H * HQ * D + E * H + 2 * H + 2 * D) + 2 * VOCAB * H + 2 * H
+        kv = L * self.B * 2 * HK * D * 2 * ctx
+        return dense + L * self.distinct / self.world * self.nb + kv
+
+    def roofline(self, ms_per_step, peak, peak_src, ctx):
+        b = self.step_bytes(ctx)
+        ach = b / (ms_per_step * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "traffic": None,
+                "kernel": "whole decode step on one GPU (every kernel of the graph): algorithmic bytes per step / step time",
+                "bytes_per_call": b, "us_per_call": ms_per_step * 1e3, "peak_source": peak_src}
+
+    def release(self):
+        self.dec.release()
+        if self.ep is not None:
+            self.ep.close()
 
 
 # ------------------------------------------------------------------------------------------------
@@ -1265,6 +1431,9 @@ def main():
     elif a.workload == "gptoss":
         bench = GptOssDecodeBench(a, dev, seed=rank)
         pool, nbytes = None, bench.nb
+    elif a.workload == "qwen-batched":
+        bench = QwenBatchedBench(a, dev, rank, world)
+        pool, nbytes = None, bench.nb
     elif a.workload == "gptoss-moe":
         bench = GptOssStack(a, dev, seed=rank)
         bench.capture()
@@ -1296,7 +1465,7 @@ def main():
     barrier()
     clocks.window(w0, time.perf_counter())
     ms = e0.elapsed_time(e1)
-    if a.workload == "gptoss":
+    if a.workload in ("gptoss", "qwen-batched"):
         bench.record_routes()
     # e2e: host buffers, copies inside the timed region
     inp = bench.e2e_inputs()
@@ -1325,6 +1494,10 @@ def main():
         peak, src = load_peaks()
         src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
         roof = bench.roofline(ms / a.steps, peak, src, GO_PROMPT + a.warmup + a.steps)
+    elif a.workload == "qwen-batched":
+        peak, src = load_peaks()
+        src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
+        roof = bench.roofline(ms / a.steps, peak, src, QB_CONTEXT + a.warmup + a.steps)
     elif a.workload in ("gptoss-moe", "moe-ep"):
         peak, src = load_peaks()
         src = f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src
@@ -1340,8 +1513,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = t.tolist()
     if rank == 0:
-        cpu_v, cores, sample = cpu_tok_s(a, distinct=bench.distinct if a.workload in ("moe-ep", "gptoss-moe", "gptoss") else 60.0)
-        tok = a.steps * (EP_BATCH if a.workload == "moe-ep" else (a.batch * world if a.workload in ("gptoss-moe", "gptoss") else world))
+        cpu_v, cores, sample = cpu_tok_s(
+            a, distinct=bench.distinct if a.workload in ("moe-ep", "gptoss-moe", "gptoss", "qwen-batched") else 60.0)
+        tok = a.steps * (EP_BATCH if a.workload in ("moe-ep", "qwen-batched")
+                         else (a.batch * world if a.workload in ("gptoss-moe", "gptoss") else world))
         h2d, d2h = bench.e2e_bytes()
         line = {
             "metric": metric_name(a),
@@ -1352,7 +1527,7 @@ def main():
             "warmup": a.warmup,
             "ms_per_step": ms / a.steps,
             "higher_is_better": True,
-            "scaling": "strong" if a.workload == "moe-ep" else "weak",
+            "scaling": "strong" if a.workload in ("moe-ep", "qwen-batched") else "weak",
             "vs_baseline": None,
             "dtype": f"u{a.bits}->f32 experts, bf16 dense",
             "data": "synthetic",
@@ -1372,6 +1547,9 @@ def main():
             line["paging"] = paging
         if a.workload == "gptoss-moe":
             line["distinct_experts_per_layer"] = bench.distinct
+        if a.workload == "qwen-batched":
+            line["distinct_experts_per_layer"] = bench.distinct
+            line["context"] = f"{QB_CONTEXT} seeded K/V positions per sequence before the warm-up steps"
         if a.workload == "moe-ep":
             line["distinct_experts_per_layer"] = bench.distinct
             # expert bytes each GPU streams per layer (its share of the distinct experts) per layer time

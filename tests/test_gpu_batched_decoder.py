@@ -87,3 +87,34 @@ def test_sequences_are_independent():
             one.load_kv(ks[:, b : b + 1], vs[:, b : b + 1], 6)
             got = one.step(t[b : b + 1]).float()
             assert (got[0] - both[b]).abs().max().item() <= 2e-2 * both[b].abs().max().item(), b
+
+
+def test_expert_parallel_path_on_one_rank():
+    """The decoder's expert-parallel branch (router rows -> dispatch -> batched experts -> combine, one
+    rank owning every expert) against its resident branch on the same weights, routing and cache."""
+    from wisp.batched_decoder import BatchedDecoder, zipf_bias
+    from wisp.ep import ExpertParallelMoE, batched_expert_fn
+
+    model, w, _, ids = _setup(4, 6, True)
+    c = w.cfg
+    with torch.no_grad():
+        out = model(input_ids=ids, use_cache=True)
+        pk = out.past_key_values
+        ks = torch.stack([_kv(pk, i)[0] for i in range(c.layers)])
+        vs = torch.stack([_kv(pk, i)[1] for i in range(c.layers)])
+        t = out.logits[:, -1].argmax(-1)
+        zb = zipf_bias(c.layers, c.experts, device="cuda")
+        fn = batched_expert_fn(w.pool, lambda l, e: l * c.experts + e, c.hidden * c.moe_inter, c.hidden, c.moe_inter, c.bits,
+                               c.group)
+        ep = ExpertParallelMoE(c.experts, c.top_k, c.hidden, 4, fn, device="cuda", slot_base=lambda l: l * c.experts)
+        a = BatchedDecoder(w, batch=4, tmax=64, expert_bias=zb)
+        b = BatchedDecoder(w, batch=4, tmax=64, expert_bias=zb, ep=ep)
+        for dec in (a, b):
+            dec.load_kv(ks, vs, 6)
+        for _ in range(3):
+            la = a.step(t).float()
+            lb = b.step(t).float()
+            assert torch.equal(a.routes, b.routes)
+            assert (la - lb).abs().max().item() <= 2e-2 * la.abs().max().item()
+            t = la.argmax(-1)
+        ep.close()

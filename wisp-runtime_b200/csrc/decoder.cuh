@@ -238,12 +238,21 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
 
 // one CTA per (query head, sequence): out = sum_c O_c e^(m_c - M) / (sum_c l_c e^(m_c - M) [+ e^(sink - M)]);
 // sinks (fp32 [Hq], nullable) are per-head logits that take part in the softmax's normalisation but
-// contribute no value (attention sinks)
-__global__ void attn_combine_kernel(const float* __restrict__ part, int Hq, int Hk, int D, int nchunk_max,
-                                    const int64_t* __restrict__ pos_ptr, int64_t tmax, uint16_t* __restrict__ out, int window,
-                                    const float* __restrict__ sinks) {
+// contribute no value (attention sinks).  The chunks are spread over the threads (max and
+// normaliser) and over the warps (outputs: warp w sums chunks c0 + w, c0 + w + 4, ..., its lanes hold
+// D / 32 columns each), and the warps' sums are added in a fixed order, so long contexts keep many
+// independent loads in flight and the result does not depend on scheduling.
+constexpr int CMB_THREADS = 128;
+__global__ void __launch_bounds__(CMB_THREADS) attn_combine_kernel(const float* __restrict__ part, int Hq, int Hk, int D,
+                                                                   int nchunk_max, const int64_t* __restrict__ pos_ptr, int64_t tmax,
+                                                                   uint16_t* __restrict__ out, int window,
+                                                                   const float* __restrict__ sinks) {
+  constexpr int NW = CMB_THREADS / 32;
+  __shared__ float red[NW];
+  __shared__ float osum[NW][MAX_D];
   const int head = blockIdx.x, b = blockIdx.y;
   const int G = Hq / Hk, h = head / G, g = head % G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   pdl_launch_dependents();
   const int64_t pos = pos_ptr[b];
@@ -251,20 +260,51 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int Hq, int 
   part += int64_t(b) * Hk * nchunk_max * G * (D + 2);
   out += int64_t(b) * Hq * D;
   const int c0 = int(window_lo(pos, window) / CHUNK), nc = int(pos / CHUNK) + 1;
-  float M = sinks ? sinks[head] : -INFINITY;
-  for (int c = c0; c < nc; ++c) M = fmaxf(M, part[((int64_t(h) * nchunk_max + c) * G + g) * (D + 2) + D]);
-  float Ls = sinks ? __expf(sinks[head] - M) : 0.0f;
-  for (int c = c0; c < nc; ++c) {
-    const float* rec = part + ((int64_t(h) * nchunk_max + c) * G + g) * (D + 2);
+  const int64_t rs = D + 2;  // floats per record
+  const float* rec0 = part + (int64_t(h) * nchunk_max * G + g) * rs;  // record of chunk c: rec0 + c * G * rs
+  // M = max over the chunks' maxima (and the sink)
+  float M = -INFINITY;
+  for (int c = c0 + threadIdx.x; c < nc; c += CMB_THREADS) M = fmaxf(M, rec0[int64_t(c) * G * rs + D]);
+  M = warp_max(M);
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = sinks ? sinks[head] : -INFINITY;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) M = fmaxf(M, red[w]);
+  __syncthreads();
+  // the normaliser
+  float Ls = 0.0f;
+  for (int c = c0 + threadIdx.x; c < nc; c += CMB_THREADS) {
+    const float* rec = rec0 + int64_t(c) * G * rs;
     Ls += rec[D + 1] * __expf(rec[D] - M);
   }
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  Ls = warp_sum(Ls);
+  if (lane == 0) red[warp] = Ls;
+  // the outputs: warp w takes chunks c0 + w, c0 + w + NW, ...
+  const int dpl = D / 32;
+  float acc[MAX_D / 32];
+#pragma unroll
+  for (int e = 0; e < MAX_D / 32; ++e) acc[e] = 0.0f;
+#pragma unroll 2
+  for (int c = c0 + warp; c < nc; c += NW) {
+    const float* rec = rec0 + int64_t(c) * G * rs;
+    const float f = __expf(rec[D] - M);
+#pragma unroll
+    for (int e = 0; e < MAX_D / 32; ++e)
+      if (e < dpl) acc[e] = fmaf(rec[lane * dpl + e], f, acc[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < MAX_D / 32; ++e)
+    if (e < dpl) osum[warp][lane * dpl + e] = acc[e];
+  __syncthreads();
+  float L = sinks ? __expf(sinks[head] - M) : 0.0f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) L += red[w];
+  for (int d = threadIdx.x; d < D; d += CMB_THREADS) {
     float o = 0.0f;
-    for (int c = c0; c < nc; ++c) {
-      const float* rec = part + ((int64_t(h) * nchunk_max + c) * G + g) * (D + 2);
-      o += rec[d] * __expf(rec[D] - M);
-    }
-    out[int64_t(head) * D + d] = f32_to_bf16(o / Ls);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) o += osum[w][d];
+    out[int64_t(head) * D + d] = f32_to_bf16(o / L);
   }
 }
 
@@ -318,6 +358,134 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(smem_u32(p)));
+}
+
+// ---- attention chunk partials on the tensor cores (D = 64 or 128) ------------------------------------
+// The same records as attn_split_kernel (grid (Hk, chunks, batch), CHUNK positions per CTA), with
+// S = Q K^T and O = P V as mma.sync m16n8k16 (bf16 operands, fp32 accumulation): the G query heads are
+// rows 0..G-1 of the 16-row A tile (the rest zero), K rows are the B operand as stored, V enters
+// through ldmatrix.trans.  Warp w scores positions 16w..16w+15 and owns D/4 output columns.  Scores
+// are kept in log2 units (exp2) and the record's maximum is stored back in natural units, which is
+// what attn_combine_kernel reads; P is rounded to bf16 for its MMA.
+template <int TD>
+struct SplitSmem {
+  static constexpr int KP = TD + 8;  // padded rows: fragment loads are conflict-free
+  uint16_t q[16][KP];
+  uint16_t k[CHUNK][KP];
+  uint16_t v[CHUNK][KP];
+  uint16_t p[16][CHUNK + 8];
+  float s[MAX_G][CHUNK];
+};
+
+template <int TD>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint16_t* __restrict__ q, int Hq, int Hk,
+                                                                     const uint16_t* __restrict__ kc,
+                                                                     const uint16_t* __restrict__ vc, int64_t tmax,
+                                                                     const int64_t* __restrict__ pos_ptr, float scale,
+                                                                     float* __restrict__ part, int64_t kv_bstride, int window) {
+  static_assert(ATTN_THREADS == 128 && CHUNK == 64, "four warps of 16 positions");
+  using Sm = SplitSmem<TD>;
+  constexpr int KP = Sm::KP;
+  __shared__ __align__(16) Sm S;
+  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hk;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = lane & 3;  // mma fragment row / column pair
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t pos = pos_ptr[b];
+  if (pos < 0 || pos >= tmax) return;  // flagged by the cache-write kernel
+  const int64_t lo = window_lo(pos, window);
+  const int64_t t0 = int64_t(c) * CHUNK > lo ? int64_t(c) * CHUNK : lo;
+  if (t0 > pos || t0 >= int64_t(c + 1) * CHUNK) return;  // outside [lo, pos]: the combine never reads this record
+  const int n = int((pos + 1 - t0) < int64_t(c + 1) * CHUNK - t0 ? (pos + 1 - t0) : int64_t(c + 1) * CHUNK - t0);
+  // positions t0 .. t0 + n - 1 sit in smem rows r0 .. r0 + n - 1 with r0 = t0 - c*CHUNK (a window can cut the chunk's start)
+  const int r0 = int(t0 - int64_t(c) * CHUNK);
+  q += int64_t(b) * Hq * TD;
+  kc += int64_t(b) * kv_bstride;
+  vc += int64_t(b) * kv_bstride;
+  part += int64_t(b) * Hk * gridDim.y * G * (TD + 2);
+  {
+    const uint16_t* kb = kc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
+    const uint16_t* vb = vc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
+    constexpr int PR = TD / 8;  // 16-byte pieces per row
+    for (int i = tid; i < CHUNK * PR; i += ATTN_THREADS) {
+      const int r = i / PR, cp = i % PR;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (r >= r0 && r < r0 + n) {
+        kv = reinterpret_cast<const uint4*>(kb + int64_t(r) * TD)[cp];
+        vv = reinterpret_cast<const uint4*>(vb + int64_t(r) * TD)[cp];
+      }
+      reinterpret_cast<uint4*>(&S.k[r][0])[cp] = kv;
+      reinterpret_cast<uint4*>(&S.v[r][0])[cp] = vv;
+    }
+    for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
+      const int r = i / PR, cp = i % PR;
+      reinterpret_cast<uint4*>(&S.q[r][0])[cp] =
+          r < G ? reinterpret_cast<const uint4*>(q + (int64_t(h) * G + r) * TD)[cp] : make_uint4(0, 0, 0, 0);
+    }
+    for (int i = tid; i < 16 * (CHUNK + 8) / 2; i += ATTN_THREADS) reinterpret_cast<uint32_t*>(&S.p[0][0])[i] = 0u;
+  }
+  __syncthreads();
+  const float qscale = scale * 1.4426950408889634f;  // log2 units
+  // scores: warp w, positions 16w + 8nt + (0..7)
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int t = 16 * warp + 8 * nt;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < TD / 16; ++j) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.q[gq][16 * j + 2 * cq]);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.q[gq][16 * j + 8 + 2 * cq]);
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&S.k[t + gq][16 * j + 2 * cq]);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&S.k[t + gq][16 * j + 8 + 2 * cq]);
+      mma_bf16(d, a0, 0u, a2, 0u, b0, b1);
+    }
+    if (gq < G) {
+      const int p0 = t + 2 * cq;
+      S.s[gq][p0] = p0 >= r0 && p0 < r0 + n ? d[0] * qscale : -INFINITY;
+      S.s[gq][p0 + 1] = p0 + 1 >= r0 && p0 + 1 < r0 + n ? d[1] * qscale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  // softmax within the chunk: warp w takes heads w, w + 4
+  for (int g = warp; g < G; g += ATTN_THREADS / 32) {
+    const float v0 = S.s[g][lane], v1 = S.s[g][lane + 32];
+    const float m = warp_max(fmaxf(v0, v1));  // finite: the chunk holds at least one position
+    const float e0 = exp2f(v0 - m), e1 = exp2f(v1 - m);
+    const float l = warp_sum(e0 + e1);
+    S.p[g][lane] = f32_to_bf16(e0);
+    S.p[g][lane + 32] = f32_to_bf16(e1);
+    if (lane == 0) {
+      float* rec = part + ((int64_t(h) * gridDim.y + c) * G + g) * (TD + 2);
+      rec[TD] = m * 0.6931471805599453f;  // back to natural units
+      rec[TD + 1] = l;
+    }
+  }
+  __syncthreads();
+  // P V: warp w owns output columns w * TD/4 .. (w + 1) * TD/4 - 1
+  constexpr int NT = TD / 32;  // n-tiles of 8 per warp
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  const int mi = lane >> 3, ri = lane & 7;  // ldmatrix: matrix mi, row ri
+#pragma unroll
+  for (int j = 0; j < CHUNK / 16; ++j) {
+    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.p[gq][16 * j + 2 * cq]);
+    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.p[gq][16 * j + 8 + 2 * cq]);
+#pragma unroll
+    for (int pr = 0; pr < NT / 2; ++pr) {
+      uint32_t bv[4];
+      ldsm_x4_trans(bv, &S.v[16 * j + (mi & 1) * 8 + ri][warp * (TD / 4) + 16 * pr + (mi >> 1) * 8]);
+      mma_bf16(o[2 * pr], a0, 0u, a2, 0u, bv[0], bv[1]);
+      mma_bf16(o[2 * pr + 1], a0, 0u, a2, 0u, bv[2], bv[3]);
+    }
+  }
+  if (gq < G) {
+    float* rec = part + ((int64_t(h) * gridDim.y + c) * G + gq) * (TD + 2) + warp * (TD / 4);
+#pragma unroll
+    for (int i = 0; i < NT; ++i) *reinterpret_cast<float2*>(rec + 8 * i + 2 * cq) = make_float2(o[i][0], o[i][1]);
+  }
 }
 
 // one warp, one head of FD values (4 per lane): bf16(w * bf16(x * rsqrt(mean(x^2) + eps))), then

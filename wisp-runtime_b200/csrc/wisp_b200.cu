@@ -921,6 +921,20 @@ int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {
   return int64_t(Hk) * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * (D + 2);
 }
 
+// chunk partials of decode attention: the tensor-core kernel for head_dim 64 and 128, the CUDA-core one otherwise
+static cudaError_t launch_attn_split(dim3 grid, const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache,
+                                     const uint16_t* v_cache, int64_t tmax, const int64_t* pos, float scale, float* workspace,
+                                     int64_t kv_bstride, int window, cudaStream_t s) {
+  if (D == 128)
+    return launch_pdl(dec::attn_split_tc_kernel<128>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, k_cache, v_cache, tmax, pos, scale,
+                      workspace, kv_bstride, window);
+  if (D == 64)
+    return launch_pdl(dec::attn_split_tc_kernel<64>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, k_cache, v_cache, tmax, pos, scale,
+                      workspace, kv_bstride, window);
+  return launch_pdl(dec::attn_split_kernel, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
+                    kv_bstride, window);
+}
+
 int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache, int64_t tmax,
                          const int64_t* pos, float scale, float* workspace, uint16_t* out, void* stream) {
   WISP_REQUIRE(q && k_cache && v_cache && pos && workspace && out, "wisp_gqa_decode_attn: NULL pointer");
@@ -930,19 +944,9 @@ int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_
   WISP_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16), "wisp_gqa_decode_attn: caches must be 16-byte aligned");
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(Hk, nchunk);
-  cfg.blockDim = dim3(dec::ATTN_THREADS);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, dec::attn_split_kernel, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
-                                     int64_t(0), 0);
+  cudaError_t e = launch_attn_split(dim3(Hk, nchunk), q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace, 0, 0, s);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
-  e = launch_pdl(dec::attn_combine_kernel, Hq, 128, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, 0,
+  e = launch_pdl(dec::attn_combine_kernel, Hq, dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, 0,
                  (const float*)nullptr);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_attn");
@@ -968,10 +972,10 @@ int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D
                "wisp_gqa_decode_attn_batched: workspace of %lld floats is too small", (long long)workspace_floats);
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_pdl(dec::attn_split_kernel, dim3(Hk, nchunk, B), dec::ATTN_THREADS, 0, s, q, Hq, Hk, D, k_cache, v_cache, tmax,
-                             pos, scale, workspace, int64_t(Hk) * tmax * D, window);
+  cudaError_t e = launch_attn_split(dim3(Hk, nchunk, B), q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
+                                    int64_t(Hk) * tmax * D, window, s);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
-  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), 128, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, window,
+  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, window,
                  sinks);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_attn_batched");

@@ -63,11 +63,15 @@ class DecoderWeights:
     # ------------------------------------------------------------------------------------------------
     @staticmethod
     @torch.no_grad()
-    def random(cfg: DecoderConfig, device="cuda", seed=0, std=0.02, expert_std=0.02, resid_scale=False):
+    def random(cfg: DecoderConfig, device="cuda", seed=0, std=0.02, expert_std=0.02, resid_scale=False, local_experts=None,
+               router_std=0.5):
         """Seeded random-init weights of the given shape; experts quantized into a resident pool.
         ``resid_scale``: the projections that write into the residual stream (attention o_proj, the
         experts' down) start at std / sqrt(2 * layers), the scaled initialisation of GPT-2-style models,
-        so the stream stays dominated by the token's own embedding and routing follows the token."""
+        so the stream stays dominated by the token's own embedding and routing follows the token.
+        ``local_experts`` = (first, count): the pool holds only experts [first, first + count) of every
+        layer, slot l * count + (e - first) (one rank's share under expert parallelism; their weights
+        come from a generator seeded with ``seed`` + first)."""
         w = DecoderWeights(cfg)
         g = torch.Generator(device=device).manual_seed(seed)
         H, D, Hq, Hk, E, I, V = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.moe_inter, cfg.vocab
@@ -91,21 +95,24 @@ class DecoderWeights:
                     k_norm=norm(D),
                     wo=rnd(H, Hq * D, s=std / (2 * cfg.layers) ** 0.5 if resid_scale else std),
                     post_norm=norm(H),
-                    router=rnd(E, H, s=0.5),
+                    router=rnd(E, H, s=router_std),
                 )
             )
         n = H * I
         w.nbytes = quant.expert_nbytes(n, cfg.bits, cfg.group)
-        w.pool = torch.empty((cfg.layers * E, w.nbytes), dtype=torch.uint8, device=device)
+        first, count = (0, E) if local_experts is None else local_experts
+        if local_experts is not None:
+            g = torch.Generator(device=device).manual_seed(seed + first)
+        w.pool = torch.empty((cfg.layers * count, w.nbytes), dtype=torch.uint8, device=device)
         chunk = 32
         for l in range(cfg.layers):
-            for e0 in range(0, E, chunk):
-                e1 = min(E, e0 + chunk)
+            for e0 in range(0, count, chunk):
+                e1 = min(count, e0 + chunk)
                 w3 = torch.randn(e1 - e0, 3, n, device=device, generator=g) * expert_std
                 if resid_scale:
                     w3[:, 2] /= (2 * cfg.layers) ** 0.5
                 w3 = w3.to(bf)
-                w.pool[l * E + e0 : l * E + e1].copy_(quant.quantize_batch(w3, cfg.bits, cfg.group))
+                w.pool[l * count + e0 : l * count + e1].copy_(quant.quantize_batch(w3, cfg.bits, cfg.group))
                 del w3
         return w
 
