@@ -367,6 +367,11 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
 // through ldmatrix.trans.  Warp w scores positions 16w..16w+15 and owns D/4 output columns.  Scores
 // are kept in log2 units (exp2) and the record's maximum is stored back in natural units, which is
 // what attn_combine_kernel reads; P is rounded to bf16 for its MMA.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 template <int TD>
 struct SplitSmem {
   static constexpr int KP = TD + 8;  // padded rows: fragment loads are conflict-free
@@ -409,16 +414,18 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
     const uint16_t* kb = kc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
     const uint16_t* vb = vc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
     constexpr int PR = TD / 8;  // 16-byte pieces per row
+    // every piece of the chunk's K and V rows in flight at once (cp.async), rows outside [r0, r0 + n) zero
     for (int i = tid; i < CHUNK * PR; i += ATTN_THREADS) {
       const int r = i / PR, cp = i % PR;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
       if (r >= r0 && r < r0 + n) {
-        kv = reinterpret_cast<const uint4*>(kb + int64_t(r) * TD)[cp];
-        vv = reinterpret_cast<const uint4*>(vb + int64_t(r) * TD)[cp];
+        cp_async16(&S.k[r][8 * cp], kb + int64_t(r) * TD + 8 * cp);
+        cp_async16(&S.v[r][8 * cp], vb + int64_t(r) * TD + 8 * cp);
+      } else {
+        reinterpret_cast<uint4*>(&S.k[r][0])[cp] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(&S.v[r][0])[cp] = make_uint4(0, 0, 0, 0);
       }
-      reinterpret_cast<uint4*>(&S.k[r][0])[cp] = kv;
-      reinterpret_cast<uint4*>(&S.v[r][0])[cp] = vv;
     }
+    cp_async_wait_all();
     for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
       const int r = i / PR, cp = i % PR;
       reinterpret_cast<uint4*>(&S.q[r][0])[cp] =
