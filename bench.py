@@ -79,6 +79,12 @@ def parse():
                     help="decoder, device paging: page every miss in (all), only experts whose decayed use "
                     "frequency reached the cache's admit threshold (hot), only experts used more often than the "
                     "one they would evict (lfu), or none; misses are read from the pinned host store either way")
+    ap.add_argument("--profile-one-step", action="store_true",
+                    help="after the warm-up, one extra untimed step between cudaProfilerStart / Stop (for "
+                    "ncu --profile-from-start off)")
+    ap.add_argument("--kernel-shares", type=int, default=0,
+                    help="after the timed regions, run this many steps under the torch profiler (CUPTI) and print "
+                    "each kernel's device time and share to stderr")
     ap.add_argument("--batched-path", default="auto", choices=["auto", "mma", "tcgen05"],
                     help="moe-ep: the batched MoE kernels (auto = tcgen05 for 4/2-bit codes; mma = the warp-level path)")
     ap.add_argument("--transport", default="auto", choices=["auto", "nccl", "p2p"],
@@ -1404,6 +1410,25 @@ class EPStack:
 
 
 # ------------------------------------------------------------------------------------------------
+def kernel_shares(bench, steps):
+    """Device time per kernel over ``steps`` steps (torch profiler, CUDA activity) to stderr.  Kernels
+    chained by programmatic dependent launch start before their predecessor ends and wait inside, so
+    their durations overlap: the shares point at the heavy kernels, the step time is the bench's."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for t in range(steps):
+            bench.step(t)
+        torch.cuda.synchronize()
+    rows = [(e.key, e.device_time_total, e.count) for e in prof.key_averages() if e.device_time_total > 0]
+    tot = sum(r[1] for r in rows) or 1.0
+    print(f"kernel shares over {steps} steps (device time, us; PDL-overlapped durations)", file=sys.stderr)
+    for name, us, n in sorted(rows, key=lambda r: -r[1])[:25]:
+        print(f"{us:12.1f} {n:6d}x {100 * us / tot:6.2f}%  {name[:110]}", file=sys.stderr)
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -1446,6 +1471,11 @@ def main():
     for t in range(a.warmup):
         bench.step(t)
     torch.cuda.synchronize()
+    if a.profile_one_step:
+        torch.cuda.cudart().cudaProfilerStart()
+        bench.step(a.warmup)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
 
     def barrier():
         if world > 1:
@@ -1508,6 +1538,8 @@ def main():
         ctx = bench.dec.pos + a.warmup + 2 * a.steps + 3  # context length at the end of the timed steps
         roof["step_bytes_per_token"] = bench.bytes_per_token(ctx)
         roof["step_achieved_gbs"] = bench.bytes_per_token(ctx) / (ms / a.steps * 1e-3) / 1e9
+    if a.kernel_shares > 0:
+        kernel_shares(bench, a.kernel_shares)
     t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -13,7 +13,6 @@
 #include "dense.cuh"
 #include "moe_decode.cuh"
 #include "moe_decode_v4.cuh"
-#include "moe_decode_v5.cuh"
 #include "moe_batched.cuh"
 #include "moe_batched_umma.cuh"
 #include "moe_gptoss.cuh"
@@ -198,6 +197,34 @@ static int moe_shape(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   return WISP_OK;
 }
 
+// The opt-in for dynamic shared memory beyond 48 KB is an attribute of the kernel function, and a
+// captured graph node keeps its launch's size while the attribute keeps whatever was set last.  So
+// the attribute only ever grows: a later launch of the same kernel with less shared memory (a GEMV of
+// smaller K) must not lower it under a node captured earlier with more (profilers and graph updates
+// re-launch nodes against the function's current attribute).
+static void raise_smem_limit(const void* fn, size_t smem) {
+  if (smem == 0) return;
+  static std::mutex mu;
+  struct Entry {
+    const void* fn;
+    int dev;
+    size_t smem;
+  };
+  static Entry seen[512];
+  static int nseen = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < nseen; ++i)
+    if (seen[i].fn == fn && seen[i].dev == dev) {
+      if (smem > seen[i].smem && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) == cudaSuccess)
+        seen[i].smem = smem;
+      return;
+    }
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) == cudaSuccess && nseen < 512)
+    seen[nseen++] = Entry{fn, dev, smem};
+}
+
 static int v1_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
                      float* scratch, uint16_t* out, cudaStream_t s) {
   const int64_t H = S.H, I = S.I;
@@ -214,7 +241,7 @@ static int v1_launch(const uint8_t* pool, const float* meta, const uint16_t* x, 
 #define WISP_DN(B, U)                                                                                   \
   do {                                                                                                  \
     auto kern = moe_down_kernel<B, U>;                                                                  \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+    if (smem > 48 * 1024) raise_smem_limit(reinterpret_cast<const void*>(kern), smem);                   \
     kern<<<g2, 256, smem, s>>>(pool, meta, scratch, S, out);                                            \
   } while (0)
 #define WISP_BITS(B)                                   \
@@ -252,7 +279,7 @@ static int num_sms() {
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int block, size_t smem, cudaStream_t s, Args... args) {
   // dynamic shared memory beyond the default 48 KB window (static + dynamic) needs the opt-in
-  if (smem > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  raise_smem_limit(reinterpret_cast<const void*>(kern), smem);
   if (smem > 48 * 1024) {
     // the whole unified L1 as shared memory, so CTAs of the next kernel in a PDL chain fit beside
     // this one's (the carveout is chosen per launch; a smaller one would keep them out)
@@ -375,52 +402,10 @@ static int noalloc_scratch(float** out) {
 
 extern "C" {
 
-// the single-grid path (v5): the v4 shape rules plus a plan that fits; partials need k * cs * H floats
-static bool v5_plan(const MoeShape& S, int bits, int nctas, v5::Plan& P) {
-  if (!v4_supported(S, bits, nctas)) return false;
-  P = v5::plan(S.H, S.I, S.k, S.group, bits, nctas);
-  return P.ok && int64_t(S.k) * P.cs <= nctas;
-}
-
-static int64_t v5_scratch_floats(const MoeShape& S, const v5::Plan& P) { return int64_t(S.k) * P.cs * S.H; }
-
-static int v5_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits, const v5::Plan& P,
-                     float* scratch, uint16_t* out, cudaStream_t s, const MoeRoute& RT = MoeRoute{}) {
-  cudaError_t e = cudaSuccess;
-  const int grid = S.k * P.cs;
-  const bool paged = RT.host_store != nullptr;
-#define WISP_V5(B)                                                                                                         \
-  e = paged ? launch_pdl(v5::fused_kernel<B, true>, grid, v5::THREADS, size_t(P.bytes), s, pool, meta, x, S, P, scratch, RT)  \
-            : launch_pdl(v5::fused_kernel<B, false>, grid, v5::THREADS, size_t(P.bytes), s, pool, meta, x, S, P, scratch, RT);
-  switch (bits) {
-    case 4: WISP_V5(4) break;
-    case 3: WISP_V5(3) break;
-    case 2: WISP_V5(2) break;
-  }
-#undef WISP_V5
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode (single grid): %s", cudaGetErrorString(e));
-  const int g2 = int((S.H + 31) / 32);
-  e = launch_pdl(v5::combine_kernel, g2, 256, 0, s, (const float*)scratch, grid, int64_t(S.H), out);
-  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "moe_decode combine: %s", cudaGetErrorString(e));
-  return check_launch("moe_decode");
-}
-
 int64_t wisp_moe_scratch_floats(int k, int64_t H, int64_t I, int bits, int group) {
+  (void)H, (void)bits, (void)group;
   if (k < 1 || H <= 0 || I <= 0) return -1;
-  MoeShape S{};
-  S.k = k;
-  S.H = int(H);
-  S.I = int(I);
-  S.group = group;
-  S.gshift = 0;
-  for (int gq = group / 128; gq > 1 && (gq & 1) == 0; gq >>= 1) ++S.gshift;
-  const int64_t base = int64_t(k) * I;
-  v5::Plan P;
-  if (group > 0 && group % 128 == 0 && v5_plan(S, bits, num_sms(), P)) {
-    const int64_t v = v5_scratch_floats(S, P);
-    return v > base ? v : base;
-  }
-  return base;
+  return int64_t(k) * I;
 }
 
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
@@ -429,20 +414,13 @@ int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes,
   MoeShape S;
   int rc = moe_shape(pool, nslots, nbytes, meta, k, x, H, I, bits, group, scratch, out, S);
   if (rc) return rc;
-  WISP_REQUIRE(variant >= 0 && variant <= 3, "wisp_moe_decode_variant: variant must be 0 (auto), 1, 2 or 3");
+  WISP_REQUIRE(variant >= 0 && variant <= 2, "wisp_moe_decode_variant: variant must be 0 (auto), 1 or 2");
   WISP_REQUIRE(scratch_floats >= int64_t(k) * I, "wisp_moe_decode: scratch of %lld floats, need at least k*I = %lld",
                (long long)scratch_floats, (long long)(int64_t(k) * I));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nctas = num_sms();
-  v5::Plan P;
-  const bool ok3 = v5_plan(S, bits, nctas, P) && scratch_floats >= v5_scratch_floats(S, P);
   const bool ok2 = v4_supported(S, bits, nctas);
-  if (variant == 3 && !ok3)
-    return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape or scratch (%lld floats) not supported by variant 3",
-                (long long)scratch_floats);
   if (variant == 2 && !ok2) return fail(WISP_ERR_UNSUPPORTED, "wisp_moe_decode_variant: shape not supported by variant 2");
-  // variant 3 only on request: measured 19 us per Qwen3 layer against 12.4 us for the two-kernel path
-  if (variant == 3) return v5_launch(pool, meta, x, S, bits, P, scratch, out, s);
   if (variant == 2 || (variant == 0 && ok2)) return v4_launch(pool, meta, x, S, bits, scratch, out, s, nctas);
   return v1_launch(pool, meta, x, S, bits, scratch, out, s);
 }
@@ -1093,7 +1071,7 @@ int wisp_rmsnorm(const uint16_t* x, const uint16_t* delta, uint16_t* sum_out, co
   }
   const size_t smem = size_t(H) * 4;
   // the kernel also has a small static array: opt in to large dynamic shared memory well before 48 KB
-  if (smem > 32 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (smem > 32 * 1024) raise_smem_limit(reinterpret_cast<const void*>(rmsnorm_kernel), smem);
   rmsnorm_kernel<<<(unsigned)rows, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, delta, sum_out, w, H, eps, out);
   return check_launch("rmsnorm");
 }
