@@ -74,15 +74,14 @@ int wisp_unpack_codes(const uint8_t* pool, int64_t pool_rows, int64_t nbytes, co
                       int64_t n, int bits, uint8_t* codes, void* stream);
 
 /* ---- fused MoE decode, one token ---------------------------------------------------------------- */
-/* Floats of scratch that let every path run for this shape on the current device: at least k*I (the
- * two-kernel path's intermediate a), k * cs * H when the single-grid variant 3 applies (its partial
- * output vectors, cs = CTAs per expert).  Host-only; -1 for an invalid shape. */
+/* Floats of scratch every path needs for this shape: k*I (the intermediate a = silu(g) * u).
+ * Host-only; -1 for an invalid shape. */
 int64_t wisp_moe_scratch_floats(int k, int64_t H, int64_t I, int bits, int group);
 
 /* out[h] = sum_j w_j * Wd_j[h,:] . (silu(Wg_j x) * (Wu_j x)), dequant folded into the dot products,
  * weights read straight from the slot pool.  meta: fp32 [2k] = [slot_0..slot_{k-1}, w_0..w_{k-1}] on
  * the device.  x, out: bf16 [H].  scratch: fp32 [scratch_floats], at least k*I (the intermediate
- * a = silu(g) * u); wisp_moe_scratch_floats() floats also admit variant 3.
+ * a = silu(g) * u).
  * bits in {8, 4, 3, 2}; H, I multiples of 32 and of group; group a multiple of 32; pool 16-byte
  * aligned with nbytes a multiple of 16.
  * Replaces wisp/kernels.py:188-203 (moe_decode_q4_fast), :310-322 (moe_decode_q3_fast), and adds the
@@ -96,12 +95,7 @@ int wisp_moe_decode(const uint8_t* pool, int64_t nslots, int64_t nbytes, const f
  * feeding the warp-level integer MMA (u8 codes x int8 activation limbs, exact int32 sums), gate/up
  * and down as two kernels chained by programmatic dependent launch, the gate/up grid pulling the
  * down rows into L2 while it computes (bits 4/3/2, group a multiple of 128, H and I multiples of
- * 128, k <= 32, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise), 3 = one grid of
- * k * cs CTAs: CTA (j, r) computes rows [i0, i1) of a_j (the variant-2 math) and at once their
- * contribution to every output row from the down matrix's column slice (no grid-wide dependency),
- * then a small grid sums the k * cs partials in a fixed order (the variant-2 shape rules, a plan
- * that fits shared memory, scratch of wisp_moe_scratch_floats() floats; only on request: its
- * serialized load / gate-up / down / combine phases measured slower than variant 2).
+ * 128, k <= 32, at most 16 output rows per SM; WISP_ERR_UNSUPPORTED otherwise).
  * Automatic = 2 when it applies, else 1. */
 int wisp_moe_decode_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes, const float* meta, int k,
                             const uint16_t* x, int64_t H, int64_t I, int bits, int group, float* scratch,

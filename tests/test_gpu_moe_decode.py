@@ -53,15 +53,15 @@ def _setup(bits, H, I, E, k, G=128, seed=0):
     return pool, x, perm, wts
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+@pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("bits", [4, 3, 2, 8])
 def test_full_shape_vs_oracle(bits, variant):
     """Qwen3-30B-A3B layer shape: H=2048, I=768, top-8 of 16 resident experts, every kernel variant
-    (0 = automatic, 1 = warp-per-row CUDA cores, 2 = bulk copies + integer MMA in two kernels, 3 = one
-    grid with per-CTA down slices and a fixed-order partial sum; 2 and 3 take 4/3/2-bit experts only)."""
+    (0 = automatic, 1 = warp-per-row CUDA cores, 2 = bulk copies + integer MMA in two kernels; 2 takes
+    4/3/2-bit experts only)."""
     from wisp import kernels
 
-    if bits == 8 and variant in (2, 3):
+    if bits == 8 and variant == 2:
         pytest.skip("8-bit experts run on variant 1")
     H, I, E, k = 2048, 768, 16, 8
     n = H * I
@@ -88,7 +88,7 @@ def test_variants_agree_and_are_deterministic(bits):
     pool, x, slots, wts = _setup(bits, H, I, E, k, seed=40 + bits)
     meta = torch.cat([slots.float(), wts])
     o1 = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=1))
-    for v in (2, 3):
+    for v in (2,):
         ov = _bf16_np(kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, variant=v))
         # fp32 sums in a different order: results may differ by about one bf16 ulp of the largest output
         assert np.abs(ov - o1).max() <= 2.0**-7 * np.abs(o1).max(), v
@@ -299,17 +299,15 @@ def test_paged_rejects_unpinned_store_and_short_table():
                                  store_host=pool.cpu().pin_memory())
 
 
-def test_single_grid_needs_its_scratch():
-    """Variant 3 refuses a k*I scratch (its partial vectors need wisp_moe_scratch_floats floats); the
-    automatic choice is the two-kernel path whatever the scratch."""
+def test_scratch_is_k_times_I_and_unknown_variants_are_refused():
+    """Every path runs on k*I floats of scratch; a variant outside 0..2 is refused with WispError."""
     from wisp import _lib, kernels
 
     H, I, E, k, bits = 2048, 768, 16, 8, 4
     n = H * I
     pool, x, slots, wts = _setup(bits, H, I, E, k, seed=5)
     meta = torch.cat([slots.float(), wts])
-    need = _lib.lib().wisp_moe_scratch_floats(k, H, I, bits, 128)
-    assert need > k * I
+    assert _lib.lib().wisp_moe_scratch_floats(k, H, I, bits, 128) == k * I
     small = torch.empty(k * I, dtype=torch.float32, device="cuda")
     with pytest.raises(kernels.WispError):
         kernels.moe_decode_fast(pool, meta, x, k, n, H, I, bits, scratch=small, variant=3)

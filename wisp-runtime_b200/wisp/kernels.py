@@ -60,9 +60,8 @@ def _need_cuda(*ts):
 
 
 def moe_scratch(k, I, device, H=None, bits=4, group=128):
-    """Scratch for the fused MoE calls; reusable by calls that do not overlap.  With H (and the
-    quantization) it is sized for the fastest path (wisp_moe_scratch_floats: the single-grid path's
-    partial vectors), else k*I floats (the two-kernel path's intermediate a)."""
+    """Scratch for the fused MoE calls (k*I floats: the intermediate a = silu(g) * u, what
+    wisp_moe_scratch_floats reports); reusable by calls that do not overlap."""
     n = k * I
     if H is not None:
         with torch.cuda.device(torch.device(device)) if torch.device(device).type == "cuda" else _null():
