@@ -358,6 +358,19 @@ int wisp_router_rows(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w
                      const uint16_t* bias, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* meta,
                      int32_t* experts, float* row, void* stream);
 
+/* Bytes of the workspace of wisp_router_rows_ws (host-only; -1 for a bad shape). */
+int64_t wisp_router_workspace_bytes(int B, int E);
+
+/* wisp_router_rows with the gate split over CTAs (grid B x ceil(E / 4), one warp per expert): each
+ * CTA norms its token's row and computes four logits into the workspace; the last CTA of a token (an
+ * arrival counter in the workspace) runs the top-k and resets its counter.  The workspace (256-byte
+ * aligned, wisp_router_workspace_bytes(B, E) bytes) must be zero-filled before its first use and is
+ * left ready for the next launch; calls sharing one workspace must not overlap.  NULL workspace: the
+ * one-CTA-per-token kernel of wisp_router_rows.  Same results either way. */
+int wisp_router_rows_ws(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* W,
+                        const uint16_t* bias, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* meta,
+                        int32_t* experts, float* row, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* out [H] = table[*token] (bf16 rows, H % 8 == 0).  *token outside [0, V) sets WISP_STATUS_BAD_ROUTE. */
 int wisp_embed(const uint16_t* table, int64_t V, int64_t H, const int64_t* token, uint16_t* out, void* stream);
 

@@ -127,6 +127,38 @@ def test_router_rows(B, H, E, k, mode):
     assert torch.allclose(row[:, k:].sum(-1), torch.ones(B, device="cuda"), atol=2e-2) or mode is False
 
 
+@pytest.mark.parametrize("B,H,E,k,mode", [(1, 2880, 32, 4, "selected"), (64, 2048, 128, 8, True), (3, 256, 10, 3, False)])
+def test_router_split_matches_one_cta(B, H, E, k, mode):
+    """The gate split over CTAs (four experts each, the last CTA of a token runs the top-k) against the
+    one-CTA router: the same experts and weights (the RMSNorm's sum of squares is added in another order,
+    so the normed rows may differ by a bf16 step), and the workspace is left ready: a second launch on
+    it gives the same result."""
+    from wisp import kernels
+
+    g = _gen(B * 7 + E)
+    x = torch.randn(B, H, device="cuda", generator=g).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
+    W = (torch.randn(E, H, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(E, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    ws = kernels.router_workspace(B, E, "cuda")
+    outs = []
+    for workspace in (None, ws, ws):
+        xn = torch.empty_like(x)
+        row = torch.empty(B, 2 * k, dtype=torch.float32, device="cuda")
+        experts = torch.empty(B, k, dtype=torch.int32, device="cuda")
+        meta = kernels.router_rows(x, W, k, mode, norm_w=nw, eps=1e-5, bias=bias, xn_out=xn, base=3 * E, experts=experts, row=row,
+                                   workspace=workspace)
+        outs.append((xn, row, experts, meta))
+    assert torch.equal(outs[1][1], outs[2][1]) and torch.equal(outs[1][0], outs[2][0])  # repeatable on the same workspace
+    assert torch.count_nonzero(ws[-4 * B:]) == 0  # arrival counters back at zero
+    (xa, ra, ea, ma), (xb, rb, eb, mb) = outs[0], outs[1]
+    assert (xa.float() - xb.float()).abs().max().item() <= 2.0**-7 * xa.float().abs().max().item()
+    same = (ra[:, :k] == rb[:, :k]).all(-1)
+    assert same.float().mean().item() >= 0.9, same  # a near-tie may flip with a one-step difference in xn
+    assert (ra[same, k:] - rb[same, k:]).abs().max().item() <= 0.02
+    assert torch.equal(eb.long(), rb[:, :k].long()) and torch.equal(mb[:, :k].long(), rb[:, :k].long() + 3 * E)
+
+
 def test_gemv_rejects_aliasing():
     from wisp import kernels
     from wisp._lib import WispError

@@ -95,6 +95,8 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq,
 __device__ __forceinline__ int64_t window_lo(int64_t pos, int window) {
   return window > 0 && pos - window + 1 > 0 ? pos - window + 1 : 0;
 }
+// floats per chunk record: D outputs, the maximum, the sum, two pad floats (records start 16-byte aligned)
+__host__ __device__ constexpr int rec_floats(int D) { return D + 4; }
 
 __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t* __restrict__ q, int Hq, int Hk, int D,
                                                                   const uint16_t* __restrict__ kc,
@@ -124,7 +126,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
   q += int64_t(b) * Hq * D;
   kc += int64_t(b) * kv_bstride;
   vc += int64_t(b) * kv_bstride;
-  part += int64_t(b) * Hk * gridDim.y * G * (D + 2);
+  part += int64_t(b) * Hk * gridDim.y * G * rec_floats(D);
   {
     const uint4* kg = reinterpret_cast<const uint4*>(kc + (int64_t(h) * tmax + t0) * D);
     const uint4* vg = reinterpret_cast<const uint4*>(vc + (int64_t(h) * tmax + t0) * D);
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
     }
     l = warp_sum(l);
     if (lane == 0) {
-      float* rec = part + ((int64_t(h) * gridDim.y + c) * G + g) * (D + 2);
+      float* rec = part + ((int64_t(h) * gridDim.y + c) * G + g) * rec_floats(D);
       rec[D] = m;
       rec[D + 1] = l;
     }
@@ -232,23 +234,23 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_kernel(const uint16_t
     const int ln = d / dpl, e = d % dpl;
     float s = 0.0f;
     for (int w = 0; w < nw; ++w) s += red[w][g][ln * (MAX_D / 32) + e];
-    part[((int64_t(h) * gridDim.y + c) * G + g) * (D + 2) + d] = s;
+    part[((int64_t(h) * gridDim.y + c) * G + g) * rec_floats(D) + d] = s;
   }
 }
 
 // one CTA per (query head, sequence): out = sum_c O_c e^(m_c - M) / (sum_c l_c e^(m_c - M) [+ e^(sink - M)]);
 // sinks (fp32 [Hq], nullable) are per-head logits that take part in the softmax's normalisation but
-// contribute no value (attention sinks).  The chunks are spread over the threads (max and
-// normaliser) and over the warps (outputs: warp w sums chunks c0 + w, c0 + w + 4, ..., its lanes hold
-// D / 32 columns each), and the warps' sums are added in a fixed order, so long contexts keep many
-// independent loads in flight and the result does not depend on scheduling.
+// contribute no value (attention sinks).  One pass over the records: warp w merges chunks c0 + w,
+// c0 + w + 4, ... with a running maximum (each lane holds D / 32 outputs, loaded as float4 / float2 from
+// 16-byte aligned records), and the warps' states are merged in a fixed order, so the result does not
+// depend on scheduling.
 constexpr int CMB_THREADS = 128;
 __global__ void __launch_bounds__(CMB_THREADS) attn_combine_kernel(const float* __restrict__ part, int Hq, int Hk, int D,
                                                                    int nchunk_max, const int64_t* __restrict__ pos_ptr, int64_t tmax,
                                                                    uint16_t* __restrict__ out, int window,
                                                                    const float* __restrict__ sinks) {
   constexpr int NW = CMB_THREADS / 32;
-  __shared__ float red[NW];
+  __shared__ float wm[NW], wl[NW];
   __shared__ float osum[NW][MAX_D];
   const int head = blockIdx.x, b = blockIdx.y;
   const int G = Hq / Hk, h = head / G, g = head % G;
@@ -257,53 +259,54 @@ __global__ void __launch_bounds__(CMB_THREADS) attn_combine_kernel(const float* 
   pdl_launch_dependents();
   const int64_t pos = pos_ptr[b];
   if (pos < 0 || pos >= tmax) return;
-  part += int64_t(b) * Hk * nchunk_max * G * (D + 2);
+  const int rs = rec_floats(D);
+  part += int64_t(b) * Hk * nchunk_max * G * rs;
   out += int64_t(b) * Hq * D;
   const int c0 = int(window_lo(pos, window) / CHUNK), nc = int(pos / CHUNK) + 1;
-  const int64_t rs = D + 2;  // floats per record
   const float* rec0 = part + (int64_t(h) * nchunk_max * G + g) * rs;  // record of chunk c: rec0 + c * G * rs
-  // M = max over the chunks' maxima (and the sink)
-  float M = -INFINITY;
-  for (int c = c0 + threadIdx.x; c < nc; c += CMB_THREADS) M = fmaxf(M, rec0[int64_t(c) * G * rs + D]);
-  M = warp_max(M);
-  if (lane == 0) red[warp] = M;
-  __syncthreads();
-  M = sinks ? sinks[head] : -INFINITY;
-#pragma unroll
-  for (int w = 0; w < NW; ++w) M = fmaxf(M, red[w]);
-  __syncthreads();
-  // the normaliser
-  float Ls = 0.0f;
-  for (int c = c0 + threadIdx.x; c < nc; c += CMB_THREADS) {
-    const float* rec = rec0 + int64_t(c) * G * rs;
-    Ls += rec[D + 1] * __expf(rec[D] - M);
-  }
-  Ls = warp_sum(Ls);
-  if (lane == 0) red[warp] = Ls;
-  // the outputs: warp w takes chunks c0 + w, c0 + w + NW, ...
-  const int dpl = D / 32;
-  float acc[MAX_D / 32];
-#pragma unroll
-  for (int e = 0; e < MAX_D / 32; ++e) acc[e] = 0.0f;
-#pragma unroll 2
+  const int dpl = D / 32;  // outputs per lane: 1, 2, 3 or 4
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float m = -INFINITY, l = 0.0f;
+#pragma unroll 4
   for (int c = c0 + warp; c < nc; c += NW) {
     const float* rec = rec0 + int64_t(c) * G * rs;
-    const float f = __expf(rec[D] - M);
+    const float2 ml = *reinterpret_cast<const float2*>(rec + D);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (dpl == 4) {
+      const float4 t = reinterpret_cast<const float4*>(rec)[lane];
+      v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+    } else if (dpl == 2) {
+      const float2 t = reinterpret_cast<const float2*>(rec)[lane];
+      v[0] = t.x, v[1] = t.y;
+    } else {
+      for (int e = 0; e < dpl; ++e) v[e] = rec[lane * dpl + e];
+    }
+    const float mn = fmaxf(m, ml.x);
+    const float so = __expf(m - mn), sc = __expf(ml.x - mn);  // m = -inf at the first chunk: so = 0
 #pragma unroll
-    for (int e = 0; e < MAX_D / 32; ++e)
-      if (e < dpl) acc[e] = fmaf(rec[lane * dpl + e], f, acc[e]);
+    for (int e = 0; e < 4; ++e) acc[e] = acc[e] * so + v[e] * sc;
+    l = l * so + ml.y * sc;
+    m = mn;
   }
+  if (lane == 0) wm[warp] = m, wl[warp] = l;
 #pragma unroll
-  for (int e = 0; e < MAX_D / 32; ++e)
+  for (int e = 0; e < 4; ++e)
     if (e < dpl) osum[warp][lane * dpl + e] = acc[e];
   __syncthreads();
-  float L = sinks ? __expf(sinks[head] - M) : 0.0f;
+  float M = sinks ? sinks[head] : -INFINITY;
 #pragma unroll
-  for (int w = 0; w < NW; ++w) L += red[w];
+  for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w]);
+  float L = sinks ? __expf(sinks[head] - M) : 0.0f;
+  float f[NW];
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    f[w] = wm[w] == -INFINITY ? 0.0f : __expf(wm[w] - M);  // a warp with no chunk contributes nothing
+    L += wl[w] * f[w];
+  }
   for (int d = threadIdx.x; d < D; d += CMB_THREADS) {
     float o = 0.0f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) o += osum[w][d];
+    for (int w = 0; w < NW; ++w) o += osum[w][d] * f[w];
     out[int64_t(head) * D + d] = f32_to_bf16(o / L);
   }
 }
@@ -409,7 +412,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
   q += int64_t(b) * Hq * TD;
   kc += int64_t(b) * kv_bstride;
   vc += int64_t(b) * kv_bstride;
-  part += int64_t(b) * Hk * gridDim.y * G * (TD + 2);
+  part += int64_t(b) * Hk * gridDim.y * G * rec_floats(TD);
   {
     const uint16_t* kb = kc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
     const uint16_t* vb = vc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
@@ -464,7 +467,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
     S.p[g][lane] = f32_to_bf16(e0);
     S.p[g][lane + 32] = f32_to_bf16(e1);
     if (lane == 0) {
-      float* rec = part + ((int64_t(h) * gridDim.y + c) * G + g) * (TD + 2);
+      float* rec = part + ((int64_t(h) * gridDim.y + c) * G + g) * rec_floats(TD);
       rec[TD] = m * 0.6931471805599453f;  // back to natural units
       rec[TD + 1] = l;
     }
@@ -489,7 +492,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
     }
   }
   if (gq < G) {
-    float* rec = part + ((int64_t(h) * gridDim.y + c) * G + gq) * (TD + 2) + warp * (TD / 4);
+    float* rec = part + ((int64_t(h) * gridDim.y + c) * G + gq) * rec_floats(TD) + warp * (TD / 4);
 #pragma unroll
     for (int i = 0; i < NT; ++i) *reinterpret_cast<float2*>(rec + 8 * i + 2 * cq) = make_float2(o[i][0], o[i][1]);
   }
@@ -873,6 +876,111 @@ __global__ void __launch_bounds__(ROUTER_THREADS) router_rows_kernel(
         row[int64_t(b) * 2 * k + k + lane] = w;
       }
     }
+  }
+}
+
+// The same router with the gate split over CTAs: grid (B, ceil(E / ROUTER_SPLIT_E)); CTA (b, s) norms
+// token b's row (every CTA of the token redundantly; CTA 0 stores it) and computes the logits of experts
+// [s*ROUTER_SPLIT_E, ...) with one warp per expert, into ws_logits [B, E] (fp32 values of the bf16
+// logits).  The last CTA of a token to finish (an arrival counter per token, after a fence) loads the
+// token's E logits and runs the top-k; it then resets the counter, so the workspace stays ready for
+// the next launch (it must be zero before the first one).  No CTA waits for another: the counter only
+// elects which one finishes.
+constexpr int ROUTER_SPLIT_E = 4;
+constexpr int ROUTER_SPLIT_THREADS = 32 * ROUTER_SPLIT_E;
+__global__ void __launch_bounds__(ROUTER_SPLIT_THREADS) router_split_kernel(
+    const uint16_t* __restrict__ x, int64_t H, const uint16_t* __restrict__ norm_w, float eps, uint16_t* __restrict__ xn_out,
+    const uint16_t* __restrict__ W, const uint16_t* __restrict__ bias, int E, int k, int norm_topk,
+    const int32_t* __restrict__ slot_table, int64_t base, float* __restrict__ meta, int32_t* __restrict__ experts,
+    float* __restrict__ row, float* __restrict__ ws_logits, unsigned int* __restrict__ ws_count) {
+  __shared__ __align__(16) uint16_t xs[ROUTER_MAX_H];
+  __shared__ float p[1024];
+  __shared__ float red[ROUTER_SPLIT_E];
+  __shared__ unsigned int s_last;
+  const int b = blockIdx.x, sl = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NW = ROUTER_SPLIT_E;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t nch = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(b) * H);
+  float ss = 0.0f;
+  for (int64_t c = threadIdx.x; c < nch; c += ROUTER_SPLIT_THREADS) {
+    const uint4 v = xr[c];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss += bf_lo(w4[i]) * bf_lo(w4[i]) + bf_hi(w4[i]) * bf_hi(w4[i]);
+    reinterpret_cast<uint4*>(xs)[c] = v;
+  }
+  if (norm_w) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) tot += red[w];
+    const float inv = rsqrtf(tot / float(H) + eps);
+    for (int64_t c = threadIdx.x; c < nch; c += ROUTER_SPLIT_THREADS) {
+      const uint4 v = reinterpret_cast<const uint4*>(xs)[c];
+      const uint4 wv = reinterpret_cast<const uint4*>(norm_w)[c];
+      const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = bf_lo(ww[i]) * bf16_to_f32(f32_to_bf16(bf_lo(xv[i]) * inv));
+        const float hi = bf_hi(ww[i]) * bf16_to_f32(f32_to_bf16(bf_hi(xv[i]) * inv));
+        o[i] = uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
+      }
+      const uint4 on = make_uint4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<uint4*>(xs)[c] = on;
+      if (xn_out && sl == 0) reinterpret_cast<uint4*>(xn_out + int64_t(b) * H)[c] = on;
+    }
+  } else if (xn_out && sl == 0) {
+    for (int64_t c = threadIdx.x; c < nch; c += ROUTER_SPLIT_THREADS)
+      reinterpret_cast<uint4*>(xn_out + int64_t(b) * H)[c] = reinterpret_cast<const uint4*>(xs)[c];
+  }
+  __syncthreads();
+  // this CTA's experts: warp w takes expert sl * NW + w
+  const int e = sl * NW + warp;
+  if (e < E) {
+    const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
+    const uint4* wr = reinterpret_cast<const uint4*>(W + int64_t(e) * H);
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 8
+    for (int64_t c = lane; c < nch; c += 32) {
+      const uint4 w = __ldg(wr + c), xv4 = xs4[c];
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w}, xv[4] = {xv4.x, xv4.y, xv4.z, xv4.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        a0 = fmaf(bf_lo(wv[q]), bf_lo(xv[q]), a0);
+        a1 = fmaf(bf_hi(wv[q]), bf_hi(xv[q]), a1);
+      }
+    }
+    const float acc = warp_sum(a0 + a1);
+    if (lane == 0) ws_logits[int64_t(b) * E + e] = bf16_to_f32(f32_to_bf16(acc + (bias ? bf16_to_f32(bias[e]) : 0.0f)));
+  }
+  __threadfence();  // this CTA's logits are visible device-wide before it counts itself in
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&ws_count[b], 1u) == gridDim.y - 1 ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (warp == 0) {
+    for (int i = lane; i < E; i += 32) p[i] = __ldcg(ws_logits + int64_t(b) * E + i);
+    __syncwarp();
+    int sele;
+    float w;
+    topk_weights(p, E, k, norm_topk, lane, sele, w);
+    if (lane < k) {
+      const int64_t slot = slot_table ? int64_t(slot_table[base + sele]) : base + sele;
+      meta[int64_t(b) * 2 * k + lane] = float(slot);
+      meta[int64_t(b) * 2 * k + k + lane] = w;
+      if (experts) experts[int64_t(b) * k + lane] = sele;
+      if (row) {
+        row[int64_t(b) * 2 * k + lane] = float(sele);
+        row[int64_t(b) * 2 * k + k + lane] = w;
+      }
+    }
+    if (lane == 0) ws_count[b] = 0u;  // every CTA of this token has counted itself in: ready for the next launch
   }
 }
 

@@ -896,7 +896,7 @@ int wisp_qk_norm_rope_kv_batched(const uint16_t* qkv, int B, int64_t qkv_stride,
 
 int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {
   if (Hq <= 0 || Hk <= 0 || D <= 0 || tmax <= 0 || Hq % Hk) return -1;
-  return int64_t(Hk) * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * (D + 2);
+  return int64_t(Hk) * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * dec::rec_floats(D);
 }
 
 // chunk partials of decode attention: the tensor-core kernel for head_dim 64 and 128, the CUDA-core one otherwise
@@ -932,7 +932,7 @@ int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_
 
 int64_t wisp_attn_batched_workspace_floats(int B, int Hq, int Hk, int D, int64_t tmax) {
   if (B < 1 || Hq <= 0 || Hk <= 0 || D <= 0 || tmax <= 0 || Hq % Hk) return -1;
-  return int64_t(B) * Hk * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * (D + 2);
+  return int64_t(B) * Hk * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * dec::rec_floats(D);
 }
 
 int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D, const uint16_t* k_cache, const uint16_t* v_cache,
@@ -1015,9 +1015,21 @@ int wisp_router_topk(const uint16_t* logits, int E, int k, int norm_topk, const 
   return check_launch("router_topk");
 }
 
+int64_t wisp_router_workspace_bytes(int B, int E) {
+  if (B < 1 || E < 1 || E > 1024) return -1;
+  return (int64_t(B) * E * 4 + 255) / 256 * 256 + int64_t(B) * 4;
+}
+
 int wisp_router_rows(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* W,
                      const uint16_t* bias, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* meta,
                      int32_t* experts, float* row, void* stream) {
+  return wisp_router_rows_ws(x, B, H, norm_w, eps, xn_out, W, bias, E, k, norm_topk, slot_table, base, meta, experts, row, nullptr, 0,
+                             stream);
+}
+
+int wisp_router_rows_ws(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w, float eps, uint16_t* xn_out, const uint16_t* W,
+                        const uint16_t* bias, int E, int k, int norm_topk, const int32_t* slot_table, int64_t base, float* meta,
+                        int32_t* experts, float* row, void* workspace, int64_t workspace_bytes, void* stream) {
   WISP_REQUIRE(x && W && meta, "wisp_router_rows: NULL pointer");
   WISP_REQUIRE(B >= 1 && B <= 65535, "wisp_router_rows: need 1 <= B <= 65535");
   WISP_REQUIRE(H > 0 && H % 8 == 0 && H <= dec::ROUTER_MAX_H, "wisp_router_rows: need H a multiple of 8, <= %d", dec::ROUTER_MAX_H);
@@ -1026,8 +1038,19 @@ int wisp_router_rows(const uint16_t* x, int B, int64_t H, const uint16_t* norm_w
   WISP_REQUIRE(aligned(x, 16) && aligned(W, 16) && (!norm_w || aligned(norm_w, 16)) && (!xn_out || aligned(xn_out, 16)),
                "wisp_router_rows: x, W, norm_w and xn_out must be 16-byte aligned");
   WISP_REQUIRE(xn_out != x, "wisp_router_rows: xn_out must not alias x");
-  const cudaError_t e = launch_pdl(dec::router_rows_kernel, B, dec::ROUTER_THREADS, 0, static_cast<cudaStream_t>(stream), x, H, norm_w,
-                                   eps, xn_out, W, bias, E, k, norm_topk, slot_table, base, meta, experts, row);
+  cudaError_t e;
+  if (workspace) {
+    WISP_REQUIRE(workspace_bytes >= wisp_router_workspace_bytes(B, E) && aligned(workspace, 256),
+                 "wisp_router_rows: workspace must be 256-byte aligned and hold wisp_router_workspace_bytes(B, E) bytes");
+    float* logits = static_cast<float*>(workspace);
+    unsigned int* count = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + (int64_t(B) * E * 4 + 255) / 256 * 256);
+    const dim3 grid(B, (E + dec::ROUTER_SPLIT_E - 1) / dec::ROUTER_SPLIT_E);
+    e = launch_pdl(dec::router_split_kernel, grid, dec::ROUTER_SPLIT_THREADS, 0, static_cast<cudaStream_t>(stream), x, H, norm_w, eps,
+                   xn_out, W, bias, E, k, norm_topk, slot_table, base, meta, experts, row, logits, count);
+  } else {
+    e = launch_pdl(dec::router_rows_kernel, B, dec::ROUTER_THREADS, 0, static_cast<cudaStream_t>(stream), x, H, norm_w, eps, xn_out, W,
+                   bias, E, k, norm_topk, slot_table, base, meta, experts, row);
+  }
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_router_rows: %s", cudaGetErrorString(e));
   return check_launch("router_rows");
 }

@@ -68,6 +68,8 @@ SIGNATURES = {
     "wisp_attn_decode": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _F, _P, _P]),
     "wisp_router_topk": (_I, [_P, _I, _I, _I, _P, _L, _P, _P, _P]),
     "wisp_router_rows": (_I, [_P, _I, _L, _P, _F, _P, _P, _P, _I, _I, _I, _P, _L, _P, _P, _P, _P]),
+    "wisp_router_rows_ws": (_I, [_P, _I, _L, _P, _F, _P, _P, _P, _I, _I, _I, _P, _L, _P, _P, _P, _P, _L, _P]),
+    "wisp_router_workspace_bytes": (_L, [_I, _I]),
     "wisp_embed": (_I, [_P, _L, _L, _P, _P, _P]),
     "wisp_argmax": (_I, [_P, _L, _P, _P, _P]),
     "wisp_rmsnorm": (_I, [_P, _P, _P, _P, _L, _L, _F, _P, _P]),

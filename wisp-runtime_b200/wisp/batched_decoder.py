@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib, kernels
+from . import kernels
 from .model import DecoderWeights, rotary_tables
 
 
@@ -62,6 +62,7 @@ class BatchedDecoder:
         self.sel = torch.zeros(B, self.k, dtype=torch.int64, device=dev)
         self.rw = torch.zeros(B, self.k, dtype=torch.float32, device=dev)
         self.attn_ws = kernels.attn_batched_workspace(B, self.Hq, self.Hk, self.D, self.tmax, dev)
+        self.router_ws = kernels.router_workspace(B, self.E, dev)
         self.moe_ws = None if ep is not None else kernels.moe_batched_workspace(B, self.k, self.H, self.I, dev)
         self.scale = self.D ** -0.5
         self.graph = None
@@ -102,12 +103,12 @@ class BatchedDecoder:
         bias = None if self.bias is None else self.bias[l]
         if self.ep is None:
             kernels.router_rows(self.h_mid, lw["router"], self.k, c.norm_topk, norm_w=lw["post_norm"], eps=eps, bias=bias,
-                                xn_out=self.xn, base=l * self.E, meta=self.meta, row=self.rrow[l])
+                                xn_out=self.xn, base=l * self.E, meta=self.meta, row=self.rrow[l], workspace=self.router_ws)
             kernels.moe_batched(self.w.pool, self.meta, self.xn, self.k, self.H * self.I, self.H, self.I, c.bits, c.group,
                                 out=self.moe, workspace=self.moe_ws, variant=self.variant)
         else:
             kernels.router_rows(self.h_mid, lw["router"], self.k, c.norm_topk, norm_w=lw["post_norm"], eps=eps, bias=bias,
-                                xn_out=self.xn, meta=self.meta, row=self.rrow[l])
+                                xn_out=self.xn, meta=self.meta, row=self.rrow[l], workspace=self.router_ws)
             self.sel.copy_(self.rrow[l, :, : self.k])
             self.rw.copy_(self.rrow[l, :, self.k :])
             self.moe.copy_(self.ep.forward(self.xn, self.sel, self.rw, layer=l))

@@ -167,6 +167,7 @@ class GptOssDecoder:
         self.experts = torch.zeros(B, self.k, dtype=torch.int32, device=dev)
         self.rrow = torch.zeros(self.L, B, 2 * self.k, dtype=torch.float32, device=dev)  # per layer [experts | weights]
         self.attn_ws = kernels.attn_batched_workspace(B, self.Hq, self.Hk, self.D, self.tmax, dev)
+        self.router_ws = kernels.router_workspace(B, self.E, dev)
         self.moe_ws = torch.empty(_lib.lib().wisp_moe_gptoss_workspace_bytes(B, self.k, self.H, self.I), dtype=torch.uint8,
                                   device=dev)
         self.tmp = torch.zeros(B, self.H, **d)
@@ -213,7 +214,8 @@ class GptOssDecoder:
             torch.addmm(lw["bo"], self.att.view(B, -1), lw["wo"].t(), out=self.tmp)
             torch.add(self.h, self.tmp, out=self.h_mid)
         kernels.router_rows(self.h_mid, lw["router"], self.k, "selected", norm_w=lw["post_norm"], eps=eps, bias=lw["router_b"],
-                            xn_out=self.xn, base=l * self.E, meta=self.meta, experts=self.experts, row=self.rrow[l])
+                            xn_out=self.xn, base=l * self.E, meta=self.meta, experts=self.experts, row=self.rrow[l],
+                            workspace=self.router_ws)
         kernels.moe_gptoss(self.w.pool, self.meta, self.experts, self.xn, self.k, self.H, self.I, c.bits, lw["gub"], lw["db"],
                            c.group, out=self.moe, workspace=self.moe_ws)
 

@@ -659,11 +659,21 @@ def router_topk(logits, k, norm_topk=True, slot_table=None, base=0, row=None, me
     return meta
 
 
+def router_workspace(B, E, device):
+    """Zero-filled workspace of the split router (router_rows(..., workspace=)); reusable by calls that
+    do not overlap (each launch leaves it zeroed again)."""
+    nb = _lib.lib().wisp_router_workspace_bytes(B, E)
+    if nb < 0:
+        raise WispError("router_workspace: bad shape")
+    return torch.zeros(nb, dtype=torch.uint8, device=device)
+
+
 def router_rows(x, W, k, norm_topk, norm_w=None, eps=1e-6, bias=None, xn_out=None, slot_table=None, base=0, meta=None,
-                experts=None, row=None):
+                experts=None, row=None, workspace=None):
     """Router of B tokens (x bf16 [B, H]) in one launch: RMSNorm (norm_w), gate logits W [E, H] (+ bias),
     top-k and weights (norm_topk 0 / 1 / 2 as in router_topk) -> meta fp32 [B, 2k] = [slots | weights];
-    optionally experts int32 [B, k], row fp32 [B, 2k] = [ids | weights], xn_out = the normed rows."""
+    optionally experts int32 [B, k], row fp32 [B, 2k] = [ids | weights], xn_out = the normed rows.  With
+    ``workspace`` (router_workspace) the gate is split over CTAs, four experts each."""
     _need_cuda(x, W)
     _bf16(x, W, norm_w, bias, xn_out)
     B, H = x.shape
@@ -674,10 +684,17 @@ def router_rows(x, W, k, norm_topk, norm_w=None, eps=1e-6, bias=None, xn_out=Non
     for t, dt in ((slot_table, torch.int32), (experts, torch.int32), (row, torch.float32), (meta, torch.float32)):
         if t is not None and (t.dtype != dt or not t.is_contiguous()):
             raise WispError("router_rows: slot_table / experts int32, meta / row float32, contiguous")
-    _lib.call(
-        "wisp_router_rows", x.data_ptr(), B, H, _ptr(norm_w), float(eps), _ptr(xn_out), W.data_ptr(), _ptr(bias), E, k, int(mode),
-        _ptr(slot_table), int(base), meta.data_ptr(), _ptr(experts), _ptr(row), _stream(x),
-    )
+    if workspace is None:
+        _lib.call(
+            "wisp_router_rows", x.data_ptr(), B, H, _ptr(norm_w), float(eps), _ptr(xn_out), W.data_ptr(), _ptr(bias), E, k,
+            int(mode), _ptr(slot_table), int(base), meta.data_ptr(), _ptr(experts), _ptr(row), _stream(x),
+        )
+    else:
+        _lib.call(
+            "wisp_router_rows_ws", x.data_ptr(), B, H, _ptr(norm_w), float(eps), _ptr(xn_out), W.data_ptr(), _ptr(bias), E, k,
+            int(mode), _ptr(slot_table), int(base), meta.data_ptr(), _ptr(experts), _ptr(row), workspace.data_ptr(),
+            workspace.numel(), _stream(x),
+        )
     return meta
 
 
