@@ -10,20 +10,24 @@
 //               item's (and the next item's) code rows
 //   warp 22     activation producer: the tokens' activation rows (fp16, 128-byte swizzled boxes of 32
 //               rows); a ring of its own, so the code ring runs ahead of the tensor core by its full depth
-//   warps 2-17  dequantize the codes into the MMA's A operand: per 8 codes one LOP3 builds fp16 pairs
-//               1024 + q, one HSUB2 makes q exact, one HFMA2 applies scale and min (a single rounding of
-//               q*s + m to fp16: closer to the exact weight than the reference's bf16(q*s + m)); the
-//               tile is written in the K-major 128-byte-swizzled layout the tensor core reads
-//   warp 1      one thread issues tcgen05.mma (kind::f16, M = 128, N = the item's tokens rounded up to
-//               32, K = 16 per instruction) for gate and up (or down) into TMEM, and commits each
-//               stage back to the producer and the dequantizers
+//   warps 2-17  dequantize the codes into the MMA's A operand, which lives in TMEM: per 8 codes one
+//               LOP3 builds fp16 pairs 1024 + q, one HSUB2 makes q exact, one HFMA2 applies scale and
+//               min (a single rounding of q*s + m to fp16: closer to the exact weight than the
+//               reference's bf16(q*s + m)); thread t of a warp owns weight row 32 (warp % 4) + t (the
+//               TMEM lane it may write) and stores its K pairs with tcgen05.st, four warps per lane
+//               quarter splitting the stage's code words
+//   warp 1      one thread issues tcgen05.mma (kind::f16, A from TMEM, B from shared memory, M = 128,
+//               N = the item's tokens rounded up to 32, K = 16 per instruction) for gate and up (or
+//               down) into TMEM accumulators, and commits each stage back to the producers
 //   warps 18-21 epilogue: tcgen05.ld of the accumulators; gate/up -> a = silu(g)*u as fp16 rows of the
 //               intermediate (pair-permuted, the down pass's activation operand); down -> fp32 rows of
 //               y that the combine kernel sums per token in a fixed order.  Two accumulator buffers in
 //               TMEM let this run while the other warps stream the next item.
 //
 // Each code word is read from HBM once per item, however many tokens the expert received (up to
-// NMAX per N tile), and it is unpacked once.  Inside a code word the MMA's K order is the pair order
+// NMAX per N tile), and it is unpacked once.  With A in TMEM the dequantized tile never passes through
+// shared memory: the tensor core reads only the codes' staging and the activation tiles there (the
+// shared-memory A tile, 32 KB written and read per stage, bounded the stage time at small N).  Inside a code word the MMA's K order is the pair order
 // (codes i and i + W/2 of a W-code word sit side by side); the activations are staged in the same
 // order, so the products are the plain dot products.
 //
@@ -45,21 +49,28 @@ constexpr int BK = 64;        // K per stage: 64 fp16 = one 128-byte swizzle row
 constexpr int NMAX = 64;      // tokens per N tile (MMA N <= 64; an expert with more tokens takes several tiles)
 constexpr int BOXR = 32;      // token rows per activation box; MMA N is a multiple of it
 constexpr int CST = 4;        // code stages
-constexpr int AST = 3;        // dequantized A stages
+constexpr int AST = 3;        // dequantized A stages (in TMEM)
 constexpr int BST = 6;        // activation stages
 constexpr int DQ_WARPS = 16;  // dequantizing warps (warps 2..17)
 constexpr int EPI_WARPS = 4;  // epilogue warps (warps 18..21: one per TMEM lane quarter)
 constexpr int EPI0 = 2 + DQ_WARPS;
 constexpr int BPROD = EPI0 + EPI_WARPS;  // warp 22: activation producer
 constexpr int THREADS = (BPROD + 1) * 32;
-// two accumulator buffers, so the epilogue of one item overlaps the main loop of the next; inside one,
-// every matrix has two accumulators that alternate over the K steps (two independent MMA chains per
-// matrix instead of one: with the few tokens of an expert each MMA is short and a single chain waits on
-// the previous MMA's result): gate/up [gate0 | gate1 | up0 | up1] of NMAX columns, down [down0 | down1]
+// TMEM columns: two accumulator buffers (the epilogue of one item overlaps the main loop of the next),
+// gate/up [gate | up] of NMAX columns each, down [down]; then AST stages of the A operand, BK/2
+// columns (fp16 pairs) per matrix.  The allocation is the next power of two.
 template <int MAT>
-constexpr uint32_t acc_cols() { return MAT == 0 ? 4 * NMAX : 2 * NMAX; }
+constexpr uint32_t acc_cols() { return MAT == 0 ? 2 * NMAX : NMAX; }
 template <int MAT>
-constexpr uint32_t tmem_cols() { return 2 * acc_cols<MAT>(); }
+constexpr uint32_t a_cols() { return (MAT == 0 ? 2 : 1) * (BK / 2); }
+template <int MAT>
+constexpr uint32_t a_base() { return 2 * acc_cols<MAT>(); }
+template <int MAT>
+constexpr uint32_t tmem_cols() {
+  constexpr uint32_t need = 2 * acc_cols<MAT>() + AST * a_cols<MAT>();
+  return need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+}
+static_assert(2 * acc_cols<0>() + AST * a_cols<0>() <= 512, "TMEM holds the accumulators and the A stages");
 
 template <int BITS, int MAT>
 struct Cfg {
@@ -67,11 +78,8 @@ struct Cfg {
   static constexpr int CODE_ROW = BK * BITS / 8;            // code bytes of one row per stage
   static constexpr int CODE_MAT = BM * CODE_ROW;
   static constexpr int CODE_STAGE = NMAT * CODE_MAT;
-  static constexpr int A_MAT = BM * BK * 2;                 // 16 KB
-  static constexpr int A_STAGE = NMAT * A_MAT;
   static constexpr int B_STAGE = NMAX * BK * 2;             // 8 KB
-  static constexpr int OFF_A = 0;                           // 1024-aligned pieces first
-  static constexpr int OFF_B = OFF_A + AST * A_STAGE;
+  static constexpr int OFF_B = 0;                           // 1024-aligned pieces first
   static constexpr int OFF_C = OFF_B + BST * B_STAGE;
   static constexpr int OFF_S = OFF_C + CST * CODE_STAGE;    // scales/mins: 2 item buffers
   static __host__ __device__ constexpr int scale_bytes(int gpr) { return NMAT * 2 * BM * gpr * 2; }
@@ -108,13 +116,6 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// D[tmem] (+)= A[smem] . B[smem]^T, fp16 inputs, fp32 accumulation
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // 16 consecutive fp32 columns of this thread's TMEM lane
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -125,6 +126,28 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// D[tmem] (+)= A[tmem] . B[smem]^T, fp16 inputs, fp32 accumulation (A: 128 lanes = rows, K/2 columns)
+__device__ __forceinline__ void tc_mma_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// this thread's TMEM lane, N consecutive 32-bit columns from taddr
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]),
+      "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // shared-memory matrix descriptor: K-major operand in the 128-byte swizzled canonical layout (rows of
 // 128 bytes, 8-row atoms of 1 KB stacked at a stride of 1 KB), Blackwell descriptor version 1
@@ -179,8 +202,6 @@ __device__ __forceinline__ Item item_of(int i, int rtiles, int maxnt) {
   return it;
 }
 
-// byte offset of 16-byte chunk `ch` of row r in a 128-row, 128-byte-row swizzled tile
-__device__ __forceinline__ uint32_t sw128_off(int r, int ch) { return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4)); }
 
 // ---- activation staging: the tokens' rows in group order, fp16, pair-permuted ---------------------------
 // xh[p] = x[order[p] / k] for every sorted position p; inside each code word's span of W = 32/BITS
@@ -243,7 +264,6 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
   const int KT = K / BK;
   const int gpr = K / S.group;                      // quantization groups per row
   const int sc_bytes = (C::scale_bytes(gpr) + 127) / 128 * 128;
-  uint8_t* sA = smem + C::OFF_A;
   uint8_t* sB = smem + C::OFF_B;
   uint8_t* sC = smem + C::OFF_C;
   uint8_t* sS = smem + C::OFF_S;
@@ -409,14 +429,13 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
         if (!ok) break;
         if (lane == 0) {
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + as * C::A_STAGE), b0 = smem_u32(sB + bs * C::B_STAGE);
+          const uint32_t a0 = tmem + a_base<MAT>() + as * a_cols<MAT>(), b0 = smem_u32(sB + bs * C::B_STAGE);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t bd = sdesc_sw128(b0 + kk * 32);
-            const uint32_t acc = kt != 0 || kk >= 2;  // each of the two accumulators starts at its first K step
-            const uint32_t half = (kk & 1) * NMAX;
-            tc_mma(d0 + half, sdesc_sw128(a0 + kk * 32), bd, idesc, acc);
-            if (MAT == 0) tc_mma(d0 + 2 * NMAX + half, sdesc_sw128(a0 + C::A_MAT + kk * 32), bd, idesc, acc);
+            const uint32_t acc = kt != 0 || kk != 0;
+            tc_mma_ta(d0, a0 + kk * 8, bd, idesc, acc);  // A: 8 columns = 16 fp16 of K per lane (row)
+            if (MAT == 0) tc_mma_ta(d0 + NMAX, a0 + BK / 2 + kk * 8, bd, idesc, acc);
           }
           tc_commit(a_empty + as);  // arrives once these MMAs have read the stage
           tc_commit(b_empty + bs);
@@ -435,12 +454,18 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
     }
     __syncwarp();
   } else if (warp < EPI0) {
-    // ================= dequantize =================
-    const int d = threadIdx.x - 64;      // 0 .. 32 DQ_WARPS - 1
-    constexpr int WPR = BK * BITS / 32;  // code words per row per stage: 8 (4-bit), 4 (2-bit)
-    constexpr int RPT = BM * WPR / (DQ_WARPS * 32);  // rows per thread per matrix: 2 / 1
-    const int wc = d % WPR, rb = d / WPR;
-    constexpr int RSTEP = DQ_WARPS * 32 / WPR;  // 64 / 128
+    // ================= dequantize into TMEM =================
+    // thread t of warp w writes weight row 32 (w % 4) + t (its TMEM lane); the four warps of a lane
+    // quarter split the stage's code words: flat word f = sub * WPS + j over [matrix][word of the row]
+    const int q4 = warp & 3, sub = (warp - 2) >> 2;  // warps 2..17: four per quarter
+    const int r = 32 * q4 + lane;                      // weight row of the tile
+    constexpr int WPR = BK * BITS / 32;               // code words per row per stage and matrix: 8 (4-bit), 4 (2-bit)
+    constexpr int WPS = C::NMAT * WPR / 4;            // words of a row this thread takes per stage: 4/2 (gate/up), 2/1 (down)
+    constexpr int UPW = 16 / BITS;                    // fp16 pairs (TMEM columns) per code word: 4 / 8
+    constexpr int NCOL = WPS * UPW;                   // 16 (gate/up) or 8 (down)
+    static_assert(NCOL == 16 || NCOL == 8, "one tcgen05.st per stage");
+    const int m = (sub * WPS) / WPR, wc0 = (sub * WPS) % WPR;  // the thread's matrix and first word
+    const uint32_t lane_addr = tmem + (uint32_t(32 * q4) << 16) + a_base<MAT>() + uint32_t(m * (BK / 2) + wc0 * UPW);
     uint32_t cs = 0, cph = 0, as = 0, aph = 0, ss = 0, sph = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
@@ -450,56 +475,32 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
       ok = warp_wait(sc_full + ss, sph, abort);
       if (!ok) break;
       const __half* scl = reinterpret_cast<const __half*>(sS + ss * sc_bytes);
-      __half2 s2[C::NMAT][RPT], m2[C::NMAT][RPT];
+      __half2 s2 = __half2(__float2half_rn(0.0f), __float2half_rn(0.0f)), m2 = s2;
       int gcur = -1;
       for (int kt = 0; kt < KT; ++kt) {
         ok = warp_wait(code_full + cs, cph, abort) && warp_wait(a_empty + as, aph ^ 1, abort);
         if (!ok) break;
+        tc_fence_after();  // the MMAs that read this A stage have completed
         const int gcol = kt * BK / S.group;  // the stage's quantization group within the row
-        if (gcol != gcur) {  // scales and mins stay in registers for the stages of one group
+        if (gcol != gcur) {  // scale and min stay in registers for the stages of one group
           gcur = gcol;
-#pragma unroll
-          for (int m = 0; m < C::NMAT; ++m)
-#pragma unroll
-            for (int j = 0; j < RPT; ++j) {
-              const int r = rb + RSTEP * j;
-              const __half sv = scl[((2 * m) * BM + r) * gpr + gcol], mv = scl[((2 * m + 1) * BM + r) * gpr + gcol];
-              s2[m][j] = __half2(sv, sv);
-              m2[m][j] = __half2(mv, mv);
-            }
+          const __half sv = scl[((2 * m) * BM + r) * gpr + gcol], mv = scl[((2 * m + 1) * BM + r) * gpr + gcol];
+          s2 = __half2(sv, sv);
+          m2 = __half2(mv, mv);
         }
-        const uint8_t* cst = sC + cs * C::CODE_STAGE;
-        uint8_t* ast = sA + as * C::A_STAGE;
+        const uint8_t* cst = sC + cs * C::CODE_STAGE + m * C::CODE_MAT + r * C::CODE_ROW + 4 * wc0;
+        uint32_t w[WPS];
 #pragma unroll
-        for (int m = 0; m < C::NMAT; ++m) {
+        for (int j = 0; j < WPS; ++j) w[j] = reinterpret_cast<const uint32_t*>(cst)[j];
+        uint32_t o[16];
 #pragma unroll
-          for (int j = 0; j < RPT; ++j) {
-            const int r = rb + RSTEP * j;
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(cst + m * C::CODE_MAT + r * C::CODE_ROW + 4 * wc);
-            const __half2 sj = s2[m][j], mj = m2[m][j];
-            if (BITS == 4) {
-              uint4 o;
-              o.x = deq2(q_pair<4>(w, 0), sj, mj);
-              o.y = deq2(q_pair<4>(w, 1), sj, mj);
-              o.z = deq2(q_pair<4>(w, 2), sj, mj);
-              o.w = deq2(q_pair<4>(w, 3), sj, mj);
-              *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, wc)) = o;
-            } else {
-              uint4 o0, o1;
-              o0.x = deq2(q_pair<2>(w, 0), sj, mj);
-              o0.y = deq2(q_pair<2>(w, 1), sj, mj);
-              o0.z = deq2(q_pair<2>(w, 2), sj, mj);
-              o0.w = deq2(q_pair<2>(w, 3), sj, mj);
-              o1.x = deq2(q_pair<2>(w, 4), sj, mj);
-              o1.y = deq2(q_pair<2>(w, 5), sj, mj);
-              o1.z = deq2(q_pair<2>(w, 6), sj, mj);
-              o1.w = deq2(q_pair<2>(w, 7), sj, mj);
-              *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, 2 * wc)) = o0;
-              *reinterpret_cast<uint4*>(ast + m * C::A_MAT + sw128_off(r, 2 * wc + 1)) = o1;
-            }
-          }
-        }
-        fence_proxy_async();  // the generic-proxy stores become visible to the tensor core
+        for (int j = 0; j < WPS; ++j)
+#pragma unroll
+          for (int u = 0; u < UPW; ++u) o[j * UPW + u] = deq2(q_pair<BITS>(w[j], u), s2, m2);
+        if (NCOL == 16) tc_st16(lane_addr + as * a_cols<MAT>(), o);
+        else tc_st8(lane_addr + as * a_cols<MAT>(), o);
+        tc_wait_st();
+        tc_fence_before();  // the stores are ordered before the arrival the MMA thread waits on
         __syncwarp();
         if (lane == 0) {
           mbar_arrive1(a_full + as);
@@ -566,19 +567,16 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
       const uint32_t lane_base = tmem + (uint32_t(32 * q4) << 16) + buf * acc_cols<MAT>();
       const int pr = batched::perm_pos<BITS>(r);
       for (int c0 = 0; c0 < ntok; c0 += 16) {
-        uint32_t g[16], g1[16];
+        uint32_t g[16];
         tc_ld16(lane_base + c0, g);
-        tc_ld16(lane_base + NMAX + c0, g1);
         if (MAT == 0) {
-          uint32_t u[16], u1[16];
-          tc_ld16(lane_base + 2 * NMAX + c0, u);
-          tc_ld16(lane_base + 3 * NMAX + c0, u1);
+          uint32_t u[16];
+          tc_ld16(lane_base + NMAX + c0, u);
           tc_wait_ld();
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             if (c0 + c < ntok) {
-              const float gs = __uint_as_float(g[c]) + __uint_as_float(g1[c]), us = __uint_as_float(u[c]) + __uint_as_float(u1[c]);
-              float a = silu_mul(gs, us);
+              float a = silu_mul(__uint_as_float(g[c]), __uint_as_float(u[c]));
               if (!(fabsf(a) <= 65504.0f)) {  // outside fp16 (or NaN): saturate and say so
                 flag(WISP_STATUS_RANGE);
                 a = a != a ? 0.0f : copysignf(65504.0f, a);
@@ -591,7 +589,7 @@ __global__ void __launch_bounds__(THREADS, 1) grouped_umma_kernel(const __grid_c
           tc_wait_ld();
 #pragma unroll
           for (int c = 0; c < 16; ++c)
-            if (c0 + c < ntok) W.y[int64_t(row0 + c0 + c) * S.H + r] = __uint_as_float(g[c]) + __uint_as_float(g1[c]);
+            if (c0 + c < ntok) W.y[int64_t(row0 + c0 + c) * S.H + r] = __uint_as_float(g[c]);
         }
       }
       tc_fence_before();
