@@ -315,6 +315,16 @@ int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D
                                  int64_t tmax, const int64_t* pos, int window, const float* sinks, float scale, float* workspace,
                                  int64_t workspace_floats, uint16_t* out, void* stream);
 
+/* wisp_qk_norm_rope_kv_batched and wisp_gqa_decode_attn_batched in one pass over the cache: qkv
+ * [B, qkv_stride] holds each sequence's raw q, k, v heads; every attention CTA norms (qn_w, kn_w:
+ * both or neither) and rotates its query heads itself, and the CTA whose chunk holds pos[b] makes the
+ * new key / value row, writes it into the caches and uses it.  Same arithmetic, hence the same bits,
+ * as the two calls; one launch fewer.  D = 64 or 128 (WISP_ERR_UNSUPPORTED otherwise). */
+int wisp_attn_decode_batched(const uint16_t* qkv, int64_t qkv_stride, int B, int Hq, int Hk, int D, const uint16_t* qn_w,
+                             const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, uint16_t* k_cache,
+                             uint16_t* v_cache, int64_t tmax, const int64_t* pos, int window, const float* sinks, float scale,
+                             float* workspace, int64_t workspace_floats, uint16_t* out, void* stream);
+
 /* fp32 elements of the workspace wisp_gqa_decode_attn needs (host-only; -1 for a bad shape). */
 int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax);
 

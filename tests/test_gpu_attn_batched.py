@@ -88,3 +88,29 @@ def test_batched_rope_kv_write(norm):
             assert (q[b].float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
         others = [t for t in range(tmax) if t != p]
         assert (kc[b, :, others] == 0).all()  # nothing else of that cache was written
+
+
+@pytest.mark.parametrize("D,norm,window,use_sinks", [(128, True, 0, False), (64, False, 8, True), (64, False, 0, True)])
+def test_fused_rotary_attention_equals_two_calls(D, norm, window, use_sinks):
+    """wisp_attn_decode_batched (norm + rotary + cache write inside the attention kernel) against
+    qk_norm_rope_kv_batched + gqa_decode_attn_batched: the same bits in the output and in both caches,
+    sequences at their own positions (one at a chunk's first row, one at the cache's last)."""
+    from wisp import kernels
+    from wisp.model import rotary_tables
+
+    g = torch.Generator(device="cuda").manual_seed(D + window)
+    B, Hq, Hk, tmax = 4, 8, 2, 192
+    qkv = torch.randn(B, (Hq + 2 * Hk) * D, device="cuda", generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16) if norm else None
+    kn = (1 + 0.1 * torch.randn(D, device="cuda", generator=g)).to(torch.bfloat16) if norm else None
+    cos, sin = rotary_tables(D, tmax, 150000.0, "cuda")
+    pos = torch.tensor([0, 64, 100, 191], dtype=torch.int64, device="cuda")
+    kc = torch.randn(B, Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    sinks = torch.randn(Hq, device="cuda", generator=g).float() if use_sinks else None
+    kc2, vc2 = kc.clone(), vc.clone()
+    q = kernels.qk_norm_rope_kv_batched(qkv, Hq, Hk, D, qn, kn, 1e-6, cos, sin, pos, kc, vc)
+    want = kernels.gqa_decode_attn_batched(q, Hq, Hk, D, kc, vc, pos, D ** -0.5, window=window, sinks=sinks)
+    got = kernels.attn_decode_batched(qkv, Hq, Hk, D, qn, kn, 1e-6, cos, sin, pos, kc2, vc2, D ** -0.5, window=window, sinks=sinks)
+    assert torch.equal(got, want)
+    assert torch.equal(kc2, kc) and torch.equal(vc2, vc)

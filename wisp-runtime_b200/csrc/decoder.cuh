@@ -31,6 +31,32 @@ constexpr int MAX_G = 8;        // query heads per KV head (attention)
 // (pos_step 0); a chunk of one sequence's prompt (pos_step 0, pos_inc 1); one token of each of
 // several sequences (pos_step 1, pos_inc 0, kv_bstride = one sequence's cache).  qn_w == nullptr:
 // no per-head RMSNorm (models without q/k norms).
+// One warp, one head of D values: optional RMSNorm (HF: weight * bf16(x * rsqrt(mean(x^2) + eps)),
+// rounded to bf16) then rotate-half rotary in fp32 with one rounding per element (no FMA contraction),
+// into dst (bf16 [D], shared or global memory).  x: fp32 scratch [D] of this warp.
+__device__ __forceinline__ void norm_rope_warp(const uint16_t* __restrict__ src, const uint16_t* __restrict__ w, float eps,
+                                               const uint16_t* __restrict__ cs, const uint16_t* __restrict__ sn, int D, int lane,
+                                               float* x, uint16_t* dst) {
+  float ss = 0.0f;
+  for (int i = lane; i < D; i += 32) {
+    const float v = bf16_to_f32(src[i]);
+    x[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / float(D) + eps);
+  __syncwarp();
+  if (w)
+    for (int i = lane; i < D; i += 32) x[i] = bf16_to_f32(f32_to_bf16(bf16_to_f32(w[i]) * bf16_to_f32(f32_to_bf16(x[i] * inv))));
+  __syncwarp();
+  const int half = D / 2;
+  for (int i = lane; i < D; i += 32) {
+    const float xp = i < half ? -x[i + half] : x[i - half];
+    dst[i] = f32_to_bf16(__fadd_rn(__fmul_rn(x[i], bf16_to_f32(cs[i])), __fmul_rn(xp, bf16_to_f32(sn[i]))));
+  }
+  __syncwarp();
+}
+
 __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq, int Hk, int D,
                                        const uint16_t* __restrict__ qn_w, const uint16_t* __restrict__ kn_w, float eps,
                                        const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t,
@@ -60,29 +86,8 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* __restrict__ qkv, int Hq,
     return;
   }
   const bool is_q = head < Hq;
-  const uint16_t* w = is_q ? qn_w : kn_w;
-  float* x = xs[wib];
-  float ss = 0.0f;
-  for (int i = lane; i < D; i += 32) {
-    const float v = bf16_to_f32(src[i]);
-    x[i] = v;
-    ss = fmaf(v, v, ss);
-  }
-  ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / float(D) + eps);
-  __syncwarp();
-  // HF RMSNorm: weight * bf16(x * rsqrt(mean(x^2) + eps)), rounded to bf16
-  if (w)
-    for (int i = lane; i < D; i += 32) x[i] = bf16_to_f32(f32_to_bf16(bf16_to_f32(w[i]) * bf16_to_f32(f32_to_bf16(x[i] * inv))));
-  __syncwarp();
-  const uint16_t* cs = cos_t + pos * D;
-  const uint16_t* sn = sin_t + pos * D;
   uint16_t* dst = is_q ? q_out + int64_t(head) * D : kc + (int64_t(head - Hq) * tmax + pos) * D;
-  const int half = D / 2;
-  for (int i = lane; i < D; i += 32) {
-    const float xp = i < half ? -x[i + half] : x[i - half];
-    dst[i] = f32_to_bf16(__fadd_rn(__fmul_rn(x[i], bf16_to_f32(cs[i])), __fmul_rn(xp, bf16_to_f32(sn[i]))));
-  }
+  norm_rope_warp(src, is_q ? qn_w : kn_w, eps, cos_t + pos * D, sin_t + pos * D, D, lane, xs[wib], dst);
 }
 
 // ---- attention: chunk partials --------------------------------------------------------------------
@@ -383,14 +388,27 @@ struct SplitSmem {
   uint16_t v[CHUNK][KP];
   uint16_t p[16][CHUNK + 8];
   float s[MAX_G][CHUNK];
+  float x[ATTN_THREADS / 32][TD];  // per-warp scratch of the fused norm + rotary
 };
 
-template <int TD>
+// Operands of the fused form: the projection's raw q/k/v rows instead of rotated queries.
+struct RopeArgs {
+  const uint16_t* qkv;  // [B, qkv_stride]: q heads, k heads, v heads
+  int64_t qkv_stride;
+  const uint16_t *qn_w, *kn_w;  // nullable (no q/k norm)
+  float eps;
+  const uint16_t *cos_t, *sin_t;  // [tmax, D]
+};
+
+// ROPE: the queries come raw from qkv (RopeArgs); every CTA norms and rotates its G query heads itself,
+// and the CTA whose chunk holds pos also makes the new key / value row, writes it into the cache and
+// uses it directly (the arithmetic of qk_norm_rope_kv_kernel, so both forms give the same bits).
+template <int TD, bool ROPE>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint16_t* __restrict__ q, int Hq, int Hk,
-                                                                     const uint16_t* __restrict__ kc,
-                                                                     const uint16_t* __restrict__ vc, int64_t tmax,
-                                                                     const int64_t* __restrict__ pos_ptr, float scale,
-                                                                     float* __restrict__ part, int64_t kv_bstride, int window) {
+                                                                     uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
+                                                                     int64_t tmax, const int64_t* __restrict__ pos_ptr, float scale,
+                                                                     float* __restrict__ part, int64_t kv_bstride, int window,
+                                                                     RopeArgs ra) {
   static_assert(ATTN_THREADS == 128 && CHUNK == 64, "four warps of 16 positions");
   using Sm = SplitSmem<TD>;
   constexpr int KP = Sm::KP;
@@ -402,13 +420,18 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
   pdl_wait();
   pdl_launch_dependents();
   const int64_t pos = pos_ptr[b];
-  if (pos < 0 || pos >= tmax) return;  // flagged by the cache-write kernel
+  if (pos < 0 || pos >= tmax) {  // the unfused form's cache-write kernel flags it
+    if (ROPE && h == 0 && c == 0 && tid == 0) flag(WISP_STATUS_BAD_POS);
+    return;
+  }
   const int64_t lo = window_lo(pos, window);
   const int64_t t0 = int64_t(c) * CHUNK > lo ? int64_t(c) * CHUNK : lo;
   if (t0 > pos || t0 >= int64_t(c + 1) * CHUNK) return;  // outside [lo, pos]: the combine never reads this record
   const int n = int((pos + 1 - t0) < int64_t(c + 1) * CHUNK - t0 ? (pos + 1 - t0) : int64_t(c + 1) * CHUNK - t0);
   // positions t0 .. t0 + n - 1 sit in smem rows r0 .. r0 + n - 1 with r0 = t0 - c*CHUNK (a window can cut the chunk's start)
   const int r0 = int(t0 - int64_t(c) * CHUNK);
+  // fused form: the chunk holding pos makes the new row (smem row rnew); -1 elsewhere
+  const int rnew = ROPE && pos < int64_t(c + 1) * CHUNK ? int(pos - int64_t(c) * CHUNK) : -1;
   q += int64_t(b) * Hq * TD;
   kc += int64_t(b) * kv_bstride;
   vc += int64_t(b) * kv_bstride;
@@ -420,6 +443,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
     // every piece of the chunk's K and V rows in flight at once (cp.async), rows outside [r0, r0 + n) zero
     for (int i = tid; i < CHUNK * PR; i += ATTN_THREADS) {
       const int r = i / PR, cp = i % PR;
+      if (r == rnew) continue;  // made below
       if (r >= r0 && r < r0 + n) {
         cp_async16(&S.k[r][8 * cp], kb + int64_t(r) * TD + 8 * cp);
         cp_async16(&S.v[r][8 * cp], vb + int64_t(r) * TD + 8 * cp);
@@ -428,13 +452,41 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
         reinterpret_cast<uint4*>(&S.v[r][0])[cp] = make_uint4(0, 0, 0, 0);
       }
     }
-    cp_async_wait_all();
-    for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
-      const int r = i / PR, cp = i % PR;
-      reinterpret_cast<uint4*>(&S.q[r][0])[cp] =
-          r < G ? reinterpret_cast<const uint4*>(q + (int64_t(h) * G + r) * TD)[cp] : make_uint4(0, 0, 0, 0);
+    if (ROPE) {
+      for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
+        const int r = i / PR, cp = i % PR;
+        if (r >= G) reinterpret_cast<uint4*>(&S.q[r][0])[cp] = make_uint4(0, 0, 0, 0);
+      }
+      const uint16_t* row = ra.qkv + int64_t(b) * ra.qkv_stride;
+      const uint16_t* cs = ra.cos_t + pos * TD;
+      const uint16_t* sn = ra.sin_t + pos * TD;
+      for (int g = warp; g < G; g += ATTN_THREADS / 32)
+        norm_rope_warp(row + int64_t(h * G + g) * TD, ra.qn_w, ra.eps, cs, sn, TD, lane, S.x[warp], &S.q[g][0]);
+      if (rnew >= 0) {
+        // warp 0: the new key (norm + rotary) into the cache and into smem row rnew; warp 1: the value
+        uint16_t* kdst = kc + (int64_t(h) * tmax + pos) * TD;
+        if (warp == 0) {
+          norm_rope_warp(row + int64_t(Hq + h) * TD, ra.kn_w, ra.eps, cs, sn, TD, lane, S.x[0], &S.k[rnew][0]);
+          for (int i = lane; i < TD; i += 32) kdst[i] = S.k[rnew][i];
+        } else if (warp == 1) {
+          const uint16_t* vs = row + int64_t(Hq + Hk + h) * TD;
+          uint16_t* vdst = vc + (int64_t(h) * tmax + pos) * TD;
+          for (int i = lane; i < TD; i += 32) {
+            const uint16_t v = vs[i];
+            S.v[rnew][i] = v;
+            vdst[i] = v;
+          }
+        }
+      }
+    } else {
+      for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
+        const int r = i / PR, cp = i % PR;
+        reinterpret_cast<uint4*>(&S.q[r][0])[cp] =
+            r < G ? reinterpret_cast<const uint4*>(q + (int64_t(h) * G + r) * TD)[cp] : make_uint4(0, 0, 0, 0);
+      }
     }
     for (int i = tid; i < 16 * (CHUNK + 8) / 2; i += ATTN_THREADS) reinterpret_cast<uint32_t*>(&S.p[0][0])[i] = 0u;
+    cp_async_wait_all();  // the chunk's K / V rows (the query work above overlapped their flight)
   }
   __syncthreads();
   const float qscale = scale * 1.4426950408889634f;  // log2 units

@@ -903,12 +903,15 @@ int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {
 static cudaError_t launch_attn_split(dim3 grid, const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache,
                                      const uint16_t* v_cache, int64_t tmax, const int64_t* pos, float scale, float* workspace,
                                      int64_t kv_bstride, int window, cudaStream_t s) {
+  const dec::RopeArgs none{};
+  uint16_t* kc = const_cast<uint16_t*>(k_cache);  // not written without the fused rotary
+  uint16_t* vc = const_cast<uint16_t*>(v_cache);
   if (D == 128)
-    return launch_pdl(dec::attn_split_tc_kernel<128>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, k_cache, v_cache, tmax, pos, scale,
-                      workspace, kv_bstride, window);
+    return launch_pdl(dec::attn_split_tc_kernel<128, false>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, kc, vc, tmax, pos, scale,
+                      workspace, kv_bstride, window, none);
   if (D == 64)
-    return launch_pdl(dec::attn_split_tc_kernel<64>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, k_cache, v_cache, tmax, pos, scale,
-                      workspace, kv_bstride, window);
+    return launch_pdl(dec::attn_split_tc_kernel<64, false>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, kc, vc, tmax, pos, scale,
+                      workspace, kv_bstride, window, none);
   return launch_pdl(dec::attn_split_kernel, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
                     kv_bstride, window);
 }
@@ -957,6 +960,35 @@ int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D
                  sinks);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_attn_batched");
+}
+
+int wisp_attn_decode_batched(const uint16_t* qkv, int64_t qkv_stride, int B, int Hq, int Hk, int D, const uint16_t* qn_w,
+                             const uint16_t* kn_w, float eps, const uint16_t* cos_t, const uint16_t* sin_t, uint16_t* k_cache,
+                             uint16_t* v_cache, int64_t tmax, const int64_t* pos, int window, const float* sinks, float scale,
+                             float* workspace, int64_t workspace_floats, uint16_t* out, void* stream) {
+  WISP_REQUIRE(qkv && cos_t && sin_t && k_cache && v_cache && pos && workspace && out, "wisp_attn_decode_batched: NULL pointer");
+  WISP_REQUIRE((qn_w == nullptr) == (kn_w == nullptr), "wisp_attn_decode_batched: give both norm weights or neither");
+  WISP_REQUIRE(B >= 1 && B <= 65535, "wisp_attn_decode_batched: need 1 <= B <= 65535");
+  WISP_REQUIRE(Hq > 0 && Hk > 0 && Hq % Hk == 0 && Hq / Hk <= dec::MAX_G, "wisp_attn_decode_batched: need Hq a multiple of Hk, Hq/Hk <= %d",
+               dec::MAX_G);
+  if (D != 64 && D != 128) return fail(WISP_ERR_UNSUPPORTED, "wisp_attn_decode_batched: head_dim must be 64 or 128 (got %d)", D);
+  WISP_REQUIRE(tmax > 0 && window >= 0 && qkv_stride >= int64_t(Hq + 2 * Hk) * D, "wisp_attn_decode_batched: bad shape");
+  WISP_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16), "wisp_attn_decode_batched: caches must be 16-byte aligned");
+  WISP_REQUIRE(workspace_floats >= wisp_attn_batched_workspace_floats(B, Hq, Hk, D, tmax),
+               "wisp_attn_decode_batched: workspace of %lld floats is too small", (long long)workspace_floats);
+  const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dec::RopeArgs ra{qkv, qkv_stride, qn_w, kn_w, eps, cos_t, sin_t};
+  const int64_t kvb = int64_t(Hk) * tmax * D;
+  cudaError_t e = D == 128 ? launch_pdl(dec::attn_split_tc_kernel<128, true>, dim3(Hk, nchunk, B), dec::ATTN_THREADS, 0, s,
+                                        (const uint16_t*)nullptr, Hq, Hk, k_cache, v_cache, tmax, pos, scale, workspace, kvb, window, ra)
+                           : launch_pdl(dec::attn_split_tc_kernel<64, true>, dim3(Hk, nchunk, B), dec::ATTN_THREADS, 0, s,
+                                        (const uint16_t*)nullptr, Hq, Hk, k_cache, v_cache, tmax, pos, scale, workspace, kvb, window, ra);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_attn_decode_batched: %s", cudaGetErrorString(e));
+  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out,
+                 window, sinks);
+  if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_attn_decode_batched: %s", cudaGetErrorString(e));
+  return check_launch("attn_decode_batched");
 }
 
 int wisp_attn_decode(const uint16_t* qkv, int Hq, int Hk, int D, const uint16_t* qn_w, const uint16_t* kn_w, float eps,

@@ -64,6 +64,7 @@ SIGNATURES = {
     "wisp_qk_norm_rope_kv_batched": (_I, [_P, _I, _L, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _P, _P]),
     "wisp_attn_batched_workspace_floats": (_L, [_I, _I, _I, _I, _L]),
     "wisp_gqa_decode_attn_batched": (_I, [_P, _I, _I, _I, _I, _P, _P, _L, _P, _I, _P, _F, _P, _L, _P, _P]),
+    "wisp_attn_decode_batched": (_I, [_P, _L, _I, _I, _I, _I, _P, _P, _F, _P, _P, _P, _P, _L, _P, _I, _P, _F, _P, _L, _P, _P]),
     "wisp_gqa_decode_attn": (_I, [_P, _I, _I, _I, _P, _P, _L, _P, _F, _P, _P, _P]),
     "wisp_attn_decode": (_I, [_P, _I, _I, _I, _P, _P, _F, _P, _P, _P, _L, _P, _P, _F, _P, _P]),
     "wisp_router_topk": (_I, [_P, _I, _I, _I, _P, _L, _P, _P, _P]),

@@ -602,6 +602,29 @@ def gqa_decode_attn_batched(q, Hq, Hk, D, k_cache, v_cache, pos, scale, window=0
     return out
 
 
+def attn_decode_batched(qkv, Hq, Hk, D, qn_w, kn_w, eps, cos_t, sin_t, pos, k_cache, v_cache, scale, window=0, sinks=None,
+                        workspace=None, out=None):
+    """qk_norm_rope_kv_batched + gqa_decode_attn_batched in one pass (wisp_attn_decode_batched): qkv
+    [B, (Hq + 2 Hk) D] raw projections -> attention output [B, Hq, D]; the new K/V rows go into the
+    caches.  Same bits as the two calls.  D = 64 or 128."""
+    _need_cuda(qkv, pos, k_cache, v_cache)
+    _bf16(qkv, cos_t, sin_t, k_cache, v_cache, qn_w, kn_w)
+    B = qkv.shape[0]
+    tmax = k_cache.shape[-2]
+    if workspace is None:
+        workspace = attn_batched_workspace(B, Hq, Hk, D, tmax, qkv.device)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=qkv.device)
+    if sinks is not None and (sinks.dtype != torch.float32 or not sinks.is_contiguous()):
+        raise WispError("sinks must be contiguous float32")
+    _lib.call(
+        "wisp_attn_decode_batched", qkv.data_ptr(), qkv.stride(0), B, Hq, Hk, D, _ptr(qn_w), _ptr(kn_w), float(eps), cos_t.data_ptr(),
+        sin_t.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), tmax, pos.data_ptr(), int(window), _ptr(sinks), float(scale),
+        workspace.data_ptr(), workspace.numel(), out.data_ptr(), _stream(qkv),
+    )
+    return out
+
+
 def attn_workspace(Hq, Hk, D, tmax, device):
     n = _lib.lib().wisp_attn_workspace_floats(Hq, Hk, D, tmax)
     if n < 0:
