@@ -6,8 +6,8 @@ Per layer, for the B tokens at once:
 
     xn  = RMSNorm(h)                      (the previous layer's residual add fused in: wisp_rmsnorm)
     qkv = xn Wqkv^T                       (cuBLAS over the batch)
-    q   = rotary(q_norm(q)); k/v -> cache, then GQA attention over [0, pos[b]] (per-sequence positions),
-          one launch pair: wisp_attn_decode_batched
+    q   = rotary(q_norm(q)); k/v -> cache (wisp_qk_norm_rope_kv_batched, per-sequence positions)
+    att = GQA attention over [0, pos[b]]  (wisp_gqa_decode_attn_batched)
     h'  = h + att Wo^T
     xn  = RMSNorm(h'); router logits (+ an optional per-expert bias) -> softmax, top-8, renormalise
                                           (wisp_router_rows: one launch for the batch)
@@ -52,6 +52,7 @@ class BatchedDecoder:
         self.h_mid = torch.zeros(B, self.H, **d)
         self.xn = torch.zeros(B, self.H, **d)
         self.qkv = torch.zeros(B, (self.Hq + 2 * self.Hk) * self.D, **d)
+        self.q = torch.zeros(B, self.Hq, self.D, **d)
         self.att = torch.zeros(B, self.Hq, self.D, **d)
         self.tmp = torch.zeros(B, self.H, **d)
         self.moe = torch.zeros(B, self.H, **d)
@@ -94,8 +95,10 @@ class BatchedDecoder:
         else:
             kernels.rmsnorm(self.h_mid, lw["in_norm"], eps, delta=self.moe, sum_out=self.h, out=self.xn)
         torch.matmul(self.xn, lw["wqkv"].t(), out=self.qkv)
-        kernels.attn_decode_batched(self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], eps, self.cos, self.sin,
-                                    self.pos, self.kc[l], self.vc[l], self.scale, workspace=self.attn_ws, out=self.att)
+        q = kernels.qk_norm_rope_kv_batched(self.qkv, self.Hq, self.Hk, self.D, lw["q_norm"], lw["k_norm"], eps, self.cos,
+                                            self.sin, self.pos, self.kc[l], self.vc[l], q_out=self.q)
+        kernels.gqa_decode_attn_batched(q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], self.pos, self.scale,
+                                        workspace=self.attn_ws, out=self.att)
         torch.matmul(self.att.view(self.B, -1), lw["wo"].t(), out=self.tmp)
         torch.add(self.h, self.tmp, out=self.h_mid)
         bias = None if self.bias is None else self.bias[l]

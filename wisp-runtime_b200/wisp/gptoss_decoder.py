@@ -159,6 +159,7 @@ class GptOssDecoder:
         self.h_mid = torch.zeros(B, self.H, **d)
         self.xn = torch.zeros(B, self.H, **d)
         self.qkv = torch.zeros(B, (self.Hq + 2 * self.Hk) * self.D, **d)
+        self.q = torch.zeros(B, self.Hq, self.D, **d)
         self.att = torch.zeros(B, self.Hq, self.D, **d)
         self.moe = torch.zeros(B, self.H, **d)
         self.logits = torch.zeros(B, cfg.vocab, **d)
@@ -203,9 +204,11 @@ class GptOssDecoder:
             else:
                 kernels.rmsnorm(self.h_mid, lw["in_norm"], eps, delta=self.moe, sum_out=self.h, out=self.xn)
             torch.addmm(lw["bqkv"], self.xn, lw["wqkv"].t(), out=self.qkv)
+        q = kernels.qk_norm_rope_kv_batched(self.qkv, self.Hq, self.Hk, self.D, None, None, eps, self.cos, self.sin, self.pos,
+                                            self.kc[l], self.vc[l], q_out=self.q)
         window = c.window if c.layer_types[l] == "sliding_attention" else 0
-        kernels.attn_decode_batched(self.qkv, self.Hq, self.Hk, self.D, None, None, eps, self.cos, self.sin, self.pos, self.kc[l],
-                                    self.vc[l], self.scale, window=window, sinks=lw["sinks"], workspace=self.attn_ws, out=self.att)
+        kernels.gqa_decode_attn_batched(q, self.Hq, self.Hk, self.D, self.kc[l], self.vc[l], self.pos, self.scale, window=window,
+                                        sinks=lw["sinks"], workspace=self.attn_ws, out=self.att)
         if B == 1:
             kernels.gemv(lw["wo"], self.att.view(-1), bias=lw["bo"], res=self.h[0], out=self.h_mid[0])
         else:
