@@ -796,6 +796,10 @@ __device__ __forceinline__ void topk_weights(float* p, int E, int k, int norm_to
       const int oe = __shfl_xor_sync(0xffffffffu, be, o);
       if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
     }
+    if (be >= E) {  // nothing left that compares (NaN logits): a valid id with weight 0, never an id past E
+      be = j;
+      bv = 0.0f;
+    }
     if (lane == j) { selw = bv; sele = be; }
     tot += bv;
     __syncwarp();
