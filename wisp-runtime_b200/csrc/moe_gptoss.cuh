@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_kernel(const uint8_t* __restr
 }
 
 // The split partials are summed by SG thread groups (group g takes splits g, g + SG, ..., all loads
-// independent) and the groups' sums are added in order through shared memory, so the result does not
+// independent) and the groups' sums meet in a fixed tree through shared memory, so the result does not
 // depend on scheduling.  A block covers RED_THREADS / SG float4 columns of one pair (act) or one token
 // (combine).  Many splits over few pairs (one token) use 16 or 32 groups; few splits or many pairs use
 // one group (each thread sums its column's splits in order), so no thread idles and the grid stays
@@ -219,10 +219,13 @@ __global__ void __launch_bounds__(RED_THREADS) act_kernel(MoeShape S, int P, int
     }
     red[sg][c4] = acc;
     __syncthreads();
-    if (sg == 0 && col4 < n4) {
-      float4 v = red[0][c4];
 #pragma unroll
-      for (int g = 1; g < RED_SG; ++g) v = f4add(v, red[g][c4]);
+    for (int st = RED_SG / 2; st > 0; st >>= 1) {  // fixed tree over the groups
+      if (sg < st) red[sg][c4] = f4add(red[sg][c4], red[sg + st][c4]);
+      __syncthreads();
+    }
+    if (sg == 0 && col4 < n4) {
+      const float4 v = red[0][c4];
       const uint32_t lo = swiglu_clamped(v.x, v.y, uint16_t(bias.x), uint16_t(bias.x >> 16)),
                      hi = swiglu_clamped(v.z, v.w, uint16_t(bias.y), uint16_t(bias.y >> 16));
       *reinterpret_cast<uint32_t*>(W.act + int64_t(pos) * S.I + 2 * col4) = lo | (hi << 16);
@@ -279,13 +282,19 @@ __global__ void __launch_bounds__(RED_THREADS) combine_kernel(const float* __res
 #pragma unroll
       for (int jj = 0; jj < RED_KB; ++jj) red[jj][sg][c4] = acc[jj];
       __syncthreads();
+      // the groups' sums meet in a fixed tree (every thread of the lower half adds, log2(CMB_SG) steps)
+#pragma unroll
+      for (int st = CMB_SG / 2; st > 0; st >>= 1) {
+        if (sg < st)
+#pragma unroll
+          for (int jj = 0; jj < RED_KB; ++jj) red[jj][sg][c4] = f4add(red[jj][sg][c4], red[jj][sg + st][c4]);
+        __syncthreads();
+      }
       if (sg == 0 && col4 < n4) {
 #pragma unroll
         for (int jj = 0; jj < RED_KB; ++jj) {
           if (pos[jj] < 0) continue;
-          float4 v = red[jj][0][c4];
-#pragma unroll
-          for (int g = 1; g < CMB_SG; ++g) v = f4add(v, red[jj][g][c4]);
+          const float4 v = red[jj][0][c4];
           const float y[4] = {v.x, v.y, v.z, v.w};
           const uint16_t b[4] = {uint16_t(bias[jj].x), uint16_t(bias[jj].x >> 16), uint16_t(bias[jj].y), uint16_t(bias[jj].y >> 16)};
 #pragma unroll
