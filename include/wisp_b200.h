@@ -164,8 +164,8 @@ int wisp_moe_batched_variant(const uint8_t* pool, int64_t nslots, int64_t nbytes
  * (pair order).  send_x [world, capacity, H] bf16 gets x[t] at (d, c); send_meta [world, capacity, 2]
  * fp32 gets [slot_base + sel - d*E_local, 1] there and [-1, 0] in unused capacity (the batched MoE
  * skips those), so after the exchange the receiver's meta feeds wisp_moe_batched with k = 1;
- * src_pos [N*k] int32 = d*capacity + c for the combine.  capacity >= N*k.  Replaces the dispatch
- * bucketing the survey plans around NCCL (the reference has no expert parallelism). */
+ * src_pos [N*k] int32 = d*capacity + c for the combine.  capacity >= N*k.  Does the dispatch
+ * bucketing of a pack-then-all-to-all exchange over NCCL (the reference itself has no expert parallelism). */
 int wisp_ep_dispatch(const uint16_t* x, int N, int64_t H, const int64_t* sel, int k, int E_local, int world, int64_t capacity,
                      int64_t slot_base, uint16_t* send_x, float* send_meta, int32_t* src_pos, void* stream);
 
