@@ -17,6 +17,7 @@ struct MoeShape {
   int64_t ng;         // groups per expert
   int64_t mat_bytes;  // code bytes per matrix
   int glog;           // log2(group) when group is a power of two, else -1
+  int dn_beside;      // two-kernel pipeline: a down CTA fits beside a gate/up CTA (it fetches its own rows early)
 };
 
 // group index of element e of an expert's code stream (3n < 2^32 for every accepted shape): a shift

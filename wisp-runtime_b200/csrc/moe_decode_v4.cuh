@@ -25,14 +25,20 @@
 namespace wisp {
 namespace v4 {
 
-constexpr int GU_WARPS = 16;
-constexpr int DN_WARPS = 16;
+constexpr int GU_WARPS = 12;
+constexpr int DN_WARPS = 8;
 constexpr int GU_THREADS = GU_WARPS * 32;
 constexpr int DN_THREADS = DN_WARPS * 32;
 constexpr int CH = 8;           // rows per gate/up block (A rows 0-7 gate, 8-15 the same up rows)
-constexpr int NSPLIT = 2;       // K halves: two warps per gate/up block, two pieces per down expert
-constexpr int MAX_REGIONS = 8;  // gate/up blocks in flight per CTA (two warps each)
+constexpr int NSPLIT = 2;       // K halves: two warps per gate/up block
+constexpr int DN_SPLIT = 1;     // a down piece is one expert over all of I (one accumulator chain)
+constexpr int MAX_REGIONS = GU_WARPS / 2;  // gate/up blocks in flight per CTA (two warps each)
 constexpr int SMEM_LIMIT = 220 * 1024;
+// register caps that let one down CTA sit beside one gate/up CTA on an SM (65536 registers)
+constexpr int SM_SMEM_BYTES = 228 * 1024;  // shared memory of one B200 SM
+constexpr int GU_REGS = 96;
+constexpr int DN_REGS = 104;
+static_assert(GU_THREADS * GU_REGS + DN_THREADS * DN_REGS <= 65536, "gate/up and down CTAs must fit one SM together");
 
 template <int BITS>
 __device__ __forceinline__ void lds_unit(const uint8_t* p, uint32_t (&w)[BITS]) {
@@ -103,7 +109,7 @@ struct DnL {
 __host__ __device__ inline DnL dn_layout(int H, int I, int k, int group, int bits, int nctas) {
   DnL L;
   L.groups = I / 128;
-  L.groups_per_piece = (L.groups + NSPLIT - 1) / NSPLIT;
+  L.groups_per_piece = (L.groups + DN_SPLIT - 1) / DN_SPLIT;
   L.gpr = I / group;
   L.units = I / 32;
   L.rows_max = (H + nctas - 1) / nctas;  // <= 16 (checked on the host)
@@ -176,7 +182,7 @@ __device__ __forceinline__ const uint8_t* src_of(float f, const MoeShape& S, con
 }
 
 template <int BITS, bool PAGED>
-__global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* __restrict__ pool,
+__global__ void __maxnreg__(GU_REGS) gate_up_kernel(const uint8_t* __restrict__ pool,
                                                                 const float* __restrict__ meta,
                                                                 const uint16_t* __restrict__ x, MoeShape S,
                                                                 float* __restrict__ a_out, MoeRoute RT) {
@@ -261,8 +267,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
     __syncwarp();
     if ((warp >> 1) < nb) issue_block(warp >> 1);
   }
-  // the down rows the down kernel's CTA of the same index will read, pulled into L2 now
-  if (warp == GU_WARPS - 1) {
+  // the down rows the down kernel's CTA of the same index will read, pulled into L2 now (unless that
+  // CTA runs beside this one and brings them itself)
+  if (warp == GU_WARPS - 1 && !S.dn_beside) {
     const int h0 = int(int64_t(S.H) * blockIdx.x / gridDim.x), h1 = int(int64_t(S.H) * (blockIdx.x + 1) / gridDim.x);
     const int64_t gpr_d = S.I / S.group, row_d = int64_t(S.I) * BITS / 8;
     for (int j = lane; j < S.k && h1 > h0; j += 32) {
@@ -381,7 +388,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) gate_up_kernel(const uint8_t* _
 
 // ------------------------------------------------------------------------------------------------
 template <int BITS, bool PAGED>
-__global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __restrict__ pool,
+__global__ void __maxnreg__(DN_REGS) down_kernel(const uint8_t* __restrict__ pool,
                                                              const float* __restrict__ meta,
                                                              const float* __restrict__ a, MoeShape S,
                                                              uint16_t* __restrict__ out, MoeRoute RT) {
@@ -398,7 +405,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   const int nrows = h1 - h0;
   const int64_t ngm = S.ng / 3;
   const int units = Ld.units;
-  const int npieces = S.k * NSPLIT;  // (expert, K half)
+  const int npieces = S.k * DN_SPLIT;  // (expert, K piece)
 
   // routing: this runs before griddepcontrol.wait, after the producer of the routing inputs has
   // completed (the gate/up grid triggers this launch only after its own wait), so reads go to L2
@@ -491,7 +498,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
   pdl_launch_dependents();
 
   for (int piece = warp; piece < npieces; piece += DN_WARPS) {
-    const int j = piece / NSPLIT, sp = piece % NSPLIT;
+    const int j = piece / DN_SPLIT, sp = piece % DN_SPLIT;
     bool host;
     const bool ok = src_of<PAGED>(mt[j], S, pool, RT, host) != nullptr;
     const float wj = mt[S.k + j];
@@ -511,26 +518,30 @@ __global__ void __launch_bounds__(DN_THREADS, 1) down_kernel(const uint8_t* __re
     float acc = 0.0f;
     const uint32_t* bj = bd + int64_t(j) * units * 24;
     const float* ds = dsum + 2 * int64_t(j) * Ld.groups;
+    // groups in pairs (two independent MMA chains); an odd last group runs alone
     for (int G = 0; G < ng; G += 2) {
-      const int G1 = min(G + 1, ng - 1);
+      const bool two = G + 1 < ng;  // warp-uniform
       uint32_t wa0[BITS], wb0[BITS], wa1[BITS], wb1[BITS], bb0[8], bb1[8];
+      int d0[4], d1[4];
       lds_unit<BITS>(eb + g * Ld.row_bytes + (4 * (G0 + G) + c) * 4 * BITS, wa0);
       lds_unit<BITS>(eb + (g + 8) * Ld.row_bytes + (4 * (G0 + G) + c) * 4 * BITS, wb0);
-      lds_unit<BITS>(eb + g * Ld.row_bytes + (4 * (G0 + G1) + c) * 4 * BITS, wa1);
-      lds_unit<BITS>(eb + (g + 8) * Ld.row_bytes + (4 * (G0 + G1) + c) * 4 * BITS, wb1);
       lds_b8(g < 3 ? bj + ((4 * (G0 + G) + c) * 3 + g) * 8 : zero, bb0);
-      lds_b8(g < 3 ? bj + ((4 * (G0 + G1) + c) * 3 + g) * 8 : zero, bb1);
-      int d0[4], d1[4];
+      if (two) {
+        lds_unit<BITS>(eb + g * Ld.row_bytes + (4 * (G0 + G + 1) + c) * 4 * BITS, wa1);
+        lds_unit<BITS>(eb + (g + 8) * Ld.row_bytes + (4 * (G0 + G + 1) + c) * 4 * BITS, wb1);
+        lds_b8(g < 3 ? bj + ((4 * (G0 + G + 1) + c) * 3 + g) * 8 : zero, bb1);
+      }
       imma_group<BITS>(wa0, wb0, bb0, d0);
-      imma_group<BITS>(wa1, wb1, bb1, d1);
-      const float D0 = quad_row_dot(d0, c), D1 = quad_row_dot(d1, c);
+      if (two) imma_group<BITS>(wa1, wb1, bb1, d1);
+      const float D0 = quad_row_dot(d0, c);
       {
         const int qg = (G0 + G) >> S.gshift;
         acc += f16_bits_to_f32(srow[qg]) * (D0 * ds[2 * (G0 + G) + 1]) + f16_bits_to_f32(mrow[qg]) * ds[2 * (G0 + G)];
       }
-      if (G1 != G) {
-        const int qg = (G0 + G1) >> S.gshift;
-        acc += f16_bits_to_f32(srow[qg]) * (D1 * ds[2 * (G0 + G1) + 1]) + f16_bits_to_f32(mrow[qg]) * ds[2 * (G0 + G1)];
+      if (two) {
+        const float D1 = quad_row_dot(d1, c);
+        const int qg = (G0 + G + 1) >> S.gshift;
+        acc += f16_bits_to_f32(srow[qg]) * (D1 * ds[2 * (G0 + G + 1) + 1]) + f16_bits_to_f32(mrow[qg]) * ds[2 * (G0 + G + 1)];
       }
     }
     if (c < 2 && myrow < nrows) part[warp * 16 + myrow] += wj * acc;

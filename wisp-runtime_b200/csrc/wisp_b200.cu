@@ -194,6 +194,7 @@ static int moe_shape(const uint8_t* pool, int64_t nslots, int64_t nbytes, const 
   S.gshift = 0;
   for (int gq = group / 128; gq > 1 && (gq & 1) == 0; gq >>= 1) ++S.gshift;
   S.glog = log2_or_neg(group);
+  S.dn_beside = 0;
   return WISP_OK;
 }
 
@@ -312,10 +313,13 @@ static bool v4_supported(const MoeShape& S, int bits, int nctas) {
   return Lg.R > 0 && Ld.bytes <= v4::SMEM_LIMIT;
 }
 
-static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S, int bits,
+static int v4_launch(const uint8_t* pool, const float* meta, const uint16_t* x, const MoeShape& S_in, int bits,
                      float* scratch, uint16_t* out, cudaStream_t s, int nctas, const MoeRoute& RT = MoeRoute{}) {
-  const int64_t gsm = v4::gu_layout(S.H, S.I, S.k, S.group, bits, nctas).bytes;
-  const v4::DnL Ld = v4::dn_layout(S.H, S.I, S.k, S.group, bits, nctas);
+  const int64_t gsm = v4::gu_layout(S_in.H, S_in.I, S_in.k, S_in.group, bits, nctas).bytes;
+  const v4::DnL Ld = v4::dn_layout(S_in.H, S_in.I, S_in.k, S_in.group, bits, nctas);
+  // registers always allow a down CTA beside a gate/up CTA; shared memory (1 KB reserved per CTA) decides
+  MoeShape S = S_in;
+  S.dn_beside = gsm + Ld.bytes + 2 * 1024 <= int64_t(v4::SM_SMEM_BYTES);
   cudaError_t e = cudaSuccess;
   const bool paged = RT.host_store != nullptr;
 #define WISP_V4(B)                                                                                                    \
