@@ -39,7 +39,7 @@ N_ROUTES = 16  # moe-stack: distinct seeded routings (tokens) cycled through by 
 EP_BATCH = 64  # moe-ep: tokens per step over all ranks (config 4 batch)
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up + one down launch (4-bit, this shape),
 # from one ncu capture of the fused decode kernels
-NCU_TRAFFIC_PER_CALL = 13_405_696 + 6_746_368
+NCU_TRAFFIC_PER_CALL = 13_419_008 + 6_755_328
 # DRAM read + write of the batched gate/up and down grids for one 64-token Zipf(1.1) layer (ncu)
 NCU_TRAFFIC_BATCHED_LAYER = 96_768_256 + 3_038_720 + 48_437_504 + 489_472
 # DRAM bytes of the two gpt-oss GEMVs (gate_up + down) of one 20b layer at one token (4 experts), one ncu capture
