@@ -114,3 +114,58 @@ def test_fused_rotary_attention_equals_two_calls(D, norm, window, use_sinks):
     got = kernels.attn_decode_batched(qkv, Hq, Hk, D, qn, kn, 1e-6, cos, sin, pos, kc2, vc2, D ** -0.5, window=window, sinks=sinks)
     assert torch.equal(got, want)
     assert torch.equal(kc2, kc) and torch.equal(vc2, vc)
+
+
+def _ref_attn_gpu(q, kc, vc, pos, scale, window, sinks):
+    """_ref_attn on the GPU in fp32, all heads of a sequence at once (for long caches)."""
+    B, Hq, D = q.shape
+    Hk, tmax = kc.shape[1], kc.shape[2]
+    G = Hq // Hk
+    out = torch.zeros(B, Hq, D, device=q.device)
+    t = torch.arange(tmax, device=q.device)
+    for b in range(B):
+        p = int(pos[b])
+        lo = max(0, p - window + 1) if window > 0 else 0
+        s = torch.einsum("hgd,htd->hgt", q[b].float().view(Hk, G, D), kc[b].float()) * scale
+        s = s.masked_fill(((t < lo) | (t > p))[None, None], float("-inf"))
+        if sinks is not None:
+            s = torch.cat([s, sinks.float().view(Hk, G, 1)], -1)
+        w = torch.softmax(s, -1)[..., :tmax]
+        out[b] = torch.einsum("hgt,htd->hgd", w, vc[b].float()).reshape(Hq, D)
+    return out
+
+
+@pytest.mark.parametrize("D,Hq,Hk,B,tmax,window,use_sinks", [(128, 32, 4, 64, 4096, 0, False), (128, 32, 4, 64, 4096, 1000, True),
+                                                            (64, 64, 8, 32, 2048, 128, True)])
+def test_long_context_several_chunks_per_cta(D, Hq, Hk, B, tmax, window, use_sinks):
+    """At many sequences and long caches each attention CTA takes several consecutive chunks (an online
+    softmax across them) and writes one record for all of them: the output still matches the fp32
+    restatement, for positions at chunk edges, mid-chunk and at the cache's last slot, with a sliding
+    window that starts mid-chunk; the fused rotary form stays bit-identical to the two calls there."""
+    from wisp import _lib, kernels
+    from wisp.model import rotary_tables
+
+    g = torch.Generator(device="cuda").manual_seed(D + B + window)
+    q = torch.randn(B, Hq, D, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hk, tmax, D, device="cuda", generator=g).to(torch.bfloat16)
+    edges = [0, 63, 64, 255, 256, 257, tmax - 1, tmax - 64, 1000, 1023, 1024, 2047]
+    rnd = torch.randint(0, tmax, (B,), device="cuda", generator=g)
+    pos = torch.tensor([edges[i] if i < len(edges) else int(rnd[i]) for i in range(B)], dtype=torch.int64, device="cuda")
+    sinks = torch.randn(Hq, device="cuda", generator=g).float() * 2 if use_sinks else None
+    scale = D ** -0.5
+    _lib.device_status(0, clear=True)
+    out = kernels.gqa_decode_attn_batched(q, Hq, Hk, D, kc, vc, pos, scale, window=window, sinks=sinks)
+    ref = _ref_attn_gpu(q, kc, vc, pos, scale, window, sinks)
+    err = ((out.float() - ref).abs().amax(-1) / ref.abs().amax(-1).clamp_min(1e-6)).max().item()
+    assert err < 2 * TOL, err
+    assert _lib.device_status(0) == 0
+    # the fused rotary form at the same shape: the same bits as the two calls
+    qkv = torch.randn(B, (Hq + 2 * Hk) * D, device="cuda", generator=g).to(torch.bfloat16)
+    cos, sin = rotary_tables(D, tmax, 150000.0, "cuda")
+    kc2, vc2 = kc.clone(), vc.clone()
+    qr = kernels.qk_norm_rope_kv_batched(qkv, Hq, Hk, D, None, None, 1e-6, cos, sin, pos, kc, vc)
+    want = kernels.gqa_decode_attn_batched(qr, Hq, Hk, D, kc, vc, pos, scale, window=window, sinks=sinks)
+    got = kernels.attn_decode_batched(qkv, Hq, Hk, D, None, None, 1e-6, cos, sin, pos, kc2, vc2, scale, window=window, sinks=sinks)
+    assert torch.equal(got, want)
+    assert torch.equal(kc2, kc) and torch.equal(vc2, vc)

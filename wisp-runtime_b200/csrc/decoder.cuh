@@ -253,7 +253,7 @@ constexpr int CMB_THREADS = 128;
 __global__ void __launch_bounds__(CMB_THREADS) attn_combine_kernel(const float* __restrict__ part, int Hq, int Hk, int D,
                                                                    int nchunk_max, const int64_t* __restrict__ pos_ptr, int64_t tmax,
                                                                    uint16_t* __restrict__ out, int window,
-                                                                   const float* __restrict__ sinks) {
+                                                                   const float* __restrict__ sinks, int chunk) {
   constexpr int NW = CMB_THREADS / 32;
   __shared__ float wm[NW], wl[NW];
   __shared__ float osum[NW][MAX_D];
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(CMB_THREADS) attn_combine_kernel(const float* 
   const int rs = rec_floats(D);
   part += int64_t(b) * Hk * nchunk_max * G * rs;
   out += int64_t(b) * Hq * D;
-  const int c0 = int(window_lo(pos, window) / CHUNK), nc = int(pos / CHUNK) + 1;
+  const int c0 = int(window_lo(pos, window) / chunk), nc = int(pos / chunk) + 1;  // chunk: positions per record
   const float* rec0 = part + (int64_t(h) * nchunk_max * G + g) * rs;  // record of chunk c: rec0 + c * G * rs
   const int dpl = D / 32;  // outputs per lane: 1, 2, 3 or 4
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -369,7 +369,9 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
 }
 
 // ---- attention chunk partials on the tensor cores (D = 64 or 128) ------------------------------------
-// The same records as attn_split_kernel (grid (Hk, chunks, batch), CHUNK positions per CTA), with
+// The same records as attn_split_kernel, one per CTA of grid (Hk, chunk groups, batch): CTA y takes the
+// `span` consecutive chunks of CHUNK positions y*span .. y*span + span - 1, one after another, with an
+// online softmax across them (span = 1: one record per chunk, the same bits as a single pass), with
 // S = Q K^T and O = P V as mma.sync m16n8k16 (bf16 operands, fp32 accumulation): the G query heads are
 // rows 0..G-1 of the 16-row A tile (the rest zero), K rows are the B operand as stored, V enters
 // through ldmatrix.trans.  Warp w scores positions 16w..16w+15 and owns D/4 output columns.  Scores
@@ -389,6 +391,7 @@ struct SplitSmem {
   uint16_t p[16][CHUNK + 8];
   float s[MAX_G][CHUNK];
   float x[ATTN_THREADS / 32][TD];  // per-warp scratch of the fused norm + rotary
+  float mrun[MAX_G], lrun[MAX_G], alpha[MAX_G];  // running softmax state over the CTA's chunks (log2 units)
 };
 
 // Operands of the fused form: the projection's raw q/k/v rows instead of rotated queries.
@@ -408,12 +411,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
                                                                      uint16_t* __restrict__ kc, uint16_t* __restrict__ vc,
                                                                      int64_t tmax, const int64_t* __restrict__ pos_ptr, float scale,
                                                                      float* __restrict__ part, int64_t kv_bstride, int window,
-                                                                     RopeArgs ra) {
+                                                                     RopeArgs ra, int span) {
   static_assert(ATTN_THREADS == 128 && CHUNK == 64, "four warps of 16 positions");
   using Sm = SplitSmem<TD>;
   constexpr int KP = Sm::KP;
   __shared__ __align__(16) Sm S;
-  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.x, cs = blockIdx.y, b = blockIdx.z;
   const int G = Hq / Hk;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, cq = lane & 3;  // mma fragment row / column pair
@@ -421,22 +424,29 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
   pdl_launch_dependents();
   const int64_t pos = pos_ptr[b];
   if (pos < 0 || pos >= tmax) {  // the unfused form's cache-write kernel flags it
-    if (ROPE && h == 0 && c == 0 && tid == 0) flag(WISP_STATUS_BAD_POS);
+    if (ROPE && h == 0 && cs == 0 && tid == 0) flag(WISP_STATUS_BAD_POS);
     return;
   }
   const int64_t lo = window_lo(pos, window);
-  const int64_t t0 = int64_t(c) * CHUNK > lo ? int64_t(c) * CHUNK : lo;
-  if (t0 > pos || t0 >= int64_t(c + 1) * CHUNK) return;  // outside [lo, pos]: the combine never reads this record
-  const int n = int((pos + 1 - t0) < int64_t(c + 1) * CHUNK - t0 ? (pos + 1 - t0) : int64_t(c + 1) * CHUNK - t0);
-  // positions t0 .. t0 + n - 1 sit in smem rows r0 .. r0 + n - 1 with r0 = t0 - c*CHUNK (a window can cut the chunk's start)
-  const int r0 = int(t0 - int64_t(c) * CHUNK);
-  // fused form: the chunk holding pos makes the new row (smem row rnew); -1 elsewhere
-  const int rnew = ROPE && pos < int64_t(c + 1) * CHUNK ? int(pos - int64_t(c) * CHUNK) : -1;
+  // this CTA's chunks [cs*span, cs*span + span) that meet [lo, pos]; none: the combine never reads its record
+  const int cfirst = max(cs * span, int(lo / CHUNK)), clast = min(cs * span + span - 1, int(pos / CHUNK));
+  if (cfirst > clast) return;
   q += int64_t(b) * Hq * TD;
   kc += int64_t(b) * kv_bstride;
   vc += int64_t(b) * kv_bstride;
   part += int64_t(b) * Hk * gridDim.y * G * rec_floats(TD);
-  {
+  const float qscale = scale * 1.4426950408889634f;  // log2 units
+  constexpr int NT = TD / 32;  // P V n-tiles of 8 per warp
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  for (int c = cfirst; c <= clast; ++c) {
+    const int64_t t0 = int64_t(c) * CHUNK > lo ? int64_t(c) * CHUNK : lo;
+    const int n = int((pos + 1 - t0) < int64_t(c + 1) * CHUNK - t0 ? (pos + 1 - t0) : int64_t(c + 1) * CHUNK - t0);
+    // positions t0 .. t0 + n - 1 sit in smem rows r0 .. r0 + n - 1 with r0 = t0 - c*CHUNK (a window can cut the chunk's start)
+    const int r0 = int(t0 - int64_t(c) * CHUNK);
+    // fused form: the chunk holding pos makes the new row (smem row rnew); -1 elsewhere
+    const int rnew = ROPE && pos < int64_t(c + 1) * CHUNK ? int(pos - int64_t(c) * CHUNK) : -1;
     const uint16_t* kb = kc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
     const uint16_t* vb = vc + (int64_t(h) * tmax + int64_t(c) * CHUNK) * TD;
     constexpr int PR = TD / 8;  // 16-byte pieces per row
@@ -452,101 +462,114 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_split_tc_kernel(const uint1
         reinterpret_cast<uint4*>(&S.v[r][0])[cp] = make_uint4(0, 0, 0, 0);
       }
     }
-    if (ROPE) {
-      for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
-        const int r = i / PR, cp = i % PR;
-        if (r >= G) reinterpret_cast<uint4*>(&S.q[r][0])[cp] = make_uint4(0, 0, 0, 0);
-      }
-      const uint16_t* row = ra.qkv + int64_t(b) * ra.qkv_stride;
-      const uint16_t* cs = ra.cos_t + pos * TD;
-      const uint16_t* sn = ra.sin_t + pos * TD;
-      for (int g = warp; g < G; g += ATTN_THREADS / 32)
-        norm_rope_warp(row + int64_t(h * G + g) * TD, ra.qn_w, ra.eps, cs, sn, TD, lane, S.x[warp], &S.q[g][0]);
-      if (rnew >= 0) {
-        // warp 0: the new key (norm + rotary) into the cache and into smem row rnew; warp 1: the value
-        uint16_t* kdst = kc + (int64_t(h) * tmax + pos) * TD;
-        if (warp == 0) {
-          norm_rope_warp(row + int64_t(Hq + h) * TD, ra.kn_w, ra.eps, cs, sn, TD, lane, S.x[0], &S.k[rnew][0]);
-          for (int i = lane; i < TD; i += 32) kdst[i] = S.k[rnew][i];
-        } else if (warp == 1) {
-          const uint16_t* vs = row + int64_t(Hq + Hk + h) * TD;
-          uint16_t* vdst = vc + (int64_t(h) * tmax + pos) * TD;
-          for (int i = lane; i < TD; i += 32) {
-            const uint16_t v = vs[i];
-            S.v[rnew][i] = v;
-            vdst[i] = v;
-          }
+    if (c == cfirst) {  // the queries and the running state, while the first chunk's rows are in flight
+      if (ROPE) {
+        for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
+          const int r = i / PR, cp = i % PR;
+          if (r >= G) reinterpret_cast<uint4*>(&S.q[r][0])[cp] = make_uint4(0, 0, 0, 0);
+        }
+        const uint16_t* row = ra.qkv + int64_t(b) * ra.qkv_stride;
+        for (int g = warp; g < G; g += ATTN_THREADS / 32)
+          norm_rope_warp(row + int64_t(h * G + g) * TD, ra.qn_w, ra.eps, ra.cos_t + pos * TD, ra.sin_t + pos * TD, TD, lane,
+                         S.x[warp], &S.q[g][0]);
+      } else {
+        for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
+          const int r = i / PR, cp = i % PR;
+          reinterpret_cast<uint4*>(&S.q[r][0])[cp] =
+              r < G ? reinterpret_cast<const uint4*>(q + (int64_t(h) * G + r) * TD)[cp] : make_uint4(0, 0, 0, 0);
         }
       }
-    } else {
-      for (int i = tid; i < 16 * PR; i += ATTN_THREADS) {
-        const int r = i / PR, cp = i % PR;
-        reinterpret_cast<uint4*>(&S.q[r][0])[cp] =
-            r < G ? reinterpret_cast<const uint4*>(q + (int64_t(h) * G + r) * TD)[cp] : make_uint4(0, 0, 0, 0);
+      for (int i = tid; i < 16 * (CHUNK + 8) / 2; i += ATTN_THREADS) reinterpret_cast<uint32_t*>(&S.p[0][0])[i] = 0u;
+      if (tid < G) S.mrun[tid] = -INFINITY, S.lrun[tid] = 0.0f;
+    }
+    if (ROPE && rnew >= 0) {
+      // warp 0: the new key (norm + rotary) into the cache and into smem row rnew; warp 1: the value
+      const uint16_t* row = ra.qkv + int64_t(b) * ra.qkv_stride;
+      uint16_t* kdst = kc + (int64_t(h) * tmax + pos) * TD;
+      if (warp == 0) {
+        norm_rope_warp(row + int64_t(Hq + h) * TD, ra.kn_w, ra.eps, ra.cos_t + pos * TD, ra.sin_t + pos * TD, TD, lane, S.x[0],
+                       &S.k[rnew][0]);
+        for (int i = lane; i < TD; i += 32) kdst[i] = S.k[rnew][i];
+      } else if (warp == 1) {
+        const uint16_t* vs = row + int64_t(Hq + Hk + h) * TD;
+        uint16_t* vdst = vc + (int64_t(h) * tmax + pos) * TD;
+        for (int i = lane; i < TD; i += 32) {
+          const uint16_t v = vs[i];
+          S.v[rnew][i] = v;
+          vdst[i] = v;
+        }
       }
     }
-    for (int i = tid; i < 16 * (CHUNK + 8) / 2; i += ATTN_THREADS) reinterpret_cast<uint32_t*>(&S.p[0][0])[i] = 0u;
     cp_async_wait_all();  // the chunk's K / V rows (the query work above overlapped their flight)
-  }
-  __syncthreads();
-  const float qscale = scale * 1.4426950408889634f;  // log2 units
-  // scores: warp w, positions 16w + 8nt + (0..7)
+    __syncthreads();
+    // scores: warp w, positions 16w + 8nt + (0..7)
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    const int t = 16 * warp + 8 * nt;
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int nt = 0; nt < 2; ++nt) {
+      const int t = 16 * warp + 8 * nt;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < TD / 16; ++j) {
-      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.q[gq][16 * j + 2 * cq]);
-      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.q[gq][16 * j + 8 + 2 * cq]);
-      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&S.k[t + gq][16 * j + 2 * cq]);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&S.k[t + gq][16 * j + 8 + 2 * cq]);
-      mma_bf16(d, a0, 0u, a2, 0u, b0, b1);
+      for (int j = 0; j < TD / 16; ++j) {
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.q[gq][16 * j + 2 * cq]);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.q[gq][16 * j + 8 + 2 * cq]);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&S.k[t + gq][16 * j + 2 * cq]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&S.k[t + gq][16 * j + 8 + 2 * cq]);
+        mma_bf16(d, a0, 0u, a2, 0u, b0, b1);
+      }
+      if (gq < G) {
+        const int p0 = t + 2 * cq;
+        S.s[gq][p0] = p0 >= r0 && p0 < r0 + n ? d[0] * qscale : -INFINITY;
+        S.s[gq][p0 + 1] = p0 + 1 >= r0 && p0 + 1 < r0 + n ? d[1] * qscale : -INFINITY;
+      }
     }
+    __syncthreads();
+    // online softmax: warp w takes heads w, w + 4; the running maximum rescales what came before
+    for (int g = warp; g < G; g += ATTN_THREADS / 32) {
+      const float v0 = S.s[g][lane], v1 = S.s[g][lane + 32];
+      const float mp = S.mrun[g];
+      const float m = fmaxf(mp, warp_max(fmaxf(v0, v1)));  // finite: the chunk holds at least one position
+      const float al = exp2f(mp - m);                      // 0 at the CTA's first chunk
+      const float e0 = exp2f(v0 - m), e1 = exp2f(v1 - m);
+      const float l = warp_sum(e0 + e1);
+      S.p[g][lane] = f32_to_bf16(e0);
+      S.p[g][lane + 32] = f32_to_bf16(e1);
+      __syncwarp();
+      if (lane == 0) {
+        S.lrun[g] = S.lrun[g] * al + l;
+        S.mrun[g] = m;
+        S.alpha[g] = al;
+      }
+    }
+    __syncthreads();
+    // P V: warp w owns output columns w * TD/4 .. (w + 1) * TD/4 - 1 (rows >= G of P are zero)
     if (gq < G) {
-      const int p0 = t + 2 * cq;
-      S.s[gq][p0] = p0 >= r0 && p0 < r0 + n ? d[0] * qscale : -INFINITY;
-      S.s[gq][p0 + 1] = p0 + 1 >= r0 && p0 + 1 < r0 + n ? d[1] * qscale : -INFINITY;
-    }
-  }
-  __syncthreads();
-  // softmax within the chunk: warp w takes heads w, w + 4
-  for (int g = warp; g < G; g += ATTN_THREADS / 32) {
-    const float v0 = S.s[g][lane], v1 = S.s[g][lane + 32];
-    const float m = warp_max(fmaxf(v0, v1));  // finite: the chunk holds at least one position
-    const float e0 = exp2f(v0 - m), e1 = exp2f(v1 - m);
-    const float l = warp_sum(e0 + e1);
-    S.p[g][lane] = f32_to_bf16(e0);
-    S.p[g][lane + 32] = f32_to_bf16(e1);
-    if (lane == 0) {
-      float* rec = part + ((int64_t(h) * gridDim.y + c) * G + g) * rec_floats(TD);
-      rec[TD] = m * 0.6931471805599453f;  // back to natural units
-      rec[TD + 1] = l;
-    }
-  }
-  __syncthreads();
-  // P V: warp w owns output columns w * TD/4 .. (w + 1) * TD/4 - 1
-  constexpr int NT = TD / 32;  // n-tiles of 8 per warp
-  float o[NT][4];
+      const float al = S.alpha[gq];
 #pragma unroll
-  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-  const int mi = lane >> 3, ri = lane & 7;  // ldmatrix: matrix mi, row ri
-#pragma unroll
-  for (int j = 0; j < CHUNK / 16; ++j) {
-    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.p[gq][16 * j + 2 * cq]);
-    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.p[gq][16 * j + 8 + 2 * cq]);
-#pragma unroll
-    for (int pr = 0; pr < NT / 2; ++pr) {
-      uint32_t bv[4];
-      ldsm_x4_trans(bv, &S.v[16 * j + (mi & 1) * 8 + ri][warp * (TD / 4) + 16 * pr + (mi >> 1) * 8]);
-      mma_bf16(o[2 * pr], a0, 0u, a2, 0u, bv[0], bv[1]);
-      mma_bf16(o[2 * pr + 1], a0, 0u, a2, 0u, bv[2], bv[3]);
+      for (int i = 0; i < NT; ++i) o[i][0] *= al, o[i][1] *= al;
     }
+    const int mi = lane >> 3, ri = lane & 7;  // ldmatrix: matrix mi, row ri
+#pragma unroll
+    for (int j = 0; j < CHUNK / 16; ++j) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&S.p[gq][16 * j + 2 * cq]);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&S.p[gq][16 * j + 8 + 2 * cq]);
+#pragma unroll
+      for (int pr = 0; pr < NT / 2; ++pr) {
+        uint32_t bv[4];
+        ldsm_x4_trans(bv, &S.v[16 * j + (mi & 1) * 8 + ri][warp * (TD / 4) + 16 * pr + (mi >> 1) * 8]);
+        mma_bf16(o[2 * pr], a0, 0u, a2, 0u, bv[0], bv[1]);
+        mma_bf16(o[2 * pr + 1], a0, 0u, a2, 0u, bv[2], bv[3]);
+      }
+    }
+    __syncthreads();  // the next chunk overwrites K, V, P and the scores
   }
   if (gq < G) {
-    float* rec = part + ((int64_t(h) * gridDim.y + c) * G + gq) * rec_floats(TD) + warp * (TD / 4);
+    float* rec = part + ((int64_t(h) * gridDim.y + cs) * G + gq) * rec_floats(TD);
 #pragma unroll
-    for (int i = 0; i < NT; ++i) *reinterpret_cast<float2*>(rec + 8 * i + 2 * cq) = make_float2(o[i][0], o[i][1]);
+    for (int i = 0; i < NT; ++i)
+      *reinterpret_cast<float2*>(rec + warp * (TD / 4) + 8 * i + 2 * cq) = make_float2(o[i][0], o[i][1]);
+    if (warp == 0 && cq == 0) {
+      rec[TD] = S.mrun[gq] * 0.6931471805599453f;  // back to natural units
+      rec[TD + 1] = S.lrun[gq];
+    }
   }
 }
 

@@ -903,19 +903,30 @@ int64_t wisp_attn_workspace_floats(int Hq, int Hk, int D, int64_t tmax) {
   return int64_t(Hk) * ((tmax + dec::CHUNK - 1) / dec::CHUNK) * (Hq / Hk) * dec::rec_floats(D);
 }
 
-// chunk partials of decode attention: the tensor-core kernel for head_dim 64 and 128, the CUDA-core one otherwise
+// Chunks of CHUNK positions per attention CTA (tensor-core kernel): the largest of 1, 2, 4, 8 that still
+// leaves at least 16 CTAs per SM, so long contexts write (and the merge reads) a fraction of the records
+// while short ones keep one chunk per CTA.
+static int attn_span(int D, int Hk, int nchunk, int B) {
+  if (D != 64 && D != 128) return 1;  // the CUDA-core kernel takes one chunk per CTA
+  int span = 1;
+  while (span < 8 && int64_t(Hk) * ((nchunk + 2 * span - 1) / (2 * span)) * B >= 16 * int64_t(num_sms())) span *= 2;
+  return span;
+}
+
+// chunk partials of decode attention: the tensor-core kernel for head_dim 64 and 128, the CUDA-core one
+// otherwise; grid.y = chunk groups of `span` chunks
 static cudaError_t launch_attn_split(dim3 grid, const uint16_t* q, int Hq, int Hk, int D, const uint16_t* k_cache,
                                      const uint16_t* v_cache, int64_t tmax, const int64_t* pos, float scale, float* workspace,
-                                     int64_t kv_bstride, int window, cudaStream_t s) {
+                                     int64_t kv_bstride, int window, int span, cudaStream_t s) {
   const dec::RopeArgs none{};
   uint16_t* kc = const_cast<uint16_t*>(k_cache);  // not written without the fused rotary
   uint16_t* vc = const_cast<uint16_t*>(v_cache);
   if (D == 128)
     return launch_pdl(dec::attn_split_tc_kernel<128, false>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, kc, vc, tmax, pos, scale,
-                      workspace, kv_bstride, window, none);
+                      workspace, kv_bstride, window, none, span);
   if (D == 64)
     return launch_pdl(dec::attn_split_tc_kernel<64, false>, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, kc, vc, tmax, pos, scale,
-                      workspace, kv_bstride, window, none);
+                      workspace, kv_bstride, window, none, span);
   return launch_pdl(dec::attn_split_kernel, grid, dec::ATTN_THREADS, 0, s, q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
                     kv_bstride, window);
 }
@@ -928,11 +939,12 @@ int wisp_gqa_decode_attn(const uint16_t* q, int Hq, int Hk, int D, const uint16_
   WISP_REQUIRE(D > 0 && D % 32 == 0 && D <= dec::MAX_D && tmax > 0, "wisp_gqa_decode_attn: need D a multiple of 32, <= %d", dec::MAX_D);
   WISP_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16), "wisp_gqa_decode_attn: caches must be 16-byte aligned");
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
+  const int span = attn_span(D, Hk, nchunk, 1), ngrp = (nchunk + span - 1) / span;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_attn_split(dim3(Hk, nchunk), q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace, 0, 0, s);
+  cudaError_t e = launch_attn_split(dim3(Hk, ngrp), q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace, 0, 0, span, s);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
-  e = launch_pdl(dec::attn_combine_kernel, Hq, dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, 0,
-                 (const float*)nullptr);
+  e = launch_pdl(dec::attn_combine_kernel, Hq, dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, ngrp, pos, tmax, out, 0,
+                 (const float*)nullptr, dec::CHUNK * span);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_attn");
 }
@@ -956,12 +968,13 @@ int wisp_gqa_decode_attn_batched(const uint16_t* q, int B, int Hq, int Hk, int D
   WISP_REQUIRE(workspace_floats >= wisp_attn_batched_workspace_floats(B, Hq, Hk, D, tmax),
                "wisp_gqa_decode_attn_batched: workspace of %lld floats is too small", (long long)workspace_floats);
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
+  const int span = attn_span(D, Hk, nchunk, B), ngrp = (nchunk + span - 1) / span;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_attn_split(dim3(Hk, nchunk, B), q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
-                                    int64_t(Hk) * tmax * D, window, s);
+  cudaError_t e = launch_attn_split(dim3(Hk, ngrp, B), q, Hq, Hk, D, k_cache, v_cache, tmax, pos, scale, workspace,
+                                    int64_t(Hk) * tmax * D, window, span, s);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
-  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out, window,
-                 sinks);
+  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, ngrp, pos, tmax, out, window,
+                 sinks, dec::CHUNK * span);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gqa_decode_attn_batched: %s", cudaGetErrorString(e));
   return check_launch("gqa_decode_attn_batched");
 }
@@ -981,16 +994,19 @@ int wisp_attn_decode_batched(const uint16_t* qkv, int64_t qkv_stride, int B, int
   WISP_REQUIRE(workspace_floats >= wisp_attn_batched_workspace_floats(B, Hq, Hk, D, tmax),
                "wisp_attn_decode_batched: workspace of %lld floats is too small", (long long)workspace_floats);
   const int nchunk = int((tmax + dec::CHUNK - 1) / dec::CHUNK);
+  const int span = attn_span(D, Hk, nchunk, B), ngrp = (nchunk + span - 1) / span;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dec::RopeArgs ra{qkv, qkv_stride, qn_w, kn_w, eps, cos_t, sin_t};
   const int64_t kvb = int64_t(Hk) * tmax * D;
-  cudaError_t e = D == 128 ? launch_pdl(dec::attn_split_tc_kernel<128, true>, dim3(Hk, nchunk, B), dec::ATTN_THREADS, 0, s,
-                                        (const uint16_t*)nullptr, Hq, Hk, k_cache, v_cache, tmax, pos, scale, workspace, kvb, window, ra)
-                           : launch_pdl(dec::attn_split_tc_kernel<64, true>, dim3(Hk, nchunk, B), dec::ATTN_THREADS, 0, s,
-                                        (const uint16_t*)nullptr, Hq, Hk, k_cache, v_cache, tmax, pos, scale, workspace, kvb, window, ra);
+  cudaError_t e = D == 128 ? launch_pdl(dec::attn_split_tc_kernel<128, true>, dim3(Hk, ngrp, B), dec::ATTN_THREADS, 0, s,
+                                        (const uint16_t*)nullptr, Hq, Hk, k_cache, v_cache, tmax, pos, scale, workspace, kvb, window, ra,
+                                        span)
+                           : launch_pdl(dec::attn_split_tc_kernel<64, true>, dim3(Hk, ngrp, B), dec::ATTN_THREADS, 0, s,
+                                        (const uint16_t*)nullptr, Hq, Hk, k_cache, v_cache, tmax, pos, scale, workspace, kvb, window, ra,
+                                        span);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_attn_decode_batched: %s", cudaGetErrorString(e));
-  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, nchunk, pos, tmax, out,
-                 window, sinks);
+  e = launch_pdl(dec::attn_combine_kernel, dim3(Hq, B), dec::CMB_THREADS, 0, s, (const float*)workspace, Hq, Hk, D, ngrp, pos, tmax, out,
+                 window, sinks, dec::CHUNK * span);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_attn_decode_batched: %s", cudaGetErrorString(e));
   return check_launch("attn_decode_batched");
 }
