@@ -21,7 +21,14 @@ namespace dense {
 
 constexpr int CONSUMERS = 8;
 constexpr int THREADS = 32 * (CONSUMERS + 1);  // warp 0 produces, warps 1..8 consume
-constexpr int STAGES = 3;  // 96 KB ring: a GEMV CTA fits beside the previous kernel's CTA (PDL prefetch)
+// ring of 3 stages (96 KB at K = 2048 / 4096: a GEMV CTA fits beside the previous kernel's CTA for the
+// PDL prefetch), or 4 where 4 stages fit in 120 KB and a CTA's rows need them (K = 2880: 4 x 28.8 KB).
+// The 4th stage (gpt-oss q/k/v and lm_head) measured 4.6% faster per token on the gpt-oss decoder; a 4th
+// 32 KB stage measured 1.8% slower on Qwen3, and rings below 3 stages slower on both (they change how
+// the neighbouring kernels' CTAs share the SMs).
+constexpr int STAGES = 3;
+constexpr int STAGES_MAX = 4;
+constexpr int64_t RING_BYTES_MAX = 120 * 1024;
 constexpr int STAGE_BYTES = 32 * 1024;
 
 struct GemvArgs {
@@ -43,16 +50,17 @@ struct GemvLayout {
   int64_t stage_bytes, off_x, off_red, off_bars, bytes;
 };
 
+template <int NST = STAGES>
 __host__ __device__ inline GemvLayout gemv_layout(int64_t K) {
   GemvLayout L;
   const int64_t row = K * 2;
   int64_t sr = STAGE_BYTES / row;
   L.rows_per_stage = int(sr < 1 ? 1 : (sr > 16 ? 16 : sr));
   L.stage_bytes = L.rows_per_stage * row;
-  L.off_x = STAGES * L.stage_bytes;      // normalised x, bf16 [K]
+  L.off_x = NST * L.stage_bytes;         // normalised x, bf16 [K]
   L.off_red = ru16(L.off_x + row);       // [CONSUMERS] f32 partial sums of squares
-  L.off_bars = ru16(L.off_red + CONSUMERS * 4);  // full[STAGES], empty[STAGES]
-  L.bytes = L.off_bars + 16 * STAGES;
+  L.off_bars = ru16(L.off_red + CONSUMERS * 4);  // full[NST], empty[NST]
+  L.bytes = L.off_bars + 16 * NST;
   return L;
 }
 
@@ -63,10 +71,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+template <int STAGES>
 __global__ void __launch_bounds__(THREADS, 1) gemv_kernel(GemvArgs A) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const GemvLayout L = gemv_layout(A.K);
+  const GemvLayout L = gemv_layout<STAGES>(A.K);
   uint16_t* xs = reinterpret_cast<uint16_t*>(sm + L.off_x);
   float* red = reinterpret_cast<float*>(sm + L.off_red);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.off_bars);

@@ -844,11 +844,17 @@ int wisp_gemv_bias(const uint16_t* W, int64_t N, int64_t K, const uint16_t* x, c
                    (!xn_out || (xn_out != x && xn_out != x_add)),
                "wisp_gemv: y, x_sum_out and xn_out must not alias x or x_add");
   dense::GemvArgs A{W, N, K, x, x_add, x_sum_out, norm_w, eps, xn_out, res, y, bias};
-  const dense::GemvLayout L = dense::gemv_layout(K);
   const int grid = int(N < num_sms() ? N : num_sms());
+  // a 4th ring stage where 4 fit in 120 KB and a CTA's rows need more than 3
+  const dense::GemvLayout L3 = dense::gemv_layout<dense::STAGES>(K);
+  const int64_t rows_cta = (N + grid - 1) / grid;
+  const bool four = dense::STAGES_MAX * L3.stage_bytes <= dense::RING_BYTES_MAX && rows_cta > dense::STAGES * L3.rows_per_stage;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  e = launch_pdl(dense::gemv_kernel, grid, dense::THREADS, size_t(L.bytes), s, A);
+  if (four)
+    e = launch_pdl(dense::gemv_kernel<dense::STAGES_MAX>, grid, dense::THREADS, size_t(dense::gemv_layout<dense::STAGES_MAX>(K).bytes), s, A);
+  else
+    e = launch_pdl(dense::gemv_kernel<dense::STAGES>, grid, dense::THREADS, size_t(L3.bytes), s, A);
   if (e != cudaSuccess) return fail(WISP_ERR_CUDA, "wisp_gemv: %s", cudaGetErrorString(e));
   return check_launch("gemv");
 }
